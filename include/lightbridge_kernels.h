@@ -1,0 +1,285 @@
+/*
+ * lightbridge_kernels.h -- C ABI of the B200 (sm_100a) quantized routed-MoE
+ * expert kernels.
+ *
+ * This is the drop-in boundary for LightBridge's quantized expert hot path:
+ * packed IQ2_S / IQ3_S / Q4_K / Q5_K weight rows dotted against Q8_K
+ * activations inside the Hy3 routed + shared SwiGLU expert FFN with top-k
+ * routing. The reference (a Rust workspace) exposes this path as Rust
+ * functions over borrowed slices; every entry point below names the reference
+ * function it replaces (path:line inside the reference project).
+ *
+ * Conventions (kept from the reference):
+ *  - Caller-owned outputs and scratch. No entry point allocates on the hot
+ *    path; scratch sizes are queryable (lbk_required_q8k_bytes,
+ *    lbk_moe_workspace_bytes).
+ *  - All host-checkable validation (types, widths, lengths, finite scalars,
+ *    routed-expert order) happens before anything is launched; on a non-zero
+ *    status nothing was written.
+ *  - Device pointers only (except where a parameter says "host"). Launches are
+ *    stream-ordered and asynchronous. Conditions that need device data
+ *    (non-finite activations, non-finite weight scales, non-finite SwiGLU
+ *    values) are recorded in a device status word that the caller reads with
+ *    lbk_context_sync_status(); kernels that write outputs check it first, so
+ *    outputs of a launch whose inputs failed validation are left unchanged.
+ *  - Packed weights use the GGUF byte layout unchanged (LBK_LAYOUT_GGUF), or
+ *    the row-planar device layout produced by lbk_repack (LBK_LAYOUT_PLANAR),
+ *    which has an exact byte-for-byte inverse (lbk_unpack).
+ *  - Matrices follow GGML order [input_width, output_width]: output row r is
+ *    input_width/256 consecutive packed blocks.
+ *  - A context is bound to one device. Distinct contexts may be used from
+ *    different host threads; one context is not reentrant.
+ */
+#ifndef LIGHTBRIDGE_KERNELS_H
+#define LIGHTBRIDGE_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LBK_ABI_VERSION 1
+
+/* GGML type discriminants (reference: crates/bridge-core/src/ggml_type.rs:9-30). */
+typedef enum lbk_ggml_type {
+    LBK_TYPE_F32 = 0,
+    LBK_TYPE_Q4_K = 12,
+    LBK_TYPE_Q5_K = 13,
+    LBK_TYPE_Q8_K = 15,
+    LBK_TYPE_IQ3_S = 21,
+    LBK_TYPE_IQ2_S = 22
+} lbk_ggml_type;
+
+/* Block constants (reference: bridge-quant-layout/src/q8_k.rs:7-12,
+ * src/k_quants.rs:7-13). */
+#define LBK_QK_K 256
+#define LBK_Q8K_BLOCK_BYTES 292
+#define LBK_Q4K_BLOCK_BYTES 144
+#define LBK_Q5K_BLOCK_BYTES 176
+#define LBK_IQ2S_BLOCK_BYTES 82
+#define LBK_IQ3S_BLOCK_BYTES 110
+
+/* Status codes. Values 1..29 map one-to-one onto the reference error variants
+ * QuantError (bridge-quant-layout/src/error.rs:9-60), KernelError
+ * (bridge-kernels-reference/src/error.rs:6-58) and the routing errors of
+ * Hy3Error (bridge-model-hy3/src/routing.rs:25-107). */
+typedef enum lbk_status {
+    LBK_OK = 0,
+    LBK_UNSUPPORTED_TYPE = 1,
+    LBK_ZERO_LOGICAL_ELEMENTS = 2,
+    LBK_LOGICAL_ELEMENTS_NOT_DIVISIBLE = 3,
+    LBK_ARITHMETIC_OVERFLOW = 4,
+    LBK_ENCODED_LENGTH_MISMATCH = 5,
+    LBK_OUTPUT_LENGTH_MISMATCH = 6,
+    LBK_NON_FINITE_SCALE = 7,        /* packed binary16 d / dmin */
+    LBK_NON_FINITE_ACTIVATION = 8,   /* Q8_K quantizer input */
+    LBK_NON_FINITE_Q8_SCALE = 9,     /* encoded Q8_K d */
+    LBK_DIMENSION_MISMATCH = 10,
+    LBK_SCRATCH_TOO_SMALL = 11,
+    LBK_NON_FINITE_VALUE = 12,       /* GEMV input, coefficient, SwiGLU value ... */
+    LBK_ROUTED_EXPERT_ORDER = 13,
+    LBK_DUPLICATE_ROUTED_EXPERT = 14,
+    LBK_INVALID_PARAMETER = 15,
+    LBK_ROUTING_TOPK = 16,
+    LBK_ROUTING_LENGTH = 17,
+    LBK_NON_FINITE_ROUTING_VALUE = 18,
+    LBK_CUDA_ERROR = 30,
+    LBK_TIMEOUT = 31,
+    LBK_NO_DEVICE = 32
+} lbk_status;
+
+/* Packed weight byte layouts. */
+typedef enum lbk_layout {
+    LBK_LAYOUT_GGUF = 0,   /* GGUF / reference block layout, unchanged */
+    LBK_LAYOUT_PLANAR = 1  /* per-matrix field planes (see lbk_repack) */
+} lbk_layout;
+
+/* Router dot-product order. */
+typedef enum lbk_router_mode {
+    /* One sequential f32 chain per row, in lane order: bit-identical to the
+     * reference F32 GEMV (bridge-kernels-reference/src/gemv.rs:286-303). */
+    LBK_ROUTER_SEQUENTIAL = 0,
+    /* Fixed-shape tree reduction: deterministic, within 1e-5 relative of the
+     * sequential order, and much faster. */
+    LBK_ROUTER_TREE = 1
+} lbk_router_mode;
+
+/* Detail of the last failure, host- or device-detected. */
+typedef struct lbk_error_detail {
+    int32_t status;        /* lbk_status */
+    int32_t cuda_error;    /* cudaError_t when status == LBK_CUDA_ERROR */
+    uint64_t index;        /* block / lane / expert index, where meaningful */
+    uint32_t bits;         /* offending value bits, where meaningful */
+    uint64_t expected;     /* expected length / width, where meaningful */
+    uint64_t actual;       /* actual length / width, where meaningful */
+    char message[160];
+} lbk_error_detail;
+
+typedef struct lbk_context lbk_context;
+
+/* One packed matrix in device memory. Its byte length must be exactly
+ * output_width * (input_width / 256) * block_bytes(type). */
+typedef struct lbk_matrix {
+    int32_t type;            /* lbk_ggml_type */
+    int32_t layout;          /* lbk_layout */
+    uint64_t input_width;    /* GGML ne[0]: logical elements per row */
+    uint64_t output_width;   /* GGML ne[1]: rows */
+    const void* data;        /* device pointer */
+    uint64_t bytes;          /* encoded byte length */
+} lbk_matrix;
+
+/* A SwiGLU expert (reference: SwiGluExpert, activation.rs:5-47). */
+typedef struct lbk_expert {
+    lbk_matrix gate;
+    lbk_matrix up;
+    lbk_matrix down;
+} lbk_expert;
+
+/* A routed selection (reference: RoutedExpert, bridge-model-hy3/src/routing.rs). */
+typedef struct lbk_routed {
+    uint32_t expert_id;
+    float coefficient;
+} lbk_routed;
+
+/* ---------------------------------------------------------------- context */
+
+int32_t lbk_abi_version(void);
+
+/* Name of the backend, "cuda_sm100a_q8_k"; the CPU backend of the reference is
+ * named by CpuCapabilities::backend_name (bridge-kernels-cpu/src/lib.rs:50-56). */
+const char* lbk_backend_name(void);
+
+/* Creates a context on `device` (also loads the IQ codebooks into device
+ * memory and allocates the device status word). Not on the hot path. */
+int32_t lbk_context_create(int32_t device, lbk_context** out);
+int32_t lbk_context_destroy(lbk_context* ctx);
+
+/* Synchronizes `stream` (a cudaStream_t, NULL = legacy default), reads and
+ * clears the device status word. Returns its status; fills `detail` if given. */
+int32_t lbk_context_sync_status(lbk_context* ctx, void* stream, lbk_error_detail* detail);
+
+/* Detail of the last host-side failure of any call on this thread. */
+void lbk_last_error_detail(lbk_error_detail* out);
+
+/* ------------------------------------------------------------- sizes */
+
+/* reference: required_q8_k_bytes, bridge-kernels-reference/src/gemv.rs:18-31 */
+int32_t lbk_required_q8k_bytes(uint64_t input_width, uint64_t* bytes);
+
+/* Encoded byte length of a [input_width, output_width] matrix of `type`
+ * (reference: EncodedTensorView::new, matrix.rs:26-78). */
+int32_t lbk_matrix_bytes(int32_t type, uint64_t input_width, uint64_t output_width, uint64_t* bytes);
+
+/* ------------------------------------------------------------- kernels */
+
+/* Q8_K activation quantization of x[n] into q8[n/256*292].
+ * reference: quantize_row_q8_k_into, bridge-quant-layout/src/q8_k.rs:16-76.
+ * Non-finite input is reported through the device status word
+ * (LBK_NON_FINITE_ACTIVATION, first lane index) and q8 is left unchanged. */
+int32_t lbk_quantize_q8k(lbk_context* ctx, const float* x, uint64_t n, uint8_t* q8,
+                         uint64_t q8_bytes, void* stream);
+
+/* Dot products of `rows` packed rows (each input_width wide) with one Q8_K
+ * activation row, writing f32 results -- the per-row result of
+ * vec_dot_q8_k / vec_dot_q8_k_cpu (q8_k.rs:80-119), bit-identical.
+ * If block_sums is non-NULL it receives the per-super-block int32 sums that
+ * feed the f32 tail: 1 per block for IQ2_S / IQ3_S, 9 per block (8 lane sums,
+ * then the min sum) for Q4_K / Q5_K. */
+int32_t lbk_vec_dot_q8k(lbk_context* ctx, const lbk_matrix* w, const uint8_t* q8, uint64_t q8_bytes,
+                        float* out, int32_t* block_sums, void* stream);
+
+/* y = W x with x quantized to Q8_K into caller scratch.
+ * reference: gemv_into (CpuParallelQ8K), bridge-kernels-reference/src/gemv.rs:88-115,
+ * and gemv_cpu_parallel_q8k_into (:56-70). */
+int32_t lbk_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, float* y,
+                 uint8_t* q8_scratch, uint64_t q8_scratch_bytes, void* stream);
+
+/* y[r] += scale * dot(W_r, Q8_K(x)), non-contracted multiply then add.
+ * reference: gemv_accumulate_scaled_into, gemv.rs:117-174. `scale` is
+ * checked on the host; non-finite y is reported via the status word. */
+int32_t lbk_gemv_accumulate_scaled(lbk_context* ctx, const lbk_matrix* w, const float* x, float* y,
+                                   float scale, uint8_t* q8_scratch, uint64_t q8_scratch_bytes,
+                                   void* stream);
+
+/* Router logits for `tokens` tokens: logits[t*E + e] = dot(router_e, x_t),
+ * router an F32 [hidden, E] matrix.
+ * reference: gemv_into on an F32 matrix, gemv.rs:72-86 and :286-303. */
+int32_t lbk_router_logits(lbk_context* ctx, const lbk_matrix* router, const float* x, uint64_t tokens,
+                          float* logits, int32_t mode, void* stream);
+
+/* Hy3 top-k routing of `tokens` rows of E logits: sigmoid, + selection bias for
+ * the ranking only, ties to ascending ID, renormalise over the top k with the
+ * 2^-14 floor, scale by weight_scale, output sorted by expert ID.
+ * reference: route_experts_into, bridge-model-hy3/src/routing.rs:25-107. */
+int32_t lbk_route_topk(lbk_context* ctx, const float* logits, const float* selection_bias,
+                       uint64_t expert_count, uint64_t tokens, uint32_t k, float weight_scale,
+                       lbk_routed* routed, void* stream);
+
+/* SwiGLU expert, accumulated: dst += coefficient * down(swiglu(gate x, up x)).
+ * reference: expert_swiglu_accumulate_into, activation.rs:104-144. */
+int32_t lbk_expert_swiglu_accumulate(lbk_context* ctx, const lbk_expert* expert, const float* x,
+                                     float* dst, float coefficient, void* workspace,
+                                     uint64_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------- MoE layer */
+
+/* One layer's resident expert table. All matrices must share one layout. */
+typedef struct lbk_moe_weights {
+    const lbk_expert* experts;   /* host array of expert_count descriptors */
+    uint64_t expert_count;
+    lbk_expert shared;           /* always-on shared expert, coefficient 1.0 */
+    lbk_matrix router;           /* F32 [hidden, expert_count] */
+    const float* selection_bias; /* device, expert_count floats */
+    uint32_t top_k;
+    float weight_scale;          /* Hy3 expert_weights_scale (2.826 default) */
+} lbk_moe_weights;
+
+/* Workspace bytes needed by lbk_moe_layer for `tokens` tokens. */
+int32_t lbk_moe_workspace_bytes(const lbk_moe_weights* w, uint64_t tokens, uint64_t* bytes);
+
+/* Full routed-MoE FFN for `tokens` tokens: router logits, top-k routing, then
+ * out[t] = sum over routed experts in ascending ID of coef * expert(x[t]),
+ * then + 1.0 * shared(x[t]) -- the combine order of moe_routed_by_id_into
+ * (bridge-kernels-reference/src/moe.rs:64-147) and the route/finish pair
+ * hy3_moe_route_token / hy3_moe_finish_token (layer.rs:473-659) minus the
+ * norm and residual. `routed_out` (device, tokens*top_k, may be NULL)
+ * receives the routing. */
+int32_t lbk_moe_layer(lbk_context* ctx, const lbk_moe_weights* w, const float* x, uint64_t tokens,
+                      float* out, lbk_routed* routed_out, int32_t router_mode, void* workspace,
+                      uint64_t workspace_bytes, void* stream);
+
+/* Same combine for a caller-supplied routing (device `routed`, tokens*k entries,
+ * IDs strictly ascending per token, finite coefficients).
+ * reference: moe_routed_by_id_into, moe.rs:64-147. */
+int32_t lbk_moe_routed(lbk_context* ctx, const lbk_moe_weights* w, const float* x, uint64_t tokens,
+                       const lbk_routed* routed, uint32_t k, float* out, void* workspace,
+                       uint64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------- layout tools */
+
+/* Converts a GGUF-layout matrix into the planar device layout (same byte
+ * count). Planar layout, per matrix of R rows and nb = input_width/256 blocks
+ * per row, is a sequence of field planes, each row-major over (row, block):
+ *   IQ2_S: qs[32] | signs[32] | qh[8] | scales[8] | d[2]
+ *   IQ3_S: qs[64] | signs[32] | qh[8] | scales[4] | d[2]
+ *   Q4_K : qs[128] | scales[12] | d[2] | dmin[2]
+ *   Q5_K : qs[128] | qh[32] | scales[12] | d[2] | dmin[2]
+ * so plane f of row r starts at plane_offset_f + r*nb*field_bytes_f. */
+int32_t lbk_repack(lbk_context* ctx, const lbk_matrix* src_gguf, void* dst_planar, uint64_t dst_bytes,
+                   void* stream);
+/* Exact inverse of lbk_repack. */
+int32_t lbk_unpack(lbk_context* ctx, const lbk_matrix* src_planar, void* dst_gguf, uint64_t dst_bytes,
+                   void* stream);
+
+/* Scans every binary16 d (and dmin) of a matrix; non-finite scales are
+ * reported through the status word as LBK_NON_FINITE_SCALE with the global
+ * block index. reference: validate_scales, k_quants.rs:178-208. */
+int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIGHTBRIDGE_KERNELS_H */
