@@ -1,0 +1,472 @@
+"""Benchmark: routed-MoE single-token decode through HBM-resident expert tables.
+
+Workload: one routed-MoE FFN layer per decode token --
+hidden 4096, 192 experts (gate/up IQ2_S 4096->1536, down IQ3_S 1536->4096),
+one shared expert (all Q4_K), F32 router 4096x192 ~ N(0, 0.02), top-8 with
+the reference's renormalisation (weight_scale 2.826, zero selection bias),
+token ~ N(0, 1). Weights are synthetic (seeded; see synth.py) because the
+reference measures only a real checkpoint that is not available.
+
+A step is one batch of TOKENS_PER_STEP independent single-token layer passes.
+Consecutive tokens rotate over LAYERS distinct resident layer tables (10.4 GB
+in total), so every pass streams its weights from HBM, not from the 126 MB
+L2 ("inputs larger than L2").
+
+value   : tokens/s with inputs already resident (CUDA graph of one step,
+          CUDA events, max over ranks).
+e2e     : tokens/s through the C ABI call per token (lbk_moe_forward), with
+          each step's tokens copied from pinned host memory and its outputs
+          read back inside the timed region.
+roofline: the dominant kernel's algorithmic bytes / its CUDA-event time.
+cpu_baseline: the CPU restatement of the reference's AVX2 path (oracle/),
+          moe_routed_by_id_into as the reference runs it (preflight + accept).
+
+--impl reference times that CPU path on the host cores on the same config.
+With N>1 GPUs every rank runs its own resident copy of the layers on its own
+tokens (replicas; weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "lightbridge-engine_b200"))
+
+H, F, E, K_TOP = 4096, 1536, 192, 8
+WEIGHT_SCALE = 2.826
+TOKENS_PER_STEP = 256
+LAYERS = 8
+TYPE_IQ2_S, TYPE_IQ3_S, TYPE_Q4_K = 22, 21, 12
+METRIC = "routed-MoE decode tokens/s (single-token MoE FFN layer, config 3)"
+
+
+def row_bytes(ty: int, k: int) -> int:
+    return k // 256 * {TYPE_IQ2_S: 82, TYPE_IQ3_S: 110, TYPE_Q4_K: 144}[ty]
+
+
+# algorithmic bytes per token: router + 8 routed experts + shared
+ROUTER_B = E * H * 4
+GATE_UP_B = K_TOP * 2 * F * row_bytes(TYPE_IQ2_S, H) + 2 * F * row_bytes(TYPE_Q4_K, H)
+DOWN_B = K_TOP * H * row_bytes(TYPE_IQ3_S, F) + H * row_bytes(TYPE_Q4_K, F)
+X_B, OUT_B = H * 4, H * 4
+LAYER_B = ROUTER_B + GATE_UP_B + DOWN_B + X_B + OUT_B
+
+
+def peaks() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from a committed ncu summary, if any."""
+    for f in sorted((REPO / "profiles").glob("*.md")) + sorted((REPO / "profiles").glob("*.txt")):
+        for line in f.read_text().splitlines():
+            if line.startswith(f"traffic_bytes_per_launch[{kernel}]:"):
+                try:
+                    return int(float(line.split(":", 1)[1].split()[0]))
+                except ValueError:
+                    pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.proc = None
+        self.index = index
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 6:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[2:]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ---------------------------------------------------------------- reference
+
+def reference_arm(args, rank: int) -> None:
+    """The reference's CPU path (its AVX2 restatement in oracle/) on the host cores."""
+    if rank != 0:
+        return
+    sys.path.insert(0, str(REPO / "oracle"))
+    import numpy as np
+
+    import oracle as orc
+    import synth
+
+    threads = orc.hw_threads()
+    rng = np.random.default_rng(2)
+    router = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    experts = []
+    for _ in range(E):
+        experts.append((TYPE_IQ2_S, synth.packed_np(rng, TYPE_IQ2_S, H, F), TYPE_IQ2_S,
+                        synth.packed_np(rng, TYPE_IQ2_S, H, F), TYPE_IQ3_S, synth.packed_np(rng, TYPE_IQ3_S, F, H), H, F))
+    shared = (TYPE_Q4_K, synth.packed_np(rng, TYPE_Q4_K, H, F), TYPE_Q4_K, synth.packed_np(rng, TYPE_Q4_K, H, F),
+              TYPE_Q4_K, synth.packed_np(rng, TYPE_Q4_K, F, H), H, F)
+    table = orc.ExpertTable(experts, shared, router=router, hidden=H)
+    bias = np.zeros(E, np.float32)
+    xs = rng.standard_normal((args.warmup + args.steps, H)).astype(np.float32)
+    for i in range(args.warmup):
+        orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs[i], preflight=True, simd=True, threads=threads)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs[args.warmup + i], preflight=True, simd=True, threads=threads)
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1000 / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "q8_k x packed (int8 dots, f32 tails)",
+        "data": "synthetic (seeded, config shapes)",
+        "config": {"workload": "config3: routed-MoE FFN layer, single-token decode", "hidden": H, "experts": E,
+                   "expert_ffn": F, "top_k": K_TOP, "gate_up": "IQ2_S", "down": "IQ3_S", "shared": "Q4_K",
+                   "step": "1 token (bounded sample of the GPU arm's 256-token step)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} tokens through one layer, moe_routed_by_id_into as-is (preflight + accept), AVX2 restatement"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+
+def build_layers(ctx, lbk, torch, dev, layers: int, seed0: int, keep_gguf_layer0: bool):
+    import synth
+
+    gen = torch.Generator(device=dev)
+    tables = []
+    host0 = None
+    for l in range(layers):
+        gen.manual_seed(seed0 + l)
+        keep = []
+        router = (torch.randn(E, H, device=dev, generator=gen) * 0.02).contiguous()
+        keep.append(router)
+
+        def stacked(ty, k, rows):
+            g = synth.packed_torch(gen, ty, k, rows * E, dev)
+            p = torch.empty_like(g)
+            mb = synth.matrix_bytes(ty, k, rows)
+            for e in range(E):
+                ctx.repack(lbk.matrix(ty, k, rows, g[e * mb:(e + 1) * mb]), p[e * mb:(e + 1) * mb])
+            return g, p
+
+        gg, gp = stacked(TYPE_IQ2_S, H, F)
+        ug, up = stacked(TYPE_IQ2_S, H, F)
+        dg, dp = stacked(TYPE_IQ3_S, F, H)
+        keep += [gp, up, dp]
+        sh = []
+        for ty, k, rows in [(TYPE_Q4_K, H, F), (TYPE_Q4_K, H, F), (TYPE_Q4_K, F, H)]:
+            g = synth.packed_torch(gen, ty, k, rows, dev)
+            p = torch.empty_like(g)
+            ctx.repack(lbk.matrix(ty, k, rows, g), p)
+            sh.append((ty, k, rows, g, p))
+            keep.append(p)
+        torch.cuda.synchronize()
+        if l == 0 and keep_gguf_layer0:
+            host0 = {
+                "router": router.cpu().numpy(),
+                "gate": gg.cpu().numpy(), "up": ug.cpu().numpy(), "down": dg.cpu().numpy(),
+                "shared": [s[3].cpu().numpy() for s in sh],
+            }
+        del gg, ug, dg
+        mbg, mbd = synth.matrix_bytes(TYPE_IQ2_S, H, F), synth.matrix_bytes(TYPE_IQ3_S, F, H)
+        experts = [
+            lbk.Expert(lbk.matrix(TYPE_IQ2_S, H, F, gp[e * mbg:(e + 1) * mbg], lbk.LAYOUT_PLANAR),
+                       lbk.matrix(TYPE_IQ2_S, H, F, up[e * mbg:(e + 1) * mbg], lbk.LAYOUT_PLANAR),
+                       lbk.matrix(TYPE_IQ3_S, F, H, dp[e * mbd:(e + 1) * mbd], lbk.LAYOUT_PLANAR))
+            for e in range(E)
+        ]
+        shared = lbk.Expert(*[lbk.matrix(ty, k, rows, p, lbk.LAYOUT_PLANAR) for ty, k, rows, _, p in sh])
+        bias = torch.zeros(E, device=dev)
+        keep.append(bias)
+        rm = lbk.Matrix(lbk.TYPE_F32, lbk.LAYOUT_GGUF, H, E, router.data_ptr(), router.numel() * 4)
+        layer = lbk.MoeLayer(ctx, experts, shared, rm, bias, K_TOP, WEIGHT_SCALE)
+        assert layer.fused
+        tables.append((layer, keep))
+    return tables, host0
+
+
+def cpu_baseline(host0, xs_host, budget_s: float = 12.0) -> dict:
+    sys.path.insert(0, str(REPO / "oracle"))
+    import numpy as np
+
+    import oracle as orc
+
+    mbg = H // 256 * 82 * F
+    mbd = F // 256 * 110 * H
+    experts = [(TYPE_IQ2_S, host0["gate"][e * mbg:(e + 1) * mbg], TYPE_IQ2_S, host0["up"][e * mbg:(e + 1) * mbg],
+                TYPE_IQ3_S, host0["down"][e * mbd:(e + 1) * mbd], H, F) for e in range(E)]
+    s = host0["shared"]
+    shared = (TYPE_Q4_K, s[0], TYPE_Q4_K, s[1], TYPE_Q4_K, s[2], H, F)
+    table = orc.ExpertTable(experts, shared, router=host0["router"], hidden=H)
+    bias = np.zeros(E, np.float32)
+    threads = orc.hw_threads()
+    orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs_host[0], preflight=True, simd=True, threads=threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs_host[(n + 1) % len(xs_host)], preflight=True, simd=True,
+                      threads=threads)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s or n >= 2000:
+            break
+    return {"value": n / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} tokens through layer 0, moe_routed_by_id_into as-is (preflight + accept), AVX2 restatement"}
+
+
+def our_arm(args, rank: int, world: int, local_rank: int) -> None:
+    import numpy as np
+    import torch
+
+    import lbk
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+
+        dist = dist_mod
+    ctx = lbk.Context(local_rank)
+    tables, host0 = build_layers(ctx, lbk, torch, dev, LAYERS, 4 + 97 * rank, keep_gguf_layer0=(rank == 0 and world == 1))
+    ws_bytes = tables[0][0].workspace_bytes(1)
+    wss = [torch.zeros(ws_bytes, dtype=torch.uint8, device=dev) for _ in tables]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 + rank)
+    xs = torch.randn(TOKENS_PER_STEP, H, device=dev, generator=gen)
+    outs = torch.zeros(TOKENS_PER_STEP, H, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step_calls(s):
+        for t in range(TOKENS_PER_STEP):
+            layer = tables[t % LAYERS][0]
+            layer.forward(xs[t], 1, outs[t], wss[t % LAYERS], stream=s.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        step_calls(stream)  # warm: sets kernel attributes outside capture
+    torch.cuda.synchronize()
+    ctx.raise_status(stream.cuda_stream)
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_calls(stream)
+    torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    ctx.raise_status(stream.cuda_stream)
+
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ctx.raise_status(stream.cuda_stream)
+    tokens_total = args.steps * TOKENS_PER_STEP * world
+    value = tokens_total / (ms / 1000.0)
+
+    # per-kernel times: a traced copy of one step, replayed with a sync each time
+    for layer, _ in tables:
+        layer.trace(True)
+    tgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(tgraph, stream=stream):
+        for t in range(LAYERS):
+            tables[t][0].forward(xs[t], 1, outs[t], wss[t], stream=stream.cuda_stream)
+    sums = [0.0, 0.0, 0.0]
+    reps = 64
+    for _ in range(reps):
+        tgraph.replay()
+        torch.cuda.synchronize()
+        for layer, _ in tables:
+            r = layer.trace_read()
+            for i in range(3):
+                sums[i] += r[i]
+    n_traced = reps * LAYERS
+    avg = [s / n_traced for s in sums]  # ms: router, gate/up, down
+    for layer, _ in tables:
+        layer.trace(False)
+    del tgraph
+    kernels = [("router_fused", ROUTER_B + X_B, avg[0]), ("moe_gate_up", GATE_UP_B, avg[1]),
+               ("moe_down", DOWN_B + OUT_B, avg[2])]
+    dom = max(kernels, key=lambda k: k[2])
+    peak, peak_kind = peaks()
+    achieved = dom[1] / (dom[2] / 1000.0) / 1e9
+    traffic = profiled_traffic(dom[0])
+
+    # e2e: per-token C-ABI calls, step inputs from pinned host, outputs read back
+    x_host = torch.randn(TOKENS_PER_STEP, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
+    o_host = torch.zeros(TOKENS_PER_STEP, H).pin_memory()
+    e2e_steps = max(1, min(args.steps, 20))
+    with torch.cuda.stream(stream):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            xs.copy_(x_host, non_blocking=True)
+            step_calls(stream)
+            o_host.copy_(outs, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    e2e_ms = max(e0.elapsed_time(e1), wall * 1000.0)
+    if dist:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = e2e_steps * TOKENS_PER_STEP * world / (e2e_ms / 1000.0)
+    ctx.raise_status(stream.cuda_stream)
+
+    cpu = None
+    if rank == 0 and world == 1 and host0 is not None and not args.no_cpu_baseline:
+        cpu = cpu_baseline(host0, x_host.numpy()[:16])
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q8_k x packed (int8 dots, f32 tails)",
+            "data": "synthetic (seeded, config shapes)",
+            "config": {
+                "workload": "config3: routed-MoE FFN layer, single-token decode",
+                "hidden": H, "experts": E, "expert_ffn": F, "top_k": K_TOP,
+                "gate_up": "IQ2_S", "down": "IQ3_S", "shared": "Q4_K", "router": "F32 (tree order)",
+                "tokens_per_step": TOKENS_PER_STEP, "resident_layers": LAYERS,
+                "l2": f"inputs larger than L2: tokens rotate over {LAYERS} resident layers ({LAYERS * 1.3:.1f} GB)",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "algorithmic_bytes_per_token": LAYER_B,
+            },
+            "hbm_gbs_achieved": LAYER_B * tokens_total / (ms / 1000.0) / 1e9 / world,
+            "kernel_ms": {"router_fused": avg[0], "moe_gate_up": avg[1], "moe_down": avg[2]},
+            "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": dom[1]},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": TOKENS_PER_STEP * H * 4,
+                    "d2h_bytes_per_step": TOKENS_PER_STEP * H * 4},
+            "gpu_launches": args.steps * TOKENS_PER_STEP * 3,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    for layer, _ in tables:
+        layer.close()
+    ctx.close()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    try:
+        our_arm(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

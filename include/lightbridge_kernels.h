@@ -218,44 +218,75 @@ int32_t lbk_route_topk(lbk_context* ctx, const float* logits, const float* selec
                        lbk_routed* routed, void* stream);
 
 /* SwiGLU expert, accumulated: dst += coefficient * down(swiglu(gate x, up x)).
- * reference: expert_swiglu_accumulate_into, activation.rs:104-144. */
+ * reference: expert_swiglu_accumulate_into, activation.rs:104-144.
+ * Workspace: lbk_expert_workspace_bytes. */
+int32_t lbk_expert_workspace_bytes(const lbk_expert* expert, uint64_t* bytes);
 int32_t lbk_expert_swiglu_accumulate(lbk_context* ctx, const lbk_expert* expert, const float* x,
                                      float* dst, float coefficient, void* workspace,
                                      uint64_t workspace_bytes, void* stream);
 
 /* --------------------------------------------------------- MoE layer */
 
-/* One layer's resident expert table. All matrices must share one layout. */
+/* One layer's expert table, mirroring Hy3MoeWeights
+ * (bridge-kernels-reference/src/layer.rs:28-36). Routed expert e's gate, up
+ * and down matrices are experts[e]; the matrices stay resident in device
+ * memory for the life of the layer handle. */
 typedef struct lbk_moe_weights {
     const lbk_expert* experts;   /* host array of expert_count descriptors */
     uint64_t expert_count;
     lbk_expert shared;           /* always-on shared expert, coefficient 1.0 */
     lbk_matrix router;           /* F32 [hidden, expert_count] */
     const float* selection_bias; /* device, expert_count floats */
-    uint32_t top_k;
+    uint32_t top_k;              /* expert_used_count */
     float weight_scale;          /* Hy3 expert_weights_scale (2.826 default) */
 } lbk_moe_weights;
 
-/* Workspace bytes needed by lbk_moe_layer for `tokens` tokens. */
-int32_t lbk_moe_workspace_bytes(const lbk_moe_weights* w, uint64_t tokens, uint64_t* bytes);
+typedef struct lbk_moe_layer lbk_moe_layer;
 
-/* Full routed-MoE FFN for `tokens` tokens: router logits, top-k routing, then
- * out[t] = sum over routed experts in ascending ID of coef * expert(x[t]),
- * then + 1.0 * shared(x[t]) -- the combine order of moe_routed_by_id_into
- * (bridge-kernels-reference/src/moe.rs:64-147) and the route/finish pair
- * hy3_moe_route_token / hy3_moe_finish_token (layer.rs:473-659) minus the
- * norm and residual. `routed_out` (device, tokens*top_k, may be NULL)
- * receives the routing. */
-int32_t lbk_moe_layer(lbk_context* ctx, const lbk_moe_weights* w, const float* x, uint64_t tokens,
-                      float* out, lbk_routed* routed_out, int32_t router_mode, void* workspace,
-                      uint64_t workspace_bytes, void* stream);
+/* Registers a layer's resident expert table: checks every shape and type
+ * (SwiGluExpert::new, activation.rs:13-22; widths of moe.rs:272-314), scans
+ * every binary16 scale once (validate_scales, k_quants.rs:178-208) -- the
+ * reference re-validates every row on every call (gemv.rs:268-270); here that
+ * happens once at registration -- uploads the expert pointer table, and picks
+ * the fused sm_100a kernels when every matrix is in the planar layout with a
+ * supported type combination (else the per-expert kernels). Synchronizes
+ * `stream`. Not on the hot path. */
+int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w, void* stream, lbk_moe_layer** out);
+int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer);
+/* 1 when the fused kernels are used, 0 for the per-expert path. */
+int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer);
 
-/* Same combine for a caller-supplied routing (device `routed`, tokens*k entries,
- * IDs strictly ascending per token, finite coefficients).
- * reference: moe_routed_by_id_into, moe.rs:64-147. */
-int32_t lbk_moe_routed(lbk_context* ctx, const lbk_moe_weights* w, const float* x, uint64_t tokens,
-                       const lbk_routed* routed, uint32_t k, float* out, void* workspace,
-                       uint64_t workspace_bytes, void* stream);
+/* Workspace bytes for `tokens` tokens. The workspace must be zero-filled once
+ * before its first use; every call leaves it ready for the next one. */
+int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes);
+
+/* Full routed-MoE FFN for `tokens` tokens (x: tokens*hidden f32): router
+ * logits, top-k routing, then per token
+ *   out = 0; out += coef_e * expert_e(x) for routed e in ascending ID;
+ *   out += 1.0 * shared(x)
+ * -- the combine order of moe_routed_by_id_into
+ * (bridge-kernels-reference/src/moe.rs:64-147); together this is
+ * hy3_moe_route_token + hy3_moe_finish_token (layer.rs:473-659) without the
+ * FFN norm and the residual add. `routed_out` (device, tokens*top_k entries,
+ * may be NULL) receives the routing. */
+int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
+                        lbk_routed* routed_out, int32_t router_mode, void* workspace,
+                        uint64_t workspace_bytes, void* stream);
+
+/* Kernel-level tracing: while enabled, lbk_moe_forward records CUDA events
+ * around its router, gate/up and down launches (three event records per call;
+ * they are captured into CUDA graphs like the launches).
+ * lbk_moe_layer_trace_read returns the three durations of the most recent
+ * traced call (ms), after synchronizing on its last event. */
+int32_t lbk_moe_layer_trace(lbk_moe_layer* layer, int32_t enable);
+int32_t lbk_moe_layer_trace_read(lbk_moe_layer* layer, float ms[3]);
+
+/* Same combine for a caller-supplied routing (device `routed`, tokens*top_k
+ * entries, IDs strictly ascending per token, finite coefficients; checked on
+ * the device, reported through the status word). reference:
+ * moe_routed_by_id_into, moe.rs:64-147. */
+int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, const lbk_routed* routed,
+                       float* out, void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------- layout tools */
 

@@ -1,0 +1,914 @@
+// abi.cu -- the C ABI (include/lightbridge_kernels.h): contexts, host-side
+// validation in the reference's order, and the launch sequences.
+//
+// Host validation mirrors the reference's checks so that a caller sees the
+// same error for the same bad input: PackedMatrix / EncodedTensorView
+// (bridge-kernels-reference/src/matrix.rs:26-150), required_q8_k_bytes
+// (gemv.rs:18-31), prepare_llama_q8k (gemv.rs:245-272), quantize_row_q8_k_into
+// (bridge-quant-layout/src/q8_k.rs:16-33), vec_dot validation (q8_k.rs:121-161),
+// route_experts_into (bridge-model-hy3/src/routing.rs:25-56), SwiGluExpert::new
+// (activation.rs:13-22) and the MoE structure checks (moe.rs:64-129).
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <set>
+#include <utility>
+#include <vector>
+
+#include "lbk_iq_tables.h"
+#include "lbk_kernels.h"
+#include "lbk_moe.h"
+
+#define LBK_API extern "C" __attribute__((visibility("default")))
+
+struct lbk_context {
+    int device;
+    int sm_count;
+    lbk::DeviceStatus* status;          // device
+    unsigned long long* scratch_min;    // device, 8 bytes
+    uint64_t* iq2s;                     // device, 1024
+    uint32_t* iq3s;                     // device, 512
+    lbk::Tables tables() const { return lbk::Tables{iq2s, iq3s}; }
+};
+
+struct lbk_moe_layer {
+    lbk_context* ctx;
+    uint64_t E, H, F, k;
+    float weight_scale;
+    bool fused;
+    lbk_moe_weights w;                   // host copy (experts pointer not kept)
+    std::vector<lbk_expert> experts;     // host copy of the expert descriptors
+    const uint8_t** d_gate;              // device pointer tables [E]
+    const uint8_t** d_up;
+    const uint8_t** d_down;
+    int gate_type, down_type, sgate_type, sdown_type;
+    cudaEvent_t trace[4];
+    bool tracing;
+};
+
+namespace {
+
+thread_local lbk_error_detail g_err;
+
+int32_t ok() {
+    std::memset(&g_err, 0, sizeof(g_err));
+    return LBK_OK;
+}
+
+int32_t fail(int32_t status, const char* msg, uint64_t index = 0, uint64_t expected = 0, uint64_t actual = 0,
+             uint32_t bits = 0) {
+    std::memset(&g_err, 0, sizeof(g_err));
+    g_err.status = status;
+    g_err.index = index;
+    g_err.expected = expected;
+    g_err.actual = actual;
+    g_err.bits = bits;
+    std::snprintf(g_err.message, sizeof(g_err.message), "%s", msg);
+    return status;
+}
+
+int32_t cuda_fail(cudaError_t e, const char* where) {
+    int32_t s = fail(LBK_CUDA_ERROR, where);
+    g_err.cuda_error = (int32_t)e;
+    std::snprintf(g_err.message, sizeof(g_err.message), "%s: %s", where, cudaGetErrorString(e));
+    return s;
+}
+
+uint32_t f32_bits(float v) {
+    uint32_t b;
+    std::memcpy(&b, &v, 4);
+    return b;
+}
+
+uint64_t block_bytes(int32_t ty) {
+    switch (ty) {
+        case LBK_TYPE_F32: return 4;
+        case LBK_TYPE_Q4_K: return 144;
+        case LBK_TYPE_Q5_K: return 176;
+        case LBK_TYPE_IQ2_S: return 82;
+        case LBK_TYPE_IQ3_S: return 110;
+        default: return 0;
+    }
+}
+
+bool dot_type(int32_t ty) {
+    return ty == LBK_TYPE_Q4_K || ty == LBK_TYPE_Q5_K || ty == LBK_TYPE_IQ2_S || ty == LBK_TYPE_IQ3_S;
+}
+
+bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p & (a - 1)) == 0; }
+
+// PackedMatrix::new (matrix.rs:26-150) for a descriptor.
+int32_t check_matrix(const lbk_matrix* m, const char* what) {
+    if (m == nullptr) return fail(LBK_INVALID_PARAMETER, what);
+    uint64_t bb = block_bytes(m->type);
+    if (bb == 0) return fail(LBK_UNSUPPORTED_TYPE, "unsupported GGML type", (uint64_t)m->type);
+    if (m->layout != LBK_LAYOUT_GGUF && m->layout != LBK_LAYOUT_PLANAR)
+        return fail(LBK_INVALID_PARAMETER, "unknown layout", (uint64_t)m->layout);
+    if (m->layout == LBK_LAYOUT_PLANAR && m->type == LBK_TYPE_F32)
+        return fail(LBK_INVALID_PARAMETER, "F32 matrices have no planar layout");
+    if (m->input_width == 0 || m->output_width == 0) return fail(LBK_DIMENSION_MISMATCH, "zero tensor dimension");
+    uint64_t be = m->type == LBK_TYPE_F32 ? 1 : LBK_QK_K;
+    if (m->input_width % be != 0)
+        return fail(LBK_DIMENSION_MISMATCH, "block-aligned matrix input width", 0, be, m->input_width);
+    uint64_t nb = m->input_width / be;
+    if (nb > UINT64_MAX / bb || nb * bb > UINT64_MAX / m->output_width)
+        return fail(LBK_ARITHMETIC_OVERFLOW, "tensor encoded byte length");
+    uint64_t expected = nb * bb * m->output_width;
+    if (m->bytes != expected) return fail(LBK_ENCODED_LENGTH_MISMATCH, "tensor encoded length", 0, expected, m->bytes);
+    if (m->data == nullptr) return fail(LBK_INVALID_PARAMETER, "null matrix data");
+    if (!aligned(m->data, 16)) return fail(LBK_INVALID_PARAMETER, "matrix data must be 16-byte aligned");
+    return LBK_OK;
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int32_t set_device(lbk_context* ctx) {
+    cudaError_t e = cudaSetDevice(ctx->device);
+    return e == cudaSuccess ? LBK_OK : cuda_fail(e, "cudaSetDevice");
+}
+
+lbk::MatrixRef mref(const lbk_matrix* m) {
+    return lbk::MatrixRef{reinterpret_cast<const uint8_t*>(m->data), m->output_width, (int)(m->input_width / LBK_QK_K)};
+}
+
+// Common GEMV launch (quantized matrices).
+int32_t run_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, const uint8_t* q8_in, uint8_t* q8_out,
+                 float* y, float scale, int mode, int32_t* block_sums, const uint8_t* const* mat_table,
+                 const lbk_routed* sel, cudaStream_t stream, uint64_t mat_count = 0) {
+    lbk::GemvArgs a{};
+    a.mat_count = mat_count;
+    a.w = mref(w);
+    a.x = x;
+    a.q8_in = q8_in;
+    a.q8_out = q8_out;
+    a.y = y;
+    a.scale = scale;
+    a.mode = mode;
+    a.block_sums = block_sums;
+    a.mat_table = mat_table;
+    a.sel = sel;
+    a.status = ctx->status;
+    a.tables = ctx->tables();
+    lbk::gemv_plan(w->type, a.w.nb, &a.tpr, &a.tail_slots);
+    if (lbk::gemv_smem_required(w->type, a.w.nb, a.tail_slots) > lbk::kMaxSmem)
+        return fail(LBK_INVALID_PARAMETER, "input_width too large for the shared-memory activation image", 0, 0,
+                    (uint64_t)a.w.nb * LBK_QK_K);
+    cudaError_t e = lbk::launch_gemv(w->type, w->layout, a, ctx->sm_count, stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "gemv launch");
+}
+
+int32_t run_f32_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, uint64_t tokens, float* y,
+                     cudaStream_t stream) {
+    lbk::RouterArgs r{};
+    r.w = reinterpret_cast<const float*>(w->data);
+    r.x = x;
+    r.logits = y;
+    r.hidden = w->input_width;
+    r.experts = w->output_width;
+    r.tokens = tokens;
+    r.status = ctx->status;
+    cudaError_t e = lbk::launch_router(r, LBK_ROUTER_SEQUENTIAL, ctx->sm_count, stream);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "router launch");
+}
+
+struct WsLayout {
+    uint64_t logits, partials, q8x, routed, h, hq, counters, g, u, total;
+};
+
+uint64_t up256(uint64_t v) { return (v + 255) & ~(uint64_t)255; }
+
+WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T) {
+    WsLayout o{};
+    uint64_t off = 0;
+    uint64_t slots = T * (L->k + 1);
+    uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
+    o.counters = off;  // first, so that a zero-filled prefix covers them
+    off = up256(off + slots * nbf * 4 + 4);
+    o.logits = off;
+    off = up256(off + T * L->E * 4);
+    o.partials = off;
+    off = up256(off + lbk::router_partials_floats(L->H, L->E, T) * 4);
+    o.q8x = off;
+    off = up256(off + T * nbh * LBK_Q8K_BLOCK_BYTES);
+    o.routed = off;
+    off = up256(off + T * L->k * sizeof(lbk_routed));
+    o.h = off;
+    off = up256(off + slots * L->F * 4);
+    o.hq = off;
+    off = up256(off + slots * nbf * LBK_Q8K_BLOCK_BYTES);
+    o.g = off;  // per-expert path: gate / up scratch, q8 scratch
+    off = up256(off + L->F * 4);
+    o.u = off;
+    off = up256(off + L->F * 4 + (L->F > L->H ? L->F : L->H) / LBK_QK_K * LBK_Q8K_BLOCK_BYTES);
+    o.total = off;
+    return o;
+}
+
+__global__ void check_routed_kernel(const lbk_routed* routed, uint64_t tokens, uint64_t k, uint64_t experts,
+                                    lbk::DeviceStatus* st) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < tokens; t += (uint64_t)gridDim.x * blockDim.x) {
+        const lbk_routed* r = routed + t * k;
+        for (uint64_t i = 0; i < k; i++) {  // moe.rs:282-304
+            float c = r[i].coefficient;
+            if (!isfinite(c)) {
+                lbk::report(st, LBK_NON_FINITE_VALUE, t * k + i, __float_as_uint(c));
+                return;
+            }
+            if (i > 0 && r[i].expert_id == r[i - 1].expert_id) {
+                lbk::report(st, LBK_DUPLICATE_ROUTED_EXPERT, r[i].expert_id, 0);
+                return;
+            }
+            if (i > 0 && r[i].expert_id < r[i - 1].expert_id) {
+                lbk::report(st, LBK_ROUTED_EXPERT_ORDER, r[i].expert_id, r[i - 1].expert_id);
+                return;
+            }
+            if (r[i].expert_id >= experts) {
+                lbk::report(st, LBK_INVALID_PARAMETER, r[i].expert_id, 0);
+                return;
+            }
+        }
+    }
+}
+
+__global__ void fill_zero_kernel(float* p, uint64_t n, const lbk::DeviceStatus* st) {
+    if (lbk::status_set(st)) return;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        p[i] = 0.0f;
+}
+
+std::mutex g_attr_mu;
+std::set<std::pair<int, const void*>> g_attr_done;
+
+}  // namespace
+
+namespace lbk {
+cudaError_t ensure_max_smem(const void* kernel) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (g_attr_done.count({dev, kernel})) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    if (e == cudaSuccess) g_attr_done.insert({dev, kernel});
+    return e;
+}
+}  // namespace lbk
+
+// ===================================================================== ABI
+
+LBK_API int32_t lbk_abi_version(void) { return LBK_ABI_VERSION; }
+
+LBK_API const char* lbk_backend_name(void) { return "cuda_sm100a_q8_k"; }
+
+LBK_API void lbk_last_error_detail(lbk_error_detail* out) {
+    if (out) *out = g_err;
+}
+
+LBK_API int32_t lbk_context_create(int32_t device, lbk_context** out) {
+    if (out == nullptr) return fail(LBK_INVALID_PARAMETER, "null output pointer");
+    *out = nullptr;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) return fail(LBK_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= count) return fail(LBK_INVALID_PARAMETER, "device index", (uint64_t)device);
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10) return fail(LBK_NO_DEVICE, "this build targets sm_100a (B200)", 0, 100, (uint64_t)(prop.major * 10 + prop.minor));
+    lbk_context* c = new lbk_context{};
+    c->device = device;
+    c->sm_count = prop.multiProcessorCount;
+    void* p = nullptr;
+    if ((e = cudaMalloc(&p, sizeof(lbk::DeviceStatus) + 64 + sizeof(lbk_iq2s_grid) + sizeof(lbk_iq3s_grid))) != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "cudaMalloc context");
+    }
+    uint8_t* base = static_cast<uint8_t*>(p);
+    c->status = reinterpret_cast<lbk::DeviceStatus*>(base);
+    c->scratch_min = reinterpret_cast<unsigned long long*>(base + 32);
+    c->iq2s = reinterpret_cast<uint64_t*>(base + 64 + 32);
+    c->iq3s = reinterpret_cast<uint32_t*>(base + 64 + 32 + sizeof(lbk_iq2s_grid));
+    cudaMemset(base, 0, 96);
+    cudaMemcpy(c->iq2s, lbk_iq2s_grid, sizeof(lbk_iq2s_grid), cudaMemcpyHostToDevice);
+    if ((e = cudaMemcpy(c->iq3s, lbk_iq3s_grid, sizeof(lbk_iq3s_grid), cudaMemcpyHostToDevice)) != cudaSuccess) {
+        cudaFree(p);
+        delete c;
+        return cuda_fail(e, "upload codebooks");
+    }
+    *out = c;
+    return ok();
+}
+
+LBK_API int32_t lbk_context_destroy(lbk_context* ctx) {
+    if (ctx == nullptr) return ok();
+    cudaSetDevice(ctx->device);
+    cudaFree(ctx->status);
+    delete ctx;
+    return ok();
+}
+
+LBK_API int32_t lbk_context_sync_status(lbk_context* ctx, void* stream, lbk_error_detail* detail) {
+    if (ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null context");
+    if (int32_t s = set_device(ctx)) return s;
+    cudaError_t e = cudaStreamSynchronize(as_stream(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "stream synchronize");
+    lbk::DeviceStatus st;
+    if ((e = cudaMemcpy(&st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "read status");
+    if ((e = cudaMemset(ctx->status, 0, sizeof(st))) != cudaSuccess) return cuda_fail(e, "clear status");
+    lbk_error_detail d{};
+    d.status = st.status;
+    d.index = st.index;
+    d.bits = st.bits;
+    if (st.status != 0) std::snprintf(d.message, sizeof(d.message), "device-detected status %d", st.status);
+    if (detail) *detail = d;
+    g_err = d;
+    return st.status;
+}
+
+LBK_API int32_t lbk_required_q8k_bytes(uint64_t input_width, uint64_t* bytes) {
+    if (bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null output pointer");
+    if (input_width == 0 || input_width % LBK_QK_K != 0)
+        return fail(LBK_DIMENSION_MISMATCH, "Q8_K input width", 0, LBK_QK_K, input_width);
+    *bytes = input_width / LBK_QK_K * LBK_Q8K_BLOCK_BYTES;
+    return ok();
+}
+
+LBK_API int32_t lbk_matrix_bytes(int32_t type, uint64_t input_width, uint64_t output_width, uint64_t* bytes) {
+    if (bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null output pointer");
+    uint64_t bb = block_bytes(type);
+    if (bb == 0) return fail(LBK_UNSUPPORTED_TYPE, "unsupported GGML type", (uint64_t)type);
+    uint64_t be = type == LBK_TYPE_F32 ? 1 : LBK_QK_K;
+    if (input_width == 0 || output_width == 0 || input_width % be != 0)
+        return fail(LBK_DIMENSION_MISMATCH, "block-aligned matrix input width", 0, be, input_width);
+    *bytes = input_width / be * bb * output_width;
+    return ok();
+}
+
+LBK_API int32_t lbk_quantize_q8k(lbk_context* ctx, const float* x, uint64_t n, uint8_t* q8, uint64_t q8_bytes,
+                                 void* stream) {
+    if (n == 0) return fail(LBK_ZERO_LOGICAL_ELEMENTS, "a row must contain at least one logical element");
+    if (n % LBK_QK_K != 0) return fail(LBK_LOGICAL_ELEMENTS_NOT_DIVISIBLE, "logical elements not divisible", 0, LBK_QK_K, n);
+    uint64_t expected = n / LBK_QK_K * LBK_Q8K_BLOCK_BYTES;
+    if (q8_bytes != expected) return fail(LBK_ENCODED_LENGTH_MISMATCH, "Q8_K encoded row length", 0, expected, q8_bytes);
+    if (ctx == nullptr || x == nullptr || q8 == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(q8, 4)) return fail(LBK_INVALID_PARAMETER, "q8 must be 4-byte aligned");
+    if (int32_t s = set_device(ctx)) return s;
+    cudaError_t e = lbk::launch_quantize_q8k_ws(x, n, q8, ctx->scratch_min, ctx->status, ctx->sm_count, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "quantize launch");
+}
+
+LBK_API int32_t lbk_vec_dot_q8k(lbk_context* ctx, const lbk_matrix* w, const uint8_t* q8, uint64_t q8_bytes, float* out,
+                                int32_t* block_sums, void* stream) {
+    if (w == nullptr) return fail(LBK_INVALID_PARAMETER, "null matrix");
+    if (!dot_type(w->type)) return fail(LBK_UNSUPPORTED_TYPE, "unsupported dot type", (uint64_t)w->type);
+    if (w->input_width == 0) return fail(LBK_ZERO_LOGICAL_ELEMENTS, "zero logical elements");
+    if (w->input_width % LBK_QK_K != 0)
+        return fail(LBK_LOGICAL_ELEMENTS_NOT_DIVISIBLE, "logical elements not divisible", 0, LBK_QK_K, w->input_width);
+    if (int32_t s = check_matrix(w, "matrix")) return s;
+    uint64_t expected = w->input_width / LBK_QK_K * LBK_Q8K_BLOCK_BYTES;
+    if (q8_bytes != expected) return fail(LBK_ENCODED_LENGTH_MISMATCH, "packed dot Q8_K row length", 0, expected, q8_bytes);
+    if (ctx == nullptr || q8 == nullptr || out == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(q8, 4)) return fail(LBK_INVALID_PARAMETER, "q8 must be 4-byte aligned");
+    if (int32_t s = set_device(ctx)) return s;
+    return run_gemv(ctx, w, nullptr, q8, nullptr, out, 0.0f, lbk::kGemvStore, block_sums, nullptr, nullptr,
+                    as_stream(stream));
+}
+
+LBK_API int32_t lbk_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, float* y, uint8_t* q8_scratch,
+                         uint64_t q8_scratch_bytes, void* stream) {
+    if (int32_t s = check_matrix(w, "matrix")) return s;
+    if (x == nullptr || y == nullptr || ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (w->type == LBK_TYPE_F32) {  // gemv_into on an F32 matrix: sequential f32 rows (gemv.rs:96-105)
+        if (int32_t s = set_device(ctx)) return s;
+        return run_f32_gemv(ctx, w, x, 1, y, as_stream(stream));
+    }
+    if (w->input_width % LBK_QK_K != 0)
+        return fail(LBK_DIMENSION_MISMATCH, "Q8_K input width", 0, LBK_QK_K, w->input_width);
+    uint64_t required = w->input_width / LBK_QK_K * LBK_Q8K_BLOCK_BYTES;
+    if (q8_scratch != nullptr && q8_scratch_bytes < required)
+        return fail(LBK_SCRATCH_TOO_SMALL, "Q8_K row scratch", 0, required, q8_scratch_bytes);
+    if (!aligned(x, 16)) return fail(LBK_INVALID_PARAMETER, "x must be 16-byte aligned");
+    if (q8_scratch != nullptr && !aligned(q8_scratch, 4)) return fail(LBK_INVALID_PARAMETER, "q8 scratch must be 4-byte aligned");
+    if (int32_t s = set_device(ctx)) return s;
+    return run_gemv(ctx, w, x, nullptr, q8_scratch, y, 0.0f, lbk::kGemvStore, nullptr, nullptr, nullptr,
+                    as_stream(stream));
+}
+
+LBK_API int32_t lbk_gemv_accumulate_scaled(lbk_context* ctx, const lbk_matrix* w, const float* x, float* y, float scale,
+                                           uint8_t* q8_scratch, uint64_t q8_scratch_bytes, void* stream) {
+    if (!std::isfinite(scale)) return fail(LBK_NON_FINITE_VALUE, "accumulation scale", 0, 0, 0, f32_bits(scale));
+    if (int32_t s = check_matrix(w, "matrix")) return s;
+    if (x == nullptr || y == nullptr || ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (w->type == LBK_TYPE_F32) return fail(LBK_UNSUPPORTED_TYPE, "F32 accumulate is not on this path", LBK_TYPE_F32);
+    uint64_t required = w->input_width / LBK_QK_K * LBK_Q8K_BLOCK_BYTES;
+    if (q8_scratch != nullptr && q8_scratch_bytes < required)
+        return fail(LBK_SCRATCH_TOO_SMALL, "Q8_K row scratch", 0, required, q8_scratch_bytes);
+    if (!aligned(x, 16)) return fail(LBK_INVALID_PARAMETER, "x must be 16-byte aligned");
+    if (int32_t s = set_device(ctx)) return s;
+    return run_gemv(ctx, w, x, nullptr, q8_scratch, y, scale, lbk::kGemvAccumulate, nullptr, nullptr, nullptr,
+                    as_stream(stream));
+}
+
+LBK_API int32_t lbk_router_logits(lbk_context* ctx, const lbk_matrix* router, const float* x, uint64_t tokens,
+                                  float* logits, int32_t mode, void* stream) {
+    if (int32_t s = check_matrix(router, "router")) return s;
+    if (router->type != LBK_TYPE_F32) return fail(LBK_UNSUPPORTED_TYPE, "router must be F32", (uint64_t)router->type);
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    if (mode != LBK_ROUTER_SEQUENTIAL && mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "router mode");
+    if (ctx == nullptr || x == nullptr || logits == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (int32_t s = set_device(ctx)) return s;
+    if (mode == LBK_ROUTER_SEQUENTIAL) return run_f32_gemv(ctx, router, x, tokens, logits, as_stream(stream));
+    return fail(LBK_INVALID_PARAMETER, "tree order needs a workspace: use lbk_moe_forward");
+}
+
+LBK_API int32_t lbk_route_topk(lbk_context* ctx, const float* logits, const float* selection_bias, uint64_t expert_count,
+                               uint64_t tokens, uint32_t k, float weight_scale, lbk_routed* routed, void* stream) {
+    if (k == 0 || k > expert_count) return fail(LBK_ROUTING_TOPK, "expert_used_count", 0, expert_count, k);
+    if (!std::isfinite(weight_scale))
+        return fail(LBK_NON_FINITE_ROUTING_VALUE, "weight_scale", 0, 0, 0, f32_bits(weight_scale));
+    if (expert_count > 1024 || k > 32) return fail(LBK_INVALID_PARAMETER, "this build routes at most 1024 experts, k <= 32");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    if (ctx == nullptr || logits == nullptr || selection_bias == nullptr || routed == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (int32_t s = set_device(ctx)) return s;
+    lbk::TopkArgs a{logits, selection_bias, expert_count, tokens, k, weight_scale, routed, ctx->status};
+    cudaError_t e = lbk::launch_topk(a, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "top-k launch");
+}
+
+namespace {
+
+// SwiGluExpert::new (activation.rs:13-22) plus PackedMatrix checks.
+int32_t check_expert(const lbk_expert* ex) {
+    if (ex == nullptr) return fail(LBK_INVALID_PARAMETER, "null expert");
+    if (int32_t s = check_matrix(&ex->gate, "gate")) return s;
+    if (int32_t s = check_matrix(&ex->up, "up")) return s;
+    if (int32_t s = check_matrix(&ex->down, "down")) return s;
+    if (ex->gate.input_width != ex->up.input_width)
+        return fail(LBK_DIMENSION_MISMATCH, "SwiGLU gate/up input width", 0, ex->gate.input_width, ex->up.input_width);
+    if (ex->gate.output_width != ex->up.output_width)
+        return fail(LBK_DIMENSION_MISMATCH, "SwiGLU gate/up hidden width", 0, ex->gate.output_width, ex->up.output_width);
+    if (ex->gate.output_width != ex->down.input_width)
+        return fail(LBK_DIMENSION_MISMATCH, "SwiGLU down input width", 0, ex->gate.output_width, ex->down.input_width);
+    for (const lbk_matrix* m : {&ex->gate, &ex->up, &ex->down})
+        if (!dot_type(m->type)) return fail(LBK_UNSUPPORTED_TYPE, "expert matrices must be quantized", (uint64_t)m->type);
+    return LBK_OK;
+}
+
+// gate/up GEMVs, SwiGLU and the scaled down accumulation for one expert
+// (activation.rs:104-144); the expert may be selected on the device.
+int32_t expert_accumulate(lbk_context* ctx, const lbk_expert* ex, const float* x, float* dst, float coef, float* g,
+                          float* u, uint8_t* q8, const uint8_t* const* tg, const uint8_t* const* tu,
+                          const uint8_t* const* td, const lbk_routed* sel, cudaStream_t stream,
+                          uint64_t table_count = 0) {
+    if (int32_t s = run_gemv(ctx, &ex->gate, x, nullptr, q8, g, 0.0f, lbk::kGemvStore, nullptr, tg, sel, stream,
+                             table_count))
+        return s;
+    if (int32_t s = run_gemv(ctx, &ex->up, x, nullptr, q8, u, 0.0f, lbk::kGemvStore, nullptr, tu, sel, stream,
+                             table_count))
+        return s;
+    cudaError_t e = lbk::launch_swiglu(g, u, g, ex->gate.output_width, ctx->status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "swiglu launch");
+    return run_gemv(ctx, &ex->down, g, nullptr, q8, dst, coef, lbk::kGemvAccumulate, nullptr, td, sel, stream,
+                    table_count);
+}
+
+}  // namespace
+
+LBK_API int32_t lbk_expert_workspace_bytes(const lbk_expert* expert, uint64_t* bytes) {
+    if (bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null output pointer");
+    if (int32_t s = check_expert(expert)) return s;
+    uint64_t F = expert->gate.output_width, H = expert->gate.input_width;
+    uint64_t w = (F > H ? F : H) / LBK_QK_K;
+    *bytes = up256(F * 4) * 2 + up256(w * LBK_Q8K_BLOCK_BYTES);
+    return ok();
+}
+
+LBK_API int32_t lbk_expert_swiglu_accumulate(lbk_context* ctx, const lbk_expert* expert, const float* x, float* dst,
+                                             float coefficient, void* workspace, uint64_t workspace_bytes,
+                                             void* stream) {
+    if (!std::isfinite(coefficient))
+        return fail(LBK_NON_FINITE_VALUE, "expert coefficient", 0, 0, 0, f32_bits(coefficient));
+    if (int32_t s = check_expert(expert)) return s;
+    uint64_t need = 0;
+    lbk_expert_workspace_bytes(expert, &need);
+    if (workspace_bytes < need) return fail(LBK_SCRATCH_TOO_SMALL, "SwiGLU gate/up", 0, need, workspace_bytes);
+    if (ctx == nullptr || x == nullptr || dst == nullptr || workspace == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(x, 16) || !aligned(workspace, 256)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
+    if (int32_t s = set_device(ctx)) return s;
+    uint64_t F = expert->gate.output_width;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* g = reinterpret_cast<float*>(ws);
+    float* u = reinterpret_cast<float*>(ws + up256(F * 4));
+    uint8_t* q8 = ws + 2 * up256(F * 4);
+    return expert_accumulate(ctx, expert, x, dst, coefficient, g, u, q8, nullptr, nullptr, nullptr, nullptr,
+                             as_stream(stream));
+}
+
+// ------------------------------------------------------------- MoE layer
+
+LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w, void* stream, lbk_moe_layer** out) {
+    if (out == nullptr || w == nullptr || ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    *out = nullptr;
+    if (w->expert_count == 0 || w->experts == nullptr) return fail(LBK_DIMENSION_MISMATCH, "expert count", 0, 1, 0);
+    if (int32_t s = check_expert(&w->shared)) return s;
+    if (int32_t s = check_matrix(&w->router, "router")) return s;
+    if (w->router.type != LBK_TYPE_F32) return fail(LBK_UNSUPPORTED_TYPE, "router must be F32", (uint64_t)w->router.type);
+    const uint64_t H = w->shared.gate.input_width, F = w->shared.gate.output_width, E = w->expert_count;
+    if (w->router.input_width != H) return fail(LBK_DIMENSION_MISMATCH, "router input width", 0, H, w->router.input_width);
+    if (w->router.output_width != E) return fail(LBK_DIMENSION_MISMATCH, "router output width", 0, E, w->router.output_width);
+    if (w->shared.down.output_width != H) return fail(LBK_DIMENSION_MISMATCH, "MoE output", 0, H, w->shared.down.output_width);
+    if (w->top_k == 0 || w->top_k > E) return fail(LBK_ROUTING_TOPK, "expert_used_count", 0, E, w->top_k);
+    if (!std::isfinite(w->weight_scale))
+        return fail(LBK_NON_FINITE_ROUTING_VALUE, "weight_scale", 0, 0, 0, f32_bits(w->weight_scale));
+    if (E > 1024 || w->top_k > 32) return fail(LBK_INVALID_PARAMETER, "this build routes at most 1024 experts, k <= 32");
+    if (w->selection_bias == nullptr) return fail(LBK_INVALID_PARAMETER, "null selection bias");
+    if (H % LBK_QK_K != 0 || F % LBK_QK_K != 0) return fail(LBK_DIMENSION_MISMATCH, "Q8_K input width", 0, LBK_QK_K, H);
+    for (uint64_t e = 0; e < E; e++) {
+        const lbk_expert* ex = &w->experts[e];
+        if (int32_t s = check_expert(ex)) {
+            g_err.index = e;
+            return s;
+        }
+        if (ex->gate.input_width != H) return fail(LBK_DIMENSION_MISMATCH, "routed expert input width", e, H, ex->gate.input_width);
+        if (ex->down.output_width != H) return fail(LBK_DIMENSION_MISMATCH, "routed expert output width", e, H, ex->down.output_width);
+        if (ex->gate.output_width != F) return fail(LBK_DIMENSION_MISMATCH, "routed expert hidden width", e, F, ex->gate.output_width);
+    }
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+
+    auto* L = new lbk_moe_layer{};
+    L->ctx = ctx;
+    L->E = E;
+    L->H = H;
+    L->F = F;
+    L->k = w->top_k;
+    L->weight_scale = w->weight_scale;
+    L->w = *w;
+    L->experts.assign(w->experts, w->experts + E);
+    L->w.experts = nullptr;
+    L->gate_type = w->experts[0].gate.type;
+    L->down_type = w->experts[0].down.type;
+    L->sgate_type = w->shared.gate.type;
+    L->sdown_type = w->shared.down.type;
+    bool uniform = true, planar = w->shared.gate.layout == LBK_LAYOUT_PLANAR && w->shared.up.layout == LBK_LAYOUT_PLANAR &&
+                                  w->shared.down.layout == LBK_LAYOUT_PLANAR && w->shared.up.type == w->shared.gate.type;
+    bool same_layout = true;
+    for (uint64_t e = 0; e < E; e++) {
+        const lbk_expert& ex = w->experts[e];
+        uniform &= ex.gate.type == L->gate_type && ex.up.type == w->experts[0].up.type && ex.down.type == L->down_type;
+        planar &= ex.gate.layout == LBK_LAYOUT_PLANAR && ex.up.layout == LBK_LAYOUT_PLANAR && ex.down.layout == LBK_LAYOUT_PLANAR;
+        same_layout &= ex.gate.layout == w->experts[0].gate.layout && ex.up.layout == w->experts[0].up.layout &&
+                       ex.down.layout == w->experts[0].down.layout;
+    }
+    // Routed experts are slices of one stacked tensor per projection in the
+    // reference schema (bridge-model-hy3/src/schema.rs:219-243), so they share
+    // types and layouts; the device-side expert selection relies on it.
+    if (!uniform || !same_layout) {
+        delete L;
+        return fail(LBK_INVALID_PARAMETER, "routed experts must share each projection's type and layout");
+    }
+    uniform &= w->experts[0].up.type == L->gate_type;
+    L->fused = uniform && planar && lbk::moe_fused_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type) &&
+               L->k + 1 <= 18;
+
+    std::vector<const uint8_t*> ptrs(3 * E);
+    for (uint64_t e = 0; e < E; e++) {
+        ptrs[e] = static_cast<const uint8_t*>(w->experts[e].gate.data);
+        ptrs[E + e] = static_cast<const uint8_t*>(w->experts[e].up.data);
+        ptrs[2 * E + e] = static_cast<const uint8_t*>(w->experts[e].down.data);
+    }
+    void* d = nullptr;
+    cudaError_t e = cudaMalloc(&d, 3 * E * sizeof(void*));
+    if (e != cudaSuccess) {
+        delete L;
+        return cuda_fail(e, "cudaMalloc expert table");
+    }
+    L->d_gate = static_cast<const uint8_t**>(d);
+    L->d_up = L->d_gate + E;
+    L->d_down = L->d_gate + 2 * E;
+    e = cudaMemcpyAsync(d, ptrs.data(), 3 * E * sizeof(void*), cudaMemcpyHostToDevice, st);
+    // One scale scan per matrix (validate_scales), results gathered at the sync.
+    auto scan = [&](const lbk_matrix& m) {
+        if (e != cudaSuccess) return;
+        e = lbk::launch_validate_scales(m.type, m.layout, static_cast<const uint8_t*>(m.data), m.output_width,
+                                        (int)(m.input_width / LBK_QK_K), ctx->scratch_min, ctx->status, st);
+    };
+    for (uint64_t x = 0; x < E; x++) {
+        scan(w->experts[x].gate);
+        scan(w->experts[x].up);
+        scan(w->experts[x].down);
+    }
+    scan(w->shared.gate);
+    scan(w->shared.up);
+    scan(w->shared.down);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        delete L;
+        return cuda_fail(e, "layer registration");
+    }
+    lbk_error_detail det{};
+    int32_t s = lbk_context_sync_status(ctx, stream, &det);
+    if (s != LBK_OK) {
+        cudaFree(d);
+        delete L;
+        g_err = det;
+        return s;
+    }
+    *out = L;
+    return ok();
+}
+
+LBK_API int32_t lbk_moe_layer_trace(lbk_moe_layer* layer, int32_t enable) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (int32_t s = set_device(layer->ctx)) return s;
+    if (enable && !layer->tracing) {
+        for (int i = 0; i < 4; i++) {
+            cudaError_t e = cudaEventCreate(&layer->trace[i]);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+        }
+        layer->tracing = true;
+    } else if (!enable && layer->tracing) {
+        for (int i = 0; i < 4; i++) cudaEventDestroy(layer->trace[i]);
+        layer->tracing = false;
+    }
+    return ok();
+}
+
+LBK_API int32_t lbk_moe_layer_trace_read(lbk_moe_layer* layer, float ms[3]) {
+    if (layer == nullptr || ms == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!layer->tracing) return fail(LBK_INVALID_PARAMETER, "tracing is not enabled");
+    if (int32_t s = set_device(layer->ctx)) return s;
+    cudaError_t e = cudaEventSynchronize(layer->trace[3]);
+    for (int i = 0; i < 3 && e == cudaSuccess; i++) e = cudaEventElapsedTime(&ms[i], layer->trace[i], layer->trace[i + 1]);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "trace read");
+}
+
+LBK_API int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer) {
+    if (layer == nullptr) return ok();
+    cudaSetDevice(layer->ctx->device);
+    lbk_moe_layer_trace(layer, 0);
+    cudaFree(layer->d_gate);
+    delete layer;
+    return ok();
+}
+
+LBK_API int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer) { return layer && layer->fused ? 1 : 0; }
+
+LBK_API int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes) {
+    if (layer == nullptr || bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    *bytes = moe_ws(layer, tokens).total;
+    return ok();
+}
+
+namespace {
+
+// Expert stage of one MoE call for `tokens` tokens with routing in `routed`.
+int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_routed* routed, float* out, uint8_t* ws,
+                    const WsLayout& o, cudaStream_t st) {
+    lbk_context* ctx = L->ctx;
+    cudaError_t e = cudaSuccess;
+    const uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
+    if (L->fused) {
+        lbk::MoeGateUpArgs g{};
+        g.hidden = L->H;
+        g.ffn = L->F;
+        g.nb_h = (int)nbh;
+        g.nb_f = (int)nbf;
+        int slots_unused = 0;
+        lbk::gemv_plan(L->gate_type, (int)nbh, &g.tpr_h, &slots_unused);
+        g.tokens = T;
+        g.k = L->k;
+        g.experts = L->E;
+        g.gate = L->d_gate;
+        g.up = L->d_up;
+        g.sgate = static_cast<const uint8_t*>(L->w.shared.gate.data);
+        g.sup = static_cast<const uint8_t*>(L->w.shared.up.data);
+        g.routed = routed;
+        g.q8x = ws + o.q8x;
+        g.h = reinterpret_cast<float*>(ws + o.h);
+        g.hq = ws + o.hq;
+        g.counters = reinterpret_cast<unsigned int*>(ws + o.counters);
+        // Balance bytes over ~ (SMs x 16) warps: routed and shared rows differ in size.
+        const int rps = 32 / g.tpr_h;
+        const double br = 2.0 * (double)(nbh * block_bytes(L->gate_type)), bs = 2.0 * (double)(nbh * block_bytes(L->sgate_type));
+        const double total = (double)T * L->F * ((double)L->k * br + bs);
+        const double per_warp = total / (double)(ctx->sm_count * 16);
+        auto chunk_of = [&](double b) {
+            uint64_t c = (uint64_t)(per_warp / b + 0.5);
+            c = c < 1 ? 1 : c;
+            c = (c + rps - 1) / rps * rps;
+            return c > 256 ? (uint64_t)256 : c;
+        };
+        g.chunk_r = chunk_of(br);
+        g.chunk_s = chunk_of(bs);
+        g.chunks_r = (L->F + g.chunk_r - 1) / g.chunk_r;
+        g.chunks_s = (L->F + g.chunk_s - 1) / g.chunk_s;
+        g.bmax_iq = 16 > rps ? 16 : rps;
+        g.bmax_k = 2 > rps ? 2 : rps;
+        const int kt_g = dot_type(L->gate_type) && (L->gate_type == LBK_TYPE_Q4_K || L->gate_type == LBK_TYPE_Q5_K) ? 9 : 1;
+        const int kt_s = (L->sgate_type == LBK_TYPE_Q4_K || L->sgate_type == LBK_TYPE_Q5_K) ? 9 : 1;
+        auto pf = [&](int kt) { return (uint64_t)(kt == 9 ? g.bmax_k : g.bmax_iq) * 2 * nbh * kt; };
+        g.prod_floats = pf(kt_g) > pf(kt_s) ? pf(kt_g) : pf(kt_s);
+        uint64_t dots = (uint64_t)2 * (g.bmax_iq > g.bmax_k ? g.bmax_iq : g.bmax_k);
+        g.chain_floats = (dots * 9 + 64 + 3) & ~(uint64_t)3;
+        g.status = ctx->status;
+        g.tables = ctx->tables();
+        if (lbk::moe_gate_up_fixed_smem(L->gate_type, L->sgate_type) + 16 * (g.prod_floats + g.chain_floats) * 4 > lbk::kMaxSmem)
+            return fail(LBK_INVALID_PARAMETER, "MoE gate/up shapes exceed shared memory");
+        e = lbk::launch_moe_gate_up(L->gate_type, L->sgate_type, g, st);
+        if (e != cudaSuccess) return cuda_fail(e, "moe gate/up launch");
+        if (L->tracing) cudaEventRecordWithFlags(L->trace[2], st, cudaEventRecordExternal);
+
+        lbk::MoeDownArgs d{};
+        d.hidden = L->H;
+        d.ffn = L->F;
+        d.nb_f = (int)nbf;
+        lbk::gemv_plan(L->down_type, (int)nbf, &d.tpr_f, &slots_unused);
+        d.tokens = T;
+        d.k = L->k;
+        d.experts = L->E;
+        d.down = L->d_down;
+        d.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);
+        d.routed = routed;
+        d.hq = ws + o.hq;
+        d.out = out;
+        d.wps = (L->k + 1) * 2 <= 18 ? 2 : 1;
+        const uint64_t rpsf = 32 / d.tpr_f;
+        uint64_t ctas_x = (uint64_t)ctx->sm_count;
+        uint64_t rows = (L->H + ctas_x - 1) / ctas_x;
+        rows = (rows + d.wps * rpsf - 1) / (d.wps * rpsf) * (d.wps * rpsf);
+        if (rows > 64 * d.wps) rows = 64 * d.wps;  // <= 64 dots per warp
+        d.rows_per_cta = rows;
+        const uint64_t dots_w = (rows + d.wps * rpsf - 1) / (d.wps * rpsf) * rpsf;
+        const int kt_d = (L->down_type == LBK_TYPE_Q4_K || L->down_type == LBK_TYPE_Q5_K) ? 9 : 1;
+        const int kt_sd = (L->sdown_type == LBK_TYPE_Q4_K || L->sdown_type == LBK_TYPE_Q5_K) ? 9 : 1;
+        const int kt = kt_d > kt_sd ? kt_d : kt_sd;
+        d.prod_floats = dots_w * nbf * kt;
+        d.chain_floats = (dots_w * 9 + 64 + 3) & ~(uint64_t)3;
+        d.status = ctx->status;
+        d.tables = ctx->tables();
+        const uint64_t warps = (L->k + 1) * d.wps;
+        if (lbk::moe_down_fixed_smem(L->down_type, L->sdown_type) + (L->k + 1) * rows * 4 +
+                warps * (d.prod_floats + d.chain_floats) * 4 >
+            lbk::kMaxSmem)
+            return fail(LBK_INVALID_PARAMETER, "MoE down shapes exceed shared memory");
+        e = lbk::launch_moe_down(L->down_type, L->sdown_type, d, st);
+        if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
+        if (L->tracing) cudaEventRecordWithFlags(L->trace[3], st, cudaEventRecordExternal);
+        return ok();
+    }
+    // Per-expert path: any types and layouts, one token at a time.
+    float* g = reinterpret_cast<float*>(ws + o.g);
+    float* u = reinterpret_cast<float*>(ws + o.u);
+    uint8_t* q8 = ws + o.u + up256(L->F * 4);
+    for (uint64_t t = 0; t < T; t++) {
+        const float* xt = x + t * L->H;
+        float* ot = out + t * L->H;
+        fill_zero_kernel<<<(unsigned)((L->H + 255) / 256), 256, 0, st>>>(ot, L->H, ctx->status);
+        for (uint64_t j = 0; j < L->k; j++) {
+            const lbk_expert& proto = L->experts[0];
+            if (int32_t s = expert_accumulate(ctx, &proto, xt, ot, 0.0f, g, u, q8, L->d_gate, L->d_up, L->d_down,
+                                              routed + t * L->k + j, st, L->E))
+                return s;
+        }
+        if (int32_t s = expert_accumulate(ctx, &L->w.shared, xt, ot, 1.0f, g, u, q8, nullptr, nullptr, nullptr, nullptr, st))
+            return s;
+    }
+    return ok();
+}
+
+}  // namespace
+
+LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
+                                lbk_routed* routed_out, int32_t router_mode, void* workspace, uint64_t workspace_bytes,
+                                void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    if (router_mode != LBK_ROUTER_SEQUENTIAL && router_mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "router mode");
+    WsLayout o = moe_ws(layer, tokens);
+    if (workspace_bytes < o.total) return fail(LBK_SCRATCH_TOO_SMALL, "MoE workspace", 0, o.total, workspace_bytes);
+    if (x == nullptr || out == nullptr || workspace == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(x, 16) || !aligned(workspace, 256)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    lbk_routed* routed = routed_out ? routed_out : reinterpret_cast<lbk_routed*>(ws + o.routed);
+    float* logits = reinterpret_cast<float*>(ws + o.logits);
+
+    lbk::RouterFusedArgs f{};
+    f.r.w = static_cast<const float*>(layer->w.router.data);
+    f.r.x = x;
+    f.r.logits = logits;
+    f.r.hidden = layer->H;
+    f.r.experts = layer->E;
+    f.r.tokens = tokens;
+    f.r.status = ctx->status;
+    f.partials = reinterpret_cast<float*>(ws + o.partials);
+    f.q8x = layer->fused ? ws + o.q8x : nullptr;
+    f.counter = reinterpret_cast<unsigned int*>(ws + o.counters + tokens * (layer->k + 1) * (layer->F / LBK_QK_K) * 4);
+    f.bias = layer->w.selection_bias;
+    f.k = (uint32_t)layer->k;
+    f.weight_scale = layer->weight_scale;
+    f.routed = routed;
+    cudaError_t e;
+    if (layer->tracing) cudaEventRecordWithFlags(layer->trace[0], st, cudaEventRecordExternal);
+    if (router_mode == LBK_ROUTER_TREE) {
+        e = lbk::launch_router_fused(f, ctx->sm_count, st);
+        if (e != cudaSuccess) return cuda_fail(e, "router launch");
+    } else {
+        if (int32_t s = run_f32_gemv(ctx, &layer->w.router, x, tokens, logits, st)) return s;
+        lbk::TopkArgs ta{logits, layer->w.selection_bias, layer->E, tokens, (uint32_t)layer->k, layer->weight_scale, routed,
+                         ctx->status};
+        if ((e = lbk::launch_topk(ta, st)) != cudaSuccess) return cuda_fail(e, "top-k launch");
+        if (layer->fused) {  // quantize the tokens only
+            lbk::RouterFusedArgs q = f;
+            q.r.experts = 0;
+            q.routed = nullptr;
+            if ((e = lbk::launch_router_fused(q, ctx->sm_count, st)) != cudaSuccess) return cuda_fail(e, "quantize launch");
+        }
+    }
+    if (layer->tracing) cudaEventRecordWithFlags(layer->trace[1], st, cudaEventRecordExternal);
+    int32_t s = moe_experts(layer, x, tokens, routed, out, ws, o, st);
+    if (s == LBK_OK && layer->tracing && !layer->fused) {
+        cudaEventRecordWithFlags(layer->trace[2], st, cudaEventRecordExternal);
+        cudaEventRecordWithFlags(layer->trace[3], st, cudaEventRecordExternal);
+    }
+    return s;
+}
+
+LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, const lbk_routed* routed,
+                               float* out, void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "selected routed expert count", 0, 1, 0);
+    WsLayout o = moe_ws(layer, tokens);
+    if (workspace_bytes < o.total) return fail(LBK_SCRATCH_TOO_SMALL, "MoE workspace", 0, o.total, workspace_bytes);
+    if (x == nullptr || out == nullptr || workspace == nullptr || routed == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(x, 16) || !aligned(workspace, 256)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    check_routed_kernel<<<(unsigned)((tokens + 127) / 128), 128, 0, st>>>(routed, tokens, layer->k, layer->E, ctx->status);
+    if (layer->fused) {
+        lbk::RouterFusedArgs q{};
+        q.r.x = x;
+        q.r.hidden = layer->H;
+        q.r.experts = 0;
+        q.r.tokens = tokens;
+        q.r.status = ctx->status;
+        q.q8x = ws + o.q8x;
+        q.counter = reinterpret_cast<unsigned int*>(ws + o.counters + tokens * (layer->k + 1) * (layer->F / LBK_QK_K) * 4);
+        cudaError_t e = lbk::launch_router_fused(q, ctx->sm_count, st);
+        if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+    }
+    return moe_experts(layer, x, tokens, routed, out, ws, o, st);
+}
+
+// ------------------------------------------------------------ layout tools
+
+namespace {
+int32_t repack_common(lbk_context* ctx, const lbk_matrix* src, void* dst, uint64_t dst_bytes, int expect_layout,
+                      int to_planar, void* stream) {
+    if (int32_t s = check_matrix(src, "source")) return s;
+    if (!dot_type(src->type)) return fail(LBK_UNSUPPORTED_TYPE, "only packed types have a planar layout", (uint64_t)src->type);
+    if (src->layout != expect_layout) return fail(LBK_INVALID_PARAMETER, "source layout");
+    if (dst_bytes != src->bytes) return fail(LBK_ENCODED_LENGTH_MISMATCH, "destination length", 0, src->bytes, dst_bytes);
+    if (ctx == nullptr || dst == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(dst, 16)) return fail(LBK_INVALID_PARAMETER, "destination must be 16-byte aligned");
+    if (int32_t s = set_device(ctx)) return s;
+    lbk::RepackArgs a{static_cast<const uint8_t*>(src->data), static_cast<uint8_t*>(dst), src->output_width,
+                      (int)(src->input_width / LBK_QK_K), src->type, to_planar};
+    cudaError_t e = lbk::launch_repack(a, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "repack launch");
+}
+}  // namespace
+
+LBK_API int32_t lbk_repack(lbk_context* ctx, const lbk_matrix* src_gguf, void* dst_planar, uint64_t dst_bytes, void* stream) {
+    return repack_common(ctx, src_gguf, dst_planar, dst_bytes, LBK_LAYOUT_GGUF, 1, stream);
+}
+
+LBK_API int32_t lbk_unpack(lbk_context* ctx, const lbk_matrix* src_planar, void* dst_gguf, uint64_t dst_bytes, void* stream) {
+    return repack_common(ctx, src_planar, dst_gguf, dst_bytes, LBK_LAYOUT_PLANAR, 0, stream);
+}
+
+LBK_API int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void* stream) {
+    if (int32_t s = check_matrix(w, "matrix")) return s;
+    if (!dot_type(w->type)) return fail(LBK_UNSUPPORTED_TYPE, "only packed types carry binary16 scales", (uint64_t)w->type);
+    if (ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null context");
+    if (int32_t s = set_device(ctx)) return s;
+    cudaError_t e = lbk::launch_validate_scales(w->type, w->layout, static_cast<const uint8_t*>(w->data), w->output_width,
+                                                (int)(w->input_width / LBK_QK_K), ctx->scratch_min, ctx->status,
+                                                as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "validate launch");
+}

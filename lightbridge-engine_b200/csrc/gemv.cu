@@ -1,0 +1,366 @@
+// gemv.cu -- packed-row GEMV / dot kernels (IQ2_S, IQ3_S, Q4_K, Q5_K) x Q8_K.
+//
+// Replaces gemv_into / gemv_cpu_parallel_q8k_into / gemv_accumulate_scaled_into
+// (bridge-kernels-reference/src/gemv.rs:56-70, :88-115, :117-174) and
+// vec_dot_q8_k (bridge-quant-layout/src/q8_k.rs:80-119), bit-identical.
+//
+// One kernel per call: every CTA quantizes x to Q8_K itself (x is small and
+// L2-resident), so a non-finite x is seen by every CTA and no output is
+// written -- the reference's validate-before-write atomicity without a
+// second launch. Each thread owns one half block (128 lanes) of the input
+// and streams that half block of its rows; the per-block f32 products go to a
+// per-warp shared buffer and one lane per row replays the sequential tail.
+
+#include "lbk_kernels.h"
+
+namespace lbk {
+
+namespace {
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+
+template <int T>
+struct GemvCfg {
+    static constexpr bool kIq = (T == LBK_TYPE_IQ2_S || T == LBK_TYPE_IQ3_S);
+    static constexpr int kTail = TypeInfo<T>::kTail;
+    static constexpr int kTableBytes =
+        T == LBK_TYPE_IQ2_S ? (kIq2CodeBytes + kSignBytes) : (T == LBK_TYPE_IQ3_S ? (kIq3GridBytes + kSignBytes) : 0);
+};
+
+template <int T>
+struct HBOf;
+template <>
+struct HBOf<LBK_TYPE_IQ2_S> {
+    using type = Iq2HB;
+};
+template <>
+struct HBOf<LBK_TYPE_IQ3_S> {
+    using type = Iq3HB;
+};
+template <>
+struct HBOf<LBK_TYPE_Q4_K> {
+    using type = Q4HB;
+};
+template <>
+struct HBOf<LBK_TYPE_Q5_K> {
+    using type = Q5HB;
+};
+
+// Shared memory: [tables][act qs K][act d nb][bsums nb*16][tail kWarps*slots*nb*kTail][flag]
+template <int T>
+__host__ __device__ inline size_t gemv_smem_bytes(int nb, int slots) {
+    size_t s = (size_t)GemvCfg<T>::kTableBytes;
+    s += (size_t)nb * kQK;                 // qs
+    s += (size_t)nb * 4;                   // d
+    s += (size_t)nb * 16 * 2;              // bsums
+    s = (s + 15) & ~(size_t)15;
+    s += (size_t)kWarps * slots * nb * GemvCfg<T>::kTail * 4;
+    s += 16;
+    return s;
+}
+
+// Quantizes x (or parses a given Q8_K row) into the CTA's activation image.
+// Returns false if the input failed validation (reported to the status word).
+__device__ bool stage_activations(const GemvArgs& a, int nb, int8_t* qs, float* dsm, int16_t* bs, int* flag) {
+    int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) *flag = 0;
+    __syncthreads();
+    for (int b = warp; b < nb; b += kWarps) {
+        if (a.q8_in != nullptr) {
+            const uint8_t* src = a.q8_in + (size_t)b * kQ8Bytes;
+            // qs at +4: 4-byte aligned words
+            const uint32_t* qw = reinterpret_cast<const uint32_t*>(src + 4);
+            uint32_t* dst = reinterpret_cast<uint32_t*>(qs + b * kQK);
+            dst[lane * 2] = __ldg(qw + lane * 2);
+            dst[lane * 2 + 1] = __ldg(qw + lane * 2 + 1);
+            if (lane < 16) bs[b * 16 + lane] = (int16_t)ldg_u16(src + 260 + 2 * lane);
+            if (lane == 0) {
+                float d = __uint_as_float(__ldg(reinterpret_cast<const unsigned int*>(src)));
+                dsm[b] = d;
+                if (!isfinite(d)) {
+                    report(a.status, LBK_NON_FINITE_Q8_SCALE, (uint64_t)b, __float_as_uint(d));
+                    atomicExch(flag, 1);
+                }
+            }
+            continue;
+        }
+        float v[8];
+        const float4* xp = reinterpret_cast<const float4*>(a.x + (size_t)b * kQK + lane * 8);
+        float4 p0 = __ldg(xp), p1 = __ldg(xp + 1);
+        v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+        v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+        bool bad = false;
+        int bad_i = 0;
+#pragma unroll
+        for (int i = 7; i >= 0; i--)
+            if (!isfinite(v[i])) {
+                bad = true;
+                bad_i = i;
+            }
+        unsigned badmask = __ballot_sync(0xffffffffu, bad);
+        if (badmask) {
+            int first_lane = __ffs(badmask) - 1;
+            if (lane == first_lane)
+                report(a.status, LBK_NON_FINITE_ACTIVATION, (uint64_t)b * kQK + lane * 8 + bad_i,
+                       __float_as_uint(v[bad_i]));
+            if (lane == 0) atomicExch(flag, 1);
+            continue;
+        }
+        Q8Block q = quantize_q8k_warp(v, lane);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(qs + b * kQK);
+        dst[lane * 2] = q.q[0];
+        dst[lane * 2 + 1] = q.q[1];
+        int32_t pair = q.pair_sum + __shfl_xor_sync(0xffffffffu, q.pair_sum, 1);
+        if ((lane & 1) == 0) bs[b * 16 + (lane >> 1)] = (int16_t)pair;
+        if (lane == 0) dsm[b] = q.d;
+        if (a.q8_out != nullptr && blockIdx.x == 0) {
+            uint8_t* o = a.q8_out + (size_t)b * kQ8Bytes;
+            uint32_t* ow = reinterpret_cast<uint32_t*>(o + 4);
+            ow[lane * 2] = q.q[0];
+            ow[lane * 2 + 1] = q.q[1];
+            if ((lane & 1) == 0) *reinterpret_cast<int16_t*>(o + 260 + lane) = (int16_t)pair;
+            if (lane == 0) *reinterpret_cast<float*>(o) = q.d;
+        }
+    }
+    __syncthreads();
+    bool ok = (*flag == 0);
+    // The accumulate form also requires a finite destination (gemv.rs:126-127).
+    if (ok && a.mode == kGemvAccumulate) {
+        for (uint64_t i = threadIdx.x; i < a.w.rows; i += kThreads) {
+            float yv = a.y[i];
+            if (!isfinite(yv)) {
+                report(a.status, LBK_NON_FINITE_VALUE, i, __float_as_uint(yv));
+                atomicExch(flag, 1);
+            }
+        }
+        __syncthreads();
+        ok = (*flag == 0);
+    }
+    return ok;
+}
+
+template <int T, int L>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
+    if (a.mat_table != nullptr) {  // routed expert selected on the device
+        uint32_t e = a.sel->expert_id;
+        if (e >= a.mat_count) {  // bad routing: report and skip (no out-of-table read)
+            if (blockIdx.x == 0 && threadIdx.x == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
+            return;
+        }
+        a.w.data = a.mat_table[e];
+        a.scale = a.sel->coefficient;
+    }
+    using Cfg = GemvCfg<T>;
+    using HB = typename HBOf<T>::type;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int nb = a.w.nb;
+    uint32_t* tab0 = reinterpret_cast<uint32_t*>(smem);
+    uint32_t* tab1 = reinterpret_cast<uint32_t*>(smem + (T == LBK_TYPE_IQ2_S ? kIq2CodeBytes : kIq3GridBytes));
+    int8_t* qs = reinterpret_cast<int8_t*>(smem + Cfg::kTableBytes);
+    float* dsm = reinterpret_cast<float*>(qs + (size_t)nb * kQK);
+    int16_t* bs = reinterpret_cast<int16_t*>(dsm + nb);
+    size_t tail_off = ((size_t)Cfg::kTableBytes + (size_t)nb * kQK + nb * 4 + nb * 32 + 15) & ~(size_t)15;
+    float* tail_all = reinterpret_cast<float*>(smem + tail_off);
+    int* flag = reinterpret_cast<int*>(tail_all + (size_t)kWarps * a.tail_slots * nb * Cfg::kTail);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* tail = tail_all + (size_t)warp * a.tail_slots * nb * Cfg::kTail;
+
+    // lane -> (row within step, half block)
+    const int tpr = a.tpr;  // threads per row (power of two, >= 2*nb when nb <= 16, else 32)
+    const int rps = 32 / tpr;
+    const int sub = lane / tpr;
+    const int hb0 = lane % tpr;
+    const int nhb = 2 * nb;
+    const uint64_t rows = a.w.rows;
+    const uint64_t steps = (rows + rps - 1) / rps;
+    const uint64_t gwarp = (uint64_t)blockIdx.x * kWarps + warp;
+    const uint64_t nwarp = (uint64_t)gridDim.x * kWarps;
+
+    // Issue the first step's weight loads before the prologue so their latency
+    // overlaps the table fill and the quantization.
+    HB cur;
+    uint64_t step = gwarp;
+    auto row_of = [&](uint64_t s) -> uint64_t { return s * rps + sub; };
+    const bool single = (nhb <= tpr);  // each thread owns at most one half block
+    if (single && step < steps && row_of(step) < rows && hb0 < nhb) load_hb<L>(cur, a.w, row_of(step), hb0 >> 1, hb0 & 1);
+
+    if (T == LBK_TYPE_IQ2_S) {
+        fill_iq2_codes(tab0, a.tables.iq2s_grid);
+        fill_signs(tab1);
+    } else if (T == LBK_TYPE_IQ3_S) {
+        fill_iq3_grid(tab0, a.tables.iq3s_grid);
+        fill_signs(tab1);
+    }
+    if (!stage_activations(a, nb, qs, dsm, bs, flag)) return;
+
+    ActSmem as{qs, dsm, bs};
+    constexpr bool kTr = !Cfg::kIq;
+    ActHB act;
+    uint32_t nact[32];
+    if (single && hb0 < nhb) {
+        load_act_hb<kTr>(act, as, hb0 >> 1, hb0 & 1, !Cfg::kIq);
+        if (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+        }
+    }
+    const uint32_t* t0 = tab0 + lane;
+    const uint32_t* t1 = tab1 + lane;
+
+    const int slots = a.tail_slots;  // >= rps, multiple of rps
+    auto flush = [&](int nslots, uint64_t first_step) {
+        __syncwarp();
+        if (lane < nslots) {
+            int s_in = lane / rps, sb = lane % rps;
+            uint64_t row = (first_step + (uint64_t)s_in * nwarp) * rps + sb;
+            if (row < rows) {
+                const float* prod = tail + (size_t)lane * nb * Cfg::kTail;
+                float v = Cfg::kIq ? iq_tail(prod, nb, 1, T == LBK_TYPE_IQ2_S) : k_tail(prod, nb, 9);
+                if (a.mode == kGemvAccumulate)
+                    a.y[row] = __fadd_rn(a.y[row], __fmul_rn(a.scale, v));
+                else
+                    a.y[row] = v;
+            }
+        }
+        __syncwarp();
+    };
+
+    uint64_t batch_first = step;
+    const int steps_per_batch = slots / rps;
+    const int iters = single ? 1 : (nhb + 31) / 32;  // uniform across the warp
+    int in_batch = 0;
+    for (; step < steps; step += nwarp) {
+        const uint64_t row = row_of(step);
+        const bool active = row < rows;
+        const int slot = in_batch * rps + sub;
+        for (int it = 0; it < iters; ++it) {
+            const int hb = hb0 + it * tpr;
+            const int b = hb >> 1, h = hb & 1;
+            const bool mine = active && hb < nhb;
+            HB w;
+            if (single) {
+                w = cur;
+                // prefetch the next step's half block while this one computes
+                uint64_t ns = step + nwarp;
+                if (ns < steps && row_of(ns) < rows && hb0 < nhb) load_hb<L>(cur, a.w, row_of(ns), b, h);
+            } else if (mine) {
+                load_hb<L>(w, a.w, row, b, h);
+                load_act_hb<kTr>(act, as, b, h, !Cfg::kIq);
+                if (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+                }
+            }
+            if constexpr (Cfg::kIq) {
+                IqPart p{0, 0};
+                if (mine) {
+                    if constexpr (T == LBK_TYPE_IQ2_S)
+                        p = dot_hb(w, act, t0, t1);
+                    else
+                        p = dot_hb(w, act, nact, t0, t1);
+                }
+                int other = __shfl_xor_sync(0xffffffffu, p.sum, 1);
+                if (mine && h == 0) {
+                    p.sum += other;
+                    if (a.block_sums) a.block_sums[row * nb + b] = p.sum;
+                    tail[(size_t)slot * nb + b] = iq_block_product(p, dsm[b]);
+                    if (!h_finite(p.d)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b, p.d);
+                }
+            } else {
+                KPart p;
+#pragma unroll
+                for (int l = 0; l < 8; l++) p.lane[l] = 0;
+                p.min_sum = 0;
+                p.dm = 0;
+                if (mine) p = dot_hb(w, act, h);
+#pragma unroll
+                for (int l = 0; l < 8; l++) p.lane[l] += __shfl_xor_sync(0xffffffffu, p.lane[l], 1);
+                p.min_sum += __shfl_xor_sync(0xffffffffu, p.min_sum, 1);
+                if (mine && h == 0) {
+                    if (a.block_sums) {
+#pragma unroll
+                        for (int l = 0; l < 8; l++) a.block_sums[(row * nb + b) * 9 + l] = p.lane[l];
+                        a.block_sums[(row * nb + b) * 9 + 8] = p.min_sum;
+                    }
+                    float pr[9];
+                    k_block_products(p, dsm[b], pr);
+                    float* dst = tail + ((size_t)slot * nb + b) * 9;
+#pragma unroll
+                    for (int i = 0; i < 9; i++) dst[i] = pr[i];
+                    if (!h_finite(p.dm & 0xffffu)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b, p.dm & 0xffffu);
+                    if (!h_finite(p.dm >> 16)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b, p.dm >> 16);
+                }
+            }
+        }
+        if (++in_batch == steps_per_batch) {
+            flush(steps_per_batch * rps, batch_first);
+            in_batch = 0;
+            batch_first = step + nwarp;
+        }
+    }
+    if (in_batch > 0) flush(in_batch * rps, batch_first);
+}
+
+template <int T, int L>
+cudaError_t launch_gemv_t(const GemvArgs& a, int sm_count, cudaStream_t stream) {
+    size_t smem = gemv_smem_bytes<T>(a.w.nb, a.tail_slots);
+    if (smem > kMaxSmem) return cudaErrorInvalidValue;
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(gemv_kernel<T, L>));
+    if (e != cudaSuccess) return e;
+    uint64_t rps = 32 / a.tpr;
+    uint64_t steps = (a.w.rows + rps - 1) / rps;
+    uint64_t ctas = (steps + kWarps - 1) / kWarps;
+    if (ctas > (uint64_t)sm_count) ctas = sm_count;
+    if (ctas < 1) ctas = 1;
+    gemv_kernel<T, L><<<(unsigned)ctas, kThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t gemv_smem_required(int type, int nb, int slots) {
+    switch (type) {
+        case LBK_TYPE_IQ2_S: return gemv_smem_bytes<LBK_TYPE_IQ2_S>(nb, slots);
+        case LBK_TYPE_IQ3_S: return gemv_smem_bytes<LBK_TYPE_IQ3_S>(nb, slots);
+        case LBK_TYPE_Q4_K: return gemv_smem_bytes<LBK_TYPE_Q4_K>(nb, slots);
+        default: return gemv_smem_bytes<LBK_TYPE_Q5_K>(nb, slots);
+    }
+}
+
+void gemv_plan(int type, int nb, int* tpr, int* slots) {
+    int t = 32;
+    if (nb <= 16) {
+        t = 2;
+        while (t < 2 * nb) t <<= 1;
+    }
+    int rps = 32 / t;
+    bool iq = type == LBK_TYPE_IQ2_S || type == LBK_TYPE_IQ3_S;
+    int s = iq ? 32 : 8;
+    if (s < rps) s = rps;
+    // keep the tail buffer within shared memory for wide rows
+    while (s > rps && gemv_smem_required(type, nb, s) > kMaxSmem) s -= rps;
+    *tpr = t;
+    *slots = s;
+}
+
+cudaError_t launch_gemv(int type, int layout, const GemvArgs& a, int sm_count, cudaStream_t stream) {
+    const bool planar = layout == LBK_LAYOUT_PLANAR;
+    switch (type) {
+        case LBK_TYPE_IQ2_S:
+            return planar ? launch_gemv_t<LBK_TYPE_IQ2_S, LBK_LAYOUT_PLANAR>(a, sm_count, stream)
+                          : launch_gemv_t<LBK_TYPE_IQ2_S, LBK_LAYOUT_GGUF>(a, sm_count, stream);
+        case LBK_TYPE_IQ3_S:
+            return planar ? launch_gemv_t<LBK_TYPE_IQ3_S, LBK_LAYOUT_PLANAR>(a, sm_count, stream)
+                          : launch_gemv_t<LBK_TYPE_IQ3_S, LBK_LAYOUT_GGUF>(a, sm_count, stream);
+        case LBK_TYPE_Q4_K:
+            return planar ? launch_gemv_t<LBK_TYPE_Q4_K, LBK_LAYOUT_PLANAR>(a, sm_count, stream)
+                          : launch_gemv_t<LBK_TYPE_Q4_K, LBK_LAYOUT_GGUF>(a, sm_count, stream);
+        default:
+            return planar ? launch_gemv_t<LBK_TYPE_Q5_K, LBK_LAYOUT_PLANAR>(a, sm_count, stream)
+                          : launch_gemv_t<LBK_TYPE_Q5_K, LBK_LAYOUT_GGUF>(a, sm_count, stream);
+    }
+}
+
+}  // namespace lbk

@@ -1,0 +1,660 @@
+// lbk_device.cuh -- device building blocks of the quantized expert kernels.
+//
+// Work unit: a "half block" (HB) = 128 consecutive lanes of one 256-lane
+// super-block of one packed row. A thread owns one HB position of the input
+// vector for the whole kernel and keeps that HB's Q8_K activation bytes in
+// registers; it then streams the matching HB of many weight rows. Integer sums
+// are exact, so any split of a block's lanes gives the reference's per-block
+// int32 sums; the f32 tail (product per block, then a sequential sum over
+// blocks in block order) is replayed separately, one row per lane.
+//
+// Reference arithmetic restated here: bridge-quant-layout/src/q8_k.rs
+// (quantize :16-76, nearest_int :224-228, dot_q4_or_q5_k :247-327,
+// dot_iq2_s :329-370, dot_iq3_s :372-434), k_quants.rs (scale_min :231-240).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/lightbridge_kernels.h"
+
+namespace lbk {
+
+constexpr int kQK = 256;
+constexpr int kQ8Bytes = 292;
+
+// ------------------------------------------------------------ device status
+
+// First device-detected failure; written once (CAS on `status`).
+struct DeviceStatus {
+    int32_t status;
+    uint32_t bits;
+    uint64_t index;
+};
+
+__device__ __forceinline__ void report(DeviceStatus* st, int32_t code, uint64_t index, uint32_t bits) {
+    if (st == nullptr) return;
+    if (atomicCAS(&st->status, 0, -1) == 0) {
+        st->index = index;
+        st->bits = bits;
+        __threadfence();
+        atomicExch(&st->status, code);
+    }
+}
+
+__device__ __forceinline__ bool status_set(const DeviceStatus* st) {
+    return st != nullptr && *((volatile const int32_t*)&st->status) != 0;
+}
+
+// ----------------------------------------------------------------- types
+
+template <int T>
+struct TypeInfo;
+template <>
+struct TypeInfo<LBK_TYPE_IQ2_S> {
+    static constexpr int kBlockBytes = 82;
+    static constexpr int kTail = 1;  // f32 products per block in the tail
+};
+template <>
+struct TypeInfo<LBK_TYPE_IQ3_S> {
+    static constexpr int kBlockBytes = 110;
+    static constexpr int kTail = 1;
+};
+template <>
+struct TypeInfo<LBK_TYPE_Q4_K> {
+    static constexpr int kBlockBytes = 144;
+    static constexpr int kTail = 9;  // 8 lane products + min product
+};
+template <>
+struct TypeInfo<LBK_TYPE_Q5_K> {
+    static constexpr int kBlockBytes = 176;
+    static constexpr int kTail = 9;
+};
+
+// ------------------------------------------------------------ small helpers
+
+__device__ __forceinline__ uint32_t ldg_u16(const uint8_t* p) {
+    return (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p));
+}
+__device__ __forceinline__ uint32_t ldg_u32(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }
+__device__ __forceinline__ uint4 ldg_u128(const uint8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+// Streaming loads for packed weights: read once, do not keep in L1.
+__device__ __forceinline__ uint4 ldw_u128(const uint8_t* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldw_u32(const uint8_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldw_u16(const uint8_t* p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
+}
+// Two-byte-aligned 4-byte load (GGUF IQ blocks are only 2-byte aligned).
+__device__ __forceinline__ uint32_t ldw_u32_a2(const uint8_t* p) { return ldw_u16(p) | (ldw_u16(p + 2) << 16); }
+__device__ __forceinline__ uint4 ldw_u128_a2(const uint8_t* p) {
+    return make_uint4(ldw_u32_a2(p), ldw_u32_a2(p + 4), ldw_u32_a2(p + 8), ldw_u32_a2(p + 12));
+}
+
+__device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
+__device__ __forceinline__ bool h_finite(uint32_t bits16) { return ((bits16 >> 10) & 0x1f) != 0x1f; }
+__device__ __forceinline__ uint32_t w32(const uint4& v, int i) {
+    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+
+// 4x4 byte transpose: out[k] byte i = in[i] byte k.
+__device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t& o0,
+                                           uint32_t& o1, uint32_t& o2, uint32_t& o3) {
+    uint32_t t0 = __byte_perm(a, b, 0x5140);
+    uint32_t t1 = __byte_perm(a, b, 0x7362);
+    uint32_t t2 = __byte_perm(c, d, 0x5140);
+    uint32_t t3 = __byte_perm(c, d, 0x7362);
+    o0 = __byte_perm(t0, t2, 0x5410);
+    o1 = __byte_perm(t0, t2, 0x7632);
+    o2 = __byte_perm(t1, t3, 0x5410);
+    o3 = __byte_perm(t1, t3, 0x7632);
+}
+
+// ------------------------------------------------------- shared-memory tables
+//
+// Lookup tables are replicated 32 times, copy c living entirely in bank c
+// (word address = entry * 32 + c). Lane l reads copy l, so a warp-wide lookup
+// with arbitrary indices is one shared-memory wavefront.
+
+constexpr int kIq2CodeEntries = 1024;  // IQ2_S grid as 8 code nibbles (0,1,2 = 8,25,43)
+constexpr int kIq3GridEntries = 512;   // IQ3_S grid magnitudes, 4 bytes
+constexpr int kSignEntries = 256;      // sign byte -> bit 2 of nibble i set iff bit i set
+
+constexpr int kIq2CodeBytes = kIq2CodeEntries * 32 * 4;  // 128 KiB
+constexpr int kIq3GridBytes = kIq3GridEntries * 32 * 4;  // 64 KiB
+constexpr int kSignBytes = kSignEntries * 32 * 4;        // 32 KiB
+
+// Codebooks in global memory, uploaded once per context (from lbk_iq_tables.h).
+struct Tables {
+    const uint64_t* iq2s_grid;  // 1024
+    const uint32_t* iq3s_grid;  // 512
+};
+
+__device__ __forceinline__ uint32_t sign_spread(uint32_t s) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) v |= ((s >> i) & 1u) << (4 * i + 2);
+    return v;
+}
+
+__device__ __forceinline__ uint32_t iq2_code_of(uint64_t g) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int l = 0; l < 8; l++) {
+        uint32_t m = (uint32_t)(g >> (8 * l)) & 0xff;
+        uint32_t c = m == 8 ? 0u : (m == 25 ? 1u : 2u);
+        v |= c << (4 * l);
+    }
+    return v;
+}
+
+// Fills a replicated table; all threads of the block participate.
+__device__ __forceinline__ void fill_iq2_codes(uint32_t* tab, const uint64_t* grid) {
+    for (int i = threadIdx.x; i < kIq2CodeEntries * 32; i += blockDim.x) {
+        int e = i >> 5;
+        tab[i] = iq2_code_of(__ldg(grid + e));
+    }
+}
+__device__ __forceinline__ void fill_iq3_grid(uint32_t* tab, const uint32_t* grid) {
+    for (int i = threadIdx.x; i < kIq3GridEntries * 32; i += blockDim.x) tab[i] = __ldg(grid + (i >> 5));
+}
+__device__ __forceinline__ void fill_signs(uint32_t* tab) {
+    for (int i = threadIdx.x; i < kSignEntries * 32; i += blockDim.x) tab[i] = sign_spread((uint32_t)(i >> 5));
+}
+
+// Pools for IQ2_S signed-grid expansion through byte permutes: selector
+// nibble c in {0,1,2} picks +8/+25/+43, c+4 picks the negated value.
+constexpr uint32_t kIq2PoolPos = 0x002b1908u;
+constexpr uint32_t kIq2PoolNeg = 0x00d5e7f8u;
+
+// ------------------------------------------------------------------- exp
+// exp for the sigmoid / SwiGLU stages: CUDA's double-precision exp rounded to
+// f32, i.e. the correctly rounded f32 result except in vanishingly rare
+// cases. The reference uses the platform libm expf (glibc's is also correctly
+// rounded in all but rare cases); these stages are held to 1e-5 relative.
+__device__ __forceinline__ float exp_f32(float v) { return (float)exp((double)v); }
+
+// sigmoid, bridge-model-hy3/src/routing.rs:109-111
+__device__ __forceinline__ float sigmoid_ref(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_f32(-v))); }
+
+// SwiGLU of one lane, apply_swiglu (activation.rs:170-178)
+__device__ __forceinline__ float swiglu_ref(float g, float u) {
+    float act = __fdiv_rn(g, __fadd_rn(1.0f, exp_f32(-g)));
+    return __fmul_rn(act, u);
+}
+
+// ------------------------------------------------------------ Q8_K quantizer
+
+// Activations of one Q8_K block held by a warp: lane l owns lanes 8l..8l+7.
+// Returns false (and writes nothing) when a value is non-finite.
+// Restates quantize_row_q8_k_into (q8_k.rs:35-73) for one block:
+//   first index of the largest |x| keeps its sign as `max`;
+//   iscale = -127/max; q = min(nearest_int(iscale*x), 127);
+//   16 group sums of 16 lanes; d = 1/iscale.
+struct Q8Block {
+    uint32_t q[2];      // this lane's 8 quants
+    int32_t pair_sum;   // sum of this lane's 8 quants
+    float d;            // block scale (all lanes)
+};
+
+__device__ __forceinline__ Q8Block quantize_q8k_warp(const float v[8], int lane) {
+    // max-abs with ties to the first index: key = (|x| bits, ~index)
+    unsigned long long key = 0ull;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        uint32_t ab = __float_as_uint(fabsf(v[i]));
+        uint32_t idx = (uint32_t)(lane * 8 + i);
+        unsigned long long k = ((unsigned long long)ab << 32) | (unsigned long long)(0xffffffffu - idx);
+        key = k > key ? k : key;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+    }
+    uint32_t amax_bits = (uint32_t)(key >> 32);
+    uint32_t idx = 0xffffffffu - (uint32_t)(key & 0xffffffffull);
+    Q8Block out;
+    if (amax_bits == 0u) {
+        out.q[0] = out.q[1] = 0u;
+        out.pair_sum = 0;
+        out.d = 0.0f;
+        return out;
+    }
+    float mine = v[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++)
+        if ((int)(idx & 7) == i) mine = v[i];
+    float maxv = __shfl_sync(0xffffffffu, mine, (int)(idx >> 3));
+    float iscale = __fdiv_rn(-127.0f, maxv);
+    int32_t s = 0;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int q = __float2int_rn(__fmul_rn(iscale, v[i]));
+        q = q > 127 ? 127 : q;
+        s += q;
+        w[i >> 2] |= ((uint32_t)q & 0xffu) << (8 * (i & 3));
+    }
+    out.q[0] = w[0];
+    out.q[1] = w[1];
+    out.pair_sum = s;
+    out.d = __fdiv_rn(1.0f, iscale);
+    return out;
+}
+
+// ------------------------------------------------------ activation registers
+
+// A thread's HB of Q8_K activations: 128 int8 lanes as 32 words, in natural
+// lane order for the IQ types and transposed per 32-lane sub-block for the
+// K-quants (word 8j+l holds lanes l, l+8, l+16, l+24 of sub-block j).
+struct ActHB {
+    uint32_t w[32];
+    float d;
+    int32_t bsum[8];  // the HB's 8 Q8_K 16-lane group sums (K-quants only)
+};
+
+// Smem image of a Q8_K row: qs[K] int8 (16 B aligned), d[nb], bsums[nb*16].
+struct ActSmem {
+    const int8_t* qs;
+    const float* d;
+    const int16_t* bsums;
+};
+
+template <bool kTransposed>
+__device__ __forceinline__ void load_act_hb(ActHB& a, const ActSmem& s, int block, int half, bool with_bsums) {
+    const uint4* src = reinterpret_cast<const uint4*>(s.qs + block * kQK + half * 128);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        uint4 v = src[i];
+        a.w[4 * i + 0] = v.x;
+        a.w[4 * i + 1] = v.y;
+        a.w[4 * i + 2] = v.z;
+        a.w[4 * i + 3] = v.w;
+    }
+    if (kTransposed) {
+        // sub-block j (32 lanes = words 8j..8j+7 in natural order):
+        // out word l (l<4)  = byte l of words 8j+0, +2, +4, +6
+        // out word l (l>=4) = byte l-4 of words 8j+1, +3, +5, +7
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint32_t n[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) n[i] = a.w[8 * j + i];
+            transpose4(n[0], n[2], n[4], n[6], a.w[8 * j + 0], a.w[8 * j + 1], a.w[8 * j + 2], a.w[8 * j + 3]);
+            transpose4(n[1], n[3], n[5], n[7], a.w[8 * j + 4], a.w[8 * j + 5], a.w[8 * j + 6], a.w[8 * j + 7]);
+        }
+    }
+    a.d = s.d[block];
+    if (with_bsums) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) a.bsum[i] = s.bsums[block * 16 + half * 8 + i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) a.bsum[i] = 0;
+    }
+}
+
+// ------------------------------------------------------------ HB weight data
+
+// Field planes of the planar layout (bytes per block, in plane order).
+//   IQ2_S: qs 32 | signs 32 | qh 8 | scales 8 | d 2
+//   IQ3_S: qs 64 | signs 32 | qh 8 | scales 4 | d 2
+//   Q4_K : qs 128 (lane-major) | scales 12 | dm 4
+//   Q5_K : qs 128 (lane-major) | qh 32 (lane-major) | scales 12 | dm 4
+// "lane-major" permutes the 32 bytes of each qs group g as
+// new[4k+i] = old[k+8i] (k < 8, i < 4), so after nibble extraction a word
+// holds four lanes of one lane class (index mod 8) of one sub-block.
+struct MatrixRef {
+    const uint8_t* data;
+    uint64_t rows;
+    int nb;  // blocks per row
+};
+
+__device__ __forceinline__ uint64_t blk_index(const MatrixRef& m, uint64_t row, int b) {
+    return row * (uint64_t)m.nb + (uint64_t)b;
+}
+
+struct Iq2HB {
+    uint4 qs, sg;
+    uint32_t qh, sc, d;
+};
+struct Iq3HB {
+    uint4 qs0, qs1, sg;
+    uint32_t qh, sc, d;
+};
+struct Q4HB {
+    uint4 qs[4];
+    uint32_t sc[3];
+    uint32_t dm;
+};
+struct Q5HB {
+    uint4 qs[4];
+    uint4 qh[2];
+    uint32_t sc[3];
+    uint32_t dm;
+};
+
+template <int LAYOUT>
+__device__ __forceinline__ void load_hb(Iq2HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
+    uint64_t bi = blk_index(m, row, b);
+    if (LAYOUT == LBK_LAYOUT_PLANAR) {
+        uint64_t nblk = m.rows * (uint64_t)m.nb;
+        const uint8_t* base = m.data;
+        o.qs = ldw_u128(base + bi * 32 + 16 * h);
+        o.sg = ldw_u128(base + nblk * 32 + bi * 32 + 16 * h);
+        o.qh = ldw_u32(base + nblk * 64 + bi * 8 + 4 * h);
+        o.sc = ldw_u32(base + nblk * 72 + bi * 8 + 4 * h);
+        o.d = ldw_u16(base + nblk * 80 + bi * 2);
+    } else {
+        const uint8_t* p = m.data + bi * 82;
+        o.d = ldw_u16(p);
+        o.qs = ldw_u128_a2(p + 2 + 16 * h);
+        o.sg = ldw_u128_a2(p + 34 + 16 * h);
+        o.qh = ldw_u32_a2(p + 66 + 4 * h);
+        o.sc = ldw_u32_a2(p + 74 + 4 * h);
+    }
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void load_hb(Iq3HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
+    uint64_t bi = blk_index(m, row, b);
+    if (LAYOUT == LBK_LAYOUT_PLANAR) {
+        uint64_t nblk = m.rows * (uint64_t)m.nb;
+        const uint8_t* base = m.data;
+        o.qs0 = ldw_u128(base + bi * 64 + 32 * h);
+        o.qs1 = ldw_u128(base + bi * 64 + 32 * h + 16);
+        o.sg = ldw_u128(base + nblk * 64 + bi * 32 + 16 * h);
+        o.qh = ldw_u32(base + nblk * 96 + bi * 8 + 4 * h);
+        o.sc = ldw_u16(base + nblk * 104 + bi * 4 + 2 * h);
+        o.d = ldw_u16(base + nblk * 108 + bi * 2);
+    } else {
+        const uint8_t* p = m.data + bi * 110;
+        o.d = ldw_u16(p);
+        o.qs0 = ldw_u128_a2(p + 2 + 32 * h);
+        o.qs1 = ldw_u128_a2(p + 2 + 32 * h + 16);
+        o.qh = ldw_u32_a2(p + 66 + 4 * h);
+        o.sg = ldw_u128_a2(p + 74 + 16 * h);
+        o.sc = ldw_u16(p + 106 + 2 * h);
+    }
+}
+
+// GGUF qs group (8 words, natural order) -> lane-major order.
+__device__ __forceinline__ void lane_major8(uint32_t* w) {
+    uint32_t n[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) n[i] = w[i];
+    transpose4(n[0], n[2], n[4], n[6], w[0], w[1], w[2], w[3]);
+    transpose4(n[1], n[3], n[5], n[7], w[4], w[5], w[6], w[7]);
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void load_hb(Q4HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
+    uint64_t bi = blk_index(m, row, b);
+    if (LAYOUT == LBK_LAYOUT_PLANAR) {
+        uint64_t nblk = m.rows * (uint64_t)m.nb;
+        const uint8_t* base = m.data;
+#pragma unroll
+        for (int i = 0; i < 4; i++) o.qs[i] = ldw_u128(base + bi * 128 + 64 * h + 16 * i);
+        const uint8_t* s = base + nblk * 128 + bi * 12;
+        o.sc[0] = ldw_u32(s);
+        o.sc[1] = ldw_u32(s + 4);
+        o.sc[2] = ldw_u32(s + 8);
+        o.dm = ldw_u32(base + nblk * 140 + bi * 4);
+    } else {
+        const uint8_t* p = m.data + bi * 144;
+        o.dm = ldw_u32(p);
+        o.sc[0] = ldw_u32(p + 4);
+        o.sc[1] = ldw_u32(p + 8);
+        o.sc[2] = ldw_u32(p + 12);
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+            uint4 a = ldw_u128(p + 16 + 64 * h + 32 * g);
+            uint4 c = ldw_u128(p + 16 + 64 * h + 32 * g + 16);
+            uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+            lane_major8(w);
+            o.qs[2 * g] = make_uint4(w[0], w[1], w[2], w[3]);
+            o.qs[2 * g + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+    }
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void load_hb(Q5HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
+    uint64_t bi = blk_index(m, row, b);
+    if (LAYOUT == LBK_LAYOUT_PLANAR) {
+        uint64_t nblk = m.rows * (uint64_t)m.nb;
+        const uint8_t* base = m.data;
+#pragma unroll
+        for (int i = 0; i < 4; i++) o.qs[i] = ldw_u128(base + bi * 128 + 64 * h + 16 * i);
+        o.qh[0] = ldw_u128(base + nblk * 128 + bi * 32);
+        o.qh[1] = ldw_u128(base + nblk * 128 + bi * 32 + 16);
+        const uint8_t* s = base + nblk * 160 + bi * 12;
+        o.sc[0] = ldw_u32(s);
+        o.sc[1] = ldw_u32(s + 4);
+        o.sc[2] = ldw_u32(s + 8);
+        o.dm = ldw_u32(base + nblk * 172 + bi * 4);
+    } else {
+        const uint8_t* p = m.data + bi * 176;
+        o.dm = ldw_u32(p);
+        o.sc[0] = ldw_u32(p + 4);
+        o.sc[1] = ldw_u32(p + 8);
+        o.sc[2] = ldw_u32(p + 12);
+        {
+            uint4 a = ldw_u128(p + 16);
+            uint4 c = ldw_u128(p + 32);
+            uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+            lane_major8(w);
+            o.qh[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            o.qh[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+#pragma unroll
+        for (int g = 0; g < 2; g++) {
+            uint4 a = ldw_u128(p + 48 + 64 * h + 32 * g);
+            uint4 c = ldw_u128(p + 48 + 64 * h + 32 * g + 16);
+            uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+            lane_major8(w);
+            o.qs[2 * g] = make_uint4(w[0], w[1], w[2], w[3]);
+            o.qs[2 * g + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+    }
+}
+
+// ------------------------------------------------------------ HB int dots
+
+// Result of one HB: integer partial sums of its block plus the block scales.
+struct IqPart {
+    int32_t sum;
+    uint32_t d;  // binary16 bits
+};
+struct KPart {
+    int32_t lane[8];
+    int32_t min_sum;
+    uint32_t dm;  // d | dmin << 16 (binary16 bits)
+};
+
+// dot_iq2_s (q8_k.rs:339-364) over groups 4h..4h+3 of one block.
+// code_tab / sign_tab point at this lane's copy of the replicated tables.
+__device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, const uint32_t* code_tab,
+                                         const uint32_t* sign_tab) {
+    int32_t total = 0;
+#pragma unroll
+    for (int gi = 0; gi < 4; gi++) {
+        uint32_t qsw = w32(w.qs, gi);
+        uint32_t sgw = w32(w.sg, gi);
+        uint32_t qh = (w.qh >> (8 * gi)) & 0xffu;
+        uint32_t sc = (w.sc >> (8 * gi)) & 0xffu;
+        int32_t s1 = 1 + 2 * (int32_t)(sc & 0x0f);
+        int32_t s2 = 1 + 2 * (int32_t)(sc >> 4);
+        int32_t part[2] = {0, 0};
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            uint32_t idx = ((qsw >> (8 * l)) & 0xffu) | ((qh << (8 - 2 * l)) & 0x300u);
+            uint32_t code = code_tab[idx * 32];
+            uint32_t sp = sign_tab[((sgw >> (8 * l)) & 0xffu) * 32];
+            uint32_t sel = code | sp;
+            uint32_t g0 = __byte_perm(kIq2PoolPos, kIq2PoolNeg, sel & 0xffffu);
+            uint32_t g1 = __byte_perm(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
+            int32_t p = dp4a(g0, a.w[gi * 8 + 2 * l], 0);
+            p = dp4a(g1, a.w[gi * 8 + 2 * l + 1], p);
+            part[l >> 1] += p;
+        }
+        total += s1 * part[0] + s2 * part[1];
+    }
+    IqPart r;
+    r.sum = total;
+    r.d = w.d;
+    return r;
+}
+
+// dot_iq3_s (q8_k.rs:380-428) over groups 4h..4h+3 of one block. Signs are
+// applied to the activations: na holds the negated activation words and a
+// byte permute picks a or -a per lane.
+__device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const uint32_t* na, const uint32_t* grid_tab,
+                                         const uint32_t* sign_tab) {
+    int32_t total = 0;
+#pragma unroll
+    for (int gi = 0; gi < 4; gi++) {
+        uint32_t qa = gi < 2 ? w32(w.qs0, gi * 2) : w32(w.qs1, (gi - 2) * 2);
+        uint32_t qb = gi < 2 ? w32(w.qs0, gi * 2 + 1) : w32(w.qs1, (gi - 2) * 2 + 1);
+        uint32_t sgw = w32(w.sg, gi);
+        uint32_t qh = (w.qh >> (8 * gi)) & 0xffu;
+        // pair p = 2h + (gi>>1), nibble gi&1
+        uint32_t sc = (w.sc >> (8 * (gi >> 1))) & 0xffu;
+        int32_t scale = 2 * (int32_t)((gi & 1) ? (sc >> 4) : (sc & 0x0f)) + 1;
+        int32_t gsum = 0;
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            uint32_t q2 = l < 2 ? qa : qb;
+            uint32_t lo1 = (q2 >> (16 * (l & 1))) & 0xffu;
+            uint32_t lo2 = (q2 >> (16 * (l & 1) + 8)) & 0xffu;
+            uint32_t i1 = lo1 | ((qh << (8 - 2 * l)) & 0x100u);
+            uint32_t i2 = lo2 | ((qh << (7 - 2 * l)) & 0x100u);
+            uint32_t g1 = grid_tab[i1 * 32];
+            uint32_t g2 = grid_tab[i2 * 32];
+            uint32_t sp = sign_tab[((sgw >> (8 * l)) & 0xffu) * 32];
+            // selector nibble i = i (+4 when lane i is negative)
+            uint32_t sel1 = 0x3210u | (sp & 0xffffu);
+            uint32_t sel2 = 0x3210u | (sp >> 16);
+            int wi = gi * 8 + 2 * l;
+            uint32_t a1 = __byte_perm(a.w[wi], na[wi], sel1);
+            uint32_t a2 = __byte_perm(a.w[wi + 1], na[wi + 1], sel2);
+            gsum = dp4a(g1, a1, gsum);
+            gsum = dp4a(g2, a2, gsum);
+        }
+        total += gsum * scale;
+    }
+    IqPart r;
+    r.sum = total;
+    r.d = w.d;
+    return r;
+}
+
+// scale_min (k_quants.rs:231-240) from three little-endian words of scales[12].
+__device__ __forceinline__ void scale_min_dev(const uint32_t sc[3], int j, int32_t& s, int32_t& m) {
+    auto byte = [&](int i) -> uint32_t { return (sc[i >> 2] >> (8 * (i & 3))) & 0xffu; };
+    if (j < 4) {
+        s = (int32_t)(byte(j) & 0x3f);
+        m = (int32_t)(byte(j + 4) & 0x3f);
+    } else {
+        s = (int32_t)((byte(j + 4) & 0x0f) | ((byte(j - 4) >> 6) << 4));
+        m = (int32_t)((byte(j + 4) >> 4) | ((byte(j) >> 6) << 4));
+    }
+}
+
+// dot_q4_or_q5_k (q8_k.rs:257-312) over sub-blocks 4h..4h+3 of one block.
+template <bool kQ5>
+__device__ __forceinline__ KPart dot_hb_k(const uint4* qs, const uint4* qh, const uint32_t sc[3], uint32_t dm,
+                                          const ActHB& a, int h) {
+    KPart r;
+#pragma unroll
+    for (int l = 0; l < 8; l++) r.lane[l] = 0;
+    int32_t ms = 0;
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {  // qs group g = 2h + gg covers sub-blocks 2g (lo) and 2g+1 (hi)
+        int g = 2 * h + gg;
+        int32_t s_lo, m_lo, s_hi, m_hi;
+        scale_min_dev(sc, 2 * g, s_lo, m_lo);
+        scale_min_dev(sc, 2 * g + 1, s_hi, m_hi);
+        // Q8_K group sums of the 16-lane groups of these two sub-blocks
+        ms += (a.bsum[4 * gg + 0] + a.bsum[4 * gg + 1]) * m_lo;
+        ms += (a.bsum[4 * gg + 2] + a.bsum[4 * gg + 3]) * m_hi;
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            uint32_t q = w32(qs[2 * gg + (k >> 2)], k & 3);
+            uint32_t lo = q & 0x0f0f0f0fu;
+            uint32_t hi = (q >> 4) & 0x0f0f0f0fu;
+            if (kQ5) {
+                uint32_t hb = w32(qh[k >> 2], k & 3);
+                lo |= ((hb >> (2 * g)) & 0x01010101u) << 4;
+                hi |= ((hb >> (2 * g + 1)) & 0x01010101u) << 4;
+            }
+            // act word for sub-block (4h + 2gg [+1]) lane k: index 8*(2gg [+1]) + k
+            int32_t plo = dp4a(lo, a.w[8 * (2 * gg) + k], 0);
+            int32_t phi = dp4a(hi, a.w[8 * (2 * gg + 1) + k], 0);
+            r.lane[k] += s_lo * plo + s_hi * phi;
+        }
+    }
+    r.min_sum = ms;
+    r.dm = dm;
+    return r;
+}
+
+__device__ __forceinline__ KPart dot_hb(const Q4HB& w, const ActHB& a, int h) {
+    return dot_hb_k<false>(w.qs, nullptr, w.sc, w.dm, a, h);
+}
+__device__ __forceinline__ KPart dot_hb(const Q5HB& w, const ActHB& a, int h) {
+    return dot_hb_k<true>(w.qs, w.qh, w.sc, w.dm, a, h);
+}
+
+// ------------------------------------------------------------ block products
+// The per-block f32 products of the reference tails, computed by the thread
+// that holds half 0 after adding half 1's integers (shfl_xor 1).
+
+__device__ __forceinline__ float iq_block_product(const IqPart& p, float dx) {
+    float scale = __fmul_rn(h2f(p.d), dx);
+    return __fmul_rn(scale, __int2float_rn(p.sum));
+}
+
+// The nine products of dot_q4_or_q5_k's per-block tail (q8_k.rs:314-320).
+__device__ __forceinline__ void k_block_products(const KPart& p, float dx, float out[9]) {
+    float scale = __fmul_rn(h2f(p.dm & 0xffffu), dx);
+#pragma unroll
+    for (int l = 0; l < 8; l++) out[l] = __fmul_rn(scale, __int2float_rn(p.lane[l]));
+    float mscale = __fmul_rn(h2f(p.dm >> 16), dx);
+    out[8] = __fmul_rn(mscale, __int2float_rn(p.min_sum));
+}
+
+// Sequential per-row tails: products for blocks 0..nb-1 at stride `stride`.
+__device__ __forceinline__ float iq_tail(const float* prod, int nb, int stride, bool iq2) {
+    float sum = 0.0f;
+    for (int b = 0; b < nb; b++) sum = __fadd_rn(sum, prod[b * stride]);
+    return iq2 ? __fmul_rn(0.125f, sum) : sum;
+}
+
+__device__ __forceinline__ float k_tail(const float* prod, int nb, int stride) {
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float sum = 0.0f;
+    for (int b = 0; b < nb; b++) {
+#pragma unroll
+        for (int l = 0; l < 8; l++) sums[l] = __fadd_rn(sums[l], prod[b * stride + l]);
+        sum = __fsub_rn(sum, prod[b * stride + 8]);
+    }
+#pragma unroll
+    for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, sums[l]);
+    return sum;
+}
+
+}  // namespace lbk

@@ -1,0 +1,59 @@
+// lbk_moe.h -- launch interface of the fused MoE kernels (moe.cu).
+#pragma once
+
+#include "lbk_kernels.h"
+
+namespace lbk {
+
+struct MoeGateUpArgs {
+    uint64_t hidden, ffn;
+    int nb_h, nb_f;
+    int tpr_h;                       // threads per row over the hidden width
+    uint64_t tokens;
+    uint64_t k;                      // routed experts per token
+    uint64_t experts;
+    const uint8_t* const* gate;      // [experts] planar matrices
+    const uint8_t* const* up;
+    const uint8_t* sgate;            // shared expert
+    const uint8_t* sup;
+    const lbk_routed* routed;        // [tokens][k]
+    const uint8_t* q8x;              // [tokens][nb_h][292]
+    float* h;                        // [tokens][k+1][ffn]
+    uint8_t* hq;                     // [tokens][k+1][nb_f][292]
+    unsigned int* counters;          // [tokens][k+1][nb_f], zero between launches
+    uint64_t chunk_r, chunk_s;       // rows per warp (routed / shared slot)
+    uint64_t chunks_r, chunks_s;     // chunks per slot
+    int bmax_iq, bmax_k;             // rows per tail batch
+    uint64_t prod_floats;            // per-warp product buffer
+    uint64_t chain_floats;           // per-warp chain + result buffer (>= 9*dots + 64)
+    DeviceStatus* status;
+    Tables tables;
+};
+
+struct MoeDownArgs {
+    uint64_t hidden, ffn;
+    int nb_f;
+    int tpr_f;                       // threads per row over the ffn width
+    uint64_t tokens;
+    uint64_t k;
+    uint64_t experts;
+    const uint8_t* const* down;      // [experts] planar matrices
+    const uint8_t* sdown;
+    const lbk_routed* routed;
+    const uint8_t* hq;               // [tokens][k+1][nb_f][292]
+    float* out;                      // [tokens][hidden]
+    uint64_t rows_per_cta;
+    uint64_t wps;                    // warps per slot
+    uint64_t prod_floats;
+    uint64_t chain_floats;
+    DeviceStatus* status;
+    Tables tables;
+};
+
+bool moe_fused_supported(int gate_type, int shared_gate_type, int down_type, int shared_down_type);
+size_t moe_gate_up_fixed_smem(int gate_type, int shared_gate_type);
+size_t moe_down_fixed_smem(int down_type, int shared_down_type);
+cudaError_t launch_moe_gate_up(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, cudaStream_t stream);
+cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream);
+
+}  // namespace lbk

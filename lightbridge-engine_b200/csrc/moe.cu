@@ -1,0 +1,543 @@
+// moe.cu -- fused routed + shared SwiGLU expert FFN over HBM-resident tables.
+//
+// Replaces the per-token expert work of hy3_moe_finish_token
+// (bridge-kernels-reference/src/layer.rs:610-659) -> moe_routed_by_id_into
+// (moe.rs:64-147) -> expert_swiglu_accumulate_into (activation.rs:104-144) ->
+// gemv_into / gemv_accumulate_scaled_into (gemv.rs:88-174):
+//
+//   gate/up kernel: for every (token, slot) -- slot j < k the j-th routed
+//     expert in ascending ID, slot k the shared expert -- both projections of
+//     the token's Q8_K activations, SwiGLU (activation.rs:170-178), and the
+//     Q8_K quantization of the hidden vector, done per 256-row block by the
+//     warp that completes the block (arrival counter, no grid barrier);
+//   down kernel: every output row's k+1 down-projection dots, then
+//     out = 0; out += c_j * dot_j (ascending ID); out += 1.0 * dot_shared --
+//     the reference's exact f32 combine order (moe.rs:331-336).
+//
+// The reference runs every expert twice (a preflight pass into scratch, then
+// the accepting pass); here validation is carried by the device status word
+// instead: a non-finite SwiGLU value or scale is reported and the down kernel
+// then leaves `out` untouched.
+
+#include "lbk_kernels.h"
+#include "lbk_moe.h"
+
+namespace lbk {
+
+namespace {
+
+constexpr int kGUThreads = 512;
+constexpr int kGUWarps = kGUThreads / 32;
+
+template <int T>
+struct HBOf;
+template <>
+struct HBOf<LBK_TYPE_IQ2_S> {
+    using type = Iq2HB;
+};
+template <>
+struct HBOf<LBK_TYPE_IQ3_S> {
+    using type = Iq3HB;
+};
+template <>
+struct HBOf<LBK_TYPE_Q4_K> {
+    using type = Q4HB;
+};
+template <>
+struct HBOf<LBK_TYPE_Q5_K> {
+    using type = Q5HB;
+};
+
+template <int T>
+constexpr bool is_iq() {
+    return T == LBK_TYPE_IQ2_S || T == LBK_TYPE_IQ3_S;
+}
+
+// Loads a thread's half block of a Q8_K row held in global memory.
+template <bool kTr>
+__device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, int b, int h, bool bsums) {
+    const uint8_t* blk = q8row + (size_t)b * kQ8Bytes;
+    const uint32_t* qw = reinterpret_cast<const uint32_t*>(blk + 4 + 128 * h);
+#pragma unroll
+    for (int i = 0; i < 32; i++) a.w[i] = __ldcg(reinterpret_cast<const unsigned int*>(qw + i));
+    if (kTr) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint32_t n[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) n[i] = a.w[8 * j + i];
+            transpose4(n[0], n[2], n[4], n[6], a.w[8 * j + 0], a.w[8 * j + 1], a.w[8 * j + 2], a.w[8 * j + 3]);
+            transpose4(n[1], n[3], n[5], n[7], a.w[8 * j + 4], a.w[8 * j + 5], a.w[8 * j + 6], a.w[8 * j + 7]);
+        }
+    }
+    a.d = __uint_as_float(__ldcg(reinterpret_cast<const unsigned int*>(blk)));
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        uint32_t v = bsums ? __ldcg(reinterpret_cast<const unsigned short*>(blk + 260 + 16 * h + 2 * i)) : 0u;
+        a.bsum[i] = (int32_t)(int16_t)v;
+    }
+}
+
+// Integer dot of one half block, dispatched on the weight type.
+template <int T>
+struct HBDot {
+    template <class HB>
+    __device__ __forceinline__ static void run(const HB& w, const ActHB& a, const uint32_t* na, const uint32_t* t0,
+                                               const uint32_t* t1, int h, IqPart& ip, KPart& kp) {
+        if constexpr (T == LBK_TYPE_IQ2_S) {
+            ip = dot_hb(w, a, t0, t1);
+        } else if constexpr (T == LBK_TYPE_IQ3_S) {
+            ip = dot_hb(w, a, na, t0, t1);
+        } else {
+            kp = dot_hb(w, a, h);
+        }
+        (void)na;
+        (void)h;
+    }
+};
+
+// Tails of a warp's batch: prod[(row*nmat + mat)][nb][kTail] -> res[row*nmat + mat].
+// Chains are spread over lanes (one lane per chain), so a batch costs about
+// nb dependent adds regardless of its size.
+template <int T>
+__device__ __forceinline__ void warp_tails(const float* prod, int ndots, int nb, float* chains, float* res) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (is_iq<T>()) {
+        for (int c = lane; c < ndots; c += 32) {
+            float v = iq_tail(prod + (size_t)c * nb, nb, 1, T == LBK_TYPE_IQ2_S);
+            res[c] = v;
+        }
+    } else {
+        for (int c = lane; c < ndots * 9; c += 32) {
+            int d = c / 9, l = c % 9;
+            const float* p = prod + (size_t)d * nb * 9 + l;
+            float acc = 0.0f;
+            if (l < 8) {
+                for (int b = 0; b < nb; b++) acc = __fadd_rn(acc, p[b * 9]);
+            } else {
+                for (int b = 0; b < nb; b++) acc = __fsub_rn(acc, p[b * 9]);
+            }
+            chains[c] = acc;
+        }
+        __syncwarp();
+        for (int d = lane; d < ndots; d += 32) {
+            float sum = chains[d * 9 + 8];
+#pragma unroll
+            for (int l = 0; l < 8; l++) sum = __fadd_rn(sum, chains[d * 9 + l]);
+            res[d] = sum;
+        }
+    }
+    __syncwarp();
+}
+
+// Per-row products of one half block pair, written into prod[dot][b][kTail].
+template <int T>
+__device__ __forceinline__ void write_products(float* prod_dot, int b, int h, bool mine, IqPart ip, KPart kp, float dx,
+                                               DeviceStatus* st, uint64_t blk_id) {
+    if constexpr (is_iq<T>()) {
+        int other = __shfl_xor_sync(0xffffffffu, ip.sum, 1);
+        if (mine && h == 0) {
+            ip.sum += other;
+            prod_dot[b] = iq_block_product(ip, dx);
+            if (!h_finite(ip.d)) report(st, LBK_NON_FINITE_SCALE, blk_id, ip.d);
+        }
+    } else {
+#pragma unroll
+        for (int l = 0; l < 8; l++) kp.lane[l] += __shfl_xor_sync(0xffffffffu, kp.lane[l], 1);
+        kp.min_sum += __shfl_xor_sync(0xffffffffu, kp.min_sum, 1);
+        if (mine && h == 0) {
+            float pr[9];
+            k_block_products(kp, dx, pr);
+#pragma unroll
+            for (int i = 0; i < 9; i++) prod_dot[b * 9 + i] = pr[i];
+            if (!h_finite(kp.dm & 0xffffu) || !h_finite(kp.dm >> 16))
+                report(st, LBK_NON_FINITE_SCALE, blk_id, h_finite(kp.dm & 0xffffu) ? kp.dm >> 16 : kp.dm & 0xffffu);
+        }
+    }
+}
+
+template <int T>
+constexpr int table_bytes() {
+    return T == LBK_TYPE_IQ2_S ? kIq2CodeBytes : (T == LBK_TYPE_IQ3_S ? kIq3GridBytes : 0);
+}
+
+template <int T>
+__device__ __forceinline__ void fill_tables(uint32_t* tab, uint32_t* signs, const Tables& t) {
+    if constexpr (T == LBK_TYPE_IQ2_S) fill_iq2_codes(tab, t.iq2s_grid);
+    if constexpr (T == LBK_TYPE_IQ3_S) fill_iq3_grid(tab, t.iq3s_grid);
+    (void)signs;
+}
+
+// ---------------------------------------------------------------- gate / up
+
+// One warp = one (token, slot, row chunk). Shared memory:
+//   [routed-type table][shared-type table][sign table][per-warp prod][per-warp chains/results]
+template <int TG, int TS>
+struct GUSmem {
+    static constexpr int kTabG = table_bytes<TG>();
+    static constexpr int kTabS = (TS == TG) ? 0 : table_bytes<TS>();
+    static constexpr bool kSigns = is_iq<TG>() || is_iq<TS>();
+    static constexpr int kSignB = kSigns ? kSignBytes : 0;
+    static constexpr int kFixed = kTabG + kTabS + kSignB;
+};
+
+template <int T>
+__device__ __forceinline__ void gate_up_rows(const MoeGateUpArgs& a, uint64_t t, uint64_t slot, const uint8_t* gmat,
+                                             const uint8_t* umat, uint64_t r0, uint64_t r1, float* prod, float* chains,
+                                             float* res, const uint32_t* tab, const uint32_t* signs) {
+    using HB = typename HBOf<T>::type;
+    constexpr bool kIq = is_iq<T>();
+    const int lane = threadIdx.x & 31;
+    const int nb = a.nb_h;
+    const int tpr = a.tpr_h;
+    const int rps = 32 / tpr;
+    const int sub = lane / tpr, hb = lane % tpr;
+    const int b = hb >> 1, h = hb & 1;
+    const bool lane_on = hb < 2 * nb;
+    constexpr int kTail = TypeInfo<T>::kTail;
+
+    ActHB act;
+    uint32_t nact[32];
+    if (lane_on) {
+        load_act_global<!kIq>(act, a.q8x + t * (uint64_t)nb * kQ8Bytes, b, h, !kIq);
+        if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+        }
+    }
+    const uint32_t* t0 = tab + lane;
+    const uint32_t* t1 = signs + lane;
+    MatrixRef gm{gmat, a.ffn, nb}, um{umat, a.ffn, nb};
+
+    // Rows stream with a one-step prefetch; every `bmax` rows (a multiple of
+    // rps) the batch's tails and SwiGLU are replayed.
+    const int bmax = kIq ? a.bmax_iq : a.bmax_k;
+    float* hrow = a.h + (t * (a.k + 1) + slot) * a.ffn;
+    HB gcur, ucur;
+    if (lane_on && r0 + sub < r1) {
+        load_hb<LBK_LAYOUT_PLANAR>(gcur, gm, r0 + sub, b, h);
+        load_hb<LBK_LAYOUT_PLANAR>(ucur, um, r0 + sub, b, h);
+    }
+    uint64_t rb = r0;
+    for (uint64_t r = r0; r < r1; r += rps) {
+        const uint64_t row = r + sub;
+        const bool mine = lane_on && row < r1;
+        HB gw = gcur, uw = ucur;
+        const uint64_t nrow = row + rps;
+        if (lane_on && nrow < r1) {
+            load_hb<LBK_LAYOUT_PLANAR>(gcur, gm, nrow, b, h);
+            load_hb<LBK_LAYOUT_PLANAR>(ucur, um, nrow, b, h);
+        }
+        IqPart gi{0, 0}, ui{0, 0};
+        KPart gk, uk;
+#pragma unroll
+        for (int l = 0; l < 8; l++) gk.lane[l] = uk.lane[l] = 0;
+        gk.min_sum = uk.min_sum = 0;
+        gk.dm = uk.dm = 0;
+        if (mine) {
+            HBDot<T>::run(gw, act, nact, t0, t1, h, gi, gk);
+            HBDot<T>::run(uw, act, nact, t0, t1, h, ui, uk);
+        }
+        const int ri = (int)(row - rb);
+        float* pg = prod + (size_t)(ri * 2 + 0) * nb * kTail;
+        float* pu = prod + (size_t)(ri * 2 + 1) * nb * kTail;
+        write_products<T>(pg, b, h, mine, gi, gk, act.d, a.status, row * nb + b);
+        write_products<T>(pu, b, h, mine, ui, uk, act.d, a.status, row * nb + b);
+        const uint64_t rn = r + rps;
+        if (rn - rb >= (uint64_t)bmax || rn >= r1) {
+            const int nrows = (int)((rn < r1 ? rn : r1) - rb);
+            __syncwarp();
+            warp_tails<T>(prod, nrows * 2, nb, chains, res);
+            // SwiGLU per row; one lane per row
+            for (int q = lane; q < nrows; q += 32) {
+                float g = res[q * 2], u = res[q * 2 + 1];
+                float v = swiglu_ref(g, u);
+                if (!isfinite(v))
+                    report(a.status, LBK_NON_FINITE_VALUE, (t * (a.k + 1) + slot) * a.ffn + rb + q, __float_as_uint(v));
+                hrow[rb + q] = v;
+            }
+            __syncwarp();
+            rb = rn;
+        }
+    }
+}
+
+// Arrival counting on the 256-row Q8_K blocks of h; the completing warp
+// quantizes the block (quantize_row_q8_k_into, q8_k.rs:35-73).
+__device__ __forceinline__ void arrive_and_quantize(const MoeGateUpArgs& a, uint64_t t, uint64_t slot, uint64_t r0,
+                                                   uint64_t r1) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t sidx = t * (a.k + 1) + slot;
+    for (uint64_t blk = r0 / kQK; blk * kQK < r1; blk++) {
+        uint64_t lo = blk * kQK > r0 ? blk * kQK : r0;
+        uint64_t hi = (blk + 1) * kQK < r1 ? (blk + 1) * kQK : r1;
+        unsigned n = (unsigned)(hi - lo);
+        unsigned int* cnt = a.counters + sidx * a.nb_f + blk;
+        unsigned old = 0;
+        if (lane == 0) {
+            __threadfence();
+            old = atomicAdd(cnt, n);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old + n != (unsigned)kQK) continue;
+        __threadfence();
+        const float* hb = a.h + sidx * a.ffn + blk * kQK + lane * 8;
+        float v[8];
+        bool bad = false;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            v[i] = __ldcg(hb + i);
+            bad |= !isfinite(v[i]);
+        }
+        if (lane == 0) *cnt = 0u;  // ready for the next launch
+        if (__ballot_sync(0xffffffffu, bad)) continue;  // already reported by the SwiGLU check
+        Q8Block q = quantize_q8k_warp(v, lane);
+        uint8_t* o = a.hq + (sidx * a.nb_f + blk) * kQ8Bytes;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(o + 4);
+        ow[lane * 2] = q.q[0];
+        ow[lane * 2 + 1] = q.q[1];
+        int32_t pair = q.pair_sum + __shfl_xor_sync(0xffffffffu, q.pair_sum, 1);
+        if ((lane & 1) == 0) *reinterpret_cast<int16_t*>(o + 260 + lane) = (int16_t)pair;
+        if (lane == 0) *reinterpret_cast<float*>(o) = q.d;
+    }
+}
+
+template <int TG, int TS>
+__global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArgs a) {
+    using S = GUSmem<TG, TS>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t* tabG = reinterpret_cast<uint32_t*>(smem);
+    uint32_t* tabS = S::kTabS ? reinterpret_cast<uint32_t*>(smem + S::kTabG) : tabG;
+    uint32_t* signs = reinterpret_cast<uint32_t*>(smem + S::kTabG + S::kTabS);
+    float* prod_all = reinterpret_cast<float*>(smem + S::kFixed);
+    const int warp = threadIdx.x >> 5;
+    float* prod = prod_all + (size_t)warp * a.prod_floats;
+    float* chains = prod_all + (size_t)kGUWarps * a.prod_floats + (size_t)warp * a.chain_floats;
+    float* res = chains + a.chain_floats - 64;
+
+    fill_tables<TG>(tabG, signs, a.tables);
+    if constexpr (S::kTabS != 0) fill_tables<TS>(tabS, signs, a.tables);
+    if constexpr (S::kSigns) fill_signs(signs);
+    __syncthreads();
+
+    const uint64_t gw = (uint64_t)blockIdx.x * kGUWarps + warp;
+    const uint64_t routed_items = a.tokens * a.k * a.chunks_r;
+    const uint64_t shared_items = a.tokens * a.chunks_s;
+    if (gw < routed_items) {
+        uint64_t t = gw / (a.k * a.chunks_r);
+        uint64_t rem = gw % (a.k * a.chunks_r);
+        uint64_t j = rem / a.chunks_r, c = rem % a.chunks_r;
+        uint32_t e = a.routed[t * a.k + j].expert_id;
+        if (e >= a.experts) {  // reported; compute on expert 0 so the arrival counts stay balanced
+            if ((threadIdx.x & 31) == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
+            e = 0;
+        }
+        uint64_t r0 = c * a.chunk_r, r1 = r0 + a.chunk_r < a.ffn ? r0 + a.chunk_r : a.ffn;
+        gate_up_rows<TG>(a, t, j, a.gate[e], a.up[e], r0, r1, prod, chains, res, tabG, signs);
+        arrive_and_quantize(a, t, j, r0, r1);
+    } else if (gw < routed_items + shared_items) {
+        uint64_t q = gw - routed_items;
+        uint64_t t = q / a.chunks_s, c = q % a.chunks_s;
+        uint64_t r0 = c * a.chunk_s, r1 = r0 + a.chunk_s < a.ffn ? r0 + a.chunk_s : a.ffn;
+        gate_up_rows<TS>(a, t, a.k, a.sgate, a.sup, r0, r1, prod, chains, res, tabS, signs);
+        arrive_and_quantize(a, t, a.k, r0, r1);
+    }
+}
+
+// -------------------------------------------------------------------- down
+
+template <int TD, int TSD>
+struct DownSmem {
+    static constexpr int kTabD = table_bytes<TD>();
+    static constexpr int kTabS = (TSD == TD) ? 0 : table_bytes<TSD>();
+    static constexpr bool kSigns = is_iq<TD>() || is_iq<TSD>();
+    static constexpr int kSignB = kSigns ? kSignBytes : 0;
+    static constexpr int kFixed = kTabD + kTabS + kSignB;
+};
+
+template <int T>
+__device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint64_t slot, const uint8_t* dmat,
+                                          int wsub, uint64_t r0, uint64_t r1, float* prod, float* chains, float* res,
+                                          float* dots, const uint32_t* tab, const uint32_t* signs) {
+    using HB = typename HBOf<T>::type;
+    constexpr bool kIq = is_iq<T>();
+    constexpr int kTail = TypeInfo<T>::kTail;
+    const int lane = threadIdx.x & 31;
+    const int nb = a.nb_f;
+    const int tpr = a.tpr_f;
+    const int rps = 32 / tpr;
+    const int sub = lane / tpr, hb = lane % tpr;
+    const int b = hb >> 1, h = hb & 1;
+    const bool lane_on = hb < 2 * nb;
+    const uint64_t sidx = t * (a.k + 1) + slot;
+
+    ActHB act;
+    uint32_t nact[32];
+    if (lane_on) {
+        load_act_global<!kIq>(act, a.hq + sidx * (uint64_t)nb * kQ8Bytes, b, h, !kIq);
+        if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+        }
+    }
+    const uint32_t* t0 = tab + lane;
+    const uint32_t* t1 = signs + lane;
+    MatrixRef dm{dmat, a.hidden, nb};
+    // this warp's rows: r0 + wsub*rps + i*wps*rps + sub
+    const uint64_t stride = (uint64_t)a.wps * rps;
+    int nd = 0;
+    HB cur;
+    {
+        uint64_t row = r0 + (uint64_t)wsub * rps + sub;
+        if (lane_on && row < r1) load_hb<LBK_LAYOUT_PLANAR>(cur, dm, row, b, h);
+    }
+    for (uint64_t base = r0 + (uint64_t)wsub * rps; base < r1; base += stride) {
+        const uint64_t row = base + sub;
+        const bool mine = lane_on && row < r1;
+        HB w = cur;
+        const uint64_t nrow = row + stride;
+        if (lane_on && nrow < r1) load_hb<LBK_LAYOUT_PLANAR>(cur, dm, nrow, b, h);
+        IqPart ip{0, 0};
+        KPart kp;
+#pragma unroll
+        for (int l = 0; l < 8; l++) kp.lane[l] = 0;
+        kp.min_sum = 0;
+        kp.dm = 0;
+        if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
+        float* pd = prod + (size_t)(nd + sub) * nb * kTail;
+        write_products<T>(pd, b, h, mine, ip, kp, act.d, a.status, row * nb + b);
+        nd += rps;
+    }
+    __syncwarp();
+    warp_tails<T>(prod, nd, nb, chains, res);
+    // scatter results to dots[slot][row - r0]
+    for (int d = lane; d < nd; d += 32) {
+        uint64_t row = r0 + (uint64_t)wsub * rps + (uint64_t)(d / rps) * stride + (d % rps);
+        if (row < r1) dots[slot * a.rows_per_cta + (row - r0)] = res[d];
+    }
+}
+
+template <int TD, int TSD>
+__global__ void __launch_bounds__(576, 1) moe_down_kernel(MoeDownArgs a) {
+    using S = DownSmem<TD, TSD>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t* tabD = reinterpret_cast<uint32_t*>(smem);
+    uint32_t* tabS = S::kTabS ? reinterpret_cast<uint32_t*>(smem + S::kTabD) : tabD;
+    uint32_t* signs = reinterpret_cast<uint32_t*>(smem + S::kTabD + S::kTabS);
+    float* dots = reinterpret_cast<float*>(smem + S::kFixed);
+    float* prod_all = dots + (a.k + 1) * a.rows_per_cta;
+    const int warp = threadIdx.x >> 5;
+    const int nwarps = blockDim.x >> 5;
+    float* prod = prod_all + (size_t)warp * a.prod_floats;
+    float* chains = prod_all + (size_t)nwarps * a.prod_floats + (size_t)warp * a.chain_floats;
+    float* res = chains + a.chain_floats - 64;
+
+    fill_tables<TD>(tabD, signs, a.tables);
+    if constexpr (S::kTabS != 0) fill_tables<TSD>(tabS, signs, a.tables);
+    if constexpr (S::kSigns) fill_signs(signs);
+    __syncthreads();
+
+    const uint64_t t = blockIdx.y;
+    const uint64_t r0 = (uint64_t)blockIdx.x * a.rows_per_cta;
+    const uint64_t r1 = r0 + a.rows_per_cta < a.hidden ? r0 + a.rows_per_cta : a.hidden;
+    const uint64_t slot = warp / a.wps;
+    const int wsub = warp % a.wps;
+    if (slot < a.k) {
+        uint32_t e = a.routed[t * a.k + slot].expert_id;
+        if (e < a.experts) down_rows<TD>(a, t, slot, a.down[e], wsub, r0, r1, prod, chains, res, dots, tabD, signs);
+    } else if (slot == a.k) {
+        down_rows<TSD>(a, t, slot, a.sdown, wsub, r0, r1, prod, chains, res, dots, tabS, signs);
+    }
+    __syncthreads();
+    if (status_set(a.status)) return;  // validation failed upstream: leave out unchanged
+    for (uint64_t i = threadIdx.x; i < r1 - r0; i += blockDim.x) {
+        float acc = 0.0f;
+        for (uint64_t j = 0; j < a.k; j++) {
+            float c = a.routed[t * a.k + j].coefficient;
+            acc = __fadd_rn(acc, __fmul_rn(c, dots[j * a.rows_per_cta + i]));
+        }
+        acc = __fadd_rn(acc, __fmul_rn(1.0f, dots[a.k * a.rows_per_cta + i]));
+        a.out[t * a.hidden + r0 + i] = acc;
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+
+template <int TG, int TS>
+cudaError_t launch_gu(const MoeGateUpArgs& a, cudaStream_t stream) {
+    using S = GUSmem<TG, TS>;
+    size_t smem = S::kFixed + (size_t)kGUWarps * (a.prod_floats + a.chain_floats) * 4;
+    if (smem > kMaxSmem) return cudaErrorInvalidValue;
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_kernel<TG, TS>));
+    if (e != cudaSuccess) return e;
+    uint64_t items = a.tokens * a.k * a.chunks_r + a.tokens * a.chunks_s;
+    uint64_t ctas = (items + kGUWarps - 1) / kGUWarps;
+    moe_gate_up_kernel<TG, TS><<<(unsigned)ctas, kGUThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+template <int TD, int TSD>
+cudaError_t launch_down(const MoeDownArgs& a, cudaStream_t stream) {
+    using S = DownSmem<TD, TSD>;
+    int warps = (int)((a.k + 1) * a.wps);
+    size_t smem = S::kFixed + (size_t)(a.k + 1) * a.rows_per_cta * 4 + (size_t)warps * (a.prod_floats + a.chain_floats) * 4;
+    if (smem > kMaxSmem) return cudaErrorInvalidValue;
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_down_kernel<TD, TSD>));
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)((a.hidden + a.rows_per_cta - 1) / a.rows_per_cta), (unsigned)a.tokens);
+    moe_down_kernel<TD, TSD><<<grid, warps * 32, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
+__global__ void swiglu_kernel(const float* gate, const float* up, float* h, uint64_t n, DeviceStatus* st) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        float v = swiglu_ref(gate[i], up[i]);
+        if (!isfinite(v)) report(st, LBK_NON_FINITE_VALUE, i, __float_as_uint(v));
+        h[i] = v;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_swiglu(const float* gate, const float* up, float* h, uint64_t n, DeviceStatus* status,
+                          cudaStream_t stream) {
+    uint64_t grid = (n + 255) / 256;
+    if (grid > 4096) grid = 4096;
+    if (grid < 1) grid = 1;
+    swiglu_kernel<<<(unsigned)grid, 256, 0, stream>>>(gate, up, h, n, status);
+    return cudaGetLastError();
+}
+
+bool moe_fused_supported(int gate_type, int shared_gate_type, int down_type, int shared_down_type) {
+    bool gu = (gate_type == LBK_TYPE_IQ2_S || gate_type == LBK_TYPE_Q4_K) && shared_gate_type == LBK_TYPE_Q4_K;
+    bool dn = (down_type == LBK_TYPE_IQ3_S || down_type == LBK_TYPE_IQ2_S || down_type == LBK_TYPE_Q4_K) &&
+              shared_down_type == LBK_TYPE_Q4_K;
+    return gu && dn;
+}
+
+size_t moe_gate_up_fixed_smem(int gate_type, int shared_gate_type) {
+    if (gate_type == LBK_TYPE_IQ2_S && shared_gate_type == LBK_TYPE_Q4_K) return GUSmem<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>::kFixed;
+    return GUSmem<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>::kFixed;
+}
+
+size_t moe_down_fixed_smem(int down_type, int shared_down_type) {
+    (void)shared_down_type;
+    if (down_type == LBK_TYPE_IQ3_S) return DownSmem<LBK_TYPE_IQ3_S, LBK_TYPE_Q4_K>::kFixed;
+    if (down_type == LBK_TYPE_IQ2_S) return DownSmem<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>::kFixed;
+    return DownSmem<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>::kFixed;
+}
+
+cudaError_t launch_moe_gate_up(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, cudaStream_t stream) {
+    (void)shared_gate_type;
+    if (gate_type == LBK_TYPE_IQ2_S) return launch_gu<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, stream);
+    return launch_gu<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, stream);
+}
+
+cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream) {
+    (void)shared_down_type;
+    if (down_type == LBK_TYPE_IQ3_S) return launch_down<LBK_TYPE_IQ3_S, LBK_TYPE_Q4_K>(a, stream);
+    if (down_type == LBK_TYPE_IQ2_S) return launch_down<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, stream);
+    return launch_down<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, stream);
+}
+
+}  // namespace lbk

@@ -1,0 +1,137 @@
+// repack.cu -- GGUF <-> planar layout conversion and binary16 scale scans.
+//
+// The planar layout (described in include/lightbridge_kernels.h) is a byte
+// permutation of the GGUF bytes: every field of every block lands in its own
+// plane, and Q4_K / Q5_K quant bytes are reordered lane-major inside each
+// 32-byte group. It exists so that a thread's half block is a handful of
+// aligned 16-byte loads; both directions are exact.
+//
+// The scale scan restates validate_scales (bridge-quant-layout/src/k_quants.rs:178-208)
+// over a whole matrix, reporting the first non-finite block in row-major order.
+
+#include "lbk_kernels.h"
+
+namespace lbk {
+
+namespace {
+
+struct Field {
+    int src_off;   // offset inside the GGUF block
+    int bytes;     // field bytes per block
+    int lane_major;  // Q4_K/Q5_K qs or Q5_K qh: permute 32-byte groups
+};
+
+__host__ __device__ inline int fields_of(int type, Field* f) {
+    switch (type) {
+        case LBK_TYPE_IQ2_S:  // qs | signs | qh | scales | d
+            f[0] = {2, 32, 0};
+            f[1] = {34, 32, 0};
+            f[2] = {66, 8, 0};
+            f[3] = {74, 8, 0};
+            f[4] = {0, 2, 0};
+            return 5;
+        case LBK_TYPE_IQ3_S:  // qs | signs | qh | scales | d
+            f[0] = {2, 64, 0};
+            f[1] = {74, 32, 0};
+            f[2] = {66, 8, 0};
+            f[3] = {106, 4, 0};
+            f[4] = {0, 2, 0};
+            return 5;
+        case LBK_TYPE_Q4_K:  // qs (lane-major) | scales | d,dmin
+            f[0] = {16, 128, 1};
+            f[1] = {4, 12, 0};
+            f[2] = {0, 4, 0};
+            return 3;
+        default:  // Q5_K: qs (lane-major) | qh (lane-major) | scales | d,dmin
+            f[0] = {48, 128, 1};
+            f[1] = {16, 32, 1};
+            f[2] = {4, 12, 0};
+            f[3] = {0, 4, 0};
+            return 4;
+    }
+}
+
+// lane-major position of byte j of a 32-byte group: new[4k+i] = old[k+8i]
+__host__ __device__ inline int lane_major_pos(int j) {
+    int k = j & 7, i = j >> 3;  // old index j = k + 8i
+    return 4 * k + i;
+}
+
+__global__ void repack_kernel(RepackArgs a, int block_bytes) {
+    Field f[5];
+    int nf = fields_of(a.type, f);
+    const uint64_t nblk = a.rows * (uint64_t)a.nb;
+    for (uint64_t bi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; bi < nblk; bi += (uint64_t)gridDim.x * blockDim.x) {
+        uint64_t plane = 0;
+        for (int k = 0; k < nf; k++) {
+            const int fb = f[k].bytes;
+            for (int j = 0; j < fb; j++) {
+                int pj = j;
+                if (f[k].lane_major) pj = (j & ~31) + lane_major_pos(j & 31);
+                uint64_t g = bi * block_bytes + f[k].src_off + j;  // GGUF byte
+                uint64_t p = plane + bi * fb + pj;                   // planar byte
+                if (a.to_planar)
+                    a.dst[p] = a.src[g];
+                else
+                    a.dst[g] = a.src[p];
+            }
+            plane += nblk * (uint64_t)fb;
+        }
+    }
+}
+
+__global__ void scan_scales_kernel(int type, int layout, const uint8_t* data, uint64_t rows, int nb,
+                                   unsigned long long* first_bad) {
+    const uint64_t nblk = rows * (uint64_t)nb;
+    const bool two = type == LBK_TYPE_Q4_K || type == LBK_TYPE_Q5_K;
+    int bb = type == LBK_TYPE_IQ2_S ? 82 : type == LBK_TYPE_IQ3_S ? 110 : type == LBK_TYPE_Q4_K ? 144 : 176;
+    uint64_t dplane = type == LBK_TYPE_IQ2_S ? 80 : type == LBK_TYPE_IQ3_S ? 108 : type == LBK_TYPE_Q4_K ? 140 : 172;
+    for (uint64_t bi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; bi < nblk; bi += (uint64_t)gridDim.x * blockDim.x) {
+        const uint8_t* p = layout == LBK_LAYOUT_PLANAR ? data + nblk * dplane + bi * (two ? 4 : 2) : data + bi * bb;
+        uint32_t d = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
+        bool bad = !h_finite(d);
+        if (two) bad |= !h_finite((uint32_t)p[2] | ((uint32_t)p[3] << 8));
+        if (bad) atomicMin(first_bad, (unsigned long long)bi);
+    }
+}
+
+__global__ void report_scale_kernel(int type, int layout, const uint8_t* data, uint64_t rows, int nb,
+                                    const unsigned long long* first_bad, DeviceStatus* st) {
+    unsigned long long bi = *first_bad;
+    if (bi == ~0ull) return;
+    const uint64_t nblk = rows * (uint64_t)nb;
+    const bool two = type == LBK_TYPE_Q4_K || type == LBK_TYPE_Q5_K;
+    int bb = type == LBK_TYPE_IQ2_S ? 82 : type == LBK_TYPE_IQ3_S ? 110 : type == LBK_TYPE_Q4_K ? 144 : 176;
+    uint64_t dplane = type == LBK_TYPE_IQ2_S ? 80 : type == LBK_TYPE_IQ3_S ? 108 : type == LBK_TYPE_Q4_K ? 140 : 172;
+    const uint8_t* p = layout == LBK_LAYOUT_PLANAR ? data + nblk * dplane + bi * (two ? 4 : 2) : data + bi * bb;
+    uint32_t d = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
+    uint32_t bits = h_finite(d) ? ((uint32_t)p[2] | ((uint32_t)p[3] << 8)) : d;
+    report(st, LBK_NON_FINITE_SCALE, bi, bits);
+}
+
+}  // namespace
+
+cudaError_t launch_repack(const RepackArgs& a, cudaStream_t stream) {
+    int bb = a.type == LBK_TYPE_IQ2_S ? 82 : a.type == LBK_TYPE_IQ3_S ? 110 : a.type == LBK_TYPE_Q4_K ? 144 : 176;
+    uint64_t nblk = a.rows * (uint64_t)a.nb;
+    uint64_t grid = (nblk + 255) / 256;
+    if (grid > 65535) grid = 65535;
+    if (grid < 1) grid = 1;
+    repack_kernel<<<(unsigned)grid, 256, 0, stream>>>(a, bb);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_validate_scales(int type, int layout, const uint8_t* data, uint64_t rows, int nb,
+                                   unsigned long long* scratch_min, DeviceStatus* status, cudaStream_t stream) {
+    cudaError_t e = cudaMemsetAsync(scratch_min, 0xff, sizeof(unsigned long long), stream);
+    if (e != cudaSuccess) return e;
+    uint64_t nblk = rows * (uint64_t)nb;
+    uint64_t grid = (nblk + 255) / 256;
+    if (grid > 65535) grid = 65535;
+    if (grid < 1) grid = 1;
+    scan_scales_kernel<<<(unsigned)grid, 256, 0, stream>>>(type, layout, data, rows, nb, scratch_min);
+    report_scale_kernel<<<1, 1, 0, stream>>>(type, layout, data, rows, nb, scratch_min, status);
+    return cudaGetLastError();
+}
+
+}  // namespace lbk

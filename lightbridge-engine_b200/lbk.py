@@ -1,0 +1,294 @@
+"""ctypes binding of liblbk_b200.so (include/lightbridge_kernels.h).
+
+A thin host-side mirror of the reference's operator API for the quantized
+expert path -- gemv_into / gemv_accumulate_scaled_into / vec_dot_q8_k /
+quantize_row_q8_k_into / route_experts_into / expert_swiglu_accumulate_into /
+moe_routed_by_id_into -- over device memory held in torch tensors. Every call
+goes through the C ABI into the sm_100a kernels; there is no CPU or PyTorch
+fallback: if the library is missing, importing this module raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import subprocess
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = HERE / "liblbk_b200.so"
+
+TYPE_F32, TYPE_Q4_K, TYPE_Q5_K, TYPE_Q8_K, TYPE_IQ3_S, TYPE_IQ2_S = 0, 12, 13, 15, 21, 22
+BLOCK_BYTES = {TYPE_F32: 4, TYPE_Q4_K: 144, TYPE_Q5_K: 176, TYPE_IQ2_S: 82, TYPE_IQ3_S: 110}
+Q8K_BLOCK_BYTES = 292
+LAYOUT_GGUF, LAYOUT_PLANAR = 0, 1
+ROUTER_SEQUENTIAL, ROUTER_TREE = 0, 1
+
+STATUS = {
+    0: "OK", 1: "UNSUPPORTED_TYPE", 2: "ZERO_LOGICAL_ELEMENTS", 3: "LOGICAL_ELEMENTS_NOT_DIVISIBLE",
+    4: "ARITHMETIC_OVERFLOW", 5: "ENCODED_LENGTH_MISMATCH", 6: "OUTPUT_LENGTH_MISMATCH", 7: "NON_FINITE_SCALE",
+    8: "NON_FINITE_ACTIVATION", 9: "NON_FINITE_Q8_SCALE", 10: "DIMENSION_MISMATCH", 11: "SCRATCH_TOO_SMALL",
+    12: "NON_FINITE_VALUE", 13: "ROUTED_EXPERT_ORDER", 14: "DUPLICATE_ROUTED_EXPERT", 15: "INVALID_PARAMETER",
+    16: "ROUTING_TOPK", 17: "ROUTING_LENGTH", 18: "NON_FINITE_ROUTING_VALUE", 30: "CUDA_ERROR", 31: "TIMEOUT",
+    32: "NO_DEVICE",
+}
+
+
+class ErrorDetail(ctypes.Structure):
+    _fields_ = [
+        ("status", ctypes.c_int32),
+        ("cuda_error", ctypes.c_int32),
+        ("index", ctypes.c_uint64),
+        ("bits", ctypes.c_uint32),
+        ("expected", ctypes.c_uint64),
+        ("actual", ctypes.c_uint64),
+        ("message", ctypes.c_char * 160),
+    ]
+
+
+class Matrix(ctypes.Structure):
+    _fields_ = [
+        ("type", ctypes.c_int32),
+        ("layout", ctypes.c_int32),
+        ("input_width", ctypes.c_uint64),
+        ("output_width", ctypes.c_uint64),
+        ("data", ctypes.c_void_p),
+        ("bytes", ctypes.c_uint64),
+    ]
+
+
+class Expert(ctypes.Structure):
+    _fields_ = [("gate", Matrix), ("up", Matrix), ("down", Matrix)]
+
+
+class Routed(ctypes.Structure):
+    _fields_ = [("expert_id", ctypes.c_uint32), ("coefficient", ctypes.c_float)]
+
+
+class MoeWeights(ctypes.Structure):
+    _fields_ = [
+        ("experts", ctypes.POINTER(Expert)),
+        ("expert_count", ctypes.c_uint64),
+        ("shared", Expert),
+        ("router", Matrix),
+        ("selection_bias", ctypes.c_void_p),
+        ("top_k", ctypes.c_uint32),
+        ("weight_scale", ctypes.c_float),
+    ]
+
+
+class LbkError(RuntimeError):
+    def __init__(self, status: int, detail: ErrorDetail | None = None):
+        self.status = status
+        self.detail = detail
+        msg = STATUS.get(status, str(status))
+        if detail is not None:
+            msg += f" (index={detail.index}, bits={detail.bits:#x}, expected={detail.expected}, actual={detail.actual}, {detail.message.decode(errors='replace')})"
+        super().__init__(msg)
+
+
+def build() -> None:
+    """Compile liblbk_b200.so for sm_100a in place (nvcc; no GPU needed)."""
+    subprocess.run(["make", "-s", "-j8", "-C", str(HERE)], check=True)
+
+
+def _load() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` (or __graft_entry__.build())")
+    L = ctypes.CDLL(str(LIB_PATH))
+    P, U64, I32, U32, F = ctypes.c_void_p, ctypes.c_uint64, ctypes.c_int32, ctypes.c_uint32, ctypes.c_float
+    PM = ctypes.POINTER(Matrix)
+    PE = ctypes.POINTER(Expert)
+    sigs = {
+        "lbk_abi_version": ([], I32),
+        "lbk_backend_name": ([], ctypes.c_char_p),
+        "lbk_context_create": ([I32, ctypes.POINTER(P)], I32),
+        "lbk_context_destroy": ([P], I32),
+        "lbk_context_sync_status": ([P, P, ctypes.POINTER(ErrorDetail)], I32),
+        "lbk_last_error_detail": ([ctypes.POINTER(ErrorDetail)], None),
+        "lbk_required_q8k_bytes": ([U64, ctypes.POINTER(U64)], I32),
+        "lbk_matrix_bytes": ([I32, U64, U64, ctypes.POINTER(U64)], I32),
+        "lbk_quantize_q8k": ([P, P, U64, P, U64, P], I32),
+        "lbk_vec_dot_q8k": ([P, PM, P, U64, P, P, P], I32),
+        "lbk_gemv": ([P, PM, P, P, P, U64, P], I32),
+        "lbk_gemv_accumulate_scaled": ([P, PM, P, P, F, P, U64, P], I32),
+        "lbk_router_logits": ([P, PM, P, U64, P, I32, P], I32),
+        "lbk_route_topk": ([P, P, P, U64, U64, U32, F, P, P], I32),
+        "lbk_expert_workspace_bytes": ([PE, ctypes.POINTER(U64)], I32),
+        "lbk_expert_swiglu_accumulate": ([P, PE, P, P, F, P, U64, P], I32),
+        "lbk_moe_layer_create": ([P, ctypes.POINTER(MoeWeights), P, ctypes.POINTER(P)], I32),
+        "lbk_moe_layer_destroy": ([P], I32),
+        "lbk_moe_layer_fused": ([P], I32),
+        "lbk_moe_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
+        "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
+        "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
+        "lbk_moe_layer_trace": ([P, I32], I32),
+        "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
+        "lbk_repack": ([P, PM, P, U64, P], I32),
+        "lbk_unpack": ([P, PM, P, U64, P], I32),
+        "lbk_validate_matrix": ([P, PM, P], I32),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    return L
+
+
+lib = _load()
+EXPORTED = (
+    "lbk_abi_version lbk_backend_name lbk_context_create lbk_context_destroy lbk_context_sync_status "
+    "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
+    "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
+    "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused "
+    "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_layer_trace lbk_moe_layer_trace_read "
+    "lbk_repack lbk_unpack lbk_validate_matrix"
+).split()
+
+
+def last_error() -> ErrorDetail:
+    d = ErrorDetail()
+    lib.lbk_last_error_detail(ctypes.byref(d))
+    return d
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise LbkError(status, last_error())
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    return stream
+
+
+def matrix(ty: int, input_width: int, output_width: int, data, layout: int = LAYOUT_GGUF) -> Matrix:
+    """Descriptor of a packed matrix held in a device tensor (uint8 / f32)."""
+    nbytes = data.numel() * data.element_size()
+    return Matrix(ty, layout, input_width, output_width, data.data_ptr(), nbytes)
+
+
+class Context:
+    """Per-device context (status word, codebooks). Mirrors the reference's
+    CpuBackend (bridge-kernels-cpu/src/lib.rs:75-118): create once, reuse."""
+
+    def __init__(self, device: int = 0):
+        p = ctypes.c_void_p()
+        check(lib.lbk_context_create(device, ctypes.byref(p)))
+        self.ptr = p
+        self.device = device
+
+    def close(self) -> None:
+        if self.ptr:
+            lib.lbk_context_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):  # pragma: no cover
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def sync_status(self, stream=None) -> int:
+        d = ErrorDetail()
+        st = lib.lbk_context_sync_status(self.ptr, _stream(stream), ctypes.byref(d))
+        self.last_detail = d
+        return st
+
+    def raise_status(self, stream=None) -> None:
+        st = self.sync_status(stream)
+        if st != 0:
+            raise LbkError(st, self.last_detail)
+
+    # -- kernels (device tensors) --------------------------------------
+    def quantize_q8k(self, x, q8, stream=None) -> None:
+        check(lib.lbk_quantize_q8k(self.ptr, _ptr(x), x.numel(), _ptr(q8), q8.numel(), _stream(stream)))
+
+    def vec_dot(self, m: Matrix, q8, out, block_sums=None, stream=None) -> None:
+        check(lib.lbk_vec_dot_q8k(self.ptr, ctypes.byref(m), _ptr(q8), q8.numel(), _ptr(out), _ptr(block_sums), _stream(stream)))
+
+    def gemv(self, m: Matrix, x, y, q8_scratch=None, stream=None) -> None:
+        n = 0 if q8_scratch is None else q8_scratch.numel()
+        check(lib.lbk_gemv(self.ptr, ctypes.byref(m), _ptr(x), _ptr(y), _ptr(q8_scratch), n, _stream(stream)))
+
+    def gemv_accumulate_scaled(self, m: Matrix, x, y, scale: float, q8_scratch=None, stream=None) -> None:
+        n = 0 if q8_scratch is None else q8_scratch.numel()
+        check(lib.lbk_gemv_accumulate_scaled(self.ptr, ctypes.byref(m), _ptr(x), _ptr(y), float(scale), _ptr(q8_scratch), n, _stream(stream)))
+
+    def router_logits(self, router: Matrix, x, tokens: int, logits, mode: int = ROUTER_SEQUENTIAL, stream=None) -> None:
+        check(lib.lbk_router_logits(self.ptr, ctypes.byref(router), _ptr(x), tokens, _ptr(logits), mode, _stream(stream)))
+
+    def route_topk(self, logits, bias, expert_count: int, tokens: int, k: int, weight_scale: float, routed, stream=None) -> None:
+        check(lib.lbk_route_topk(self.ptr, _ptr(logits), _ptr(bias), expert_count, tokens, k, float(weight_scale), _ptr(routed), _stream(stream)))
+
+    def expert_workspace_bytes(self, e: Expert) -> int:
+        n = ctypes.c_uint64()
+        check(lib.lbk_expert_workspace_bytes(ctypes.byref(e), ctypes.byref(n)))
+        return n.value
+
+    def expert_swiglu_accumulate(self, e: Expert, x, dst, coef: float, workspace, stream=None) -> None:
+        check(lib.lbk_expert_swiglu_accumulate(self.ptr, ctypes.byref(e), _ptr(x), _ptr(dst), float(coef), _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def repack(self, m: Matrix, dst, stream=None) -> None:
+        check(lib.lbk_repack(self.ptr, ctypes.byref(m), _ptr(dst), dst.numel(), _stream(stream)))
+
+    def unpack(self, m: Matrix, dst, stream=None) -> None:
+        check(lib.lbk_unpack(self.ptr, ctypes.byref(m), _ptr(dst), dst.numel(), _stream(stream)))
+
+    def validate_matrix(self, m: Matrix, stream=None) -> None:
+        check(lib.lbk_validate_matrix(self.ptr, ctypes.byref(m), _stream(stream)))
+
+
+class MoeLayer:
+    """A registered, HBM-resident MoE layer (lbk_moe_layer_create)."""
+
+    def __init__(self, ctx: Context, experts: list[Expert], shared: Expert, router: Matrix, bias, top_k: int,
+                 weight_scale: float, stream=None):
+        self.ctx = ctx
+        self._experts = (Expert * len(experts))(*experts)
+        self._w = MoeWeights(
+            ctypes.cast(self._experts, ctypes.POINTER(Expert)), len(experts), shared, router, bias.data_ptr(), top_k,
+            float(weight_scale),
+        )
+        self._keep = [bias]
+        p = ctypes.c_void_p()
+        check(lib.lbk_moe_layer_create(ctx.ptr, ctypes.byref(self._w), _stream(stream), ctypes.byref(p)))
+        self.ptr = p
+        self.top_k = top_k
+        self.hidden = shared.gate.input_width
+
+    @property
+    def fused(self) -> bool:
+        return bool(lib.lbk_moe_layer_fused(self.ptr))
+
+    def workspace_bytes(self, tokens: int) -> int:
+        n = ctypes.c_uint64()
+        check(lib.lbk_moe_workspace_bytes(self.ptr, tokens, ctypes.byref(n)))
+        return n.value
+
+    def forward(self, x, tokens: int, out, workspace, routed_out=None, router_mode: int = ROUTER_TREE, stream=None) -> None:
+        check(lib.lbk_moe_forward(self.ptr, _ptr(x), tokens, _ptr(out), _ptr(routed_out), router_mode, _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def routed(self, x, tokens: int, routed, out, workspace, stream=None) -> None:
+        check(lib.lbk_moe_routed(self.ptr, _ptr(x), tokens, _ptr(routed), _ptr(out), _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def trace(self, enable: bool = True) -> None:
+        check(lib.lbk_moe_layer_trace(self.ptr, int(enable)))
+
+    def trace_read(self) -> tuple[float, float, float]:
+        ms = (ctypes.c_float * 3)()
+        check(lib.lbk_moe_layer_trace_read(self.ptr, ms))
+        return ms[0], ms[1], ms[2]
+
+    def close(self) -> None:
+        if self.ptr:
+            lib.lbk_moe_layer_destroy(self.ptr)
+            self.ptr = None

@@ -1,0 +1,100 @@
+"""Seeded synthetic packed weights and activations for the benchmark configs.
+
+The reference measures only a real 96 GB checkpoint that is not available
+here, so every input is synthetic with the configs' shapes and value
+distributions: packed blocks are uniform random bytes except the binary16
+scale fields d (and dmin for K-quants), which are drawn from U(lo, hi) and
+rounded to binary16, so every scale is finite; activations are N(0, 1); the
+F32 router is N(0, 0.02).
+
+Two generators give the same distributions: numpy (host; parity tests, the
+CPU baseline) and torch on the device (the benchmark's multi-GB tables).
+Also holds planar_np, a numpy restatement of the planar layout that the CPU
+tests use to pin the device repack kernel.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+TYPE_F32, TYPE_Q4_K, TYPE_Q5_K, TYPE_IQ3_S, TYPE_IQ2_S = 0, 12, 13, 21, 22
+BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q5_K: 176, TYPE_IQ2_S: 82, TYPE_IQ3_S: 110}
+SCALE_FIELDS = {TYPE_Q4_K: 2, TYPE_Q5_K: 2, TYPE_IQ2_S: 1, TYPE_IQ3_S: 1}
+# d ranges of the configs: K-quants U(0.001, 0.02), IQ U(0.001, 0.01)
+D_RANGE = {TYPE_Q4_K: (0.001, 0.02), TYPE_Q5_K: (0.001, 0.02), TYPE_IQ2_S: (0.001, 0.01), TYPE_IQ3_S: (0.001, 0.01)}
+
+
+def matrix_bytes(ty: int, in_w: int, out_w: int) -> int:
+    return in_w // 256 * BLOCK_BYTES[ty] * out_w
+
+
+def packed_np(rng: np.random.Generator, ty: int, in_w: int, out_w: int, d_range=None) -> np.ndarray:
+    """GGUF-layout packed matrix [in_w, out_w] as uint8 (host)."""
+    lo, hi = d_range or D_RANGE[ty]
+    bb = BLOCK_BYTES[ty]
+    nblk = in_w // 256 * out_w
+    w = rng.integers(0, 256, size=(nblk, bb), dtype=np.uint8)
+    for f in range(SCALE_FIELDS[ty]):
+        d = rng.uniform(lo, hi, size=nblk).astype(np.float16)
+        w[:, 2 * f : 2 * f + 2] = d.view(np.uint8).reshape(nblk, 2)
+    return w.reshape(-1)
+
+
+def packed_torch(gen, ty: int, in_w: int, out_w: int, device, d_range=None):
+    """Same distribution, generated on the device with a seeded torch.Generator."""
+    import torch
+
+    lo, hi = d_range or D_RANGE[ty]
+    bb = BLOCK_BYTES[ty]
+    nblk = in_w // 256 * out_w
+    w = torch.randint(0, 256, (nblk, bb), dtype=torch.uint8, device=device, generator=gen)
+    for f in range(SCALE_FIELDS[ty]):
+        d = torch.empty(nblk, dtype=torch.float32, device=device).uniform_(lo, hi, generator=gen).to(torch.float16)
+        w[:, 2 * f : 2 * f + 2] = d.view(torch.uint8).view(nblk, 2)
+    return w.view(-1)
+
+
+# ---------------------------------------------------------------- planar
+
+_FIELDS = {  # (GGUF offset, bytes per block, lane-major) in plane order
+    TYPE_IQ2_S: [(2, 32, False), (34, 32, False), (66, 8, False), (74, 8, False), (0, 2, False)],
+    TYPE_IQ3_S: [(2, 64, False), (74, 32, False), (66, 8, False), (106, 4, False), (0, 2, False)],
+    TYPE_Q4_K: [(16, 128, True), (4, 12, False), (0, 4, False)],
+    TYPE_Q5_K: [(48, 128, True), (16, 32, True), (4, 12, False), (0, 4, False)],
+}
+
+
+def _lane_major(field: np.ndarray) -> np.ndarray:
+    # per 32-byte group: new[4k+i] = old[k+8i]
+    n = field.shape[0]
+    g = field.reshape(n, -1, 4, 8)  # [blk, group, i, k] with old index k + 8i
+    return g.transpose(0, 1, 3, 2).reshape(n, -1)  # [blk, group, k, i] -> index 4k + i
+
+
+def _lane_major_inv(field: np.ndarray) -> np.ndarray:
+    n = field.shape[0]
+    g = field.reshape(n, -1, 8, 4)  # [blk, group, k, i]
+    return g.transpose(0, 1, 3, 2).reshape(n, -1)
+
+
+def planar_np(ty: int, gguf: np.ndarray) -> np.ndarray:
+    """GGUF bytes -> planar bytes (the layout of lbk_repack)."""
+    bb = BLOCK_BYTES[ty]
+    blocks = gguf.reshape(-1, bb)
+    planes = []
+    for off, nbytes, lm in _FIELDS[ty]:
+        f = blocks[:, off : off + nbytes]
+        planes.append((_lane_major(f) if lm else f).reshape(-1))
+    return np.concatenate(planes)
+
+
+def gguf_from_planar_np(ty: int, planar: np.ndarray) -> np.ndarray:
+    bb = BLOCK_BYTES[ty]
+    nblk = planar.size // bb
+    out = np.zeros((nblk, bb), dtype=np.uint8)
+    pos = 0
+    for off, nbytes, lm in _FIELDS[ty]:
+        f = planar[pos : pos + nblk * nbytes].reshape(nblk, nbytes)
+        out[:, off : off + nbytes] = _lane_major_inv(f) if lm else f
+        pos += nblk * nbytes
+    return out.reshape(-1)

@@ -1,0 +1,107 @@
+"""Shared helpers of the GPU parity tests (device buffers via torch, the C
+ABI via lbk, the CPU oracle as the checker)."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+import lbk
+import oracle as orc
+import synth
+
+DEV = "cuda:0"
+
+_ctx = None
+
+
+def ctx() -> lbk.Context:
+    global _ctx
+    if _ctx is None:
+        _ctx = lbk.Context(0)
+    return _ctx
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def host(t: torch.Tensor) -> np.ndarray:
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def bits(a) -> np.ndarray:
+    return np.asarray(a, dtype=np.float32).view(np.uint32)
+
+
+def rel_err(got: np.ndarray, want: np.ndarray) -> float:
+    """max |got - want| / max |want| (norm-wise relative error)."""
+    scale = float(np.max(np.abs(want))) or 1.0
+    return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / scale
+
+
+def planar_dev(ty: int, gguf: np.ndarray) -> torch.Tensor:
+    return dev(synth.planar_np(ty, gguf))
+
+
+def matrix(ty, in_w, out_w, t: torch.Tensor, layout=lbk.LAYOUT_GGUF) -> lbk.Matrix:
+    return lbk.matrix(ty, in_w, out_w, t, layout)
+
+
+def expect_status(code: int) -> lbk.ErrorDetail:
+    st = ctx().sync_status()
+    assert st == code, f"status {st} ({lbk.STATUS.get(st)}), expected {code}"
+    return ctx().last_detail
+
+
+def clean_status() -> None:
+    st = ctx().sync_status()
+    assert st == 0, f"unexpected device status {st} ({lbk.STATUS.get(st)}): {ctx().last_detail.index}"
+
+
+def make_layer_np(rng, H, F, E, gty=orc.TYPE_IQ2_S, dty=orc.TYPE_IQ3_S, sty=orc.TYPE_Q4_K, sdty=orc.TYPE_Q4_K):
+    """Host expert table in the order of the synthetic generator: router,
+    experts 0..E-1 (gate, up, down), shared (gate, up, down)."""
+    router = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    experts = []
+    for _ in range(E):
+        g = synth.packed_np(rng, gty, H, F)
+        u = synth.packed_np(rng, gty, H, F)
+        d = synth.packed_np(rng, dty, F, H)
+        experts.append((gty, g, gty, u, dty, d, H, F))
+    sg = synth.packed_np(rng, sty, H, F)
+    su = synth.packed_np(rng, sty, H, F)
+    sd = synth.packed_np(rng, sdty, F, H)
+    shared = (sty, sg, sty, su, sdty, sd, H, F)
+    return router, experts, shared
+
+
+def upload_layer(router, experts, shared, layout, top_k, weight_scale=2.826, bias=None):
+    """Device copies + an lbk.MoeLayer; returns (layer, keepalive)."""
+    H = shared[6]
+    E = len(experts)
+    keep = []
+
+    def up(ty, b):
+        t = planar_dev(ty, b) if layout == lbk.LAYOUT_PLANAR else dev(b)
+        keep.append(t)
+        return t
+
+    def ex(e):
+        gty, gb, uty, ub, dty, db, h, f = e
+        return lbk.Expert(
+            matrix(gty, h, f, up(gty, gb), layout),
+            matrix(uty, h, f, up(uty, ub), layout),
+            matrix(dty, f, h, up(dty, db), layout),
+        )
+
+    dex = [ex(e) for e in experts]
+    sh = ex(shared)
+    rt = dev(router)
+    keep.append(rt)
+    rm = lbk.Matrix(lbk.TYPE_F32, lbk.LAYOUT_GGUF, H, E, rt.data_ptr(), rt.numel() * 4)
+    b = dev(np.zeros(E, np.float32) if bias is None else bias)
+    keep.append(b)
+    layer = lbk.MoeLayer(ctx(), dex, sh, rm, b, top_k, weight_scale)
+    return layer, keep

@@ -1,0 +1,161 @@
+"""GPU parity of the routed + shared SwiGLU MoE layer against the CPU oracle
+(route_experts_into + moe_routed_by_id_into, i.e. hy3_moe_route_token /
+hy3_moe_finish_token without norm and residual).
+
+Bars (north star): top-k expert IDs identical; f32 outputs within 1e-5
+relative (norm-wise). Stages that call exp (sigmoid, SwiGLU) use CUDA's
+double exp rounded to f32 where the reference uses the platform expf, so
+the layer output is held to the tolerance; every integer sum and every
+exp-free f32 tail is bit-exact (tests/test_gpu_quant_dot.py).
+Also covers the combine order of bridge-kernels-reference/tests/moe.rs:106-153
+and validate-before-write (moe.rs:156-244).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import lbk
+import oracle as orc
+from gpu_helpers import bits, clean_status, ctx, dev, expect_status, host, make_layer_np, rel_err, upload_layer
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def run_forward(layer, xs, mode=lbk.ROUTER_TREE):
+    T, H = xs.shape
+    ws = torch.zeros(layer.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.full((T * H,), float("nan"), device="cuda")
+    routed = torch.zeros(T * layer.top_k * 2, dtype=torch.int32, device="cuda")
+    layer.forward(dev(xs.reshape(-1)), T, out, ws, routed_out=routed, router_mode=mode)
+    clean_status()
+    r = host(routed).reshape(T, layer.top_k, 2)
+    return host(out).reshape(T, H), r[:, :, 0].astype(np.uint32), r[:, :, 1].view(np.float32)
+
+
+def oracle_tokens(router, experts, shared, xs, k):
+    table = orc.ExpertTable(experts, shared, router=router, hidden=xs.shape[1])
+    E = len(experts)
+    outs, ids, coefs = [], [], []
+    for x in xs:
+        o, i, c = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, x)
+        outs.append(o)
+        ids.append(i)
+        coefs.append(c)
+    return np.stack(outs), np.stack(ids), np.stack(coefs), table
+
+
+@pytest.mark.parametrize("layout", [lbk.LAYOUT_PLANAR, lbk.LAYOUT_GGUF])
+@pytest.mark.parametrize("H,F,E,k,T", [(512, 256, 8, 2, 1), (1024, 512, 16, 4, 3), (768, 768, 12, 3, 2)])
+def test_small_layers_match_oracle(H, F, E, k, T, layout):
+    rng = np.random.default_rng(H + F + E + k)
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    xs = rng.standard_normal((T, H)).astype(np.float32)
+    layer, keep = upload_layer(router, experts, shared, layout, k)
+    assert layer.fused == (layout == lbk.LAYOUT_PLANAR)
+    for mode in (lbk.ROUTER_TREE, lbk.ROUTER_SEQUENTIAL):
+        out, ids, coefs = run_forward(layer, xs, mode)
+        want, wids, wcoefs, _ = oracle_tokens(router, experts, shared, xs, k)
+        np.testing.assert_array_equal(ids, wids)
+        np.testing.assert_allclose(coefs, wcoefs, rtol=1e-6)
+        assert rel_err(out, want) <= TOL, rel_err(out, want)
+    layer.close()
+
+
+def test_fused_and_per_expert_paths_are_bit_identical():
+    rng = np.random.default_rng(77)
+    H, F, E, k, T = 1024, 512, 16, 4, 2
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    xs = rng.standard_normal((T, H)).astype(np.float32)
+    lp, kp = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    lg, kg = upload_layer(router, experts, shared, lbk.LAYOUT_GGUF, k)
+    a, ia, _ = run_forward(lp, xs, lbk.ROUTER_SEQUENTIAL)
+    b, ib, _ = run_forward(lg, xs, lbk.ROUTER_SEQUENTIAL)
+    np.testing.assert_array_equal(ia, ib)
+    np.testing.assert_array_equal(bits(a), bits(b))
+    lp.close()
+    lg.close()
+
+
+def test_caller_supplied_routing_and_combine_order():
+    rng = np.random.default_rng(5)
+    H, F, E, k = 512, 256, 8, 3
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    ids = np.array([1, 4, 6], np.uint32)
+    coefs = np.array([0.25, 0.75, -1.5], np.float32)
+    rt = np.zeros(k * 2, np.int32)
+    rt[0::2] = ids.view(np.int32)
+    rt[1::2] = coefs.view(np.int32)
+    ws = torch.zeros(layer.workspace_bytes(1), dtype=torch.uint8, device="cuda")
+    out = torch.zeros(H, device="cuda")
+    layer.routed(dev(x.reshape(-1)), 1, dev(rt), out, ws)
+    clean_status()
+    table = orc.ExpertTable(experts, shared)
+    want = orc.moe_routed(table, ids, coefs, x[0], preflight=True)
+    assert rel_err(host(out), want) <= TOL
+    layer.close()
+
+
+@pytest.mark.parametrize(
+    "ids,code", [([3, 3, 5], 14), ([4, 2, 5], 13), ([1, 2, 99], 15)]
+)
+def test_bad_routing_rejected_before_output_write(ids, code):
+    rng = np.random.default_rng(6)
+    H, F, E, k = 512, 256, 8, 3
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    rt = np.zeros(k * 2, np.int32)
+    rt[0::2] = np.array(ids, np.uint32).view(np.int32)
+    rt[1::2] = np.ones(k, np.float32).view(np.int32)
+    ws = torch.zeros(layer.workspace_bytes(1), dtype=torch.uint8, device="cuda")
+    sentinel = np.full(H, -4.25, np.float32)
+    out = dev(sentinel)
+    layer.routed(dev(rng.standard_normal(H).astype(np.float32)), 1, dev(rt), out, ws)
+    expect_status(code)
+    np.testing.assert_array_equal(host(out), sentinel)
+    layer.close()
+
+
+def test_non_finite_token_leaves_output_unchanged():
+    rng = np.random.default_rng(8)
+    H, F, E, k = 512, 256, 8, 2
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    x = rng.standard_normal(H).astype(np.float32)
+    x[100] = np.inf
+    ws = torch.zeros(layer.workspace_bytes(1), dtype=torch.uint8, device="cuda")
+    sentinel = np.full(H, 9.0, np.float32)
+    out = dev(sentinel)
+    layer.forward(dev(x), 1, out, ws)
+    expect_status(12)
+    np.testing.assert_array_equal(host(out), sentinel)
+    # the workspace stays usable: a clean call afterwards is correct
+    x[100] = 0.5
+    out2 = torch.zeros(H, device="cuda")
+    layer.forward(dev(x), 1, out2, ws)
+    clean_status()
+    want, _, _, _ = oracle_tokens(router, experts, shared, x[None], k)
+    assert rel_err(host(out2), want[0]) <= TOL
+    layer.close()
+
+
+def test_config3_layer_single_token():
+    """hidden 4096, 192 experts (IQ2_S gate/up, IQ3_S down,
+    FFN 1536), shared Q4_K expert, F32 router N(0, 0.02), top-8, seed 2."""
+    rng = np.random.default_rng(2)
+    H, F, E, k = 4096, 1536, 192, 8
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    xs = rng.standard_normal((2, H)).astype(np.float32)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    assert layer.fused
+    out, ids, coefs = run_forward(layer, xs, lbk.ROUTER_TREE)
+    want, wids, wcoefs, _ = oracle_tokens(router, experts, shared, xs, k)
+    np.testing.assert_array_equal(ids, wids)
+    np.testing.assert_allclose(coefs, wcoefs, rtol=1e-6)
+    err = rel_err(out, want)
+    assert err <= TOL, err
+    layer.close()
