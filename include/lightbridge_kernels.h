@@ -297,7 +297,11 @@ int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, co
  *   IQ3_S: qs[64] | signs[32] | qh[8] | scales[4] | d[2]
  *   Q4_K : qs[128] | scales[12] | d[2] | dmin[2]
  *   Q5_K : qs[128] | qh[32] | scales[12] | d[2] | dmin[2]
- * so plane f of row r starts at plane_offset_f + r*nb*field_bytes_f. */
+ * so plane f of row r starts at plane_offset_f + r*nb*field_bytes_f. Inside
+ * a block, Q4_K / Q5_K qs (and Q5_K qh) bytes are lane-major per 32-byte
+ * group (new[4k+i] = old[k+8i]), and each little-endian 32-bit word of the
+ * IQ2_S / IQ3_S qh field is stored as the transpose of its 4x4 matrix of
+ * 2-bit cells (cell (r, c) at bit 8r+2c moves to bit 8c+2r). */
 int32_t lbk_repack(lbk_context* ctx, const lbk_matrix* src_gguf, void* dst_planar, uint64_t dst_bytes,
                    void* stream);
 /* Exact inverse of lbk_repack. */

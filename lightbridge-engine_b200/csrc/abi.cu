@@ -32,7 +32,14 @@ struct lbk_context {
     unsigned long long* scratch_min;    // device, 8 bytes
     uint64_t* iq2s;                     // device, 1024
     uint32_t* iq3s;                     // device, 512
-    lbk::Tables tables() const { return lbk::Tables{iq2s, iq3s}; }
+    uint32_t* img_iq2;                  // replicated shared-memory images
+    uint32_t* img_iq3;
+    uint32_t* img_sign;
+    uint32_t* img_sel;
+    lbk::Tables tables() const {
+        return lbk::Tables{reinterpret_cast<const uint4*>(img_iq2), reinterpret_cast<const uint4*>(img_iq3),
+                           reinterpret_cast<const uint4*>(img_sign), reinterpret_cast<const uint4*>(img_sel)};
+    }
 };
 
 struct lbk_moe_layer {
@@ -193,13 +200,13 @@ WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T) {
     o.partials = off;
     off = up256(off + lbk::router_partials_floats(L->H, L->E, T) * 4);
     o.q8x = off;
-    off = up256(off + T * nbh * LBK_Q8K_BLOCK_BYTES);
+    off = up256(off + T * nbh * lbk::kQ8IBytes);  // internal Q8_K images
     o.routed = off;
     off = up256(off + T * L->k * sizeof(lbk_routed));
     o.h = off;
     off = up256(off + slots * L->F * 4);
     o.hq = off;
-    off = up256(off + slots * nbf * LBK_Q8K_BLOCK_BYTES);
+    off = up256(off + slots * nbf * lbk::kQ8IBytes);
     o.g = off;  // per-expert path: gate / up scratch, q8 scratch
     off = up256(off + L->F * 4);
     o.u = off;
@@ -243,6 +250,17 @@ __global__ void fill_zero_kernel(float* p, uint64_t n, const lbk::DeviceStatus* 
 std::mutex g_attr_mu;
 std::set<std::pair<int, const void*>> g_attr_done;
 
+// Records a trace event; inside a stream capture it becomes an event-record
+// node of the graph (cudaEventRecordExternal), outside it is a plain record.
+void trace_record(cudaEvent_t ev, cudaStream_t st, unsigned int capture_flags) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(ev, st, capture_flags);
+    else
+        cudaEventRecord(ev, st);
+}
+
 }  // namespace
 
 namespace lbk {
@@ -252,7 +270,11 @@ cudaError_t ensure_max_smem(const void* kernel) {
     if (e != cudaSuccess) return e;
     std::lock_guard<std::mutex> lock(g_attr_mu);
     if (g_attr_done.count({dev, kernel})) return cudaSuccess;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, kernel);
+    if (e != cudaSuccess) return e;
+    // the per-block limit covers static + dynamic shared memory
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kMaxSmem - fa.sharedSizeBytes));
     if (e == cudaSuccess) g_attr_done.insert({dev, kernel});
     return e;
 }
@@ -283,18 +305,31 @@ LBK_API int32_t lbk_context_create(int32_t device, lbk_context** out) {
     c->device = device;
     c->sm_count = prop.multiProcessorCount;
     void* p = nullptr;
-    if ((e = cudaMalloc(&p, sizeof(lbk::DeviceStatus) + 64 + sizeof(lbk_iq2s_grid) + sizeof(lbk_iq3s_grid))) != cudaSuccess) {
+    // [status 32 B][scratch_min 8 B .. 256][iq2s grid 8 KB][iq3s grid 2 KB]
+    // [IQ2 code image 128 KB][IQ3 grid image 64 KB][sign image 32 KB][sign-select image 32 KB]
+    static_assert(sizeof(lbk::DeviceStatus) <= 32, "status word layout");
+    const size_t img_off = 256 + sizeof(lbk_iq2s_grid) + sizeof(lbk_iq3s_grid);
+    const size_t total = img_off + lbk::kIq2CodeBytes + lbk::kIq3GridBytes + 2 * lbk::kSignBytes;
+    if ((e = cudaMalloc(&p, total)) != cudaSuccess) {
         delete c;
         return cuda_fail(e, "cudaMalloc context");
     }
     uint8_t* base = static_cast<uint8_t*>(p);
     c->status = reinterpret_cast<lbk::DeviceStatus*>(base);
     c->scratch_min = reinterpret_cast<unsigned long long*>(base + 32);
-    c->iq2s = reinterpret_cast<uint64_t*>(base + 64 + 32);
-    c->iq3s = reinterpret_cast<uint32_t*>(base + 64 + 32 + sizeof(lbk_iq2s_grid));
-    cudaMemset(base, 0, 96);
-    cudaMemcpy(c->iq2s, lbk_iq2s_grid, sizeof(lbk_iq2s_grid), cudaMemcpyHostToDevice);
-    if ((e = cudaMemcpy(c->iq3s, lbk_iq3s_grid, sizeof(lbk_iq3s_grid), cudaMemcpyHostToDevice)) != cudaSuccess) {
+    c->iq2s = reinterpret_cast<uint64_t*>(base + 256);
+    c->iq3s = reinterpret_cast<uint32_t*>(base + 256 + sizeof(lbk_iq2s_grid));
+    c->img_iq2 = reinterpret_cast<uint32_t*>(base + img_off);
+    c->img_iq3 = reinterpret_cast<uint32_t*>(base + img_off + lbk::kIq2CodeBytes);
+    c->img_sign = reinterpret_cast<uint32_t*>(base + img_off + lbk::kIq2CodeBytes + lbk::kIq3GridBytes);
+    c->img_sel = c->img_sign + lbk::kSignBytes / 4;
+    e = cudaMemset(base, 0, 256);
+    if (e == cudaSuccess) e = cudaMemcpy(c->iq2s, lbk_iq2s_grid, sizeof(lbk_iq2s_grid), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(c->iq3s, lbk_iq3s_grid, sizeof(lbk_iq3s_grid), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = lbk::launch_build_tables(c->iq2s, c->iq3s, c->img_iq2, c->img_iq3, c->img_sign,
+                                                    c->img_sel, nullptr);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
         cudaFree(p);
         delete c;
         return cuda_fail(e, "upload codebooks");
@@ -576,7 +611,7 @@ LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w,
     }
     uniform &= w->experts[0].up.type == L->gate_type;
     L->fused = uniform && planar && lbk::moe_fused_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type) &&
-               L->k + 1 <= 18;
+               L->k + 1 <= (uint64_t)lbk::kMoeDownMaxSlots;
 
     std::vector<const uint8_t*> ptrs(3 * E);
     for (uint64_t e = 0; e < E; e++) {
@@ -672,13 +707,21 @@ LBK_API int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tok
 namespace {
 
 // Expert stage of one MoE call for `tokens` tokens with routing in `routed`.
+// With defer_topk (single token, fused kernels) the routing is computed by the
+// gate/up kernel from the router's chunk partials and stored into `routed`.
 int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_routed* routed, float* out, uint8_t* ws,
-                    const WsLayout& o, cudaStream_t st) {
+                    const WsLayout& o, cudaStream_t st, bool defer_topk = false) {
     lbk_context* ctx = L->ctx;
     cudaError_t e = cudaSuccess;
     const uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
     if (L->fused) {
         lbk::MoeGateUpArgs g{};
+        g.defer_topk = defer_topk ? 1 : 0;
+        g.partials = reinterpret_cast<const float*>(ws + o.partials);
+        g.chunks = lbk::router_partials_floats(L->H, 1, 1);
+        g.bias = L->w.selection_bias;
+        g.weight_scale = L->weight_scale;
+        g.routed_store = const_cast<lbk_routed*>(routed);
         g.hidden = L->H;
         g.ffn = L->F;
         g.nb_h = (int)nbh;
@@ -701,7 +744,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         const int rps = 32 / g.tpr_h;
         const double br = 2.0 * (double)(nbh * block_bytes(L->gate_type)), bs = 2.0 * (double)(nbh * block_bytes(L->sgate_type));
         const double total = (double)T * L->F * ((double)L->k * br + bs);
-        const double per_warp = total / (double)(ctx->sm_count * 16);
+        const double per_warp = total / (double)(ctx->sm_count * lbk::kMoeGateUpWarps);
         auto chunk_of = [&](double b) {
             uint64_t c = (uint64_t)(per_warp / b + 0.5);
             c = c < 1 ? 1 : c;
@@ -712,6 +755,16 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.chunk_s = chunk_of(bs);
         g.chunks_r = (L->F + g.chunk_r - 1) / g.chunk_r;
         g.chunks_s = (L->F + g.chunk_s - 1) / g.chunk_s;
+        // One CTA per SM (the tables fill shared memory): keep the grid to a
+        // single wave by growing the chunks until every warp item fits.
+        const uint64_t warp_cap = (uint64_t)ctx->sm_count * lbk::kMoeGateUpWarps;
+        while (T * L->k * g.chunks_r + T * g.chunks_s > warp_cap && (g.chunk_r < 256 || g.chunk_s < 256)) {
+            if (g.chunk_r < 256) g.chunk_r += rps;
+            if (T * L->k * ((L->F + g.chunk_r - 1) / g.chunk_r) + T * g.chunks_s > warp_cap && g.chunk_s < 256)
+                g.chunk_s += rps;
+            g.chunks_r = (L->F + g.chunk_r - 1) / g.chunk_r;
+            g.chunks_s = (L->F + g.chunk_s - 1) / g.chunk_s;
+        }
         g.bmax_iq = 16 > rps ? 16 : rps;
         g.bmax_k = 2 > rps ? 2 : rps;
         const int kt_g = dot_type(L->gate_type) && (L->gate_type == LBK_TYPE_Q4_K || L->gate_type == LBK_TYPE_Q5_K) ? 9 : 1;
@@ -722,11 +775,13 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.chain_floats = (dots * 9 + 64 + 3) & ~(uint64_t)3;
         g.status = ctx->status;
         g.tables = ctx->tables();
-        if (lbk::moe_gate_up_fixed_smem(L->gate_type, L->sgate_type) + 16 * (g.prod_floats + g.chain_floats) * 4 > lbk::kMaxSmem)
+        if (lbk::moe_gate_up_fixed_smem(L->gate_type, L->sgate_type) +
+                lbk::kMoeGateUpWarps * (g.prod_floats + g.chain_floats) * 4 >
+            lbk::kMaxSmem - 8192)  // static top-k buffers
             return fail(LBK_INVALID_PARAMETER, "MoE gate/up shapes exceed shared memory");
         e = lbk::launch_moe_gate_up(L->gate_type, L->sgate_type, g, st);
         if (e != cudaSuccess) return cuda_fail(e, "moe gate/up launch");
-        if (L->tracing) cudaEventRecordWithFlags(L->trace[2], st, cudaEventRecordExternal);
+        if (L->tracing) trace_record(L->trace[2], st, cudaEventRecordExternal);
 
         lbk::MoeDownArgs d{};
         d.hidden = L->H;
@@ -741,7 +796,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         d.routed = routed;
         d.hq = ws + o.hq;
         d.out = out;
-        d.wps = (L->k + 1) * 2 <= 18 ? 2 : 1;
+        d.wps = 1;  // one warp per slot (the kernel's 288-thread bound covers top-k <= 8)
         const uint64_t rpsf = 32 / d.tpr_f;
         uint64_t ctas_x = (uint64_t)ctx->sm_count;
         uint64_t rows = (L->H + ctas_x - 1) / ctas_x;
@@ -763,7 +818,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             return fail(LBK_INVALID_PARAMETER, "MoE down shapes exceed shared memory");
         e = lbk::launch_moe_down(L->down_type, L->sdown_type, d, st);
         if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
-        if (L->tracing) cudaEventRecordWithFlags(L->trace[3], st, cudaEventRecordExternal);
+        if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);
         return ok();
     }
     // Per-expert path: any types and layouts, one token at a time.
@@ -821,7 +876,11 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
     f.weight_scale = layer->weight_scale;
     f.routed = routed;
     cudaError_t e;
-    if (layer->tracing) cudaEventRecordWithFlags(layer->trace[0], st, cudaEventRecordExternal);
+    // Single-token decode on the fused kernels: the gate/up kernel finishes the
+    // router (partials -> logits -> top-k) in every CTA's prologue.
+    const bool defer = layer->fused && tokens == 1 && router_mode == LBK_ROUTER_TREE;
+    f.defer = defer ? 1 : 0;
+    if (layer->tracing) trace_record(layer->trace[0], st, cudaEventRecordExternal);
     if (router_mode == LBK_ROUTER_TREE) {
         e = lbk::launch_router_fused(f, ctx->sm_count, st);
         if (e != cudaSuccess) return cuda_fail(e, "router launch");
@@ -837,11 +896,11 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
             if ((e = lbk::launch_router_fused(q, ctx->sm_count, st)) != cudaSuccess) return cuda_fail(e, "quantize launch");
         }
     }
-    if (layer->tracing) cudaEventRecordWithFlags(layer->trace[1], st, cudaEventRecordExternal);
-    int32_t s = moe_experts(layer, x, tokens, routed, out, ws, o, st);
+    if (layer->tracing) trace_record(layer->trace[1], st, cudaEventRecordExternal);
+    int32_t s = moe_experts(layer, x, tokens, routed, out, ws, o, st, defer);
     if (s == LBK_OK && layer->tracing && !layer->fused) {
-        cudaEventRecordWithFlags(layer->trace[2], st, cudaEventRecordExternal);
-        cudaEventRecordWithFlags(layer->trace[3], st, cudaEventRecordExternal);
+        trace_record(layer->trace[2], st, cudaEventRecordExternal);
+        trace_record(layer->trace[3], st, cudaEventRecordExternal);
     }
     return s;
 }

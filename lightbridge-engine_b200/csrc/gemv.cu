@@ -187,11 +187,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     if (single && step < steps && row_of(step) < rows && hb0 < nhb) load_hb<L>(cur, a.w, row_of(step), hb0 >> 1, hb0 & 1);
 
     if (T == LBK_TYPE_IQ2_S) {
-        fill_iq2_codes(tab0, a.tables.iq2s_grid);
-        fill_signs(tab1);
+        fill_iq2_codes(tab0, a.tables);
+        fill_signs(tab1, a.tables);
     } else if (T == LBK_TYPE_IQ3_S) {
-        fill_iq3_grid(tab0, a.tables.iq3s_grid);
-        fill_signs(tab1);
+        fill_iq3_grid(tab0, a.tables);
+        fill_sign_sel(tab1, a.tables);
     }
     if (!stage_activations(a, nb, qs, dsm, bs, flag)) return;
 
@@ -206,8 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
             for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
         }
     }
-    const uint32_t* t0 = tab0 + lane;
-    const uint32_t* t1 = tab1 + lane;
+    const uint32_t t0 = (uint32_t)__cvta_generic_to_shared(tab0 + lane);
+    const uint32_t t1 = (uint32_t)__cvta_generic_to_shared(tab1 + lane);
 
     const int slots = a.tail_slots;  // >= rps, multiple of rps
     auto flush = [&](int nslots, uint64_t first_step) {

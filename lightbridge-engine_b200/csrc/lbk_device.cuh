@@ -109,6 +109,33 @@ __device__ __forceinline__ uint32_t w32(const uint4& v, int i) {
 }
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
 
+// PTX byte permute with the full 4-bit selector (bit 3 = replicate the
+// selected byte's sign bit; __byte_perm only honours 3 bits).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 32-bit shared-memory load at a shared-window address.
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+// Transpose of a 4x4 matrix of 2-bit cells (cell (r, c) at bit 8r + 2c).
+// The planar layout stores a thread's IQ2_S / IQ3_S qh word transposed, so
+// byte l holds the high index bits of subgroup l of all four groups. It is its
+// own inverse.
+__host__ __device__ __forceinline__ uint32_t qh_transpose(uint32_t w) {
+    uint32_t t = ((w >> 12) ^ w) & 0x0000f0f0u;
+    w ^= t ^ (t << 12);
+    t = ((w >> 6) ^ w) & 0x00cc00ccu;
+    w ^= t ^ (t << 6);
+    return w;
+}
+
 // 4x4 byte transpose: out[k] byte i = in[i] byte k.
 __device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t& o0,
                                            uint32_t& o1, uint32_t& o2, uint32_t& o3) {
@@ -136,11 +163,31 @@ constexpr int kIq2CodeBytes = kIq2CodeEntries * 32 * 4;  // 128 KiB
 constexpr int kIq3GridBytes = kIq3GridEntries * 32 * 4;  // 64 KiB
 constexpr int kSignBytes = kSignEntries * 32 * 4;        // 32 KiB
 
-// Codebooks in global memory, uploaded once per context (from lbk_iq_tables.h).
+// Replicated table images in global memory, built once per context from the
+// codebooks of lbk_iq_tables.h (build_table_images). A kernel copies the
+// images it needs into shared memory with 16-byte loads.
 struct Tables {
-    const uint64_t* iq2s_grid;  // 1024
-    const uint32_t* iq3s_grid;  // 512
+    const uint4* iq2_codes;  // kIq2CodeBytes
+    const uint4* iq3_grid;   // kIq3GridBytes
+    const uint4* signs;      // kSignBytes: IQ2_S selector sign bits
+    const uint4* sign_sel;   // kSignBytes: IQ3_S activation selectors (see sign_select)
 };
+
+// IQ3_S activation selector for a sign byte: low half selects lanes 0-3 of
+// {a, -a} by sign bits 0-3, high half lanes 0-3 by sign bits 4-7.
+__host__ __device__ __forceinline__ uint32_t sign_select(uint32_t s) {
+    uint32_t lo = 0x3210u, hi = 0x3210u;
+    for (int i = 0; i < 4; i++) {
+        lo |= ((s >> i) & 1u) << (4 * i + 2);
+        hi |= ((s >> (i + 4)) & 1u) << (4 * i + 2);
+    }
+    return lo | (hi << 16);
+}
+
+__device__ __forceinline__ void copy_table(uint32_t* dst, const uint4* src, int bytes) {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = __ldg(src + i);
+}
 
 __device__ __forceinline__ uint32_t sign_spread(uint32_t s) {
     uint32_t v = 0;
@@ -160,19 +207,11 @@ __device__ __forceinline__ uint32_t iq2_code_of(uint64_t g) {
     return v;
 }
 
-// Fills a replicated table; all threads of the block participate.
-__device__ __forceinline__ void fill_iq2_codes(uint32_t* tab, const uint64_t* grid) {
-    for (int i = threadIdx.x; i < kIq2CodeEntries * 32; i += blockDim.x) {
-        int e = i >> 5;
-        tab[i] = iq2_code_of(__ldg(grid + e));
-    }
-}
-__device__ __forceinline__ void fill_iq3_grid(uint32_t* tab, const uint32_t* grid) {
-    for (int i = threadIdx.x; i < kIq3GridEntries * 32; i += blockDim.x) tab[i] = __ldg(grid + (i >> 5));
-}
-__device__ __forceinline__ void fill_signs(uint32_t* tab) {
-    for (int i = threadIdx.x; i < kSignEntries * 32; i += blockDim.x) tab[i] = sign_spread((uint32_t)(i >> 5));
-}
+// Copies the replicated images into shared memory; all threads participate.
+__device__ __forceinline__ void fill_iq2_codes(uint32_t* tab, const Tables& t) { copy_table(tab, t.iq2_codes, kIq2CodeBytes); }
+__device__ __forceinline__ void fill_iq3_grid(uint32_t* tab, const Tables& t) { copy_table(tab, t.iq3_grid, kIq3GridBytes); }
+__device__ __forceinline__ void fill_signs(uint32_t* tab, const Tables& t) { copy_table(tab, t.signs, kSignBytes); }
+__device__ __forceinline__ void fill_sign_sel(uint32_t* tab, const Tables& t) { copy_table(tab, t.sign_sel, kSignBytes); }
 
 // Pools for IQ2_S signed-grid expansion through byte permutes: selector
 // nibble c in {0,1,2} picks +8/+25/+43, c+4 picks the negated value.
@@ -253,6 +292,21 @@ __device__ __forceinline__ Q8Block quantize_q8k_warp(const float v[8], int lane)
     out.pair_sum = s;
     out.d = __fdiv_rn(1.0f, iscale);
     return out;
+}
+
+// Internal Q8_K block image used inside workspaces (never exposed): the same
+// values as the 292-byte Q8_K block, with 16-byte aligned fields so a thread's
+// half block is eight 16-byte loads:
+//   qs int8[256] @0 | bsums int16[16] @256 | d f32 @288 | pad to 304
+constexpr int kQ8IBytes = 304;
+
+// Stores a warp's quantized block (see quantize_q8k_warp); `pair` is the
+// lane-pair group sum (valid on even lanes).
+__device__ __forceinline__ void store_q8i(uint8_t* blk, const Q8Block& q, int32_t pair, int lane) {
+    uint2* qs = reinterpret_cast<uint2*>(blk);
+    qs[lane] = make_uint2(q.q[0], q.q[1]);
+    if ((lane & 1) == 0) reinterpret_cast<int16_t*>(blk + 256)[lane >> 1] = (int16_t)pair;
+    if (lane == 0) *reinterpret_cast<float*>(blk + 288) = q.d;
 }
 
 // ------------------------------------------------------ activation registers
@@ -363,7 +417,7 @@ __device__ __forceinline__ void load_hb(Iq2HB& o, const MatrixRef& m, uint64_t r
         o.d = ldw_u16(p);
         o.qs = ldw_u128_a2(p + 2 + 16 * h);
         o.sg = ldw_u128_a2(p + 34 + 16 * h);
-        o.qh = ldw_u32_a2(p + 66 + 4 * h);
+        o.qh = qh_transpose(ldw_u32_a2(p + 66 + 4 * h));
         o.sc = ldw_u32_a2(p + 74 + 4 * h);
     }
 }
@@ -385,7 +439,7 @@ __device__ __forceinline__ void load_hb(Iq3HB& o, const MatrixRef& m, uint64_t r
         o.d = ldw_u16(p);
         o.qs0 = ldw_u128_a2(p + 2 + 32 * h);
         o.qs1 = ldw_u128_a2(p + 2 + 32 * h + 16);
-        o.qh = ldw_u32_a2(p + 66 + 4 * h);
+        o.qh = qh_transpose(ldw_u32_a2(p + 66 + 4 * h));
         o.sg = ldw_u128_a2(p + 74 + 16 * h);
         o.sc = ldw_u16(p + 106 + 2 * h);
     }
@@ -485,33 +539,54 @@ struct KPart {
     uint32_t dm;  // d | dmin << 16 (binary16 bits)
 };
 
+// Selector of prmt() giving [byte `lo` of a, byte `hi` of b, 0, 0]: the two
+// upper selector nibbles replicate the sign of b's byte `hi` (bit 3 set),
+// which is zero because b's bytes hold 2-bit values.
+__host__ __device__ constexpr uint32_t sel_idx(int lo, int hi) {
+    return (uint32_t)(lo | ((4 + hi) << 4) | ((0xC + hi) << 8) | ((0xC + hi) << 12));
+}
+// [byte `lo` of a, 0, 0, 0] (zeros from b's non-negative byte `z`)
+__host__ __device__ constexpr uint32_t sel_byte(int lo, int z) {
+    return (uint32_t)(lo | ((0xC + z) << 4) | ((0xC + z) << 8) | ((0xC + z) << 12));
+}
+
 // dot_iq2_s (q8_k.rs:339-364) over groups 4h..4h+3 of one block.
-// code_tab / sign_tab point at this lane's copy of the replicated tables.
-__device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, const uint32_t* code_tab,
-                                         const uint32_t* sign_tab) {
+// code_base / sign_base are shared-window addresses of this lane's copy of
+// the replicated tables (entry e at base + 128 e). The qh word is the
+// bit-transposed one (qh_transpose): byte l, bits 2g..2g+1 = high index bits
+// of subgroup l of group g. Per subgroup of 8 lanes: one permute builds the
+// 10-bit index, one multiply-add its table address; the code nibbles plus
+// the sign bits select signed grid bytes from a byte pool.
+__device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, uint32_t code_base, uint32_t sign_base) {
     int32_t total = 0;
+    const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;          // 1 + 2*(scale & 15), four groups
+    const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;   // 1 + 2*(scale >> 4)
 #pragma unroll
     for (int gi = 0; gi < 4; gi++) {
-        uint32_t qsw = w32(w.qs, gi);
-        uint32_t sgw = w32(w.sg, gi);
-        uint32_t qh = (w.qh >> (8 * gi)) & 0xffu;
-        uint32_t sc = (w.sc >> (8 * gi)) & 0xffu;
-        int32_t s1 = 1 + 2 * (int32_t)(sc & 0x0f);
-        int32_t s2 = 1 + 2 * (int32_t)(sc >> 4);
-        int32_t part[2] = {0, 0};
+        const uint32_t qsw = w32(w.qs, gi);
+        const uint32_t sgw = w32(w.sg, gi);
+        const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;  // byte l: high index bits of subgroup l
+        int32_t part0 = 0, part1 = 0;
 #pragma unroll
         for (int l = 0; l < 4; l++) {
-            uint32_t idx = ((qsw >> (8 * l)) & 0xffu) | ((qh << (8 - 2 * l)) & 0x300u);
-            uint32_t code = code_tab[idx * 32];
-            uint32_t sp = sign_tab[((sgw >> (8 * l)) & 0xffu) * 32];
-            uint32_t sel = code | sp;
-            uint32_t g0 = __byte_perm(kIq2PoolPos, kIq2PoolNeg, sel & 0xffffu);
-            uint32_t g1 = __byte_perm(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
-            int32_t p = dp4a(g0, a.w[gi * 8 + 2 * l], 0);
-            p = dp4a(g1, a.w[gi * 8 + 2 * l + 1], p);
-            part[l >> 1] += p;
+            const uint32_t idx = prmt(qsw, Q, sel_idx(l, l));
+            const uint32_t code = lds32(idx * 128u + code_base);
+            const uint32_t sb = prmt(sgw, Q, sel_byte(l, l));
+            const uint32_t sp = lds32(sb * 128u + sign_base);
+            const uint32_t sel = code | sp;
+            const uint32_t g0 = prmt(kIq2PoolPos, kIq2PoolNeg, sel);
+            const uint32_t g1 = prmt(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
+            if (l < 2) {
+                part0 = dp4a(g0, a.w[gi * 8 + 2 * l], part0);
+                part0 = dp4a(g1, a.w[gi * 8 + 2 * l + 1], part0);
+            } else {
+                part1 = dp4a(g0, a.w[gi * 8 + 2 * l], part1);
+                part1 = dp4a(g1, a.w[gi * 8 + 2 * l + 1], part1);
+            }
         }
-        total += s1 * part[0] + s2 * part[1];
+        const int32_t s1 = (int32_t)prmt(s1w, 0, 0x4440u | gi);
+        const int32_t s2 = (int32_t)prmt(s2w, 0, 0x4440u | gi);
+        total += s1 * part0 + s2 * part1;
     }
     IqPart r;
     r.sum = total;
@@ -519,41 +594,42 @@ __device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, const u
     return r;
 }
 
-// dot_iq3_s (q8_k.rs:380-428) over groups 4h..4h+3 of one block. Signs are
-// applied to the activations: na holds the negated activation words and a
-// byte permute picks a or -a per lane.
-__device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const uint32_t* na, const uint32_t* grid_tab,
-                                         const uint32_t* sign_tab) {
+// dot_iq3_s (q8_k.rs:380-428) over groups 4h..4h+3 of one block. The signs
+// are applied to the activations: na holds the negated activation words and
+// a byte permute picks a or -a per lane, its selector read from the
+// sign-select table. qh is bit-transposed as for IQ2_S: bit 0 of byte l
+// holds the high bit of the first index of subgroup l, bit 1 of the second.
+__device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const uint32_t* na, uint32_t grid_base,
+                                         uint32_t sel_base) {
     int32_t total = 0;
+    // pair scales: bytes [lo0, lo1, hi0, hi1] -> 1 + 2*nibble; group gi uses byte {0,2,1,3}[gi]
+    const uint32_t st = (w.sc & 0x0f0fu) | ((w.sc & 0xf0f0u) << 12);
+    const uint32_t sw = st * 2u + 0x01010101u;
 #pragma unroll
     for (int gi = 0; gi < 4; gi++) {
-        uint32_t qa = gi < 2 ? w32(w.qs0, gi * 2) : w32(w.qs1, (gi - 2) * 2);
-        uint32_t qb = gi < 2 ? w32(w.qs0, gi * 2 + 1) : w32(w.qs1, (gi - 2) * 2 + 1);
-        uint32_t sgw = w32(w.sg, gi);
-        uint32_t qh = (w.qh >> (8 * gi)) & 0xffu;
-        // pair p = 2h + (gi>>1), nibble gi&1
-        uint32_t sc = (w.sc >> (8 * (gi >> 1))) & 0xffu;
-        int32_t scale = 2 * (int32_t)((gi & 1) ? (sc >> 4) : (sc & 0x0f)) + 1;
+        const uint32_t qa = gi < 2 ? w32(w.qs0, gi * 2) : w32(w.qs1, (gi - 2) * 2);
+        const uint32_t qb = gi < 2 ? w32(w.qs0, gi * 2 + 1) : w32(w.qs1, (gi - 2) * 2 + 1);
+        const uint32_t sgw = w32(w.sg, gi);
+        const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
+        const uint32_t Q1 = Q & 0x01010101u;          // high bit of the first index
+        const uint32_t Q2 = (Q >> 1) & 0x01010101u;   // high bit of the second index
         int32_t gsum = 0;
 #pragma unroll
         for (int l = 0; l < 4; l++) {
-            uint32_t q2 = l < 2 ? qa : qb;
-            uint32_t lo1 = (q2 >> (16 * (l & 1))) & 0xffu;
-            uint32_t lo2 = (q2 >> (16 * (l & 1) + 8)) & 0xffu;
-            uint32_t i1 = lo1 | ((qh << (8 - 2 * l)) & 0x100u);
-            uint32_t i2 = lo2 | ((qh << (7 - 2 * l)) & 0x100u);
-            uint32_t g1 = grid_tab[i1 * 32];
-            uint32_t g2 = grid_tab[i2 * 32];
-            uint32_t sp = sign_tab[((sgw >> (8 * l)) & 0xffu) * 32];
-            // selector nibble i = i (+4 when lane i is negative)
-            uint32_t sel1 = 0x3210u | (sp & 0xffffu);
-            uint32_t sel2 = 0x3210u | (sp >> 16);
-            int wi = gi * 8 + 2 * l;
-            uint32_t a1 = __byte_perm(a.w[wi], na[wi], sel1);
-            uint32_t a2 = __byte_perm(a.w[wi + 1], na[wi + 1], sel2);
+            const uint32_t q2 = l < 2 ? qa : qb;
+            const uint32_t i1 = prmt(q2, Q1, sel_idx(2 * (l & 1), l));
+            const uint32_t i2 = prmt(q2, Q2, sel_idx(2 * (l & 1) + 1, l));
+            const uint32_t g1 = lds32(i1 * 128u + grid_base);
+            const uint32_t g2 = lds32(i2 * 128u + grid_base);
+            const uint32_t sb = prmt(sgw, Q1, sel_byte(l, l));
+            const uint32_t ss = lds32(sb * 128u + sel_base);
+            const int wi = gi * 8 + 2 * l;
+            const uint32_t a1 = prmt(a.w[wi], na[wi], ss);
+            const uint32_t a2 = prmt(a.w[wi + 1], na[wi + 1], ss >> 16);
             gsum = dp4a(g1, a1, gsum);
             gsum = dp4a(g2, a2, gsum);
         }
+        const int32_t scale = (int32_t)prmt(sw, 0, 0x4440u | (uint32_t)((gi & 1) * 2 + (gi >> 1)));
         total += gsum * scale;
     }
     IqPart r;

@@ -73,6 +73,7 @@ struct RouterFusedArgs {
     uint32_t k;
     float weight_scale;
     lbk_routed* routed;     // [tokens][k], or null (logits only)
+    int defer;              // 1: leave the chunk partials for the consumer (no last-CTA pass)
 };
 size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens);
 cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStream_t stream);
@@ -99,6 +100,8 @@ struct RepackArgs {
     int to_planar;          // 1: GGUF -> planar, 0: planar -> GGUF
 };
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t stream);
+cudaError_t launch_build_tables(const uint64_t* iq2s, const uint32_t* iq3s, uint32_t* iq2_img, uint32_t* iq3_img,
+                                uint32_t* sign_img, uint32_t* sel_img, cudaStream_t stream);
 cudaError_t launch_validate_scales(int type, int layout, const uint8_t* data, uint64_t rows, int nb,
                                    unsigned long long* scratch_min, DeviceStatus* status, cudaStream_t stream);
 

@@ -5,6 +5,9 @@
 
 namespace lbk {
 
+constexpr int kMoeGateUpWarps = 8;   // warps per gate/up CTA (one CTA per SM)
+constexpr int kMoeDownMaxSlots = 9;  // routed top-k + shared, one warp each
+
 struct MoeGateUpArgs {
     uint64_t hidden, ffn;
     int nb_h, nb_f;
@@ -26,6 +29,13 @@ struct MoeGateUpArgs {
     int bmax_iq, bmax_k;             // rows per tail batch
     uint64_t prod_floats;            // per-warp product buffer
     uint64_t chain_floats;           // per-warp chain + result buffer (>= 9*dots + 64)
+    // single-token decode: finish the router here (see router_fused_kernel's defer)
+    int defer_topk;
+    const float* partials;           // [experts][chunks]
+    uint64_t chunks;
+    const float* bias;
+    float weight_scale;
+    lbk_routed* routed_store;        // CTA 0 writes the routing here
     DeviceStatus* status;
     Tables tables;
 };

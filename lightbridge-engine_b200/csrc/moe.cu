@@ -21,13 +21,25 @@
 
 #include "lbk_kernels.h"
 #include "lbk_moe.h"
+#include "lbk_topk.cuh"
 
 namespace lbk {
 
 namespace {
 
-constexpr int kGUThreads = 512;
-constexpr int kGUWarps = kGUThreads / 32;
+// 8 warps per SM with deep per-warp prefetch: registers, not warps, carry
+// the bytes in flight (about 80 KB per SM for IQ2_S gate/up).
+constexpr int kGUThreads = kMoeGateUpWarps * 32;
+constexpr int kGUWarps = kMoeGateUpWarps;
+constexpr int kDownMaxThreads = kMoeDownMaxSlots * 32;  // one warp per slot, top-k <= 8
+
+// Prefetch ring depth (steps of rps rows held in registers) per weight type.
+template <int T>
+struct RingDepth {
+    static constexpr bool kIq = (T == LBK_TYPE_IQ2_S || T == LBK_TYPE_IQ3_S);
+    static constexpr int kGateUp = kIq ? 4 : 1;  // two matrices per step
+    static constexpr int kDown = 3;  // 9 warps share 4 SMSPs: <= 168 registers per thread
+};
 
 template <int T>
 struct HBOf;
@@ -53,13 +65,20 @@ constexpr bool is_iq() {
     return T == LBK_TYPE_IQ2_S || T == LBK_TYPE_IQ3_S;
 }
 
-// Loads a thread's half block of a Q8_K row held in global memory.
+// Loads a thread's half block of a Q8_K row held in global memory in the
+// internal image layout (store_q8i).
 template <bool kTr>
 __device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, int b, int h, bool bsums) {
-    const uint8_t* blk = q8row + (size_t)b * kQ8Bytes;
-    const uint32_t* qw = reinterpret_cast<const uint32_t*>(blk + 4 + 128 * h);
+    const uint8_t* blk = q8row + (size_t)b * kQ8IBytes;
+    const uint4* qw = reinterpret_cast<const uint4*>(blk + 128 * h);
 #pragma unroll
-    for (int i = 0; i < 32; i++) a.w[i] = __ldcg(reinterpret_cast<const unsigned int*>(qw + i));
+    for (int i = 0; i < 8; i++) {
+        uint4 v = __ldcg(qw + i);
+        a.w[4 * i + 0] = v.x;
+        a.w[4 * i + 1] = v.y;
+        a.w[4 * i + 2] = v.z;
+        a.w[4 * i + 3] = v.w;
+    }
     if (kTr) {
 #pragma unroll
         for (int j = 0; j < 4; j++) {
@@ -70,20 +89,20 @@ __device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, 
             transpose4(n[1], n[3], n[5], n[7], a.w[8 * j + 4], a.w[8 * j + 5], a.w[8 * j + 6], a.w[8 * j + 7]);
         }
     }
-    a.d = __uint_as_float(__ldcg(reinterpret_cast<const unsigned int*>(blk)));
+    a.d = __uint_as_float(__ldcg(reinterpret_cast<const unsigned int*>(blk + 288)));
+    uint4 bs = bsums ? __ldcg(reinterpret_cast<const uint4*>(blk + 256 + 16 * h)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        uint32_t v = bsums ? __ldcg(reinterpret_cast<const unsigned short*>(blk + 260 + 16 * h + 2 * i)) : 0u;
-        a.bsum[i] = (int32_t)(int16_t)v;
-    }
+    for (int i = 0; i < 8; i++) a.bsum[i] = (int32_t)(int16_t)((w32(bs, i >> 1) >> (16 * (i & 1))) & 0xffffu);
 }
 
 // Integer dot of one half block, dispatched on the weight type.
 template <int T>
 struct HBDot {
+    // t0 / t1: shared-window addresses of this lane's copy of the type's table
+    // and of the sign table (sign spread for IQ2_S, sign select for IQ3_S).
     template <class HB>
-    __device__ __forceinline__ static void run(const HB& w, const ActHB& a, const uint32_t* na, const uint32_t* t0,
-                                               const uint32_t* t1, int h, IqPart& ip, KPart& kp) {
+    __device__ __forceinline__ static void run(const HB& w, const ActHB& a, const uint32_t* na, uint32_t t0,
+                                               uint32_t t1, int h, IqPart& ip, KPart& kp) {
         if constexpr (T == LBK_TYPE_IQ2_S) {
             ip = dot_hb(w, a, t0, t1);
         } else if constexpr (T == LBK_TYPE_IQ3_S) {
@@ -163,9 +182,22 @@ constexpr int table_bytes() {
 
 template <int T>
 __device__ __forceinline__ void fill_tables(uint32_t* tab, uint32_t* signs, const Tables& t) {
-    if constexpr (T == LBK_TYPE_IQ2_S) fill_iq2_codes(tab, t.iq2s_grid);
-    if constexpr (T == LBK_TYPE_IQ3_S) fill_iq3_grid(tab, t.iq3s_grid);
+    if constexpr (T == LBK_TYPE_IQ2_S) fill_iq2_codes(tab, t);
+    if constexpr (T == LBK_TYPE_IQ3_S) fill_iq3_grid(tab, t);
     (void)signs;
+}
+
+// The sign table a kernel holds: one IQ type per kernel at most.
+template <int TA, int TB>
+__device__ __forceinline__ void fill_sign_table(uint32_t* signs, const Tables& t) {
+    static_assert(!(TA == LBK_TYPE_IQ2_S && TB == LBK_TYPE_IQ3_S) && !(TA == LBK_TYPE_IQ3_S && TB == LBK_TYPE_IQ2_S),
+                  "one IQ type per kernel");
+    if constexpr (TA == LBK_TYPE_IQ3_S || TB == LBK_TYPE_IQ3_S) fill_sign_sel(signs, t);
+    else fill_signs(signs, t);
+}
+
+__device__ __forceinline__ uint32_t lane_addr(const uint32_t* tab) {
+    return (uint32_t)__cvta_generic_to_shared(tab + (threadIdx.x & 31));
 }
 
 // ---------------------------------------------------------------- gate / up
@@ -199,65 +231,77 @@ __device__ __forceinline__ void gate_up_rows(const MoeGateUpArgs& a, uint64_t t,
     ActHB act;
     uint32_t nact[32];
     if (lane_on) {
-        load_act_global<!kIq>(act, a.q8x + t * (uint64_t)nb * kQ8Bytes, b, h, !kIq);
+        load_act_global<!kIq>(act, a.q8x + t * (uint64_t)nb * kQ8IBytes, b, h, !kIq);
         if constexpr (T == LBK_TYPE_IQ3_S) {
 #pragma unroll
             for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
         }
     }
-    const uint32_t* t0 = tab + lane;
-    const uint32_t* t1 = signs + lane;
+    const uint32_t t0 = lane_addr(tab);
+    const uint32_t t1 = lane_addr(signs);
     MatrixRef gm{gmat, a.ffn, nb}, um{umat, a.ffn, nb};
 
-    // Rows stream with a one-step prefetch; every `bmax` rows (a multiple of
-    // rps) the batch's tails and SwiGLU are replayed.
+    // Rows stream through a ring of D prefetched steps held in registers
+    // (the loads of step i+D are issued before step i is decoded); every
+    // `bmax` rows (a multiple of rps) the batch's tails and SwiGLU are replayed.
+    constexpr int D = RingDepth<T>::kGateUp;
     const int bmax = kIq ? a.bmax_iq : a.bmax_k;
     float* hrow = a.h + (t * (a.k + 1) + slot) * a.ffn;
-    HB gcur, ucur;
-    if (lane_on && r0 + sub < r1) {
-        load_hb<LBK_LAYOUT_PLANAR>(gcur, gm, r0 + sub, b, h);
-        load_hb<LBK_LAYOUT_PLANAR>(ucur, um, r0 + sub, b, h);
+    HB gbuf[D], ubuf[D];
+#pragma unroll
+    for (int i = 0; i < D; i++) {
+        const uint64_t row = r0 + (uint64_t)i * rps + sub;
+        if (lane_on && row < r1) {
+            load_hb<LBK_LAYOUT_PLANAR>(gbuf[i], gm, row, b, h);
+            load_hb<LBK_LAYOUT_PLANAR>(ubuf[i], um, row, b, h);
+        }
     }
     uint64_t rb = r0;
-    for (uint64_t r = r0; r < r1; r += rps) {
-        const uint64_t row = r + sub;
-        const bool mine = lane_on && row < r1;
-        HB gw = gcur, uw = ucur;
-        const uint64_t nrow = row + rps;
-        if (lane_on && nrow < r1) {
-            load_hb<LBK_LAYOUT_PLANAR>(gcur, gm, nrow, b, h);
-            load_hb<LBK_LAYOUT_PLANAR>(ucur, um, nrow, b, h);
-        }
-        IqPart gi{0, 0}, ui{0, 0};
-        KPart gk, uk;
+    for (uint64_t base = r0; base < r1; base += (uint64_t)D * rps) {
 #pragma unroll
-        for (int l = 0; l < 8; l++) gk.lane[l] = uk.lane[l] = 0;
-        gk.min_sum = uk.min_sum = 0;
-        gk.dm = uk.dm = 0;
-        if (mine) {
-            HBDot<T>::run(gw, act, nact, t0, t1, h, gi, gk);
-            HBDot<T>::run(uw, act, nact, t0, t1, h, ui, uk);
-        }
-        const int ri = (int)(row - rb);
-        float* pg = prod + (size_t)(ri * 2 + 0) * nb * kTail;
-        float* pu = prod + (size_t)(ri * 2 + 1) * nb * kTail;
-        write_products<T>(pg, b, h, mine, gi, gk, act.d, a.status, row * nb + b);
-        write_products<T>(pu, b, h, mine, ui, uk, act.d, a.status, row * nb + b);
-        const uint64_t rn = r + rps;
-        if (rn - rb >= (uint64_t)bmax || rn >= r1) {
-            const int nrows = (int)((rn < r1 ? rn : r1) - rb);
-            __syncwarp();
-            warp_tails<T>(prod, nrows * 2, nb, chains, res);
-            // SwiGLU per row; one lane per row
-            for (int q = lane; q < nrows; q += 32) {
-                float g = res[q * 2], u = res[q * 2 + 1];
-                float v = swiglu_ref(g, u);
-                if (!isfinite(v))
-                    report(a.status, LBK_NON_FINITE_VALUE, (t * (a.k + 1) + slot) * a.ffn + rb + q, __float_as_uint(v));
-                hrow[rb + q] = v;
+        for (int i = 0; i < D; i++) {
+            const uint64_t r = base + (uint64_t)i * rps;
+            if (r >= r1) break;  // warp-uniform
+            const uint64_t row = r + sub;
+            const bool mine = lane_on && row < r1;
+            const HB gw = gbuf[i], uw = ubuf[i];
+            const uint64_t nrow = row + (uint64_t)D * rps;
+            if (lane_on && nrow < r1) {
+                load_hb<LBK_LAYOUT_PLANAR>(gbuf[i], gm, nrow, b, h);
+                load_hb<LBK_LAYOUT_PLANAR>(ubuf[i], um, nrow, b, h);
             }
-            __syncwarp();
-            rb = rn;
+            IqPart gi{0, 0}, ui{0, 0};
+            KPart gk, uk;
+#pragma unroll
+            for (int l = 0; l < 8; l++) gk.lane[l] = uk.lane[l] = 0;
+            gk.min_sum = uk.min_sum = 0;
+            gk.dm = uk.dm = 0;
+            if (mine) {
+                HBDot<T>::run(gw, act, nact, t0, t1, h, gi, gk);
+                HBDot<T>::run(uw, act, nact, t0, t1, h, ui, uk);
+            }
+            const int ri = (int)(row - rb);
+            float* pg = prod + (size_t)(ri * 2 + 0) * nb * kTail;
+            float* pu = prod + (size_t)(ri * 2 + 1) * nb * kTail;
+            write_products<T>(pg, b, h, mine, gi, gk, act.d, a.status, row * nb + b);
+            write_products<T>(pu, b, h, mine, ui, uk, act.d, a.status, row * nb + b);
+            const uint64_t rn = r + rps;
+            if (rn - rb >= (uint64_t)bmax || rn >= r1) {
+                const int nrows = (int)((rn < r1 ? rn : r1) - rb);
+                __syncwarp();
+                warp_tails<T>(prod, nrows * 2, nb, chains, res);
+                // SwiGLU per row; one lane per row
+                for (int q = lane; q < nrows; q += 32) {
+                    float g = res[q * 2], u = res[q * 2 + 1];
+                    float v = swiglu_ref(g, u);
+                    if (!isfinite(v))
+                        report(a.status, LBK_NON_FINITE_VALUE, (t * (a.k + 1) + slot) * a.ffn + rb + q,
+                               __float_as_uint(v));
+                    hrow[rb + q] = v;
+                }
+                __syncwarp();
+                rb = rn;
+            }
         }
     }
 }
@@ -292,13 +336,8 @@ __device__ __forceinline__ void arrive_and_quantize(const MoeGateUpArgs& a, uint
         if (lane == 0) *cnt = 0u;  // ready for the next launch
         if (__ballot_sync(0xffffffffu, bad)) continue;  // already reported by the SwiGLU check
         Q8Block q = quantize_q8k_warp(v, lane);
-        uint8_t* o = a.hq + (sidx * a.nb_f + blk) * kQ8Bytes;
-        uint32_t* ow = reinterpret_cast<uint32_t*>(o + 4);
-        ow[lane * 2] = q.q[0];
-        ow[lane * 2 + 1] = q.q[1];
         int32_t pair = q.pair_sum + __shfl_xor_sync(0xffffffffu, q.pair_sum, 1);
-        if ((lane & 1) == 0) *reinterpret_cast<int16_t*>(o + 260 + lane) = (int16_t)pair;
-        if (lane == 0) *reinterpret_cast<float*>(o) = q.d;
+        store_q8i(a.hq + (sidx * a.nb_f + blk) * kQ8IBytes, q, pair, lane);
     }
 }
 
@@ -315,9 +354,28 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
     float* chains = prod_all + (size_t)kGUWarps * a.prod_floats + (size_t)warp * a.chain_floats;
     float* res = chains + a.chain_floats - 64;
 
+    // Single-token decode: every CTA finishes the router itself (sum of the
+    // chunk partials in chunk order, then top-k) while the other warps copy
+    // the tables; CTA 0 publishes the routing for the down kernel.
+    __shared__ float s_logits[1024];
+    __shared__ lbk_routed s_routed[32];
+    if (a.defer_topk && warp == 0) {
+        const int lane = threadIdx.x & 31;
+        for (uint64_t e = lane; e < a.experts; e += 32) {
+            const float* pp = a.partials + e * a.chunks;
+            float sum = 0.0f;
+            for (uint64_t c = 0; c < a.chunks; c++) sum = __fadd_rn(sum, __ldcg(pp + c));
+            s_logits[e] = sum;
+        }
+        __syncwarp();
+        topk_warp(s_logits, a.bias, (int)a.experts, (int)a.k, a.weight_scale, s_routed,
+                  blockIdx.x == 0 ? a.status : nullptr, 0);
+        __syncwarp();
+        if (blockIdx.x == 0 && lane < (int)a.k) a.routed_store[lane] = s_routed[lane];
+    }
     fill_tables<TG>(tabG, signs, a.tables);
     if constexpr (S::kTabS != 0) fill_tables<TS>(tabS, signs, a.tables);
-    if constexpr (S::kSigns) fill_signs(signs);
+    if constexpr (S::kSigns) fill_sign_table<TG, TS>(signs, a.tables);
     __syncthreads();
 
     const uint64_t gw = (uint64_t)blockIdx.x * kGUWarps + warp;
@@ -327,7 +385,7 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
         uint64_t t = gw / (a.k * a.chunks_r);
         uint64_t rem = gw % (a.k * a.chunks_r);
         uint64_t j = rem / a.chunks_r, c = rem % a.chunks_r;
-        uint32_t e = a.routed[t * a.k + j].expert_id;
+        uint32_t e = a.defer_topk ? s_routed[j].expert_id : a.routed[t * a.k + j].expert_id;
         if (e >= a.experts) {  // reported; compute on expert 0 so the arrival counts stay balanced
             if ((threadIdx.x & 31) == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
             e = 0;
@@ -374,39 +432,48 @@ __device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint
     ActHB act;
     uint32_t nact[32];
     if (lane_on) {
-        load_act_global<!kIq>(act, a.hq + sidx * (uint64_t)nb * kQ8Bytes, b, h, !kIq);
+        load_act_global<!kIq>(act, a.hq + sidx * (uint64_t)nb * kQ8IBytes, b, h, !kIq);
         if constexpr (T == LBK_TYPE_IQ3_S) {
 #pragma unroll
             for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
         }
     }
-    const uint32_t* t0 = tab + lane;
-    const uint32_t* t1 = signs + lane;
+    const uint32_t t0 = lane_addr(tab);
+    const uint32_t t1 = lane_addr(signs);
     MatrixRef dm{dmat, a.hidden, nb};
-    // this warp's rows: r0 + wsub*rps + i*wps*rps + sub
+    // this warp's rows: r0 + wsub*rps + i*wps*rps + sub, through a ring of D
+    // prefetched steps in registers
+    constexpr int D = RingDepth<T>::kDown;
     const uint64_t stride = (uint64_t)a.wps * rps;
+    const uint64_t first = r0 + (uint64_t)wsub * rps;
     int nd = 0;
-    HB cur;
-    {
-        uint64_t row = r0 + (uint64_t)wsub * rps + sub;
-        if (lane_on && row < r1) load_hb<LBK_LAYOUT_PLANAR>(cur, dm, row, b, h);
-    }
-    for (uint64_t base = r0 + (uint64_t)wsub * rps; base < r1; base += stride) {
-        const uint64_t row = base + sub;
-        const bool mine = lane_on && row < r1;
-        HB w = cur;
-        const uint64_t nrow = row + stride;
-        if (lane_on && nrow < r1) load_hb<LBK_LAYOUT_PLANAR>(cur, dm, nrow, b, h);
-        IqPart ip{0, 0};
-        KPart kp;
+    HB buf[D];
 #pragma unroll
-        for (int l = 0; l < 8; l++) kp.lane[l] = 0;
-        kp.min_sum = 0;
-        kp.dm = 0;
-        if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
-        float* pd = prod + (size_t)(nd + sub) * nb * kTail;
-        write_products<T>(pd, b, h, mine, ip, kp, act.d, a.status, row * nb + b);
-        nd += rps;
+    for (int i = 0; i < D; i++) {
+        const uint64_t row = first + (uint64_t)i * stride + sub;
+        if (lane_on && row < r1) load_hb<LBK_LAYOUT_PLANAR>(buf[i], dm, row, b, h);
+    }
+    for (uint64_t base = first; base < r1; base += (uint64_t)D * stride) {
+#pragma unroll
+        for (int i = 0; i < D; i++) {
+            const uint64_t r = base + (uint64_t)i * stride;
+            if (r >= r1) break;  // warp-uniform
+            const uint64_t row = r + sub;
+            const bool mine = lane_on && row < r1;
+            const HB w = buf[i];
+            const uint64_t nrow = row + (uint64_t)D * stride;
+            if (lane_on && nrow < r1) load_hb<LBK_LAYOUT_PLANAR>(buf[i], dm, nrow, b, h);
+            IqPart ip{0, 0};
+            KPart kp;
+#pragma unroll
+            for (int l = 0; l < 8; l++) kp.lane[l] = 0;
+            kp.min_sum = 0;
+            kp.dm = 0;
+            if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
+            float* pd = prod + (size_t)(nd + sub) * nb * kTail;
+            write_products<T>(pd, b, h, mine, ip, kp, act.d, a.status, row * nb + b);
+            nd += rps;
+        }
     }
     __syncwarp();
     warp_tails<T>(prod, nd, nb, chains, res);
@@ -418,7 +485,7 @@ __device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint
 }
 
 template <int TD, int TSD>
-__global__ void __launch_bounds__(576, 1) moe_down_kernel(MoeDownArgs a) {
+__global__ void __launch_bounds__(kDownMaxThreads, 1) moe_down_kernel(MoeDownArgs a) {
     using S = DownSmem<TD, TSD>;
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t* tabD = reinterpret_cast<uint32_t*>(smem);
@@ -434,7 +501,7 @@ __global__ void __launch_bounds__(576, 1) moe_down_kernel(MoeDownArgs a) {
 
     fill_tables<TD>(tabD, signs, a.tables);
     if constexpr (S::kTabS != 0) fill_tables<TSD>(tabS, signs, a.tables);
-    if constexpr (S::kSigns) fill_signs(signs);
+    if constexpr (S::kSigns) fill_sign_table<TD, TSD>(signs, a.tables);
     __syncthreads();
 
     const uint64_t t = blockIdx.y;

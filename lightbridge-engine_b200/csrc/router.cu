@@ -14,6 +14,7 @@
 //    tokens to Q8_K for the expert kernels and, in its last CTA, runs top-k.
 
 #include "lbk_kernels.h"
+#include "lbk_topk.cuh"
 
 namespace lbk {
 
@@ -21,102 +22,6 @@ namespace {
 
 constexpr int kRouterThreads = 512;
 constexpr int kChunk = 512;     // hidden lanes per warp work item
-constexpr int kMaxCand = 32;    // candidates per lane in top-k (E <= 1024)
-
-__device__ __forceinline__ uint32_t ord_f32(float f) {
-    if (f == 0.0f) f = 0.0f;  // -0 and +0 compare equal in the reference sort
-    uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Top-k of one token by one warp (routing.rs:25-107).
-__device__ void topk_warp(const float* logits, const float* bias, int E, int k, float weight_scale, lbk_routed* out,
-                          DeviceStatus* st, uint64_t token) {
-    const int lane = threadIdx.x & 31;
-    float p[kMaxCand], s[kMaxCand];
-    uint32_t bad_idx = 0xffffffffu, bad_bits = 0;
-#pragma unroll
-    for (int c = 0; c < kMaxCand; c++) {
-        int i = c * 32 + lane;
-        p[c] = 0.0f;
-        s[c] = 0.0f;
-        if (i < E) {
-            float l = logits[i], b = bias[i];
-            float pv = sigmoid_ref(l);
-            float sv = __fadd_rn(pv, b);
-            if (!isfinite(l) || !isfinite(b) || !isfinite(sv)) {
-                if ((uint32_t)i < bad_idx) {
-                    bad_idx = (uint32_t)i;
-                    bad_bits = !isfinite(l) ? __float_as_uint(l) : (!isfinite(b) ? __float_as_uint(b) : __float_as_uint(sv));
-                }
-            }
-            p[c] = pv;
-            s[c] = sv;
-        }
-    }
-    uint32_t min_bad = bad_idx;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) min_bad = min(min_bad, __shfl_xor_sync(0xffffffffu, min_bad, o));
-    if (min_bad != 0xffffffffu) {
-        if (bad_idx == min_bad) report(st, LBK_NON_FINITE_ROUTING_VALUE, token * (uint64_t)E + min_bad, bad_bits);
-        return;
-    }
-    uint32_t taken = 0;  // bit c: candidate c of this lane selected
-    uint32_t sel_id[32];
-    float sel_p[32];
-    for (int r = 0; r < k; r++) {
-        unsigned long long best = 0ull;
-#pragma unroll
-        for (int c = 0; c < kMaxCand; c++) {
-            int i = c * 32 + lane;
-            if (i < E && !((taken >> c) & 1u)) {
-                unsigned long long key = ((unsigned long long)ord_f32(s[c]) << 32) | (0xffffffffu - (uint32_t)i);
-                best = key > best ? key : best;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-            best = other > best ? other : best;
-        }
-        uint32_t id = 0xffffffffu - (uint32_t)(best & 0xffffffffull);
-        int owner = (int)(id & 31), c_sel = (int)(id >> 5);
-        float pv = 0.0f;
-#pragma unroll
-        for (int c = 0; c < kMaxCand; c++)
-            if (c == c_sel) pv = p[c];
-        pv = __shfl_sync(0xffffffffu, pv, owner);
-        if (lane == owner) taken |= 1u << c_sel;
-        sel_id[r] = id;
-        sel_p[r] = pv;
-    }
-    if (lane == 0) {
-        float wsum = 0.0f;
-        for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, sel_p[r]);
-        const float floor_v = 0.000061035156f;  // 2^-14 (routing.rs:5)
-        wsum = wsum < floor_v ? floor_v : wsum;
-        // output sorted by expert ID (routing.rs:105)
-        for (int i = 1; i < k; i++) {
-            uint32_t id = sel_id[i];
-            float pv = sel_p[i];
-            int j = i - 1;
-            while (j >= 0 && sel_id[j] > id) {
-                sel_id[j + 1] = sel_id[j];
-                sel_p[j + 1] = sel_p[j];
-                j--;
-            }
-            sel_id[j + 1] = id;
-            sel_p[j + 1] = pv;
-        }
-        for (int r = 0; r < k; r++) {
-            lbk_routed o;
-            o.expert_id = sel_id[r];
-            o.coefficient = __fmul_rn(__fdiv_rn(sel_p[r], wsum), weight_scale);
-            out[r] = o;
-        }
-    }
-}
-
 __global__ void topk_kernel(TopkArgs a) {
     const int warp = threadIdx.x >> 5;
     const int nw = blockDim.x >> 5;
@@ -161,26 +66,39 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
             uint64_t e = it / chunks, c = it % chunks;
             uint64_t j0 = c * kChunk;
             const float* w = a.w + e * a.hidden;
-            float wr[16];
+            // All loads first: no store (partials, status) may sit between
+            // them, or the compiler serializes the loads behind it.
+            float wr[16], xr[16];
 #pragma unroll
             for (int q = 0; q < 16; q++) {
                 uint64_t j = j0 + (uint64_t)q * 32 + lane;
                 wr[q] = j < a.hidden ? __ldcs(w + j) : 0.0f;
-                if (j < a.hidden && !isfinite(wr[q])) report(a.status, LBK_NON_FINITE_VALUE, e * a.hidden + j, __float_as_uint(wr[q]));
+                xr[q] = j < a.hidden ? __ldg(a.x + j) : 0.0f;  // token 0
             }
             for (uint64_t t = 0; t < a.tokens; t++) {
-                const float* x = a.x + t * a.hidden;
+                if (t > 0) {
+#pragma unroll
+                    for (int q = 0; q < 16; q++) {
+                        uint64_t j = j0 + (uint64_t)q * 32 + lane;
+                        xr[q] = j < a.hidden ? __ldg(a.x + t * a.hidden + j) : 0.0f;
+                    }
+                }
                 float acc = 0.0f;
 #pragma unroll
-                for (int q = 0; q < 16; q++) {
-                    uint64_t j = j0 + (uint64_t)q * 32 + lane;
-                    float xv = j < a.hidden ? __ldg(x + j) : 0.0f;
-                    acc = __fadd_rn(acc, __fmul_rn(wr[q], xv));
-                }
+                for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(wr[q], xr[q]));
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
                 if (lane == 0) f.partials[(t * a.experts + e) * chunks + c] = acc;
             }
+            int bad_q = -1;
+            uint32_t bad_bits = 0;
+#pragma unroll
+            for (int q = 15; q >= 0; q--)
+                if (!isfinite(wr[q])) {
+                    bad_q = q;
+                    bad_bits = __float_as_uint(wr[q]);
+                }
+            if (bad_q >= 0) report(a.status, LBK_NON_FINITE_VALUE, e * a.hidden + j0 + (uint64_t)bad_q * 32 + lane, bad_bits);
         } else {
             uint64_t q = it - row_items;
             uint64_t t = q / nbq, b = q % nbq;
@@ -203,17 +121,14 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
                 continue;
             }
             Q8Block qb = quantize_q8k_warp(v, lane);
-            uint8_t* o = f.q8x + (t * nbq + b) * kQ8Bytes;
-            uint32_t* ow = reinterpret_cast<uint32_t*>(o + 4);
-            ow[lane * 2] = qb.q[0];
-            ow[lane * 2 + 1] = qb.q[1];
             int32_t pair = qb.pair_sum + __shfl_xor_sync(0xffffffffu, qb.pair_sum, 1);
-            if ((lane & 1) == 0) *reinterpret_cast<int16_t*>(o + 260 + lane) = (int16_t)pair;
-            if (lane == 0) *reinterpret_cast<float*>(o) = qb.d;
+            store_q8i(f.q8x + (t * nbq + b) * kQ8IBytes, qb, pair, lane);
         }
     }
 
-    // The last CTA to finish sums the chunk partials in chunk order and routes.
+    // The last CTA to finish sums the chunk partials in chunk order and routes
+    // (unless the consumer kernel does both itself).
+    if (f.defer) return;
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();

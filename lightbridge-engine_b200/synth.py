@@ -56,9 +56,10 @@ def packed_torch(gen, ty: int, in_w: int, out_w: int, device, d_range=None):
 
 # ---------------------------------------------------------------- planar
 
-_FIELDS = {  # (GGUF offset, bytes per block, lane-major) in plane order
-    TYPE_IQ2_S: [(2, 32, False), (34, 32, False), (66, 8, False), (74, 8, False), (0, 2, False)],
-    TYPE_IQ3_S: [(2, 64, False), (74, 32, False), (66, 8, False), (106, 4, False), (0, 2, False)],
+_FIELDS = {  # (GGUF offset, bytes per block, permutation) in plane order
+    # permutation: False none, True lane-major, "qh" bit-transposed words
+    TYPE_IQ2_S: [(2, 32, False), (34, 32, False), (66, 8, "qh"), (74, 8, False), (0, 2, False)],
+    TYPE_IQ3_S: [(2, 64, False), (74, 32, False), (66, 8, "qh"), (106, 4, False), (0, 2, False)],
     TYPE_Q4_K: [(16, 128, True), (4, 12, False), (0, 4, False)],
     TYPE_Q5_K: [(48, 128, True), (16, 32, True), (4, 12, False), (0, 4, False)],
 }
@@ -77,6 +78,29 @@ def _lane_major_inv(field: np.ndarray) -> np.ndarray:
     return g.transpose(0, 1, 3, 2).reshape(n, -1)
 
 
+def qh_transpose(w: np.ndarray) -> np.ndarray:
+    """Transpose of the 4x4 matrix of 2-bit cells of each uint32 (cell (r, c)
+    at bit 8r + 2c); its own inverse."""
+    w = w.astype(np.uint32)
+    t = ((w >> np.uint32(12)) ^ w) & np.uint32(0x0000F0F0)
+    w = w ^ t ^ (t << np.uint32(12))
+    t = ((w >> np.uint32(6)) ^ w) & np.uint32(0x00CC00CC)
+    return w ^ t ^ (t << np.uint32(6))
+
+
+def _qh_words(field: np.ndarray) -> np.ndarray:
+    words = np.ascontiguousarray(field).view("<u4")
+    return qh_transpose(words).astype("<u4").view(np.uint8).reshape(field.shape)
+
+
+def _permute(field: np.ndarray, how, inverse: bool) -> np.ndarray:
+    if how == "qh":
+        return _qh_words(field)
+    if how:
+        return _lane_major_inv(field) if inverse else _lane_major(field)
+    return field
+
+
 def planar_np(ty: int, gguf: np.ndarray) -> np.ndarray:
     """GGUF bytes -> planar bytes (the layout of lbk_repack)."""
     bb = BLOCK_BYTES[ty]
@@ -84,7 +108,7 @@ def planar_np(ty: int, gguf: np.ndarray) -> np.ndarray:
     planes = []
     for off, nbytes, lm in _FIELDS[ty]:
         f = blocks[:, off : off + nbytes]
-        planes.append((_lane_major(f) if lm else f).reshape(-1))
+        planes.append(_permute(f, lm, False).reshape(-1))
     return np.concatenate(planes)
 
 
@@ -95,6 +119,6 @@ def gguf_from_planar_np(ty: int, planar: np.ndarray) -> np.ndarray:
     pos = 0
     for off, nbytes, lm in _FIELDS[ty]:
         f = planar[pos : pos + nblk * nbytes].reshape(nblk, nbytes)
-        out[:, off : off + nbytes] = _lane_major_inv(f) if lm else f
+        out[:, off : off + nbytes] = _permute(f, lm, True)
         pos += nblk * nbytes
     return out.reshape(-1)

@@ -131,10 +131,23 @@ def test_expert_validation():
 
 
 @pytest.mark.parametrize("ty", [synth.TYPE_IQ2_S, synth.TYPE_IQ3_S, synth.TYPE_Q4_K, synth.TYPE_Q5_K])
-def test_planar_layout_is_a_byte_permutation(ty):
+def test_planar_layout_round_trips(ty):
     rng = np.random.default_rng(ty)
     w = synth.packed_np(rng, ty, 768, 5)
     p = synth.planar_np(ty, w)
     assert p.size == w.size
-    assert np.array_equal(np.sort(p), np.sort(w))
+    if ty in (synth.TYPE_Q4_K, synth.TYPE_Q5_K):  # a pure byte permutation
+        assert np.array_equal(np.sort(p), np.sort(w))
     assert np.array_equal(synth.gguf_from_planar_np(ty, p), w)
+
+
+def test_qh_transpose_moves_two_bit_cells():
+    rng = np.random.default_rng(7)
+    w = rng.integers(0, 1 << 32, size=4096, dtype=np.uint64).astype(np.uint32)
+    t = synth.qh_transpose(w)
+    assert np.array_equal(synth.qh_transpose(t), w)
+    for r in range(4):
+        for c in range(4):
+            src = (w >> np.uint32(8 * r + 2 * c)) & np.uint32(3)
+            dst = (t >> np.uint32(8 * c + 2 * r)) & np.uint32(3)
+            assert np.array_equal(src, dst)
