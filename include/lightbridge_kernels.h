@@ -288,6 +288,25 @@ int32_t lbk_moe_layer_trace_read(lbk_moe_layer* layer, float ms[3]);
 int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, const lbk_routed* routed,
                        float* out, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* lbk_moe_forward without a caller workspace and without any allocation: the
+ * workspace is a fixed 1 MiB array of this library's device memory, one per
+ * device. No counterpart in the reference (its moe_routed_by_id_into takes
+ * caller scratch, moe.rs:64-71). For callers that cannot allocate device
+ * memory: an FFI host holding only device pointers handed to it, with no
+ * device allocator of its own, and decode loops in which cudaMalloc / cudaFree
+ * would synchronize the device.
+ *   - Returns LBK_SCRATCH_TOO_SMALL (detail: expected = bytes needed) when the
+ *     layer's workspace for `tokens` exceeds 1 MiB (hidden 4096, ffn 1536,
+ *     top-8 fits up to 8 tokens).
+ *   - The first call on a device looks up the array and zero-fills it
+ *     synchronously; make it before any stream capture on that device. The
+ *     array's counter prefix must be zero when a call starts; every call that
+ *     runs to completion leaves it at zero.
+ *   - Calls that overlap in time on one device (any stream, thread or layer)
+ *     share the array and race: serialize them. */
+int32_t lbk_moe_forward_no_alloc(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
+                                 lbk_routed* routed_out, int32_t router_mode, void* stream);
+
 /* ------------------------------------------------------- layout tools */
 
 /* Converts a GGUF-layout matrix into the planar device layout (same byte

@@ -934,6 +934,71 @@ LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t to
     return moe_experts(layer, x, tokens, routed, out, ws, o, st);
 }
 
+// ------------------------------------------------- MoE forward, no allocation
+//
+// lbk_moe_forward_no_alloc runs lbk_moe_forward with its workspace in a fixed
+// array of this library's device memory, so the caller allocates nothing and
+// the call allocates nothing (no cudaMalloc / cudaFree, no allocating library
+// routine). It serves callers that cannot allocate device memory: an FFI host
+// that receives device pointers from another component and has no device
+// allocator of its own to create the workspace, and decode loops in which a
+// cudaMalloc / cudaFree would synchronize the device between layers.
+//
+// Limits: one array per device, shared by every call on that device, so calls
+// that overlap in time (other streams, other host threads, other layers)
+// race on it; serialize them (one stream, or events). Layers and token counts
+// whose workspace exceeds kStaticScratchBytes are rejected with
+// LBK_SCRATCH_TOO_SMALL. The counter prefix of the workspace must be zero when
+// a call starts: the first call on a device zero-fills the whole array, and
+// every call that runs to completion leaves the counters at zero again.
+namespace {
+
+constexpr uint64_t kStaticScratchBytes = 1ull << 20;  // 1 MiB: hidden 4096 / ffn 1536 / top-8 decode up to 8 tokens
+constexpr int kStaticScratchDevices = 64;
+
+static __device__ __align__(256) uint8_t g_moe_scratch[kStaticScratchBytes];
+
+std::mutex g_static_scratch_mu;
+uint8_t* g_static_scratch[kStaticScratchDevices];
+
+// Address of the array on `device`, which must be current. First call per
+// device: symbol lookup plus a synchronous zero fill (setup work that belongs
+// before any stream capture on that device).
+int32_t static_scratch(int device, uint8_t** out) {
+    if (device < 0 || device >= kStaticScratchDevices)
+        return fail(LBK_INVALID_PARAMETER, "device ordinal beyond the static scratch table", 0,
+                    (uint64_t)kStaticScratchDevices, (uint64_t)device);
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    if (g_static_scratch[device] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_moe_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static MoE scratch)");
+        if ((e = cudaMemset(p, 0, kStaticScratchBytes)) != cudaSuccess) return cuda_fail(e, "zero static MoE scratch");
+        if ((e = cudaDeviceSynchronize()) != cudaSuccess) return cuda_fail(e, "zero static MoE scratch");
+        g_static_scratch[device] = static_cast<uint8_t*>(p);
+    }
+    *out = g_static_scratch[device];
+    return LBK_OK;
+}
+
+}  // namespace
+
+LBK_API int32_t lbk_moe_forward_no_alloc(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
+                                         lbk_routed* routed_out, int32_t router_mode, void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    const uint64_t need = moe_ws(layer, tokens).total;
+    if (need > kStaticScratchBytes)
+        return fail(LBK_SCRATCH_TOO_SMALL,
+                    "static MoE scratch (1 MiB) is smaller than this layer's workspace for this token count; "
+                    "use lbk_moe_forward with a caller workspace",
+                    0, need, kStaticScratchBytes);
+    if (int32_t s = set_device(layer->ctx)) return s;
+    uint8_t* ws = nullptr;
+    if (int32_t s = static_scratch(layer->ctx->device, &ws)) return s;
+    return lbk_moe_forward(layer, x, tokens, out, routed_out, router_mode, ws, kStaticScratchBytes, stream);
+}
+
 // ------------------------------------------------------------ layout tools
 
 namespace {

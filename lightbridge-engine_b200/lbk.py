@@ -121,6 +121,7 @@ def _load() -> ctypes.CDLL:
         "lbk_moe_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
         "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
         "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
+        "lbk_moe_forward_no_alloc": ([P, P, U64, P, P, I32, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
         "lbk_repack": ([P, PM, P, U64, P], I32),
@@ -140,7 +141,8 @@ EXPORTED = (
     "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
     "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused "
-    "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_layer_trace lbk_moe_layer_trace_read "
+    "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
+    "lbk_moe_layer_trace_read "
     "lbk_repack lbk_unpack lbk_validate_matrix"
 ).split()
 
