@@ -199,10 +199,10 @@ def build_layers(ctx, lbk, torch, dev, layers: int, seed0: int, keep_gguf_layer0
 
         def stacked(ty, k, rows):
             g = synth.packed_torch(gen, ty, k, rows * E, dev)
-            p = torch.empty_like(g)
-            mb = synth.matrix_bytes(ty, k, rows)
+            mb, pb = synth.matrix_bytes(ty, k, rows), synth.planar_bytes(ty, k, rows)
+            p = torch.empty(pb * E, dtype=torch.uint8, device=dev)
             for e in range(E):
-                ctx.repack(lbk.matrix(ty, k, rows, g[e * mb:(e + 1) * mb]), p[e * mb:(e + 1) * mb])
+                ctx.repack(lbk.matrix(ty, k, rows, g[e * mb:(e + 1) * mb]), p[e * pb:(e + 1) * pb])
             return g, p
 
         gg, gp = stacked(TYPE_IQ2_S, H, F)
@@ -212,7 +212,7 @@ def build_layers(ctx, lbk, torch, dev, layers: int, seed0: int, keep_gguf_layer0
         sh = []
         for ty, k, rows in [(TYPE_Q4_K, H, F), (TYPE_Q4_K, H, F), (TYPE_Q4_K, F, H)]:
             g = synth.packed_torch(gen, ty, k, rows, dev)
-            p = torch.empty_like(g)
+            p = torch.empty(synth.planar_bytes(ty, k, rows), dtype=torch.uint8, device=dev)
             ctx.repack(lbk.matrix(ty, k, rows, g), p)
             sh.append((ty, k, rows, g, p))
             keep.append(p)
@@ -224,7 +224,7 @@ def build_layers(ctx, lbk, torch, dev, layers: int, seed0: int, keep_gguf_layer0
                 "shared": [s[3].cpu().numpy() for s in sh],
             }
         del gg, ug, dg
-        mbg, mbd = synth.matrix_bytes(TYPE_IQ2_S, H, F), synth.matrix_bytes(TYPE_IQ3_S, F, H)
+        mbg, mbd = synth.planar_bytes(TYPE_IQ2_S, H, F), synth.planar_bytes(TYPE_IQ3_S, F, H)
         experts = [
             lbk.Expert(lbk.matrix(TYPE_IQ2_S, H, F, gp[e * mbg:(e + 1) * mbg], lbk.LAYOUT_PLANAR),
                        lbk.matrix(TYPE_IQ2_S, H, F, up[e * mbg:(e + 1) * mbg], lbk.LAYOUT_PLANAR),

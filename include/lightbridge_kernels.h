@@ -93,7 +93,7 @@ typedef enum lbk_status {
 /* Packed weight byte layouts. */
 typedef enum lbk_layout {
     LBK_LAYOUT_GGUF = 0,   /* GGUF / reference block layout, unchanged */
-    LBK_LAYOUT_PLANAR = 1  /* per-matrix field planes (see lbk_repack) */
+    LBK_LAYOUT_PLANAR = 1  /* row-planar, 16-byte row stride (see lbk_repack) */
 } lbk_layout;
 
 /* Router dot-product order. */
@@ -120,7 +120,8 @@ typedef struct lbk_error_detail {
 typedef struct lbk_context lbk_context;
 
 /* One packed matrix in device memory. Its byte length must be exactly
- * output_width * (input_width / 256) * block_bytes(type). */
+ * output_width * (input_width / 256) * block_bytes(type) in the GGUF layout,
+ * lbk_planar_bytes in the planar layout. */
 typedef struct lbk_matrix {
     int32_t type;            /* lbk_ggml_type */
     int32_t layout;          /* lbk_layout */
@@ -171,6 +172,10 @@ int32_t lbk_required_q8k_bytes(uint64_t input_width, uint64_t* bytes);
 /* Encoded byte length of a [input_width, output_width] matrix of `type`
  * (reference: EncodedTensorView::new, matrix.rs:26-78). */
 int32_t lbk_matrix_bytes(int32_t type, uint64_t input_width, uint64_t output_width, uint64_t* bytes);
+
+/* Byte length of the same matrix in the planar device layout (rows padded
+ * to 16 bytes, see lbk_repack); no counterpart in the reference. */
+int32_t lbk_planar_bytes(int32_t type, uint64_t input_width, uint64_t output_width, uint64_t* bytes);
 
 /* ------------------------------------------------------------- kernels */
 
@@ -309,21 +314,22 @@ int32_t lbk_moe_forward_no_alloc(lbk_moe_layer* layer, const float* x, uint64_t 
 
 /* ------------------------------------------------------- layout tools */
 
-/* Converts a GGUF-layout matrix into the planar device layout (same byte
- * count). Planar layout, per matrix of R rows and nb = input_width/256 blocks
- * per row, is a sequence of field planes, each row-major over (row, block):
- *   IQ2_S: qs[32] | signs[32] | qh[8] | scales[8] | d[2]
- *   IQ3_S: qs[64] | signs[32] | qh[8] | scales[4] | d[2]
- *   Q4_K : qs[128] | scales[12] | d[2] | dmin[2]
- *   Q5_K : qs[128] | qh[32] | scales[12] | d[2] | dmin[2]
- * so plane f of row r starts at plane_offset_f + r*nb*field_bytes_f. Inside
- * a block, Q4_K / Q5_K qs (and Q5_K qh) bytes are lane-major per 32-byte
- * group (new[4k+i] = old[k+8i]), and each little-endian 32-bit word of the
- * IQ2_S / IQ3_S qh field is stored as the transpose of its 4x4 matrix of
- * 2-bit cells (cell (r, c) at bit 8r+2c moves to bit 8c+2r). */
+/* Converts a GGUF-layout matrix into the planar device layout
+ * (lbk_planar_bytes long). Planar layout: rows at a stride of
+ * ceil16(nb * block_bytes) bytes (nb = input_width/256; the pad bytes are
+ * zero), each row a sequence of field planes over its nb blocks:
+ *   IQ2_S: qs[nb][32] | signs[nb][32] | qh[nb][8] | scales[nb][8] | d[nb][2]
+ *   IQ3_S: qs[nb][64] | signs[nb][32] | qh[nb][8] | scales[nb][4] | d[nb][2]
+ *   Q4_K : qs[nb][128] | scales[nb][12] | d,dmin[nb][4]
+ *   Q5_K : qs[nb][128] | qh[nb][32] | scales[nb][12] | d,dmin[nb][4]
+ * Inside a block, Q4_K / Q5_K qs (and Q5_K qh) bytes are lane-major per
+ * 32-byte group (new[4k+i] = old[k+8i]), and each little-endian 32-bit word
+ * of the IQ2_S / IQ3_S qh field is stored as the transpose of its 4x4 matrix
+ * of 2-bit cells (cell (r, c) at bit 8r+2c moves to bit 8c+2r). Every row
+ * starts 16-byte aligned, so any run of rows is one contiguous aligned copy. */
 int32_t lbk_repack(lbk_context* ctx, const lbk_matrix* src_gguf, void* dst_planar, uint64_t dst_bytes,
                    void* stream);
-/* Exact inverse of lbk_repack. */
+/* Exact inverse of lbk_repack (dst_bytes = lbk_matrix_bytes). */
 int32_t lbk_unpack(lbk_context* ctx, const lbk_matrix* src_planar, void* dst_gguf, uint64_t dst_bytes,
                    void* stream);
 

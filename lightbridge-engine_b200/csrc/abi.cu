@@ -124,7 +124,9 @@ int32_t check_matrix(const lbk_matrix* m, const char* what) {
     uint64_t nb = m->input_width / be;
     if (nb > UINT64_MAX / bb || nb * bb > UINT64_MAX / m->output_width)
         return fail(LBK_ARITHMETIC_OVERFLOW, "tensor encoded byte length");
-    uint64_t expected = nb * bb * m->output_width;
+    const uint64_t row_bytes = m->layout == LBK_LAYOUT_PLANAR ? (nb * bb + 15) & ~(uint64_t)15 : nb * bb;
+    if (row_bytes > UINT64_MAX / m->output_width) return fail(LBK_ARITHMETIC_OVERFLOW, "tensor encoded byte length");
+    uint64_t expected = row_bytes * m->output_width;
     if (m->bytes != expected) return fail(LBK_ENCODED_LENGTH_MISMATCH, "tensor encoded length", 0, expected, m->bytes);
     if (m->data == nullptr) return fail(LBK_INVALID_PARAMETER, "null matrix data");
     if (!aligned(m->data, 16)) return fail(LBK_INVALID_PARAMETER, "matrix data must be 16-byte aligned");
@@ -381,6 +383,15 @@ LBK_API int32_t lbk_matrix_bytes(int32_t type, uint64_t input_width, uint64_t ou
     if (input_width == 0 || output_width == 0 || input_width % be != 0)
         return fail(LBK_DIMENSION_MISMATCH, "block-aligned matrix input width", 0, be, input_width);
     *bytes = input_width / be * bb * output_width;
+    return ok();
+}
+
+LBK_API int32_t lbk_planar_bytes(int32_t type, uint64_t input_width, uint64_t output_width, uint64_t* bytes) {
+    if (bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null output pointer");
+    if (!dot_type(type)) return fail(LBK_UNSUPPORTED_TYPE, "only packed types have a planar layout", (uint64_t)type);
+    if (input_width == 0 || output_width == 0 || input_width % LBK_QK_K != 0)
+        return fail(LBK_DIMENSION_MISMATCH, "block-aligned matrix input width", 0, LBK_QK_K, input_width);
+    *bytes = ((input_width / LBK_QK_K * block_bytes(type) + 15) & ~(uint64_t)15) * output_width;
     return ok();
 }
 
@@ -740,8 +751,32 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.h = reinterpret_cast<float*>(ws + o.h);
         g.hq = ws + o.hq;
         g.counters = reinterpret_cast<unsigned int*>(ws + o.counters);
-        // Balance bytes over ~ (SMs x 16) warps: routed and shared rows differ in size.
+        g.status = ctx->status;
+        g.tables = ctx->tables();
         const int rps = 32 / g.tpr_h;
+        if (lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)nbh)) {
+            // Split the SMs between routed and shared CTAs by bytes streamed,
+            // then spread each role's rows evenly over its warps.
+            const double br = (double)T * L->k * L->F * 2.0 * nbh * block_bytes(L->gate_type);
+            const double bs = (double)T * L->F * 2.0 * nbh * block_bytes(L->sgate_type);
+            const unsigned ctas = (unsigned)ctx->sm_count;
+            long rc = std::lround(ctas * br / (br + bs));
+            rc = rc < 1 ? 1 : (rc > (long)ctas - 1 ? (long)ctas - 1 : rc);
+            g.routed_ctas = (uint32_t)rc;
+            auto chunk_for = [&](uint64_t warps, uint64_t instances) {
+                uint64_t per = warps / instances;
+                per = per < 1 ? 1 : per;
+                uint64_t c = (L->F + per - 1) / per;
+                return (c + rps - 1) / rps * rps;
+            };
+            g.chunk_r = chunk_for((uint64_t)rc * lbk::kMoeGateUpTmaWarps, T * L->k);
+            g.chunk_s = chunk_for((uint64_t)(ctas - rc) * lbk::kMoeGateUpTmaWarps, T);
+            g.chunks_r = (L->F + g.chunk_r - 1) / g.chunk_r;
+            g.chunks_s = (L->F + g.chunk_s - 1) / g.chunk_s;
+            e = lbk::launch_moe_gate_up_tma(L->gate_type, L->sgate_type, g, ctas, st);
+            if (e != cudaSuccess) return cuda_fail(e, "moe gate/up launch");
+        } else {
+        // Balance bytes over ~ (SMs x 16) warps: routed and shared rows differ in size.
         const double br = 2.0 * (double)(nbh * block_bytes(L->gate_type)), bs = 2.0 * (double)(nbh * block_bytes(L->sgate_type));
         const double total = (double)T * L->F * ((double)L->k * br + bs);
         const double per_warp = total / (double)(ctx->sm_count * lbk::kMoeGateUpWarps);
@@ -773,14 +808,13 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.prod_floats = pf(kt_g) > pf(kt_s) ? pf(kt_g) : pf(kt_s);
         uint64_t dots = (uint64_t)2 * (g.bmax_iq > g.bmax_k ? g.bmax_iq : g.bmax_k);
         g.chain_floats = (dots * 9 + 64 + 3) & ~(uint64_t)3;
-        g.status = ctx->status;
-        g.tables = ctx->tables();
         if (lbk::moe_gate_up_fixed_smem(L->gate_type, L->sgate_type) +
                 lbk::kMoeGateUpWarps * (g.prod_floats + g.chain_floats) * 4 >
             lbk::kMaxSmem - 8192)  // static top-k buffers
             return fail(LBK_INVALID_PARAMETER, "MoE gate/up shapes exceed shared memory");
         e = lbk::launch_moe_gate_up(L->gate_type, L->sgate_type, g, st);
         if (e != cudaSuccess) return cuda_fail(e, "moe gate/up launch");
+        }
         if (L->tracing) trace_record(L->trace[2], st, cudaEventRecordExternal);
 
         lbk::MoeDownArgs d{};
@@ -878,7 +912,10 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
     cudaError_t e;
     // Single-token decode on the fused kernels: the gate/up kernel finishes the
     // router (partials -> logits -> top-k) in every CTA's prologue.
-    const bool defer = layer->fused && tokens == 1 && router_mode == LBK_ROUTER_TREE;
+    const bool defer = layer->fused && tokens == 1 && router_mode == LBK_ROUTER_TREE &&
+                       (!lbk::moe_gate_up_tma_supported(layer->gate_type, layer->sgate_type, (int)(layer->H / LBK_QK_K)) ||
+                        lbk::moe_gate_up_tma_defer_fits(layer->gate_type, layer->E,
+                                                        lbk::router_partials_floats(layer->H, 1, 1)));
     f.defer = defer ? 1 : 0;
     if (layer->tracing) trace_record(layer->trace[0], st, cudaEventRecordExternal);
     if (router_mode == LBK_ROUTER_TREE) {
@@ -1007,7 +1044,13 @@ int32_t repack_common(lbk_context* ctx, const lbk_matrix* src, void* dst, uint64
     if (int32_t s = check_matrix(src, "source")) return s;
     if (!dot_type(src->type)) return fail(LBK_UNSUPPORTED_TYPE, "only packed types have a planar layout", (uint64_t)src->type);
     if (src->layout != expect_layout) return fail(LBK_INVALID_PARAMETER, "source layout");
-    if (dst_bytes != src->bytes) return fail(LBK_ENCODED_LENGTH_MISMATCH, "destination length", 0, src->bytes, dst_bytes);
+    uint64_t want = 0;
+    if (to_planar) {
+        if (int32_t s = lbk_planar_bytes(src->type, src->input_width, src->output_width, &want)) return s;
+    } else {
+        if (int32_t s = lbk_matrix_bytes(src->type, src->input_width, src->output_width, &want)) return s;
+    }
+    if (dst_bytes != want) return fail(LBK_ENCODED_LENGTH_MISMATCH, "destination length", 0, want, dst_bytes);
     if (ctx == nullptr || dst == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
     if (!aligned(dst, 16)) return fail(LBK_INVALID_PARAMETER, "destination must be 16-byte aligned");
     if (int32_t s = set_device(ctx)) return s;

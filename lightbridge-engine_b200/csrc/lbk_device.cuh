@@ -102,6 +102,69 @@ __device__ __forceinline__ uint4 ldw_u128_a2(const uint8_t* p) {
     return make_uint4(ldw_u32_a2(p), ldw_u32_a2(p + 4), ldw_u32_a2(p + 8), ldw_u32_a2(p + 12));
 }
 
+// Planar rows staged in shared memory (a copy of consecutive planar rows is
+// itself a planar matrix): the HB loaders read it with ordinary shared loads.
+constexpr int kLayoutStage = 2;
+
+template <int LAYOUT>
+__device__ __forceinline__ uint4 wld128(const uint8_t* p) {
+    if constexpr (LAYOUT == kLayoutStage) return *reinterpret_cast<const uint4*>(p);
+    else return ldw_u128(p);
+}
+template <int LAYOUT>
+__device__ __forceinline__ uint32_t wld32(const uint8_t* p) {
+    if constexpr (LAYOUT == kLayoutStage) return *reinterpret_cast<const uint32_t*>(p);
+    else return ldw_u32(p);
+}
+template <int LAYOUT>
+__device__ __forceinline__ uint32_t wld16(const uint8_t* p) {
+    if constexpr (LAYOUT == kLayoutStage) return *reinterpret_cast<const uint16_t*>(p);
+    else return ldw_u16(p);
+}
+
+// ------------------------------------------------ bulk copies and mbarriers
+//
+// Global -> shared bulk copies (cp.async.bulk, no multicast) completing on an
+// mbarrier in the issuing CTA. Source and destination 16-byte aligned, size a
+// multiple of 16.
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with the given parity: false after ~2^22 polls
+// (each poll may itself suspend briefly), so a lost copy ends in an error
+// status instead of a hang.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); i++)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Orders this thread's earlier generic-proxy shared accesses before later
+// async-proxy (bulk copy) writes to the same shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Hint that [p, p+bytes) will be read soon: bring it into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 __device__ __forceinline__ bool h_finite(uint32_t bits16) { return ((bits16 >> 10) & 0x1f) != 0x1f; }
 __device__ __forceinline__ uint32_t w32(const uint4& v, int i) {
@@ -381,6 +444,15 @@ __device__ __forceinline__ uint64_t blk_index(const MatrixRef& m, uint64_t row, 
     return row * (uint64_t)m.nb + (uint64_t)b;
 }
 
+// Row stride of the planar layout: the GGUF row bytes rounded up to 16.
+__host__ __device__ __forceinline__ constexpr uint32_t planar_row_bytes(int block_bytes, int nb) {
+    return ((uint32_t)(nb * block_bytes) + 15u) & ~15u;
+}
+template <int T>
+__device__ __forceinline__ const uint8_t* planar_row(const MatrixRef& m, uint64_t row) {
+    return m.data + row * planar_row_bytes(TypeInfo<T>::kBlockBytes, m.nb);
+}
+
 struct Iq2HB {
     uint4 qs, sg;
     uint32_t qh, sc, d;
@@ -403,15 +475,15 @@ struct Q5HB {
 
 template <int LAYOUT>
 __device__ __forceinline__ void load_hb(Iq2HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
-    uint64_t bi = blk_index(m, row, b);
-    if (LAYOUT == LBK_LAYOUT_PLANAR) {
-        uint64_t nblk = m.rows * (uint64_t)m.nb;
-        const uint8_t* base = m.data;
-        o.qs = ldw_u128(base + bi * 32 + 16 * h);
-        o.sg = ldw_u128(base + nblk * 32 + bi * 32 + 16 * h);
-        o.qh = ldw_u32(base + nblk * 64 + bi * 8 + 4 * h);
-        o.sc = ldw_u32(base + nblk * 72 + bi * 8 + 4 * h);
-        o.d = ldw_u16(base + nblk * 80 + bi * 2);
+    const uint64_t bi = blk_index(m, row, b);  // GGUF
+    if (LAYOUT != LBK_LAYOUT_GGUF) {
+        const uint8_t* base = planar_row<LBK_TYPE_IQ2_S>(m, row);
+        const int nb = m.nb;
+        o.qs = wld128<LAYOUT>(base + b * 32 + 16 * h);
+        o.sg = wld128<LAYOUT>(base + nb * 32 + b * 32 + 16 * h);
+        o.qh = wld32<LAYOUT>(base + nb * 64 + b * 8 + 4 * h);
+        o.sc = wld32<LAYOUT>(base + nb * 72 + b * 8 + 4 * h);
+        o.d = wld16<LAYOUT>(base + nb * 80 + b * 2);
     } else {
         const uint8_t* p = m.data + bi * 82;
         o.d = ldw_u16(p);
@@ -425,15 +497,15 @@ __device__ __forceinline__ void load_hb(Iq2HB& o, const MatrixRef& m, uint64_t r
 template <int LAYOUT>
 __device__ __forceinline__ void load_hb(Iq3HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
     uint64_t bi = blk_index(m, row, b);
-    if (LAYOUT == LBK_LAYOUT_PLANAR) {
-        uint64_t nblk = m.rows * (uint64_t)m.nb;
-        const uint8_t* base = m.data;
-        o.qs0 = ldw_u128(base + bi * 64 + 32 * h);
-        o.qs1 = ldw_u128(base + bi * 64 + 32 * h + 16);
-        o.sg = ldw_u128(base + nblk * 64 + bi * 32 + 16 * h);
-        o.qh = ldw_u32(base + nblk * 96 + bi * 8 + 4 * h);
-        o.sc = ldw_u16(base + nblk * 104 + bi * 4 + 2 * h);
-        o.d = ldw_u16(base + nblk * 108 + bi * 2);
+    if (LAYOUT != LBK_LAYOUT_GGUF) {
+        const uint8_t* base = planar_row<LBK_TYPE_IQ3_S>(m, row);
+        const int nb = m.nb;
+        o.qs0 = wld128<LAYOUT>(base + b * 64 + 32 * h);
+        o.qs1 = wld128<LAYOUT>(base + b * 64 + 32 * h + 16);
+        o.sg = wld128<LAYOUT>(base + nb * 64 + b * 32 + 16 * h);
+        o.qh = wld32<LAYOUT>(base + nb * 96 + b * 8 + 4 * h);
+        o.sc = wld16<LAYOUT>(base + nb * 104 + b * 4 + 2 * h);
+        o.d = wld16<LAYOUT>(base + nb * 108 + b * 2);
     } else {
         const uint8_t* p = m.data + bi * 110;
         o.d = ldw_u16(p);
@@ -443,6 +515,81 @@ __device__ __forceinline__ void load_hb(Iq3HB& o, const MatrixRef& m, uint64_t r
         o.sg = ldw_u128_a2(p + 74 + 16 * h);
         o.sc = ldw_u16(p + 106 + 2 * h);
     }
+}
+
+// Half-block loads from a stage of planar rows in shared memory (same row
+// stride as in global memory): the lane's byte offsets are fixed for a
+// kernel, so they are computed once (stage_off) and every step is a handful
+// of shared loads at constant offsets.
+struct StageOff {
+    uint32_t f0, f1, f2, f3, f4;
+};
+
+template <int T>
+__device__ __forceinline__ StageOff stage_off(int nb, int sub, int b, int h) {
+    const uint32_t r = (uint32_t)sub * planar_row_bytes(TypeInfo<T>::kBlockBytes, nb), n = (uint32_t)nb;
+    StageOff o{};
+    if constexpr (T == LBK_TYPE_IQ2_S) {
+        o.f0 = r + b * 32 + 16 * h;            // qs
+        o.f1 = r + n * 32 + b * 32 + 16 * h;   // signs
+        o.f2 = r + n * 64 + b * 8 + 4 * h;     // qh
+        o.f3 = r + n * 72 + b * 8 + 4 * h;     // scales
+        o.f4 = r + n * 80 + b * 2;             // d
+    } else if constexpr (T == LBK_TYPE_IQ3_S) {
+        o.f0 = r + b * 64 + 32 * h;            // qs (two 16-byte words)
+        o.f1 = r + n * 64 + b * 32 + 16 * h;   // signs
+        o.f2 = r + n * 96 + b * 8 + 4 * h;     // qh
+        o.f3 = r + n * 104 + b * 4 + 2 * h;    // scales
+        o.f4 = r + n * 108 + b * 2;            // d
+    } else if constexpr (T == LBK_TYPE_Q4_K) {
+        o.f0 = r + b * 128 + 64 * h;           // qs (four 16-byte words)
+        o.f1 = r + n * 128 + b * 12;           // scales
+        o.f2 = r + n * 140 + b * 4;            // d, dmin
+    } else {
+        o.f0 = r + b * 128 + 64 * h;           // qs
+        o.f1 = r + n * 128 + b * 32;           // qh
+        o.f2 = r + n * 160 + b * 12;           // scales
+        o.f3 = r + n * 172 + b * 4;            // d, dmin
+    }
+    return o;
+}
+
+__device__ __forceinline__ uint4 sld128(const uint8_t* s, uint32_t off) { return *reinterpret_cast<const uint4*>(s + off); }
+__device__ __forceinline__ uint32_t sld32(const uint8_t* s, uint32_t off) { return *reinterpret_cast<const uint32_t*>(s + off); }
+__device__ __forceinline__ uint32_t sld16(const uint8_t* s, uint32_t off) { return *reinterpret_cast<const uint16_t*>(s + off); }
+
+__device__ __forceinline__ void load_stage(Iq2HB& o, const uint8_t* s, const StageOff& f) {
+    o.qs = sld128(s, f.f0);
+    o.sg = sld128(s, f.f1);
+    o.qh = sld32(s, f.f2);
+    o.sc = sld32(s, f.f3);
+    o.d = sld16(s, f.f4);
+}
+__device__ __forceinline__ void load_stage(Iq3HB& o, const uint8_t* s, const StageOff& f) {
+    o.qs0 = sld128(s, f.f0);
+    o.qs1 = sld128(s, f.f0 + 16);
+    o.sg = sld128(s, f.f1);
+    o.qh = sld32(s, f.f2);
+    o.sc = sld16(s, f.f3);
+    o.d = sld16(s, f.f4);
+}
+__device__ __forceinline__ void load_stage(Q4HB& o, const uint8_t* s, const StageOff& f) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) o.qs[i] = sld128(s, f.f0 + 16 * i);
+    o.sc[0] = sld32(s, f.f1);
+    o.sc[1] = sld32(s, f.f1 + 4);
+    o.sc[2] = sld32(s, f.f1 + 8);
+    o.dm = sld32(s, f.f2);
+}
+__device__ __forceinline__ void load_stage(Q5HB& o, const uint8_t* s, const StageOff& f) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) o.qs[i] = sld128(s, f.f0 + 16 * i);
+    o.qh[0] = sld128(s, f.f1);
+    o.qh[1] = sld128(s, f.f1 + 16);
+    o.sc[0] = sld32(s, f.f2);
+    o.sc[1] = sld32(s, f.f2 + 4);
+    o.sc[2] = sld32(s, f.f2 + 8);
+    o.dm = sld32(s, f.f3);
 }
 
 // GGUF qs group (8 words, natural order) -> lane-major order.
@@ -457,16 +604,16 @@ __device__ __forceinline__ void lane_major8(uint32_t* w) {
 template <int LAYOUT>
 __device__ __forceinline__ void load_hb(Q4HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
     uint64_t bi = blk_index(m, row, b);
-    if (LAYOUT == LBK_LAYOUT_PLANAR) {
-        uint64_t nblk = m.rows * (uint64_t)m.nb;
-        const uint8_t* base = m.data;
+    if (LAYOUT != LBK_LAYOUT_GGUF) {
+        const uint8_t* base = planar_row<LBK_TYPE_Q4_K>(m, row);
+        const int nb = m.nb;
 #pragma unroll
-        for (int i = 0; i < 4; i++) o.qs[i] = ldw_u128(base + bi * 128 + 64 * h + 16 * i);
-        const uint8_t* s = base + nblk * 128 + bi * 12;
-        o.sc[0] = ldw_u32(s);
-        o.sc[1] = ldw_u32(s + 4);
-        o.sc[2] = ldw_u32(s + 8);
-        o.dm = ldw_u32(base + nblk * 140 + bi * 4);
+        for (int i = 0; i < 4; i++) o.qs[i] = wld128<LAYOUT>(base + b * 128 + 64 * h + 16 * i);
+        const uint8_t* s = base + nb * 128 + b * 12;
+        o.sc[0] = wld32<LAYOUT>(s);
+        o.sc[1] = wld32<LAYOUT>(s + 4);
+        o.sc[2] = wld32<LAYOUT>(s + 8);
+        o.dm = wld32<LAYOUT>(base + nb * 140 + b * 4);
     } else {
         const uint8_t* p = m.data + bi * 144;
         o.dm = ldw_u32(p);
@@ -488,18 +635,18 @@ __device__ __forceinline__ void load_hb(Q4HB& o, const MatrixRef& m, uint64_t ro
 template <int LAYOUT>
 __device__ __forceinline__ void load_hb(Q5HB& o, const MatrixRef& m, uint64_t row, int b, int h) {
     uint64_t bi = blk_index(m, row, b);
-    if (LAYOUT == LBK_LAYOUT_PLANAR) {
-        uint64_t nblk = m.rows * (uint64_t)m.nb;
-        const uint8_t* base = m.data;
+    if (LAYOUT != LBK_LAYOUT_GGUF) {
+        const uint8_t* base = planar_row<LBK_TYPE_Q5_K>(m, row);
+        const int nb = m.nb;
 #pragma unroll
-        for (int i = 0; i < 4; i++) o.qs[i] = ldw_u128(base + bi * 128 + 64 * h + 16 * i);
-        o.qh[0] = ldw_u128(base + nblk * 128 + bi * 32);
-        o.qh[1] = ldw_u128(base + nblk * 128 + bi * 32 + 16);
-        const uint8_t* s = base + nblk * 160 + bi * 12;
-        o.sc[0] = ldw_u32(s);
-        o.sc[1] = ldw_u32(s + 4);
-        o.sc[2] = ldw_u32(s + 8);
-        o.dm = ldw_u32(base + nblk * 172 + bi * 4);
+        for (int i = 0; i < 4; i++) o.qs[i] = wld128<LAYOUT>(base + b * 128 + 64 * h + 16 * i);
+        o.qh[0] = wld128<LAYOUT>(base + nb * 128 + b * 32);
+        o.qh[1] = wld128<LAYOUT>(base + nb * 128 + b * 32 + 16);
+        const uint8_t* s = base + nb * 160 + b * 12;
+        o.sc[0] = wld32<LAYOUT>(s);
+        o.sc[1] = wld32<LAYOUT>(s + 4);
+        o.sc[2] = wld32<LAYOUT>(s + 8);
+        o.dm = wld32<LAYOUT>(base + nb * 172 + b * 4);
     } else {
         const uint8_t* p = m.data + bi * 176;
         o.dm = ldw_u32(p);

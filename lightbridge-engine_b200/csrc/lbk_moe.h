@@ -7,6 +7,7 @@ namespace lbk {
 
 constexpr int kMoeGateUpWarps = 8;   // warps per gate/up CTA (one CTA per SM)
 constexpr int kMoeDownMaxSlots = 9;  // routed top-k + shared, one warp each
+constexpr int kMoeGateUpTmaWarps = 16;  // warps per bulk-copy-staged gate/up CTA
 
 struct MoeGateUpArgs {
     uint64_t hidden, ffn;
@@ -36,6 +37,8 @@ struct MoeGateUpArgs {
     const float* bias;
     float weight_scale;
     lbk_routed* routed_store;        // CTA 0 writes the routing here
+    // bulk-copy-staged kernel: CTAs [0, routed_ctas) stream routed slots, the rest the shared expert
+    uint32_t routed_ctas;
     DeviceStatus* status;
     Tables tables;
 };
@@ -64,6 +67,12 @@ bool moe_fused_supported(int gate_type, int shared_gate_type, int down_type, int
 size_t moe_gate_up_fixed_smem(int gate_type, int shared_gate_type);
 size_t moe_down_fixed_smem(int down_type, int shared_down_type);
 cudaError_t launch_moe_gate_up(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, cudaStream_t stream);
+// Bulk-copy-staged gate/up over `ctas` CTAs (planar, nb_h in {8, 16}).
+bool moe_gate_up_tma_supported(int gate_type, int shared_gate_type, int nb_h);
+// Whether its routed CTAs can finish the router (partials + logits in shared memory).
+bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks);
+cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
+                                   cudaStream_t stream);
 cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream);
 
 }  // namespace lbk

@@ -66,14 +66,17 @@ constexpr bool is_iq() {
 }
 
 // Loads a thread's half block of a Q8_K row held in global memory in the
-// internal image layout (store_q8i).
+// internal image layout (store_q8i). The image was written by an earlier
+// launch and every warp of the grid reads it: read-only loads through L1, so
+// each SM fetches a line from L2 once instead of once per warp (thousands of
+// warps on the same few lines would stall every other L2 request behind them).
 template <bool kTr>
 __device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, int b, int h, bool bsums) {
     const uint8_t* blk = q8row + (size_t)b * kQ8IBytes;
     const uint4* qw = reinterpret_cast<const uint4*>(blk + 128 * h);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        uint4 v = __ldcg(qw + i);
+        uint4 v = __ldg(qw + i);
         a.w[4 * i + 0] = v.x;
         a.w[4 * i + 1] = v.y;
         a.w[4 * i + 2] = v.z;
@@ -89,8 +92,8 @@ __device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, 
             transpose4(n[1], n[3], n[5], n[7], a.w[8 * j + 4], a.w[8 * j + 5], a.w[8 * j + 6], a.w[8 * j + 7]);
         }
     }
-    a.d = __uint_as_float(__ldcg(reinterpret_cast<const unsigned int*>(blk + 288)));
-    uint4 bs = bsums ? __ldcg(reinterpret_cast<const uint4*>(blk + 256 + 16 * h)) : make_uint4(0, 0, 0, 0);
+    a.d = __uint_as_float(__ldg(reinterpret_cast<const unsigned int*>(blk + 288)));
+    uint4 bs = bsums ? __ldg(reinterpret_cast<const uint4*>(blk + 256 + 16 * h)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int i = 0; i < 8; i++) a.bsum[i] = (int32_t)(int16_t)((w32(bs, i >> 1) >> (16 * (i & 1))) & 0xffffu);
 }
@@ -402,6 +405,240 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
     }
 }
 
+// ------------------------------------------------- gate / up, bulk-copy staged
+//
+// For planar weights with nb_h a multiple of 8 and at most 16: every planar
+// field of a row is then a multiple of 16 bytes, and one warp step of
+// 32/tpr rows covers exactly 32 half blocks. CTAs [0, routed_ctas) take the
+// routed slots and hold the routed type's lookup tables; the other CTAs take
+// the shared expert and hold none. Each warp owns one stage in shared memory:
+// lane 0 fills it with bulk copies (one per planar field of gate and of up)
+// completing on the warp's mbarrier; the lanes copy their half blocks into
+// registers, lane 0 refills the stage with the next step's rows, and this
+// step's decode overlaps that transfer.
+
+constexpr int kGUTWarps = kMoeGateUpTmaWarps;
+constexpr int kGUTThreads = kGUTWarps * 32;
+
+// Shared-memory plan of one CTA role streaming type T.
+template <int T>
+struct GUTRole {
+    static constexpr bool kIq = is_iq<T>();
+    static constexpr int kBB = TypeInfo<T>::kBlockBytes;
+    static constexpr int kMat = 16 * kBB;                 // 32 half blocks of one matrix (16-byte multiple)
+    static constexpr int kStage = 2 * kMat;               // gate + up
+    static constexpr int kBmax = kIq ? 8 : 4;             // rows per tail batch
+    static constexpr int kTail = TypeInfo<T>::kTail;
+    static constexpr int kProd = kBmax * 2 * 16 * kTail;  // floats per warp
+    static constexpr int kChain = kIq ? 0 : kBmax * 2 * 9;
+    static constexpr int kRes = 64;
+    static constexpr int kTab = table_bytes<T>();
+    static constexpr int kSign = kIq ? kSignBytes : 0;
+    static constexpr int kRingOff = kTab + kSign;
+    static constexpr int kProdOff = kRingOff + kGUTWarps * kStage;
+    static constexpr int kChainOff = kProdOff + kGUTWarps * kProd * 4;
+    static constexpr int kResOff = kChainOff + kGUTWarps * kChain * 4;
+    static constexpr int kBytes = kResOff + kGUTWarps * kRes * 4;
+};
+
+// Lane 0: rows [ra, ra+nr) of gate and of up, one contiguous planar copy
+// each, into the stage ([gate: R rows][up: R rows], rows at stride rs).
+__device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const uint8_t* gmat, const uint8_t* umat,
+                                          uint32_t rs, int R, uint32_t ra, uint32_t nr) {
+    mbar_expect_tx(bar, 2u * nr * rs);
+    bulk_g2s(stage, gmat + (uint64_t)ra * rs, nr * rs, bar);
+    bulk_g2s(stage + (uint32_t)R * rs, umat + (uint64_t)ra * rs, nr * rs, bar);
+}
+
+// One role's items: (token, slot, chunk of rows) spread over the role's warps.
+template <int T, bool kRouted>
+__device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar, const lbk_routed* s_routed,
+                                        uint32_t role_warp, uint32_t role_warps) {
+    using RL = GUTRole<T>;
+    using HB = typename HBOf<T>::type;
+    constexpr bool kIq = RL::kIq;
+    constexpr int kTail = RL::kTail;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = a.nb_h, tpr = a.tpr_h, R = 32 / tpr;
+    const int sub = lane / tpr, hb = lane % tpr, b = hb >> 1, h = hb & 1;
+    const bool lane_on = hb < 2 * nb;
+    const uint32_t rs = planar_row_bytes(RL::kBB, nb);  // R * rs == kMat for nb in {8, 16}
+    uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
+    const uint8_t* ustage = stage + R * rs;
+    const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
+    float* prod = reinterpret_cast<float*>(smem + RL::kProdOff) + warp * RL::kProd;
+    float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
+    float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
+    const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
+    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
+    const StageOff so = stage_off<T>(nb, sub, b, h);
+    const int pstride = 2 * nb * kTail;  // prod[(ri*2 + m)*nb + b][kTail]
+
+    const uint32_t ffn = (uint32_t)a.ffn;
+    const uint32_t chunk = (uint32_t)(kRouted ? a.chunk_r : a.chunk_s);
+    const uint32_t chunks = (uint32_t)(kRouted ? a.chunks_r : a.chunks_s);
+    const uint32_t slots = kRouted ? (uint32_t)a.k : 1u;
+    const uint32_t items = (uint32_t)a.tokens * slots * chunks;
+    uint32_t phase = 0;
+    bool live = true;  // false after a wait ran out: no further copies are issued
+    for (uint32_t it = role_warp; it < items; it += role_warps) {
+        const uint32_t t = it / (slots * chunks);
+        const uint32_t rem = it - t * (slots * chunks);
+        const uint32_t j = rem / chunks, c = rem - j * chunks;
+        const uint32_t slot = kRouted ? j : (uint32_t)a.k;
+        const uint8_t* gmat = a.sgate;
+        const uint8_t* umat = a.sup;
+        if constexpr (kRouted) {
+            uint32_t e = a.defer_topk ? s_routed[j].expert_id : a.routed[(uint64_t)t * a.k + j].expert_id;
+            if (e >= a.experts) {  // reported; compute on expert 0 so the arrival counts stay balanced
+                if (lane == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
+                e = 0;
+            }
+            gmat = a.gate[e];
+            umat = a.up[e];
+        }
+        const uint32_t r0 = c * chunk, r1 = r0 + chunk < ffn ? r0 + chunk : ffn;
+        if (r0 >= r1) continue;
+        if (lane == 0 && live) gut_issue(stage_s, bar, gmat, umat, rs, R, r0, r1 - r0 < (uint32_t)R ? r1 - r0 : R);
+
+        ActHB act;
+        uint32_t nact[32];
+        if (lane_on) {
+            load_act_global<!kIq>(act, a.q8x + (uint64_t)t * nb * kQ8IBytes, b, h, !kIq);
+            if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+                for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+            }
+        }
+        float* hrow = a.h + ((uint64_t)t * (a.k + 1) + slot) * a.ffn;
+        uint32_t rb = r0;
+        for (uint32_t ra = r0; ra < r1; ra += R) {
+            const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
+            if (live && !mbar_wait(bar, phase)) {
+                live = false;
+                if (lane == 0) report(a.status, LBK_TIMEOUT, it, 0);
+            }
+            live = __all_sync(0xffffffffu, live);
+            phase ^= 1u;
+            const bool mine = lane_on && (uint32_t)sub < nr;
+            HB gw, uw;
+            if (mine) {
+                load_stage(gw, stage, so);
+                load_stage(uw, ustage, so);
+            }
+            __syncwarp();
+            const uint32_t rn = ra + R;
+            if (lane == 0 && live && rn < r1) {
+                fence_proxy_async_smem();
+                gut_issue(stage_s, bar, gmat, umat, rs, R, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
+            }
+            IqPart gi{0, 0}, ui{0, 0};
+            KPart gk, uk;
+#pragma unroll
+            for (int l = 0; l < 8; l++) gk.lane[l] = uk.lane[l] = 0;
+            gk.min_sum = uk.min_sum = 0;
+            gk.dm = uk.dm = 0;
+            if (mine) {
+                HBDot<T>::run(gw, act, nact, t0, t1, h, gi, gk);
+                HBDot<T>::run(uw, act, nact, t0, t1, h, ui, uk);
+            }
+            const uint32_t row = ra + sub;
+            float* pg = prod + (int)(row - rb) * pstride;
+            write_products<T>(pg, b, h, mine, gi, gk, act.d, a.status, (uint64_t)row * nb + b);
+            write_products<T>(pg + nb * kTail, b, h, mine, ui, uk, act.d, a.status, (uint64_t)row * nb + b);
+            if (rn - rb >= (uint32_t)RL::kBmax || rn >= r1) {
+                const int nrows = (int)((rn < r1 ? rn : r1) - rb);
+                __syncwarp();
+                warp_tails<T>(prod, nrows * 2, nb, chains, res);
+                for (int q = lane; q < nrows; q += 32) {
+                    float g = res[q * 2], u = res[q * 2 + 1];
+                    float v = swiglu_ref(g, u);
+                    if (!isfinite(v))
+                        report(a.status, LBK_NON_FINITE_VALUE, ((uint64_t)t * (a.k + 1) + slot) * a.ffn + rb + q,
+                               __float_as_uint(v));
+                    hrow[rb + q] = v;
+                }
+                __syncwarp();
+                rb = rn;
+            }
+        }
+        arrive_and_quantize(a, t, slot, r0, r1);
+    }
+}
+
+template <int TG, int TS>
+__global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGateUpArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[kGUTWarps];
+    __shared__ lbk_routed s_routed[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[warp]);
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_init_fence();
+    }
+    __syncwarp();
+    if (blockIdx.x < a.routed_ctas) {
+        using RL = GUTRole<TG>;
+        // Prologue by bulk copies: the lookup tables, and (single-token decode)
+        // the router's chunk partials, land in shared memory while warp 0
+        // finishes the router: logits = partials summed in chunk order, then
+        // top-k. CTA 0 publishes the routing for the down kernel.
+        __shared__ __align__(8) uint64_t s_pro[2];  // [0] partials, [1] tables
+        const uint32_t bar_p = (uint32_t)__cvta_generic_to_shared(&s_pro[0]);
+        const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_pro[1]);
+        float* s_part = reinterpret_cast<float*>(smem + RL::kProdOff);  // free until the rows start
+        const uint64_t pfloats = a.experts * a.chunks;
+        const bool bulk_p = a.defer_topk && pfloats % 4 == 0;
+        if (threadIdx.x == 0) {
+            mbar_init(bar_p, 1);
+            mbar_init(bar_t, 1);
+            mbar_init_fence();
+            if constexpr (RL::kTab != 0) {
+                const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
+                mbar_expect_tx(bar_t, RL::kTab + RL::kSign);
+                bulk_g2s(base, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
+                         RL::kTab, bar_t);
+                bulk_g2s(base + RL::kTab, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
+                         RL::kSign, bar_t);
+            }
+            if (bulk_p) {
+                mbar_expect_tx(bar_p, (uint32_t)(pfloats * 4));
+                bulk_g2s((uint32_t)__cvta_generic_to_shared(s_part), a.partials, (uint32_t)(pfloats * 4), bar_p);
+            }
+        }
+        __syncthreads();
+        if (a.defer_topk && warp == 0) {
+            if (bulk_p) {
+                if (!mbar_wait(bar_p, 0) && lane == 0) report(a.status, LBK_TIMEOUT, 0, 0);
+            } else {
+                for (uint64_t i = lane; i < pfloats; i += 32) s_part[i] = __ldcg(a.partials + i);
+                __syncwarp();
+            }
+            float* s_logits = s_part + ((pfloats + 3) & ~(uint64_t)3);
+            for (uint64_t e = lane; e < a.experts; e += 32) {
+                const float* pp = s_part + e * a.chunks;
+                float sum = 0.0f;
+                for (uint64_t c = 0; c < a.chunks; c++) sum = __fadd_rn(sum, pp[c]);
+                s_logits[e] = sum;
+            }
+            __syncwarp();
+            topk_warp(s_logits, a.bias, (int)a.experts, (int)a.k, a.weight_scale, s_routed,
+                      blockIdx.x == 0 ? a.status : nullptr, 0);
+            __syncwarp();
+            if (blockIdx.x == 0 && lane < (int)a.k) a.routed_store[lane] = s_routed[lane];
+        }
+        __syncthreads();
+        if constexpr (RL::kTab != 0) {
+            if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 1, 0);
+        }
+        gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps);
+    } else {
+        gut_run<TS, false>(a, smem, bar, nullptr, (blockIdx.x - a.routed_ctas) * kGUTWarps + warp,
+                           (gridDim.x - a.routed_ctas) * kGUTWarps);
+    }
+}
+
 // -------------------------------------------------------------------- down
 
 template <int TD, int TSD>
@@ -543,6 +780,18 @@ cudaError_t launch_gu(const MoeGateUpArgs& a, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+template <int TG, int TS>
+cudaError_t launch_gut(const MoeGateUpArgs& a, unsigned ctas, cudaStream_t stream) {
+    constexpr int kA = GUTRole<TG>::kBytes, kB = GUTRole<TS>::kBytes;
+    constexpr size_t smem = kA > kB ? kA : kB;
+    static_assert(smem + 32 * sizeof(lbk_routed) + kGUTWarps * 8 <= (size_t)kMaxSmem, "gate/up stage plan");
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_tma_kernel<TG, TS>));
+    if (e != cudaSuccess) return e;
+    if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
+    moe_gate_up_tma_kernel<TG, TS><<<ctas, kGUTThreads, smem, stream>>>(a);
+    return cudaGetLastError();
+}
+
 template <int TD, int TSD>
 cudaError_t launch_down(const MoeDownArgs& a, cudaStream_t stream) {
     using S = DownSmem<TD, TSD>;
@@ -598,6 +847,24 @@ cudaError_t launch_moe_gate_up(int gate_type, int shared_gate_type, const MoeGat
     (void)shared_gate_type;
     if (gate_type == LBK_TYPE_IQ2_S) return launch_gu<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, stream);
     return launch_gu<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, stream);
+}
+
+bool moe_gate_up_tma_supported(int gate_type, int shared_gate_type, int nb_h) {
+    return (gate_type == LBK_TYPE_IQ2_S || gate_type == LBK_TYPE_Q4_K) && shared_gate_type == LBK_TYPE_Q4_K &&
+           (nb_h == 8 || nb_h == 16);
+}
+
+bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks) {
+    const uint64_t floats = gate_type == LBK_TYPE_IQ2_S ? (uint64_t)kGUTWarps * GUTRole<LBK_TYPE_IQ2_S>::kProd
+                                                        : (uint64_t)kGUTWarps * GUTRole<LBK_TYPE_Q4_K>::kProd;
+    return ((experts * chunks + 3) & ~(uint64_t)3) + experts <= floats;
+}
+
+cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
+                                   cudaStream_t stream) {
+    (void)shared_gate_type;
+    if (gate_type == LBK_TYPE_IQ2_S) return launch_gut<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
+    return launch_gut<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);
 }
 
 cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream) {

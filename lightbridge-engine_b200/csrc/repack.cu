@@ -60,50 +60,65 @@ __host__ __device__ inline int lane_major_pos(int j) {
     return 4 * k + i;
 }
 
+// One thread per block: its fields move between the GGUF block and the
+// block's slots in its row's planes; the thread of block 0 also zeroes the
+// row's pad bytes.
 __global__ void repack_kernel(RepackArgs a, int block_bytes) {
     Field f[5];
     int nf = fields_of(a.type, f);
     const uint64_t nblk = a.rows * (uint64_t)a.nb;
+    const uint64_t rs = planar_row_bytes(block_bytes, a.nb);
     for (uint64_t bi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; bi < nblk; bi += (uint64_t)gridDim.x * blockDim.x) {
-        uint64_t plane = 0;
+        const uint64_t row = bi / (uint64_t)a.nb, b = bi % (uint64_t)a.nb;
+        uint64_t plane = row * rs;  // start of field plane k inside the planar row
         for (int k = 0; k < nf; k++) {
             const int fb = f[k].bytes;
             if (f[k].lane_major == 2) {
                 for (int j = 0; j < fb; j += 4) {
                     uint64_t g = bi * block_bytes + f[k].src_off + j;
-                    uint64_t p = plane + bi * fb + j;
+                    uint64_t p = plane + b * fb + j;
                     const uint8_t* s = a.to_planar ? a.src + g : a.src + p;
                     uint8_t* d = a.to_planar ? a.dst + p : a.dst + g;
                     uint32_t w = (uint32_t)s[0] | ((uint32_t)s[1] << 8) | ((uint32_t)s[2] << 16) | ((uint32_t)s[3] << 24);
                     w = qh_transpose(w);
                     for (int i = 0; i < 4; i++) d[i] = (uint8_t)(w >> (8 * i));
                 }
-                plane += nblk * (uint64_t)fb;
+                plane += (uint64_t)a.nb * fb;
                 continue;
             }
             for (int j = 0; j < fb; j++) {
                 int pj = j;
                 if (f[k].lane_major) pj = (j & ~31) + lane_major_pos(j & 31);
                 uint64_t g = bi * block_bytes + f[k].src_off + j;  // GGUF byte
-                uint64_t p = plane + bi * fb + pj;                   // planar byte
+                uint64_t p = plane + b * fb + pj;                    // planar byte
                 if (a.to_planar)
                     a.dst[p] = a.src[g];
                 else
                     a.dst[g] = a.src[p];
             }
-            plane += nblk * (uint64_t)fb;
+            plane += (uint64_t)a.nb * fb;
         }
+        if (a.to_planar && b == 0)
+            for (uint64_t p = row * rs + (uint64_t)a.nb * block_bytes; p < (row + 1) * rs; p++) a.dst[p] = 0;
     }
+}
+
+// Bytes of block bi's binary16 d (followed by dmin for the K types).
+__device__ __forceinline__ const uint8_t* scale_ptr(int type, int layout, const uint8_t* data, int nb, uint64_t bi) {
+    const bool two = type == LBK_TYPE_Q4_K || type == LBK_TYPE_Q5_K;
+    const int bb = type == LBK_TYPE_IQ2_S ? 82 : type == LBK_TYPE_IQ3_S ? 110 : type == LBK_TYPE_Q4_K ? 144 : 176;
+    const uint64_t dplane = type == LBK_TYPE_IQ2_S ? 80 : type == LBK_TYPE_IQ3_S ? 108 : type == LBK_TYPE_Q4_K ? 140 : 172;
+    if (layout != LBK_LAYOUT_PLANAR) return data + bi * bb;
+    const uint64_t row = bi / (uint64_t)nb, b = bi % (uint64_t)nb;
+    return data + row * planar_row_bytes(bb, nb) + (uint64_t)nb * dplane + b * (two ? 4 : 2);
 }
 
 __global__ void scan_scales_kernel(int type, int layout, const uint8_t* data, uint64_t rows, int nb,
                                    unsigned long long* first_bad) {
     const uint64_t nblk = rows * (uint64_t)nb;
     const bool two = type == LBK_TYPE_Q4_K || type == LBK_TYPE_Q5_K;
-    int bb = type == LBK_TYPE_IQ2_S ? 82 : type == LBK_TYPE_IQ3_S ? 110 : type == LBK_TYPE_Q4_K ? 144 : 176;
-    uint64_t dplane = type == LBK_TYPE_IQ2_S ? 80 : type == LBK_TYPE_IQ3_S ? 108 : type == LBK_TYPE_Q4_K ? 140 : 172;
     for (uint64_t bi = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; bi < nblk; bi += (uint64_t)gridDim.x * blockDim.x) {
-        const uint8_t* p = layout == LBK_LAYOUT_PLANAR ? data + nblk * dplane + bi * (two ? 4 : 2) : data + bi * bb;
+        const uint8_t* p = scale_ptr(type, layout, data, nb, bi);
         uint32_t d = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
         bool bad = !h_finite(d);
         if (two) bad |= !h_finite((uint32_t)p[2] | ((uint32_t)p[3] << 8));
@@ -115,11 +130,8 @@ __global__ void report_scale_kernel(int type, int layout, const uint8_t* data, u
                                     const unsigned long long* first_bad, DeviceStatus* st) {
     unsigned long long bi = *first_bad;
     if (bi == ~0ull) return;
-    const uint64_t nblk = rows * (uint64_t)nb;
-    const bool two = type == LBK_TYPE_Q4_K || type == LBK_TYPE_Q5_K;
-    int bb = type == LBK_TYPE_IQ2_S ? 82 : type == LBK_TYPE_IQ3_S ? 110 : type == LBK_TYPE_Q4_K ? 144 : 176;
-    uint64_t dplane = type == LBK_TYPE_IQ2_S ? 80 : type == LBK_TYPE_IQ3_S ? 108 : type == LBK_TYPE_Q4_K ? 140 : 172;
-    const uint8_t* p = layout == LBK_LAYOUT_PLANAR ? data + nblk * dplane + bi * (two ? 4 : 2) : data + bi * bb;
+    (void)rows;
+    const uint8_t* p = scale_ptr(type, layout, data, nb, bi);
     uint32_t d = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
     uint32_t bits = h_finite(d) ? ((uint32_t)p[2] | ((uint32_t)p[3] << 8)) : d;
     report(st, LBK_NON_FINITE_SCALE, bi, bits);

@@ -107,6 +107,7 @@ def _load() -> ctypes.CDLL:
         "lbk_last_error_detail": ([ctypes.POINTER(ErrorDetail)], None),
         "lbk_required_q8k_bytes": ([U64, ctypes.POINTER(U64)], I32),
         "lbk_matrix_bytes": ([I32, U64, U64, ctypes.POINTER(U64)], I32),
+        "lbk_planar_bytes": ([I32, U64, U64, ctypes.POINTER(U64)], I32),
         "lbk_quantize_q8k": ([P, P, U64, P, U64, P], I32),
         "lbk_vec_dot_q8k": ([P, PM, P, U64, P, P, P], I32),
         "lbk_gemv": ([P, PM, P, P, P, U64, P], I32),
@@ -138,7 +139,7 @@ def _load() -> ctypes.CDLL:
 lib = _load()
 EXPORTED = (
     "lbk_abi_version lbk_backend_name lbk_context_create lbk_context_destroy lbk_context_sync_status "
-    "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
+    "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_planar_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
     "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused "
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "

@@ -101,24 +101,41 @@ def _permute(field: np.ndarray, how, inverse: bool) -> np.ndarray:
     return field
 
 
-def planar_np(ty: int, gguf: np.ndarray) -> np.ndarray:
-    """GGUF bytes -> planar bytes (the layout of lbk_repack)."""
-    bb = BLOCK_BYTES[ty]
-    blocks = gguf.reshape(-1, bb)
-    planes = []
-    for off, nbytes, lm in _FIELDS[ty]:
-        f = blocks[:, off : off + nbytes]
-        planes.append(_permute(f, lm, False).reshape(-1))
-    return np.concatenate(planes)
+def planar_row_bytes(ty: int, in_w: int) -> int:
+    """Row stride of the planar layout: GGUF row bytes rounded up to 16."""
+    return (in_w // 256 * BLOCK_BYTES[ty] + 15) // 16 * 16
 
 
-def gguf_from_planar_np(ty: int, planar: np.ndarray) -> np.ndarray:
+def planar_bytes(ty: int, in_w: int, out_w: int) -> int:
+    return planar_row_bytes(ty, in_w) * out_w
+
+
+def planar_np(ty: int, gguf: np.ndarray, in_w: int) -> np.ndarray:
+    """GGUF bytes -> planar bytes (the layout of lbk_repack): per row, one
+    plane per field over the row's blocks, rows padded with zeros to 16 bytes."""
     bb = BLOCK_BYTES[ty]
-    nblk = planar.size // bb
-    out = np.zeros((nblk, bb), dtype=np.uint8)
+    nb = in_w // 256
+    blocks = gguf.reshape(-1, nb, bb)
+    rows = blocks.shape[0]
+    out = np.zeros((rows, planar_row_bytes(ty, in_w)), dtype=np.uint8)
     pos = 0
     for off, nbytes, lm in _FIELDS[ty]:
-        f = planar[pos : pos + nblk * nbytes].reshape(nblk, nbytes)
-        out[:, off : off + nbytes] = _permute(f, lm, True)
-        pos += nblk * nbytes
+        f = blocks[:, :, off : off + nbytes].reshape(rows * nb, nbytes)
+        out[:, pos : pos + nb * nbytes] = _permute(f, lm, False).reshape(rows, nb * nbytes)
+        pos += nb * nbytes
+    return out.reshape(-1)
+
+
+def gguf_from_planar_np(ty: int, planar: np.ndarray, in_w: int) -> np.ndarray:
+    bb = BLOCK_BYTES[ty]
+    nb = in_w // 256
+    rs = planar_row_bytes(ty, in_w)
+    rows = planar.size // rs
+    p = planar.reshape(rows, rs)
+    out = np.zeros((rows, nb, bb), dtype=np.uint8)
+    pos = 0
+    for off, nbytes, lm in _FIELDS[ty]:
+        f = np.ascontiguousarray(p[:, pos : pos + nb * nbytes]).reshape(rows * nb, nbytes)
+        out[:, :, off : off + nbytes] = _permute(f, lm, True).reshape(rows, nb, nbytes)
+        pos += nb * nbytes
     return out.reshape(-1)

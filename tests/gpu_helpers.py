@@ -41,8 +41,8 @@ def rel_err(got: np.ndarray, want: np.ndarray) -> float:
     return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / scale
 
 
-def planar_dev(ty: int, gguf: np.ndarray) -> torch.Tensor:
-    return dev(synth.planar_np(ty, gguf))
+def planar_dev(ty: int, gguf: np.ndarray, in_w: int) -> torch.Tensor:
+    return dev(synth.planar_np(ty, gguf, in_w))
 
 
 def matrix(ty, in_w, out_w, t: torch.Tensor, layout=lbk.LAYOUT_GGUF) -> lbk.Matrix:
@@ -83,17 +83,17 @@ def upload_layer(router, experts, shared, layout, top_k, weight_scale=2.826, bia
     E = len(experts)
     keep = []
 
-    def up(ty, b):
-        t = planar_dev(ty, b) if layout == lbk.LAYOUT_PLANAR else dev(b)
+    def up(ty, b, in_w):
+        t = planar_dev(ty, b, in_w) if layout == lbk.LAYOUT_PLANAR else dev(b)
         keep.append(t)
         return t
 
     def ex(e):
         gty, gb, uty, ub, dty, db, h, f = e
         return lbk.Expert(
-            matrix(gty, h, f, up(gty, gb), layout),
-            matrix(uty, h, f, up(uty, ub), layout),
-            matrix(dty, f, h, up(dty, db), layout),
+            matrix(gty, h, f, up(gty, gb, h), layout),
+            matrix(uty, h, f, up(uty, ub, h), layout),
+            matrix(dty, f, h, up(dty, db, f), layout),
         )
 
     dex = [ex(e) for e in experts]

@@ -56,6 +56,13 @@ def test_required_q8k_bytes_and_matrix_bytes():
     assert L.lbk_matrix_bytes(0, 7, 2, ctypes.byref(n)) == 0 and n.value == 56
     assert L.lbk_matrix_bytes(8, 256, 1, ctypes.byref(n)) == 1  # Q8_0: unsupported
     assert L.lbk_matrix_bytes(12, 255, 1, ctypes.byref(n)) == 10
+    # planar rows are padded to 16 bytes: IQ3_S 6 blocks = 660 -> 672, IQ2_S 16 blocks = 1312
+    assert L.lbk_planar_bytes(21, 1536, 5, ctypes.byref(n)) == 0 and n.value == 672 * 5
+    assert L.lbk_planar_bytes(22, 4096, 3, ctypes.byref(n)) == 0 and n.value == 1312 * 3
+    assert L.lbk_planar_bytes(0, 256, 1, ctypes.byref(n)) == 1  # F32 has no planar layout
+    for ty in (12, 13, 21, 22):
+        for k in (256, 768, 1536, 4096):
+            assert L.lbk_planar_bytes(ty, k, 7, ctypes.byref(n)) == 0 and n.value == synth.planar_bytes(ty, k, 7)
 
 
 def test_quantize_validation_order():
@@ -131,14 +138,19 @@ def test_expert_validation():
 
 
 @pytest.mark.parametrize("ty", [synth.TYPE_IQ2_S, synth.TYPE_IQ3_S, synth.TYPE_Q4_K, synth.TYPE_Q5_K])
-def test_planar_layout_round_trips(ty):
-    rng = np.random.default_rng(ty)
-    w = synth.packed_np(rng, ty, 768, 5)
-    p = synth.planar_np(ty, w)
-    assert p.size == w.size
-    if ty in (synth.TYPE_Q4_K, synth.TYPE_Q5_K):  # a pure byte permutation
-        assert np.array_equal(np.sort(p), np.sort(w))
-    assert np.array_equal(synth.gguf_from_planar_np(ty, p), w)
+@pytest.mark.parametrize("k", [256, 768, 1536, 4096])
+def test_planar_layout_round_trips(ty, k):
+    rng = np.random.default_rng(ty + k)
+    rows = 5
+    w = synth.packed_np(rng, ty, k, rows)
+    p = synth.planar_np(ty, w, k)
+    rs = synth.planar_row_bytes(ty, k)
+    assert rs % 16 == 0 and p.size == rs * rows
+    raw = k // 256 * synth.BLOCK_BYTES[ty]
+    assert not p.reshape(rows, rs)[:, raw:].any()  # zero pad
+    if ty in (synth.TYPE_Q4_K, synth.TYPE_Q5_K):  # within a row: a pure byte permutation
+        assert np.array_equal(np.sort(p.reshape(rows, rs)[:, :raw], axis=1), np.sort(w.reshape(rows, raw), axis=1))
+    assert np.array_equal(synth.gguf_from_planar_np(ty, p, k), w)
 
 
 def test_qh_transpose_moves_two_bit_cells():

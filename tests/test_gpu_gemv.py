@@ -19,7 +19,7 @@ ALL = [orc.TYPE_Q4_K, orc.TYPE_Q5_K, orc.TYPE_IQ2_S, orc.TYPE_IQ3_S]
 
 
 def run_gemv(ty, k, rows, w, x, layout):
-    wd = planar_dev(ty, w) if layout == lbk.LAYOUT_PLANAR else dev(w)
+    wd = planar_dev(ty, w, k) if layout == lbk.LAYOUT_PLANAR else dev(w)
     y = torch.full((rows,), float("nan"), device="cuda")
     q8 = torch.zeros(k // 256 * 292, dtype=torch.uint8, device="cuda")
     ctx().gemv(matrix(ty, k, rows, wd, layout), dev(x), y, q8)
@@ -121,15 +121,16 @@ def test_non_finite_weight_scale_reported():
 
 
 @pytest.mark.parametrize("ty", ALL)
-def test_repack_matches_numpy_and_unpack_inverts(ty):
-    rng = np.random.default_rng(20 + ty)
-    k, rows = 1536, 37
+@pytest.mark.parametrize("k", [768, 1536, 4096])
+def test_repack_matches_numpy_and_unpack_inverts(ty, k):
+    rng = np.random.default_rng(20 + ty + k)
+    rows = 37
     w = synth.packed_np(rng, ty, k, rows)
     src = dev(w)
-    planar = torch.zeros_like(src)
+    planar = torch.full((synth.planar_bytes(ty, k, rows),), 0xA5, dtype=torch.uint8, device="cuda")
     ctx().repack(matrix(ty, k, rows, src), planar)
     back = torch.zeros_like(src)
     ctx().unpack(matrix(ty, k, rows, planar, lbk.LAYOUT_PLANAR), back)
     clean_status()
-    np.testing.assert_array_equal(host(planar), synth.planar_np(ty, w))
+    np.testing.assert_array_equal(host(planar), synth.planar_np(ty, w, k))  # pad bytes zeroed too
     np.testing.assert_array_equal(host(back), w)

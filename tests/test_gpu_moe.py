@@ -79,6 +79,29 @@ def test_fused_and_per_expert_paths_are_bit_identical():
     lg.close()
 
 
+@pytest.mark.parametrize("H,F,E,k,T", [(2048, 512, 8, 2, 1), (4096, 768, 12, 4, 3), (2048, 256, 16, 8, 1)])
+def test_bulk_staged_gate_up_matches_oracle_and_per_expert_path(H, F, E, k, T):
+    """Hidden widths of 8 or 16 blocks take the bulk-copy-staged gate/up
+    kernel (routed and shared CTA roles); the result must equal the oracle to
+    the tolerance and the per-expert GGUF path bit for bit."""
+    rng = np.random.default_rng(H + 3 * F + E + k + T)
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    xs = rng.standard_normal((T, H)).astype(np.float32)
+    lp, kp = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    lg, kg = upload_layer(router, experts, shared, lbk.LAYOUT_GGUF, k)
+    want, wids, wcoefs, _ = oracle_tokens(router, experts, shared, xs, k)
+    for mode in (lbk.ROUTER_TREE, lbk.ROUTER_SEQUENTIAL):
+        out, ids, coefs = run_forward(lp, xs, mode)
+        np.testing.assert_array_equal(ids, wids)
+        np.testing.assert_allclose(coefs, wcoefs, rtol=1e-6)
+        assert rel_err(out, want) <= TOL, rel_err(out, want)
+        ref, rids, _ = run_forward(lg, xs, mode)
+        np.testing.assert_array_equal(ids, rids)
+        np.testing.assert_array_equal(bits(out), bits(ref))
+    lp.close()
+    lg.close()
+
+
 def test_caller_supplied_routing_and_combine_order():
     rng = np.random.default_rng(5)
     H, F, E, k = 512, 256, 8, 3

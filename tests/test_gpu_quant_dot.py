@@ -78,7 +78,7 @@ def test_dot_golden_fixture_bit_exact(name, ty, bb, layout):
     enc = np.frombuffer(read_golden(f"decode-{name}.input.bin"), dtype=np.uint8).copy()
     q8 = np.frombuffer(read_golden("q8-k-activations.output-q8-k.bin"), dtype=np.uint8).copy()
     want = np.frombuffer(read_golden(f"dot-{name}-q8-k.output-f32le.bin"), dtype="<u4")[0]
-    w = planar_dev(ty, enc) if layout == lbk.LAYOUT_PLANAR else dev(enc)
+    w = planar_dev(ty, enc, 768) if layout == lbk.LAYOUT_PLANAR else dev(enc)
     out = torch.full((1,), float("nan"), device="cuda")
     sums = torch.zeros(27, dtype=torch.int32, device="cuda")
     ctx().vec_dot(matrix(ty, 768, 1, w, layout), dev(q8), out, sums)
@@ -95,7 +95,7 @@ def test_block_sums_and_dots_match_oracle(ty, k, rows, layout):
     rng = np.random.default_rng(k * 31 + rows + ty)
     w = synth.packed_np(rng, ty, k, rows)
     q8 = orc.quantize_q8k(rng.standard_normal(k).astype(np.float32))
-    wd = planar_dev(ty, w) if layout == lbk.LAYOUT_PLANAR else dev(w)
+    wd = planar_dev(ty, w, k) if layout == lbk.LAYOUT_PLANAR else dev(w)
     out = torch.zeros(rows, device="cuda")
     per = 9 if ty in (orc.TYPE_Q4_K, orc.TYPE_Q5_K) else 1
     sums = torch.zeros(rows * k // 256 * per, dtype=torch.int32, device="cuda")
