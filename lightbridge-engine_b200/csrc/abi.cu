@@ -810,7 +810,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.chain_floats = (dots * 9 + 64 + 3) & ~(uint64_t)3;
         if (lbk::moe_gate_up_fixed_smem(L->gate_type, L->sgate_type) +
                 lbk::kMoeGateUpWarps * (g.prod_floats + g.chain_floats) * 4 >
-            lbk::kMaxSmem - 8192)  // static top-k buffers
+            lbk::kMaxSmem - 8704)  // static top-k buffers
             return fail(LBK_INVALID_PARAMETER, "MoE gate/up shapes exceed shared memory");
         e = lbk::launch_moe_gate_up(L->gate_type, L->sgate_type, g, st);
         if (e != cudaSuccess) return cuda_fail(e, "moe gate/up launch");

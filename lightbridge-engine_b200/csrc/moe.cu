@@ -361,6 +361,7 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
     // chunk partials in chunk order, then top-k) while the other warps copy
     // the tables; CTA 0 publishes the routing for the down kernel.
     __shared__ float s_logits[1024];
+    __shared__ float s_tkp[1024];
     __shared__ lbk_routed s_routed[32];
     if (a.defer_topk && warp == 0) {
         const int lane = threadIdx.x & 31;
@@ -372,7 +373,7 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
         }
         __syncwarp();
         topk_warp(s_logits, a.bias, (int)a.experts, (int)a.k, a.weight_scale, s_routed,
-                  blockIdx.x == 0 ? a.status : nullptr, 0);
+                  blockIdx.x == 0 ? a.status : nullptr, 0, s_logits, s_tkp);
         __syncwarp();
         if (blockIdx.x == 0 && lane < (int)a.k) a.routed_store[lane] = s_routed[lane];
     }
@@ -441,18 +442,21 @@ struct GUTRole {
     static constexpr int kBytes = kResOff + kGUTWarps * kRes * 4;
 };
 
-// Lane 0: rows [ra, ra+nr) of gate and of up, one contiguous planar copy
-// each, into the stage ([gate: R rows][up: R rows], rows at stride rs).
-__device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const uint8_t* gmat, const uint8_t* umat,
-                                          uint32_t rs, int R, uint32_t ra, uint32_t nr) {
-    mbar_expect_tx(bar, 2u * nr * rs);
-    bulk_g2s(stage, gmat + (uint64_t)ra * rs, nr * rs, bar);
-    bulk_g2s(stage + (uint32_t)R * rs, umat + (uint64_t)ra * rs, nr * rs, bar);
+// Lane 0: rows [ra, ra+nr) of one matrix, one contiguous planar copy (rows
+// at stride rs), into a stage.
+__device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const uint8_t* mat, uint32_t rs, uint32_t ra,
+                                          uint32_t nr) {
+    mbar_expect_tx(bar, nr * rs);
+    bulk_g2s(stage, mat + (uint64_t)ra * rs, nr * rs, bar);
 }
 
 // One role's items: (token, slot, chunk of rows) spread over the role's warps.
+// Work unit: R rows (one warp step, 32 half blocks) of one matrix. Units
+// alternate gate, up, gate, up ... through the warp's two stages (stage m
+// holds matrix m); each refill is issued as soon as its stage is copied to
+// registers, two units ahead of its use.
 template <int T, bool kRouted>
-__device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar, const lbk_routed* s_routed,
+__device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar0, const lbk_routed* s_routed,
                                         uint32_t role_warp, uint32_t role_warps) {
     using RL = GUTRole<T>;
     using HB = typename HBOf<T>::type;
@@ -463,8 +467,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     const int sub = lane / tpr, hb = lane % tpr, b = hb >> 1, h = hb & 1;
     const bool lane_on = hb < 2 * nb;
     const uint32_t rs = planar_row_bytes(RL::kBB, nb);  // R * rs == kMat for nb in {8, 16}
-    uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
-    const uint8_t* ustage = stage + R * rs;
+    const uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
     const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
     float* prod = reinterpret_cast<float*>(smem + RL::kProdOff) + warp * RL::kProd;
     float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
@@ -479,7 +482,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     const uint32_t chunks = (uint32_t)(kRouted ? a.chunks_r : a.chunks_s);
     const uint32_t slots = kRouted ? (uint32_t)a.k : 1u;
     const uint32_t items = (uint32_t)a.tokens * slots * chunks;
-    uint32_t phase = 0;
+    uint32_t phase = 0;  // bit m: parity of stage m's next phase
     bool live = true;  // false after a wait ran out: no further copies are issued
     for (uint32_t it = role_warp; it < items; it += role_warps) {
         const uint32_t t = it / (slots * chunks);
@@ -499,7 +502,16 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         }
         const uint32_t r0 = c * chunk, r1 = r0 + chunk < ffn ? r0 + chunk : ffn;
         if (r0 >= r1) continue;
-        if (lane == 0 && live) gut_issue(stage_s, bar, gmat, umat, rs, R, r0, r1 - r0 < (uint32_t)R ? r1 - r0 : R);
+        const uint32_t units = 2 * ((r1 - r0 + R - 1) / R);
+        if (lane == 0 && live) {
+            // The whole chunk heads for L2 at once (HBM sees every byte of the
+            // item in flight); the per-unit copies into the stages then hit L2.
+            prefetch_l2(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            prefetch_l2(umat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            const uint32_t nr0 = r1 - r0 < (uint32_t)R ? r1 - r0 : R;
+            gut_issue(stage_s, bar0, gmat, rs, r0, nr0);
+            gut_issue(stage_s + RL::kMat, bar0 + 8, umat, rs, r0, nr0);
+        }
 
         ActHB act;
         uint32_t nact[32];
@@ -512,41 +524,39 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         }
         float* hrow = a.h + ((uint64_t)t * (a.k + 1) + slot) * a.ffn;
         uint32_t rb = r0;
-        for (uint32_t ra = r0; ra < r1; ra += R) {
+        // one rolled loop over units: the decode is emitted once (its code is
+        // fetched cold once per launch)
+#pragma unroll 1
+        for (uint32_t u = 0; u < units; u++) {
+            const uint32_t m = u & 1;
+            const uint32_t ra = r0 + (u >> 1) * R;
             const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
-            if (live && !mbar_wait(bar, phase)) {
+            if (live && !mbar_wait(bar0 + 8 * m, (phase >> m) & 1u)) {
                 live = false;
                 if (lane == 0) report(a.status, LBK_TIMEOUT, it, 0);
             }
             live = __all_sync(0xffffffffu, live);
-            phase ^= 1u;
+            phase ^= 1u << m;
             const bool mine = lane_on && (uint32_t)sub < nr;
-            HB gw, uw;
-            if (mine) {
-                load_stage(gw, stage, so);
-                load_stage(uw, ustage, so);
-            }
+            HB w;
+            if (mine) load_stage(w, stage + m * RL::kMat, so);
             __syncwarp();
             const uint32_t rn = ra + R;
-            if (lane == 0 && live && rn < r1) {
+            if (lane == 0 && live && u + 2 < units) {
                 fence_proxy_async_smem();
-                gut_issue(stage_s, bar, gmat, umat, rs, R, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
-            }
-            IqPart gi{0, 0}, ui{0, 0};
-            KPart gk, uk;
-#pragma unroll
-            for (int l = 0; l < 8; l++) gk.lane[l] = uk.lane[l] = 0;
-            gk.min_sum = uk.min_sum = 0;
-            gk.dm = uk.dm = 0;
-            if (mine) {
-                HBDot<T>::run(gw, act, nact, t0, t1, h, gi, gk);
-                HBDot<T>::run(uw, act, nact, t0, t1, h, ui, uk);
+                gut_issue(stage_s + m * RL::kMat, bar0 + 8 * m, m ? umat : gmat, rs, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
             }
             const uint32_t row = ra + sub;
-            float* pg = prod + (int)(row - rb) * pstride;
-            write_products<T>(pg, b, h, mine, gi, gk, act.d, a.status, (uint64_t)row * nb + b);
-            write_products<T>(pg + nb * kTail, b, h, mine, ui, uk, act.d, a.status, (uint64_t)row * nb + b);
-            if (rn - rb >= (uint32_t)RL::kBmax || rn >= r1) {
+            IqPart ip{0, 0};
+            KPart kp;
+#pragma unroll
+            for (int l = 0; l < 8; l++) kp.lane[l] = 0;
+            kp.min_sum = 0;
+            kp.dm = 0;
+            if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
+            write_products<T>(prod + (int)(row - rb) * pstride + m * nb * kTail, b, h, mine, ip, kp, act.d, a.status,
+                              (uint64_t)row * nb + b);
+            if (m == 1 && (rn - rb >= (uint32_t)RL::kBmax || rn >= r1)) {
                 const int nrows = (int)((rn < r1 ? rn : r1) - rb);
                 __syncwarp();
                 warp_tails<T>(prod, nrows * 2, nb, chains, res);
@@ -569,31 +579,42 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
 template <int TG, int TS>
 __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGateUpArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ __align__(8) uint64_t s_bar[kGUTWarps];
+    __shared__ __align__(8) uint64_t s_bar[kGUTWarps * 2];  // two stages per warp
     __shared__ lbk_routed s_routed[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[warp]);
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[2 * warp]);
     if (lane == 0) {
         mbar_init(bar, 1);
+        mbar_init(bar + 8, 1);
         mbar_init_fence();
     }
     __syncwarp();
     if (blockIdx.x < a.routed_ctas) {
         using RL = GUTRole<TG>;
-        // Prologue by bulk copies: the lookup tables, and (single-token decode)
-        // the router's chunk partials, land in shared memory while warp 0
-        // finishes the router: logits = partials summed in chunk order, then
-        // top-k. CTA 0 publishes the routing for the down kernel.
+        // Prologue by bulk copies: (single-token decode) the router's chunk
+        // partials, then the lookup tables, land in shared memory; the whole
+        // CTA finishes the router from the partials (logits in chunk order,
+        // then top-k) while the tables arrive. CTA 0 publishes the routing
+        // for the down kernel.
         __shared__ __align__(8) uint64_t s_pro[2];  // [0] partials, [1] tables
+        __shared__ uint32_t s_sel[32];
+        __shared__ int s_bad;
         const uint32_t bar_p = (uint32_t)__cvta_generic_to_shared(&s_pro[0]);
         const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_pro[1]);
-        float* s_part = reinterpret_cast<float*>(smem + RL::kProdOff);  // free until the rows start
+        // free until the rows start: [partials][keys][p]
+        float* s_part = reinterpret_cast<float*>(smem + RL::kProdOff);
         const uint64_t pfloats = a.experts * a.chunks;
+        unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_part + ((pfloats + 3) & ~(uint64_t)3));
+        float* s_p = reinterpret_cast<float*>(s_key + a.experts);
         const bool bulk_p = a.defer_topk && pfloats % 4 == 0;
         if (threadIdx.x == 0) {
             mbar_init(bar_p, 1);
             mbar_init(bar_t, 1);
             mbar_init_fence();
+            if (bulk_p) {
+                mbar_expect_tx(bar_p, (uint32_t)(pfloats * 4));
+                bulk_g2s((uint32_t)__cvta_generic_to_shared(s_part), a.partials, (uint32_t)(pfloats * 4), bar_p);
+            }
             if constexpr (RL::kTab != 0) {
                 const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
                 mbar_expect_tx(bar_t, RL::kTab + RL::kSign);
@@ -602,33 +623,19 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 bulk_g2s(base + RL::kTab, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
                          RL::kSign, bar_t);
             }
-            if (bulk_p) {
-                mbar_expect_tx(bar_p, (uint32_t)(pfloats * 4));
-                bulk_g2s((uint32_t)__cvta_generic_to_shared(s_part), a.partials, (uint32_t)(pfloats * 4), bar_p);
-            }
         }
         __syncthreads();
-        if (a.defer_topk && warp == 0) {
+        if (a.defer_topk) {
             if (bulk_p) {
-                if (!mbar_wait(bar_p, 0) && lane == 0) report(a.status, LBK_TIMEOUT, 0, 0);
+                if (!mbar_wait(bar_p, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 0, 0);
             } else {
-                for (uint64_t i = lane; i < pfloats; i += 32) s_part[i] = __ldcg(a.partials + i);
-                __syncwarp();
+                for (uint64_t i = threadIdx.x; i < pfloats; i += blockDim.x) s_part[i] = __ldcg(a.partials + i);
+                __syncthreads();
             }
-            float* s_logits = s_part + ((pfloats + 3) & ~(uint64_t)3);
-            for (uint64_t e = lane; e < a.experts; e += 32) {
-                const float* pp = s_part + e * a.chunks;
-                float sum = 0.0f;
-                for (uint64_t c = 0; c < a.chunks; c++) sum = __fadd_rn(sum, pp[c]);
-                s_logits[e] = sum;
-            }
-            __syncwarp();
-            topk_warp(s_logits, a.bias, (int)a.experts, (int)a.k, a.weight_scale, s_routed,
-                      blockIdx.x == 0 ? a.status : nullptr, 0);
-            __syncwarp();
-            if (blockIdx.x == 0 && lane < (int)a.k) a.routed_store[lane] = s_routed[lane];
+            topk_cta(s_part, (int)a.chunks, a.bias, (int)a.experts, (int)a.k, a.weight_scale, s_routed,
+                     blockIdx.x == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
+            if (blockIdx.x == 0 && threadIdx.x < a.k) a.routed_store[threadIdx.x] = s_routed[threadIdx.x];
         }
-        __syncthreads();
         if constexpr (RL::kTab != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 1, 0);
         }
@@ -784,7 +791,7 @@ template <int TG, int TS>
 cudaError_t launch_gut(const MoeGateUpArgs& a, unsigned ctas, cudaStream_t stream) {
     constexpr int kA = GUTRole<TG>::kBytes, kB = GUTRole<TS>::kBytes;
     constexpr size_t smem = kA > kB ? kA : kB;
-    static_assert(smem + 32 * sizeof(lbk_routed) + kGUTWarps * 8 <= (size_t)kMaxSmem, "gate/up stage plan");
+    static_assert(smem + 32 * sizeof(lbk_routed) + kGUTWarps * 16 <= (size_t)kMaxSmem, "gate/up stage plan");
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_tma_kernel<TG, TS>));
     if (e != cudaSuccess) return e;
     if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
@@ -857,7 +864,7 @@ bool moe_gate_up_tma_supported(int gate_type, int shared_gate_type, int nb_h) {
 bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks) {
     const uint64_t floats = gate_type == LBK_TYPE_IQ2_S ? (uint64_t)kGUTWarps * GUTRole<LBK_TYPE_IQ2_S>::kProd
                                                         : (uint64_t)kGUTWarps * GUTRole<LBK_TYPE_Q4_K>::kProd;
-    return ((experts * chunks + 3) & ~(uint64_t)3) + experts <= floats;
+    return ((experts * chunks + 3) & ~(uint64_t)3) + 3 * experts <= floats;  // partials, 64-bit keys, p
 }
 
 cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,

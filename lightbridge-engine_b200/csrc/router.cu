@@ -22,12 +22,14 @@ namespace {
 
 constexpr int kRouterThreads = 512;
 constexpr int kChunk = 512;     // hidden lanes per warp work item
+constexpr int kTopkWarps = 4;  // per CTA; each holds 2 x 1024 floats of scratch
+
 __global__ void topk_kernel(TopkArgs a) {
+    __shared__ float s_tk[kTopkWarps][2][1024];
     const int warp = threadIdx.x >> 5;
-    const int nw = blockDim.x >> 5;
-    for (uint64_t t = (uint64_t)blockIdx.x * nw + warp; t < a.tokens; t += (uint64_t)gridDim.x * nw)
+    for (uint64_t t = (uint64_t)blockIdx.x * kTopkWarps + warp; t < a.tokens; t += (uint64_t)gridDim.x * kTopkWarps)
         topk_warp(a.logits + t * a.experts, a.bias, (int)a.experts, (int)a.k, a.weight_scale, a.routed + t * a.k,
-                  a.status, t);
+                  a.status, t, s_tk[warp][0], s_tk[warp][1]);
 }
 
 // Sequential order: bit-identical to dot_f32_row (gemv.rs:286-303).
@@ -146,10 +148,11 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
         a.logits[i] = sum;
     }
     __syncthreads();
-    if (f.routed != nullptr) {
-        for (uint64_t t = warp; t < a.tokens; t += kRouterThreads / 32)
+    if (f.routed != nullptr && warp < kTopkWarps) {
+        __shared__ float s_tk[kTopkWarps][2][1024];
+        for (uint64_t t = warp; t < a.tokens; t += kTopkWarps)
             topk_warp(a.logits + t * a.experts, f.bias, (int)a.experts, (int)f.k, f.weight_scale, f.routed + t * f.k,
-                      a.status, t);
+                      a.status, t, s_tk[warp][0], s_tk[warp][1]);
     }
     if (threadIdx.x == 0) *f.counter = 0u;
 }
@@ -181,9 +184,9 @@ cudaError_t launch_router(const RouterArgs& a, int mode, int sm_count, cudaStrea
 }
 
 cudaError_t launch_topk(const TopkArgs& a, cudaStream_t stream) {
-    uint64_t grid = (a.tokens + 7) / 8;
+    uint64_t grid = (a.tokens + kTopkWarps - 1) / kTopkWarps;
     if (grid < 1) grid = 1;
-    topk_kernel<<<(unsigned)grid, 256, 0, stream>>>(a);
+    topk_kernel<<<(unsigned)grid, kTopkWarps * 32, 0, stream>>>(a);
     return cudaGetLastError();
 }
 
