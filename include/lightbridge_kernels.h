@@ -262,7 +262,9 @@ int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer);
 int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer);
 
 /* Workspace bytes for `tokens` tokens. The workspace must be zero-filled once
- * before its first use; every call leaves it ready for the next one. */
+ * before its first use (its first 16 bytes hold an arrival counter that every
+ * completed call leaves at zero; the rest is rewritten by every call), so one
+ * workspace of the largest size serves calls of any layer and token count. */
 int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes);
 
 /* Full routed-MoE FFN for `tokens` tokens (x: tokens*hidden f32): router
@@ -302,11 +304,11 @@ int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, co
  * would synchronize the device.
  *   - Returns LBK_SCRATCH_TOO_SMALL (detail: expected = bytes needed) when the
  *     layer's workspace for `tokens` exceeds 1 MiB (hidden 4096, ffn 1536,
- *     top-8 fits up to 8 tokens).
+ *     top-8 fits up to 4 tokens).
  *   - The first call on a device looks up the array and zero-fills it
  *     synchronously; make it before any stream capture on that device. The
- *     array's counter prefix must be zero when a call starts; every call that
- *     runs to completion leaves it at zero.
+ *     array's first 16 bytes (an arrival counter) must be zero when a call
+ *     starts; every call that runs to completion leaves them at zero.
  *   - Calls that overlap in time on one device (any stream, thread or layer)
  *     share the array and race: serialize them. */
 int32_t lbk_moe_forward_no_alloc(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,

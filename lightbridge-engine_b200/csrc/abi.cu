@@ -185,18 +185,28 @@ int32_t run_f32_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, uint
 }
 
 struct WsLayout {
-    uint64_t logits, partials, q8x, routed, h, hq, counters, g, u, total;
+    uint64_t rcounter, logits, partials, q8x, routed, h, hq, counters, dcounters, counter_words, dots, g, u, total;
 };
 
 uint64_t up256(uint64_t v) { return (v + 255) & ~(uint64_t)255; }
 
+// Workspace of one MoE call. Byte 0 holds the router's arrival counter, at
+// the same place for every layer and token count, so a workspace stays valid
+// across calls of different shapes once it was zero-filled; the other arrival
+// counters ([gate/up h blocks][down combine blocks]) move with the shape and
+// are zeroed by the router kernel of every call.
 WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T) {
     WsLayout o{};
-    uint64_t off = 0;
     uint64_t slots = T * (L->k + 1);
     uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
-    o.counters = off;  // first, so that a zero-filled prefix covers them
-    off = up256(off + slots * nbf * 4 + 4);
+    o.rcounter = 0;
+    o.counters = 16;
+    o.dcounters = o.counters + slots * nbf * 4;
+    const uint64_t cend = o.dcounters + T * ((L->H + lbk::kMoeDownCombineRows - 1) / lbk::kMoeDownCombineRows) * 4;
+    o.counter_words = (cend - o.counters) / 4;
+    uint64_t off = up256(cend);
+    o.dots = off;  // down row dots [T][k+1][H]
+    off = up256(off + slots * L->H * 4);
     o.logits = off;
     off = up256(off + T * L->E * 4);
     o.partials = off;
@@ -830,6 +840,36 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         d.routed = routed;
         d.hq = ws + o.hq;
         d.out = out;
+        d.status = ctx->status;
+        d.tables = ctx->tables();
+        if (lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
+            // Split the SMs by bytes streamed, then spread each role's rows
+            // over its warps (chunks in whole steps of 32 / tpr rows).
+            const uint64_t rsd = (nbf * block_bytes(L->down_type) + 15) & ~(uint64_t)15;
+            const uint64_t rss = (nbf * block_bytes(L->sdown_type) + 15) & ~(uint64_t)15;
+            const double br = (double)T * L->k * L->H * rsd, bs = (double)T * L->H * rss;
+            const unsigned ctas = (unsigned)ctx->sm_count;
+            long rc = std::lround(ctas * br / (br + bs));
+            rc = rc < 1 ? 1 : (rc > (long)ctas - 1 ? (long)ctas - 1 : rc);
+            d.routed_ctas = (uint32_t)rc;
+            const uint64_t R = 32 / d.tpr_f;
+            auto chunk_for = [&](uint64_t warps, uint64_t instances) {
+                uint64_t per = warps / instances;
+                per = per < 1 ? 1 : per;
+                uint64_t c = (L->H + per - 1) / per;
+                return (c + R - 1) / R * R;
+            };
+            d.chunk_r = chunk_for((uint64_t)rc * lbk::kMoeDownTmaWarps, T * L->k);
+            d.chunk_s = chunk_for((uint64_t)(ctas - rc) * lbk::kMoeDownTmaWarps, T);
+            d.chunks_r = (L->H + d.chunk_r - 1) / d.chunk_r;
+            d.chunks_s = (L->H + d.chunk_s - 1) / d.chunk_s;
+            d.dots = reinterpret_cast<float*>(ws + o.dots);
+            d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
+            e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
+            if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
+            if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);
+            return ok();
+        }
         d.wps = 1;  // one warp per slot (the kernel's 288-thread bound covers top-k <= 8)
         const uint64_t rpsf = 32 / d.tpr_f;
         uint64_t ctas_x = (uint64_t)ctx->sm_count;
@@ -904,7 +944,9 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
     f.r.status = ctx->status;
     f.partials = reinterpret_cast<float*>(ws + o.partials);
     f.q8x = layer->fused ? ws + o.q8x : nullptr;
-    f.counter = reinterpret_cast<unsigned int*>(ws + o.counters + tokens * (layer->k + 1) * (layer->F / LBK_QK_K) * 4);
+    f.counter = reinterpret_cast<unsigned int*>(ws + o.rcounter);
+    f.zero = reinterpret_cast<unsigned int*>(ws + o.counters);
+    f.zero_words = layer->fused ? o.counter_words : 0;
     f.bias = layer->w.selection_bias;
     f.k = (uint32_t)layer->k;
     f.weight_scale = layer->weight_scale;
@@ -964,7 +1006,9 @@ LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t to
         q.r.tokens = tokens;
         q.r.status = ctx->status;
         q.q8x = ws + o.q8x;
-        q.counter = reinterpret_cast<unsigned int*>(ws + o.counters + tokens * (layer->k + 1) * (layer->F / LBK_QK_K) * 4);
+        q.counter = reinterpret_cast<unsigned int*>(ws + o.rcounter);
+        q.zero = reinterpret_cast<unsigned int*>(ws + o.counters);
+        q.zero_words = o.counter_words;
         cudaError_t e = lbk::launch_router_fused(q, ctx->sm_count, st);
         if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
     }
@@ -985,12 +1029,13 @@ LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t to
 // that overlap in time (other streams, other host threads, other layers)
 // race on it; serialize them (one stream, or events). Layers and token counts
 // whose workspace exceeds kStaticScratchBytes are rejected with
-// LBK_SCRATCH_TOO_SMALL. The counter prefix of the workspace must be zero when
-// a call starts: the first call on a device zero-fills the whole array, and
-// every call that runs to completion leaves the counters at zero again.
+// LBK_SCRATCH_TOO_SMALL. The workspace's first 16 bytes (the router's arrival
+// counter) must be zero when a call starts: the first call on a device
+// zero-fills the whole array, and every call that runs to completion leaves
+// that counter at zero again.
 namespace {
 
-constexpr uint64_t kStaticScratchBytes = 1ull << 20;  // 1 MiB: hidden 4096 / ffn 1536 / top-8 decode up to 8 tokens
+constexpr uint64_t kStaticScratchBytes = 1ull << 20;  // 1 MiB: hidden 4096 / ffn 1536 / top-8 decode up to 4 tokens
 constexpr int kStaticScratchDevices = 64;
 
 static __device__ __align__(256) uint8_t g_moe_scratch[kStaticScratchBytes];

@@ -160,6 +160,11 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
 // Orders this thread's earlier generic-proxy shared accesses before later
 // async-proxy (bulk copy) writes to the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Programmatic dependent launch: wait until the grid this one depends on has
+// completed and its writes are visible (a no-op for an ordinary launch), and
+// let the grid that depends on this one start launching.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // Hint that [p, p+bytes) will be read soon: bring it into L2.
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");

@@ -74,6 +74,8 @@ struct RouterFusedArgs {
     float weight_scale;
     lbk_routed* routed;     // [tokens][k], or null (logits only)
     int defer;              // 1: leave the chunk partials for the consumer (no last-CTA pass)
+    unsigned int* zero;     // arrival counters of the launches that follow, zeroed here
+    uint64_t zero_words;
 };
 size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens);
 cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStream_t stream);

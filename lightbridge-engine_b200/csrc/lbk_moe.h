@@ -59,9 +59,18 @@ struct MoeDownArgs {
     uint64_t wps;                    // warps per slot
     uint64_t prod_floats;
     uint64_t chain_floats;
+    // bulk-copy-staged kernel: CTAs [0, routed_ctas) take routed slots, the
+    // rest the shared expert; items (token, slot, chunk of rows)
+    uint32_t routed_ctas;
+    uint64_t chunk_r, chunk_s, chunks_r, chunks_s;
+    float* dots;                     // [tokens][k+1][hidden] row dots
+    unsigned int* counters;          // [tokens][hidden/64] arrivals, zero between launches
     DeviceStatus* status;
     Tables tables;
 };
+
+constexpr int kMoeDownTmaWarps = 16;   // warps per bulk-copy-staged down CTA
+constexpr int kMoeDownCombineRows = 64;  // rows combined by the last arriving warp
 
 bool moe_fused_supported(int gate_type, int shared_gate_type, int down_type, int shared_down_type);
 size_t moe_gate_up_fixed_smem(int gate_type, int shared_gate_type);
@@ -74,5 +83,9 @@ bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks
 cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
                                    cudaStream_t stream);
 cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream);
+// Bulk-copy-staged down over `ctas` CTAs (planar, nb_f <= 16).
+bool moe_down_tma_supported(int down_type, int shared_down_type, int nb_f);
+cudaError_t launch_moe_down_tma(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
+                                cudaStream_t stream);
 
 }  // namespace lbk

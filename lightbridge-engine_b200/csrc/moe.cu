@@ -454,10 +454,11 @@ __device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const ui
 // Work unit: R rows (one warp step, 32 half blocks) of one matrix. Units
 // alternate gate, up, gate, up ... through the warp's two stages (stage m
 // holds matrix m); each refill is issued as soon as its stage is copied to
-// registers, two units ahead of its use.
+// registers, two units ahead of its use. dep_wait: the grid dependency
+// (router output) is still to be waited for, after the first copies.
 template <int T, bool kRouted>
 __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar0, const lbk_routed* s_routed,
-                                        uint32_t role_warp, uint32_t role_warps) {
+                                        uint32_t role_warp, uint32_t role_warps, bool dep_wait) {
     using RL = GUTRole<T>;
     using HB = typename HBOf<T>::type;
     constexpr bool kIq = RL::kIq;
@@ -511,6 +512,10 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
             const uint32_t nr0 = r1 - r0 < (uint32_t)R ? r1 - r0 : R;
             gut_issue(stage_s, bar0, gmat, rs, r0, nr0);
             gut_issue(stage_s + RL::kMat, bar0 + 8, umat, rs, r0, nr0);
+        }
+        if (dep_wait) {
+            grid_dep_wait();
+            dep_wait = false;
         }
 
         ActHB act;
@@ -583,6 +588,7 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
     __shared__ lbk_routed s_routed[32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[2 * warp]);
+    grid_dep_launch();  // the down kernel may start on SMs this grid leaves
     if (lane == 0) {
         mbar_init(bar, 1);
         mbar_init(bar + 8, 1);
@@ -611,10 +617,7 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
             mbar_init(bar_p, 1);
             mbar_init(bar_t, 1);
             mbar_init_fence();
-            if (bulk_p) {
-                mbar_expect_tx(bar_p, (uint32_t)(pfloats * 4));
-                bulk_g2s((uint32_t)__cvta_generic_to_shared(s_part), a.partials, (uint32_t)(pfloats * 4), bar_p);
-            }
+            // constant data first: this part overlaps the router kernel's tail
             if constexpr (RL::kTab != 0) {
                 const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
                 mbar_expect_tx(bar_t, RL::kTab + RL::kSign);
@@ -623,6 +626,11 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 bulk_g2s(base + RL::kTab, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
                          RL::kSign, bar_t);
             }
+        }
+        grid_dep_wait();  // the router's partials, Q8_K image and zeroed counters
+        if (threadIdx.x == 0 && bulk_p) {
+            mbar_expect_tx(bar_p, (uint32_t)(pfloats * 4));
+            bulk_g2s((uint32_t)__cvta_generic_to_shared(s_part), a.partials, (uint32_t)(pfloats * 4), bar_p);
         }
         __syncthreads();
         if (a.defer_topk) {
@@ -639,10 +647,12 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         if constexpr (RL::kTab != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 1, 0);
         }
-        gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps);
+        gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps, false);
     } else {
+        // shared expert: its first rows are constant data, requested before
+        // the wait for the router's output (inside gut_run)
         gut_run<TS, false>(a, smem, bar, nullptr, (blockIdx.x - a.routed_ctas) * kGUTWarps + warp,
-                           (gridDim.x - a.routed_ctas) * kGUTWarps);
+                           (gridDim.x - a.routed_ctas) * kGUTWarps, true);
     }
 }
 
@@ -772,7 +782,248 @@ __global__ void __launch_bounds__(kDownMaxThreads, 1) moe_down_kernel(MoeDownArg
     }
 }
 
+// ---------------------------------------------------- down, bulk-copy staged
+//
+// Items (token, slot, chunk of output rows) over two CTA roles as in the
+// gate/up kernel: CTAs [0, routed_ctas) take the routed slots (and hold the
+// routed type's tables), the others the shared expert. A unit is R rows of
+// one down matrix (32 half blocks at most), streamed through the warp's two
+// stages. Each warp writes its rows' dots to `dots` and arrives on the
+// 64-row combine blocks it touched; the last arrival of a block forms
+// out = 0; += c_j * dot_j (routed, ascending ID); += 1.0 * dot_shared
+// (moe.rs:331-336) for those rows, unless validation failed upstream.
+
+constexpr int kDNWarps = kMoeDownTmaWarps;
+constexpr int kDNThreads = kDNWarps * 32;
+constexpr int kDNBlock = kMoeDownCombineRows;
+
+template <int T>
+struct DNRole {
+    static constexpr bool kIq = is_iq<T>();
+    static constexpr int kBB = TypeInfo<T>::kBlockBytes;
+    static constexpr int kUnit = 16 * kBB + 256;  // R rows of <= 16 blocks, each padded to 16 bytes
+    static constexpr int kStage = 2 * kUnit;
+    static constexpr int kBmax = T == LBK_TYPE_IQ3_S ? 16 : 8;  // rows per tail batch (IQ2_S: tables leave less room)
+    static constexpr int kTail = TypeInfo<T>::kTail;
+    static constexpr int kProd = kBmax * 16 * kTail;  // a batch holds <= 16 blocks of rows (R * nb <= 16)
+    static constexpr int kChain = kIq ? 0 : 16 * 9;   // a batch has <= max(kBmax, R) <= 16 rows
+    static constexpr int kRes = 32;
+    static constexpr int kTab = table_bytes<T>();
+    static constexpr int kSign = kIq ? kSignBytes : 0;
+    static constexpr int kRingOff = kTab + kSign;
+    static constexpr int kProdOff = kRingOff + kDNWarps * kStage;
+    static constexpr int kChainOff = kProdOff + kDNWarps * kProd * 4;
+    static constexpr int kResOff = kChainOff + kDNWarps * kChain * 4;
+    static constexpr int kBytes = kResOff + kDNWarps * kRes * 4;
+};
+
+// Arrivals on the combine blocks of rows [r0, r1) of slot `slot`; the last
+// arriving warp of a block combines its rows.
+__device__ __forceinline__ void dn_arrive_and_combine(const MoeDownArgs& a, uint32_t t, uint32_t r0, uint32_t r1) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t H = (uint32_t)a.hidden;
+    const uint32_t nblk = (H + kDNBlock - 1) / kDNBlock;
+    for (uint32_t blk = r0 / kDNBlock; blk * kDNBlock < r1; blk++) {
+        const uint32_t lo = blk * kDNBlock > r0 ? blk * kDNBlock : r0;
+        const uint32_t hi = (blk + 1) * kDNBlock < r1 ? (blk + 1) * kDNBlock : r1;
+        const uint32_t bend = (blk + 1) * kDNBlock < H ? (blk + 1) * kDNBlock : H;
+        const uint32_t target = (uint32_t)(a.k + 1) * (bend - blk * kDNBlock);
+        unsigned int* cnt = a.counters + (uint64_t)t * nblk + blk;
+        unsigned old = 0;
+        if (lane == 0) {
+            __threadfence();
+            old = atomicAdd(cnt, hi - lo);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old + (hi - lo) != target) continue;
+        __threadfence();
+        if (lane == 0) *cnt = 0u;  // ready for the next launch
+        if (status_set(a.status)) continue;  // validation failed upstream: leave out unchanged
+        const float* dt = a.dots + (uint64_t)t * (a.k + 1) * H;
+        for (uint32_t r = blk * kDNBlock + lane; r < bend; r += 32) {
+            float acc = 0.0f;
+            for (uint64_t j = 0; j < a.k; j++) {
+                const float c = a.routed[(uint64_t)t * a.k + j].coefficient;
+                acc = __fadd_rn(acc, __fmul_rn(c, __ldcg(dt + j * H + r)));
+            }
+            acc = __fadd_rn(acc, __fmul_rn(1.0f, __ldcg(dt + a.k * H + r)));
+            a.out[(uint64_t)t * H + r] = acc;
+        }
+    }
+}
+
+template <int T, bool kRouted>
+__device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint32_t bar0, uint32_t role_warp,
+                                       uint32_t role_warps, bool dep_wait) {
+    using RL = DNRole<T>;
+    using HB = typename HBOf<T>::type;
+    constexpr bool kIq = RL::kIq;
+    constexpr int kTail = RL::kTail;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = a.nb_f, tpr = a.tpr_f, R = 32 / tpr;
+    const int sub = lane / tpr, hb = lane % tpr, b = hb >> 1, h = hb & 1;
+    const bool lane_on = hb < 2 * nb;
+    const uint32_t rs = planar_row_bytes(RL::kBB, nb);
+    const uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
+    const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
+    float* prod = reinterpret_cast<float*>(smem + RL::kProdOff) + warp * RL::kProd;
+    float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
+    float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
+    const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
+    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
+    const StageOff so = stage_off<T>(nb, sub, b, h);
+
+    const uint32_t H = (uint32_t)a.hidden;
+    const uint32_t chunk = (uint32_t)(kRouted ? a.chunk_r : a.chunk_s);
+    const uint32_t chunks = (uint32_t)(kRouted ? a.chunks_r : a.chunks_s);
+    const uint32_t slots = kRouted ? (uint32_t)a.k : 1u;
+    const uint32_t items = (uint32_t)a.tokens * slots * chunks;
+    uint32_t phase = 0;  // bit s: parity of stage s's next phase
+    bool live = true;
+    for (uint32_t it = role_warp; it < items; it += role_warps) {
+        const uint32_t t = it / (slots * chunks);
+        const uint32_t rem = it - t * (slots * chunks);
+        const uint32_t j = rem / chunks, c = rem - j * chunks;
+        const uint32_t slot = kRouted ? j : (uint32_t)a.k;
+        const uint8_t* mat = a.sdown;
+        if constexpr (kRouted) {
+            uint32_t e = a.routed[(uint64_t)t * a.k + j].expert_id;
+            if (e >= a.experts) {  // reported; compute on expert 0 so the arrival counts stay balanced
+                if (lane == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
+                e = 0;
+            }
+            mat = a.down[e];
+        }
+        const uint32_t r0 = c * chunk, r1 = r0 + chunk < H ? r0 + chunk : H;
+        if (r0 >= r1) continue;
+        const uint32_t units = (r1 - r0 + R - 1) / R;
+        if (lane == 0 && live) {
+            prefetch_l2(mat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            for (uint32_t u = 0; u < 2 && u < units; u++) {
+                const uint32_t ra = r0 + u * R;
+                gut_issue(stage_s + u * RL::kUnit, bar0 + 8 * u, mat, rs, ra, r1 - ra < (uint32_t)R ? r1 - ra : R);
+            }
+        }
+        if (dep_wait) {
+            grid_dep_wait();
+            dep_wait = false;
+        }
+        ActHB act;
+        uint32_t nact[32];
+        if (lane_on) {
+            load_act_global<!kIq>(act, a.hq + ((uint64_t)t * (a.k + 1) + slot) * nb * kQ8IBytes, b, h, !kIq);
+            if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+                for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+            }
+        }
+        float* drow = a.dots + ((uint64_t)t * (a.k + 1) + slot) * H;
+        uint32_t rb = r0;
+#pragma unroll 1
+        for (uint32_t u = 0; u < units; u++) {
+            const uint32_t s = u & 1;
+            const uint32_t ra = r0 + u * R;
+            const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
+            if (live && !mbar_wait(bar0 + 8 * s, (phase >> s) & 1u)) {
+                live = false;
+                if (lane == 0) report(a.status, LBK_TIMEOUT, it, 1);
+            }
+            live = __all_sync(0xffffffffu, live);
+            phase ^= 1u << s;
+            const bool mine = lane_on && (uint32_t)sub < nr;
+            HB w;
+            if (mine) load_stage(w, stage + s * RL::kUnit, so);
+            __syncwarp();
+            if (lane == 0 && live && u + 2 < units) {
+                fence_proxy_async_smem();
+                const uint32_t rn = ra + 2 * R;
+                gut_issue(stage_s + s * RL::kUnit, bar0 + 8 * s, mat, rs, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
+            }
+            const uint32_t row = ra + sub;
+            IqPart ip{0, 0};
+            KPart kp;
+#pragma unroll
+            for (int l = 0; l < 8; l++) kp.lane[l] = 0;
+            kp.min_sum = 0;
+            kp.dm = 0;
+            if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
+            write_products<T>(prod + (int)(row - rb) * nb * kTail, b, h, mine, ip, kp, act.d, a.status,
+                              (uint64_t)row * nb + b);
+            const uint32_t rn = ra + R;
+            if (rn - rb >= (uint32_t)RL::kBmax || rn >= r1) {
+                const int nrows = (int)((rn < r1 ? rn : r1) - rb);
+                __syncwarp();
+                warp_tails<T>(prod, nrows, nb, chains, res);
+                if (lane < nrows) drow[rb + lane] = res[lane];
+                __syncwarp();
+                rb = rn;
+            }
+        }
+        dn_arrive_and_combine(a, t, r0, r1);
+    }
+}
+
+template <int TD, int TSD>
+__global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[kDNWarps * 2];
+    __shared__ __align__(8) uint64_t s_tab;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[2 * warp]);
+    const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_tab);
+    const bool routed_role = blockIdx.x < a.routed_ctas;
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_init(bar + 8, 1);
+        if (threadIdx.x == 0) mbar_init(bar_t, 1);
+        mbar_init_fence();
+    }
+    if (routed_role && threadIdx.x == 0) {
+        using RL = DNRole<TD>;
+        if constexpr (RL::kTab != 0) {
+            const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
+            mbar_expect_tx(bar_t, RL::kTab + RL::kSign);
+            bulk_g2s(base, TD == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
+                     RL::kTab, bar_t);
+            bulk_g2s(base + RL::kTab, TD == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
+                     RL::kSign, bar_t);
+        }
+    }
+    __syncthreads();
+    if (routed_role) {
+        grid_dep_wait();  // the routing and h images of the gate/up kernel
+        if constexpr (DNRole<TD>::kTab != 0) {
+            if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 3, 0);
+        }
+        dn_run<TD, true>(a, smem, bar, blockIdx.x * kDNWarps + warp, a.routed_ctas * kDNWarps, false);
+    } else {
+        // shared expert: its first rows are constant data, requested before
+        // the wait for the gate/up kernel's output (inside dn_run)
+        dn_run<TSD, false>(a, smem, bar, (blockIdx.x - a.routed_ctas) * kDNWarps + warp,
+                           (gridDim.x - a.routed_ctas) * kDNWarps, true);
+    }
+}
+
 // ---------------------------------------------------------------- launchers
+
+// Launch allowed to begin before the preceding kernel of the stream has
+// finished (programmatic stream serialization): the kernel calls
+// grid_dep_wait() before it reads that kernel's output.
+template <class Args>
+cudaError_t launch_dependent(void (*kernel)(Args), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                             const Args& a) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+}
 
 template <int TG, int TS>
 cudaError_t launch_gu(const MoeGateUpArgs& a, cudaStream_t stream) {
@@ -795,8 +1046,7 @@ cudaError_t launch_gut(const MoeGateUpArgs& a, unsigned ctas, cudaStream_t strea
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_tma_kernel<TG, TS>));
     if (e != cudaSuccess) return e;
     if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
-    moe_gate_up_tma_kernel<TG, TS><<<ctas, kGUTThreads, smem, stream>>>(a);
-    return cudaGetLastError();
+    return launch_dependent(moe_gate_up_tma_kernel<TG, TS>, ctas, kGUTThreads, smem, stream, a);
 }
 
 template <int TD, int TSD>
@@ -872,6 +1122,30 @@ cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const Mo
     (void)shared_gate_type;
     if (gate_type == LBK_TYPE_IQ2_S) return launch_gut<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
     return launch_gut<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);
+}
+
+template <int TD, int TSD>
+cudaError_t launch_dnt(const MoeDownArgs& a, unsigned ctas, cudaStream_t stream) {
+    constexpr int kA = DNRole<TD>::kBytes, kB = DNRole<TSD>::kBytes;
+    constexpr size_t smem = kA > kB ? kA : kB;
+    static_assert(smem + kDNWarps * 16 + 8 <= (size_t)kMaxSmem, "down stage plan");
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_down_tma_kernel<TD, TSD>));
+    if (e != cudaSuccess) return e;
+    if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
+    return launch_dependent(moe_down_tma_kernel<TD, TSD>, ctas, kDNThreads, smem, stream, a);
+}
+
+bool moe_down_tma_supported(int down_type, int shared_down_type, int nb_f) {
+    return (down_type == LBK_TYPE_IQ3_S || down_type == LBK_TYPE_IQ2_S || down_type == LBK_TYPE_Q4_K) &&
+           shared_down_type == LBK_TYPE_Q4_K && nb_f >= 1 && nb_f <= 16;
+}
+
+cudaError_t launch_moe_down_tma(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
+                                cudaStream_t stream) {
+    (void)shared_down_type;
+    if (down_type == LBK_TYPE_IQ3_S) return launch_dnt<LBK_TYPE_IQ3_S, LBK_TYPE_Q4_K>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ2_S) return launch_dnt<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
+    return launch_dnt<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);
 }
 
 cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream) {

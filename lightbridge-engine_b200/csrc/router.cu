@@ -62,6 +62,13 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
     const uint64_t items = row_items + a.tokens * nbq;
     const uint64_t nw = (uint64_t)gridDim.x * (kRouterThreads / 32);
     __shared__ bool s_last;
+    // The gate/up kernel may launch now: it does its constant-data prologue
+    // on free SMs and waits for this grid before reading its output.
+    grid_dep_launch();
+    // The arrival counters of the gate/up and down launches that follow sit
+    // at call-dependent places in the workspace: zero them for this call.
+    if (blockIdx.x == 0)
+        for (uint64_t i = threadIdx.x; i < f.zero_words; i += kRouterThreads) f.zero[i] = 0u;
 
     for (uint64_t it = (uint64_t)blockIdx.x * (kRouterThreads / 32) + warp; it < items; it += nw) {
         if (it < row_items) {

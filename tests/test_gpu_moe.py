@@ -102,6 +102,27 @@ def test_bulk_staged_gate_up_matches_oracle_and_per_expert_path(H, F, E, k, T):
     lg.close()
 
 
+@pytest.mark.parametrize("H,F,E,k", [(2048, 512, 8, 2), (1024, 512, 16, 4)])
+def test_one_workspace_serves_every_token_count(H, F, E, k):
+    """A workspace zero-filled once and sized for the largest call stays valid
+    across calls with different token counts (its regions move with T)."""
+    rng = np.random.default_rng(H + F + 11 * k)
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    ws = torch.zeros(layer.workspace_bytes(4), dtype=torch.uint8, device="cuda")
+    for T, mode in [(1, lbk.ROUTER_TREE), (4, lbk.ROUTER_TREE), (2, lbk.ROUTER_SEQUENTIAL), (1, lbk.ROUTER_SEQUENTIAL),
+                    (3, lbk.ROUTER_TREE), (1, lbk.ROUTER_TREE)]:
+        xs = rng.standard_normal((T, H)).astype(np.float32)
+        want, wids, _ = run_forward(layer, xs, mode)  # fresh workspace
+        out = torch.full((T * H,), float("nan"), device="cuda")
+        routed = torch.zeros(T * k * 2, dtype=torch.int32, device="cuda")
+        layer.forward(dev(xs.reshape(-1)), T, out, ws, routed_out=routed, router_mode=mode)
+        clean_status()
+        np.testing.assert_array_equal(host(routed).reshape(T, k, 2)[:, :, 0].astype(np.uint32), wids)
+        np.testing.assert_array_equal(bits(host(out).reshape(T, H)), bits(want))
+    layer.close()
+
+
 def test_caller_supplied_routing_and_combine_order():
     rng = np.random.default_rng(5)
     H, F, E, k = 512, 256, 8, 3
