@@ -436,6 +436,29 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
     ctx.close()
 
 
+def profile_forwards(n: int) -> None:
+    """A small case for ncu captures: one config-3 layer (1.3 GB) resident and
+    n single-token forwards through the C ABI, tokens rotating over 8."""
+    import torch
+
+    import lbk
+
+    ctx = lbk.Context(0)
+    dev = torch.device("cuda", 0)
+    tables, _ = build_layers(ctx, lbk, torch, dev, 1, 4, keep_gguf_layer0=False)
+    layer = tables[0][0]
+    ws = torch.zeros(layer.workspace_bytes(1), dtype=torch.uint8, device=dev)
+    xs = torch.randn(8, H, device=dev, generator=torch.Generator(device=dev).manual_seed(5))
+    out = torch.zeros(8, H, device=dev)
+    for i in range(n):
+        layer.forward(xs[i % 8], 1, out[i % 8], ws)
+    torch.cuda.synchronize()
+    ctx.raise_status()
+    layer.close()
+    ctx.close()
+    print(f"profile_forwards: {n} forwards ok", flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -443,11 +466,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-forwards", type=int, default=0,
+                    help="profiling driver: one resident layer, this many single-token forwards, no timing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.profile_forwards > 0:
+        profile_forwards(args.profile_forwards)
+        return
     if args.impl == "reference":
         reference_arm(args, rank)
         return

@@ -727,6 +727,34 @@ LBK_API int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tok
 
 namespace {
 
+// Per-warp time of one lane slot of a unit (one half block, microseconds, 16
+// warps per SM), measured on B200 for the bulk-copy-staged kernels.
+double hb_cost_us(int32_t ty) {
+    switch (ty) {
+        case LBK_TYPE_IQ2_S: return 0.034;
+        case LBK_TYPE_IQ3_S: return 0.028;
+        case LBK_TYPE_Q4_K: return 0.04;
+        default: return 0.045;
+    }
+}
+
+// Routed CTAs out of `ctas` so that the routed and the shared role finish
+// together: role time = fixed + work / (its warps).
+long split_roles(unsigned ctas, int warps, double work_r, double fixed_r, double work_s, double fixed_s) {
+    long best = 1;
+    double best_t = 1e300;
+    for (long r = 1; r < (long)ctas; r++) {
+        const double tr = fixed_r + work_r / (double)(r * warps);
+        const double ts = fixed_s + work_s / (double)((ctas - r) * warps);
+        const double t = tr > ts ? tr : ts;
+        if (t < best_t) {
+            best_t = t;
+            best = r;
+        }
+    }
+    return best;
+}
+
 // Expert stage of one MoE call for `tokens` tokens with routing in `routed`.
 // With defer_topk (single token, fused kernels) the routing is computed by the
 // gate/up kernel from the router's chunk partials and stored into `routed`.
@@ -765,14 +793,19 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.tables = ctx->tables();
         const int rps = 32 / g.tpr_h;
         if (lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)nbh)) {
-            // Split the SMs between routed and shared CTAs by bytes streamed,
-            // then spread each role's rows evenly over its warps.
-            const double br = (double)T * L->k * L->F * 2.0 * nbh * block_bytes(L->gate_type);
-            const double bs = (double)T * L->F * 2.0 * nbh * block_bytes(L->sgate_type);
+            // Split the SMs between routed and shared CTAs so that both roles
+            // end together, then spread each role's rows over its warps.
             const unsigned ctas = (unsigned)ctx->sm_count;
-            long rc = std::lround(ctas * br / (br + bs));
-            rc = rc < 1 ? 1 : (rc > (long)ctas - 1 ? (long)ctas - 1 : rc);
+            const double hb = 2.0 * nbh * 2.0 * L->F;  // half blocks of one slot (gate + up)
+            const long rc = split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * L->k * hb * hb_cost_us(L->gate_type),
+                                        defer_topk ? 5.0 : 1.5, T * hb * hb_cost_us(L->sgate_type), 1.0);
             g.routed_ctas = (uint32_t)rc;
+            if (T <= 4 && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
+                g.down = L->d_down;
+                g.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);
+                g.down_rs = (uint32_t)((nbf * block_bytes(L->down_type) + 15) & ~(uint64_t)15);
+                g.sdown_rs = (uint32_t)((nbf * block_bytes(L->sdown_type) + 15) & ~(uint64_t)15);
+            }
             auto chunk_for = [&](uint64_t warps, uint64_t instances) {
                 uint64_t per = warps / instances;
                 per = per < 1 ? 1 : per;
@@ -843,14 +876,12 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         d.status = ctx->status;
         d.tables = ctx->tables();
         if (lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
-            // Split the SMs by bytes streamed, then spread each role's rows
-            // over its warps (chunks in whole steps of 32 / tpr rows).
-            const uint64_t rsd = (nbf * block_bytes(L->down_type) + 15) & ~(uint64_t)15;
-            const uint64_t rss = (nbf * block_bytes(L->sdown_type) + 15) & ~(uint64_t)15;
-            const double br = (double)T * L->k * L->H * rsd, bs = (double)T * L->H * rss;
+            // Split the SMs so that both roles end together, then spread each
+            // role's rows over its warps (chunks in whole steps of 32 / tpr rows).
             const unsigned ctas = (unsigned)ctx->sm_count;
-            long rc = std::lround(ctas * br / (br + bs));
-            rc = rc < 1 ? 1 : (rc > (long)ctas - 1 ? (long)ctas - 1 : rc);
+            const double lanes = (double)L->H * d.tpr_f;  // lane slots of one slot's rows
+            const long rc = split_roles(ctas, lbk::kMoeDownTmaWarps, T * L->k * lanes * hb_cost_us(L->down_type), 4.0,
+                                        T * lanes * hb_cost_us(L->sdown_type), 1.5);
             d.routed_ctas = (uint32_t)rc;
             const uint64_t R = 32 / d.tpr_f;
             auto chunk_for = [&](uint64_t warps, uint64_t instances) {

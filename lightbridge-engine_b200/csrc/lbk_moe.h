@@ -39,6 +39,11 @@ struct MoeGateUpArgs {
     lbk_routed* routed_store;        // CTA 0 writes the routing here
     // bulk-copy-staged kernel: CTAs [0, routed_ctas) stream routed slots, the rest the shared expert
     uint32_t routed_ctas;
+    // down matrices of the layer, prefetched into L2 once the routing is known
+    // (null: no prefetch); row strides of the planar down matrices
+    const uint8_t* const* down;
+    const uint8_t* sdown;
+    uint32_t down_rs, sdown_rs;
     DeviceStatus* status;
     Tables tables;
 };

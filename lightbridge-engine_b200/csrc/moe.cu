@@ -456,9 +456,14 @@ __device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const ui
 // holds matrix m); each refill is issued as soon as its stage is copied to
 // registers, two units ahead of its use. dep_wait: the grid dependency
 // (router output) is still to be waited for, after the first copies.
+// s_ptr: the gate / up pointer tables staged in shared memory (gate at 0, up
+// at kPtrMax), or null.
+constexpr int kPtrMax = 256;
+
 template <int T, bool kRouted>
 __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar0, const lbk_routed* s_routed,
-                                        uint32_t role_warp, uint32_t role_warps, bool dep_wait) {
+                                        uint32_t role_warp, uint32_t role_warps, bool dep_wait,
+                                        const uint8_t* const* s_ptr) {
     using RL = GUTRole<T>;
     using HB = typename HBOf<T>::type;
     constexpr bool kIq = RL::kIq;
@@ -490,6 +495,22 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         const uint32_t rem = it - t * (slots * chunks);
         const uint32_t j = rem / chunks, c = rem - j * chunks;
         const uint32_t slot = kRouted ? j : (uint32_t)a.k;
+        const uint32_t r0 = c * chunk, r1 = r0 + chunk < ffn ? r0 + chunk : ffn;
+        if (r0 >= r1) continue;
+        const uint32_t units = 2 * ((r1 - r0 + R - 1) / R);
+        ActHB act;
+        uint32_t nact[32];
+        auto load_act = [&]() {
+            if (lane_on) {
+                load_act_global<!kIq>(act, a.q8x + (uint64_t)t * nb * kQ8IBytes, b, h, !kIq);
+                if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+                }
+            }
+        };
+        // the activations do not depend on the expert: in flight while it is resolved
+        if (!dep_wait) load_act();
         const uint8_t* gmat = a.sgate;
         const uint8_t* umat = a.sup;
         if constexpr (kRouted) {
@@ -498,12 +519,9 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
                 if (lane == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
                 e = 0;
             }
-            gmat = a.gate[e];
-            umat = a.up[e];
+            gmat = s_ptr ? s_ptr[e] : a.gate[e];
+            umat = s_ptr ? s_ptr[kPtrMax + e] : a.up[e];
         }
-        const uint32_t r0 = c * chunk, r1 = r0 + chunk < ffn ? r0 + chunk : ffn;
-        if (r0 >= r1) continue;
-        const uint32_t units = 2 * ((r1 - r0 + R - 1) / R);
         if (lane == 0 && live) {
             // The whole chunk heads for L2 at once (HBM sees every byte of the
             // item in flight); the per-unit copies into the stages then hit L2.
@@ -516,16 +534,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         if (dep_wait) {
             grid_dep_wait();
             dep_wait = false;
-        }
-
-        ActHB act;
-        uint32_t nact[32];
-        if (lane_on) {
-            load_act_global<!kIq>(act, a.q8x + (uint64_t)t * nb * kQ8IBytes, b, h, !kIq);
-            if constexpr (T == LBK_TYPE_IQ3_S) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
-            }
+            load_act();
         }
         float* hrow = a.h + ((uint64_t)t * (a.k + 1) + slot) * a.ffn;
         uint32_t rb = r0;
@@ -613,18 +622,27 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_part + ((pfloats + 3) & ~(uint64_t)3));
         float* s_p = reinterpret_cast<float*>(s_key + a.experts);
         const bool bulk_p = a.defer_topk && pfloats % 4 == 0;
+        // the experts' gate / up pointers, staged with the tables (16-byte copies)
+        __shared__ __align__(16) const uint8_t* s_ptr[2 * kPtrMax];
+        const bool stage_ptr = a.experts <= kPtrMax && a.experts % 2 == 0;
+        const uint32_t tab_tx = (RL::kTab != 0 ? RL::kTab + RL::kSign : 0) + (stage_ptr ? 16u * (uint32_t)a.experts : 0);
         if (threadIdx.x == 0) {
             mbar_init(bar_p, 1);
             mbar_init(bar_t, 1);
             mbar_init_fence();
             // constant data first: this part overlaps the router kernel's tail
+            if (tab_tx != 0) mbar_expect_tx(bar_t, tab_tx);
             if constexpr (RL::kTab != 0) {
                 const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
-                mbar_expect_tx(bar_t, RL::kTab + RL::kSign);
                 bulk_g2s(base, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
                          RL::kTab, bar_t);
                 bulk_g2s(base + RL::kTab, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
                          RL::kSign, bar_t);
+            }
+            if (stage_ptr) {
+                const uint32_t ps = (uint32_t)__cvta_generic_to_shared(s_ptr);
+                bulk_g2s(ps, a.gate, 8u * (uint32_t)a.experts, bar_t);
+                bulk_g2s(ps + 8 * kPtrMax, a.up, 8u * (uint32_t)a.experts, bar_t);
             }
         }
         grid_dep_wait();  // the router's partials, Q8_K image and zeroed counters
@@ -644,15 +662,29 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                      blockIdx.x == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
             if (blockIdx.x == 0 && threadIdx.x < a.k) a.routed_store[threadIdx.x] = s_routed[threadIdx.x];
         }
-        if constexpr (RL::kTab != 0) {
+        // This CTA's slice of every down matrix the call will read heads for
+        // L2 now: HBM streams it while the gate/up rows are being decoded.
+        if (a.down != nullptr && threadIdx.x == 0) {
+            const uint64_t H = a.hidden;
+            const uint64_t p0 = H * blockIdx.x / a.routed_ctas, p1 = H * (blockIdx.x + 1) / a.routed_ctas;
+            if (p1 > p0) {
+                for (uint64_t i = 0; i < a.tokens * a.k; i++) {
+                    const uint32_t e = a.defer_topk ? s_routed[i].expert_id : a.routed[i].expert_id;
+                    if (e < a.experts) prefetch_l2(a.down[e] + p0 * a.down_rs, (uint32_t)((p1 - p0) * a.down_rs));
+                }
+                prefetch_l2(a.sdown + p0 * a.sdown_rs, (uint32_t)((p1 - p0) * a.sdown_rs));
+            }
+        }
+        if (tab_tx != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 1, 0);
         }
-        gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps, false);
+        gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps, false,
+                          stage_ptr ? s_ptr : nullptr);
     } else {
         // shared expert: its first rows are constant data, requested before
         // the wait for the router's output (inside gut_run)
         gut_run<TS, false>(a, smem, bar, nullptr, (blockIdx.x - a.routed_ctas) * kGUTWarps + warp,
-                           (gridDim.x - a.routed_ctas) * kGUTWarps, true);
+                           (gridDim.x - a.routed_ctas) * kGUTWarps, true, nullptr);
     }
 }
 
@@ -854,7 +886,7 @@ __device__ __forceinline__ void dn_arrive_and_combine(const MoeDownArgs& a, uint
 
 template <int T, bool kRouted>
 __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint32_t bar0, uint32_t role_warp,
-                                       uint32_t role_warps, bool dep_wait) {
+                                       uint32_t role_warps, bool dep_wait, const uint8_t* const* s_ptr) {
     using RL = DNRole<T>;
     using HB = typename HBOf<T>::type;
     constexpr bool kIq = RL::kIq;
@@ -885,6 +917,22 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
         const uint32_t rem = it - t * (slots * chunks);
         const uint32_t j = rem / chunks, c = rem - j * chunks;
         const uint32_t slot = kRouted ? j : (uint32_t)a.k;
+        const uint32_t r0 = c * chunk, r1 = r0 + chunk < H ? r0 + chunk : H;
+        if (r0 >= r1) continue;
+        const uint32_t units = (r1 - r0 + R - 1) / R;
+        ActHB act;
+        uint32_t nact[32];
+        auto load_act = [&]() {
+            if (lane_on) {
+                load_act_global<!kIq>(act, a.hq + ((uint64_t)t * (a.k + 1) + slot) * nb * kQ8IBytes, b, h, !kIq);
+                if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+                }
+            }
+        };
+        // the activations do not depend on the expert: in flight while it is resolved
+        if (!dep_wait) load_act();
         const uint8_t* mat = a.sdown;
         if constexpr (kRouted) {
             uint32_t e = a.routed[(uint64_t)t * a.k + j].expert_id;
@@ -892,11 +940,8 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
                 if (lane == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
                 e = 0;
             }
-            mat = a.down[e];
+            mat = s_ptr ? s_ptr[e] : a.down[e];
         }
-        const uint32_t r0 = c * chunk, r1 = r0 + chunk < H ? r0 + chunk : H;
-        if (r0 >= r1) continue;
-        const uint32_t units = (r1 - r0 + R - 1) / R;
         if (lane == 0 && live) {
             prefetch_l2(mat + (uint64_t)r0 * rs, (r1 - r0) * rs);
             for (uint32_t u = 0; u < 2 && u < units; u++) {
@@ -907,15 +952,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
         if (dep_wait) {
             grid_dep_wait();
             dep_wait = false;
-        }
-        ActHB act;
-        uint32_t nact[32];
-        if (lane_on) {
-            load_act_global<!kIq>(act, a.hq + ((uint64_t)t * (a.k + 1) + slot) * nb * kQ8IBytes, b, h, !kIq);
-            if constexpr (T == LBK_TYPE_IQ3_S) {
-#pragma unroll
-                for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
-            }
+            load_act();
         }
         float* drow = a.dots + ((uint64_t)t * (a.k + 1) + slot) * H;
         uint32_t rb = r0;
@@ -978,29 +1015,37 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
         if (threadIdx.x == 0) mbar_init(bar_t, 1);
         mbar_init_fence();
     }
+    // constant data (tables, the experts' down pointers) before the wait for
+    // the gate/up kernel: this part overlaps that kernel's tail
+    __shared__ __align__(16) const uint8_t* s_ptr[kPtrMax];
+    const bool stage_ptr = a.experts <= kPtrMax && a.experts % 2 == 0;
+    const uint32_t tab_tx = (DNRole<TD>::kTab != 0 ? DNRole<TD>::kTab + DNRole<TD>::kSign : 0) +
+                            (stage_ptr ? 8u * (uint32_t)a.experts : 0);
     if (routed_role && threadIdx.x == 0) {
         using RL = DNRole<TD>;
+        if (tab_tx != 0) mbar_expect_tx(bar_t, tab_tx);
         if constexpr (RL::kTab != 0) {
             const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
-            mbar_expect_tx(bar_t, RL::kTab + RL::kSign);
             bulk_g2s(base, TD == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
                      RL::kTab, bar_t);
             bulk_g2s(base + RL::kTab, TD == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
                      RL::kSign, bar_t);
         }
+        if (stage_ptr) bulk_g2s((uint32_t)__cvta_generic_to_shared(s_ptr), a.down, 8u * (uint32_t)a.experts, bar_t);
     }
     __syncthreads();
     if (routed_role) {
         grid_dep_wait();  // the routing and h images of the gate/up kernel
-        if constexpr (DNRole<TD>::kTab != 0) {
+        if (tab_tx != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 3, 0);
         }
-        dn_run<TD, true>(a, smem, bar, blockIdx.x * kDNWarps + warp, a.routed_ctas * kDNWarps, false);
+        dn_run<TD, true>(a, smem, bar, blockIdx.x * kDNWarps + warp, a.routed_ctas * kDNWarps, false,
+                         stage_ptr ? s_ptr : nullptr);
     } else {
         // shared expert: its first rows are constant data, requested before
         // the wait for the gate/up kernel's output (inside dn_run)
         dn_run<TSD, false>(a, smem, bar, (blockIdx.x - a.routed_ctas) * kDNWarps + warp,
-                           (gridDim.x - a.routed_ctas) * kDNWarps, true);
+                           (gridDim.x - a.routed_ctas) * kDNWarps, true, nullptr);
     }
 }
 
@@ -1042,7 +1087,8 @@ template <int TG, int TS>
 cudaError_t launch_gut(const MoeGateUpArgs& a, unsigned ctas, cudaStream_t stream) {
     constexpr int kA = GUTRole<TG>::kBytes, kB = GUTRole<TS>::kBytes;
     constexpr size_t smem = kA > kB ? kA : kB;
-    static_assert(smem + 32 * sizeof(lbk_routed) + kGUTWarps * 16 <= (size_t)kMaxSmem, "gate/up stage plan");
+    static_assert(smem + 32 * sizeof(lbk_routed) + kGUTWarps * 16 + 2 * kPtrMax * 8 + 256 <= (size_t)kMaxSmem,
+                  "gate/up stage plan");
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_tma_kernel<TG, TS>));
     if (e != cudaSuccess) return e;
     if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
