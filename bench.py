@@ -52,7 +52,7 @@ def row_bytes(ty: int, k: int) -> int:
     return k // 256 * {TYPE_IQ2_S: 82, TYPE_IQ3_S: 110, TYPE_Q4_K: 144}[ty]
 
 
-# algorithmic bytes per token: router + 8 routed experts + shared
+# algorithmic bytes per token: router + 8 routed experts + shared (weights read once) + x + out
 ROUTER_B = E * H * 4
 GATE_UP_B = K_TOP * 2 * F * row_bytes(TYPE_IQ2_S, H) + 2 * F * row_bytes(TYPE_Q4_K, H)
 DOWN_B = K_TOP * H * row_bytes(TYPE_IQ3_S, F) + H * row_bytes(TYPE_Q4_K, F)

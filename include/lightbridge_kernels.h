@@ -295,6 +295,42 @@ int32_t lbk_moe_layer_trace_read(lbk_moe_layer* layer, float ms[3]);
 int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, const lbk_routed* routed,
                        float* out, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------ expert parallelism */
+
+/* A rank's layer for expert parallelism: w->experts holds this rank's
+ * resident experts, the global experts [first_expert, first_expert +
+ * w->expert_count) of a router (w->router) over global_experts; the router
+ * and the shared expert are whole. Such a layer runs only through lbk_ep_*.
+ * No counterpart in the reference, whose MoE step runs every expert on one
+ * host (bridge-runtime/src/hy3_scalar.rs:561-628). Needs planar layers with
+ * hidden 2048 or 4096. */
+int32_t lbk_ep_layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t global_experts,
+                            uint64_t first_expert, void* stream, lbk_moe_layer** out);
+/* Bytes of one token's Q8_K image as lbk_ep_route writes it and
+ * lbk_ep_items_forward / lbk_ep_combine read it (opaque, 16-byte aligned). */
+int32_t lbk_ep_q8_bytes(const lbk_moe_layer* layer, uint64_t* bytes);
+/* Workspace for lbk_ep_* calls over `count` tokens or items (zero-filled once). */
+int32_t lbk_ep_workspace_bytes(const lbk_moe_layer* layer, uint64_t count, uint64_t* bytes);
+/* Home rank: routing of `tokens` tokens (routed[tokens*k], global expert IDs
+ * in ascending order, as lbk_moe_forward) and their Q8_K images
+ * (q8[tokens * lbk_ep_q8_bytes]). reference: hy3_moe_route_token's router and
+ * route_experts_into (layer.rs:576-603, routing.rs:25-107). */
+int32_t lbk_ep_route(lbk_moe_layer* layer, const float* x, uint64_t tokens, lbk_routed* routed, uint8_t* q8,
+                     void* workspace, uint64_t workspace_bytes, void* stream);
+/* Expert rank: for each item i, the row dots of resident expert
+ * items_routed[i].expert_id (local index; the coefficient is ignored) on the
+ * token image q8_items[i]: dots[i*H + r] = down_r(SwiGLU(gate, up)) before any
+ * coefficient. reference: expert_swiglu_accumulate_into's projection
+ * (activation.rs:104-144). */
+int32_t lbk_ep_items_forward(lbk_moe_layer* layer, const uint8_t* q8_items, const lbk_routed* items_routed,
+                             uint64_t items, float* dots, void* workspace, uint64_t workspace_bytes, void* stream);
+/* Home rank: out[t] = 0; += c_j * routed_dots[t][j] in the routing's order
+ * (ascending ID); += 1.0 * shared(t) -- moe_routed_by_id_into's accept pass
+ * (moe.rs:116-147), bit-identical to lbk_moe_forward on one GPU.
+ * routed_dots: [tokens][k][H] as returned by the expert ranks. */
+int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens, const lbk_routed* routed,
+                       const float* routed_dots, float* out, void* workspace, uint64_t workspace_bytes, void* stream);
+
 /* lbk_moe_forward without a caller workspace and without any allocation: the
  * workspace is a fixed 1 MiB array of this library's device memory, one per
  * device. No counterpart in the reference (its moe_routed_by_id_into takes

@@ -45,11 +45,14 @@ struct lbk_context {
 struct lbk_moe_layer {
     lbk_context* ctx;
     uint64_t E, H, F, k;
+    // Resident routed experts: global IDs [first, first + E_local). A full
+    // layer holds all E; an expert-parallel layer holds its rank's share.
+    uint64_t E_local, first;
     float weight_scale;
     bool fused;
     lbk_moe_weights w;                   // host copy (experts pointer not kept)
     std::vector<lbk_expert> experts;     // host copy of the expert descriptors
-    const uint8_t** d_gate;              // device pointer tables [E]
+    const uint8_t** d_gate;              // device pointer tables [E_local]
     const uint8_t** d_up;
     const uint8_t** d_down;
     int gate_type, down_type, sgate_type, sdown_type;
@@ -195,9 +198,9 @@ uint64_t up256(uint64_t v) { return (v + 255) & ~(uint64_t)255; }
 // across calls of different shapes once it was zero-filled; the other arrival
 // counters ([gate/up h blocks][down combine blocks]) move with the shape and
 // are zeroed by the router kernel of every call.
-WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T) {
+WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T, uint64_t k) {
     WsLayout o{};
-    uint64_t slots = T * (L->k + 1);
+    uint64_t slots = T * (k + 1);
     uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
     o.rcounter = 0;
     o.counters = 16;
@@ -214,7 +217,7 @@ WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T) {
     o.q8x = off;
     off = up256(off + T * nbh * lbk::kQ8IBytes);  // internal Q8_K images
     o.routed = off;
-    off = up256(off + T * L->k * sizeof(lbk_routed));
+    off = up256(off + T * (k ? k : 1) * sizeof(lbk_routed));
     o.h = off;
     off = up256(off + slots * L->F * 4);
     o.hq = off;
@@ -569,7 +572,12 @@ LBK_API int32_t lbk_expert_swiglu_accumulate(lbk_context* ctx, const lbk_expert*
 
 // ------------------------------------------------------------- MoE layer
 
-LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w, void* stream, lbk_moe_layer** out) {
+namespace {
+
+// A layer over the resident experts w->experts[0, expert_count), which are the
+// global experts [first, first + expert_count) of a router over E_route.
+int32_t layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t E_route, uint64_t first, void* stream,
+                     lbk_moe_layer** out) {
     if (out == nullptr || w == nullptr || ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
     *out = nullptr;
     if (w->expert_count == 0 || w->experts == nullptr) return fail(LBK_DIMENSION_MISMATCH, "expert count", 0, 1, 0);
@@ -577,13 +585,16 @@ LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w,
     if (int32_t s = check_matrix(&w->router, "router")) return s;
     if (w->router.type != LBK_TYPE_F32) return fail(LBK_UNSUPPORTED_TYPE, "router must be F32", (uint64_t)w->router.type);
     const uint64_t H = w->shared.gate.input_width, F = w->shared.gate.output_width, E = w->expert_count;
+    if (first > E_route || E > E_route - first)
+        return fail(LBK_DIMENSION_MISMATCH, "resident experts beyond the router's experts", first, E_route, first + E);
     if (w->router.input_width != H) return fail(LBK_DIMENSION_MISMATCH, "router input width", 0, H, w->router.input_width);
-    if (w->router.output_width != E) return fail(LBK_DIMENSION_MISMATCH, "router output width", 0, E, w->router.output_width);
+    if (w->router.output_width != E_route)
+        return fail(LBK_DIMENSION_MISMATCH, "router output width", 0, E_route, w->router.output_width);
     if (w->shared.down.output_width != H) return fail(LBK_DIMENSION_MISMATCH, "MoE output", 0, H, w->shared.down.output_width);
-    if (w->top_k == 0 || w->top_k > E) return fail(LBK_ROUTING_TOPK, "expert_used_count", 0, E, w->top_k);
+    if (w->top_k == 0 || w->top_k > E_route) return fail(LBK_ROUTING_TOPK, "expert_used_count", 0, E_route, w->top_k);
     if (!std::isfinite(w->weight_scale))
         return fail(LBK_NON_FINITE_ROUTING_VALUE, "weight_scale", 0, 0, 0, f32_bits(w->weight_scale));
-    if (E > 1024 || w->top_k > 32) return fail(LBK_INVALID_PARAMETER, "this build routes at most 1024 experts, k <= 32");
+    if (E_route > 1024 || w->top_k > 32) return fail(LBK_INVALID_PARAMETER, "this build routes at most 1024 experts, k <= 32");
     if (w->selection_bias == nullptr) return fail(LBK_INVALID_PARAMETER, "null selection bias");
     if (H % LBK_QK_K != 0 || F % LBK_QK_K != 0) return fail(LBK_DIMENSION_MISMATCH, "Q8_K input width", 0, LBK_QK_K, H);
     for (uint64_t e = 0; e < E; e++) {
@@ -601,7 +612,9 @@ LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w,
 
     auto* L = new lbk_moe_layer{};
     L->ctx = ctx;
-    L->E = E;
+    L->E = E_route;
+    L->E_local = E;
+    L->first = first;
     L->H = H;
     L->F = F;
     L->k = w->top_k;
@@ -682,6 +695,17 @@ LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w,
     return ok();
 }
 
+}  // namespace
+
+LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w, void* stream, lbk_moe_layer** out) {
+    return layer_create(ctx, w, w ? w->expert_count : 0, 0, stream, out);
+}
+
+LBK_API int32_t lbk_ep_layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t global_experts,
+                                    uint64_t first_expert, void* stream, lbk_moe_layer** out) {
+    return layer_create(ctx, w, global_experts, first_expert, stream, out);
+}
+
 LBK_API int32_t lbk_moe_layer_trace(lbk_moe_layer* layer, int32_t enable) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
     if (int32_t s = set_device(layer->ctx)) return s;
@@ -721,7 +745,7 @@ LBK_API int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer) { return layer &
 LBK_API int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes) {
     if (layer == nullptr || bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
     if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
-    *bytes = moe_ws(layer, tokens).total;
+    *bytes = moe_ws(layer, tokens, layer->k).total;
     return ok();
 }
 
@@ -755,14 +779,33 @@ long split_roles(unsigned ctas, int warps, double work_r, double fixed_r, double
     return best;
 }
 
+// What one fused expert stage computes.
+struct MoeMode {
+    uint64_t k;          // routed slots per token (the routing holds tokens * k entries)
+    bool shared;         // also the shared expert (slot k)
+    bool combine;        // form `out`; else leave the row dots in `dots`
+    const uint8_t* q8x;  // the tokens' Q8_K images (null: the workspace's, from the router kernel)
+    float* dots;         // row dots [T][dots_slots][H] (null: the workspace's)
+    uint32_t dots_slots;
+};
+
+MoeMode full_mode(const lbk_moe_layer* L) { return MoeMode{L->k, true, true, nullptr, nullptr, (uint32_t)(L->k + 1)}; }
+
 // Expert stage of one MoE call for `tokens` tokens with routing in `routed`.
 // With defer_topk (single token, fused kernels) the routing is computed by the
 // gate/up kernel from the router's chunk partials and stored into `routed`.
+// A mode other than the full one (expert-parallel items and shared-expert
+// passes) needs the bulk-copy kernels.
 int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_routed* routed, float* out, uint8_t* ws,
-                    const WsLayout& o, cudaStream_t st, bool defer_topk = false) {
+                    const WsLayout& o, cudaStream_t st, bool defer_topk, const MoeMode& mode) {
     lbk_context* ctx = L->ctx;
     cudaError_t e = cudaSuccess;
     const uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
+    const uint64_t K = mode.k;
+    const bool full = mode.shared && mode.combine && K == L->k && mode.q8x == nullptr && mode.dots == nullptr;
+    if (!full && !(L->fused && lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)nbh) &&
+                   lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)))
+        return fail(LBK_INVALID_PARAMETER, "expert-parallel calls need planar layers with hidden 2048 or 4096");
     if (L->fused) {
         lbk::MoeGateUpArgs g{};
         g.defer_topk = defer_topk ? 1 : 0;
@@ -778,14 +821,15 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         int slots_unused = 0;
         lbk::gemv_plan(L->gate_type, (int)nbh, &g.tpr_h, &slots_unused);
         g.tokens = T;
-        g.k = L->k;
-        g.experts = L->E;
+        g.k = K;
+        g.experts = L->E_local;
         g.gate = L->d_gate;
         g.up = L->d_up;
         g.sgate = static_cast<const uint8_t*>(L->w.shared.gate.data);
         g.sup = static_cast<const uint8_t*>(L->w.shared.up.data);
         g.routed = routed;
-        g.q8x = ws + o.q8x;
+        g.q8x = mode.q8x ? mode.q8x : ws + o.q8x;
+        g.has_shared = mode.shared ? 1 : 0;
         g.h = reinterpret_cast<float*>(ws + o.h);
         g.hq = ws + o.hq;
         g.counters = reinterpret_cast<unsigned int*>(ws + o.counters);
@@ -797,22 +841,24 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             // end together, then spread each role's rows over its warps.
             const unsigned ctas = (unsigned)ctx->sm_count;
             const double hb = 2.0 * nbh * 2.0 * L->F;  // half blocks of one slot (gate + up)
-            const long rc = split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * L->k * hb * hb_cost_us(L->gate_type),
-                                        defer_topk ? 5.0 : 1.5, T * hb * hb_cost_us(L->sgate_type), 1.0);
+            const long rc = K == 0 ? 0
+                            : !mode.shared ? (long)ctas
+                                           : split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * K * hb * hb_cost_us(L->gate_type),
+                                                         defer_topk ? 5.0 : 1.5, T * hb * hb_cost_us(L->sgate_type), 1.0);
             g.routed_ctas = (uint32_t)rc;
-            if (T <= 4 && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
+            if (full && T <= 4 && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
                 g.down = L->d_down;
                 g.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);
                 g.down_rs = (uint32_t)((nbf * block_bytes(L->down_type) + 15) & ~(uint64_t)15);
                 g.sdown_rs = (uint32_t)((nbf * block_bytes(L->sdown_type) + 15) & ~(uint64_t)15);
             }
             auto chunk_for = [&](uint64_t warps, uint64_t instances) {
-                uint64_t per = warps / instances;
+                uint64_t per = instances ? warps / instances : 1;
                 per = per < 1 ? 1 : per;
                 uint64_t c = (L->F + per - 1) / per;
                 return (c + rps - 1) / rps * rps;
             };
-            g.chunk_r = chunk_for((uint64_t)rc * lbk::kMoeGateUpTmaWarps, T * L->k);
+            g.chunk_r = chunk_for((uint64_t)rc * lbk::kMoeGateUpTmaWarps, T * K);
             g.chunk_s = chunk_for((uint64_t)(ctas - rc) * lbk::kMoeGateUpTmaWarps, T);
             g.chunks_r = (L->F + g.chunk_r - 1) / g.chunk_r;
             g.chunks_s = (L->F + g.chunk_s - 1) / g.chunk_s;
@@ -866,8 +912,8 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         d.nb_f = (int)nbf;
         lbk::gemv_plan(L->down_type, (int)nbf, &d.tpr_f, &slots_unused);
         d.tokens = T;
-        d.k = L->k;
-        d.experts = L->E;
+        d.k = K;
+        d.experts = L->E_local;
         d.down = L->d_down;
         d.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);
         d.routed = routed;
@@ -880,21 +926,26 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             // role's rows over its warps (chunks in whole steps of 32 / tpr rows).
             const unsigned ctas = (unsigned)ctx->sm_count;
             const double lanes = (double)L->H * d.tpr_f;  // lane slots of one slot's rows
-            const long rc = split_roles(ctas, lbk::kMoeDownTmaWarps, T * L->k * lanes * hb_cost_us(L->down_type), 4.0,
-                                        T * lanes * hb_cost_us(L->sdown_type), 1.5);
+            const long rc = K == 0 ? 0
+                            : !mode.shared ? (long)ctas
+                                           : split_roles(ctas, lbk::kMoeDownTmaWarps, T * K * lanes * hb_cost_us(L->down_type),
+                                                         4.0, T * lanes * hb_cost_us(L->sdown_type), 1.5);
             d.routed_ctas = (uint32_t)rc;
             const uint64_t R = 32 / d.tpr_f;
             auto chunk_for = [&](uint64_t warps, uint64_t instances) {
-                uint64_t per = warps / instances;
+                uint64_t per = instances ? warps / instances : 1;
                 per = per < 1 ? 1 : per;
                 uint64_t c = (L->H + per - 1) / per;
                 return (c + R - 1) / R * R;
             };
-            d.chunk_r = chunk_for((uint64_t)rc * lbk::kMoeDownTmaWarps, T * L->k);
+            d.chunk_r = chunk_for((uint64_t)rc * lbk::kMoeDownTmaWarps, T * K);
             d.chunk_s = chunk_for((uint64_t)(ctas - rc) * lbk::kMoeDownTmaWarps, T);
             d.chunks_r = (L->H + d.chunk_r - 1) / d.chunk_r;
             d.chunks_s = (L->H + d.chunk_s - 1) / d.chunk_s;
-            d.dots = reinterpret_cast<float*>(ws + o.dots);
+            d.dots = mode.dots ? mode.dots : reinterpret_cast<float*>(ws + o.dots);
+            d.dots_slots = mode.dots_slots;
+            d.combine = mode.combine ? 1 : 0;
+            d.has_shared = mode.shared ? 1 : 0;
             d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
             e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
             if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
@@ -952,9 +1003,10 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
                                 lbk_routed* routed_out, int32_t router_mode, void* workspace, uint64_t workspace_bytes,
                                 void* stream) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (layer->E_local != layer->E) return fail(LBK_INVALID_PARAMETER, "an expert-parallel layer runs through lbk_ep_*");
     if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
     if (router_mode != LBK_ROUTER_SEQUENTIAL && router_mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "router mode");
-    WsLayout o = moe_ws(layer, tokens);
+    WsLayout o = moe_ws(layer, tokens, layer->k);
     if (workspace_bytes < o.total) return fail(LBK_SCRATCH_TOO_SMALL, "MoE workspace", 0, o.total, workspace_bytes);
     if (x == nullptr || out == nullptr || workspace == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
     if (!aligned(x, 16) || !aligned(workspace, 256)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
@@ -1007,7 +1059,7 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
         }
     }
     if (layer->tracing) trace_record(layer->trace[1], st, cudaEventRecordExternal);
-    int32_t s = moe_experts(layer, x, tokens, routed, out, ws, o, st, defer);
+    int32_t s = moe_experts(layer, x, tokens, routed, out, ws, o, st, defer, full_mode(layer));
     if (s == LBK_OK && layer->tracing && !layer->fused) {
         trace_record(layer->trace[2], st, cudaEventRecordExternal);
         trace_record(layer->trace[3], st, cudaEventRecordExternal);
@@ -1018,8 +1070,9 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
 LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, const lbk_routed* routed,
                                float* out, void* workspace, uint64_t workspace_bytes, void* stream) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (layer->E_local != layer->E) return fail(LBK_INVALID_PARAMETER, "an expert-parallel layer runs through lbk_ep_*");
     if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "selected routed expert count", 0, 1, 0);
-    WsLayout o = moe_ws(layer, tokens);
+    WsLayout o = moe_ws(layer, tokens, layer->k);
     if (workspace_bytes < o.total) return fail(LBK_SCRATCH_TOO_SMALL, "MoE workspace", 0, o.total, workspace_bytes);
     if (x == nullptr || out == nullptr || workspace == nullptr || routed == nullptr)
         return fail(LBK_INVALID_PARAMETER, "null pointer");
@@ -1043,7 +1096,123 @@ LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t to
         cudaError_t e = lbk::launch_router_fused(q, ctx->sm_count, st);
         if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
     }
-    return moe_experts(layer, x, tokens, routed, out, ws, o, st);
+    return moe_experts(layer, x, tokens, routed, out, ws, o, st, false, full_mode(layer));
+}
+
+// --------------------------------------------------- expert parallelism
+//
+// A rank's layer (lbk_ep_layer_create) holds the whole router and the shared
+// expert, and only its share of the routed experts. The MoE step of a token
+// becomes: route on the token's home rank (lbk_ep_route: routing + Q8_K
+// image); send each (token, slot) whose expert lives elsewhere to that rank;
+// there, lbk_ep_items_forward computes the expert's row dots (down(SwiGLU(..))
+// before the coefficient); send the dots home; lbk_ep_combine adds the shared
+// expert and combines in ascending expert ID, the single-GPU order, so the
+// result is bit-identical to lbk_moe_forward on one GPU.
+
+namespace {
+
+int32_t ep_check(const lbk_moe_layer* layer, uint64_t n, const void* ws, uint64_t ws_bytes, uint64_t need) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (n == 0) return fail(LBK_DIMENSION_MISMATCH, "token / item count", 0, 1, 0);
+    if (ws_bytes < need) return fail(LBK_SCRATCH_TOO_SMALL, "expert-parallel workspace", 0, need, ws_bytes);
+    if (ws == nullptr || !aligned(ws, 256)) return fail(LBK_INVALID_PARAMETER, "workspace null or not 256-byte aligned");
+    if (!layer->fused || !lbk::moe_gate_up_tma_supported(layer->gate_type, layer->sgate_type, (int)(layer->H / LBK_QK_K)) ||
+        !lbk::moe_down_tma_supported(layer->down_type, layer->sdown_type, (int)(layer->F / LBK_QK_K)))
+        return fail(LBK_INVALID_PARAMETER, "expert parallelism needs planar layers with hidden 2048 or 4096");
+    return LBK_OK;
+}
+
+uint64_t ep_ws_bytes(const lbk_moe_layer* L, uint64_t n) {
+    uint64_t a = moe_ws(L, n, L->k).total, b = moe_ws(L, n, 1).total, c = moe_ws(L, n, 0).total + n * L->H * 4;
+    uint64_t m = a > b ? a : b;
+    return m > c ? m : c;
+}
+
+}  // namespace
+
+LBK_API int32_t lbk_ep_q8_bytes(const lbk_moe_layer* layer, uint64_t* bytes) {
+    if (layer == nullptr || bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    *bytes = layer->H / LBK_QK_K * lbk::kQ8IBytes;
+    return ok();
+}
+
+LBK_API int32_t lbk_ep_workspace_bytes(const lbk_moe_layer* layer, uint64_t count, uint64_t* bytes) {
+    if (layer == nullptr || bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (count == 0) return fail(LBK_DIMENSION_MISMATCH, "token / item count", 0, 1, 0);
+    *bytes = ep_ws_bytes(layer, count);
+    return ok();
+}
+
+LBK_API int32_t lbk_ep_route(lbk_moe_layer* layer, const float* x, uint64_t tokens, lbk_routed* routed, uint8_t* q8,
+                             void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (int32_t s = ep_check(layer, tokens, workspace, workspace_bytes, ep_ws_bytes(layer, tokens))) return s;
+    if (x == nullptr || routed == nullptr || q8 == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(x, 16) || !aligned(q8, 16)) return fail(LBK_INVALID_PARAMETER, "x / q8 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    const WsLayout o = moe_ws(layer, tokens, layer->k);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    lbk::RouterFusedArgs f{};
+    f.r.w = static_cast<const float*>(layer->w.router.data);
+    f.r.x = x;
+    f.r.logits = reinterpret_cast<float*>(ws + o.logits);
+    f.r.hidden = layer->H;
+    f.r.experts = layer->E;
+    f.r.tokens = tokens;
+    f.r.status = ctx->status;
+    f.partials = reinterpret_cast<float*>(ws + o.partials);
+    f.q8x = q8;
+    f.counter = reinterpret_cast<unsigned int*>(ws + o.rcounter);
+    f.bias = layer->w.selection_bias;
+    f.k = (uint32_t)layer->k;
+    f.weight_scale = layer->weight_scale;
+    f.routed = routed;
+    cudaError_t e = lbk::launch_router_fused(f, ctx->sm_count, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "router launch");
+}
+
+LBK_API int32_t lbk_ep_items_forward(lbk_moe_layer* layer, const uint8_t* q8_items, const lbk_routed* items_routed,
+                                     uint64_t items, float* dots, void* workspace, uint64_t workspace_bytes,
+                                     void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (int32_t s = ep_check(layer, items, workspace, workspace_bytes, ep_ws_bytes(layer, items))) return s;
+    if (q8_items == nullptr || items_routed == nullptr || dots == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(q8_items, 16) || !aligned(dots, 16)) return fail(LBK_INVALID_PARAMETER, "q8 / dots 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    const WsLayout o = moe_ws(layer, items, 1);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
+    if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+    // one routed slot per item, the expert ID local to this layer; no shared expert, no combine
+    return moe_experts(layer, nullptr, items, items_routed, nullptr, ws, o, st, false,
+                       MoeMode{1, false, false, q8_items, dots, 1});
+}
+
+LBK_API int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens, const lbk_routed* routed,
+                               const float* routed_dots, float* out, void* workspace, uint64_t workspace_bytes,
+                               void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (int32_t s = ep_check(layer, tokens, workspace, workspace_bytes, ep_ws_bytes(layer, tokens))) return s;
+    if (q8 == nullptr || routed == nullptr || routed_dots == nullptr || out == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(q8, 16)) return fail(LBK_INVALID_PARAMETER, "q8 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    const WsLayout o = moe_ws(layer, tokens, 0);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* shared_dots = reinterpret_cast<float*>(ws + o.total);  // [tokens][H] after the pass's own workspace
+    cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
+    if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+    if (int32_t s = moe_experts(layer, nullptr, tokens, routed, nullptr, ws, o, st, false,
+                                MoeMode{0, true, false, q8, shared_dots, 1}))
+        return s;
+    e = lbk::launch_ep_combine(routed, routed_dots, shared_dots, out, tokens, layer->k, layer->H, ctx->status, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "combine launch");
 }
 
 // ------------------------------------------------- MoE forward, no allocation
@@ -1100,7 +1269,7 @@ LBK_API int32_t lbk_moe_forward_no_alloc(lbk_moe_layer* layer, const float* x, u
                                          lbk_routed* routed_out, int32_t router_mode, void* stream) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
     if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
-    const uint64_t need = moe_ws(layer, tokens).total;
+    const uint64_t need = moe_ws(layer, tokens, layer->k).total;
     if (need > kStaticScratchBytes)
         return fail(LBK_SCRATCH_TOO_SMALL,
                     "static MoE scratch (1 MiB) is smaller than this layer's workspace for this token count; "

@@ -38,7 +38,9 @@ struct MoeGateUpArgs {
     float weight_scale;
     lbk_routed* routed_store;        // CTA 0 writes the routing here
     // bulk-copy-staged kernel: CTAs [0, routed_ctas) stream routed slots, the rest the shared expert
+    // (no CTA does when has_shared is 0)
     uint32_t routed_ctas;
+    int has_shared;
     // down matrices of the layer, prefetched into L2 once the routing is known
     // (null: no prefetch); row strides of the planar down matrices
     const uint8_t* const* down;
@@ -68,7 +70,10 @@ struct MoeDownArgs {
     // rest the shared expert; items (token, slot, chunk of rows)
     uint32_t routed_ctas;
     uint64_t chunk_r, chunk_s, chunks_r, chunks_s;
-    float* dots;                     // [tokens][k+1][hidden] row dots
+    float* dots;                     // [tokens][dots_slots][hidden] row dots of slot (routed j < k, shared k)
+    uint32_t dots_slots;
+    int combine;                     // 1: form `out` from the dots (else leave the dots)
+    int has_shared;                  // 0: no shared-expert CTAs
     unsigned int* counters;          // [tokens][hidden/64] arrivals, zero between launches
     DeviceStatus* status;
     Tables tables;
@@ -88,6 +93,9 @@ bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks
 cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
                                    cudaStream_t stream);
 cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownArgs& a, cudaStream_t stream);
+// Expert-parallel combine of routed row dots [tokens][k][H] and shared row dots [tokens][H].
+cudaError_t launch_ep_combine(const lbk_routed* routed, const float* routed_dots, const float* shared_dots, float* out,
+                              uint64_t tokens, uint64_t k, uint64_t H, DeviceStatus* status, cudaStream_t stream);
 // Bulk-copy-staged down over `ctas` CTAs (planar, nb_f <= 16).
 bool moe_down_tma_supported(int down_type, int shared_down_type, int nb_f);
 cudaError_t launch_moe_down_tma(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,

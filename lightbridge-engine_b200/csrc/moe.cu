@@ -954,7 +954,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             dep_wait = false;
             load_act();
         }
-        float* drow = a.dots + ((uint64_t)t * (a.k + 1) + slot) * H;
+        float* drow = a.dots + ((uint64_t)t * a.dots_slots + slot) * H;
         uint32_t rb = r0;
 #pragma unroll 1
         for (uint32_t u = 0; u < units; u++) {
@@ -996,7 +996,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
                 rb = rn;
             }
         }
-        dn_arrive_and_combine(a, t, r0, r1);
+        if (a.combine) dn_arrive_and_combine(a, t, r0, r1);
     }
 }
 
@@ -1091,7 +1091,8 @@ cudaError_t launch_gut(const MoeGateUpArgs& a, unsigned ctas, cudaStream_t strea
                   "gate/up stage plan");
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_tma_kernel<TG, TS>));
     if (e != cudaSuccess) return e;
-    if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
+    // every role with work has CTAs: routed when k > 0, shared when present
+    if ((a.k > 0) != (a.routed_ctas > 0) || (a.has_shared != 0) != (a.routed_ctas < ctas)) return cudaErrorInvalidValue;
     return launch_dependent(moe_gate_up_tma_kernel<TG, TS>, ctas, kGUTThreads, smem, stream, a);
 }
 
@@ -1116,7 +1117,30 @@ __global__ void swiglu_kernel(const float* gate, const float* up, float* h, uint
     }
 }
 
+// Expert-parallel combine on the home GPU: out = 0; += c_j * dot_j over the
+// token's routed slots in ascending ID (the routing's order); += 1.0 * shared
+// (moe.rs:331-336), unless validation failed upstream.
+__global__ void ep_combine_kernel(const lbk_routed* routed, const float* routed_dots, const float* shared_dots,
+                                  float* out, uint64_t tokens, uint64_t k, uint64_t H, DeviceStatus* st) {
+    if (status_set(st)) return;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t t = i / H, r = i % H;
+        float acc = 0.0f;
+        for (uint64_t j = 0; j < k; j++)
+            acc = __fadd_rn(acc, __fmul_rn(routed[t * k + j].coefficient, routed_dots[(t * k + j) * H + r]));
+        out[i] = __fadd_rn(acc, __fmul_rn(1.0f, shared_dots[i]));
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_ep_combine(const lbk_routed* routed, const float* routed_dots, const float* shared_dots, float* out,
+                              uint64_t tokens, uint64_t k, uint64_t H, DeviceStatus* status, cudaStream_t stream) {
+    uint64_t grid = (tokens * H + 255) / 256;
+    if (grid > 4096) grid = 4096;
+    ep_combine_kernel<<<(unsigned)grid, 256, 0, stream>>>(routed, routed_dots, shared_dots, out, tokens, k, H, status);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_swiglu(const float* gate, const float* up, float* h, uint64_t n, DeviceStatus* status,
                           cudaStream_t stream) {
@@ -1177,7 +1201,8 @@ cudaError_t launch_dnt(const MoeDownArgs& a, unsigned ctas, cudaStream_t stream)
     static_assert(smem + kDNWarps * 16 + 8 <= (size_t)kMaxSmem, "down stage plan");
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_down_tma_kernel<TD, TSD>));
     if (e != cudaSuccess) return e;
-    if (a.routed_ctas == 0 || a.routed_ctas >= ctas) return cudaErrorInvalidValue;
+    if ((a.k > 0) != (a.routed_ctas > 0) || (a.has_shared != 0) != (a.routed_ctas < ctas)) return cudaErrorInvalidValue;
+    if (a.combine && !a.has_shared) return cudaErrorInvalidValue;
     return launch_dependent(moe_down_tma_kernel<TD, TSD>, ctas, kDNThreads, smem, stream, a);
 }
 

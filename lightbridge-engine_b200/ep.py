@@ -1,0 +1,197 @@
+"""Expert-parallel routed-MoE layer over torch.distributed, one process per GPU.
+
+Experts are sharded in contiguous ranges: with E global experts over `world`
+ranks, rank r holds global experts [r * E_r, (r + 1) * E_r), E_r = E / world
+(24 per GPU for 192 experts on 8 GPUs). The router and the shared expert are
+whole on every rank. Each rank owns its own tokens (their home rank). One
+layer step for a home rank's T tokens:
+
+1. route (lbk_ep_route): the top-k routing in ascending expert-ID order and
+   the tokens' Q8_K images, on the home rank;
+2. dispatch: every (token, slot) pair travels to the rank owning its expert as
+   one row [Q8_K image | local expert ID]; the per-peer counts go first (an
+   all-to-all of `world` integers), then the rows (all_to_all_single with those
+   splits);
+3. items_forward (lbk_ep_items_forward) on every rank over the rows it
+   received: the raw row dots down(SwiGLU(gate, up)) of each item;
+4. return: the dots travel back with the splits reversed and land at
+   routed_dots[t * k + j];
+5. combine (lbk_ep_combine) on the home rank: the coefficient-weighted sum in
+   ascending expert-ID order, then the shared expert, the one-GPU order of
+   moe_routed_by_id_into's accept pass (bridge-kernels-reference/src/moe.rs:116-147),
+   so the output is bit-identical to lbk_moe_forward on one GPU.
+
+Partial sums are never all-reduced across ranks: that would change the f32
+summation order. The reference runs every expert of a layer on one host
+(bridge-runtime/src/hy3_scalar.rs:561-628); this module has no counterpart
+there.
+
+The compute stages are the methods of `layer` (lbk.EpLayer on a GPU: route,
+items_forward, combine, q8_bytes, workspace_bytes). Every rank takes the same
+collective steps in the same order, also with no tokens of its own or no items
+to compute.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+# bytes after the Q8_K image in a dispatch row: the local expert ID (int32),
+# padded so that rows keep the image's 16-byte alignment
+ROW_HEADER_BYTES = 16
+
+
+@dataclass
+class DispatchPlan:
+    """Where the (token, slot) pairs of one home rank go.
+
+    order: pair indices (t * k + j) sorted by owning rank, stable, so each
+    peer's rows keep ascending pair order; send / recv: rows per peer."""
+
+    order: torch.Tensor
+    owner: torch.Tensor
+    send: list[int]
+    recv: list[int]
+
+
+def _world(group) -> tuple[int, int]:
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _owners(ids: torch.Tensor, experts_per_rank: int, world: int):
+    owner = ids.to(torch.int64) // experts_per_rank
+    order = torch.argsort(owner, stable=True)
+    send = torch.bincount(owner, minlength=world)
+    if send.numel() != world:
+        raise ValueError(f"routed expert ID beyond {world} ranks x {experts_per_rank} experts")
+    return owner, order, send
+
+
+def local_plan(ids: torch.Tensor, experts_per_rank: int, world: int) -> DispatchPlan:
+    """The plan without a count exchange (recv = send): for one process that
+    hands every rank's rows out itself."""
+    owner, order, send = _owners(ids, experts_per_rank, world)
+    s = send.cpu().tolist()
+    return DispatchPlan(order, owner, s, list(s))
+
+
+def plan_dispatch(ids: torch.Tensor, experts_per_rank: int, world: int, group=None) -> DispatchPlan:
+    """Owner rank of every routed pair and the per-peer row counts (one
+    all-to-all of `world` counts, then one device-to-host read of 2 * world
+    integers for the split sizes of the row exchanges)."""
+    owner, order, send = _owners(ids, experts_per_rank, world)
+    recv = torch.empty_like(send)
+    if world > 1:
+        dist.all_to_all_single(recv, send, group=group)
+    else:
+        recv.copy_(send)
+    counts = torch.cat([send, recv]).cpu().tolist()
+    return DispatchPlan(order, owner, counts[:world], counts[world:])
+
+
+def pack_rows(q8: torch.Tensor, ids: torch.Tensor, plan: DispatchPlan, k: int, experts_per_rank: int) -> torch.Tensor:
+    """Dispatch rows in plan order: [Q8_K image of the pair's token | local
+    expert ID (int32) | zero pad]."""
+    n = plan.order.numel()
+    q8b = q8.shape[1]
+    rows = torch.zeros((n, q8b + ROW_HEADER_BYTES), dtype=torch.uint8, device=q8.device)
+    if n == 0:
+        return rows
+    rows[:, :q8b] = q8.index_select(0, plan.order // k)
+    local = (ids.to(torch.int64).index_select(0, plan.order) - plan.owner.index_select(0, plan.order) * experts_per_rank)
+    rows[:, q8b:q8b + 4] = local.to(torch.int32).unsqueeze(1).view(torch.uint8)
+    return rows
+
+
+def unpack_items(rows: torch.Tensor, q8_bytes: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Received rows -> (contiguous Q8_K images [n][q8_bytes], lbk_routed items
+    [n][2] int32 with the local expert ID and a zero coefficient)."""
+    n = rows.shape[0]
+    q8_items = rows[:, :q8_bytes].contiguous()
+    items = torch.zeros((n, 2), dtype=torch.int32, device=rows.device)
+    if n:
+        items[:, 0] = rows[:, q8_bytes:q8_bytes + 4].contiguous().view(torch.int32).view(-1)
+    return q8_items, items
+
+
+def exchange(rows: torch.Tensor, send: list[int], recv: list[int], world: int, group=None) -> torch.Tensor:
+    """all_to_all_single of `rows` (first dimension split by `send`) into a new
+    tensor split by `recv`; a copy on one rank."""
+    out = rows.new_empty((sum(recv),) + tuple(rows.shape[1:]))
+    if world > 1:
+        dist.all_to_all_single(out, rows, output_split_sizes=recv, input_split_sizes=send, group=group)
+    else:
+        out.copy_(rows)
+    return out
+
+
+def place_returned(back: torch.Tensor, plan: DispatchPlan, pairs: int, hidden: int) -> torch.Tensor:
+    """Returned dots (plan order) -> routed_dots [pairs][hidden] in pair order."""
+    routed_dots = back.new_empty((pairs, hidden))
+    if pairs:
+        routed_dots.index_copy_(0, plan.order, back)
+    return routed_dots
+
+
+class ExpertParallelMoe:
+    """One rank of an expert-parallel MoE layer.
+
+    layer: this rank's compute stages (lbk.EpLayer), holding the global
+    experts [rank * E_r, (rank + 1) * E_r). group: the process group of the
+    expert-parallel ranks (None: the default group; one rank without
+    torch.distributed)."""
+
+    def __init__(self, layer, group=None):
+        self.layer = layer
+        self.group = group
+        self.world, self.rank = _world(group)
+        E = layer.global_experts
+        if E % self.world:
+            raise ValueError(f"{E} experts do not shard evenly over {self.world} ranks")
+        self.experts_per_rank = E // self.world
+        if layer.local_experts != self.experts_per_rank or layer.first_expert != self.rank * self.experts_per_rank:
+            raise ValueError(
+                f"rank {self.rank} must hold experts [{self.rank * self.experts_per_rank}, "
+                f"{(self.rank + 1) * self.experts_per_rank}), has [{layer.first_expert}, "
+                f"{layer.first_expert + layer.local_experts})"
+            )
+        self._ws = None
+
+    def workspace(self, count: int, device) -> torch.Tensor:
+        """A zero-filled workspace for `count` tokens or items, grown on demand
+        and reused (one zero fill at creation keeps it valid for every count)."""
+        need = self.layer.workspace_bytes(max(count, 1))
+        if self._ws is None or self._ws.numel() < need or self._ws.device != torch.device(device):
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=device)
+        return self._ws
+
+    def forward(self, x: torch.Tensor, tokens: int, out: torch.Tensor, routed_out: torch.Tensor | None = None) -> None:
+        """out[tokens * hidden] = the MoE layer on this rank's tokens x[tokens *
+        hidden]. Collective: every rank of the group calls it once per layer
+        step, with tokens >= 0."""
+        L = self.layer
+        k, H, q8b = L.top_k, L.hidden, L.q8_bytes
+        dev = x.device
+        routed = torch.empty((tokens * k, 2), dtype=torch.int32, device=dev)
+        q8 = torch.empty((tokens, q8b), dtype=torch.uint8, device=dev)
+        if tokens:
+            L.route(x, tokens, routed, q8, self.workspace(tokens, dev))
+        ids = routed[:, 0]
+        plan = plan_dispatch(ids, self.experts_per_rank, self.world, self.group)
+        rows = exchange(pack_rows(q8, ids, plan, k, self.experts_per_rank), plan.send, plan.recv, self.world, self.group)
+        n = rows.shape[0]
+        dots = torch.empty((n, H), dtype=torch.float32, device=dev)
+        if n:
+            q8_items, items = unpack_items(rows, q8b)
+            L.items_forward(q8_items, items, n, dots, self.workspace(n, dev))
+        back = exchange(dots, plan.recv, plan.send, self.world, self.group)
+        routed_dots = place_returned(back, plan, tokens * k, H)
+        if tokens:
+            L.combine(q8, tokens, routed, routed_dots, out, self.workspace(tokens, dev))
+        if routed_out is not None and tokens:
+            routed_out.view(torch.int32).view(-1)[: tokens * k * 2].copy_(routed.view(-1))

@@ -123,6 +123,12 @@ def _load() -> ctypes.CDLL:
         "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
         "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
         "lbk_moe_forward_no_alloc": ([P, P, U64, P, P, I32, P], I32),
+        "lbk_ep_layer_create": ([P, ctypes.POINTER(MoeWeights), U64, U64, P, ctypes.POINTER(P)], I32),
+        "lbk_ep_q8_bytes": ([P, ctypes.POINTER(U64)], I32),
+        "lbk_ep_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
+        "lbk_ep_route": ([P, P, U64, P, P, P, U64, P], I32),
+        "lbk_ep_items_forward": ([P, P, P, U64, P, P, U64, P], I32),
+        "lbk_ep_combine": ([P, P, U64, P, P, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
         "lbk_repack": ([P, PM, P, U64, P], I32),
@@ -143,7 +149,8 @@ EXPORTED = (
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
     "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused "
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
-    "lbk_moe_layer_trace_read "
+    "lbk_moe_layer_trace_read lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
+    "lbk_ep_items_forward lbk_ep_combine "
     "lbk_repack lbk_unpack lbk_validate_matrix"
 ).split()
 
@@ -295,3 +302,51 @@ class MoeLayer:
         if self.ptr:
             lib.lbk_moe_layer_destroy(self.ptr)
             self.ptr = None
+
+
+class EpLayer(MoeLayer):
+    """One rank's share of an expert-parallel MoE layer (lbk_ep_layer_create):
+    `experts` are the global experts [first_expert, first_expert + len) of a
+    router over `global_experts`; the router and the shared expert are whole."""
+
+    def __init__(self, ctx: Context, experts: list[Expert], shared: Expert, router: Matrix, bias, top_k: int,
+                 weight_scale: float, global_experts: int, first_expert: int, stream=None):
+        self.ctx = ctx
+        self._experts = (Expert * len(experts))(*experts)
+        self._w = MoeWeights(
+            ctypes.cast(self._experts, ctypes.POINTER(Expert)), len(experts), shared, router, bias.data_ptr(), top_k,
+            float(weight_scale),
+        )
+        self._keep = [bias]
+        p = ctypes.c_void_p()
+        check(lib.lbk_ep_layer_create(ctx.ptr, ctypes.byref(self._w), global_experts, first_expert, _stream(stream),
+                                      ctypes.byref(p)))
+        self.ptr = p
+        self.top_k = top_k
+        self.hidden = shared.gate.input_width
+        self.global_experts = global_experts
+        self.first_expert = first_expert
+        self.local_experts = len(experts)
+
+    @property
+    def q8_bytes(self) -> int:
+        n = ctypes.c_uint64()
+        check(lib.lbk_ep_q8_bytes(self.ptr, ctypes.byref(n)))
+        return n.value
+
+    def workspace_bytes(self, count: int) -> int:
+        n = ctypes.c_uint64()
+        check(lib.lbk_ep_workspace_bytes(self.ptr, count, ctypes.byref(n)))
+        return n.value
+
+    def route(self, x, tokens: int, routed, q8, workspace, stream=None) -> None:
+        check(lib.lbk_ep_route(self.ptr, _ptr(x), tokens, _ptr(routed), _ptr(q8), _ptr(workspace), workspace.numel(),
+                               _stream(stream)))
+
+    def items_forward(self, q8_items, items_routed, items: int, dots, workspace, stream=None) -> None:
+        check(lib.lbk_ep_items_forward(self.ptr, _ptr(q8_items), _ptr(items_routed), items, _ptr(dots), _ptr(workspace),
+                                       workspace.numel(), _stream(stream)))
+
+    def combine(self, q8, tokens: int, routed, routed_dots, out, workspace, stream=None) -> None:
+        check(lib.lbk_ep_combine(self.ptr, _ptr(q8), tokens, _ptr(routed), _ptr(routed_dots), _ptr(out),
+                                 _ptr(workspace), workspace.numel(), _stream(stream)))

@@ -1,0 +1,233 @@
+"""Expert parallelism: the dispatch / return plumbing of ep.ExpertParallelMoe
+(host logic on gloo ranks, world size 2) and, on a GPU, lbk_ep_* against
+lbk_moe_forward bit for bit -- one rank, two ranks simulated on one GPU, and
+real nccl ranks when the box has two GPUs.
+
+The reference runs every expert of a layer on one host
+(bridge-runtime/src/hy3_scalar.rs:561-628); the expert-parallel result must
+equal that single-host combine (bridge-kernels-reference/src/moe.rs:116-147)
+exactly, so every GPU check here is bit-exact, not a tolerance.
+"""
+
+import os
+import pathlib
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+import ep
+
+REPO = pathlib.Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _torchrun(nproc: int, mode: str, timeout: int) -> subprocess.CompletedProcess:
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
+           "--master-addr=127.0.0.1", f"--master-port={_free_port()}", str(REPO / "tests" / "ep_worker.py"),
+           "--mode", mode]
+    env = dict(os.environ, OMP_NUM_THREADS="1", NCCL_NVLS_ENABLE="0")
+    return subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+
+
+# ----------------------------------------------------------------- host logic
+
+
+def test_plan_orders_pairs_by_owner_stably():
+    ids = torch.tensor([5, 1, 7, 0, 2, 6, 3, 4], dtype=torch.int32)
+    plan = ep.local_plan(ids, experts_per_rank=2, world=4)
+    assert plan.send == [2, 2, 2, 2] and plan.recv == plan.send
+    assert plan.order.tolist() == [1, 3, 4, 6, 0, 7, 2, 5]
+    assert plan.owner.tolist() == [2, 0, 3, 0, 1, 3, 1, 2]
+
+
+def test_plan_rejects_expert_beyond_the_ranks():
+    with pytest.raises(ValueError):
+        ep.local_plan(torch.tensor([0, 9], dtype=torch.int32), experts_per_rank=2, world=4)
+
+
+def test_rows_round_trip_and_returned_dots_land_in_pair_order():
+    k, q8b, H = 3, 32, 5
+    q8 = torch.arange(4 * q8b, dtype=torch.int64).remainder(251).to(torch.uint8).view(4, q8b)
+    ids = torch.tensor([0, 3, 5, 1, 2, 4, 0, 1, 5, 2, 3, 4], dtype=torch.int32)  # 4 tokens x 3
+    plan = ep.local_plan(ids, experts_per_rank=2, world=3)
+    rows = ep.pack_rows(q8, ids, plan, k, 2)
+    assert rows.shape == (12, q8b + ep.ROW_HEADER_BYTES) and (q8b + ep.ROW_HEADER_BYTES) % 16 == 0
+    imgs, items = ep.unpack_items(rows, q8b)
+    for i, p in enumerate(plan.order.tolist()):
+        assert torch.equal(imgs[i], q8[p // k])
+        assert items[i, 0].item() == ids[p].item() % 2 and items[i, 1].item() == 0
+    back = torch.arange(12 * H, dtype=torch.float32).view(12, H)
+    got = ep.place_returned(back, plan, 12, H)
+    for i, p in enumerate(plan.order.tolist()):
+        assert torch.equal(got[p], back[i])
+
+
+def test_empty_dispatch():
+    plan = ep.local_plan(torch.zeros(0, dtype=torch.int32), experts_per_rank=4, world=2)
+    assert plan.send == [0, 0]
+    rows = ep.pack_rows(torch.zeros((0, 32), dtype=torch.uint8), torch.zeros(0, dtype=torch.int32), plan, 8, 4)
+    imgs, items = ep.unpack_items(rows, 32)
+    assert imgs.shape == (0, 32) and items.shape == (0, 2)
+    assert ep.place_returned(torch.zeros((0, 7)), plan, 0, 7).shape == (0, 7)
+
+
+def test_layer_must_hold_its_rank_share():
+    class L:
+        global_experts, local_experts, first_expert = 8, 4, 0
+
+    with pytest.raises(ValueError):
+        ep.ExpertParallelMoe(L())  # one rank must hold all 8
+
+
+def test_gloo_two_ranks_match_one_rank_bit_for_bit():
+    """Two gloo ranks on the host with exact stand-in compute stages:
+    ragged token counts, a rank without tokens, pairs all on one rank."""
+    r = _torchrun(2, "cpu", timeout=240)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "ok" in r.stdout
+
+
+# ------------------------------------------------------------------------ GPU
+
+
+def _gpu_layers(H, F, E, k, seed, world):
+    import lbk
+    from gpu_helpers import ctx, dev, make_layer_np, matrix, planar_dev
+
+    rng = np.random.default_rng(seed)
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    keep = []
+
+    def up(ty, b, in_w):
+        t = planar_dev(ty, b, in_w)
+        keep.append(t)
+        return t
+
+    def ex(e):
+        gty, gb, uty, ub, dty, db, h, f = e
+        return lbk.Expert(matrix(gty, h, f, up(gty, gb, h), lbk.LAYOUT_PLANAR),
+                          matrix(uty, h, f, up(uty, ub, h), lbk.LAYOUT_PLANAR),
+                          matrix(dty, f, h, up(dty, db, f), lbk.LAYOUT_PLANAR))
+
+    dex = [ex(e) for e in experts]
+    sh = ex(shared)
+    rt = dev(router)
+    keep.append(rt)
+    rm = lbk.Matrix(lbk.TYPE_F32, lbk.LAYOUT_GGUF, H, E, rt.data_ptr(), rt.numel() * 4)
+    bias = dev(np.zeros(E, np.float32))
+    keep.append(bias)
+    full = lbk.MoeLayer(ctx(), dex, sh, rm, bias, k, 2.826)
+    er = E // world
+    ranks = [lbk.EpLayer(ctx(), dex[r * er:(r + 1) * er], sh, rm, bias, k, 2.826, E, r * er) for r in range(world)]
+    return full, ranks, keep, rng
+
+
+def _full_forward(full, x, T):
+    from gpu_helpers import clean_status
+
+    H = full.hidden
+    ws = torch.zeros(full.workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    out = torch.full((T * H,), float("nan"), device="cuda")
+    routed = torch.zeros(T * full.top_k * 2, dtype=torch.int32, device="cuda")
+    full.forward(x, T, out, ws, routed_out=routed)
+    clean_status()
+    return out, routed
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,F,E,k,T", [(4096, 1536, 24, 8, 1), (2048, 512, 16, 4, 3), (4096, 256, 32, 8, 5)])
+def test_single_rank_ep_equals_moe_forward(H, F, E, k, T):
+    from gpu_helpers import clean_status, dev
+
+    full, ranks, keep, rng = _gpu_layers(H, F, E, k, H + F + E + T, 1)
+    moe = ep.ExpertParallelMoe(ranks[0])
+    x = dev(rng.standard_normal(T * H).astype(np.float32))
+    out = torch.full((T * H,), float("nan"), device="cuda")
+    routed = torch.zeros(T * k * 2, dtype=torch.int32, device="cuda")
+    moe.forward(x, T, out, routed_out=routed)
+    clean_status()
+    want, wr = _full_forward(full, x, T)
+    assert torch.equal(routed.cpu(), wr.cpu())
+    assert torch.equal(out.view(torch.int32).cpu(), want.view(torch.int32).cpu())
+    full.close()
+    ranks[0].close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,H,F,E,k,T", [(2, 4096, 1536, 48, 8, 1), (4, 2048, 512, 16, 4, 6), (8, 4096, 256, 64, 8, 2)])
+def test_ranks_simulated_on_one_gpu_equal_moe_forward(world, H, F, E, k, T):
+    """`world` rank layers on one GPU: route on rank 0, hand each rank its rows
+    (the exchange done by slicing), items_forward per rank, place, combine."""
+    from gpu_helpers import clean_status, dev
+
+    full, ranks, keep, rng = _gpu_layers(H, F, E, k, 7 * H + F + E + T, world)
+    home = ranks[0]
+    x = dev(rng.standard_normal(T * H).astype(np.float32))
+    er = E // world
+    q8b = home.q8_bytes
+    ws = torch.zeros(max(home.workspace_bytes(T), home.workspace_bytes(T * k)), dtype=torch.uint8, device="cuda")
+    routed = torch.empty((T * k, 2), dtype=torch.int32, device="cuda")
+    q8 = torch.empty((T, q8b), dtype=torch.uint8, device="cuda")
+    home.route(x, T, routed, q8, ws)
+    ids = routed[:, 0]
+    plan = ep.local_plan(ids, er, world)
+    send = plan.send
+    rows = ep.pack_rows(q8, ids, plan, k, er)
+    dots = []
+    for r, chunk in enumerate(torch.split(rows, send)):
+        n = chunk.shape[0]
+        d = torch.empty((n, H), dtype=torch.float32, device="cuda")
+        if n:
+            imgs, items = ep.unpack_items(chunk, q8b)
+            ranks[r].items_forward(imgs, items, n, d, ws)
+        dots.append(d)
+    routed_dots = ep.place_returned(torch.cat(dots), plan, T * k, H)
+    out = torch.full((T * H,), float("nan"), device="cuda")
+    home.combine(q8, T, routed, routed_dots, out, ws)
+    clean_status()
+    want, wr = _full_forward(full, x, T)
+    assert torch.equal(routed.view(-1).cpu(), wr.cpu())
+    assert torch.equal(out.view(torch.int32).cpu(), want.view(torch.int32).cpu())
+    full.close()
+    for r in ranks:
+        r.close()
+
+
+@pytest.mark.gpu
+def test_items_forward_reports_out_of_range_local_expert():
+    """A local expert ID beyond the rank's share is reported through the
+    status word (INVALID_PARAMETER, index = the ID); the kernels stay in bounds."""
+    import lbk
+    from gpu_helpers import expect_status
+
+    full, ranks, keep, rng = _gpu_layers(2048, 512, 16, 4, 5, 2)
+    r1 = ranks[1]
+    n = 2
+    imgs = torch.zeros((n, r1.q8_bytes), dtype=torch.uint8, device="cuda")
+    items = torch.tensor([[3, 0], [8, 0]], dtype=torch.int32, device="cuda")
+    ws = torch.zeros(r1.workspace_bytes(n), dtype=torch.uint8, device="cuda")
+    dots = torch.zeros((n, 2048), device="cuda")
+    r1.items_forward(imgs, items, n, dots, ws)
+    d = expect_status(15)
+    assert d.index == 8
+    full.close()
+    for r in ranks:
+        r.close()
+
+
+@pytest.mark.gpu
+def test_nccl_ranks_equal_moe_forward():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    r = _torchrun(2, "gpu", timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "ok" in r.stdout
