@@ -124,8 +124,8 @@ __device__ __forceinline__ uint32_t wld16(const uint8_t* p) {
 
 // ------------------------------------------------ bulk copies and mbarriers
 //
-// Global -> shared bulk copies (cp.async.bulk, no multicast) completing on an
-// mbarrier in the issuing CTA. Source and destination 16-byte aligned, size a
+// Global -> shared bulk copies (cp.async.bulk into the issuing CTA only)
+// completing on an mbarrier in that CTA. Source and destination 16-byte aligned, size a
 // multiple of 16.
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
