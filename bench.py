@@ -24,6 +24,10 @@ cpu_baseline: the CPU restatement of the reference's AVX2 path (oracle/),
 --impl reference times that CPU path on the host cores on the same config.
 With N>1 GPUs every rank runs its own resident copy of the layers on its own
 tokens (replicas; weak scaling).
+
+--config 4 measures the batched layer instead: 64 tokens per step per GPU,
+experts sharded over the GPUs (192 / N each), dispatch and return by NCCL
+all-to-all (lightbridge-engine_b200/ep.py); weak scaling.
 """
 
 from __future__ import annotations
@@ -44,6 +48,7 @@ H, F, E, K_TOP = 4096, 1536, 192, 8
 WEIGHT_SCALE = 2.826
 TOKENS_PER_STEP = 256
 LAYERS = 8
+BATCH_TOKENS = 64  # config 4, per GPU
 TYPE_IQ2_S, TYPE_IQ3_S, TYPE_Q4_K = 22, 21, 12
 METRIC = "routed-MoE decode tokens/s (single-token MoE FFN layer, config 3)"
 
@@ -459,6 +464,114 @@ def profile_forwards(n: int) -> None:
     print(f"profile_forwards: {n} forwards ok", flush=True)
 
 
+def build_ep_layer(ctx, lbk, torch, dev, seed: int, first: int, count: int):
+    """This rank's share of one config-3 layer (experts [first, first + count)),
+    the whole router and shared expert, as an lbk.EpLayer."""
+    import synth
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    keep = []
+    router = (torch.randn(E, H, device=dev, generator=gen) * 0.02).contiguous()
+    keep.append(router)
+
+    def planar(ty, k, rows, n):
+        g = synth.packed_torch(gen, ty, k, rows * n, dev)
+        mb, pb = synth.matrix_bytes(ty, k, rows), synth.planar_bytes(ty, k, rows)
+        p = torch.empty(pb * n, dtype=torch.uint8, device=dev)
+        for e in range(n):
+            ctx.repack(lbk.matrix(ty, k, rows, g[e * mb:(e + 1) * mb]), p[e * pb:(e + 1) * pb])
+        keep.append(p)
+        return p, pb
+
+    gp, mbg = planar(TYPE_IQ2_S, H, F, count)
+    up, _ = planar(TYPE_IQ2_S, H, F, count)
+    dp, mbd = planar(TYPE_IQ3_S, F, H, count)
+    sh = [planar(ty, k, rows, 1)[0] for ty, k, rows in [(TYPE_Q4_K, H, F), (TYPE_Q4_K, H, F), (TYPE_Q4_K, F, H)]]
+    torch.cuda.synchronize()
+    experts = [
+        lbk.Expert(lbk.matrix(TYPE_IQ2_S, H, F, gp[e * mbg:(e + 1) * mbg], lbk.LAYOUT_PLANAR),
+                   lbk.matrix(TYPE_IQ2_S, H, F, up[e * mbg:(e + 1) * mbg], lbk.LAYOUT_PLANAR),
+                   lbk.matrix(TYPE_IQ3_S, F, H, dp[e * mbd:(e + 1) * mbd], lbk.LAYOUT_PLANAR))
+        for e in range(count)
+    ]
+    shared = lbk.Expert(*[lbk.matrix(ty, k, rows, p, lbk.LAYOUT_PLANAR)
+                          for (ty, k, rows), p in zip([(TYPE_Q4_K, H, F), (TYPE_Q4_K, H, F), (TYPE_Q4_K, F, H)], sh)])
+    bias = torch.zeros(E, device=dev)
+    keep.append(bias)
+    rm = lbk.Matrix(lbk.TYPE_F32, lbk.LAYOUT_GGUF, H, E, router.data_ptr(), router.numel() * 4)
+    return lbk.EpLayer(ctx, experts, shared, rm, bias, K_TOP, WEIGHT_SCALE, E, first), keep
+
+
+def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 4: the routed-MoE layer on BATCH_TOKENS tokens per step per rank,
+    experts sharded in contiguous ranges over the ranks (E / world each), the
+    router and shared expert whole on every rank; dispatch and return of the
+    routed pairs by NCCL all-to-all (ep.ExpertParallelMoe). Weak scaling: every
+    rank is home to its own BATCH_TOKENS tokens."""
+    import torch
+    import torch.distributed as dist
+
+    import ep
+    import lbk
+
+    T = BATCH_TOKENS
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = lbk.Context(local_rank)
+    er = E // world
+    layer, keep = build_ep_layer(ctx, lbk, torch, dev, 4 + 1000 * rank, rank * er, er)
+    moe = ep.ExpertParallelMoe(layer)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 + rank)
+    xs = torch.randn(T * H, device=dev, generator=gen)
+    out = torch.empty(T * H, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        moe.forward(xs, T, out)
+    ctx.raise_status()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        moe.forward(xs, T, out)
+    end.record()
+    barrier()
+    ctx.raise_status()
+    ms = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        line = {
+            "metric": "routed-MoE batched tokens/s (config 4: 64 tokens per step per GPU, expert-parallel)",
+            "value": T * world / (ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q8_k x packed (int8 dots, f32 tails)",
+            "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": "config4: routed-MoE FFN layer, 64 tokens per step per GPU", "hidden": H,
+                       "experts": E, "experts_per_gpu": er, "expert_ffn": F, "top_k": K_TOP,
+                       "tokens_per_step_per_gpu": T, "parallelism": f"expert-parallel x{world}",
+                       "exchange": "NCCL all_to_all_single (counts, Q8_K rows, row dots)"},
+        }
+        print(json.dumps(line), flush=True)
+    layer.close()
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -466,6 +579,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", type=int, choices=[3, 4], default=3,
+                    help="3: single-token decode (the headline); 4: 64 tokens per step per GPU, expert-parallel")
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="profiling driver: one resident layer, this many single-token forwards, no timing")
     args = ap.parse_args()
@@ -488,7 +603,10 @@ def main() -> None:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
-        our_arm(args, rank, world, local_rank)
+        if args.config == 4:
+            batched_ep_arm(args, rank, world, local_rank)
+        else:
+            our_arm(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
