@@ -572,6 +572,87 @@ def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
     ctx.close()
 
 
+def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
+    """Configs 1-2: one quantized matvec y = W Q8_K(x) per call through
+    lbk_gemv (planar layout). Config 1: Q4_K 4096 x 4096; config 2: IQ2_S and
+    IQ3_S 6144 x 4096. Calls rotate over enough distinct weight copies that
+    every call streams its matrix from HBM; a step is one call per copy,
+    replayed as a CUDA graph. value = algorithmic bytes (W + x + y) / time."""
+    import torch
+
+    import lbk
+    import synth
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = lbk.Context(local_rank)
+    cases = [(TYPE_Q4_K, 4096, 4096)] if cfg == 1 else [(TYPE_IQ2_S, 4096, 6144), (TYPE_IQ3_S, 4096, 6144)]
+    results = []
+    for ty, k, rows in cases:
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(cfg + 97 * rank)
+        pb = synth.planar_bytes(ty, k, rows)
+        copies = max(8, (320 << 20) // pb + 1)  # > 2.5 x L2 in total
+        ws = []
+        for _ in range(copies):
+            g = synth.packed_torch(gen, ty, k, rows, dev)
+            p = torch.empty(pb, dtype=torch.uint8, device=dev)
+            ctx.repack(lbk.matrix(ty, k, rows, g), p)
+            ws.append(p)
+        mats = [lbk.matrix(ty, k, rows, p, lbk.LAYOUT_PLANAR) for p in ws]
+        x = torch.randn(k, device=dev, generator=gen)
+        y = torch.empty(rows, device=dev)
+        q8 = torch.empty(k // 256 * 292, dtype=torch.uint8, device=dev)
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            for m in mats:
+                ctx.gemv(m, x, y, q8, stream=stream.cuda_stream)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for m in mats:
+                    ctx.gemv(m, x, y, q8, stream=stream.cuda_stream)
+            for _ in range(args.warmup):
+                graph.replay()
+            stream.synchronize()
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            en.record(stream)
+            stream.synchronize()
+        ctx.raise_status()
+        us = st.elapsed_time(en) * 1000.0 / (args.steps * copies)
+        alg = rows * row_bytes(ty, k) + k * 4 + rows * 4
+        results.append({"type": {TYPE_Q4_K: "Q4_K", TYPE_IQ2_S: "IQ2_S", TYPE_IQ3_S: "IQ3_S"}[ty], "rows": rows,
+                        "input_width": k, "us_per_call": us, "gbs": alg / us / 1e3, "algorithmic_bytes": alg,
+                        "copies": copies})
+        del graph
+    peak, kind = peaks()
+    if rank == 0:
+        head = results[0]
+        line = {
+            "metric": f"quantized GEMV HBM GB/s (config {cfg}: {head['type']} {head['rows']}x{head['input_width']})",
+            "value": head["gbs"] * world,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": head["us_per_call"] * head["copies"] / 1000.0,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q8_k x packed (int8 dots, f32 tails)",
+            "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": f"config{cfg}: single quantized matvec", "l2": "rotating over distinct weight copies (> L2)"},
+            "roofline": {"bound": "hbm", "achieved": head["gbs"], "peak": peak, "unit": "GB/s", "frac": head["gbs"] / peak,
+                         "peak_kind": kind},
+            "cases": results,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -579,8 +660,9 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[3, 4], default=3,
-                    help="3: single-token decode (the headline); 4: 64 tokens per step per GPU, expert-parallel")
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4], default=3,
+                    help="3: single-token decode (the headline); 4: 64 tokens per step per GPU, expert-parallel; "
+                         "1, 2: single quantized matvec")
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="profiling driver: one resident layer, this many single-token forwards, no timing")
     args = ap.parse_args()
@@ -605,6 +687,8 @@ def main() -> None:
     try:
         if args.config == 4:
             batched_ep_arm(args, rank, world, local_rank)
+        elif args.config in (1, 2):
+            gemv_arm(args, args.config, rank, world, local_rank)
         else:
             our_arm(args, rank, world, local_rank)
     finally:

@@ -538,49 +538,62 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         }
         float* hrow = a.h + ((uint64_t)t * (a.k + 1) + slot) * a.ffn;
         uint32_t rb = r0;
-        // one rolled loop over units: the decode is emitted once (its code is
+        // one rolled loop over row steps (R rows of gate and of up): the lane
+        // decodes its half block of both matrices, two independent chains on
+        // the same activations; the decode is emitted once (its code is
         // fetched cold once per launch)
+        const uint32_t steps = units >> 1;
 #pragma unroll 1
-        for (uint32_t u = 0; u < units; u++) {
-            const uint32_t m = u & 1;
-            const uint32_t ra = r0 + (u >> 1) * R;
+        for (uint32_t q = 0; q < steps; q++) {
+            const uint32_t ra = r0 + q * R;
             const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
-            if (live && !mbar_wait(bar0 + 8 * m, (phase >> m) & 1u)) {
+            if (live && (!mbar_wait(bar0, phase & 1u) || !mbar_wait(bar0 + 8, (phase >> 1) & 1u))) {
                 live = false;
                 if (lane == 0) report(a.status, LBK_TIMEOUT, it, 0);
             }
             live = __all_sync(0xffffffffu, live);
-            phase ^= 1u << m;
+            phase ^= 3u;
             const bool mine = lane_on && (uint32_t)sub < nr;
-            HB w;
-            if (mine) load_stage(w, stage + m * RL::kMat, so);
+            HB wg, wu;
+            if (mine) {
+                load_stage(wg, stage, so);
+                load_stage(wu, stage + RL::kMat, so);
+            }
             __syncwarp();
             const uint32_t rn = ra + R;
-            if (lane == 0 && live && u + 2 < units) {
+            if (lane == 0 && live && q + 1 < steps) {
                 fence_proxy_async_smem();
-                gut_issue(stage_s + m * RL::kMat, bar0 + 8 * m, m ? umat : gmat, rs, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
+                const uint32_t nn = r1 - rn < (uint32_t)R ? r1 - rn : R;
+                gut_issue(stage_s, bar0, gmat, rs, rn, nn);
+                gut_issue(stage_s + RL::kMat, bar0 + 8, umat, rs, rn, nn);
             }
             const uint32_t row = ra + sub;
-            IqPart ip{0, 0};
-            KPart kp;
+            IqPart ipg{0, 0}, ipu{0, 0};
+            KPart kpg, kpu;
+            if constexpr (!kIq) {
 #pragma unroll
-            for (int l = 0; l < 8; l++) kp.lane[l] = 0;
-            kp.min_sum = 0;
-            kp.dm = 0;
-            if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
-            write_products<T>(prod + (int)(row - rb) * pstride + m * nb * kTail, b, h, mine, ip, kp, act.d, a.status,
-                              (uint64_t)row * nb + b);
-            if (m == 1 && (rn - rb >= (uint32_t)RL::kBmax || rn >= r1)) {
+                for (int l = 0; l < 8; l++) kpg.lane[l] = kpu.lane[l] = 0;
+                kpg.min_sum = kpu.min_sum = 0;
+                kpg.dm = kpu.dm = 0;
+            }
+            if (mine) {
+                HBDot<T>::run(wg, act, nact, t0, t1, h, ipg, kpg);
+                HBDot<T>::run(wu, act, nact, t0, t1, h, ipu, kpu);
+            }
+            float* pr = prod + (int)(row - rb) * pstride;
+            write_products<T>(pr, b, h, mine, ipg, kpg, act.d, a.status, (uint64_t)row * nb + b);
+            write_products<T>(pr + nb * kTail, b, h, mine, ipu, kpu, act.d, a.status, (uint64_t)row * nb + b);
+            if (rn - rb >= (uint32_t)RL::kBmax || rn >= r1) {
                 const int nrows = (int)((rn < r1 ? rn : r1) - rb);
                 __syncwarp();
                 warp_tails<T>(prod, nrows * 2, nb, chains, res);
-                for (int q = lane; q < nrows; q += 32) {
-                    float g = res[q * 2], u = res[q * 2 + 1];
+                for (int qq = lane; qq < nrows; qq += 32) {
+                    float g = res[qq * 2], u = res[qq * 2 + 1];
                     float v = swiglu_ref(g, u);
                     if (!isfinite(v))
-                        report(a.status, LBK_NON_FINITE_VALUE, ((uint64_t)t * (a.k + 1) + slot) * a.ffn + rb + q,
+                        report(a.status, LBK_NON_FINITE_VALUE, ((uint64_t)t * (a.k + 1) + slot) * a.ffn + rb + qq,
                                __float_as_uint(v));
-                    hrow[rb + q] = v;
+                    hrow[rb + qq] = v;
                 }
                 __syncwarp();
                 rb = rn;
