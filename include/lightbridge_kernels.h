@@ -295,6 +295,35 @@ int32_t lbk_moe_layer_trace_read(lbk_moe_layer* layer, float ms[3]);
 int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t tokens, const lbk_routed* routed,
                        float* out, void* workspace, uint64_t workspace_bytes, void* stream);
 
+/* ---------------------------------------- MoE block: norm and residual */
+
+/* weighted_rms_norm_into (bridge-kernels-reference/src/norm.rs:5-18) on each
+ * of `rows` rows of n values: out = (x * scale) * weight with scale =
+ * 1 / sqrt(mean(x^2) + epsilon). mode LBK_ROUTER_SEQUENTIAL sums the squares
+ * in one f32 chain as the reference does (bit-identical); LBK_ROUTER_TREE in
+ * a fixed tree (within 1e-5). Validate before write: a non-finite input,
+ * weight, scale or output is reported through the status word and the row's
+ * output is not written; n == 0 or epsilon <= 0 -> LBK_INVALID_PARAMETER,
+ * non-finite epsilon -> LBK_NON_FINITE_VALUE (host checks). */
+int32_t lbk_rms_norm(lbk_context* ctx, const float* x, const float* weight, uint64_t n, uint64_t rows, float epsilon,
+                     float* out, int32_t mode, void* stream);
+/* residual_add_in_place (norm.rs:83-100): dest += src over n values, written
+ * only when every check of the call (dest finite, src finite, sums finite, in
+ * that order) passes and the status word is clear. */
+int32_t lbk_residual_add(lbk_context* ctx, float* dest, const float* src, uint64_t n, void* stream);
+
+/* The FFN half of a Hy3 block for `tokens` tokens: hidden[t] +=
+ * MoE(RMSNorm(hidden[t], ffn_norm, epsilon)), i.e. the FFN part of
+ * hy3_moe_route_token (RMSNorm, router, top-k; layer.rs:588-608) followed by
+ * hy3_moe_finish_token (experts, combine, residual add; layer.rs:610-659)
+ * with the experts HBM-resident, so no payload is streamed between the two.
+ * router_mode selects the order of both the norm's sum and the router logits.
+ * hidden is written only if every step succeeded. */
+int32_t lbk_moe_block_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes);
+int32_t lbk_moe_block_forward(lbk_moe_layer* layer, float* hidden, const float* ffn_norm, float epsilon,
+                              uint64_t tokens, lbk_routed* routed_out, int32_t router_mode, void* workspace,
+                              uint64_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------ expert parallelism */
 
 /* A rank's layer for expert parallelism: w->experts holds this rank's

@@ -1099,6 +1099,94 @@ LBK_API int32_t lbk_moe_routed(lbk_moe_layer* layer, const float* x, uint64_t to
     return moe_experts(layer, x, tokens, routed, out, ws, o, st, false, full_mode(layer));
 }
 
+// ------------------------------------------------ MoE block: norm, residual
+
+namespace {
+
+int32_t norm_params(uint64_t n, float epsilon) {
+    // validate_norm_lengths / validate_epsilon (norm.rs:116-142)
+    if (n == 0) return fail(LBK_INVALID_PARAMETER, "RMSNorm input must not be empty");
+    if (!std::isfinite(epsilon)) return fail(LBK_NON_FINITE_VALUE, "RMSNorm epsilon", 0, 0, 0, f32_bits(epsilon));
+    if (!(epsilon > 0.0f)) return fail(LBK_INVALID_PARAMETER, "RMSNorm epsilon must be greater than zero");
+    return LBK_OK;
+}
+
+}  // namespace
+
+LBK_API int32_t lbk_rms_norm(lbk_context* ctx, const float* x, const float* weight, uint64_t n, uint64_t rows,
+                             float epsilon, float* out, int32_t mode, void* stream) {
+    if (ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null context");
+    if (int32_t s = norm_params(n, epsilon)) return s;
+    if (rows == 0) return fail(LBK_DIMENSION_MISMATCH, "RMSNorm rows", 0, 1, 0);
+    if (x == nullptr || weight == nullptr || out == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (mode != LBK_ROUTER_SEQUENTIAL && mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "norm mode");
+    if (mode == LBK_ROUTER_SEQUENTIAL && n * 4 > lbk::kMaxSmem)
+        return fail(LBK_INVALID_PARAMETER, "sequential RMSNorm rows are staged in shared memory", 0, lbk::kMaxSmem / 4, n);
+    if (int32_t s = set_device(ctx)) return s;
+    lbk::NormArgs a{x, weight, epsilon, out, rows, n, mode == LBK_ROUTER_SEQUENTIAL ? 1 : 0, ctx->status};
+    cudaError_t e = lbk::launch_rms_norm(a, ctx->sm_count, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "RMSNorm launch");
+}
+
+LBK_API int32_t lbk_residual_add(lbk_context* ctx, float* dest, const float* src, uint64_t n, void* stream) {
+    if (ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null context");
+    if (dest == nullptr || src == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (n == 0) return ok();
+    if (int32_t s = set_device(ctx)) return s;
+    cudaError_t e = lbk::launch_residual_add(dest, src, n, ctx->scratch_min, ctx->status, ctx->sm_count, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "residual add launch");
+}
+
+namespace {
+
+// [normalized input T*H][MoE output T*H][lbk_moe_forward's workspace]
+uint64_t block_ws_bytes(const lbk_moe_layer* L, uint64_t T) {
+    const uint64_t a = moe_ws(L, T, L->k).total, b = moe_ws(L, 1, L->k).total;
+    return 2 * up256(T * L->H * 4) + (a > b ? a : b);
+}
+
+}  // namespace
+
+LBK_API int32_t lbk_moe_block_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes) {
+    if (layer == nullptr || bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    *bytes = block_ws_bytes(layer, tokens);
+    return ok();
+}
+
+LBK_API int32_t lbk_moe_block_forward(lbk_moe_layer* layer, float* hidden, const float* ffn_norm, float epsilon,
+                                      uint64_t tokens, lbk_routed* routed_out, int32_t router_mode, void* workspace,
+                                      uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    if (int32_t s = norm_params(layer->H, epsilon)) return s;
+    if (hidden == nullptr || ffn_norm == nullptr || workspace == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(hidden, 16) || !aligned(workspace, 256))
+        return fail(LBK_INVALID_PARAMETER, "hidden 16-byte / workspace 256-byte alignment");
+    const uint64_t need = block_ws_bytes(layer, tokens);
+    if (workspace_bytes < need) return fail(LBK_SCRATCH_TOO_SMALL, "MoE block workspace", 0, need, workspace_bytes);
+    if (router_mode != LBK_ROUTER_SEQUENTIAL && router_mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "router mode");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const uint64_t vec = up256(tokens * layer->H * 4);
+    float* normed = reinterpret_cast<float*>(ws);
+    float* delta = reinterpret_cast<float*>(ws + vec);
+    // hy3_moe_route_token's FFN norm (layer.rs:588-593)
+    lbk::NormArgs na{hidden, ffn_norm, epsilon, normed, tokens, layer->H, router_mode == LBK_ROUTER_SEQUENTIAL ? 1 : 0,
+                     ctx->status};
+    cudaError_t e = lbk::launch_rms_norm(na, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(e, "RMSNorm launch");
+    // router, top-k, experts, combine
+    if (int32_t s = lbk_moe_forward(layer, normed, tokens, delta, routed_out, router_mode, ws + 2 * vec,
+                                    workspace_bytes - 2 * vec, stream))
+        return s;
+    // hy3_moe_finish_token's residual add (layer.rs:654)
+    e = lbk::launch_residual_add(hidden, delta, tokens * layer->H, ctx->scratch_min, ctx->status, ctx->sm_count, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "residual add launch");
+}
+
 // --------------------------------------------------- expert parallelism
 //
 // A rank's layer (lbk_ep_layer_create) holds the whole router and the shared

@@ -80,6 +80,21 @@ struct RouterFusedArgs {
 size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens);
 cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStream_t stream);
 
+// weighted_rms_norm_into per row (norm.cu): rows x n values.
+struct NormArgs {
+    const float* x;
+    const float* w;      // [n]
+    float eps;
+    float* out;
+    uint64_t rows, n;
+    int sequential;      // 1: the reference's single f32 chain (n <= 58K); 0: fixed tree
+    DeviceStatus* status;
+};
+cudaError_t launch_rms_norm(const NormArgs& a, int sm_count, cudaStream_t stream);
+// dest += src with residual_add_in_place's checks; key: 8 bytes of scratch.
+cudaError_t launch_residual_add(float* dest, const float* src, uint64_t n, unsigned long long* key, DeviceStatus* status,
+                                int sm_count, cudaStream_t stream);
+
 struct TopkArgs {
     const float* logits;    // [tokens][E]
     const float* bias;      // [E]

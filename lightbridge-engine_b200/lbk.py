@@ -123,6 +123,10 @@ def _load() -> ctypes.CDLL:
         "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
         "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
         "lbk_moe_forward_no_alloc": ([P, P, U64, P, P, I32, P], I32),
+        "lbk_rms_norm": ([P, P, P, U64, U64, F, P, I32, P], I32),
+        "lbk_residual_add": ([P, P, P, U64, P], I32),
+        "lbk_moe_block_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
+        "lbk_moe_block_forward": ([P, P, P, F, U64, P, I32, P, U64, P], I32),
         "lbk_ep_layer_create": ([P, ctypes.POINTER(MoeWeights), U64, U64, P, ctypes.POINTER(P)], I32),
         "lbk_ep_q8_bytes": ([P, ctypes.POINTER(U64)], I32),
         "lbk_ep_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
@@ -149,7 +153,8 @@ EXPORTED = (
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
     "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused "
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
-    "lbk_moe_layer_trace_read lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
+    "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward "
+    "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine "
     "lbk_repack lbk_unpack lbk_validate_matrix"
 ).split()
@@ -247,6 +252,14 @@ class Context:
     def expert_swiglu_accumulate(self, e: Expert, x, dst, coef: float, workspace, stream=None) -> None:
         check(lib.lbk_expert_swiglu_accumulate(self.ptr, ctypes.byref(e), _ptr(x), _ptr(dst), float(coef), _ptr(workspace), workspace.numel(), _stream(stream)))
 
+    def rms_norm(self, x, weight, n: int, rows: int, epsilon: float, out, mode: int = ROUTER_SEQUENTIAL,
+                 stream=None) -> None:
+        check(lib.lbk_rms_norm(self.ptr, _ptr(x), _ptr(weight), n, rows, float(epsilon), _ptr(out), mode,
+                               _stream(stream)))
+
+    def residual_add(self, dest, src, n: int, stream=None) -> None:
+        check(lib.lbk_residual_add(self.ptr, _ptr(dest), _ptr(src), n, _stream(stream)))
+
     def repack(self, m: Matrix, dst, stream=None) -> None:
         check(lib.lbk_repack(self.ptr, ctypes.byref(m), _ptr(dst), dst.numel(), _stream(stream)))
 
@@ -289,6 +302,16 @@ class MoeLayer:
 
     def routed(self, x, tokens: int, routed, out, workspace, stream=None) -> None:
         check(lib.lbk_moe_routed(self.ptr, _ptr(x), tokens, _ptr(routed), _ptr(out), _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def block_workspace_bytes(self, tokens: int) -> int:
+        n = ctypes.c_uint64()
+        check(lib.lbk_moe_block_workspace_bytes(self.ptr, tokens, ctypes.byref(n)))
+        return n.value
+
+    def block_forward(self, hidden, ffn_norm, epsilon: float, tokens: int, workspace, routed_out=None,
+                      router_mode: int = ROUTER_TREE, stream=None) -> None:
+        check(lib.lbk_moe_block_forward(self.ptr, _ptr(hidden), _ptr(ffn_norm), float(epsilon), tokens, _ptr(routed_out),
+                                        router_mode, _ptr(workspace), workspace.numel(), _stream(stream)))
 
     def trace(self, enable: bool = True) -> None:
         check(lib.lbk_moe_layer_trace(self.ptr, int(enable)))

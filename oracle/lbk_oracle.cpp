@@ -996,6 +996,47 @@ int32_t orc_moe_token(const orc_expert* experts, uint64_t expert_count, const or
     return orc_moe_routed(experts, expert_count, shared, ids, coefs, k, x, out, preflight, simd, threads);
 }
 
+int32_t orc_rms_norm(const float* input, uint64_t n, const float* weight, uint64_t weight_len, float epsilon,
+                     float* out, uint64_t out_len) {
+    // validate_norm_call (norm.rs:102-114) -> validate_norm_lengths (:116-131),
+    // validate_epsilon (:133-142), then the input and weight values
+    if (n == 0) return fail(LBK_INVALID_PARAMETER);
+    if (weight_len != n) return fail(LBK_DIMENSION_MISMATCH, 0, 0, n, weight_len);
+    if (out_len != n) return fail(LBK_DIMENSION_MISMATCH, 0, 0, n, out_len);
+    if (!std::isfinite(epsilon)) return fail(LBK_NON_FINITE_VALUE, 0, f32_bits(epsilon));
+    if (!(epsilon > 0.0f)) return fail(LBK_INVALID_PARAMETER);
+    for (uint64_t i = 0; i < n; i++)
+        if (!std::isfinite(input[i])) return fail(LBK_NON_FINITE_VALUE, i, f32_bits(input[i]));
+    for (uint64_t i = 0; i < n; i++)
+        if (!std::isfinite(weight[i])) return fail(LBK_NON_FINITE_VALUE, i, f32_bits(weight[i]));
+    // rms_scale (:144-153): one f32 chain of squares, f32 mean, 1 / sqrt(mean + eps)
+    float sum = 0.0f;
+    for (uint64_t i = 0; i < n; i++) sum += input[i] * input[i];  // -ffp-contract=off: no fused multiply-add
+    const float mean = sum / (float)n;
+    const float scale = 1.0f / std::sqrt(mean + epsilon);
+    if (!std::isfinite(scale)) return fail(LBK_NON_FINITE_VALUE, 0, f32_bits(scale));
+    for (uint64_t i = 0; i < n; i++) {
+        const float v = input[i] * scale * weight[i];
+        if (!std::isfinite(v)) return fail(LBK_NON_FINITE_VALUE, i, f32_bits(v));
+    }
+    for (uint64_t i = 0; i < n; i++) out[i] = input[i] * scale * weight[i];
+    return ok();
+}
+
+int32_t orc_residual_add(float* dest, uint64_t n, const float* src, uint64_t src_len) {
+    if (src_len != n) return fail(LBK_DIMENSION_MISMATCH, 0, 0, n, src_len);
+    for (uint64_t i = 0; i < n; i++)
+        if (!std::isfinite(dest[i])) return fail(LBK_NON_FINITE_VALUE, i, f32_bits(dest[i]));
+    for (uint64_t i = 0; i < n; i++)
+        if (!std::isfinite(src[i])) return fail(LBK_NON_FINITE_VALUE, i, f32_bits(src[i]));
+    for (uint64_t i = 0; i < n; i++) {
+        const float v = dest[i] + src[i];
+        if (!std::isfinite(v)) return fail(LBK_NON_FINITE_VALUE, i, f32_bits(v));
+    }
+    for (uint64_t i = 0; i < n; i++) dest[i] += src[i];
+    return ok();
+}
+
 float orc_f16_to_f32(uint16_t bits) { return half_to_float(bits); }
 int32_t orc_nearest_int(float v) { return nearest_int(v); }
 float orc_expf(float v) { return std::exp(v); }

@@ -90,6 +90,14 @@ int32_t orc_moe_token(const orc_expert* experts, uint64_t expert_count, const or
                       int32_t simd, int32_t threads);
 
 /* Test hooks. */
+// weighted_rms_norm_into (bridge-kernels-reference/src/norm.rs:5-18): out is
+// written only when every check passes (validation :102-143, rms_scale
+// :144-153). weight_len and out_len are the slice lengths the reference checks.
+int32_t orc_rms_norm(const float* input, uint64_t n, const float* weight, uint64_t weight_len, float epsilon,
+                     float* out, uint64_t out_len);
+// residual_add_in_place (norm.rs:83-100): dest += src, or nothing on error.
+int32_t orc_residual_add(float* dest, uint64_t n, const float* src, uint64_t src_len);
+
 float orc_f16_to_f32(uint16_t bits);
 int32_t orc_nearest_int(float v);
 float orc_expf(float v);

@@ -83,6 +83,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.orc_moe_token.argtypes = [
         ctypes.POINTER(Expert), U64, ctypes.POINTER(Expert), ctypes.POINTER(Matrix), P, U64, F, P, P, P, P, I32, I32, I32,
     ]
+    L.orc_rms_norm.argtypes = [P, U64, P, U64, F, P, U64]
+    L.orc_residual_add.argtypes = [P, U64, P, U64]
     L.orc_f16_to_f32.argtypes = [ctypes.c_uint16]
     L.orc_f16_to_f32.restype = F
     L.orc_nearest_int.argtypes = [F]
@@ -193,6 +195,25 @@ def route_experts_status(logits, bias, k, weight_scale) -> int:
     ids = np.zeros(max(k, 1), dtype=np.uint32)
     coefs = np.zeros(max(k, 1), dtype=np.float32)
     return lib().orc_route_experts(_p(logits), _p(bias), logits.size, k, float(weight_scale), _p(ids), _p(coefs))
+
+
+def rms_norm_status(x: np.ndarray, weight: np.ndarray, epsilon: float, out: np.ndarray) -> int:
+    """weighted_rms_norm_into (norm.rs:5-18); `out` is left untouched on error."""
+    x = np.ascontiguousarray(x, np.float32)
+    weight = np.ascontiguousarray(weight, np.float32)
+    return lib().orc_rms_norm(_p(x), x.size, _p(weight), weight.size, float(epsilon), _p(out), out.size)
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, epsilon: float) -> np.ndarray:
+    out = np.empty(np.asarray(x).size, np.float32)
+    _check(rms_norm_status(x, weight, epsilon, out))
+    return out
+
+
+def residual_add_status(dest: np.ndarray, src: np.ndarray) -> int:
+    """residual_add_in_place (norm.rs:83-100) on `dest` (float32, in place)."""
+    src = np.ascontiguousarray(src, np.float32)
+    return lib().orc_residual_add(_p(dest), dest.size, _p(src), src.size)
 
 
 def swiglu(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
