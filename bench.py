@@ -653,6 +653,76 @@ def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
     ctx.close()
 
 
+def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 5: a stack of STACK_LAYERS config-3 MoE blocks (attention
+    omitted), per-layer random weights from seed 4 + layer, all HBM-resident
+    (about 104 GB planar on one GPU). A step decodes args.batch tokens through
+    every layer, each layer's output feeding the next (lbk_moe_forward per
+    layer, one CUDA graph per step). Token counts above one run the
+    single-token kernels per (token, expert) pair."""
+    import torch
+
+    import lbk
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = lbk.Context(local_rank)
+    B = args.batch
+    layers = []
+    for l in range(args.stack_layers):
+        t, _ = build_layers(ctx, lbk, torch, dev, 1, 4 + l + 1000 * rank, keep_gguf_layer0=False)
+        layers.append(t[0])
+    ws = torch.zeros(layers[0][0].workspace_bytes(B), dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 + rank)
+    bufs = [torch.randn(B * H, device=dev, generator=gen), torch.empty(B * H, device=dev)]
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s):
+        for l, (layer, _) in enumerate(layers):
+            layer.forward(bufs[l % 2], B, bufs[(l + 1) % 2], ws, stream=s.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        step(stream)
+        stream.synchronize()
+        ctx.raise_status()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream)
+        for _ in range(args.warmup):
+            graph.replay()
+        stream.synchronize()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        en.record(stream)
+        stream.synchronize()
+    ctx.raise_status()
+    ms = st.elapsed_time(en) / args.steps
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"routed-MoE stack decode tokens/s (config 5: {args.stack_layers} layers, batch {B})",
+            "value": B * world / (ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q8_k x packed (int8 dots, f32 tails)",
+            "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": f"config5: {args.stack_layers}-layer stack, batch {B}", "layers": args.stack_layers,
+                       "batch": B, "resident_gb": round(args.stack_layers * 1.3066, 1),
+                       "us_per_layer_step": ms * 1000.0 / args.stack_layers,
+                       "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
+        }), flush=True)
+    del graph
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -660,9 +730,11 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4], default=3,
+    ap.add_argument("--batch", type=int, default=1, help="config 5: tokens decoded per step")
+    ap.add_argument("--stack-layers", type=int, default=80, help="config 5: layers in the stack")
+    ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=3,
                     help="3: single-token decode (the headline); 4: 64 tokens per step per GPU, expert-parallel; "
-                         "1, 2: single quantized matvec")
+                         "1, 2: single quantized matvec; 5: 80-layer stack")
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="profiling driver: one resident layer, this many single-token forwards, no timing")
     args = ap.parse_args()
@@ -689,6 +761,8 @@ def main() -> None:
             batched_ep_arm(args, rank, world, local_rank)
         elif args.config in (1, 2):
             gemv_arm(args, args.config, rank, world, local_rank)
+        elif args.config == 5:
+            stack_arm(args, rank, world, local_rank)
         else:
             our_arm(args, rank, world, local_rank)
     finally:
