@@ -657,9 +657,10 @@ def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
     """Config 5: a stack of STACK_LAYERS config-3 MoE blocks (attention
     omitted), per-layer random weights from seed 4 + layer, all HBM-resident
     (about 104 GB planar on one GPU). A step decodes args.batch tokens through
-    every layer, each layer's output feeding the next (lbk_moe_forward per
-    layer, one CUDA graph per step). Token counts above one run the
-    single-token kernels per (token, expert) pair."""
+    every layer: hidden += MoE(RMSNorm(hidden)) per layer
+    (lbk_moe_block_forward, the FFN half of a Hy3 block: the residual stream
+    feeds the next layer), one CUDA graph per step. Token counts above one run
+    the single-token kernels per (token, expert) pair."""
     import torch
 
     import lbk
@@ -672,15 +673,16 @@ def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
     for l in range(args.stack_layers):
         t, _ = build_layers(ctx, lbk, torch, dev, 1, 4 + l + 1000 * rank, keep_gguf_layer0=False)
         layers.append(t[0])
-    ws = torch.zeros(layers[0][0].workspace_bytes(B), dtype=torch.uint8, device=dev)
+    ws = torch.zeros(layers[0][0].block_workspace_bytes(B), dtype=torch.uint8, device=dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3 + rank)
-    bufs = [torch.randn(B * H, device=dev, generator=gen), torch.empty(B * H, device=dev)]
+    hidden = torch.randn(B * H, device=dev, generator=gen)
+    norm_w = torch.ones(H, device=dev)
     stream = torch.cuda.Stream(device=dev)
 
     def step(s):
-        for l, (layer, _) in enumerate(layers):
-            layer.forward(bufs[l % 2], B, bufs[(l + 1) % 2], ws, stream=s.cuda_stream)
+        for layer, _ in layers:
+            layer.block_forward(hidden, norm_w, 1e-6, B, ws, stream=s.cuda_stream)
 
     with torch.cuda.stream(stream):
         step(stream)
