@@ -644,8 +644,15 @@ int32_t layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t E_rout
         return fail(LBK_INVALID_PARAMETER, "routed experts must share each projection's type and layout");
     }
     uniform &= w->experts[0].up.type == L->gate_type;
-    L->fused = uniform && planar && lbk::moe_fused_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type) &&
-               L->k + 1 <= (uint64_t)lbk::kMoeDownMaxSlots;
+    // the fused kernels: the register-streamed ones (any shape, top-k <= 8)
+    // or the bulk-copy-staged ones, which also take the checkpoint's IQ
+    // shared-expert types
+    const bool staged = lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)(H / LBK_QK_K)) &&
+                        lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)(F / LBK_QK_K)) && L->k <= 16;
+    L->fused = uniform && planar &&
+               ((lbk::moe_fused_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type) &&
+                 L->k + 1 <= (uint64_t)lbk::kMoeDownMaxSlots) ||
+                staged);
 
     std::vector<const uint8_t*> ptrs(3 * E);
     for (uint64_t e = 0; e < E; e++) {

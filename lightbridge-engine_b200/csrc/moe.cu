@@ -603,6 +603,25 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     }
 }
 
+// A shared-expert role of an IQ type holds that type's lookup tables too:
+// bulk copies into the start of shared memory, waited for by every thread.
+template <int T, int kTab, int kSign>
+__device__ __forceinline__ void load_role_tables(const Tables& t, uint8_t* smem, uint64_t* bar_word, DeviceStatus* st) {
+    if constexpr (kTab != 0) {
+        const uint32_t bar = (uint32_t)__cvta_generic_to_shared(bar_word);
+        if (threadIdx.x == 0) {
+            mbar_init(bar, 1);
+            mbar_init_fence();
+            mbar_expect_tx(bar, (uint32_t)(kTab + kSign));
+            const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
+            bulk_g2s(base, T == LBK_TYPE_IQ2_S ? (const void*)t.iq2_codes : (const void*)t.iq3_grid, kTab, bar);
+            bulk_g2s(base + kTab, T == LBK_TYPE_IQ2_S ? (const void*)t.signs : (const void*)t.sign_sel, kSign, bar);
+        }
+        __syncthreads();
+        if (!mbar_wait(bar, 0) && threadIdx.x == 0) report(st, LBK_TIMEOUT, 5, 0);
+    }
+}
+
 template <int TG, int TS>
 __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGateUpArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -694,6 +713,8 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps, false,
                           stage_ptr ? s_ptr : nullptr);
     } else {
+        __shared__ __align__(8) uint64_t s_stab;
+        load_role_tables<TS, GUTRole<TS>::kTab, GUTRole<TS>::kSign>(a.tables, smem, &s_stab, a.status);
         // shared expert: its first rows are constant data, requested before
         // the wait for the router's output (inside gut_run)
         gut_run<TS, false>(a, smem, bar, nullptr, (blockIdx.x - a.routed_ctas) * kGUTWarps + warp,
@@ -1055,6 +1076,8 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
         dn_run<TD, true>(a, smem, bar, blockIdx.x * kDNWarps + warp, a.routed_ctas * kDNWarps, false,
                          stage_ptr ? s_ptr : nullptr);
     } else {
+        __shared__ __align__(8) uint64_t s_stab;
+        load_role_tables<TSD, DNRole<TSD>::kTab, DNRole<TSD>::kSign>(a.tables, smem, &s_stab, a.status);
         // shared expert: its first rows are constant data, requested before
         // the wait for the gate/up kernel's output (inside dn_run)
         dn_run<TSD, false>(a, smem, bar, (blockIdx.x - a.routed_ctas) * kDNWarps + warp,
@@ -1190,8 +1213,10 @@ cudaError_t launch_moe_gate_up(int gate_type, int shared_gate_type, const MoeGat
 }
 
 bool moe_gate_up_tma_supported(int gate_type, int shared_gate_type, int nb_h) {
-    return (gate_type == LBK_TYPE_IQ2_S || gate_type == LBK_TYPE_Q4_K) && shared_gate_type == LBK_TYPE_Q4_K &&
-           (nb_h == 8 || nb_h == 16);
+    // the config-3 combinations and the checkpoint's (routed and shared IQ2_S)
+    const bool types = ((gate_type == LBK_TYPE_IQ2_S || gate_type == LBK_TYPE_Q4_K) && shared_gate_type == LBK_TYPE_Q4_K) ||
+                       (gate_type == LBK_TYPE_IQ2_S && shared_gate_type == LBK_TYPE_IQ2_S);
+    return types && (nb_h == 8 || nb_h == 16);
 }
 
 bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks) {
@@ -1203,6 +1228,8 @@ bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks
 cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
                                    cudaStream_t stream) {
     (void)shared_gate_type;
+    if (gate_type == LBK_TYPE_IQ2_S && shared_gate_type == LBK_TYPE_IQ2_S)
+        return launch_gut<LBK_TYPE_IQ2_S, LBK_TYPE_IQ2_S>(a, ctas, stream);
     if (gate_type == LBK_TYPE_IQ2_S) return launch_gut<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
     return launch_gut<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);
 }
@@ -1220,13 +1247,23 @@ cudaError_t launch_dnt(const MoeDownArgs& a, unsigned ctas, cudaStream_t stream)
 }
 
 bool moe_down_tma_supported(int down_type, int shared_down_type, int nb_f) {
-    return (down_type == LBK_TYPE_IQ3_S || down_type == LBK_TYPE_IQ2_S || down_type == LBK_TYPE_Q4_K) &&
-           shared_down_type == LBK_TYPE_Q4_K && nb_f >= 1 && nb_f <= 16;
+    // the config-3 combinations (shared Q4_K) and the checkpoint's: routed
+    // IQ3_S with shared IQ3_S or IQ2_S, routed IQ2_S with shared IQ2_S
+    const bool q4 = (down_type == LBK_TYPE_IQ3_S || down_type == LBK_TYPE_IQ2_S || down_type == LBK_TYPE_Q4_K) &&
+                    shared_down_type == LBK_TYPE_Q4_K;
+    const bool iq = (down_type == LBK_TYPE_IQ3_S && (shared_down_type == LBK_TYPE_IQ3_S || shared_down_type == LBK_TYPE_IQ2_S)) ||
+                    (down_type == LBK_TYPE_IQ2_S && shared_down_type == LBK_TYPE_IQ2_S);
+    return (q4 || iq) && nb_f >= 1 && nb_f <= 16;
 }
 
 cudaError_t launch_moe_down_tma(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
                                 cudaStream_t stream) {
-    (void)shared_down_type;
+    if (down_type == LBK_TYPE_IQ3_S && shared_down_type == LBK_TYPE_IQ3_S)
+        return launch_dnt<LBK_TYPE_IQ3_S, LBK_TYPE_IQ3_S>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ3_S && shared_down_type == LBK_TYPE_IQ2_S)
+        return launch_dnt<LBK_TYPE_IQ3_S, LBK_TYPE_IQ2_S>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ2_S && shared_down_type == LBK_TYPE_IQ2_S)
+        return launch_dnt<LBK_TYPE_IQ2_S, LBK_TYPE_IQ2_S>(a, ctas, stream);
     if (down_type == LBK_TYPE_IQ3_S) return launch_dnt<LBK_TYPE_IQ3_S, LBK_TYPE_Q4_K>(a, ctas, stream);
     if (down_type == LBK_TYPE_IQ2_S) return launch_dnt<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
     return launch_dnt<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);

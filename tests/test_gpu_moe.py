@@ -203,3 +203,36 @@ def test_config3_layer_single_token():
     err = rel_err(out, want)
     assert err <= TOL, err
     layer.close()
+
+
+# The checkpoint's per-layer types (bridge-model-hy3/src/schema.rs:200-258):
+# routed gate/up and shared gate/up IQ2_S; routed down IQ3_S in layers <= 5,
+# IQ2_S after; shared down IQ3_S in layers <= 4, IQ2_S after.
+CHECKPOINT_TYPES = [
+    (orc.TYPE_IQ2_S, orc.TYPE_IQ3_S, orc.TYPE_IQ2_S, orc.TYPE_IQ3_S),  # layers 1-4
+    (orc.TYPE_IQ2_S, orc.TYPE_IQ3_S, orc.TYPE_IQ2_S, orc.TYPE_IQ2_S),  # layer 5
+    (orc.TYPE_IQ2_S, orc.TYPE_IQ2_S, orc.TYPE_IQ2_S, orc.TYPE_IQ2_S),  # layers 6+
+]
+
+
+@pytest.mark.parametrize("types", CHECKPOINT_TYPES)
+@pytest.mark.parametrize("H,F,E,k,T", [(4096, 1536, 24, 8, 1), (2048, 512, 16, 4, 3)])
+def test_checkpoint_types_take_the_fused_kernels(types, H, F, E, k, T):
+    """Layers of the checkpoint's type mix run on the bulk-copy kernels (IQ
+    shared-expert roles with their own tables): oracle to the tolerance, the
+    per-expert GGUF path bit for bit."""
+    gty, dty, sty, sdty = types
+    rng = np.random.default_rng(H + F + E + k + T + sdty)
+    router, experts, shared = make_layer_np(rng, H, F, E, gty=gty, dty=dty, sty=sty, sdty=sdty)
+    xs = rng.standard_normal((T, H)).astype(np.float32)
+    lp, kp = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    lg, kg = upload_layer(router, experts, shared, lbk.LAYOUT_GGUF, k)
+    assert lp.fused and not lg.fused
+    want, wids, _, _ = oracle_tokens(router, experts, shared, xs, k)
+    out, ids, _ = run_forward(lp, xs)
+    np.testing.assert_array_equal(ids, wids)
+    assert rel_err(out, want) <= TOL, rel_err(out, want)
+    ref, rids, _ = run_forward(lg, xs)
+    np.testing.assert_array_equal(bits(out), bits(ref))
+    lp.close()
+    lg.close()
