@@ -87,7 +87,9 @@ typedef enum lbk_status {
     LBK_NON_FINITE_ROUTING_VALUE = 18,
     LBK_CUDA_ERROR = 30,
     LBK_TIMEOUT = 31,
-    LBK_NO_DEVICE = 32
+    LBK_NO_DEVICE = 32,
+    LBK_FORMAT_ERROR = 33,  /* GGUF container or Hy3 schema; kind in detail.bits (lbk_gguf_error) */
+    LBK_IO_ERROR = 34       /* a GGUF file could not be opened or read */
 } lbk_status;
 
 /* Packed weight byte layouts. */
@@ -404,6 +406,149 @@ int32_t lbk_unpack(lbk_context* ctx, const lbk_matrix* src_planar, void* dst_ggu
  * reported through the status word as LBK_NON_FINITE_SCALE with the global
  * block index. reference: validate_scales, k_quants.rs:178-208. */
 int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void* stream);
+
+/* ------------------------------------------------------ GGUF residency */
+
+/* A GGUF split set opened for reading (bridge-gguf-split GgufSet,
+ * src/lib.rs:155-159): every shard's header parsed and checked, the tensors
+ * of all shards in one directory. Payloads are read only by
+ * lbk_moe_layer_load. */
+typedef struct lbk_gguf lbk_gguf;
+
+/* Failure kinds of LBK_FORMAT_ERROR / LBK_IO_ERROR, in lbk_error_detail.bits.
+ * They follow GgufError (bridge-gguf/src/error.rs:8-110), CoreError
+ * (bridge-core/src/error.rs:6-22), SplitError (bridge-gguf-split/src/lib.rs:
+ * 95-153), MetadataError and the Hy3 schema / config errors; the detail's
+ * message is the reference's text for the same failure. */
+typedef enum lbk_gguf_error {
+    LBK_GGUF_IO = 1,
+    LBK_GGUF_TRUNCATED = 2,
+    LBK_GGUF_BAD_MAGIC = 3,
+    LBK_GGUF_UNSUPPORTED_VERSION = 4,
+    LBK_GGUF_LIMIT_EXCEEDED = 5,
+    LBK_GGUF_INVALID_UTF8 = 6,
+    LBK_GGUF_INVALID_BOOLEAN = 7,
+    LBK_GGUF_UNKNOWN_VALUE_TYPE = 8,
+    LBK_GGUF_NESTED_ARRAY = 9,
+    LBK_GGUF_INVALID_DIMENSION_COUNT = 10,
+    LBK_GGUF_INVALID_DIMENSION_LIMIT = 11,
+    LBK_GGUF_DUPLICATE_METADATA_KEY = 12,
+    LBK_GGUF_INVALID_ALIGNMENT = 13,
+    LBK_GGUF_ALIGNMENT_WRONG_TYPE = 14,
+    LBK_GGUF_ARITHMETIC_OVERFLOW = 15,
+    LBK_GGUF_DATA_OFFSET_BEYOND_FILE = 16,
+    LBK_GGUF_TENSOR_OFFSET_MISMATCH = 17,
+    LBK_GGUF_TENSOR_PADDING_OVERFLOW = 18,
+    LBK_GGUF_TENSOR_EXTENT_OVERFLOW = 19,
+    LBK_GGUF_TENSOR_DATA_END_OVERFLOW = 20,
+    LBK_GGUF_TENSOR_DATA_SECTION_TRUNCATED = 21,
+    LBK_GGUF_UNKNOWN_GGML_TYPE = 22,
+    LBK_GGUF_ZERO_TENSOR_DIMENSION = 23,
+    LBK_GGUF_NOT_BLOCK_ALIGNED = 24,
+    LBK_GGUF_TENSOR_OUT_OF_BOUNDS = 25,
+    /* split sets */
+    LBK_GGUF_NOT_A_FILE = 30,
+    LBK_GGUF_INVALID_NUMBERED_FILENAME = 31,
+    LBK_GGUF_MISSING_SPLIT_METADATA = 32,
+    LBK_GGUF_SPLIT_METADATA_DISAGREEMENT = 33,
+    LBK_GGUF_NUMBERED_SINGLE_SHARD = 34,
+    LBK_GGUF_MISSING_SHARD = 35,
+    LBK_GGUF_SHARD_ESCAPES_PARENT = 36,
+    LBK_GGUF_DUPLICATE_TENSOR_NAME = 37,
+    LBK_GGUF_HETEROGENEOUS_VERSION = 38,
+    LBK_GGUF_HETEROGENEOUS_ENDIANNESS = 39,
+    LBK_GGUF_HETEROGENEOUS_ALIGNMENT = 40,
+    LBK_GGUF_UNALIGNED_TENSOR_OFFSET = 41,
+    LBK_GGUF_NEGATIVE_AGGREGATE_TENSOR_COUNT = 42,
+    LBK_GGUF_AGGREGATE_TENSOR_COUNT_DISAGREEMENT = 43,
+    LBK_GGUF_AGGREGATE_TENSOR_DIRECTORY_DISAGREEMENT = 44,
+    /* metadata and the Hy3 MoE block schema */
+    LBK_GGUF_METADATA_MISSING = 50,
+    LBK_GGUF_METADATA_WRONG_TYPE = 51,
+    LBK_GGUF_METADATA_VALUE = 52,
+    LBK_GGUF_NON_FINITE_METADATA = 53,
+    LBK_GGUF_MISSING_TENSOR = 54,
+    LBK_GGUF_TENSOR_SHAPE = 55,
+    LBK_GGUF_TENSOR_TYPE = 56,
+    LBK_GGUF_EXPERT_PAYLOAD_NOT_DIVISIBLE = 57,
+    LBK_GGUF_BLOCK_OUT_OF_RANGE = 58,
+    LBK_GGUF_EXPERT_RANGE = 59,
+    LBK_GGUF_SHARED_WIDTH = 60,
+    LBK_GGUF_BIG_ENDIAN_PAYLOAD = 61
+} lbk_gguf_error;
+
+/* Reader limits (ReaderLimits, bridge-gguf/src/reader.rs:21-42). */
+typedef struct lbk_gguf_limits {
+    uint32_t max_dimensions;       /* <= 4 */
+    uint64_t max_string_bytes;     /* per string */
+    uint64_t max_array_elements;   /* aggregate over the file */
+    uint64_t max_tensors;
+    uint64_t max_metadata_entries;
+    uint64_t max_metadata_bytes;   /* metadata section and tensor names */
+} lbk_gguf_limits;
+
+/* The primary shard's header facts, and the set's totals. */
+typedef struct lbk_gguf_file_info {
+    uint32_t version;       /* 2 or 3 */
+    uint32_t big_endian;    /* "FUGG" magic */
+    uint64_t alignment;     /* general.alignment, default 32 */
+    uint64_t shard_count;
+    uint64_t tensor_count;  /* all shards */
+    uint64_t metadata_count;
+    uint64_t data_offset;
+    uint64_t file_len;
+} lbk_gguf_file_info;
+
+/* One tensor of the directory (TensorLocation, bridge-gguf-split). */
+typedef struct lbk_gguf_tensor {
+    int32_t type;             /* ggml type discriminant */
+    uint32_t n_dims;
+    uint64_t dims[4];         /* ne[0..3], 1 past n_dims */
+    uint32_t shard;           /* 0-based shard ordinal */
+    uint64_t offset;          /* absolute byte offset in its shard */
+    uint64_t relative_offset; /* offset within the shard's data section */
+    uint64_t bytes;           /* encoded payload bytes */
+    uint64_t name_len;
+} lbk_gguf_tensor;
+
+/* One metadata value of the primary shard. */
+typedef struct lbk_gguf_value {
+    uint32_t type;          /* 0 U8 1 I8 2 U16 3 I16 4 U32 5 I32 6 F32 7 Bool 8 String 9 Array 10 U64 11 I64 12 F64 */
+    uint32_t element_type;  /* arrays */
+    uint64_t count;         /* arrays: elements; strings: bytes */
+    uint64_t u;             /* integers (signed ones sign-extended), bools; raw bits of floats */
+    double f;               /* F32 / F64 values */
+} lbk_gguf_value;
+
+void lbk_gguf_default_limits(lbk_gguf_limits* out);
+/* Opens the split set `entry` belongs to (open_set): a `<prefix>-NNNNN-of-
+ * MMMMM.gguf` name opens all MMMMM shards beside it (each with split.no and
+ * split.count), any other name one file. limits NULL = the defaults. */
+int32_t lbk_gguf_open(const char* entry, const lbk_gguf_limits* limits, lbk_gguf** out);
+int32_t lbk_gguf_close(lbk_gguf* gguf);
+int32_t lbk_gguf_info(const lbk_gguf* gguf, lbk_gguf_file_info* out);
+/* Tensor `index` in directory order; its name NUL-terminated into name
+ * (name_cap bytes, truncated) when name is not NULL. */
+int32_t lbk_gguf_tensor_at(const lbk_gguf* gguf, uint64_t index, lbk_gguf_tensor* out, char* name,
+                           uint64_t name_cap);
+int32_t lbk_gguf_find_tensor(const lbk_gguf* gguf, const char* name, uint64_t* index);
+int32_t lbk_gguf_metadata(const lbk_gguf* gguf, const char* key, lbk_gguf_value* out);
+int32_t lbk_gguf_metadata_string(const lbk_gguf* gguf, const char* key, char* buf, uint64_t cap, uint64_t* len);
+
+/* Builds an HBM-resident MoE layer from block `block` of a Hy3 GGUF set:
+ * checks general.architecture and the hy_v3.* configuration (resolve_config,
+ * bridge-model-hy3/src/config.rs:57-109) and the block's eight MoE tensors
+ * (schema.rs:200-258: router [H, E] and exp_probs_b [E] F32, stacked experts
+ * [H, F, E] / [F, H, E], shared expert), reads the router, the bias, the
+ * shared expert and routed experts [first_expert, first_expert +
+ * expert_count) -- each expert one slab of its stacked tensor
+ * (checked_expert_slab, schema.rs:524-580) -- repacks them to the planar
+ * layout and registers the layer as lbk_moe_layer_create (all experts) or
+ * lbk_ep_layer_create (a share) would. expert_count 0 = to the last expert.
+ * The layer owns its device memory. Weight types: IQ2_S, IQ3_S, Q4_K, Q5_K.
+ * Synchronizes `stream`; not on the hot path. */
+int32_t lbk_moe_layer_load(lbk_context* ctx, const lbk_gguf* gguf, uint32_t block, uint64_t first_expert,
+                           uint64_t expert_count, void* stream, lbk_moe_layer** out);
 
 #ifdef __cplusplus
 }

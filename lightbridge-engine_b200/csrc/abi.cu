@@ -21,9 +21,8 @@
 
 #include "lbk_iq_tables.h"
 #include "lbk_kernels.h"
+#include "lbk_host.h"
 #include "lbk_moe.h"
-
-#define LBK_API extern "C" __attribute__((visibility("default")))
 
 struct lbk_context {
     int device;
@@ -58,6 +57,7 @@ struct lbk_moe_layer {
     int gate_type, down_type, sgate_type, sdown_type;
     cudaEvent_t trace[4];
     bool tracing;
+    void* owned;                         // device memory freed with the layer (lbk_moe_layer_load)
 };
 
 namespace {
@@ -704,6 +704,25 @@ int32_t layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t E_rout
 
 }  // namespace
 
+namespace lbk {
+
+int32_t host_fail(int32_t status, const char* msg, uint64_t index, uint64_t expected, uint64_t actual, uint32_t bits) {
+    return fail(status, msg, index, expected, actual, bits);
+}
+
+int32_t host_ok() { return ok(); }
+
+int32_t host_set_device(lbk_context* ctx) { return set_device(ctx); }
+
+int32_t layer_create_owned(lbk_context* ctx, const lbk_moe_weights* w, uint64_t global_experts, uint64_t first_expert,
+                           void* stream, void* owned, lbk_moe_layer** out) {
+    const int32_t s = layer_create(ctx, w, global_experts, first_expert, stream, out);
+    if (s == LBK_OK) (*out)->owned = owned;
+    return s;
+}
+
+}  // namespace lbk
+
 LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w, void* stream, lbk_moe_layer** out) {
     return layer_create(ctx, w, w ? w->expert_count : 0, 0, stream, out);
 }
@@ -743,6 +762,7 @@ LBK_API int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer) {
     cudaSetDevice(layer->ctx->device);
     lbk_moe_layer_trace(layer, 0);
     cudaFree(layer->d_gate);
+    if (layer->owned) cudaFree(layer->owned);
     delete layer;
     return ok();
 }

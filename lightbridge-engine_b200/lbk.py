@@ -29,8 +29,12 @@ STATUS = {
     8: "NON_FINITE_ACTIVATION", 9: "NON_FINITE_Q8_SCALE", 10: "DIMENSION_MISMATCH", 11: "SCRATCH_TOO_SMALL",
     12: "NON_FINITE_VALUE", 13: "ROUTED_EXPERT_ORDER", 14: "DUPLICATE_ROUTED_EXPERT", 15: "INVALID_PARAMETER",
     16: "ROUTING_TOPK", 17: "ROUTING_LENGTH", 18: "NON_FINITE_ROUTING_VALUE", 30: "CUDA_ERROR", 31: "TIMEOUT",
-    32: "NO_DEVICE",
+    32: "NO_DEVICE", 33: "FORMAT_ERROR", 34: "IO_ERROR",
 }
+
+# GGUF value types (lbk_gguf_value.type)
+GGUF_U8, GGUF_I8, GGUF_U16, GGUF_I16, GGUF_U32, GGUF_I32, GGUF_F32, GGUF_BOOL = 0, 1, 2, 3, 4, 5, 6, 7
+GGUF_STRING, GGUF_ARRAY, GGUF_U64, GGUF_I64, GGUF_F64 = 8, 9, 10, 11, 12
 
 
 class ErrorDetail(ctypes.Structure):
@@ -73,6 +77,57 @@ class MoeWeights(ctypes.Structure):
         ("selection_bias", ctypes.c_void_p),
         ("top_k", ctypes.c_uint32),
         ("weight_scale", ctypes.c_float),
+    ]
+
+
+class GgufLimits(ctypes.Structure):
+    _fields_ = [
+        ("max_dimensions", ctypes.c_uint32),
+        ("max_string_bytes", ctypes.c_uint64),
+        ("max_array_elements", ctypes.c_uint64),
+        ("max_tensors", ctypes.c_uint64),
+        ("max_metadata_entries", ctypes.c_uint64),
+        ("max_metadata_bytes", ctypes.c_uint64),
+    ]
+
+
+class GgufFileInfo(ctypes.Structure):
+    _fields_ = [
+        ("version", ctypes.c_uint32),
+        ("big_endian", ctypes.c_uint32),
+        ("alignment", ctypes.c_uint64),
+        ("shard_count", ctypes.c_uint64),
+        ("tensor_count", ctypes.c_uint64),
+        ("metadata_count", ctypes.c_uint64),
+        ("data_offset", ctypes.c_uint64),
+        ("file_len", ctypes.c_uint64),
+    ]
+
+
+class GgufTensor(ctypes.Structure):
+    _fields_ = [
+        ("type", ctypes.c_int32),
+        ("n_dims", ctypes.c_uint32),
+        ("dims", ctypes.c_uint64 * 4),
+        ("shard", ctypes.c_uint32),
+        ("offset", ctypes.c_uint64),
+        ("relative_offset", ctypes.c_uint64),
+        ("bytes", ctypes.c_uint64),
+        ("name_len", ctypes.c_uint64),
+    ]
+
+    @property
+    def shape(self) -> tuple[int, ...]:
+        return tuple(self.dims[: self.n_dims])
+
+
+class GgufValue(ctypes.Structure):
+    _fields_ = [
+        ("type", ctypes.c_uint32),
+        ("element_type", ctypes.c_uint32),
+        ("count", ctypes.c_uint64),
+        ("u", ctypes.c_uint64),
+        ("f", ctypes.c_double),
     ]
 
 
@@ -138,6 +193,15 @@ def _load() -> ctypes.CDLL:
         "lbk_repack": ([P, PM, P, U64, P], I32),
         "lbk_unpack": ([P, PM, P, U64, P], I32),
         "lbk_validate_matrix": ([P, PM, P], I32),
+        "lbk_gguf_default_limits": ([ctypes.POINTER(GgufLimits)], None),
+        "lbk_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(GgufLimits), ctypes.POINTER(P)], I32),
+        "lbk_gguf_close": ([P], I32),
+        "lbk_gguf_info": ([P, ctypes.POINTER(GgufFileInfo)], I32),
+        "lbk_gguf_tensor_at": ([P, U64, ctypes.POINTER(GgufTensor), ctypes.c_char_p, U64], I32),
+        "lbk_gguf_find_tensor": ([P, ctypes.c_char_p, ctypes.POINTER(U64)], I32),
+        "lbk_gguf_metadata": ([P, ctypes.c_char_p, ctypes.POINTER(GgufValue)], I32),
+        "lbk_gguf_metadata_string": ([P, ctypes.c_char_p, ctypes.c_char_p, U64, ctypes.POINTER(U64)], I32),
+        "lbk_moe_layer_load": ([P, P, U32, U64, U64, P, ctypes.POINTER(P)], I32),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -156,7 +220,9 @@ EXPORTED = (
     "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward "
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine "
-    "lbk_repack lbk_unpack lbk_validate_matrix"
+    "lbk_repack lbk_unpack lbk_validate_matrix "
+    "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
+    "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
 ).split()
 
 
@@ -373,3 +439,101 @@ class EpLayer(MoeLayer):
     def combine(self, q8, tokens: int, routed, routed_dots, out, workspace, stream=None) -> None:
         check(lib.lbk_ep_combine(self.ptr, _ptr(q8), tokens, _ptr(routed), _ptr(routed_dots), _ptr(out),
                                  _ptr(workspace), workspace.numel(), _stream(stream)))
+
+
+class Gguf:
+    """A GGUF split set opened by the native reader (lbk_gguf_open): the
+    mirror of bridge-gguf-split's open_set / GgufSet and of GgufFile's typed
+    metadata getters (bridge-gguf/src/reader.rs:55-168)."""
+
+    def __init__(self, entry, limits: GgufLimits | None = None):
+        p = ctypes.c_void_p()
+        check(lib.lbk_gguf_open(str(entry).encode(), ctypes.byref(limits) if limits is not None else None,
+                                ctypes.byref(p)))
+        self.ptr = p
+
+    @staticmethod
+    def default_limits() -> GgufLimits:
+        lim = GgufLimits()
+        lib.lbk_gguf_default_limits(ctypes.byref(lim))
+        return lim
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def close(self) -> None:
+        if self.ptr:
+            lib.lbk_gguf_close(self.ptr)
+            self.ptr = None
+
+    def info(self) -> GgufFileInfo:
+        out = GgufFileInfo()
+        check(lib.lbk_gguf_info(self.ptr, ctypes.byref(out)))
+        return out
+
+    def tensors(self) -> list[tuple[str, GgufTensor]]:
+        out = []
+        for i in range(self.info().tensor_count):
+            t = GgufTensor()
+            check(lib.lbk_gguf_tensor_at(self.ptr, i, ctypes.byref(t), None, 0))
+            name = ctypes.create_string_buffer(t.name_len + 1)
+            check(lib.lbk_gguf_tensor_at(self.ptr, i, ctypes.byref(t), name, t.name_len + 1))
+            out.append((name.value.decode(), t))
+        return out
+
+    def tensor(self, name: str) -> GgufTensor:
+        i = ctypes.c_uint64()
+        check(lib.lbk_gguf_find_tensor(self.ptr, name.encode(), ctypes.byref(i)))
+        t = GgufTensor()
+        check(lib.lbk_gguf_tensor_at(self.ptr, i.value, ctypes.byref(t), None, 0))
+        return t
+
+    def value(self, key: str) -> GgufValue:
+        v = GgufValue()
+        check(lib.lbk_gguf_metadata(self.ptr, key.encode(), ctypes.byref(v)))
+        return v
+
+    def metadata(self, key: str):
+        """The primary shard's value for `key`: int, float, bool or str; for
+        arrays the tuple ("array", element_type, count)."""
+        v = self.value(key)
+        if v.type == GGUF_STRING:
+            n = ctypes.c_uint64()
+            buf = ctypes.create_string_buffer(v.count + 1)
+            check(lib.lbk_gguf_metadata_string(self.ptr, key.encode(), buf, v.count + 1, ctypes.byref(n)))
+            return buf.raw[: n.value].decode()
+        if v.type == GGUF_ARRAY:
+            return ("array", v.element_type, v.count)
+        if v.type in (GGUF_F32, GGUF_F64):
+            return v.f
+        if v.type == GGUF_BOOL:
+            return bool(v.u)
+        if v.type in (GGUF_I8, GGUF_I16, GGUF_I32, GGUF_I64):
+            return ctypes.c_int64(v.u).value
+        return v.u
+
+
+def load_layer(ctx: Context, gguf: Gguf, block: int, first_expert: int = 0, expert_count: int = 0,
+               stream=None) -> MoeLayer:
+    """HBM-resident MoE layer of block `block` read from a Hy3 GGUF set
+    (lbk_moe_layer_load): every routed expert (an MoeLayer), or the routed
+    experts [first_expert, first_expert + expert_count) of an expert-parallel
+    rank (an EpLayer)."""
+    p = ctypes.c_void_p()
+    check(lib.lbk_moe_layer_load(ctx.ptr, gguf.ptr, block, first_expert, expert_count, _stream(stream), ctypes.byref(p)))
+    experts = gguf.metadata("hy_v3.expert_count")
+    count = expert_count or experts - first_expert
+    layer = object.__new__(MoeLayer if (first_expert, count) == (0, experts) else EpLayer)
+    layer.ctx = ctx
+    layer.ptr = p
+    layer._keep = []
+    layer.top_k = gguf.metadata("hy_v3.expert_used_count")
+    layer.hidden = gguf.metadata("hy_v3.embedding_length")
+    if isinstance(layer, EpLayer):
+        layer.global_experts = experts
+        layer.first_expert = first_expert
+        layer.local_experts = count
+    return layer
