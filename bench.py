@@ -521,6 +521,8 @@ def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
     ctx = lbk.Context(local_rank)
     er = E // world
     layer, keep = build_ep_layer(ctx, lbk, torch, dev, 4 + 1000 * rank, rank * er, er)
+    if args.grouping is not None:
+        layer.set_grouping(args.grouping)
     moe = ep.ExpertParallelMoe(layer)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3 + rank)
@@ -565,10 +567,86 @@ def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": "config4: routed-MoE FFN layer, 64 tokens per step per GPU", "hidden": H,
                        "experts": E, "experts_per_gpu": er, "expert_ffn": F, "top_k": K_TOP,
                        "tokens_per_step_per_gpu": T, "parallelism": f"expert-parallel x{world}",
+                       "grouped_kernels": args.grouping != 0,
                        "exchange": "NCCL all_to_all_single (counts, Q8_K rows, row dots)"},
         }
         print(json.dumps(line), flush=True)
     layer.close()
+    ctx.close()
+
+
+def batched_direct_arm(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 4's layer without expert parallelism: one lbk_moe_forward call of
+    BATCH_TOKENS tokens per resident layer (all 192 experts on this GPU),
+    rotating over LAYERS layers (larger than L2), one CUDA graph per step.
+    With N > 1, N independent replicas (weak scaling)."""
+    import torch
+
+    import lbk
+
+    T = BATCH_TOKENS
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = lbk.Context(local_rank)
+    tables, _ = build_layers(ctx, lbk, torch, dev, LAYERS, 4 + 97 * rank, keep_gguf_layer0=False)
+    if args.grouping is not None:
+        for layer, _ in tables:
+            layer.set_grouping(args.grouping)
+    ws = torch.zeros(tables[0][0].workspace_bytes(T), dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 + rank)
+    xs = torch.randn(LAYERS, T * H, device=dev, generator=gen)
+    outs = torch.zeros(LAYERS, T * H, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(s):
+        for l, (layer, _) in enumerate(tables):
+            layer.forward(xs[l], T, outs[l], ws, stream=s.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        step(stream)
+        stream.synchronize()
+        ctx.raise_status(stream.cuda_stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream)
+        for _ in range(args.warmup):
+            graph.replay()
+        stream.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        stream.synchronize()
+    ctx.raise_status(stream.cuda_stream)
+    ms = ev0.elapsed_time(ev1) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "routed-MoE batched tokens/s (config 4 layer, 64 tokens per call, all experts on one GPU)",
+            "value": T * LAYERS * world / (ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q8_k x packed (int8 dots, f32 tails)",
+            "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": f"config4 layer: {LAYERS} calls of {T} tokens per step, one per resident layer",
+                       "hidden": H, "experts": E, "expert_ffn": F, "top_k": K_TOP, "tokens_per_call": T,
+                       "us_per_call": ms * 1000.0 / LAYERS, "grouped_kernels": args.grouping != 0,
+                       "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
+        }), flush=True)
+    del graph
     ctx.close()
 
 
@@ -672,6 +750,8 @@ def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
     layers = []
     for l in range(args.stack_layers):
         t, _ = build_layers(ctx, lbk, torch, dev, 1, 4 + l + 1000 * rank, keep_gguf_layer0=False)
+        if args.grouping is not None:
+            t[0][0].set_grouping(args.grouping)
         layers.append(t[0])
     ws = torch.zeros(layers[0][0].block_workspace_bytes(B), dtype=torch.uint8, device=dev)
     gen = torch.Generator(device=dev)
@@ -718,6 +798,7 @@ def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
             "data": "synthetic (seeded, config shapes)",
             "config": {"workload": f"config5: {args.stack_layers}-layer stack, batch {B}", "layers": args.stack_layers,
                        "batch": B, "resident_gb": round(args.stack_layers * 1.3066, 1),
+                       "grouped_kernels": B >= 2 and args.grouping != 0,
                        "us_per_layer_step": ms * 1000.0 / args.stack_layers,
                        "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
         }), flush=True)
@@ -737,6 +818,10 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=3,
                     help="3: single-token decode (the headline); 4: 64 tokens per step per GPU, expert-parallel; "
                          "1, 2: single quantized matvec; 5: 80-layer stack")
+    ap.add_argument("--direct", action="store_true",
+                    help="config 4: all experts on every GPU, one lbk_moe_forward call per layer (no expert parallelism)")
+    ap.add_argument("--grouping", type=int, default=None,
+                    help="configs 4, 5: token count from which the grouped kernels run (0: never; default: the library's)")
     ap.add_argument("--profile-forwards", type=int, default=0,
                     help="profiling driver: one resident layer, this many single-token forwards, no timing")
     args = ap.parse_args()
@@ -759,7 +844,9 @@ def main() -> None:
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     try:
-        if args.config == 4:
+        if args.config == 4 and args.direct:
+            batched_direct_arm(args, rank, world, local_rank)
+        elif args.config == 4:
             batched_ep_arm(args, rank, world, local_rank)
         elif args.config in (1, 2):
             gemv_arm(args, args.config, rank, world, local_rank)

@@ -263,6 +263,16 @@ int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer);
 /* 1 when the fused kernels are used, 0 for the per-expert path. */
 int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer);
 
+/* Token count from which lbk_moe_forward / lbk_moe_routed (and, counted in
+ * items, lbk_ep_items_forward; in tokens, lbk_ep_combine) run the grouped
+ * kernels on a fused planar layer: the call's (token, slot) pairs are grouped
+ * by expert and each weight half block is decoded once for every pair of its
+ * group. Results are bit-identical either way; only the speed differs.
+ * min_tokens 0 turns grouping off; the default is 8. No counterpart in the
+ * reference, which runs each routed expert per token
+ * (moe_routed_by_id_into, moe.rs:64-147). */
+int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens);
+
 /* Workspace bytes for `tokens` tokens. The workspace must be zero-filled once
  * before its first use (its first 16 bytes hold an arrival counter that every
  * completed call leaves at zero; the rest is rewritten by every call), so one

@@ -11,6 +11,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -58,6 +59,7 @@ struct lbk_moe_layer {
     cudaEvent_t trace[4];
     bool tracing;
     void* owned;                         // device memory freed with the layer (lbk_moe_layer_load)
+    uint64_t group_min = 8;              // calls of at least this many tokens (items) run the grouped kernels; 0: never
 };
 
 namespace {
@@ -189,6 +191,7 @@ int32_t run_f32_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, uint
 
 struct WsLayout {
     uint64_t rcounter, logits, partials, q8x, routed, h, hq, counters, dcounters, counter_words, dots, g, u, total;
+    uint64_t grp_n, grp, grp_pairs;  // grouped kernels (T >= 2): group count, groups, grouped pairs
 };
 
 uint64_t up256(uint64_t v) { return (v + 255) & ~(uint64_t)255; }
@@ -226,6 +229,13 @@ WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T, uint64_t k) {
     off = up256(off + L->F * 4);
     o.u = off;
     off = up256(off + L->F * 4 + (L->F > L->H ? L->F : L->H) / LBK_QK_K * LBK_Q8K_BLOCK_BYTES);
+    if (T >= 2) {  // the grouping of a several-token call: [count][groups {expert, first, pairs, 0}][pairs]
+        const uint64_t pairs = T * (k ? k : 1);
+        o.grp_n = off;
+        o.grp = off + 16;
+        o.grp_pairs = o.grp + pairs * 16;
+        off = up256(o.grp_pairs + pairs * 4);
+    }
     o.total = off;
     return o;
 }
@@ -769,6 +779,12 @@ LBK_API int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer) {
 
 LBK_API int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer) { return layer && layer->fused ? 1 : 0; }
 
+LBK_API int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    layer->group_min = min_tokens;
+    return ok();
+}
+
 LBK_API int32_t lbk_moe_workspace_bytes(const lbk_moe_layer* layer, uint64_t tokens, uint64_t* bytes) {
     if (layer == nullptr || bytes == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
     if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
@@ -818,6 +834,126 @@ struct MoeMode {
 
 MoeMode full_mode(const lbk_moe_layer* L) { return MoeMode{L->k, true, true, nullptr, nullptr, (uint32_t)(L->k + 1)}; }
 
+// Share of a grouped item's per-half-block time spent decoding (once per
+// group) rather than dotting (once per pair): IQ decode is most of a half
+// block's work, a K-quant half block is dotted straight from its packed bytes.
+double grp_decode_share(int32_t ty) { return ty == LBK_TYPE_IQ2_S || ty == LBK_TYPE_IQ3_S ? 0.6 : 0.15; }
+
+// Expected routed groups of a call: pairs spread over the experts hit, cut
+// into runs of at most gsize.
+double grp_groups_est(double pairs, double experts, double gsize) {
+    const double hit = experts * (1.0 - std::pow(1.0 - 1.0 / experts, pairs));
+    const double runs = std::ceil(pairs / gsize);
+    return 1.15 * (hit > runs ? hit : runs);
+}
+
+// Expert stage of a several-token call on the grouped kernels: the routed
+// pairs are grouped by expert, then gate/up + SwiGLU and down (+ combine) run
+// with each weight half block decoded once per group. Same results, bit for
+// bit, as the per-(token, slot) kernels.
+int32_t moe_experts_grouped(lbk_moe_layer* L, uint64_t T, const lbk_routed* routed, float* out, uint8_t* ws,
+                            const WsLayout& o, cudaStream_t st, const MoeMode& mode) {
+    lbk_context* ctx = L->ctx;
+    cudaError_t e = cudaSuccess;
+    const uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
+    const uint64_t K = mode.k;
+    const unsigned ctas = (unsigned)ctx->sm_count;
+    const lbk::GrpShape sgu = lbk::moe_gate_up_grp_shape(L->gate_type, L->sgate_type);
+    const lbk::GrpShape sdn = lbk::moe_down_grp_shape(L->down_type, L->sdown_type);
+    const uint32_t gr = std::min(sgu.routed, sdn.routed), gs = std::min(sgu.shared, sdn.shared);
+    uint32_t* grp_n = reinterpret_cast<uint32_t*>(ws + o.grp_n);
+    const uint4* grp = reinterpret_cast<const uint4*>(ws + o.grp);
+    uint32_t* grp_pairs = reinterpret_cast<uint32_t*>(ws + o.grp_pairs);
+    if (K > 0) {
+        lbk::MoeGroupArgs ga{routed, T, K, L->E_local, gr, grp_n, const_cast<uint4*>(grp), grp_pairs, ctx->status};
+        if ((e = lbk::launch_moe_group(ga, st)) != cudaSuccess) return cuda_fail(e, "moe grouping launch");
+    }
+    const double pairs = (double)(T * K);
+    const double groups_r = K ? grp_groups_est(pairs, (double)L->E_local, gr) : 0.0;
+    const double groups_s = std::ceil((double)T / gs);
+    auto role_work = [&](int32_t ty, double groups, double n) {
+        const double d = grp_decode_share(ty);
+        return hb_cost_us(ty) * (d * groups + (1.0 - d) * n);
+    };
+
+    lbk::MoeGateUpArgs g{};
+    g.hidden = L->H;
+    g.ffn = L->F;
+    g.nb_h = (int)nbh;
+    g.nb_f = (int)nbf;
+    int slots_unused = 0;
+    lbk::gemv_plan(L->gate_type, (int)nbh, &g.tpr_h, &slots_unused);
+    g.tokens = T;
+    g.k = K;
+    g.experts = L->E_local;
+    g.gate = L->d_gate;
+    g.up = L->d_up;
+    g.sgate = static_cast<const uint8_t*>(L->w.shared.gate.data);
+    g.sup = static_cast<const uint8_t*>(L->w.shared.up.data);
+    g.routed = routed;
+    g.q8x = mode.q8x ? mode.q8x : ws + o.q8x;
+    g.has_shared = mode.shared ? 1 : 0;
+    g.h = reinterpret_cast<float*>(ws + o.h);
+    g.hq = ws + o.hq;
+    g.counters = reinterpret_cast<unsigned int*>(ws + o.counters);
+    g.grp_n = grp_n;
+    g.grp = grp;
+    g.grp_pairs = grp_pairs;
+    g.gsize_r = gr;
+    g.gsize_s = gs;
+    g.status = ctx->status;
+    g.tables = ctx->tables();
+    {
+        const double hb = 2.0 * nbh * 2.0 * L->F;  // half blocks of one slot (gate + up)
+        const long rc = K == 0 ? 0
+                        : !mode.shared ? (long)ctas
+                                       : split_roles(ctas, (int)sgu.warps, hb * role_work(L->gate_type, groups_r, pairs),
+                                                     1.5, hb * role_work(L->sgate_type, groups_s, (double)T), 1.0);
+        g.routed_ctas = (uint32_t)rc;
+    }
+    if ((e = lbk::launch_moe_gate_up_grp(L->gate_type, L->sgate_type, g, ctas, st)) != cudaSuccess)
+        return cuda_fail(e, "moe grouped gate/up launch");
+    if (L->tracing) trace_record(L->trace[2], st, cudaEventRecordExternal);
+
+    lbk::MoeDownArgs d{};
+    d.hidden = L->H;
+    d.ffn = L->F;
+    d.nb_f = (int)nbf;
+    lbk::gemv_plan(L->down_type, (int)nbf, &d.tpr_f, &slots_unused);
+    d.tokens = T;
+    d.k = K;
+    d.experts = L->E_local;
+    d.down = L->d_down;
+    d.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);
+    d.routed = routed;
+    d.hq = ws + o.hq;
+    d.out = out;
+    d.dots = mode.dots ? mode.dots : reinterpret_cast<float*>(ws + o.dots);
+    d.dots_slots = mode.dots_slots;
+    d.combine = mode.combine ? 1 : 0;
+    d.has_shared = mode.shared ? 1 : 0;
+    d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
+    d.grp_n = grp_n;
+    d.grp = grp;
+    d.grp_pairs = grp_pairs;
+    d.gsize_r = gr;
+    d.gsize_s = gs;
+    d.status = ctx->status;
+    d.tables = ctx->tables();
+    {
+        const double lanes = (double)L->H * d.tpr_f;  // lane slots of one slot's rows
+        const long rc = K == 0 ? 0
+                        : !mode.shared ? (long)ctas
+                                       : split_roles(ctas, (int)sdn.warps, lanes * role_work(L->down_type, groups_r, pairs),
+                                                     2.0, lanes * role_work(L->sdown_type, groups_s, (double)T), 1.5);
+        d.routed_ctas = (uint32_t)rc;
+    }
+    if ((e = lbk::launch_moe_down_grp(L->down_type, L->sdown_type, d, ctas, st)) != cudaSuccess)
+        return cuda_fail(e, "moe grouped down launch");
+    if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);
+    return ok();
+}
+
 // Expert stage of one MoE call for `tokens` tokens with routing in `routed`.
 // With defer_topk (single token, fused kernels) the routing is computed by the
 // gate/up kernel from the router's chunk partials and stored into `routed`.
@@ -833,6 +969,10 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
     if (!full && !(L->fused && lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)nbh) &&
                    lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)))
         return fail(LBK_INVALID_PARAMETER, "expert-parallel calls need planar layers with hidden 2048 or 4096");
+    if (L->fused && !defer_topk && L->group_min != 0 && T >= L->group_min && T >= 2 && L->E_local <= 1024 &&
+        T * K <= 8192 &&
+        lbk::moe_grouped_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type, (int)nbh, (int)nbf))
+        return moe_experts_grouped(L, T, routed, out, ws, o, st, mode);
     if (L->fused) {
         lbk::MoeGateUpArgs g{};
         g.defer_topk = defer_topk ? 1 : 0;

@@ -848,61 +848,81 @@ __device__ __forceinline__ KPart dot_hb(const Q5HB& w, const ActHB& a, int h) {
 }
 
 // ------------------------------------------------ decode once, dot many
-// For several tokens on the same weights (a grouped expert): a half block is
-// decoded once into signed int8 words in the activation word order, then
-// dotted with each token's activations. The integer sums are the ones of
-// dot_hb (the same products, summed in another order), so every block sum is
-// identical.
+// For several tokens on the same weights (a grouped expert): each 32-weight
+// group of a half block is decoded once into signed int8 words, in the
+// activation word order, and dotted at once with the activations of every
+// pair of the group (only one group's 8 decoded words are live). The integer
+// sums are those of dot_hb -- the same products, summed in another order --
+// so every block sum is identical.
 
-struct DecHB {
-    uint32_t w[32];  // signed weights (IQ), or the 4-bit quants (K-quants)
-    uint32_t s0, s1;  // IQ2_S: scale multipliers (1 + 2 * nibble) of the four groups' two halves; IQ3_S: pair scales
-    uint32_t d;       // block scale(s): binary16 d (IQ), or d | dmin << 16 (K)
-    int32_t sk[4];    // K-quants: scales of sub-blocks (lo, hi) x (gg 0, 1)
-    int32_t mk[4];    // K-quants: mins
+// Byte-wise negation of four grid magnitudes in [1, 127]: ~g + 1 per byte
+// never carries into the next byte.
+__device__ __forceinline__ uint32_t neg4_nonzero(uint32_t g) { return ~g + 0x01010101u; }
+
+// Activations of the pairs of a group, as words gi*8 .. gi*8+7 (lo: the
+// first four) of pair p's half block held in registers.
+struct ActReg {
+    const ActHB* a;
+    __device__ __forceinline__ void operator()(int p, int gi, uint4& lo, uint4& hi) const {
+        lo = make_uint4(a[p].w[gi * 8 + 0], a[p].w[gi * 8 + 1], a[p].w[gi * 8 + 2], a[p].w[gi * 8 + 3]);
+        hi = make_uint4(a[p].w[gi * 8 + 4], a[p].w[gi * 8 + 5], a[p].w[gi * 8 + 6], a[p].w[gi * 8 + 7]);
+    }
 };
 
-// IQ2_S (dot_iq2_s, q8_k.rs:339-364): the signed grid bytes of dot_hb.
-__device__ __forceinline__ void decode_hb(const Iq2HB& w, DecHB& o, uint32_t code_base, uint32_t sign_base) {
-    o.s0 = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;
-    o.s1 = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;
-    o.d = w.d;
+// IQ2_S (dot_iq2_s, q8_k.rs:339-364) over groups 4h..4h+3 for pairs p < n:
+// tot[p] = the half block's integer sum against pair p's activations.
+// kStride: bytes between table entries (the lane's copy at base).
+template <int G, int kStride, class Act>
+__device__ __forceinline__ void dot_hb_multi(const Iq2HB& w, const Act& act, uint32_t n, uint32_t code_base,
+                                             uint32_t sign_base, int32_t* tot) {
+    const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;
+    const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;
+#pragma unroll
+    for (int p = 0; p < G; p++) tot[p] = 0;
 #pragma unroll
     for (int gi = 0; gi < 4; gi++) {
         const uint32_t qsw = w32(w.qs, gi);
         const uint32_t sgw = w32(w.sg, gi);
         const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
+        uint32_t wd[8];
 #pragma unroll
         for (int l = 0; l < 4; l++) {
-            const uint32_t code = lds32(prmt(qsw, Q, sel_idx(l, l)) * 128u + code_base);
-            const uint32_t sp = lds32(prmt(sgw, Q, sel_byte(l, l)) * 128u + sign_base);
+            const uint32_t code = lds32(prmt(qsw, Q, sel_idx(l, l)) * (uint32_t)kStride + code_base);
+            const uint32_t sp = lds32(prmt(sgw, Q, sel_byte(l, l)) * (uint32_t)kStride + sign_base);
             const uint32_t sel = code | sp;
-            o.w[gi * 8 + 2 * l] = prmt(kIq2PoolPos, kIq2PoolNeg, sel);
-            o.w[gi * 8 + 2 * l + 1] = prmt(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
+            wd[2 * l] = prmt(kIq2PoolPos, kIq2PoolNeg, sel);
+            wd[2 * l + 1] = prmt(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
+        }
+        const int32_t s1 = (int32_t)prmt(s1w, 0, 0x4440u | gi);
+        const int32_t s2 = (int32_t)prmt(s2w, 0, 0x4440u | gi);
+#pragma unroll
+        for (int p = 0; p < G; p++) {
+            if ((uint32_t)p < n) {
+                uint4 lo, hi;
+                act(p, gi, lo, hi);
+                int32_t p0 = dp4a(wd[0], lo.x, 0), p1 = dp4a(wd[4], hi.x, 0);
+                p0 = dp4a(wd[1], lo.y, p0);
+                p1 = dp4a(wd[5], hi.y, p1);
+                p0 = dp4a(wd[2], lo.z, p0);
+                p1 = dp4a(wd[6], hi.z, p1);
+                p0 = dp4a(wd[3], lo.w, p0);
+                p1 = dp4a(wd[7], hi.w, p1);
+                tot[p] += s1 * p0 + s2 * p1;
+            }
         }
     }
 }
-__device__ __forceinline__ IqPart dot_dec_iq2(const DecHB& o, const ActHB& a) {
-    int32_t total = 0;
-#pragma unroll
-    for (int gi = 0; gi < 4; gi++) {
-        int32_t p0 = 0, p1 = 0;
-#pragma unroll
-        for (int i = 0; i < 4; i++) p0 = dp4a(o.w[gi * 8 + i], a.w[gi * 8 + i], p0);
-#pragma unroll
-        for (int i = 4; i < 8; i++) p1 = dp4a(o.w[gi * 8 + i], a.w[gi * 8 + i], p1);
-        total += (int32_t)prmt(o.s0, 0, 0x4440u | gi) * p0 + (int32_t)prmt(o.s1, 0, 0x4440u | gi) * p1;
-    }
-    return IqPart{total, o.d};
-}
 
 // IQ3_S (dot_iq3_s, q8_k.rs:380-428): the grid bytes with the sign bits
-// applied to the weights (byte-wise a or -a selection, as dot_hb applies them
-// to the activations: the same products).
-__device__ __forceinline__ void decode_hb(const Iq3HB& w, DecHB& o, uint32_t grid_base, uint32_t sel_base) {
+// applied to the weights (byte-wise g or -g selection with dot_hb's
+// selectors, which apply them to the activations: the same products).
+template <int G, int kStride, class Act>
+__device__ __forceinline__ void dot_hb_multi(const Iq3HB& w, const Act& act, uint32_t n, uint32_t grid_base,
+                                             uint32_t sel_base, int32_t* tot) {
     const uint32_t st = (w.sc & 0x0f0fu) | ((w.sc & 0xf0f0u) << 12);
-    o.s0 = st * 2u + 0x01010101u;
-    o.d = w.d;
+    const uint32_t sw = st * 2u + 0x01010101u;
+#pragma unroll
+    for (int p = 0; p < G; p++) tot[p] = 0;
 #pragma unroll
     for (int gi = 0; gi < 4; gi++) {
         const uint32_t qa = gi < 2 ? w32(w.qs0, gi * 2) : w32(w.qs1, (gi - 2) * 2);
@@ -911,65 +931,34 @@ __device__ __forceinline__ void decode_hb(const Iq3HB& w, DecHB& o, uint32_t gri
         const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
         const uint32_t Q1 = Q & 0x01010101u;
         const uint32_t Q2 = (Q >> 1) & 0x01010101u;
+        uint32_t wd[8];
 #pragma unroll
         for (int l = 0; l < 4; l++) {
             const uint32_t q2 = l < 2 ? qa : qb;
-            const uint32_t g1 = lds32(prmt(q2, Q1, sel_idx(2 * (l & 1), l)) * 128u + grid_base);
-            const uint32_t g2 = lds32(prmt(q2, Q2, sel_idx(2 * (l & 1) + 1, l)) * 128u + grid_base);
-            const uint32_t ss = lds32(prmt(sgw, Q1, sel_byte(l, l)) * 128u + sel_base);
-            o.w[gi * 8 + 2 * l] = prmt(g1, (uint32_t)__vneg4((int)g1), ss);
-            o.w[gi * 8 + 2 * l + 1] = prmt(g2, (uint32_t)__vneg4((int)g2), ss >> 16);
+            const uint32_t g1 = lds32(prmt(q2, Q1, sel_idx(2 * (l & 1), l)) * (uint32_t)kStride + grid_base);
+            const uint32_t g2 = lds32(prmt(q2, Q2, sel_idx(2 * (l & 1) + 1, l)) * (uint32_t)kStride + grid_base);
+            const uint32_t ss = lds32(prmt(sgw, Q1, sel_byte(l, l)) * (uint32_t)kStride + sel_base);
+            wd[2 * l] = prmt(g1, neg4_nonzero(g1), ss);
+            wd[2 * l + 1] = prmt(g2, neg4_nonzero(g2), ss >> 16);
+        }
+        const int32_t scale = (int32_t)prmt(sw, 0, 0x4440u | (uint32_t)((gi & 1) * 2 + (gi >> 1)));
+#pragma unroll
+        for (int p = 0; p < G; p++) {
+            if ((uint32_t)p < n) {
+                uint4 lo, hi;
+                act(p, gi, lo, hi);
+                int32_t g = dp4a(wd[0], lo.x, 0);
+                g = dp4a(wd[1], lo.y, g);
+                g = dp4a(wd[2], lo.z, g);
+                g = dp4a(wd[3], lo.w, g);
+                g = dp4a(wd[4], hi.x, g);
+                g = dp4a(wd[5], hi.y, g);
+                g = dp4a(wd[6], hi.z, g);
+                g = dp4a(wd[7], hi.w, g);
+                tot[p] += g * scale;
+            }
         }
     }
-}
-__device__ __forceinline__ IqPart dot_dec_iq3(const DecHB& o, const ActHB& a) {
-    int32_t total = 0;
-#pragma unroll
-    for (int gi = 0; gi < 4; gi++) {
-        int32_t g = 0;
-#pragma unroll
-        for (int i = 0; i < 8; i++) g = dp4a(o.w[gi * 8 + i], a.w[gi * 8 + i], g);
-        total += g * (int32_t)prmt(o.s0, 0, 0x4440u | (uint32_t)((gi & 1) * 2 + (gi >> 1)));
-    }
-    return IqPart{total, o.d};
-}
-
-// Q4_K (dot_q4_or_q5_k, q8_k.rs:257-312): the low / high nibbles and the
-// (scale, min) pairs of sub-blocks 4h..4h+3.
-__device__ __forceinline__ void decode_hb_q4(const Q4HB& w, DecHB& o, int h) {
-    o.d = w.dm;
-#pragma unroll
-    for (int gg = 0; gg < 2; gg++) {
-        const int g = 2 * h + gg;
-        scale_min_dev(w.sc, 2 * g, o.sk[2 * gg], o.mk[2 * gg]);
-        scale_min_dev(w.sc, 2 * g + 1, o.sk[2 * gg + 1], o.mk[2 * gg + 1]);
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const uint32_t q = w32(w.qs[2 * gg + (k >> 2)], k & 3);
-            o.w[gg * 16 + k] = q & 0x0f0f0f0fu;
-            o.w[gg * 16 + 8 + k] = (q >> 4) & 0x0f0f0f0fu;
-        }
-    }
-}
-__device__ __forceinline__ KPart dot_dec_q4(const DecHB& o, const ActHB& a) {
-    KPart r;
-#pragma unroll
-    for (int l = 0; l < 8; l++) r.lane[l] = 0;
-    int32_t ms = 0;
-#pragma unroll
-    for (int gg = 0; gg < 2; gg++) {
-        ms += (a.bsum[4 * gg + 0] + a.bsum[4 * gg + 1]) * o.mk[2 * gg];
-        ms += (a.bsum[4 * gg + 2] + a.bsum[4 * gg + 3]) * o.mk[2 * gg + 1];
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            const int32_t plo = dp4a(o.w[gg * 16 + k], a.w[8 * (2 * gg) + k], 0);
-            const int32_t phi = dp4a(o.w[gg * 16 + 8 + k], a.w[8 * (2 * gg + 1) + k], 0);
-            r.lane[k] += o.sk[2 * gg] * plo + o.sk[2 * gg + 1] * phi;
-        }
-    }
-    r.min_sum = ms;
-    r.dm = o.d;
-    return r;
 }
 
 // ------------------------------------------------------------ block products

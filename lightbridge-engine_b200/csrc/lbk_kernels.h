@@ -74,6 +74,7 @@ struct RouterFusedArgs {
     float weight_scale;
     lbk_routed* routed;     // [tokens][k], or null (logits only)
     int defer;              // 1: leave the chunk partials for the consumer (no last-CTA pass)
+    int split;              // 1: logits and top-k in a second launch, one warp per token (set by the launcher)
     unsigned int* zero;     // arrival counters of the launches that follow, zeroed here
     uint64_t zero_words;
 };

@@ -46,6 +46,11 @@ struct MoeGateUpArgs {
     const uint8_t* const* down;
     const uint8_t* sdown;
     uint32_t down_rs, sdown_rs;
+    // grouped kernels: the routed pairs grouped by expert (moe_group_kernel)
+    const uint32_t* grp_n;           // [1] routed groups
+    const uint4* grp;                // [groups] {expert, first pair, pairs, 0}
+    const uint32_t* grp_pairs;       // [tokens*k] routed index t*k + j, grouped by expert
+    uint32_t gsize_r, gsize_s;       // pairs per group: routed / shared expert
     DeviceStatus* status;
     Tables tables;
 };
@@ -75,6 +80,11 @@ struct MoeDownArgs {
     int combine;                     // 1: form `out` from the dots (else leave the dots)
     int has_shared;                  // 0: no shared-expert CTAs
     unsigned int* counters;          // [tokens][hidden/64] arrivals, zero between launches
+    // grouped kernels (see MoeGateUpArgs)
+    const uint32_t* grp_n;
+    const uint4* grp;
+    const uint32_t* grp_pairs;
+    uint32_t gsize_r, gsize_s;
     DeviceStatus* status;
     Tables tables;
 };
@@ -99,6 +109,35 @@ cudaError_t launch_ep_combine(const lbk_routed* routed, const float* routed_dots
 // Bulk-copy-staged down over `ctas` CTAs (planar, nb_f <= 16).
 bool moe_down_tma_supported(int down_type, int shared_down_type, int nb_f);
 cudaError_t launch_moe_down_tma(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
+                                cudaStream_t stream);
+
+// Grouped kernels (several tokens per call): the (token, slot) pairs of a
+// call are grouped by routed expert, and each weight half block is decoded
+// once for all pairs of its group.
+struct MoeGroupArgs {
+    const lbk_routed* routed;        // [tokens][k]
+    uint64_t tokens, k, experts;
+    uint32_t gsize;                  // pairs per group at most
+    uint32_t* n;                     // [1] groups written
+    uint4* groups;                   // [tokens*k] {expert, first pair, pairs, 0}
+    uint32_t* pairs;                 // [tokens*k] routed index t*k + j, grouped by expert, ascending in t
+    DeviceStatus* status;
+};
+
+// Pairs per group the grouped kernels of a type pair take (the activations
+// of every pair of a group sit in registers), and their warps per CTA.
+struct GrpShape {
+    uint32_t routed, shared, warps;
+};
+GrpShape moe_gate_up_grp_shape(int gate_type, int shared_gate_type);
+GrpShape moe_down_grp_shape(int down_type, int shared_down_type);
+// Whether the grouped kernels take these types / widths (the bulk-copy ones).
+bool moe_grouped_supported(int gate_type, int shared_gate_type, int down_type, int shared_down_type, int nb_h, int nb_f);
+cudaError_t launch_moe_group(const MoeGroupArgs& a, cudaStream_t stream);
+
+cudaError_t launch_moe_gate_up_grp(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
+                                   cudaStream_t stream);
+cudaError_t launch_moe_down_grp(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
                                 cudaStream_t stream);
 
 }  // namespace lbk

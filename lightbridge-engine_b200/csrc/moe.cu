@@ -1085,6 +1085,581 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
     }
 }
 
+// ------------------------------------------------------ grouped (T tokens)
+//
+// Calls of several tokens (multi-sequence decode, short prefill, the items an
+// expert-parallel rank received). The routed (token, slot) pairs are grouped
+// by expert (moe_group_kernel); a warp item is (group, chunk of rows). A
+// lane's half-block position is fixed for the whole item, so the activation
+// half block of every pair of the group is loaded once into registers; each
+// weight half block is then decoded once and dotted with all of them. The
+// integer block sums, f32 block products and per-row tails are those of the
+// single-token kernels, so every (token, slot) result is bit-identical to
+// theirs. The shared expert is grouped the same way over consecutive tokens.
+
+constexpr int kGrpDots = 64;  // dots per tail batch at most
+
+// Pairs per group with W warps per CTA: each pair's activation half block is
+// 33 registers (IQ) or 41 (K-quants), out of 255 a thread at 8 warps, 170 at
+// 12 and 128 at 16.
+template <int T, int W>
+constexpr int grp_max() {
+    return is_iq<T>() ? (W <= 8 ? 4 : (W <= 12 ? 3 : 2)) : (W <= 8 ? 2 : 1);
+}
+
+// Shared-memory plan of one grouped CTA role streaming type T with kMats
+// matrices per unit (gate + up: one stage of both; down: two stages of one).
+template <int T, int kMats, int W>
+struct GrpRole {
+    static constexpr bool kIq = is_iq<T>();
+    static constexpr int kBB = TypeInfo<T>::kBlockBytes;
+    static constexpr int kUnit = 16 * kBB + (kMats == 1 ? 256 : 0);  // down rows are each padded to 16 bytes
+    static constexpr int kStage = 2 * kUnit;
+    static constexpr int kTail = TypeInfo<T>::kTail;
+    static constexpr int kProd = kIq ? (W <= 8 ? 512 : 256) : (W <= 8 ? 1152 : 576);  // floats per warp
+    static constexpr int kChain = kIq ? 0 : kGrpDots * 9;
+    static constexpr int kRes = kGrpDots;
+    static constexpr int kTab = table_bytes<T>();
+    static constexpr int kSign = kIq ? kSignBytes : 0;
+    static constexpr int kRingOff = kTab + kSign;
+    static constexpr int kProdOff = kRingOff + W * kStage;
+    static constexpr int kChainOff = kProdOff + W * kProd * 4;
+    static constexpr int kResOff = kChainOff + W * kChain * 4;
+    static constexpr int kBytes = kResOff + W * kRes * 4;
+    // one unit of the largest group always fits a tail batch (R * nb <= 16)
+    static_assert(16 * kMats * grp_max<T, W>() * kTail <= kProd, "grouped product buffer");
+    // dots of one unit: R * kMats * pairs, R <= 2 for gate/up (nb_h 8 or 16), R <= 16 for down
+    static_assert((kMats == 2 ? 2 : 16) * kMats * grp_max<T, W>() <= kGrpDots, "grouped dot buffer");
+};
+
+// The dots of one half block against the pairs p < n of a group: IQ types
+// decode each 32-weight group once for all pairs (dot_hb_multi); a K-quant
+// half block is dotted per pair straight from its packed words (its decode is
+// two masks per word).
+template <int T, int G>
+__device__ __forceinline__ void grp_dots(const typename HBOf<T>::type& w, const ActHB* act, uint32_t n, uint32_t t0,
+                                         uint32_t t1, int h, IqPart* ip, KPart* kp) {
+    if constexpr (is_iq<T>()) {
+        int32_t tot[G];
+        dot_hb_multi<G, 128>(w, ActReg{act}, n, t0, t1, tot);
+#pragma unroll
+        for (int p = 0; p < G; p++) ip[p] = IqPart{tot[p], w.d};
+    } else {
+#pragma unroll
+        for (int p = 0; p < G; p++)
+            if ((uint32_t)p < n) kp[p] = dot_hb(w, act[p], h);
+    }
+    (void)t0;
+    (void)t1;
+    (void)h;
+}
+
+template <int G>
+__device__ __forceinline__ void grp_zero(IqPart* ip, KPart* kp) {
+#pragma unroll
+    for (int p = 0; p < G; p++) {
+        ip[p] = IqPart{0, 0};
+#pragma unroll
+        for (int l = 0; l < 8; l++) kp[p].lane[l] = 0;
+        kp[p].min_sum = 0;
+        kp[p].dm = 0;
+    }
+}
+
+// The pairs of group gi: routed groups from the grouping kernel's table
+// (expert, first pair, count), shared groups as runs of consecutive tokens.
+// Returns the pair count; tp / sp receive each pair's token and slot.
+template <int G, bool kRouted>
+__device__ __forceinline__ uint32_t grp_pairs(const uint4* grp, const uint32_t* pairs, uint32_t gi, uint32_t gsize,
+                                              uint64_t tokens, uint64_t k, uint32_t* tp, uint32_t* sp, uint32_t& expert,
+                                              DeviceStatus* st) {
+    uint32_t n;
+    if constexpr (kRouted) {
+        const uint4 g = __ldcg(grp + gi);
+        expert = g.x;
+        n = g.z;
+        if (n > (uint32_t)G) {  // the host sizes groups for the kernel; never more pairs than registers
+            if ((threadIdx.x & 31) == 0) report(st, LBK_INVALID_PARAMETER, gi, n);
+            n = 0;
+        }
+#pragma unroll
+        for (int p = 0; p < G; p++) {
+            const uint32_t i = (uint32_t)p < n ? __ldcg(pairs + g.y + p) : 0u;
+            tp[p] = (uint32_t)(i / k);
+            sp[p] = (uint32_t)(i % k);
+        }
+    } else {
+        const uint64_t t0 = (uint64_t)gi * gsize;
+        n = (uint32_t)(tokens - t0 < gsize ? tokens - t0 : gsize);
+#pragma unroll
+        for (int p = 0; p < G; p++) {
+            tp[p] = (uint32_t)t0 + p;
+            sp[p] = (uint32_t)k;
+        }
+        (void)grp;
+        (void)pairs;
+        (void)st;
+    }
+    return n;
+}
+
+// Row chunking of a grouped role: the groups' rows spread over the role's
+// warps in whole steps of R rows.
+__device__ __forceinline__ uint32_t grp_chunk(uint32_t rows, uint32_t groups, uint32_t role_warps, uint32_t R) {
+    uint32_t per = groups ? role_warps / groups : 1u;
+    per = per < 1u ? 1u : per;
+    const uint32_t c = (rows + per - 1) / per;
+    return (c + R - 1) / R * R;
+}
+
+// Units per tail batch: whole units within the product and dot buffers.
+template <int kProd, int kTail>
+__device__ __forceinline__ uint32_t grp_units(uint32_t dots_per_unit, int nb) {
+    uint32_t ub = (uint32_t)kProd / (dots_per_unit * (uint32_t)nb * (uint32_t)kTail);
+    const uint32_t ud = (uint32_t)kGrpDots / dots_per_unit;
+    return ub < ud ? ub : ud;  // >= 1 by GrpRole's static checks
+}
+
+template <int T, bool kRouted, int W>
+__device__ __forceinline__ void gup_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar0, uint32_t role_warp,
+                                        uint32_t role_warps, const uint8_t* const* s_ptr) {
+    using RL = GrpRole<T, 2, W>;
+    using HB = typename HBOf<T>::type;
+    constexpr bool kIq = RL::kIq;
+    constexpr int kTail = RL::kTail;
+    constexpr int G = grp_max<T, W>();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = a.nb_h, tpr = a.tpr_h, R = 32 / tpr;
+    const int sub = lane / tpr, hb = lane % tpr, b = hb >> 1, h = hb & 1;
+    const bool lane_on = hb < 2 * nb;
+    const uint32_t rs = planar_row_bytes(RL::kBB, nb);  // R * rs == 16 * kBB for nb in {8, 16}
+    const uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
+    const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
+    float* prod = reinterpret_cast<float*>(smem + RL::kProdOff) + warp * RL::kProd;
+    float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
+    float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
+    const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
+    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
+    const StageOff so = stage_off<T>(nb, sub, b, h);
+
+    const uint32_t ffn = (uint32_t)a.ffn;
+    const uint32_t gsize = kRouted ? a.gsize_r : a.gsize_s;
+    const uint32_t groups = kRouted ? __ldcg(a.grp_n) : (uint32_t)((a.tokens + gsize - 1) / gsize);
+    const uint32_t chunk = grp_chunk(ffn, groups, role_warps, (uint32_t)R);
+    const uint32_t chunks = (ffn + chunk - 1) / chunk;
+    const uint32_t items = groups * chunks;
+    uint32_t phase = 0;  // bit m: parity of matrix m's barrier
+    bool live = true;    // false after a wait ran out: no further copies are issued
+    for (uint32_t it = role_warp; it < items; it += role_warps) {
+        const uint32_t gi = it / chunks, c = it - gi * chunks;
+        uint32_t tp[G], sp[G], e = 0;
+        const uint32_t n = grp_pairs<G, kRouted>(a.grp, a.grp_pairs, gi, gsize, a.tokens, a.k, tp, sp, e, a.status);
+        const uint32_t r0 = c * chunk, r1 = r0 + chunk < ffn ? r0 + chunk : ffn;
+        if (r0 >= r1 || n == 0) continue;
+        const uint8_t* gmat = a.sgate;
+        const uint8_t* umat = a.sup;
+        if constexpr (kRouted) {
+            if (e >= a.experts) {  // reported by the grouping kernel, which maps such IDs to expert 0
+                e = 0;
+            }
+            gmat = s_ptr ? s_ptr[e] : a.gate[e];
+            umat = s_ptr ? s_ptr[kPtrMax + e] : a.up[e];
+        }
+        const uint32_t steps = (r1 - r0 + R - 1) / R;
+        if (lane == 0 && live) {
+            prefetch_l2(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            prefetch_l2(umat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            const uint32_t nr0 = r1 - r0 < (uint32_t)R ? r1 - r0 : R;
+            gut_issue(stage_s, bar0, gmat, rs, r0, nr0);
+            gut_issue(stage_s + RL::kUnit, bar0 + 8, umat, rs, r0, nr0);
+        }
+        ActHB act[G];
+#pragma unroll
+        for (int p = 0; p < G; p++)
+            if ((uint32_t)p < n && lane_on)
+                load_act_global<!kIq>(act[p], a.q8x + (uint64_t)tp[p] * nb * kQ8IBytes, b, h, !kIq);
+        const uint32_t ub = grp_units<RL::kProd, kTail>((uint32_t)R * 2u * n, nb);
+        uint32_t rb = r0;
+#pragma unroll 1
+        for (uint32_t q = 0; q < steps; q++) {
+            const uint32_t ra = r0 + q * R;
+            const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
+            if (live && (!mbar_wait(bar0, phase & 1u) || !mbar_wait(bar0 + 8, (phase >> 1) & 1u))) {
+                live = false;
+                if (lane == 0) report(a.status, LBK_TIMEOUT, it, 4);
+            }
+            live = __all_sync(0xffffffffu, live);
+            phase ^= 3u;
+            const bool mine = lane_on && (uint32_t)sub < nr;
+            HB wg, wu;
+            if (mine) {
+                load_stage(wg, stage, so);
+                load_stage(wu, stage + RL::kUnit, so);
+            }
+            __syncwarp();
+            const uint32_t rn = ra + R;
+            if (lane == 0 && live && q + 1 < steps) {
+                fence_proxy_async_smem();
+                const uint32_t nn = r1 - rn < (uint32_t)R ? r1 - rn : R;
+                gut_issue(stage_s, bar0, gmat, rs, rn, nn);
+                gut_issue(stage_s + RL::kUnit, bar0 + 8, umat, rs, rn, nn);
+            }
+            const uint32_t row = ra + sub;
+            // dots of a batch: [row - rb][matrix][pair]
+            float* pr = prod + (size_t)(row - rb) * 2u * n * nb * kTail;
+#pragma unroll
+            for (int m = 0; m < 2; m++) {
+                IqPart ip[G];
+                KPart kp[G];
+                grp_zero<G>(ip, kp);
+                if (mine) grp_dots<T, G>(m == 0 ? wg : wu, act, n, t0, t1, h, ip, kp);
+#pragma unroll
+                for (int p = 0; p < G; p++)
+                    if ((uint32_t)p < n)
+                        write_products<T>(pr + ((size_t)m * n + p) * nb * kTail, b, h, mine, ip[p], kp[p], act[p].d,
+                                          a.status, (uint64_t)row * nb + b);
+            }
+            if ((rn - rb) / (uint32_t)R >= ub || rn >= r1) {
+                const uint32_t nrows = (rn < r1 ? rn : r1) - rb;
+                __syncwarp();
+                warp_tails<T>(prod, (int)(nrows * 2u * n), nb, chains, res);
+#pragma unroll
+                for (int p = 0; p < G; p++) {
+                    if ((uint32_t)p < n) {
+                        const uint64_t sidx = (uint64_t)tp[p] * (a.k + 1) + sp[p];
+                        float* hrow = a.h + sidx * a.ffn;
+                        for (uint32_t rr = lane; rr < nrows; rr += 32) {
+                            const float g = res[(rr * 2u) * n + p], u = res[(rr * 2u + 1u) * n + p];
+                            const float v = swiglu_ref(g, u);
+                            if (!isfinite(v))
+                                report(a.status, LBK_NON_FINITE_VALUE, sidx * a.ffn + rb + rr, __float_as_uint(v));
+                            hrow[rb + rr] = v;
+                        }
+                    }
+                }
+                __syncwarp();
+                rb = rn;
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < G; p++)
+            if ((uint32_t)p < n) arrive_and_quantize(a, tp[p], sp[p], r0, r1);
+    }
+}
+
+template <int T, bool kRouted, int W>
+__device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uint32_t bar0, uint32_t role_warp,
+                                        uint32_t role_warps, const uint8_t* const* s_ptr) {
+    using RL = GrpRole<T, 1, W>;
+    using HB = typename HBOf<T>::type;
+    constexpr bool kIq = RL::kIq;
+    constexpr int kTail = RL::kTail;
+    constexpr int G = grp_max<T, W>();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = a.nb_f, tpr = a.tpr_f, R = 32 / tpr;
+    const int sub = lane / tpr, hb = lane % tpr, b = hb >> 1, h = hb & 1;
+    const bool lane_on = hb < 2 * nb;
+    const uint32_t rs = planar_row_bytes(RL::kBB, nb);
+    const uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
+    const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
+    float* prod = reinterpret_cast<float*>(smem + RL::kProdOff) + warp * RL::kProd;
+    float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
+    float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
+    const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
+    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
+    const StageOff so = stage_off<T>(nb, sub, b, h);
+
+    const uint32_t H = (uint32_t)a.hidden;
+    const uint32_t gsize = kRouted ? a.gsize_r : a.gsize_s;
+    const uint32_t groups = kRouted ? __ldcg(a.grp_n) : (uint32_t)((a.tokens + gsize - 1) / gsize);
+    const uint32_t chunk = grp_chunk(H, groups, role_warps, (uint32_t)R);
+    const uint32_t chunks = (H + chunk - 1) / chunk;
+    const uint32_t items = groups * chunks;
+    uint32_t phase = 0;  // bit s: parity of stage s's barrier
+    bool live = true;
+    for (uint32_t it = role_warp; it < items; it += role_warps) {
+        const uint32_t gi = it / chunks, c = it - gi * chunks;
+        uint32_t tp[G], sp[G], e = 0;
+        const uint32_t n = grp_pairs<G, kRouted>(a.grp, a.grp_pairs, gi, gsize, a.tokens, a.k, tp, sp, e, a.status);
+        const uint32_t r0 = c * chunk, r1 = r0 + chunk < H ? r0 + chunk : H;
+        if (r0 >= r1 || n == 0) continue;
+        const uint8_t* mat = a.sdown;
+        if constexpr (kRouted) {
+            if (e >= a.experts) e = 0;  // reported by the grouping kernel
+            mat = s_ptr ? s_ptr[e] : a.down[e];
+        }
+        const uint32_t units = (r1 - r0 + R - 1) / R;
+        if (lane == 0 && live) {
+            prefetch_l2(mat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            for (uint32_t u = 0; u < 2 && u < units; u++) {
+                const uint32_t ra = r0 + u * R;
+                gut_issue(stage_s + u * RL::kUnit, bar0 + 8 * u, mat, rs, ra, r1 - ra < (uint32_t)R ? r1 - ra : R);
+            }
+        }
+        ActHB act[G];
+#pragma unroll
+        for (int p = 0; p < G; p++)
+            if ((uint32_t)p < n && lane_on)
+                load_act_global<!kIq>(act[p], a.hq + ((uint64_t)tp[p] * (a.k + 1) + sp[p]) * nb * kQ8IBytes, b, h, !kIq);
+        const uint32_t ub = grp_units<RL::kProd, kTail>((uint32_t)R * n, nb);
+        uint32_t rb = r0;
+#pragma unroll 1
+        for (uint32_t u = 0; u < units; u++) {
+            const uint32_t s = u & 1;
+            const uint32_t ra = r0 + u * R;
+            const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
+            if (live && !mbar_wait(bar0 + 8 * s, (phase >> s) & 1u)) {
+                live = false;
+                if (lane == 0) report(a.status, LBK_TIMEOUT, it, 5);
+            }
+            live = __all_sync(0xffffffffu, live);
+            phase ^= 1u << s;
+            const bool mine = lane_on && (uint32_t)sub < nr;
+            HB w;
+            if (mine) load_stage(w, stage + s * RL::kUnit, so);
+            __syncwarp();
+            if (lane == 0 && live && u + 2 < units) {
+                fence_proxy_async_smem();
+                const uint32_t rn = ra + 2 * R;
+                gut_issue(stage_s + s * RL::kUnit, bar0 + 8 * s, mat, rs, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
+            }
+            const uint32_t row = ra + sub;
+            float* pr = prod + (size_t)(row - rb) * n * nb * kTail;  // dots [row - rb][pair]
+            IqPart ip[G];
+            KPart kp[G];
+            grp_zero<G>(ip, kp);
+            if (mine) grp_dots<T, G>(w, act, n, t0, t1, h, ip, kp);
+#pragma unroll
+            for (int p = 0; p < G; p++)
+                if ((uint32_t)p < n)
+                    write_products<T>(pr + (size_t)p * nb * kTail, b, h, mine, ip[p], kp[p], act[p].d, a.status,
+                                      (uint64_t)row * nb + b);
+            const uint32_t rn = ra + R;
+            if ((rn - rb) / (uint32_t)R >= ub || rn >= r1) {
+                const uint32_t nrows = (rn < r1 ? rn : r1) - rb;
+                __syncwarp();
+                warp_tails<T>(prod, (int)(nrows * n), nb, chains, res);
+#pragma unroll
+                for (int p = 0; p < G; p++) {
+                    if ((uint32_t)p < n) {
+                        float* drow = a.dots + ((uint64_t)tp[p] * a.dots_slots + sp[p]) * H;
+                        for (uint32_t rr = lane; rr < nrows; rr += 32) drow[rb + rr] = res[rr * n + p];
+                    }
+                }
+                __syncwarp();
+                rb = rn;
+            }
+        }
+        if (a.combine) {
+#pragma unroll
+            for (int p = 0; p < G; p++)
+                if ((uint32_t)p < n) dn_arrive_and_combine(a, tp[p], r0, r1);
+        }
+    }
+}
+
+// Lookup tables of a role's type into the start of shared memory.
+template <int T>
+__device__ __forceinline__ void issue_tables(uint32_t base, const Tables& t, uint32_t bar) {
+    if constexpr (table_bytes<T>() != 0) {
+        bulk_g2s(base, T == LBK_TYPE_IQ2_S ? (const void*)t.iq2_codes : (const void*)t.iq3_grid, table_bytes<T>(), bar);
+        bulk_g2s(base + table_bytes<T>(), T == LBK_TYPE_IQ2_S ? (const void*)t.signs : (const void*)t.sign_sel,
+                 kSignBytes, bar);
+    }
+    (void)base;
+    (void)t;
+    (void)bar;
+}
+
+template <int T>
+constexpr uint32_t tables_tx() {
+    return table_bytes<T>() != 0 ? (uint32_t)(table_bytes<T>() + kSignBytes) : 0u;
+}
+
+// Grouped gate/up: CTAs [0, routed_ctas) take the routed groups, the others
+// the shared expert's token groups. Constant data (tables, the experts'
+// pointers) is requested before the wait for the grouping kernel.
+template <int TG, int TS, int W>
+__global__ void __launch_bounds__(W * 32, 1) moe_gate_up_grp_kernel(MoeGateUpArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[W * 2];
+    __shared__ __align__(8) uint64_t s_tab;
+    __shared__ __align__(16) const uint8_t* s_ptr[2 * kPtrMax];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[2 * warp]);
+    const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_tab);
+    const bool routed_role = blockIdx.x < a.routed_ctas;
+    grid_dep_launch();
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_init(bar + 8, 1);
+        if (threadIdx.x == 0) mbar_init(bar_t, 1);
+        mbar_init_fence();
+    }
+    const bool stage_ptr = routed_role && a.experts <= kPtrMax && a.experts % 2 == 0;
+    const uint32_t tab_tx = (routed_role ? tables_tx<TG>() : tables_tx<TS>()) + (stage_ptr ? 16u * (uint32_t)a.experts : 0u);
+    if (threadIdx.x == 0 && tab_tx != 0) {
+        mbar_expect_tx(bar_t, tab_tx);
+        const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
+        if (routed_role) issue_tables<TG>(base, a.tables, bar_t);
+        else issue_tables<TS>(base, a.tables, bar_t);
+        if (stage_ptr) {
+            const uint32_t ps = (uint32_t)__cvta_generic_to_shared(s_ptr);
+            bulk_g2s(ps, a.gate, 8u * (uint32_t)a.experts, bar_t);
+            bulk_g2s(ps + 8 * kPtrMax, a.up, 8u * (uint32_t)a.experts, bar_t);
+        }
+    }
+    __syncthreads();
+    grid_dep_wait();  // the groups, the tokens' Q8_K images, the zeroed counters
+    if (tab_tx != 0) {
+        if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 6, 0);
+    }
+    if (routed_role)
+        gup_run<TG, true, W>(a, smem, bar, blockIdx.x * W + warp, a.routed_ctas * W,
+                          stage_ptr ? s_ptr : nullptr);
+    else
+        gup_run<TS, false, W>(a, smem, bar, (blockIdx.x - a.routed_ctas) * W + warp, (gridDim.x - a.routed_ctas) * W,
+                              nullptr);
+}
+
+template <int TD, int TSD, int W>
+__global__ void __launch_bounds__(W * 32, 1) moe_down_grp_kernel(MoeDownArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[W * 2];
+    __shared__ __align__(8) uint64_t s_tab;
+    __shared__ __align__(16) const uint8_t* s_ptr[kPtrMax];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&s_bar[2 * warp]);
+    const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_tab);
+    const bool routed_role = blockIdx.x < a.routed_ctas;
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        mbar_init(bar + 8, 1);
+        if (threadIdx.x == 0) mbar_init(bar_t, 1);
+        mbar_init_fence();
+    }
+    const bool stage_ptr = routed_role && a.experts <= kPtrMax && a.experts % 2 == 0;
+    const uint32_t tab_tx = (routed_role ? tables_tx<TD>() : tables_tx<TSD>()) + (stage_ptr ? 8u * (uint32_t)a.experts : 0u);
+    if (threadIdx.x == 0 && tab_tx != 0) {
+        mbar_expect_tx(bar_t, tab_tx);
+        const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
+        if (routed_role) issue_tables<TD>(base, a.tables, bar_t);
+        else issue_tables<TSD>(base, a.tables, bar_t);
+        if (stage_ptr) bulk_g2s((uint32_t)__cvta_generic_to_shared(s_ptr), a.down, 8u * (uint32_t)a.experts, bar_t);
+    }
+    __syncthreads();
+    grid_dep_wait();  // the h images of the gate/up kernel
+    if (tab_tx != 0) {
+        if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 7, 0);
+    }
+    if (routed_role)
+        gdn_run<TD, true, W>(a, smem, bar, blockIdx.x * W + warp, a.routed_ctas * W,
+                          stage_ptr ? s_ptr : nullptr);
+    else
+        gdn_run<TSD, false, W>(a, smem, bar, (blockIdx.x - a.routed_ctas) * W + warp, (gridDim.x - a.routed_ctas) * W,
+                               nullptr);
+}
+
+// Groups the routed pairs of a call by expert (one CTA, one thread per
+// expert): pairs[] lists, expert by expert in ascending ID, the routed
+// indices t*k + j in ascending order; groups[] cuts each expert's list into
+// runs of at most gsize pairs. An ID outside the layer is reported and
+// counted as expert 0 (the single-token kernels compute such a slot on
+// expert 0 as well), so every pair is computed once.
+constexpr int kGroupThreads = 1024;
+constexpr int kGroupStage = 8192;  // pairs of a call at most (their expert IDs staged in shared memory)
+
+// Number of equal 16-bit halves of v and e2 (0, 1 or 2).
+__device__ __forceinline__ uint32_t halves_equal(uint32_t v, uint32_t e2) {
+    const uint32_t t = v ^ e2;
+    return __popc(~(((t & 0x7fff7fffu) + 0x7fff7fffu) | t | 0x7fff7fffu));
+}
+
+__global__ void __launch_bounds__(kGroupThreads) moe_group_kernel(MoeGroupArgs a) {
+    __shared__ uint32_t s_cnt[kGroupThreads], s_off[kGroupThreads];
+    __shared__ __align__(16) uint16_t s_id[kGroupStage];
+    __shared__ uint32_t s_wsum[2][32];
+    grid_dep_launch();
+    const uint32_t tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const uint32_t E = (uint32_t)a.experts;  // <= kGroupThreads (host-checked)
+    const uint64_t n = a.tokens * a.k;
+    s_cnt[tid] = 0u;
+    __syncthreads();
+    for (uint64_t i = tid; i < n; i += kGroupThreads) {
+        uint32_t e = a.routed[i].expert_id;
+        if (e >= E) {
+            report(a.status, LBK_INVALID_PARAMETER, e, 0);
+            e = 0;
+        }
+        atomicAdd(&s_cnt[e], 1u);
+    }
+    __syncthreads();
+    // exclusive scans of the pair counts and of the group counts
+    const uint32_t c = tid < E ? s_cnt[tid] : 0u;
+    const uint32_t g = (c + a.gsize - 1) / a.gsize;
+    uint32_t ic = c, ig = g;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t x = __shfl_up_sync(0xffffffffu, ic, d), y = __shfl_up_sync(0xffffffffu, ig, d);
+        if (lane >= (uint32_t)d) {
+            ic += x;
+            ig += y;
+        }
+    }
+    if (lane == 31) {
+        s_wsum[0][wid] = ic;
+        s_wsum[1][wid] = ig;
+    }
+    __syncthreads();
+    if (wid == 0) {
+        uint32_t v0 = s_wsum[0][lane], v1 = s_wsum[1][lane], i0 = v0, i1 = v1;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const uint32_t x = __shfl_up_sync(0xffffffffu, i0, d), y = __shfl_up_sync(0xffffffffu, i1, d);
+            if (lane >= (uint32_t)d) {
+                i0 += x;
+                i1 += y;
+            }
+        }
+        s_wsum[0][lane] = i0 - v0;
+        s_wsum[1][lane] = i1 - v1;
+    }
+    __syncthreads();
+    const uint32_t off = ic - c + s_wsum[0][wid], goff = ig - g + s_wsum[1][wid];
+    s_off[tid] = off;
+    // Stable placement: pair i goes to slot off[e] + (pairs j < i of its
+    // expert), counted over the staged IDs eight at a time.
+    const uint32_t m = (uint32_t)n;  // <= kGroupStage (host-checked)
+    const uint32_t m8 = (m + 7) & ~7u;
+    for (uint32_t i = tid; i < m8; i += kGroupThreads) {
+        uint32_t e = 0xffffu;
+        if (i < m) {
+            e = a.routed[i].expert_id;
+            e = e < E ? e : 0u;
+        }
+        s_id[i] = (uint16_t)e;
+    }
+    __syncthreads();
+    const uint4* id8 = reinterpret_cast<const uint4*>(s_id);
+    for (uint32_t i = tid; i < m; i += kGroupThreads) {
+        const uint32_t e = s_id[i], e2 = e | (e << 16);
+        uint32_t r = 0;
+        for (uint32_t j8 = 0; j8 < i / 8; j8++) {
+            const uint4 v = id8[j8];
+            r += halves_equal(v.x, e2) + halves_equal(v.y, e2) + halves_equal(v.z, e2) + halves_equal(v.w, e2);
+        }
+        for (uint32_t j = i & ~7u; j < i; j++) r += s_id[j] == e;
+        a.pairs[s_off[e] + r] = i;
+    }
+    if (tid < E) {
+        for (uint32_t q = 0; q < g; q++) {
+            const uint32_t left = c - q * a.gsize;
+            a.groups[goff + q] = make_uint4(tid, off + q * a.gsize, left < a.gsize ? left : a.gsize, 0u);
+        }
+    }
+    if (tid == E - 1) *a.n = goff + g;
+}
+
 // ---------------------------------------------------------------- launchers
 
 // Launch allowed to begin before the preceding kernel of the stream has
@@ -1275,5 +1850,116 @@ cudaError_t launch_moe_down(int down_type, int shared_down_type, const MoeDownAr
     if (down_type == LBK_TYPE_IQ2_S) return launch_down<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, stream);
     return launch_down<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, stream);
 }
+
+namespace {
+
+// Warps per CTA of a grouped kernel: the most of LBK_GRP_WARPS, 12 and 8
+// whose shared-memory plan fits (both roles' plans plus the static arrays).
+#ifndef LBK_GRP_WARPS
+#define LBK_GRP_WARPS 16
+#endif
+
+template <int TA, int TB, int kMats, int W>
+constexpr size_t grp_smem() {
+    return (size_t)(GrpRole<TA, kMats, W>::kBytes > GrpRole<TB, kMats, W>::kBytes ? GrpRole<TA, kMats, W>::kBytes
+                                                                                  : GrpRole<TB, kMats, W>::kBytes);
+}
+template <int TA, int TB, int kMats, int W>
+constexpr bool grp_fits() {
+    return grp_smem<TA, TB, kMats, W>() + (size_t)W * 16 + 16 + (size_t)kMats * kPtrMax * 8 <= (size_t)kMaxSmem;
+}
+template <int TA, int TB, int kMats>
+constexpr int grp_warps() {
+    return grp_fits<TA, TB, kMats, LBK_GRP_WARPS>() ? LBK_GRP_WARPS : (grp_fits<TA, TB, kMats, 12>() ? 12 : 8);
+}
+
+template <int TG, int TS>
+cudaError_t launch_gup(const MoeGateUpArgs& a, unsigned ctas, cudaStream_t stream) {
+    constexpr int W = grp_warps<TG, TS, 2>();
+    static_assert(grp_fits<TG, TS, 2, W>(), "grouped gate/up stage plan");
+    constexpr size_t smem = grp_smem<TG, TS, 2, W>();
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_gate_up_grp_kernel<TG, TS, W>));
+    if (e != cudaSuccess) return e;
+    if ((a.k > 0) != (a.routed_ctas > 0) || (a.has_shared != 0) != (a.routed_ctas < ctas)) return cudaErrorInvalidValue;
+    if (a.k > 0 && (a.gsize_r < 1 || a.gsize_r > (uint32_t)grp_max<TG, W>())) return cudaErrorInvalidValue;
+    if (a.has_shared && (a.gsize_s < 1 || a.gsize_s > (uint32_t)grp_max<TS, W>())) return cudaErrorInvalidValue;
+    return launch_dependent(moe_gate_up_grp_kernel<TG, TS, W>, ctas, W * 32, smem, stream, a);
+}
+
+template <int TD, int TSD>
+cudaError_t launch_gdn(const MoeDownArgs& a, unsigned ctas, cudaStream_t stream) {
+    constexpr int W = grp_warps<TD, TSD, 1>();
+    static_assert(grp_fits<TD, TSD, 1, W>(), "grouped down stage plan");
+    constexpr size_t smem = grp_smem<TD, TSD, 1, W>();
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(moe_down_grp_kernel<TD, TSD, W>));
+    if (e != cudaSuccess) return e;
+    if ((a.k > 0) != (a.routed_ctas > 0) || (a.has_shared != 0) != (a.routed_ctas < ctas)) return cudaErrorInvalidValue;
+    if (a.combine && !a.has_shared) return cudaErrorInvalidValue;
+    if (a.k > 0 && (a.gsize_r < 1 || a.gsize_r > (uint32_t)grp_max<TD, W>())) return cudaErrorInvalidValue;
+    if (a.has_shared && (a.gsize_s < 1 || a.gsize_s > (uint32_t)grp_max<TSD, W>())) return cudaErrorInvalidValue;
+    return launch_dependent(moe_down_grp_kernel<TD, TSD, W>, ctas, W * 32, smem, stream, a);
+}
+
+// Group sizes and warps of one kernel's type pair: {routed pairs, shared pairs, warps}.
+template <int TA, int TB, int kMats>
+GrpShape grp_shape() {
+    constexpr int W = grp_warps<TA, TB, kMats>();
+    return GrpShape{(uint32_t)grp_max<TA, W>(), (uint32_t)grp_max<TB, W>(), (uint32_t)W};
+}
+
+}  // namespace
+
+GrpShape moe_gate_up_grp_shape(int gate_type, int shared_gate_type) {
+    if (gate_type == LBK_TYPE_IQ2_S && shared_gate_type == LBK_TYPE_IQ2_S)
+        return grp_shape<LBK_TYPE_IQ2_S, LBK_TYPE_IQ2_S, 2>();
+    if (gate_type == LBK_TYPE_IQ2_S) return grp_shape<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K, 2>();
+    return grp_shape<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K, 2>();
+}
+
+GrpShape moe_down_grp_shape(int down_type, int shared_down_type) {
+    if (down_type == LBK_TYPE_IQ3_S && shared_down_type == LBK_TYPE_IQ3_S)
+        return grp_shape<LBK_TYPE_IQ3_S, LBK_TYPE_IQ3_S, 1>();
+    if (down_type == LBK_TYPE_IQ3_S && shared_down_type == LBK_TYPE_IQ2_S)
+        return grp_shape<LBK_TYPE_IQ3_S, LBK_TYPE_IQ2_S, 1>();
+    if (down_type == LBK_TYPE_IQ2_S && shared_down_type == LBK_TYPE_IQ2_S)
+        return grp_shape<LBK_TYPE_IQ2_S, LBK_TYPE_IQ2_S, 1>();
+    if (down_type == LBK_TYPE_IQ3_S) return grp_shape<LBK_TYPE_IQ3_S, LBK_TYPE_Q4_K, 1>();
+    if (down_type == LBK_TYPE_IQ2_S) return grp_shape<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K, 1>();
+    return grp_shape<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K, 1>();
+}
+
+bool moe_grouped_supported(int gate_type, int shared_gate_type, int down_type, int shared_down_type, int nb_h, int nb_f) {
+    return moe_gate_up_tma_supported(gate_type, shared_gate_type, nb_h) &&
+           moe_down_tma_supported(down_type, shared_down_type, nb_f);
+}
+
+cudaError_t launch_moe_group(const MoeGroupArgs& a, cudaStream_t stream) {
+    if (a.experts < 1 || a.experts > (uint64_t)kGroupThreads || a.gsize < 1 || a.tokens * a.k > (uint64_t)kGroupStage)
+        return cudaErrorInvalidValue;
+    moe_group_kernel<<<1, kGroupThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_gate_up_grp(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
+                                   cudaStream_t stream) {
+    if (gate_type == LBK_TYPE_IQ2_S && shared_gate_type == LBK_TYPE_IQ2_S)
+        return launch_gup<LBK_TYPE_IQ2_S, LBK_TYPE_IQ2_S>(a, ctas, stream);
+    if (gate_type == LBK_TYPE_IQ2_S) return launch_gup<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
+    return launch_gup<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);
+}
+
+cudaError_t launch_moe_down_grp(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
+                                cudaStream_t stream) {
+    if (down_type == LBK_TYPE_IQ3_S && shared_down_type == LBK_TYPE_IQ3_S)
+        return launch_gdn<LBK_TYPE_IQ3_S, LBK_TYPE_IQ3_S>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ3_S && shared_down_type == LBK_TYPE_IQ2_S)
+        return launch_gdn<LBK_TYPE_IQ3_S, LBK_TYPE_IQ2_S>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ2_S && shared_down_type == LBK_TYPE_IQ2_S)
+        return launch_gdn<LBK_TYPE_IQ2_S, LBK_TYPE_IQ2_S>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ3_S) return launch_gdn<LBK_TYPE_IQ3_S, LBK_TYPE_Q4_K>(a, ctas, stream);
+    if (down_type == LBK_TYPE_IQ2_S) return launch_gdn<LBK_TYPE_IQ2_S, LBK_TYPE_Q4_K>(a, ctas, stream);
+    return launch_gdn<LBK_TYPE_Q4_K, LBK_TYPE_Q4_K>(a, ctas, stream);
+}
+
 
 }  // namespace lbk

@@ -77,27 +77,32 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
             const float* w = a.w + e * a.hidden;
             // All loads first: no store (partials, status) may sit between
             // them, or the compiler serializes the loads behind it.
-            float wr[16], xr[16];
+            float wr[16];
 #pragma unroll
             for (int q = 0; q < 16; q++) {
                 uint64_t j = j0 + (uint64_t)q * 32 + lane;
                 wr[q] = j < a.hidden ? __ldcs(w + j) : 0.0f;
-                xr[q] = j < a.hidden ? __ldg(a.x + j) : 0.0f;  // token 0
             }
-            for (uint64_t t = 0; t < a.tokens; t++) {
-                if (t > 0) {
+            // tokens four at a time: their loads in flight together
+            for (uint64_t t0 = 0; t0 < a.tokens; t0 += 4) {
+                float xr[4][16];
+#pragma unroll
+                for (int u = 0; u < 4; u++)
 #pragma unroll
                     for (int q = 0; q < 16; q++) {
                         uint64_t j = j0 + (uint64_t)q * 32 + lane;
-                        xr[q] = j < a.hidden ? __ldg(a.x + t * a.hidden + j) : 0.0f;
+                        xr[u][q] = (t0 + u < a.tokens && j < a.hidden) ? __ldg(a.x + (t0 + u) * a.hidden + j) : 0.0f;
                     }
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (t0 + u >= a.tokens) break;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(wr[q], xr[u][q]));
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+                    if (lane == 0) f.partials[((t0 + u) * a.experts + e) * chunks + c] = acc;
                 }
-                float acc = 0.0f;
-#pragma unroll
-                for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(wr[q], xr[q]));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-                if (lane == 0) f.partials[(t * a.experts + e) * chunks + c] = acc;
             }
             int bad_q = -1;
             uint32_t bad_bits = 0;
@@ -137,7 +142,7 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
 
     // The last CTA to finish sums the chunk partials in chunk order and routes
     // (unless the consumer kernel does both itself).
-    if (f.defer) return;
+    if (f.defer || f.split) return;
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
@@ -164,6 +169,29 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
     if (threadIdx.x == 0) *f.counter = 0u;
 }
 
+// Several tokens: logits (chunk partials summed in chunk order, as the
+// last-CTA pass does) and top-k, one warp per token over many CTAs, after
+// the router grid (programmatic dependent launch).
+__global__ void topk_partials_kernel(RouterFusedArgs f) {
+    __shared__ float s_tk[kTopkWarps][2][1024];
+    const RouterArgs& a = f.r;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t chunks = (a.hidden + kChunk - 1) / kChunk;
+    grid_dep_launch();
+    grid_dep_wait();  // the router's partials
+    for (uint64_t t = (uint64_t)blockIdx.x * kTopkWarps + warp; t < a.tokens; t += (uint64_t)gridDim.x * kTopkWarps) {
+        for (uint64_t e = lane; e < a.experts; e += 32) {
+            const float* pp = f.partials + (t * a.experts + e) * chunks;
+            float sum = 0.0f;
+            for (uint64_t c = 0; c < chunks; c++) sum = __fadd_rn(sum, __ldcg(pp + c));
+            a.logits[t * a.experts + e] = sum;
+        }
+        __syncwarp();
+        topk_warp(a.logits + t * a.experts, f.bias, (int)a.experts, (int)f.k, f.weight_scale, f.routed + t * f.k,
+                  a.status, t, s_tk[warp][0], s_tk[warp][1]);
+    }
+}
+
 }  // namespace
 
 size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens) {
@@ -176,8 +204,21 @@ cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStre
     uint64_t ctas = (items + (kRouterThreads / 32) - 1) / (kRouterThreads / 32);
     if (ctas > (uint64_t)sm_count) ctas = sm_count;
     if (ctas < 1) ctas = 1;
-    router_fused_kernel<<<(unsigned)ctas, kRouterThreads, 0, stream>>>(f);
-    return cudaGetLastError();
+    RouterFusedArgs g = f;
+    g.split = (!f.defer && f.r.experts > 0 && f.routed != nullptr && f.r.tokens > 1 && f.r.experts <= 1024) ? 1 : 0;
+    router_fused_kernel<<<(unsigned)ctas, kRouterThreads, 0, stream>>>(g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || !g.split) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)((f.r.tokens + kTopkWarps - 1) / kTopkWarps));
+    cfg.blockDim = dim3(kTopkWarps * 32);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, topk_partials_kernel, g);
 }
 
 cudaError_t launch_router(const RouterArgs& a, int mode, int sm_count, cudaStream_t stream) {

@@ -174,6 +174,7 @@ def _load() -> ctypes.CDLL:
         "lbk_moe_layer_create": ([P, ctypes.POINTER(MoeWeights), P, ctypes.POINTER(P)], I32),
         "lbk_moe_layer_destroy": ([P], I32),
         "lbk_moe_layer_fused": ([P], I32),
+        "lbk_moe_layer_set_grouping": ([P, U64], I32),
         "lbk_moe_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
         "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
         "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
@@ -215,7 +216,7 @@ EXPORTED = (
     "lbk_abi_version lbk_backend_name lbk_context_create lbk_context_destroy lbk_context_sync_status "
     "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_planar_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
-    "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused "
+    "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused lbk_moe_layer_set_grouping "
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
     "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward "
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
@@ -357,6 +358,10 @@ class MoeLayer:
     @property
     def fused(self) -> bool:
         return bool(lib.lbk_moe_layer_fused(self.ptr))
+
+    def set_grouping(self, min_tokens: int) -> None:
+        """Calls of at least `min_tokens` tokens run the grouped kernels (0: never)."""
+        check(lib.lbk_moe_layer_set_grouping(self.ptr, min_tokens))
 
     def workspace_bytes(self, tokens: int) -> int:
         n = ctypes.c_uint64()

@@ -231,3 +231,47 @@ def test_nccl_ranks_equal_moe_forward():
     r = _torchrun(2, "gpu", timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert "ok" in r.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,T", [(2, 12), (4, 16)])
+def test_grouped_expert_parallel_equals_ungrouped_forward(world, T):
+    """Grouped kernels on every rank (items grouped by local expert; the home
+    rank's shared-expert pass grouped by token) against the ungrouped
+    single-GPU forward: bit for bit."""
+    from gpu_helpers import clean_status, dev
+
+    H, F, E, k = 2048, 512, 16, 4
+    full, ranks, keep, rng = _gpu_layers(H, F, E, k, 31 * T + world, world)
+    full.set_grouping(0)
+    for r in ranks:
+        r.set_grouping(2)
+    home = ranks[0]
+    x = dev(rng.standard_normal(T * H).astype(np.float32))
+    er = E // world
+    q8b = home.q8_bytes
+    ws = torch.zeros(max(home.workspace_bytes(T), home.workspace_bytes(T * k)), dtype=torch.uint8, device="cuda")
+    routed = torch.empty((T * k, 2), dtype=torch.int32, device="cuda")
+    q8 = torch.empty((T, q8b), dtype=torch.uint8, device="cuda")
+    home.route(x, T, routed, q8, ws)
+    ids = routed[:, 0]
+    plan = ep.local_plan(ids, er, world)
+    rows = ep.pack_rows(q8, ids, plan, k, er)
+    dots = []
+    for r, chunk in enumerate(torch.split(rows, plan.send)):
+        n = chunk.shape[0]
+        d = torch.empty((n, H), dtype=torch.float32, device="cuda")
+        if n:
+            imgs, items = ep.unpack_items(chunk, q8b)
+            ranks[r].items_forward(imgs, items, n, d, ws)
+        dots.append(d)
+    routed_dots = ep.place_returned(torch.cat(dots), plan, T * k, H)
+    out = torch.full((T * H,), float("nan"), device="cuda")
+    home.combine(q8, T, routed, routed_dots, out, ws)
+    clean_status()
+    want, wr = _full_forward(full, x, T)
+    assert torch.equal(routed.view(-1).cpu(), wr.cpu())
+    assert torch.equal(out.view(torch.int32).cpu(), want.view(torch.int32).cpu())
+    full.close()
+    for r in ranks:
+        r.close()
