@@ -805,6 +805,17 @@ double hb_cost_us(int32_t ty) {
     }
 }
 
+// The same for one lane slot of a gate/up unit (gate and up half blocks of a
+// row decoded together), from per-warp globaltimer stamps of a config-3
+// layer on B200: 0.91 us per IQ2_S unit, 1.52 us per Q4_K unit (32 slots).
+double gu_hb_cost_us(int32_t ty) {
+    switch (ty) {
+        case LBK_TYPE_IQ2_S: return 0.0285;
+        case LBK_TYPE_Q4_K: return 0.0476;
+        default: return hb_cost_us(ty);
+    }
+}
+
 // Routed CTAs out of `ctas` so that the routed and the shared role finish
 // together: role time = fixed + work / (its warps).
 long split_roles(unsigned ctas, int warps, double work_r, double fixed_r, double work_s, double fixed_s) {
@@ -1010,8 +1021,8 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             const double hb = 2.0 * nbh * 2.0 * L->F;  // half blocks of one slot (gate + up)
             const long rc = K == 0 ? 0
                             : !mode.shared ? (long)ctas
-                                           : split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * K * hb * hb_cost_us(L->gate_type),
-                                                         defer_topk ? 5.0 : 1.5, T * hb * hb_cost_us(L->sgate_type), 1.0);
+                                           : split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * K * hb * gu_hb_cost_us(L->gate_type),
+                                                         defer_topk ? 12.0 : 8.0, T * hb * gu_hb_cost_us(L->sgate_type), 8.0);
             g.routed_ctas = (uint32_t)rc;
             if (full && T <= 4 && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
                 g.down = L->d_down;

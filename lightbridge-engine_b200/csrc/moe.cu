@@ -883,6 +883,8 @@ struct DNRole {
     static constexpr int kBytes = kResOff + kDNWarps * kRes * 4;
 };
 
+constexpr int kCombineK = 8;  // routed slots the combine holds in registers
+
 // Arrivals on the combine blocks of rows [r0, r1) of slot `slot`; the last
 // arriving warp of a block combines its rows.
 __device__ __forceinline__ void dn_arrive_and_combine(const MoeDownArgs& a, uint32_t t, uint32_t r0, uint32_t r1) {
@@ -906,6 +908,32 @@ __device__ __forceinline__ void dn_arrive_and_combine(const MoeDownArgs& a, uint
         if (lane == 0) *cnt = 0u;  // ready for the next launch
         if (status_set(a.status)) continue;  // validation failed upstream: leave out unchanged
         const float* dt = a.dots + (uint64_t)t * (a.k + 1) * H;
+        if (a.k <= (uint64_t)kCombineK && kDNBlock == 64) {
+            // every dot of the block's two rows per lane in flight at once,
+            // the coefficients read once per warp
+            const float cl = (uint64_t)lane < a.k ? a.routed[(uint64_t)t * a.k + lane].coefficient : 0.0f;
+            const uint32_t ra = blk * kDNBlock + lane, rb = ra + 32;
+            float va[kCombineK], vb[kCombineK];
+#pragma unroll
+            for (int j = 0; j < kCombineK; j++) {
+                va[j] = (uint64_t)j < a.k && ra < bend ? __ldcg(dt + (uint64_t)j * H + ra) : 0.0f;
+                vb[j] = (uint64_t)j < a.k && rb < bend ? __ldcg(dt + (uint64_t)j * H + rb) : 0.0f;
+            }
+            const float sa = ra < bend ? __ldcg(dt + a.k * H + ra) : 0.0f;
+            const float sb = rb < bend ? __ldcg(dt + a.k * H + rb) : 0.0f;
+            float acc_a = 0.0f, acc_b = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kCombineK; j++) {
+                const float c = __shfl_sync(0xffffffffu, cl, j);
+                if ((uint64_t)j < a.k) {
+                    acc_a = __fadd_rn(acc_a, __fmul_rn(c, va[j]));
+                    acc_b = __fadd_rn(acc_b, __fmul_rn(c, vb[j]));
+                }
+            }
+            if (ra < bend) a.out[(uint64_t)t * H + ra] = __fadd_rn(acc_a, __fmul_rn(1.0f, sa));
+            if (rb < bend) a.out[(uint64_t)t * H + rb] = __fadd_rn(acc_b, __fmul_rn(1.0f, sb));
+            continue;
+        }
         for (uint32_t r = blk * kDNBlock + lane; r < bend; r += 32) {
             float acc = 0.0f;
             for (uint64_t j = 0; j < a.k; j++) {
