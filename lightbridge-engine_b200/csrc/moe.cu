@@ -696,15 +696,19 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         }
         // This CTA's slice of every down matrix the call will read heads for
         // L2 now: HBM streams it while the gate/up rows are being decoded.
-        if (a.down != nullptr && threadIdx.x == 0) {
-            const uint64_t H = a.hidden;
+        // One matrix per warp: a bulk prefetch can hold its thread while the
+        // SM's copy queue is full, and one thread issuing all of them started
+        // its own rows up to 5 us late.
+        if (a.down != nullptr && lane == 0) {
+            const uint64_t H = a.hidden, n = a.tokens * a.k;
             const uint64_t p0 = H * blockIdx.x / a.routed_ctas, p1 = H * (blockIdx.x + 1) / a.routed_ctas;
-            if (p1 > p0) {
-                for (uint64_t i = 0; i < a.tokens * a.k; i++) {
+            for (uint64_t i = warp; p1 > p0 && i <= n; i += kGUTWarps) {
+                if (i == n) {
+                    prefetch_l2(a.sdown + p0 * a.sdown_rs, (uint32_t)((p1 - p0) * a.sdown_rs));
+                } else {
                     const uint32_t e = a.defer_topk ? s_routed[i].expert_id : a.routed[i].expert_id;
                     if (e < a.experts) prefetch_l2(a.down[e] + p0 * a.down_rs, (uint32_t)((p1 - p0) * a.down_rs));
                 }
-                prefetch_l2(a.sdown + p0 * a.sdown_rs, (uint32_t)((p1 - p0) * a.sdown_rs));
             }
         }
         if (tab_tx != 0) {
