@@ -142,13 +142,20 @@ static __device__ __noinline__ bool topk_cta(const float* partials, int chunks, 
         __syncthreads();
         return false;
     }
+    // each expert's rank, counted by two adjacent threads over halves of the keys
+    const int half = (E + 1) >> 1;
 #pragma unroll 1
-    for (int i = tid; i < E; i += nt) {
-        const unsigned long long key = s_key[i];
-        int rank = 0;
-#pragma unroll 4
-        for (int j = 0; j < E; j++) rank += s_key[j] > key ? 1 : 0;
-        if (rank < k) s_sel[rank] = (uint32_t)i;
+    for (int base = 0; base < 2 * E; base += nt) {
+        const int i = base + tid, e = i >> 1, h = i & 1;
+        int part = 0;
+        if (i < 2 * E) {
+            const unsigned long long key = s_key[e];
+            const int j1 = h ? E : half;
+#pragma unroll 8
+            for (int j = h ? half : 0; j < j1; j++) part += s_key[j] > key ? 1 : 0;
+        }
+        const int rank = part + __shfl_xor_sync(0xffffffffu, part, 1);
+        if (i < 2 * E && h == 0 && rank < k) s_sel[rank] = (uint32_t)e;
     }
     __syncthreads();
     if (tid < 32) {

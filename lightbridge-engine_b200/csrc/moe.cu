@@ -643,17 +643,21 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         // CTA finishes the router from the partials (logits in chunk order,
         // then top-k) while the tables arrive. CTA 0 publishes the routing
         // for the down kernel.
-        __shared__ __align__(8) uint64_t s_pro[2];  // [0] partials, [1] tables
+        __shared__ __align__(8) uint64_t s_pro[3];  // [0] partials, [1] tables, [2] selection bias
         __shared__ uint32_t s_sel[32];
         __shared__ int s_bad;
         const uint32_t bar_p = (uint32_t)__cvta_generic_to_shared(&s_pro[0]);
         const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_pro[1]);
+        const uint32_t bar_b = (uint32_t)__cvta_generic_to_shared(&s_pro[2]);
         // free until the rows start: [partials][keys][p]
         float* s_part = reinterpret_cast<float*>(smem + RL::kProdOff);
         const uint64_t pfloats = a.experts * a.chunks;
         unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_part + ((pfloats + 3) & ~(uint64_t)3));
         float* s_p = reinterpret_cast<float*>(s_key + a.experts);
+        float* s_bias = s_p + a.experts;  // staged with the tables (constant data)
         const bool bulk_p = a.defer_topk && pfloats % 4 == 0;
+        const bool stage_bias = a.defer_topk && a.experts % 4 == 0 && ((uintptr_t)a.bias & 15) == 0 &&
+                                ((uintptr_t)s_bias & 15) == 0;
         // the experts' gate / up pointers, staged with the tables (16-byte copies)
         __shared__ __align__(16) const uint8_t* s_ptr[2 * kPtrMax];
         const bool stage_ptr = a.experts <= kPtrMax && a.experts % 2 == 0;
@@ -661,6 +665,7 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         if (threadIdx.x == 0) {
             mbar_init(bar_p, 1);
             mbar_init(bar_t, 1);
+            mbar_init(bar_b, 1);
             mbar_init_fence();
             // constant data first: this part overlaps the router kernel's tail
             if (tab_tx != 0) mbar_expect_tx(bar_t, tab_tx);
@@ -676,6 +681,10 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 bulk_g2s(ps, a.gate, 8u * (uint32_t)a.experts, bar_t);
                 bulk_g2s(ps + 8 * kPtrMax, a.up, 8u * (uint32_t)a.experts, bar_t);
             }
+            if (stage_bias) {
+                mbar_expect_tx(bar_b, 4u * (uint32_t)a.experts);
+                bulk_g2s((uint32_t)__cvta_generic_to_shared(s_bias), a.bias, 4u * (uint32_t)a.experts, bar_b);
+            }
         }
         grid_dep_wait();  // the router's partials, Q8_K image and zeroed counters
         if (threadIdx.x == 0 && bulk_p) {
@@ -690,8 +699,11 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 for (uint64_t i = threadIdx.x; i < pfloats; i += blockDim.x) s_part[i] = __ldcg(a.partials + i);
                 __syncthreads();
             }
-            topk_cta(s_part, (int)a.chunks, a.bias, (int)a.experts, (int)a.k, a.weight_scale, s_routed,
-                     blockIdx.x == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
+            if (stage_bias) {
+                if (!mbar_wait(bar_b, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 2, 0);
+            }
+            topk_cta(s_part, (int)a.chunks, stage_bias ? s_bias : a.bias, (int)a.experts, (int)a.k, a.weight_scale,
+                     s_routed, blockIdx.x == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
             if (blockIdx.x == 0 && threadIdx.x < a.k) a.routed_store[threadIdx.x] = s_routed[threadIdx.x];
         }
         // This CTA's slice of every down matrix the call will read heads for
@@ -1829,7 +1841,7 @@ bool moe_gate_up_tma_supported(int gate_type, int shared_gate_type, int nb_h) {
 bool moe_gate_up_tma_defer_fits(int gate_type, uint64_t experts, uint64_t chunks) {
     const uint64_t floats = gate_type == LBK_TYPE_IQ2_S ? (uint64_t)kGUTWarps * GUTRole<LBK_TYPE_IQ2_S>::kProd
                                                         : (uint64_t)kGUTWarps * GUTRole<LBK_TYPE_Q4_K>::kProd;
-    return ((experts * chunks + 3) & ~(uint64_t)3) + 3 * experts <= floats;  // partials, 64-bit keys, p
+    return ((experts * chunks + 3) & ~(uint64_t)3) + 4 * experts <= floats;  // partials, 64-bit keys, p, bias
 }
 
 cudaError_t launch_moe_gate_up_tma(int gate_type, int shared_gate_type, const MoeGateUpArgs& a, unsigned ctas,
