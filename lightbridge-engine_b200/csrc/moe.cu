@@ -1000,10 +1000,13 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
         const uint32_t units = (r1 - r0 + R - 1) / R;
         ActHB act;
         uint32_t nact[32];
+        // the negated words wait for the loads: formed after the first copies are issued
         auto load_act = [&]() {
-            if (lane_on) {
-                load_act_global<!kIq>(act, a.hq + ((uint64_t)t * (a.k + 1) + slot) * nb * kQ8IBytes, b, h, !kIq);
-                if constexpr (T == LBK_TYPE_IQ3_S) {
+            if (lane_on) load_act_global<!kIq>(act, a.hq + ((uint64_t)t * (a.k + 1) + slot) * nb * kQ8IBytes, b, h, !kIq);
+        };
+        auto negate_act = [&]() {
+            if constexpr (T == LBK_TYPE_IQ3_S) {
+                if (lane_on) {
 #pragma unroll
                     for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
                 }
@@ -1032,6 +1035,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             dep_wait = false;
             load_act();
         }
+        negate_act();
         float* drow = a.dots + ((uint64_t)t * a.dots_slots + slot) * H;
         uint32_t rb = r0;
 #pragma unroll 1
