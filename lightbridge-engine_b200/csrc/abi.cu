@@ -192,6 +192,7 @@ int32_t run_f32_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, uint
 struct WsLayout {
     uint64_t rcounter, logits, partials, q8x, routed, h, hq, counters, dcounters, counter_words, dots, g, u, total;
     uint64_t grp_n, grp, grp_pairs;  // grouped kernels (T >= 2): group count, groups, grouped pairs
+    uint64_t rflag;                  // single token: routing-published flag (in the zeroed counter region)
 };
 
 uint64_t up256(uint64_t v) { return (v + 255) & ~(uint64_t)255; }
@@ -208,7 +209,8 @@ WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T, uint64_t k) {
     o.rcounter = 0;
     o.counters = 16;
     o.dcounters = o.counters + slots * nbf * 4;
-    const uint64_t cend = o.dcounters + T * ((L->H + lbk::kMoeDownCombineRows - 1) / lbk::kMoeDownCombineRows) * 4;
+    o.rflag = o.dcounters + T * ((L->H + lbk::kMoeDownCombineRows - 1) / lbk::kMoeDownCombineRows) * 4;
+    const uint64_t cend = o.rflag + 16;
     o.counter_words = (cend - o.counters) / 4;
     uint64_t off = up256(cend);
     o.dots = off;  // down row dots [T][k+1][H]
@@ -1024,6 +1026,9 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
                                            : split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * K * hb * gu_hb_cost_us(L->gate_type),
                                                          defer_topk ? 12.0 : 8.0, T * hb * gu_hb_cost_us(L->sgate_type), 8.0);
             g.routed_ctas = (uint32_t)rc;
+            // single-token decode: the gate/up kernel publishes the routing for early down copies
+            if (full && defer_topk && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf))
+                g.route_flag = reinterpret_cast<unsigned int*>(ws + o.rflag);
             if (full && T <= 4 && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
                 g.down = L->d_down;
                 g.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);
@@ -1125,6 +1130,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             d.combine = mode.combine ? 1 : 0;
             d.has_shared = mode.shared ? 1 : 0;
             d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
+            d.route_flag = g.route_flag;
             e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
             if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
             if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);

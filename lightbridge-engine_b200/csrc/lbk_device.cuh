@@ -163,6 +163,15 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 // Programmatic dependent launch: wait until the grid this one depends on has
 // completed and its writes are visible (a no-op for an ordinary launch), and
 // let the grid that depends on this one start launching.
+// Flag published with release semantics at GPU scope, read with acquire.
+__device__ __forceinline__ void st_release_gpu(unsigned int* p, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // Hint that [p, p+bytes) will be read soon: bring it into L2.

@@ -51,6 +51,7 @@ struct MoeGateUpArgs {
     const uint4* grp;                // [groups] {expert, first pair, pairs, 0}
     const uint32_t* grp_pairs;       // [tokens*k] routed index t*k + j, grouped by expert
     uint32_t gsize_r, gsize_s;       // pairs per group: routed / shared expert
+    unsigned int* route_flag;        // single token: set (release) once CTA 0 has stored the routing, or null
     DeviceStatus* status;
     Tables tables;
 };
@@ -85,6 +86,7 @@ struct MoeDownArgs {
     const uint4* grp;
     const uint32_t* grp_pairs;
     uint32_t gsize_r, gsize_s;
+    const unsigned int* route_flag;  // single token: the gate/up kernel's routing flag (early copies), or null
     DeviceStatus* status;
     Tables tables;
 };

@@ -705,6 +705,13 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
             topk_cta(s_part, (int)a.chunks, stage_bias ? s_bias : a.bias, (int)a.experts, (int)a.k, a.weight_scale,
                      s_routed, blockIdx.x == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
             if (blockIdx.x == 0 && threadIdx.x < a.k) a.routed_store[threadIdx.x] = s_routed[threadIdx.x];
+            // The down kernel may read the routing before its grid wait:
+            // publish it (every writer's store, then the flag).
+            if (blockIdx.x == 0 && a.route_flag != nullptr) {
+                __threadfence();
+                __syncthreads();
+                if (threadIdx.x == 0) st_release_gpu(a.route_flag, 1u);
+            }
         }
         // This CTA's slice of every down matrix the call will read heads for
         // L2 now: HBM streams it while the gate/up rows are being decoded.
@@ -1016,7 +1023,8 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
         if (!dep_wait) load_act();
         const uint8_t* mat = a.sdown;
         if constexpr (kRouted) {
-            uint32_t e = a.routed[(uint64_t)t * a.k + j].expert_id;
+            // through L2: may be read before the grid wait (see route_flag)
+            uint32_t e = __ldcg(reinterpret_cast<const unsigned int*>(a.routed + (uint64_t)t * a.k + j));
             if (e >= a.experts) {  // reported; compute on expert 0 so the arrival counts stay balanced
                 if (lane == 0) report(a.status, LBK_INVALID_PARAMETER, e, 0);
                 e = 0;
@@ -1117,11 +1125,23 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
     }
     __syncthreads();
     if (routed_role) {
-        grid_dep_wait();  // the routing and h images of the gate/up kernel
+        // Single token: the routing is final long before the gate/up grid
+        // ends. Once its flag is seen (bounded poll), the first down rows are
+        // requested before the wait for that grid; h is read after it.
+        __shared__ int s_early;
+        if (threadIdx.x == 0) {
+            int ok = 0;
+            if (a.route_flag != nullptr)
+                for (uint32_t i = 0; i < (1u << 20) && !ok; i++) ok = ld_acquire_gpu(a.route_flag) != 0u;
+            s_early = ok;
+        }
+        __syncthreads();
+        const bool early = s_early != 0;
+        if (!early) grid_dep_wait();  // the routing and h images of the gate/up kernel
         if (tab_tx != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 3, 0);
         }
-        dn_run<TD, true>(a, smem, bar, blockIdx.x * kDNWarps + warp, a.routed_ctas * kDNWarps, false,
+        dn_run<TD, true>(a, smem, bar, blockIdx.x * kDNWarps + warp, a.routed_ctas * kDNWarps, early,
                          stage_ptr ? s_ptr : nullptr);
     } else {
         __shared__ __align__(8) uint64_t s_stab;
