@@ -567,7 +567,7 @@ def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
             "config": {"workload": "config4: routed-MoE FFN layer, 64 tokens per step per GPU", "hidden": H,
                        "experts": E, "experts_per_gpu": er, "expert_ffn": F, "top_k": K_TOP,
                        "tokens_per_step_per_gpu": T, "parallelism": f"expert-parallel x{world}",
-                       "grouped_kernels": args.grouping != 0,
+                       "grouped_kernels": args.grouping is not None and args.grouping != 0,  # off by default for EP layers
                        "exchange": "NCCL all_to_all_single (counts, Q8_K rows, row dots)"},
         }
         print(json.dumps(line), flush=True)

@@ -268,8 +268,10 @@ int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer);
  * kernels on a fused planar layer: the call's (token, slot) pairs are grouped
  * by expert and each weight half block is decoded once for every pair of its
  * group. Results are bit-identical either way; only the speed differs.
- * min_tokens 0 turns grouping off; the default is 8. No counterpart in the
- * reference, which runs each routed expert per token
+ * min_tokens 0 turns grouping off; the default is 8 for whole layers and 0
+ * (off) for expert-parallel layers (lbk_ep_layer_create, or lbk_moe_layer_load
+ * of a rank's share), whose passes measured no faster grouped. No counterpart
+ * in the reference, which runs each routed expert per token
  * (moe_routed_by_id_into, moe.rs:64-147). */
 int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens);
 

@@ -729,7 +729,10 @@ int32_t host_set_device(lbk_context* ctx) { return set_device(ctx); }
 int32_t layer_create_owned(lbk_context* ctx, const lbk_moe_weights* w, uint64_t global_experts, uint64_t first_expert,
                            void* stream, void* owned, lbk_moe_layer** out) {
     const int32_t s = layer_create(ctx, w, global_experts, first_expert, stream, out);
-    if (s == LBK_OK) (*out)->owned = owned;
+    if (s == LBK_OK) {
+        (*out)->owned = owned;
+        if ((*out)->E_local != (*out)->E) (*out)->group_min = 0;  // an expert-parallel share (see lbk_ep_layer_create)
+    }
     return s;
 }
 
@@ -741,7 +744,11 @@ LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w,
 
 LBK_API int32_t lbk_ep_layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t global_experts,
                                     uint64_t first_expert, void* stream, lbk_moe_layer** out) {
-    return layer_create(ctx, w, global_experts, first_expert, stream, out);
+    const int32_t st = layer_create(ctx, w, global_experts, first_expert, stream, out);
+    // The expert-parallel passes (items without the shared expert, the
+    // shared-only combine) measured no faster grouped: off unless asked for.
+    if (st == LBK_OK && out != nullptr && *out != nullptr) (*out)->group_min = 0;
+    return st;
 }
 
 LBK_API int32_t lbk_moe_layer_trace(lbk_moe_layer* layer, int32_t enable) {
