@@ -53,6 +53,32 @@ __global__ void router_seq_kernel(RouterArgs a) {
 
 namespace {
 
+// Chunk partials of one (expert, chunk) item for every token, kTB tokens at a time.
+template <int kTB>
+__device__ __forceinline__ void chunk_partials(const RouterArgs& a, const RouterFusedArgs& f, const float* wr,
+                                               uint64_t j0, uint64_t e, uint64_t c, uint64_t chunks, int lane) {
+    for (uint64_t t0 = 0; t0 < a.tokens; t0 += kTB) {
+        float xr[kTB][16];
+#pragma unroll
+        for (int u = 0; u < kTB; u++)
+#pragma unroll
+            for (int q = 0; q < 16; q++) {
+                uint64_t j = j0 + (uint64_t)q * 32 + lane;
+                xr[u][q] = (t0 + u < a.tokens && j < a.hidden) ? __ldg(a.x + (t0 + u) * a.hidden + j) : 0.0f;
+            }
+#pragma unroll
+        for (int u = 0; u < kTB; u++) {
+            if (t0 + u >= a.tokens) break;
+            float acc = 0.0f;
+#pragma unroll
+            for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(wr[q], xr[u][q]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
+            if (lane == 0) f.partials[((t0 + u) * a.experts + e) * chunks + c] = acc;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFusedArgs f) {
     const RouterArgs& a = f.r;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -83,27 +109,10 @@ __global__ void __launch_bounds__(kRouterThreads) router_fused_kernel(RouterFuse
                 uint64_t j = j0 + (uint64_t)q * 32 + lane;
                 wr[q] = j < a.hidden ? __ldcs(w + j) : 0.0f;
             }
-            // tokens four at a time: their loads in flight together
-            for (uint64_t t0 = 0; t0 < a.tokens; t0 += 4) {
-                float xr[4][16];
-#pragma unroll
-                for (int u = 0; u < 4; u++)
-#pragma unroll
-                    for (int q = 0; q < 16; q++) {
-                        uint64_t j = j0 + (uint64_t)q * 32 + lane;
-                        xr[u][q] = (t0 + u < a.tokens && j < a.hidden) ? __ldg(a.x + (t0 + u) * a.hidden + j) : 0.0f;
-                    }
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    if (t0 + u >= a.tokens) break;
-                    float acc = 0.0f;
-#pragma unroll
-                    for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(wr[q], xr[u][q]));
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-                    if (lane == 0) f.partials[((t0 + u) * a.experts + e) * chunks + c] = acc;
-                }
-            }
+            // several tokens: four at a time, their loads in flight together
+            // (a single token takes the one-token instance: no idle loads)
+            if (a.tokens == 1) chunk_partials<1>(a, f, wr, j0, e, c, chunks, lane);
+            else chunk_partials<4>(a, f, wr, j0, e, c, chunks, lane);
             int bad_q = -1;
             uint32_t bad_bits = 0;
 #pragma unroll
