@@ -192,25 +192,28 @@ int32_t run_f32_gemv(lbk_context* ctx, const lbk_matrix* w, const float* x, uint
 struct WsLayout {
     uint64_t rcounter, logits, partials, q8x, routed, h, hq, counters, dcounters, counter_words, dots, g, u, total;
     uint64_t grp_n, grp, grp_pairs;  // grouped kernels (T >= 2): group count, groups, grouped pairs
-    uint64_t rflag;                  // single token: routing-published flag (in the zeroed counter region)
+    uint64_t rflag, rreaders;        // single token: routing-published flag, and the down CTAs that have read it
 };
 
 uint64_t up256(uint64_t v) { return (v + 255) & ~(uint64_t)255; }
 
-// Workspace of one MoE call. Byte 0 holds the router's arrival counter, at
-// the same place for every layer and token count, so a workspace stays valid
-// across calls of different shapes once it was zero-filled; the other arrival
-// counters ([gate/up h blocks][down combine blocks]) move with the shape and
-// are zeroed by the router kernel of every call.
+// Workspace of one MoE call. Bytes 0-15 sit at the same place for every
+// layer and token count: the router's arrival counter (byte 0), the
+// single-token routing flag (byte 4) and the count of down CTAs that have
+// read it (byte 8). Each is back at zero when a call ends, so a workspace
+// stays valid across calls of different shapes once it was zero-filled. The
+// other arrival counters ([gate/up h blocks][down combine blocks]) move with
+// the shape and are zeroed by the router kernel of every call.
 WsLayout moe_ws(const lbk_moe_layer* L, uint64_t T, uint64_t k) {
     WsLayout o{};
     uint64_t slots = T * (k + 1);
     uint64_t nbh = L->H / LBK_QK_K, nbf = L->F / LBK_QK_K;
     o.rcounter = 0;
+    o.rflag = 4;
+    o.rreaders = 8;
     o.counters = 16;
     o.dcounters = o.counters + slots * nbf * 4;
-    o.rflag = o.dcounters + T * ((L->H + lbk::kMoeDownCombineRows - 1) / lbk::kMoeDownCombineRows) * 4;
-    const uint64_t cend = o.rflag + 16;
+    const uint64_t cend = o.dcounters + T * ((L->H + lbk::kMoeDownCombineRows - 1) / lbk::kMoeDownCombineRows) * 4;
     o.counter_words = (cend - o.counters) / 4;
     uint64_t off = up256(cend);
     o.dots = off;  // down row dots [T][k+1][H]
@@ -1138,6 +1141,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             d.has_shared = mode.shared ? 1 : 0;
             d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
             d.route_flag = g.route_flag;
+            d.route_readers = g.route_flag ? reinterpret_cast<unsigned int*>(ws + o.rreaders) : nullptr;
             e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
             if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
             if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);
@@ -1190,17 +1194,29 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
 
 }  // namespace
 
-LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
-                                lbk_routed* routed_out, int32_t router_mode, void* workspace, uint64_t workspace_bytes,
-                                void* stream) {
+namespace {
+// Checks of lbk_moe_forward's arguments other than the workspace (shared
+// with lbk_moe_forward_no_alloc, which runs them before any device work).
+int32_t check_forward_args(const lbk_moe_layer* layer, const float* x, uint64_t tokens, const float* out,
+                           int32_t router_mode) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
     if (layer->E_local != layer->E) return fail(LBK_INVALID_PARAMETER, "an expert-parallel layer runs through lbk_ep_*");
     if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
     if (router_mode != LBK_ROUTER_SEQUENTIAL && router_mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "router mode");
+    if (x == nullptr || out == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(x, 16)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
+    return LBK_OK;
+}
+}  // namespace
+
+LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
+                                lbk_routed* routed_out, int32_t router_mode, void* workspace, uint64_t workspace_bytes,
+                                void* stream) {
+    if (int32_t s = check_forward_args(layer, x, tokens, out, router_mode)) return s;
     WsLayout o = moe_ws(layer, tokens, layer->k);
     if (workspace_bytes < o.total) return fail(LBK_SCRATCH_TOO_SMALL, "MoE workspace", 0, o.total, workspace_bytes);
-    if (x == nullptr || out == nullptr || workspace == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
-    if (!aligned(x, 16) || !aligned(workspace, 256)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
+    if (workspace == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(workspace, 256)) return fail(LBK_INVALID_PARAMETER, "x 16-byte / workspace 256-byte alignment");
     lbk_context* ctx = layer->ctx;
     if (int32_t s = set_device(ctx)) return s;
     cudaStream_t st = as_stream(stream);
@@ -1509,9 +1525,9 @@ LBK_API int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t
 // race on it; serialize them (one stream, or events). Layers and token counts
 // whose workspace exceeds kStaticScratchBytes are rejected with
 // LBK_SCRATCH_TOO_SMALL. The workspace's first 16 bytes (the router's arrival
-// counter) must be zero when a call starts: the first call on a device
-// zero-fills the whole array, and every call that runs to completion leaves
-// that counter at zero again.
+// counter, the routing flag and its reader count) must be zero when a call
+// starts: the first call on a device zero-fills the whole array, and every
+// call that runs to completion leaves those words at zero again.
 namespace {
 
 constexpr uint64_t kStaticScratchBytes = 1ull << 20;  // 1 MiB: hidden 4096 / ffn 1536 / top-8 decode up to 4 tokens
@@ -1546,8 +1562,8 @@ int32_t static_scratch(int device, uint8_t** out) {
 
 LBK_API int32_t lbk_moe_forward_no_alloc(lbk_moe_layer* layer, const float* x, uint64_t tokens, float* out,
                                          lbk_routed* routed_out, int32_t router_mode, void* stream) {
-    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
-    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    // every argument check runs before the first call's set-up touches the device
+    if (int32_t s = check_forward_args(layer, x, tokens, out, router_mode)) return s;
     const uint64_t need = moe_ws(layer, tokens, layer->k).total;
     if (need > kStaticScratchBytes)
         return fail(LBK_SCRATCH_TOO_SMALL,

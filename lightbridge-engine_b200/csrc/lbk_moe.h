@@ -86,7 +86,10 @@ struct MoeDownArgs {
     const uint4* grp;
     const uint32_t* grp_pairs;
     uint32_t gsize_r, gsize_s;
-    const unsigned int* route_flag;  // single token: the gate/up kernel's routing flag (early copies), or null
+    // single token: the gate/up kernel's routing flag (early copies), or null;
+    // the last routed CTA to have read it clears it and route_readers
+    unsigned int* route_flag;
+    unsigned int* route_readers;
     DeviceStatus* status;
     Tables tables;
 };

@@ -1138,6 +1138,18 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
         __syncthreads();
         const bool early = s_early != 0;
         if (!early) grid_dep_wait();  // the routing and h images of the gate/up kernel
+        // The flag is cleared by the last routed CTA to have read it, so the
+        // next call's down kernel (which may start before that call's router
+        // has run) never sees this call's flag. A CTA that did not see the
+        // flag has waited for the gate/up grid, so the flag was set before it
+        // arrives here. The next call's router starts only after this grid
+        // ends, which orders the clear before that call's gate/up and down.
+        if (a.route_flag != nullptr && threadIdx.x == 0) {
+            if (atomicAdd(a.route_readers, 1u) + 1u == a.routed_ctas) {
+                *a.route_readers = 0u;
+                atomicExch(a.route_flag, 0u);
+            }
+        }
         if (tab_tx != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 3, 0);
         }

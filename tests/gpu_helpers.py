@@ -35,10 +35,31 @@ def bits(a) -> np.ndarray:
     return np.asarray(a, dtype=np.float32).view(np.uint32)
 
 
-def rel_err(got: np.ndarray, want: np.ndarray) -> float:
+# Element-wise relative error is taken against max(|want_i|, REL_FLOOR * max|want|):
+# an element smaller than a thousandth of the output's largest magnitude is
+# held to an absolute error of 1e-8 of that magnitude instead of to its own size.
+REL_FLOOR = 1e-3
+
+
+def norm_err(got: np.ndarray, want: np.ndarray) -> float:
     """max |got - want| / max |want| (norm-wise relative error)."""
     scale = float(np.max(np.abs(want))) or 1.0
     return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / scale
+
+
+def rel_err(got: np.ndarray, want: np.ndarray, floor: float = REL_FLOOR) -> float:
+    """Element-wise relative error: max_i |got_i - want_i| / max(|want_i|, floor * max|want|).
+
+    Never below norm_err, so a bar on it bounds both."""
+    g = np.asarray(got, np.float64)
+    w = np.asarray(want, np.float64)
+    scale = float(np.max(np.abs(w))) or 1.0
+    den = np.maximum(np.abs(w), floor * scale)
+    return float(np.max(np.abs(g - w) / den))
+
+
+def errs(got: np.ndarray, want: np.ndarray) -> str:
+    return f"element-wise {rel_err(got, want):.3e} (floor {REL_FLOOR} of max|want|), norm-wise {norm_err(got, want):.3e}"
 
 
 def planar_dev(ty: int, gguf: np.ndarray, in_w: int) -> torch.Tensor:
@@ -105,3 +126,15 @@ def upload_layer(router, experts, shared, layout, top_k, weight_scale=2.826, bia
     keep.append(b)
     layer = lbk.MoeLayer(ctx(), dex, sh, rm, b, top_k, weight_scale)
     return layer, keep
+
+
+def topk_margins(router: np.ndarray, xs: np.ndarray, bias: np.ndarray, k: int) -> np.ndarray:
+    """Per token: the gap between the k-th and (k+1)-th selection score
+    (sigmoid(logit) + bias, route_experts_into's sort key). Top-k identity on a
+    test input is only meaningful where this gap is well above rounding."""
+    out = []
+    for x in xs:
+        logits = orc.gemv_f32(router.shape[1], router.shape[0], router.reshape(-1), x).astype(np.float64)
+        s = np.sort(1.0 / (1.0 + np.exp(-logits)) + bias.astype(np.float64))[::-1]
+        out.append(s[k - 1] - s[k])
+    return np.array(out)

@@ -15,7 +15,7 @@ import ep
 import lbk
 import oracle as orc
 from gguf_fixture import Hy3Block, write_hy3
-from gpu_helpers import clean_status, ctx, dev, rel_err, upload_layer
+from gpu_helpers import clean_status, ctx, dev, errs, rel_err, upload_layer
 
 pytestmark = pytest.mark.gpu
 

@@ -14,7 +14,8 @@ import torch
 
 import lbk
 import oracle as orc
-from gpu_helpers import bits, clean_status, dev, expect_status, host, make_layer_np, rel_err, upload_layer
+from gpu_helpers import (bits, clean_status, dev, errs, expect_status, host, make_layer_np, rel_err, topk_margins,
+                         upload_layer)
 
 pytestmark = pytest.mark.gpu
 
@@ -81,14 +82,16 @@ def test_grouped_equals_ungrouped_and_oracle(H, F, E, k, T, types):
     for t in (0, T // 2, T - 1):  # oracle on a few tokens (seconds each at these sizes)
         want, wids, _ = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t])
         np.testing.assert_array_equal(ia[t], wids)
-        assert rel_err(a[t], want) <= TOL, rel_err(a[t], want)
+        assert rel_err(a[t], want) <= TOL, errs(a[t], want)
     layer.close()
 
 
 def test_config3_shapes_64_tokens():
     """BASELINE config 4's layer (hidden 4096, 192 experts, FFN 1536, IQ2_S
     gate/up, IQ3_S down, shared Q4_K, top-8) at 64 tokens, seed 3: grouped
-    equals ungrouped bit for bit; two tokens against the oracle."""
+    equals ungrouped bit for bit; every token against the oracle (single pass,
+    moe_routed_by_id_into without the preflight, which does not change the
+    result)."""
     rng = np.random.default_rng(3)
     H, F, E, k, T = 4096, 1536, 192, 8, 64
     router, experts, shared = make_layer_np(rng, H, F, E)
@@ -98,10 +101,15 @@ def test_config3_shapes_64_tokens():
     np.testing.assert_array_equal(ia, ib)
     np.testing.assert_array_equal(bits(a), bits(b))
     table = orc.ExpertTable(experts, shared, router=router, hidden=H)
-    for t in (0, 63):
-        want, wids, _ = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t])
-        np.testing.assert_array_equal(ia[t], wids)
-        assert rel_err(a[t], want) <= TOL, rel_err(a[t], want)
+    margins = topk_margins(router, xs, np.zeros(E, np.float32), k)
+    print(f"config 4: 8th/9th selection-score margin min {margins.min():.3e}, median {np.median(margins):.3e}")
+    worst = 0.0
+    for t in range(T):
+        want, wids, _ = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t], preflight=False)
+        np.testing.assert_array_equal(ia[t], wids, err_msg=f"token {t}")
+        assert rel_err(a[t], want) <= TOL, f"token {t}: " + errs(a[t], want)
+        worst = max(worst, rel_err(a[t], want))
+    print(f"config 4: 64 tokens against the oracle, worst element-wise relative error {worst:.3e}")
     layer.close()
 
 

@@ -16,7 +16,7 @@ import torch
 
 import lbk
 import oracle as orc
-from gpu_helpers import bits, clean_status, ctx, dev, expect_status, host, make_layer_np, rel_err, upload_layer
+from gpu_helpers import bits, clean_status, ctx, dev, expect_status, host, make_layer_np, errs, rel_err, upload_layer
 
 pytestmark = pytest.mark.gpu
 
@@ -125,7 +125,7 @@ def test_block_forward_matches_oracle(mode, H, F, E, k, T):
     got = host(hd).reshape(T, H)
     ids = host(routed).reshape(T, k, 2)[:, :, 0].astype(np.uint32)
     np.testing.assert_array_equal(ids, np.stack(want_ids))
-    assert rel_err(got, want) <= TOL, rel_err(got, want)
+    assert rel_err(got, want) <= TOL, errs(got, want)
     layer.close()
 
 

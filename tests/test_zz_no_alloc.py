@@ -2,7 +2,8 @@
 library's fixed device array instead of caller memory.
 
 Checked through the C ABI against lbk_moe_forward (caller workspace) on the
-same layer and inputs, for two calls in a row (the second call starts from the
+same layer and inputs, bit for bit (the same kernels on the same inputs; only
+the workspace address differs), for two calls in a row (the second call starts from the
 counters the first one left behind), on both the fused and the per-expert
 path, and its rejection of a workspace larger than the array. Named to be
 collected last, so that it also runs after every other GPU test in one
@@ -14,11 +15,10 @@ import pytest
 import torch
 
 import lbk
-from gpu_helpers import clean_status, dev, host, make_layer_np, rel_err, upload_layer
+from gpu_helpers import bits, clean_status, dev, host, make_layer_np, upload_layer
 
 pytestmark = pytest.mark.gpu
 
-TOL = 1e-5  # same bar as the workspace forward against the oracle
 STATIC_SCRATCH_BYTES = 1 << 20
 
 
@@ -57,7 +57,7 @@ def test_no_alloc_matches_workspace_forward_twice(layout, T):
             got, got_routed = forward_no_alloc(layer, x, T, mode)
             np.testing.assert_array_equal(got_routed, want_routed)
             assert np.all(np.isfinite(got))
-            assert rel_err(got, want) <= TOL, rel_err(got, want)
+            np.testing.assert_array_equal(bits(got), bits(want))
     layer.close()
     del keep
 
@@ -83,6 +83,23 @@ def test_no_alloc_rejects_workspace_beyond_the_array():
     xs = dev(rng.standard_normal(H).astype(np.float32))
     want, _ = forward_workspace(layer, xs, 1, lbk.ROUTER_TREE)
     got, _ = forward_no_alloc(layer, xs, 1, lbk.ROUTER_TREE)
-    assert rel_err(got, want) <= TOL
+    np.testing.assert_array_equal(bits(got), bits(want))
+    layer.close()
+    del keep
+
+
+def test_no_alloc_checks_arguments_first():
+    """Bad arguments are refused before the call touches the device (the
+    first call's set-up included)."""
+    rng = np.random.default_rng(10)
+    H, F, E, k = 1024, 512, 16, 4
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    x = torch.zeros(H, device="cuda")
+    out = torch.zeros(H, device="cuda")
+    assert lbk.lib.lbk_moe_forward_no_alloc(layer.ptr, x.data_ptr(), 1, out.data_ptr(), None, 7, None) == 15
+    assert lbk.lib.lbk_moe_forward_no_alloc(layer.ptr, None, 1, out.data_ptr(), None, lbk.ROUTER_TREE, None) == 15
+    assert lbk.lib.lbk_moe_forward_no_alloc(layer.ptr, x.data_ptr() + 4, 1, out.data_ptr(), None, lbk.ROUTER_TREE,
+                                            None) == 15
     layer.close()
     del keep
