@@ -76,15 +76,27 @@ def peaks() -> tuple[float, str]:
 
 
 def profiled_traffic(kernel: str):
-    """Per-launch DRAM bytes of `kernel` from a committed ncu summary, if any."""
+    """Per-launch DRAM bytes of `kernel` from a committed ncu summary, if any:
+    (bytes, the summary's path). Not measured in this run: ncu captures come
+    from a separate profiling command (named in the summary)."""
     for f in sorted((REPO / "profiles").glob("*.md")) + sorted((REPO / "profiles").glob("*.txt")):
         for line in f.read_text().splitlines():
             if line.startswith(f"traffic_bytes_per_launch[{kernel}]:"):
                 try:
-                    return int(float(line.split(":", 1)[1].split()[0]))
+                    return int(float(line.split(":", 1)[1].split()[0])), str(f.relative_to(REPO))
                 except ValueError:
                     pass
-    return None
+    return None, None
+
+
+def cpu_model() -> str:
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 class Clocks:
@@ -246,7 +258,14 @@ def build_layers(ctx, lbk, torch, dev, layers: int, seed0: int, keep_gguf_layer0
     return tables, host0
 
 
-def cpu_baseline(host0, xs_host, budget_s: float = 12.0) -> dict:
+def cpu_baseline(host0, xs_host, budget_s: float = 8.0) -> dict:
+    """The reference's CPU path (the oracle's AVX2 restatement) on the host
+    cores, on layer 0 of the bench's tables: moe_routed_by_id_into as the
+    reference runs it (a preflight pass of every expert, then the accepting
+    pass; moe.rs:29-60) on all host threads -- the reported value -- plus the
+    same at the reference's default pool of ceil(threads / 2)
+    (bridge-kernels-cpu/src/lib.rs:121-139) and a single-pass run (no
+    preflight: half the expert work, the same result)."""
     sys.path.insert(0, str(REPO / "oracle"))
     import numpy as np
 
@@ -261,17 +280,28 @@ def cpu_baseline(host0, xs_host, budget_s: float = 12.0) -> dict:
     table = orc.ExpertTable(experts, shared, router=host0["router"], hidden=H)
     bias = np.zeros(E, np.float32)
     threads = orc.hw_threads()
-    orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs_host[0], preflight=True, simd=True, threads=threads)
-    n, t0 = 0, time.perf_counter()
-    while True:
-        orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs_host[(n + 1) % len(xs_host)], preflight=True, simd=True,
-                      threads=threads)
-        n += 1
-        dt = time.perf_counter() - t0
-        if dt >= budget_s or n >= 2000:
-            break
-    return {"value": n / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} tokens through layer 0, moe_routed_by_id_into as-is (preflight + accept), AVX2 restatement"}
+
+    def run(nthreads: int, preflight: bool, budget: float):
+        orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs_host[0], preflight=preflight, simd=True, threads=nthreads)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            orc.moe_token(table, bias, K_TOP, WEIGHT_SCALE, xs_host[(n + 1) % len(xs_host)], preflight=preflight,
+                          simd=True, threads=nthreads)
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget or n >= 2000:
+                return n, n / dt
+
+    n, v = run(threads, True, budget_s)
+    half = (threads + 1) // 2
+    nh, vh = run(half, True, budget_s * 0.5)
+    ns, vs = run(threads, False, budget_s * 0.5)
+    return {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "cpu_model": cpu_model(),
+            "sample": f"{n} tokens through layer 0, moe_routed_by_id_into as-is (preflight + accept), AVX2 restatement",
+            "variants": {
+                f"as-is, {half} threads (the reference's default ceil(threads/2))": {"value": vh, "tokens": nh},
+                f"single pass (no preflight), {threads} threads": {"value": vs, "tokens": ns}},
+            "gb_per_s_as_is": v * LAYER_B / 1e9}
 
 
 def our_arm(args, rank: int, world: int, local_rank: int) -> None:
@@ -368,7 +398,29 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
     dom = max(kernels, key=lambda k: k[2])
     peak, peak_kind = peaks()
     achieved = dom[1] / (dom[2] / 1000.0) / 1e9
-    traffic = profiled_traffic(dom[0])
+    traffic, traffic_src = profiled_traffic(dom[0])
+
+    # the bit-exact router order (one f32 chain per expert, as dot_f32_row):
+    # the same calls with router_mode sequential, timed the same way
+    seq_tokens = 64
+    sgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(sgraph, stream=stream):
+        for t in range(seq_tokens):
+            tables[t % LAYERS][0].forward(xs[t], 1, outs[t], wss[t % LAYERS], router_mode=lbk.ROUTER_SEQUENTIAL,
+                                          stream=stream.cuda_stream)
+    for _ in range(3):
+        sgraph.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s0.record(stream)
+        for _ in range(5):
+            sgraph.replay()
+        s1.record(stream)
+    torch.cuda.synchronize()
+    seq_ms = s0.elapsed_time(s1) / (5 * seq_tokens)
+    del sgraph
+    ctx.raise_status(stream.cuda_stream)
 
     # e2e: per-token C-ABI calls, step inputs from pinned host, outputs read back
     x_host = torch.randn(TOKENS_PER_STEP, H, generator=torch.Generator().manual_seed(5 + rank)).pin_memory()
@@ -417,7 +469,8 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
             "config": {
                 "workload": "config3: routed-MoE FFN layer, single-token decode",
                 "hidden": H, "experts": E, "expert_ffn": F, "top_k": K_TOP,
-                "gate_up": "IQ2_S", "down": "IQ3_S", "shared": "Q4_K", "router": "F32 (tree order)",
+                "gate_up": "IQ2_S", "down": "IQ3_S", "shared": "Q4_K",
+                "router": "F32, tree order (the headline; logits within 1e-5 of the reference's sequential sum)",
                 "tokens_per_step": TOKENS_PER_STEP, "resident_layers": LAYERS,
                 "l2": f"inputs larger than L2: tokens rotate over {LAYERS} resident layers ({LAYERS * 1.3:.1f} GB)",
                 "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
@@ -427,7 +480,12 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
             "kernel_ms": {"router_fused": avg[0], "moe_gate_up": avg[1], "moe_down": avg[2]},
             "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                         "traffic_source": f"stored ncu capture ({traffic_src}), not measured in this run"
+                         if traffic_src else None,
                          "algorithmic_bytes_per_launch": dom[1]},
+            "router_sequential": {"value": 1000.0 / seq_ms, "unit": "tokens/s", "us_per_token": seq_ms * 1000.0,
+                                  "what": "the same layer calls with the bit-exact sequential router "
+                                          "(one f32 chain per expert, dot_f32_row order)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": TOKENS_PER_STEP * H * 4,
                     "d2h_bytes_per_step": TOKENS_PER_STEP * H * 4},
             "gpu_launches": args.steps * TOKENS_PER_STEP * 3,

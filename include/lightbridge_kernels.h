@@ -275,6 +275,16 @@ int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer);
  * (moe_routed_by_id_into, moe.rs:64-147). */
 int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens);
 
+/* Bound of a single-token call's wait for its routing: the down kernel polls
+ * the flag with which the gate/up kernel publishes the routing (so that it can
+ * request its first rows before the gate/up grid ends) at most `polls` times
+ * (default 2^20, far beyond the few microseconds the publication takes). A
+ * wait that runs out is reported as LBK_TIMEOUT through the status word and
+ * the call's output is left unwritten; the kernels still finish (the wait has
+ * no copy in flight), so the workspace and the context stay usable. No
+ * counterpart in the reference, whose calls are synchronous. */
+int32_t lbk_moe_layer_set_wait_limit(lbk_moe_layer* layer, uint32_t polls);
+
 /* Workspace bytes for `tokens` tokens. The workspace must be zero-filled once
  * before its first use (its first 16 bytes hold an arrival counter that every
  * completed call leaves at zero; the rest is rewritten by every call), so one
@@ -337,6 +347,29 @@ int32_t lbk_moe_block_workspace_bytes(const lbk_moe_layer* layer, uint64_t token
 int32_t lbk_moe_block_forward(lbk_moe_layer* layer, float* hidden, const float* ffn_norm, float epsilon,
                               uint64_t tokens, lbk_routed* routed_out, int32_t router_mode, void* workspace,
                               uint64_t workspace_bytes, void* stream);
+
+/* The same block in the reference's two phases, for a runtime that acts on
+ * the routing between them. Route: the FFN part of hy3_moe_route_token
+ * (layer.rs:473-605 from the FFN RMSNorm on: norm, router, top-k); the
+ * routing (tokens*top_k entries) stays in the block workspace and is copied to
+ * routed_out when that is not null. Finish: hy3_moe_finish_token
+ * (layer.rs:610-659): `selected` (device, tokens*top_k entries) must equal the
+ * route phase's routing in expert IDs and coefficient bits, checked on the
+ * device before anything is written (a mismatch is reported through the
+ * status word as LBK_INVALID_PARAMETER at the first differing entry and
+ * leaves hidden untouched); then the experts, the combine and hidden +=
+ * delta. The phase is kept per workspace as the reference keeps it per
+ * scratch: a second route on a workspace before its finish, or a finish
+ * without a route, returns LBK_INVALID_PARAMETER; a finish with another token
+ * count returns LBK_DIMENSION_MISMATCH (host checks, before any launch). The
+ * phase ends when finish has been enqueued; device-side failures of finish
+ * surface at the next status sync, as for every call. Workspace: as
+ * lbk_moe_block_workspace_bytes. */
+int32_t lbk_moe_block_route(lbk_moe_layer* layer, const float* hidden, const float* ffn_norm, float epsilon,
+                            uint64_t tokens, lbk_routed* routed_out, int32_t router_mode, void* workspace,
+                            uint64_t workspace_bytes, void* stream);
+int32_t lbk_moe_block_finish(lbk_moe_layer* layer, float* hidden, uint64_t tokens, const lbk_routed* selected,
+                             void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------ expert parallelism */
 

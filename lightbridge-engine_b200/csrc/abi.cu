@@ -15,6 +15,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -60,6 +61,12 @@ struct lbk_moe_layer {
     bool tracing;
     void* owned;                         // device memory freed with the layer (lbk_moe_layer_load)
     uint64_t group_min = 8;              // calls of at least this many tokens (items) run the grouped kernels; 0: never
+    uint32_t wait_limit = 1u << 20;      // polls of the down kernel's wait for the single-token routing flag
+    // Block workspaces between lbk_moe_block_route and lbk_moe_block_finish,
+    // with the routed call's token count (the reference keeps this phase in
+    // its per-token scratch: Hy3BlockScratch::streaming_moe_pending).
+    std::mutex phase_mu;
+    std::map<const void*, uint64_t> pending;
 };
 
 namespace {
@@ -791,6 +798,12 @@ LBK_API int32_t lbk_moe_layer_destroy(lbk_moe_layer* layer) {
 
 LBK_API int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer) { return layer && layer->fused ? 1 : 0; }
 
+LBK_API int32_t lbk_moe_layer_set_wait_limit(lbk_moe_layer* layer, uint32_t polls) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    layer->wait_limit = polls;
+    return ok();
+}
+
 LBK_API int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
     layer->group_min = min_tokens;
@@ -1142,6 +1155,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
             d.route_flag = g.route_flag;
             d.route_readers = g.route_flag ? reinterpret_cast<unsigned int*>(ws + o.rreaders) : nullptr;
+            d.route_polls = L->wait_limit;
             e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
             if (e != cudaSuccess) return cuda_fail(e, "moe down launch");
             if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);
@@ -1195,6 +1209,51 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
 }  // namespace
 
 namespace {
+// Router logits and top-k of `tokens` tokens into `routed` (unless `defer`:
+// then the gate/up kernel finishes the top-k), plus the tokens' Q8_K images
+// for the fused kernels: the route step of hy3_moe_route_token
+// (layer.rs:583-603; gemv_into on the router, route_experts_into).
+int32_t launch_routing(lbk_moe_layer* layer, const float* x, uint64_t tokens, lbk_routed* routed, int32_t router_mode,
+                       uint8_t* ws, const WsLayout& o, bool defer, cudaStream_t st) {
+    lbk_context* ctx = layer->ctx;
+    float* logits = reinterpret_cast<float*>(ws + o.logits);
+    lbk::RouterFusedArgs f{};
+    f.r.w = static_cast<const float*>(layer->w.router.data);
+    f.r.x = x;
+    f.r.logits = logits;
+    f.r.hidden = layer->H;
+    f.r.experts = layer->E;
+    f.r.tokens = tokens;
+    f.r.status = ctx->status;
+    f.partials = reinterpret_cast<float*>(ws + o.partials);
+    f.q8x = layer->fused ? ws + o.q8x : nullptr;
+    f.counter = reinterpret_cast<unsigned int*>(ws + o.rcounter);
+    f.zero = reinterpret_cast<unsigned int*>(ws + o.counters);
+    f.zero_words = layer->fused ? o.counter_words : 0;
+    f.bias = layer->w.selection_bias;
+    f.k = (uint32_t)layer->k;
+    f.weight_scale = layer->weight_scale;
+    f.routed = routed;
+    f.defer = defer ? 1 : 0;
+    cudaError_t e;
+    if (router_mode == LBK_ROUTER_TREE) {
+        e = lbk::launch_router_fused(f, ctx->sm_count, st);
+        if (e != cudaSuccess) return cuda_fail(e, "router launch");
+    } else {
+        if (int32_t s = run_f32_gemv(ctx, &layer->w.router, x, tokens, logits, st)) return s;
+        lbk::TopkArgs ta{logits, layer->w.selection_bias, layer->E, tokens, (uint32_t)layer->k, layer->weight_scale, routed,
+                         ctx->status};
+        if ((e = lbk::launch_topk(ta, st)) != cudaSuccess) return cuda_fail(e, "top-k launch");
+        if (layer->fused) {  // quantize the tokens only
+            lbk::RouterFusedArgs q = f;
+            q.r.experts = 0;
+            q.routed = nullptr;
+            if ((e = lbk::launch_router_fused(q, ctx->sm_count, st)) != cudaSuccess) return cuda_fail(e, "quantize launch");
+        }
+    }
+    return LBK_OK;
+}
+
 // Checks of lbk_moe_forward's arguments other than the workspace (shared
 // with lbk_moe_forward_no_alloc, which runs them before any device work).
 int32_t check_forward_args(const lbk_moe_layer* layer, const float* x, uint64_t tokens, const float* out,
@@ -1222,49 +1281,15 @@ LBK_API int32_t lbk_moe_forward(lbk_moe_layer* layer, const float* x, uint64_t t
     cudaStream_t st = as_stream(stream);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     lbk_routed* routed = routed_out ? routed_out : reinterpret_cast<lbk_routed*>(ws + o.routed);
-    float* logits = reinterpret_cast<float*>(ws + o.logits);
 
-    lbk::RouterFusedArgs f{};
-    f.r.w = static_cast<const float*>(layer->w.router.data);
-    f.r.x = x;
-    f.r.logits = logits;
-    f.r.hidden = layer->H;
-    f.r.experts = layer->E;
-    f.r.tokens = tokens;
-    f.r.status = ctx->status;
-    f.partials = reinterpret_cast<float*>(ws + o.partials);
-    f.q8x = layer->fused ? ws + o.q8x : nullptr;
-    f.counter = reinterpret_cast<unsigned int*>(ws + o.rcounter);
-    f.zero = reinterpret_cast<unsigned int*>(ws + o.counters);
-    f.zero_words = layer->fused ? o.counter_words : 0;
-    f.bias = layer->w.selection_bias;
-    f.k = (uint32_t)layer->k;
-    f.weight_scale = layer->weight_scale;
-    f.routed = routed;
-    cudaError_t e;
     // Single-token decode on the fused kernels: the gate/up kernel finishes the
     // router (partials -> logits -> top-k) in every CTA's prologue.
     const bool defer = layer->fused && tokens == 1 && router_mode == LBK_ROUTER_TREE &&
                        (!lbk::moe_gate_up_tma_supported(layer->gate_type, layer->sgate_type, (int)(layer->H / LBK_QK_K)) ||
                         lbk::moe_gate_up_tma_defer_fits(layer->gate_type, layer->E,
                                                         lbk::router_partials_floats(layer->H, 1, 1)));
-    f.defer = defer ? 1 : 0;
     if (layer->tracing) trace_record(layer->trace[0], st, cudaEventRecordExternal);
-    if (router_mode == LBK_ROUTER_TREE) {
-        e = lbk::launch_router_fused(f, ctx->sm_count, st);
-        if (e != cudaSuccess) return cuda_fail(e, "router launch");
-    } else {
-        if (int32_t s = run_f32_gemv(ctx, &layer->w.router, x, tokens, logits, st)) return s;
-        lbk::TopkArgs ta{logits, layer->w.selection_bias, layer->E, tokens, (uint32_t)layer->k, layer->weight_scale, routed,
-                         ctx->status};
-        if ((e = lbk::launch_topk(ta, st)) != cudaSuccess) return cuda_fail(e, "top-k launch");
-        if (layer->fused) {  // quantize the tokens only
-            lbk::RouterFusedArgs q = f;
-            q.r.experts = 0;
-            q.routed = nullptr;
-            if ((e = lbk::launch_router_fused(q, ctx->sm_count, st)) != cudaSuccess) return cuda_fail(e, "quantize launch");
-        }
-    }
+    if (int32_t s = launch_routing(layer, x, tokens, routed, router_mode, ws, o, defer, st)) return s;
     if (layer->tracing) trace_record(layer->trace[1], st, cudaEventRecordExternal);
     int32_t s = moe_experts(layer, x, tokens, routed, out, ws, o, st, defer, full_mode(layer));
     if (s == LBK_OK && layer->tracing && !layer->fused) {
@@ -1346,10 +1371,31 @@ LBK_API int32_t lbk_residual_add(lbk_context* ctx, float* dest, const float* src
 
 namespace {
 
-// [normalized input T*H][MoE output T*H][lbk_moe_forward's workspace]
-uint64_t block_ws_bytes(const lbk_moe_layer* L, uint64_t T) {
+// [normalized input T*H][MoE output T*H][routing T*k (route / finish)][lbk_moe_forward's workspace]
+struct BlockWs {
+    uint64_t normed, delta, routing, moe, total;
+};
+BlockWs block_ws(const lbk_moe_layer* L, uint64_t T) {
     const uint64_t a = moe_ws(L, T, L->k).total, b = moe_ws(L, 1, L->k).total;
-    return 2 * up256(T * L->H * 4) + (a > b ? a : b);
+    BlockWs w{};
+    w.normed = 0;
+    w.delta = up256(T * L->H * 4);
+    w.routing = w.delta + up256(T * L->H * 4);
+    w.moe = w.routing + up256(T * (L->k ? L->k : 1) * sizeof(lbk_routed));
+    w.total = w.moe + (a > b ? a : b);
+    return w;
+}
+uint64_t block_ws_bytes(const lbk_moe_layer* L, uint64_t T) { return block_ws(L, T).total; }
+
+// Entry j of the caller's routing against the route phase's: expert ID and
+// coefficient bits (layer.rs:631-640); the first mismatch is reported.
+__global__ void routing_identity_kernel(const lbk_routed* selected, const lbk_routed* routing, uint64_t n,
+                                        lbk::DeviceStatus* st) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+        const lbk_routed a = selected[i], b = routing[i];
+        if (a.expert_id != b.expert_id || __float_as_uint(a.coefficient) != __float_as_uint(b.coefficient))
+            lbk::report(st, LBK_INVALID_PARAMETER, i, __float_as_uint(a.coefficient));
+    }
 }
 
 }  // namespace
@@ -1377,21 +1423,110 @@ LBK_API int32_t lbk_moe_block_forward(lbk_moe_layer* layer, float* hidden, const
     if (int32_t s = set_device(ctx)) return s;
     cudaStream_t st = as_stream(stream);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const uint64_t vec = up256(tokens * layer->H * 4);
-    float* normed = reinterpret_cast<float*>(ws);
-    float* delta = reinterpret_cast<float*>(ws + vec);
+    const BlockWs bw = block_ws(layer, tokens);
+    float* normed = reinterpret_cast<float*>(ws + bw.normed);
+    float* delta = reinterpret_cast<float*>(ws + bw.delta);
     // hy3_moe_route_token's FFN norm (layer.rs:588-593)
     lbk::NormArgs na{hidden, ffn_norm, epsilon, normed, tokens, layer->H, router_mode == LBK_ROUTER_SEQUENTIAL ? 1 : 0,
                      ctx->status};
     cudaError_t e = lbk::launch_rms_norm(na, ctx->sm_count, st);
     if (e != cudaSuccess) return cuda_fail(e, "RMSNorm launch");
     // router, top-k, experts, combine
-    if (int32_t s = lbk_moe_forward(layer, normed, tokens, delta, routed_out, router_mode, ws + 2 * vec,
-                                    workspace_bytes - 2 * vec, stream))
+    if (int32_t s = lbk_moe_forward(layer, normed, tokens, delta, routed_out, router_mode, ws + bw.moe,
+                                    workspace_bytes - bw.moe, stream))
         return s;
     // hy3_moe_finish_token's residual add (layer.rs:654)
     e = lbk::launch_residual_add(hidden, delta, tokens * layer->H, ctx->scratch_min, ctx->status, ctx->sm_count, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "residual add launch");
+}
+
+namespace {
+int32_t block_args(const lbk_moe_layer* layer, const void* hidden, uint64_t tokens, const void* workspace,
+                   uint64_t workspace_bytes) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (layer->E_local != layer->E) return fail(LBK_INVALID_PARAMETER, "an expert-parallel layer runs through lbk_ep_*");
+    if (tokens == 0) return fail(LBK_DIMENSION_MISMATCH, "token count", 0, 1, 0);
+    if (hidden == nullptr || workspace == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(hidden, 16) || !aligned(workspace, 256))
+        return fail(LBK_INVALID_PARAMETER, "hidden 16-byte / workspace 256-byte alignment");
+    const uint64_t need = block_ws_bytes(layer, tokens);
+    if (workspace_bytes < need) return fail(LBK_SCRATCH_TOO_SMALL, "MoE block workspace", 0, need, workspace_bytes);
+    return LBK_OK;
+}
+}  // namespace
+
+LBK_API int32_t lbk_moe_block_route(lbk_moe_layer* layer, const float* hidden, const float* ffn_norm, float epsilon,
+                                    uint64_t tokens, lbk_routed* routed_out, int32_t router_mode, void* workspace,
+                                    uint64_t workspace_bytes, void* stream) {
+    if (int32_t s = block_args(layer, hidden, tokens, workspace, workspace_bytes)) return s;
+    if (int32_t s = norm_params(layer->H, epsilon)) return s;
+    if (ffn_norm == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (router_mode != LBK_ROUTER_SEQUENTIAL && router_mode != LBK_ROUTER_TREE) return fail(LBK_INVALID_PARAMETER, "router mode");
+    {
+        std::lock_guard<std::mutex> lock(layer->phase_mu);
+        if (layer->pending.count(workspace))  // layer.rs:488-493
+            return fail(LBK_INVALID_PARAMETER,
+                        "streaming MoE phase: the previous routed phase must be completed before routing again");
+    }
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const BlockWs bw = block_ws(layer, tokens);
+    float* normed = reinterpret_cast<float*>(ws + bw.normed);
+    lbk_routed* routing = reinterpret_cast<lbk_routed*>(ws + bw.routing);
+    // hy3_moe_route_token's FFN norm, router and top-k (layer.rs:588-603)
+    lbk::NormArgs na{hidden, ffn_norm, epsilon, normed, tokens, layer->H, router_mode == LBK_ROUTER_SEQUENTIAL ? 1 : 0,
+                     ctx->status};
+    cudaError_t e = lbk::launch_rms_norm(na, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(e, "RMSNorm launch");
+    uint8_t* mws = ws + bw.moe;
+    if (int32_t s = launch_routing(layer, normed, tokens, routing, router_mode, mws, moe_ws(layer, tokens, layer->k), false, st))
+        return s;
+    if (routed_out != nullptr) {
+        e = cudaMemcpyAsync(routed_out, routing, tokens * layer->k * sizeof(lbk_routed), cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "routing copy");
+    }
+    std::lock_guard<std::mutex> lock(layer->phase_mu);
+    layer->pending[workspace] = tokens;
+    return ok();
+}
+
+LBK_API int32_t lbk_moe_block_finish(lbk_moe_layer* layer, float* hidden, uint64_t tokens, const lbk_routed* selected,
+                                     void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (int32_t s = block_args(layer, hidden, tokens, workspace, workspace_bytes)) return s;
+    if (selected == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    {
+        std::lock_guard<std::mutex> lock(layer->phase_mu);
+        auto it = layer->pending.find(workspace);
+        if (it == layer->pending.end())  // layer.rs:617-622
+            return fail(LBK_INVALID_PARAMETER, "streaming MoE phase: routing must run exactly once before completion");
+        if (it->second != tokens)  // layer.rs:624-630
+            return fail(LBK_DIMENSION_MISMATCH, "streaming selected expert count", 0, it->second * layer->k,
+                        tokens * layer->k);
+    }
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const BlockWs bw = block_ws(layer, tokens);
+    const float* normed = reinterpret_cast<const float*>(ws + bw.normed);
+    float* delta = reinterpret_cast<float*>(ws + bw.delta);
+    const lbk_routed* routing = reinterpret_cast<const lbk_routed*>(ws + bw.routing);
+    // IDs and coefficient bits against the route phase (layer.rs:631-640),
+    // before anything is written: a mismatch leaves delta and hidden untouched
+    const uint64_t n = tokens * layer->k;
+    routing_identity_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(selected, routing, n, ctx->status);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "routing check launch");
+    // moe_selected_into and the residual add (layer.rs:648-656)
+    if (int32_t s = lbk_moe_routed(layer, normed, tokens, selected, delta, ws + bw.moe, workspace_bytes - bw.moe, stream))
+        return s;
+    e = lbk::launch_residual_add(hidden, delta, tokens * layer->H, ctx->scratch_min, ctx->status, ctx->sm_count, st);
+    if (e != cudaSuccess) return cuda_fail(e, "residual add launch");
+    std::lock_guard<std::mutex> lock(layer->phase_mu);
+    layer->pending.erase(workspace);
+    return ok();
 }
 
 // --------------------------------------------------- expert parallelism

@@ -90,6 +90,7 @@ struct MoeDownArgs {
     // the last routed CTA to have read it clears it and route_readers
     unsigned int* route_flag;
     unsigned int* route_readers;
+    uint32_t route_polls;            // polls of route_flag before LBK_TIMEOUT
     DeviceStatus* status;
     Tables tables;
 };

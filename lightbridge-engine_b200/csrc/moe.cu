@@ -1127,12 +1127,16 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
     if (routed_role) {
         // Single token: the routing is final long before the gate/up grid
         // ends. Once its flag is seen (bounded poll), the first down rows are
-        // requested before the wait for that grid; h is read after it.
+        // requested before the wait for that grid; h is read after it. A poll
+        // that runs out is reported (the output is then left unwritten) and
+        // the CTA goes on after the grid wait: no copy is in flight yet.
         __shared__ int s_early;
         if (threadIdx.x == 0) {
             int ok = 0;
-            if (a.route_flag != nullptr)
-                for (uint32_t i = 0; i < (1u << 20) && !ok; i++) ok = ld_acquire_gpu(a.route_flag) != 0u;
+            if (a.route_flag != nullptr) {
+                for (uint32_t i = 0; i < a.route_polls && !ok; i++) ok = ld_acquire_gpu(a.route_flag) != 0u;
+                if (!ok) report(a.status, LBK_TIMEOUT, 4, 0);
+            }
             s_early = ok;
         }
         __syncthreads();

@@ -175,6 +175,7 @@ def _load() -> ctypes.CDLL:
         "lbk_moe_layer_destroy": ([P], I32),
         "lbk_moe_layer_fused": ([P], I32),
         "lbk_moe_layer_set_grouping": ([P, U64], I32),
+        "lbk_moe_layer_set_wait_limit": ([P, U32], I32),
         "lbk_moe_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
         "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
         "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
@@ -183,6 +184,8 @@ def _load() -> ctypes.CDLL:
         "lbk_residual_add": ([P, P, P, U64, P], I32),
         "lbk_moe_block_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
         "lbk_moe_block_forward": ([P, P, P, F, U64, P, I32, P, U64, P], I32),
+        "lbk_moe_block_route": ([P, P, P, F, U64, P, I32, P, U64, P], I32),
+        "lbk_moe_block_finish": ([P, P, U64, P, P, U64, P], I32),
         "lbk_ep_layer_create": ([P, ctypes.POINTER(MoeWeights), U64, U64, P, ctypes.POINTER(P)], I32),
         "lbk_ep_q8_bytes": ([P, ctypes.POINTER(U64)], I32),
         "lbk_ep_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
@@ -216,9 +219,9 @@ EXPORTED = (
     "lbk_abi_version lbk_backend_name lbk_context_create lbk_context_destroy lbk_context_sync_status "
     "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_planar_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
-    "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused lbk_moe_layer_set_grouping "
+    "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused lbk_moe_layer_set_grouping lbk_moe_layer_set_wait_limit "
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
-    "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward "
+    "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward lbk_moe_block_route lbk_moe_block_finish "
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine "
     "lbk_repack lbk_unpack lbk_validate_matrix "
@@ -363,6 +366,9 @@ class MoeLayer:
         """Calls of at least `min_tokens` tokens run the grouped kernels (0: never)."""
         check(lib.lbk_moe_layer_set_grouping(self.ptr, min_tokens))
 
+    def set_wait_limit(self, polls: int) -> None:
+        check(lib.lbk_moe_layer_set_wait_limit(self.ptr, polls))
+
     def workspace_bytes(self, tokens: int) -> int:
         n = ctypes.c_uint64()
         check(lib.lbk_moe_workspace_bytes(self.ptr, tokens, ctypes.byref(n)))
@@ -383,6 +389,17 @@ class MoeLayer:
                       router_mode: int = ROUTER_TREE, stream=None) -> None:
         check(lib.lbk_moe_block_forward(self.ptr, _ptr(hidden), _ptr(ffn_norm), float(epsilon), tokens, _ptr(routed_out),
                                         router_mode, _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def block_route(self, hidden, ffn_norm, epsilon: float, tokens: int, workspace, routed_out=None,
+                    router_mode: int = ROUTER_TREE, stream=None) -> None:
+        """hy3_moe_route_token's FFN part (layer.rs:473-605): norm, router, top-k."""
+        check(lib.lbk_moe_block_route(self.ptr, _ptr(hidden), _ptr(ffn_norm), float(epsilon), tokens, _ptr(routed_out),
+                                      router_mode, _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def block_finish(self, hidden, tokens: int, selected, workspace, stream=None) -> None:
+        """hy3_moe_finish_token (layer.rs:610-659): identity check, experts, residual add."""
+        check(lib.lbk_moe_block_finish(self.ptr, _ptr(hidden), tokens, _ptr(selected), _ptr(workspace), workspace.numel(),
+                                       _stream(stream)))
 
     def trace(self, enable: bool = True) -> None:
         check(lib.lbk_moe_layer_trace(self.ptr, int(enable)))

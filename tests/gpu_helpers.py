@@ -35,9 +35,15 @@ def bits(a) -> np.ndarray:
     return np.asarray(a, dtype=np.float32).view(np.uint32)
 
 
-# Element-wise relative error is taken against max(|want_i|, REL_FLOOR * max|want|):
-# an element smaller than a thousandth of the output's largest magnitude is
-# held to an absolute error of 1e-8 of that magnitude instead of to its own size.
+# Element-wise relative error. A combined output row is a sum of terms
+# (moe.rs:116-147: c_j * dot_j over the routed experts, then the shared dot;
+# plus the residual in a block), and the rounding error of a sum is bounded
+# relative to the magnitude of its terms, not to the sum, which can cancel to
+# almost nothing. So the error of element i is taken against its term
+# magnitude mag_i (moe_term_magnitude) where the test supplies it, else
+# against |want_i|; in both cases with a floor of REL_FLOOR times the largest
+# denominator, so that an element a thousand times below the row's largest is
+# held to an absolute error of 1e-8 of that largest magnitude instead of to its own size.
 REL_FLOOR = 1e-3
 
 
@@ -47,19 +53,32 @@ def norm_err(got: np.ndarray, want: np.ndarray) -> float:
     return float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) / scale
 
 
-def rel_err(got: np.ndarray, want: np.ndarray, floor: float = REL_FLOOR) -> float:
-    """Element-wise relative error: max_i |got_i - want_i| / max(|want_i|, floor * max|want|).
-
-    Never below norm_err, so a bar on it bounds both."""
+def rel_err(got: np.ndarray, want: np.ndarray, mag: np.ndarray | None = None, floor: float = REL_FLOOR) -> float:
+    """Element-wise relative error: max_i |got_i - want_i| / max(d_i, floor * max d),
+    d = mag (term magnitudes) if given, else |want|."""
     g = np.asarray(got, np.float64)
     w = np.asarray(want, np.float64)
-    scale = float(np.max(np.abs(w))) or 1.0
-    den = np.maximum(np.abs(w), floor * scale)
-    return float(np.max(np.abs(g - w) / den))
+    d = np.abs(w) if mag is None else np.asarray(mag, np.float64).reshape(w.shape)
+    scale = float(np.max(d)) or 1.0
+    return float(np.max(np.abs(g - w) / np.maximum(d, floor * scale)))
 
 
-def errs(got: np.ndarray, want: np.ndarray) -> str:
-    return f"element-wise {rel_err(got, want):.3e} (floor {REL_FLOOR} of max|want|), norm-wise {norm_err(got, want):.3e}"
+def errs(got: np.ndarray, want: np.ndarray, mag: np.ndarray | None = None) -> str:
+    kind = "of term magnitudes" if mag is not None else "of |want|"
+    return (f"element-wise {rel_err(got, want, mag):.3e} ({kind}, floor {REL_FLOOR}), "
+            f"norm-wise {norm_err(got, want):.3e}")
+
+
+def moe_term_magnitude(table, ids, coefs, x) -> np.ndarray:
+    """Per output row of one token's MoE step: |shared dot| + sum_j |c_j| |routed dot_j|,
+    the magnitudes the reference's combine adds, from the oracle (one expert at a time)."""
+    x = np.ascontiguousarray(x, np.float32)
+    shared = orc.moe_routed(table, np.asarray(ids[:1], np.uint32), np.zeros(1, np.float32), x).astype(np.float64)
+    mag = np.abs(shared)
+    for e, c in zip(ids, coefs):
+        dot = orc.moe_routed(table, np.array([e], np.uint32), np.ones(1, np.float32), x).astype(np.float64) - shared
+        mag += abs(float(c)) * np.abs(dot)
+    return mag
 
 
 def planar_dev(ty: int, gguf: np.ndarray, in_w: int) -> torch.Tensor:

@@ -15,7 +15,7 @@ import ep
 import lbk
 import oracle as orc
 from gguf_fixture import Hy3Block, write_hy3
-from gpu_helpers import clean_status, ctx, dev, errs, rel_err, upload_layer
+from gpu_helpers import clean_status, ctx, dev, errs, moe_term_magnitude, rel_err, upload_layer
 
 pytestmark = pytest.mark.gpu
 
@@ -72,9 +72,10 @@ def test_loaded_layer_equals_registered_layer_and_oracle(tmp_path, H, F, E, k, T
     got = out.cpu().numpy().reshape(T, H)
     ids = routed.cpu().numpy().reshape(T, k, 2)[:, :, 0].astype(np.uint32)
     for t in range(T):
-        o, oid, _ = orc.moe_token(table, b.bias, k, SCALE, x[t])
+        o, oid, oc = orc.moe_token(table, b.bias, k, SCALE, x[t])
         np.testing.assert_array_equal(ids[t], oid)
-        assert rel_err(got[t], o) <= 1e-5
+        mag = moe_term_magnitude(table, oid, oc, x[t])
+        assert rel_err(got[t], o, mag) <= 1e-5, errs(got[t], o, mag)
     loaded.close()
     ref.close()
 

@@ -17,8 +17,8 @@ import torch
 
 import lbk
 import oracle as orc
-from gpu_helpers import (bits, clean_status, ctx, dev, errs, expect_status, host, make_layer_np, rel_err, topk_margins,
-                         upload_layer)
+from gpu_helpers import (bits, clean_status, ctx, dev, errs, expect_status, host, make_layer_np, moe_term_magnitude,
+                         rel_err, topk_margins, upload_layer)
 
 pytestmark = pytest.mark.gpu
 
@@ -37,15 +37,17 @@ def run_forward(layer, xs, mode=lbk.ROUTER_TREE):
 
 
 def oracle_tokens(router, experts, shared, xs, k):
+    """Oracle outputs, routing and (for the tolerance) each output row's term magnitude."""
     table = orc.ExpertTable(experts, shared, router=router, hidden=xs.shape[1])
     E = len(experts)
-    outs, ids, coefs = [], [], []
+    outs, ids, coefs, mags = [], [], [], []
     for x in xs:
         o, i, c = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, x)
         outs.append(o)
         ids.append(i)
         coefs.append(c)
-    return np.stack(outs), np.stack(ids), np.stack(coefs), table
+        mags.append(moe_term_magnitude(table, i, c, x))
+    return np.stack(outs), np.stack(ids), np.stack(coefs), np.stack(mags)
 
 
 @pytest.mark.parametrize("layout", [lbk.LAYOUT_PLANAR, lbk.LAYOUT_GGUF])
@@ -58,10 +60,10 @@ def test_small_layers_match_oracle(H, F, E, k, T, layout):
     assert layer.fused == (layout == lbk.LAYOUT_PLANAR)
     for mode in (lbk.ROUTER_TREE, lbk.ROUTER_SEQUENTIAL):
         out, ids, coefs = run_forward(layer, xs, mode)
-        want, wids, wcoefs, _ = oracle_tokens(router, experts, shared, xs, k)
+        want, wids, wcoefs, mag = oracle_tokens(router, experts, shared, xs, k)
         np.testing.assert_array_equal(ids, wids)
         np.testing.assert_allclose(coefs, wcoefs, rtol=1e-6)
-        assert rel_err(out, want) <= TOL, errs(out, want)
+        assert rel_err(out, want, mag) <= TOL, errs(out, want, mag)
     layer.close()
 
 
@@ -90,12 +92,12 @@ def test_bulk_staged_gate_up_matches_oracle_and_per_expert_path(H, F, E, k, T):
     xs = rng.standard_normal((T, H)).astype(np.float32)
     lp, kp = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
     lg, kg = upload_layer(router, experts, shared, lbk.LAYOUT_GGUF, k)
-    want, wids, wcoefs, _ = oracle_tokens(router, experts, shared, xs, k)
+    want, wids, wcoefs, mag = oracle_tokens(router, experts, shared, xs, k)
     for mode in (lbk.ROUTER_TREE, lbk.ROUTER_SEQUENTIAL):
         out, ids, coefs = run_forward(lp, xs, mode)
         np.testing.assert_array_equal(ids, wids)
         np.testing.assert_allclose(coefs, wcoefs, rtol=1e-6)
-        assert rel_err(out, want) <= TOL, errs(out, want)
+        assert rel_err(out, want, mag) <= TOL, errs(out, want, mag)
         ref, rids, _ = run_forward(lg, xs, mode)
         np.testing.assert_array_equal(ids, rids)
         np.testing.assert_array_equal(bits(out), bits(ref))
@@ -153,6 +155,34 @@ def test_queued_single_token_calls_on_one_workspace(H, F, E, k):
         ids = host(routs[i]).reshape(T, k, 2)[:, :, 0].astype(np.uint32)
         np.testing.assert_array_equal(ids, wids, err_msg=f"call {i}")
         np.testing.assert_array_equal(bits(host(outs[i]).reshape(T, H)), bits(want), err_msg=f"call {i}")
+    layer.close()
+
+
+def test_routing_wait_that_runs_out_reports_timeout():
+    """The down kernel's bounded wait for the single-token routing flag (a
+    wait with no copy in flight) made to run out with a zero poll limit:
+    LBK_TIMEOUT through the status word, the output left unwritten, and the
+    workspace and context still usable for the next call."""
+    rng = np.random.default_rng(15)
+    H, F, E, k = 2048, 512, 16, 4
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    x = rng.standard_normal((1, H)).astype(np.float32)
+    want, wids, _ = run_forward(layer, x)
+    ws = torch.zeros(layer.workspace_bytes(1), dtype=torch.uint8, device="cuda")
+    sentinel = np.full(H, 7.5, np.float32)
+    out = dev(sentinel)
+    layer.set_wait_limit(0)
+    layer.forward(dev(x.reshape(-1)), 1, out, ws)
+    d = expect_status(31)
+    assert d.index == 4
+    np.testing.assert_array_equal(host(out), sentinel)
+    layer.set_wait_limit(1 << 20)
+    for _ in range(2):
+        out2 = torch.full((H,), float("nan"), device="cuda")
+        layer.forward(dev(x.reshape(-1)), 1, out2, ws)
+        clean_status()
+        np.testing.assert_array_equal(bits(host(out2)), bits(want[0]))
     layer.close()
 
 
@@ -215,8 +245,8 @@ def test_non_finite_token_leaves_output_unchanged():
     out2 = torch.zeros(H, device="cuda")
     layer.forward(dev(x), 1, out2, ws)
     clean_status()
-    want, _, _, _ = oracle_tokens(router, experts, shared, x[None], k)
-    assert rel_err(host(out2), want[0]) <= TOL
+    want, _, _, mag = oracle_tokens(router, experts, shared, x[None], k)
+    assert rel_err(host(out2), want[0], mag[0]) <= TOL
     layer.close()
 
 
@@ -229,15 +259,15 @@ def test_config3_layer_single_token():
     xs = rng.standard_normal((2, H)).astype(np.float32)
     layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
     assert layer.fused
-    want, wids, wcoefs, _ = oracle_tokens(router, experts, shared, xs, k)
+    want, wids, wcoefs, mag = oracle_tokens(router, experts, shared, xs, k)
     margins = topk_margins(router, xs, np.zeros(E, np.float32), k)
     print(f"config 3: 8th/9th selection-score margins {margins}")
     for mode in (lbk.ROUTER_TREE, lbk.ROUTER_SEQUENTIAL):
         out, ids, coefs = run_forward(layer, xs, mode)
         np.testing.assert_array_equal(ids, wids)
         np.testing.assert_allclose(coefs, wcoefs, rtol=1e-6)
-        assert rel_err(out, want) <= TOL, errs(out, want)
-        print(f"config 3, router mode {mode}: {errs(out, want)}")
+        assert rel_err(out, want, mag) <= TOL, errs(out, want, mag)
+        print(f"config 3, router mode {mode}: {errs(out, want, mag)}")
     layer.close()
 
 
@@ -264,10 +294,10 @@ def test_checkpoint_types_take_the_fused_kernels(types, H, F, E, k, T):
     lp, kp = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
     lg, kg = upload_layer(router, experts, shared, lbk.LAYOUT_GGUF, k)
     assert lp.fused and not lg.fused
-    want, wids, _, _ = oracle_tokens(router, experts, shared, xs, k)
+    want, wids, _, mag = oracle_tokens(router, experts, shared, xs, k)
     out, ids, _ = run_forward(lp, xs)
     np.testing.assert_array_equal(ids, wids)
-    assert rel_err(out, want) <= TOL, errs(out, want)
+    assert rel_err(out, want, mag) <= TOL, errs(out, want, mag)
     ref, rids, _ = run_forward(lg, xs)
     np.testing.assert_array_equal(bits(out), bits(ref))
     lp.close()

@@ -14,8 +14,8 @@ import torch
 
 import lbk
 import oracle as orc
-from gpu_helpers import (bits, clean_status, dev, errs, expect_status, host, make_layer_np, rel_err, topk_margins,
-                         upload_layer)
+from gpu_helpers import (bits, clean_status, dev, errs, expect_status, host, make_layer_np, moe_term_magnitude, rel_err,
+                         topk_margins, upload_layer)
 
 pytestmark = pytest.mark.gpu
 
@@ -80,9 +80,10 @@ def test_grouped_equals_ungrouped_and_oracle(H, F, E, k, T, types):
         np.testing.assert_array_equal(bits(a), bits(b))
     table = orc.ExpertTable(experts, shared, router=router, hidden=H)
     for t in (0, T // 2, T - 1):  # oracle on a few tokens (seconds each at these sizes)
-        want, wids, _ = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t])
+        want, wids, wc = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t])
         np.testing.assert_array_equal(ia[t], wids)
-        assert rel_err(a[t], want) <= TOL, errs(a[t], want)
+        mag = moe_term_magnitude(table, wids, wc, xs[t])
+        assert rel_err(a[t], want, mag) <= TOL, errs(a[t], want, mag)
     layer.close()
 
 
@@ -105,10 +106,11 @@ def test_config3_shapes_64_tokens():
     print(f"config 4: 8th/9th selection-score margin min {margins.min():.3e}, median {np.median(margins):.3e}")
     worst = 0.0
     for t in range(T):
-        want, wids, _ = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t], preflight=False)
+        want, wids, wc = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xs[t], preflight=False)
         np.testing.assert_array_equal(ia[t], wids, err_msg=f"token {t}")
-        assert rel_err(a[t], want) <= TOL, f"token {t}: " + errs(a[t], want)
-        worst = max(worst, rel_err(a[t], want))
+        mag = moe_term_magnitude(table, wids, wc, xs[t])
+        assert rel_err(a[t], want, mag) <= TOL, f"token {t}: " + errs(a[t], want, mag)
+        worst = max(worst, rel_err(a[t], want, mag))
     print(f"config 4: 64 tokens against the oracle, worst element-wise relative error {worst:.3e}")
     layer.close()
 

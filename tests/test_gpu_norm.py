@@ -16,7 +16,8 @@ import torch
 
 import lbk
 import oracle as orc
-from gpu_helpers import bits, clean_status, ctx, dev, expect_status, host, make_layer_np, errs, rel_err, upload_layer
+from gpu_helpers import (bits, clean_status, ctx, dev, errs, expect_status, host, make_layer_np, moe_term_magnitude,
+                         rel_err, upload_layer)
 
 pytestmark = pytest.mark.gpu
 
@@ -112,10 +113,12 @@ def test_block_forward_matches_oracle(mode, H, F, E, k, T):
     table = orc.ExpertTable(experts, shared, router=router, hidden=H)
     want = hidden.copy()
     want_ids = []
+    mag = np.abs(hidden).astype(np.float64)
     for t in range(T):
         xn = orc.rms_norm(hidden[t], norm_w, eps)
-        delta, ids, _ = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xn)
+        delta, ids, coefs = orc.moe_token(table, np.zeros(E, np.float32), k, 2.826, xn)
         want_ids.append(ids)
+        mag[t] += moe_term_magnitude(table, ids, coefs, xn)
         assert orc.residual_add_status(want[t], delta) == 0
     hd = dev(hidden.reshape(-1))
     ws = torch.zeros(layer.block_workspace_bytes(T), dtype=torch.uint8, device="cuda")
@@ -125,7 +128,7 @@ def test_block_forward_matches_oracle(mode, H, F, E, k, T):
     got = host(hd).reshape(T, H)
     ids = host(routed).reshape(T, k, 2)[:, :, 0].astype(np.uint32)
     np.testing.assert_array_equal(ids, np.stack(want_ids))
-    assert rel_err(got, want) <= TOL, errs(got, want)
+    assert rel_err(got, want, mag) <= TOL, errs(got, want, mag)
     layer.close()
 
 
@@ -140,5 +143,76 @@ def test_block_forward_leaves_hidden_untouched_on_error():
     ws = torch.zeros(layer.block_workspace_bytes(2), dtype=torch.uint8, device="cuda")
     layer.block_forward(hd, dev(np.ones(H, np.float32)), 1e-6, 2, ws)
     assert expect_status(12).index == 17
+    np.testing.assert_array_equal(bits(host(hd)), bits(hidden.reshape(-1)))
+    layer.close()
+
+
+@pytest.mark.parametrize("mode", [lbk.ROUTER_SEQUENTIAL, lbk.ROUTER_TREE])
+@pytest.mark.parametrize("H,F,E,k,T", [(2048, 512, 16, 4, 1), (2048, 512, 16, 4, 3)])
+def test_route_then_finish_equals_block_forward(mode, H, F, E, k, T):
+    """hy3_moe_route_token then hy3_moe_finish_token with the routing the
+    route phase returned: bit for bit the one-call block."""
+    rng = np.random.default_rng(H + E + T + 7 * mode)
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    hidden = (rng.standard_normal((T, H)) * 2).astype(np.float32)
+    norm_w = (rng.random(H) * 2).astype(np.float32)
+    nw = dev(norm_w)
+    ws = torch.zeros(layer.block_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    one = dev(hidden.reshape(-1))
+    r1 = torch.zeros(T * k * 2, dtype=torch.int32, device="cuda")
+    layer.block_forward(one, nw, 1e-6, T, ws, routed_out=r1, router_mode=mode)
+    clean_status()
+    two = dev(hidden.reshape(-1))
+    ws2 = torch.zeros(layer.block_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    r2 = torch.zeros(T * k * 2, dtype=torch.int32, device="cuda")
+    layer.block_route(two, nw, 1e-6, T, ws2, routed_out=r2, router_mode=mode)
+    clean_status()
+    np.testing.assert_array_equal(host(r2), host(r1))
+    np.testing.assert_array_equal(bits(host(two)), bits(hidden.reshape(-1)))  # route leaves hidden alone
+    layer.block_finish(two, T, r2, ws2)
+    clean_status()
+    np.testing.assert_array_equal(bits(host(two)), bits(host(one)))
+    layer.close()
+
+
+def test_finish_refuses_routing_that_differs_in_one_bit():
+    """layer.rs:631-640: supplied IDs and coefficient bits must equal the
+    route phase's routing; otherwise InvalidParameter and hidden untouched."""
+    rng = np.random.default_rng(41)
+    H, F, E, k, T = 2048, 512, 16, 4, 2
+    router, experts, shared = make_layer_np(rng, H, F, E)
+    layer, keep = upload_layer(router, experts, shared, lbk.LAYOUT_PLANAR, k)
+    hidden = rng.standard_normal((T, H)).astype(np.float32)
+    nw = dev(np.ones(H, np.float32))
+    ws = torch.zeros(layer.block_workspace_bytes(T), dtype=torch.uint8, device="cuda")
+    hd = dev(hidden.reshape(-1))
+    r = torch.zeros(T * k * 2, dtype=torch.int32, device="cuda")
+    # a finish without a route, and two routes in a row: host errors before any launch
+    with pytest.raises(lbk.LbkError) as e:
+        layer.block_finish(hd, T, r, ws)
+    assert e.value.status == 15
+    layer.block_route(hd, nw, 1e-6, T, ws, routed_out=r)
+    with pytest.raises(lbk.LbkError) as e:
+        layer.block_route(hd, nw, 1e-6, T, ws, routed_out=r)
+    assert e.value.status == 15
+    with pytest.raises(lbk.LbkError) as e:
+        layer.block_finish(hd, T - 1, r, ws)
+    assert e.value.status == 10
+    clean_status()
+    routed = host(r).copy()
+    bad = routed.copy()
+    bad[2 * (k + 1) + 1] ^= 1  # token 1, slot 1: coefficient's last bit
+    layer.block_finish(hd, T, dev(bad), ws)
+    d = expect_status(15)
+    assert d.index == k + 1
+    np.testing.assert_array_equal(bits(host(hd)), bits(hidden.reshape(-1)))
+    # the phase ended with that finish: route again, then the matching finish
+    layer.block_route(hd, nw, 1e-6, T, ws, routed_out=r)
+    clean_status()
+    bad = host(r).copy()
+    bad[0] = (bad[0] + 1) % E  # token 0, slot 0: another expert ID
+    layer.block_finish(hd, T, dev(bad), ws)
+    expect_status(15)
     np.testing.assert_array_equal(bits(host(hd)), bits(hidden.reshape(-1)))
     layer.close()

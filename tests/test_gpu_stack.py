@@ -6,12 +6,20 @@ residual_add_in_place: bridge-kernels-reference/src/norm.rs:5-18, :83-100;
 bridge-model-hy3/src/routing.rs:25-107; moe.rs:64-147), mirroring the layer
 loop of bridge-runtime/src/hy3_scalar.rs:504-650 with attention omitted.
 
-The two chains run independently (the oracle's hidden state never takes the
-device's values), so any difference accumulates as it would over a stack.
+Two chains. In the benched mode (tree-order F32 sums in the RMSNorm and the
+router logits, each within rounding of the reference's sequential chain) every
+layer is checked on the stack's own trajectory: the device's normalized input
+(the block workspace's first region) against the oracle's RMSNorm of the same
+hidden state, then the oracle's MoE step on that normalized input plus the
+residual against the device's output. A last-bit difference in a normalized
+input can move a Q8_K rounding by one step, which no f32 bar can hold, so the
+MoE step is compared on the input it actually saw. With sequential order the
+arithmetic is the reference's own, so the two chains run independently over
+the whole depth (the oracle's hidden state never takes the device's values).
 Layers are generated on the device (seeded torch generator, seed 4 + layer as
 in config 5), repacked to the planar layout there, and their GGUF bytes copied
 to the host for the oracle. Bars per layer and token: top-8 IDs identical,
-hidden state within 1e-5 element-wise relative (tests/gpu_helpers.REL_FLOOR).
+hidden state within 1e-5 element-wise relative (tests/gpu_helpers.rel_err).
 """
 
 import numpy as np
@@ -21,7 +29,7 @@ import torch
 import lbk
 import oracle as orc
 import synth
-from gpu_helpers import clean_status, ctx, errs, host, rel_err
+from gpu_helpers import clean_status, ctx, errs, host, moe_term_magnitude, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -89,8 +97,9 @@ def stack():
         layer.close()
 
 
+@pytest.mark.parametrize("mode", [lbk.ROUTER_TREE, lbk.ROUTER_SEQUENTIAL])
 @pytest.mark.parametrize("batch", [1, 4])
-def test_chained_stack_matches_oracle(stack, batch):
+def test_chained_stack_matches_oracle(stack, batch, mode):
     rng = np.random.default_rng(300 + batch)
     hidden0 = rng.standard_normal((batch, H)).astype(np.float32)
     hd = torch.from_numpy(hidden0.reshape(-1).copy()).cuda()
@@ -98,15 +107,27 @@ def test_chained_stack_matches_oracle(stack, batch):
     ws = torch.zeros(stack[0][0].block_workspace_bytes(batch), dtype=torch.uint8, device="cuda")
     zero_bias = np.zeros(E, np.float32)
     for li, (layer, table, norm_w, norm_host, _, _) in enumerate(stack):
+        before = host(hd).reshape(batch, H)
         routed = torch.zeros(batch * K * 2, dtype=torch.int32, device="cuda")
-        layer.block_forward(hd, norm_w, EPS, batch, ws, routed_out=routed, router_mode=lbk.ROUTER_TREE)
+        layer.block_forward(hd, norm_w, EPS, batch, ws, routed_out=routed, router_mode=mode)
         clean_status()
         got = host(hd).reshape(batch, H)
         ids = host(routed).reshape(batch, K, 2)[:, :, 0].astype(np.uint32)
+        mag = None
+        if mode == lbk.ROUTER_TREE:
+            want = before.copy()
+            xn_dev = host(ws[:batch * H * 4].view(torch.float32)).reshape(batch, H)
+            mag = np.abs(before).astype(np.float64)
         for t in range(batch):
             xn = orc.rms_norm(want[t], norm_host, EPS)
-            delta, wids, _ = orc.moe_token(table, zero_bias, K, WEIGHT_SCALE, xn)
+            if mode == lbk.ROUTER_TREE:
+                assert rel_err(xn_dev[t], xn) <= TOL, f"layer {li} token {t} norm: " + errs(xn_dev[t], xn)
+                xn = xn_dev[t]
+            delta, wids, wc = orc.moe_token(table, zero_bias, K, WEIGHT_SCALE, xn)
             np.testing.assert_array_equal(ids[t], wids, err_msg=f"layer {li} token {t}")
+            if mag is not None:
+                mag[t] += moe_term_magnitude(table, wids, wc, xn)
             assert orc.residual_add_status(want[t], delta) == 0
-        assert rel_err(got, want) <= TOL, f"layer {li}: " + errs(got, want)
-        print(f"batch {batch} layer {li}: {errs(got, want)}")
+        assert rel_err(got, want, mag) <= TOL, f"layer {li}: " + errs(got, want, mag)
+        differ = int(np.count_nonzero(got.view(np.uint32) != want.view(np.uint32)))
+        print(f"batch {batch} mode {mode} layer {li}: {errs(got, want, mag)}, {differ} of {got.size} values differ in bits")
