@@ -224,6 +224,17 @@ int32_t lbk_route_topk(lbk_context* ctx, const float* logits, const float* selec
                        uint64_t expert_count, uint64_t tokens, uint32_t k, float weight_scale,
                        lbk_routed* routed, void* stream);
 
+/* f32 decode of rows [first_row, first_row + rows) of a packed matrix in the
+ * GGUF layout into out[rows * input_width], bit-identical to the reference:
+ * decode_row_into (bridge-quant-layout/src/k_quants.rs:71-105) per row over
+ * the block decoders (k_quants.rs:242-300, iq2_s.rs:9-39, iq3_s.rs:9-53;
+ * F32 rows are copied bit for bit). Every d / dmin of the range is checked
+ * first: a non-finite one is reported through the status word
+ * (LBK_NON_FINITE_SCALE, index = block within the range) and nothing is
+ * written. A planar matrix is refused (lbk_unpack converts it). */
+int32_t lbk_decode_rows(lbk_context* ctx, const lbk_matrix* w, uint64_t first_row, uint64_t rows, float* out,
+                        void* stream);
+
 /* SwiGLU expert, accumulated: dst += coefficient * down(swiglu(gate x, up x)).
  * reference: expert_swiglu_accumulate_into, activation.rs:104-144.
  * Workspace: lbk_expert_workspace_bytes. */

@@ -1744,6 +1744,33 @@ LBK_API int32_t lbk_unpack(lbk_context* ctx, const lbk_matrix* src_planar, void*
     return repack_common(ctx, src_planar, dst_gguf, dst_bytes, LBK_LAYOUT_PLANAR, 0, stream);
 }
 
+LBK_API int32_t lbk_decode_rows(lbk_context* ctx, const lbk_matrix* w, uint64_t first_row, uint64_t rows, float* out,
+                                void* stream) {
+    if (int32_t s = check_matrix(w, "matrix")) return s;
+    if (w->type != LBK_TYPE_F32 && !dot_type(w->type)) return fail(LBK_UNSUPPORTED_TYPE, "decode type", (uint64_t)w->type);
+    if (w->layout != LBK_LAYOUT_GGUF)
+        return fail(LBK_INVALID_PARAMETER, "decode takes the GGUF layout (lbk_unpack converts a planar matrix)");
+    if (rows == 0) return fail(LBK_DIMENSION_MISMATCH, "decoded rows", 0, 1, 0);
+    if (first_row > w->output_width || rows > w->output_width - first_row)
+        return fail(LBK_DIMENSION_MISMATCH, "decoded row range", 0, w->output_width, first_row + rows);
+    if (ctx == nullptr || out == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    const uint64_t nb = w->input_width / LBK_QK_K;
+    const uint64_t row_bytes = w->type == LBK_TYPE_F32 ? w->input_width * 4 : nb * block_bytes(w->type);
+    const uint8_t* data = static_cast<const uint8_t*>(w->data) + first_row * row_bytes;
+    cudaError_t e;
+    if (w->type == LBK_TYPE_F32) {  // decode_f32_validated: the bits, unchanged
+        e = cudaMemcpyAsync(out, data, rows * row_bytes, cudaMemcpyDeviceToDevice, st);
+        return e == cudaSuccess ? ok() : cuda_fail(e, "f32 row copy");
+    }
+    e = lbk::launch_validate_scales(w->type, LBK_LAYOUT_GGUF, data, rows, (int)nb, ctx->scratch_min, ctx->status, st);
+    if (e != cudaSuccess) return cuda_fail(e, "scale scan launch");
+    lbk::DecodeArgs a{w->type, data, rows, (int)nb, out, ctx->iq2s, ctx->iq3s, ctx->status};
+    e = lbk::launch_decode(a, ctx->sm_count, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "decode launch");
+}
+
 LBK_API int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void* stream) {
     if (int32_t s = check_matrix(w, "matrix")) return s;
     if (!dot_type(w->type)) return fail(LBK_UNSUPPORTED_TYPE, "only packed types carry binary16 scales", (uint64_t)w->type);

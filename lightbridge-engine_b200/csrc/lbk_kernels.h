@@ -120,6 +120,18 @@ struct RepackArgs {
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t stream);
 cudaError_t launch_build_tables(const uint64_t* iq2s, const uint32_t* iq3s, uint32_t* iq2_img, uint32_t* iq3_img,
                                 uint32_t* sign_img, uint32_t* sel_img, cudaStream_t stream);
+// f32 decode of `rows` consecutive GGUF rows of nb blocks (decode.cu)
+struct DecodeArgs {
+    int type;                 // Q4_K, Q5_K, IQ2_S or IQ3_S
+    const uint8_t* data;      // the range's first row
+    uint64_t rows;
+    int nb;
+    float* out;               // rows * nb * 256
+    const uint64_t* iq2s;     // IQ2S_GRID
+    const uint32_t* iq3s;     // IQ3S_GRID
+    DeviceStatus* status;
+};
+cudaError_t launch_decode(const DecodeArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_validate_scales(int type, int layout, const uint8_t* data, uint64_t rows, int nb,
                                    unsigned long long* scratch_min, DeviceStatus* status, cudaStream_t stream);
 

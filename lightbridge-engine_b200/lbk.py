@@ -197,6 +197,7 @@ def _load() -> ctypes.CDLL:
         "lbk_repack": ([P, PM, P, U64, P], I32),
         "lbk_unpack": ([P, PM, P, U64, P], I32),
         "lbk_validate_matrix": ([P, PM, P], I32),
+        "lbk_decode_rows": ([P, PM, U64, U64, P, P], I32),
         "lbk_gguf_default_limits": ([ctypes.POINTER(GgufLimits)], None),
         "lbk_gguf_open": ([ctypes.c_char_p, ctypes.POINTER(GgufLimits), ctypes.POINTER(P)], I32),
         "lbk_gguf_close": ([P], I32),
@@ -224,7 +225,7 @@ EXPORTED = (
     "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward lbk_moe_block_route lbk_moe_block_finish "
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine "
-    "lbk_repack lbk_unpack lbk_validate_matrix "
+    "lbk_repack lbk_unpack lbk_validate_matrix lbk_decode_rows "
     "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
     "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
 ).split()
@@ -335,6 +336,10 @@ class Context:
 
     def unpack(self, m: Matrix, dst, stream=None) -> None:
         check(lib.lbk_unpack(self.ptr, ctypes.byref(m), _ptr(dst), dst.numel(), _stream(stream)))
+
+    def decode_rows(self, m: Matrix, first_row: int, rows: int, out, stream=None) -> None:
+        """decode_row_into (k_quants.rs:71-105) over a run of rows, into f32."""
+        check(lib.lbk_decode_rows(self.ptr, ctypes.byref(m), first_row, rows, _ptr(out), _stream(stream)))
 
     def validate_matrix(self, m: Matrix, stream=None) -> None:
         check(lib.lbk_validate_matrix(self.ptr, ctypes.byref(m), _stream(stream)))

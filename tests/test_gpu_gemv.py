@@ -134,3 +134,39 @@ def test_repack_matches_numpy_and_unpack_inverts(ty, k):
     clean_status()
     np.testing.assert_array_equal(host(planar), synth.planar_np(ty, w, k))  # pad bytes zeroed too
     np.testing.assert_array_equal(host(back), w)
+
+
+@pytest.mark.parametrize("layout", [lbk.LAYOUT_GGUF, lbk.LAYOUT_PLANAR])
+@pytest.mark.parametrize("H,F,gty,dty", [(4096, 1536, 22, 21), (2048, 512, 12, 12), (1024, 768, 22, 13)])
+def test_expert_swiglu_accumulate_matches_oracle(H, F, gty, dty, layout):
+    """expert_swiglu_accumulate_into (bridge-kernels-reference/src/activation.rs:104-144):
+    dst += coef * down(swiglu(gate x, up x)), against the oracle's gemv_into ->
+    apply_swiglu -> gemv_accumulate_scaled_into chain; bit for bit up to the
+    exp of the SwiGLU (unpinned), held to 1e-5 relative element-wise."""
+    rng = np.random.default_rng(H + F + gty + dty + layout)
+    g = synth.packed_np(rng, gty, H, F)
+    u = synth.packed_np(rng, gty, H, F)
+    d = synth.packed_np(rng, dty, F, H)
+    x = rng.standard_normal(H).astype(np.float32)
+    dst0 = rng.standard_normal(H).astype(np.float32)
+    coef = np.float32(-0.8125)
+    gv, _ = orc.gemv(gty, H, F, g, x)
+    uv, _ = orc.gemv(gty, H, F, u, x)
+    hv = orc.swiglu(gv, uv)
+    want = orc.gemv_accumulate_scaled(dty, F, H, d, hv, dst0.copy(), coef)
+
+    def up(ty, b, in_w):
+        return planar_dev(ty, b, in_w) if layout == lbk.LAYOUT_PLANAR else dev(b)
+
+    keep = [up(gty, g, H), up(gty, u, H), up(dty, d, F)]
+    e = lbk.Expert(matrix(gty, H, F, keep[0], layout), matrix(gty, H, F, keep[1], layout),
+                   matrix(dty, F, H, keep[2], layout))
+    ws = torch.zeros(ctx().expert_workspace_bytes(e), dtype=torch.uint8, device="cuda")
+    dst = dev(dst0)
+    ctx().expert_swiglu_accumulate(e, dev(x), dst, float(coef), ws)
+    clean_status()
+    got = host(dst)
+    err = float(np.max(np.abs(got.astype(np.float64) - want) / np.maximum(np.abs(want), 1e-3 * np.abs(want).max())))
+    assert err <= 1e-5, err
+    print(f"expert SwiGLU accumulate H={H} F={F}: element-wise {err:.3e}, "
+          f"{int(np.count_nonzero(got.view(np.uint32) != want.view(np.uint32)))} of {H} values differ in bits")
