@@ -35,11 +35,8 @@ struct lbk_context {
     uint32_t* iq3s;                     // device, 512
     uint32_t* img_iq2;                  // replicated shared-memory images
     uint32_t* img_iq3;
-    uint32_t* img_sign;
-    uint32_t* img_sel;
     lbk::Tables tables() const {
-        return lbk::Tables{reinterpret_cast<const uint4*>(img_iq2), reinterpret_cast<const uint4*>(img_iq3),
-                           reinterpret_cast<const uint4*>(img_sign), reinterpret_cast<const uint4*>(img_sel)};
+        return lbk::Tables{reinterpret_cast<const uint4*>(img_iq2), reinterpret_cast<const uint4*>(img_iq3)};
     }
 };
 
@@ -343,10 +340,10 @@ LBK_API int32_t lbk_context_create(int32_t device, lbk_context** out) {
     c->sm_count = prop.multiProcessorCount;
     void* p = nullptr;
     // [status 32 B][scratch_min 8 B .. 256][iq2s grid 8 KB][iq3s grid 2 KB]
-    // [IQ2 code image 128 KB][IQ3 grid image 64 KB][sign image 32 KB][sign-select image 32 KB]
+    // [IQ2 code image 128 KB][IQ3 grid image 64 KB]
     static_assert(sizeof(lbk::DeviceStatus) <= 32, "status word layout");
     const size_t img_off = 256 + sizeof(lbk_iq2s_grid) + sizeof(lbk_iq3s_grid);
-    const size_t total = img_off + lbk::kIq2CodeBytes + lbk::kIq3GridBytes + 2 * lbk::kSignBytes;
+    const size_t total = img_off + lbk::kIq2CodeBytes + lbk::kIq3GridBytes;
     if ((e = cudaMalloc(&p, total)) != cudaSuccess) {
         delete c;
         return cuda_fail(e, "cudaMalloc context");
@@ -358,13 +355,10 @@ LBK_API int32_t lbk_context_create(int32_t device, lbk_context** out) {
     c->iq3s = reinterpret_cast<uint32_t*>(base + 256 + sizeof(lbk_iq2s_grid));
     c->img_iq2 = reinterpret_cast<uint32_t*>(base + img_off);
     c->img_iq3 = reinterpret_cast<uint32_t*>(base + img_off + lbk::kIq2CodeBytes);
-    c->img_sign = reinterpret_cast<uint32_t*>(base + img_off + lbk::kIq2CodeBytes + lbk::kIq3GridBytes);
-    c->img_sel = c->img_sign + lbk::kSignBytes / 4;
     e = cudaMemset(base, 0, 256);
     if (e == cudaSuccess) e = cudaMemcpy(c->iq2s, lbk_iq2s_grid, sizeof(lbk_iq2s_grid), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(c->iq3s, lbk_iq3s_grid, sizeof(lbk_iq3s_grid), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = lbk::launch_build_tables(c->iq2s, c->iq3s, c->img_iq2, c->img_iq3, c->img_sign,
-                                                    c->img_sel, nullptr);
+    if (e == cudaSuccess) e = lbk::launch_build_tables(c->iq2s, c->iq3s, c->img_iq2, c->img_iq3, nullptr);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaFree(p);

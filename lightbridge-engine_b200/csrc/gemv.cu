@@ -25,7 +25,7 @@ struct GemvCfg {
     static constexpr bool kIq = (T == LBK_TYPE_IQ2_S || T == LBK_TYPE_IQ3_S);
     static constexpr int kTail = TypeInfo<T>::kTail;
     static constexpr int kTableBytes =
-        T == LBK_TYPE_IQ2_S ? (kIq2CodeBytes + kSignBytes) : (T == LBK_TYPE_IQ3_S ? (kIq3GridBytes + kSignBytes) : 0);
+        T == LBK_TYPE_IQ2_S ? kIq2CodeBytes : (T == LBK_TYPE_IQ3_S ? kIq3GridBytes : 0);
 };
 
 template <int T>
@@ -156,7 +156,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int nb = a.w.nb;
     uint32_t* tab0 = reinterpret_cast<uint32_t*>(smem);
-    uint32_t* tab1 = reinterpret_cast<uint32_t*>(smem + (T == LBK_TYPE_IQ2_S ? kIq2CodeBytes : kIq3GridBytes));
     int8_t* qs = reinterpret_cast<int8_t*>(smem + Cfg::kTableBytes);
     float* dsm = reinterpret_cast<float*>(qs + (size_t)nb * kQK);
     int16_t* bs = reinterpret_cast<int16_t*>(dsm + nb);
@@ -186,13 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     const bool single = (nhb <= tpr);  // each thread owns at most one half block
     if (single && step < steps && row_of(step) < rows && hb0 < nhb) load_hb<L>(cur, a.w, row_of(step), hb0 >> 1, hb0 & 1);
 
-    if (T == LBK_TYPE_IQ2_S) {
-        fill_iq2_codes(tab0, a.tables);
-        fill_signs(tab1, a.tables);
-    } else if (T == LBK_TYPE_IQ3_S) {
-        fill_iq3_grid(tab0, a.tables);
-        fill_sign_sel(tab1, a.tables);
-    }
+    if (T == LBK_TYPE_IQ2_S) fill_iq2_codes(tab0, a.tables);
+    else if (T == LBK_TYPE_IQ3_S) fill_iq3_grid(tab0, a.tables);
     if (!stage_activations(a, nb, qs, dsm, bs, flag)) return;
 
     ActSmem as{qs, dsm, bs};
@@ -207,7 +201,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
         }
     }
     const uint32_t t0 = (uint32_t)__cvta_generic_to_shared(tab0 + lane);
-    const uint32_t t1 = (uint32_t)__cvta_generic_to_shared(tab1 + lane);
 
     const int slots = a.tail_slots;  // >= rps, multiple of rps
     auto flush = [&](int nslots, uint64_t first_step) {
@@ -257,9 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
                 IqPart p{0, 0};
                 if (mine) {
                     if constexpr (T == LBK_TYPE_IQ2_S)
-                        p = dot_hb(w, act, t0, t1);
+                        p = dot_hb(w, act, t0);
                     else
-                        p = dot_hb(w, act, nact, t0, t1);
+                        p = dot_hb(w, act, nact, t0);
                 }
                 int other = __shfl_xor_sync(0xffffffffu, p.sum, 1);
                 if (mine && h == 0) {

@@ -213,6 +213,37 @@ __host__ __device__ __forceinline__ uint32_t qh_transpose(uint32_t w) {
     return w;
 }
 
+// Sign words of the planar IQ2_S / IQ3_S layout. A GGUF sign word holds the
+// sign bytes of a group's four 8-lane subgroups (bit 8l + i: subgroup l, lane
+// i); the planar layout stores it transposed (bit 4i + l), so that the signs
+// of subgroup l sit one nibble apart: a shift and a mask put them where the
+// decoders need them, with no lookup. Four delta swaps rotate the five
+// bit-index bits (p4 p3 p2 p1 p0 -> p2 p1 p0 p4 p3); sign_untranspose applies
+// them in reverse order.
+__host__ __device__ __forceinline__ uint32_t delta_swap(uint32_t w, uint32_t mask, int d) {
+    const uint32_t t = ((w >> d) ^ w) & mask;
+    return w ^ t ^ (t << d);
+}
+__host__ __device__ __forceinline__ uint32_t sign_transpose(uint32_t w) {
+    w = delta_swap(w, 0x22222222u, 1);
+    w = delta_swap(w, 0x0c0c0c0cu, 2);
+    w = delta_swap(w, 0x00aa00aau, 7);
+    return delta_swap(w, 0x0000ccccu, 14);
+}
+__host__ __device__ __forceinline__ uint32_t sign_untranspose(uint32_t w) {
+    w = delta_swap(w, 0x0000ccccu, 14);
+    w = delta_swap(w, 0x00aa00aau, 7);
+    w = delta_swap(w, 0x0c0c0c0cu, 2);
+    return delta_swap(w, 0x22222222u, 1);
+}
+// The signs of subgroup L of a transposed sign word at bit 4i + 2 (lane i),
+// other bits unspecified: a shift by 2 - L.
+template <int L>
+__device__ __forceinline__ uint32_t signs_at2(uint32_t sgt) {
+    if constexpr (L <= 2) return sgt << (2 - L);
+    else return sgt >> (L - 2);
+}
+
 // 4x4 byte transpose: out[k] byte i = in[i] byte k.
 __device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t& o0,
                                            uint32_t& o1, uint32_t& o2, uint32_t& o3) {
@@ -234,43 +265,22 @@ __device__ __forceinline__ void transpose4(uint32_t a, uint32_t b, uint32_t c, u
 
 constexpr int kIq2CodeEntries = 1024;  // IQ2_S grid as 8 code nibbles (0,1,2 = 8,25,43)
 constexpr int kIq3GridEntries = 512;   // IQ3_S grid magnitudes, 4 bytes
-constexpr int kSignEntries = 256;      // sign byte -> bit 2 of nibble i set iff bit i set
 
 constexpr int kIq2CodeBytes = kIq2CodeEntries * 32 * 4;  // 128 KiB
 constexpr int kIq3GridBytes = kIq3GridEntries * 32 * 4;  // 64 KiB
-constexpr int kSignBytes = kSignEntries * 32 * 4;        // 32 KiB
 
 // Replicated table images in global memory, built once per context from the
 // codebooks of lbk_iq_tables.h (build_table_images). A kernel copies the
-// images it needs into shared memory with 16-byte loads.
+// images it needs into shared memory. (The signs need no table: see
+// sign_transpose.)
 struct Tables {
     const uint4* iq2_codes;  // kIq2CodeBytes
     const uint4* iq3_grid;   // kIq3GridBytes
-    const uint4* signs;      // kSignBytes: IQ2_S selector sign bits
-    const uint4* sign_sel;   // kSignBytes: IQ3_S activation selectors (see sign_select)
 };
-
-// IQ3_S activation selector for a sign byte: low half selects lanes 0-3 of
-// {a, -a} by sign bits 0-3, high half lanes 0-3 by sign bits 4-7.
-__host__ __device__ __forceinline__ uint32_t sign_select(uint32_t s) {
-    uint32_t lo = 0x3210u, hi = 0x3210u;
-    for (int i = 0; i < 4; i++) {
-        lo |= ((s >> i) & 1u) << (4 * i + 2);
-        hi |= ((s >> (i + 4)) & 1u) << (4 * i + 2);
-    }
-    return lo | (hi << 16);
-}
 
 __device__ __forceinline__ void copy_table(uint32_t* dst, const uint4* src, int bytes) {
     uint4* d = reinterpret_cast<uint4*>(dst);
     for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = __ldg(src + i);
-}
-
-__device__ __forceinline__ uint32_t sign_spread(uint32_t s) {
-    uint32_t v = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) v |= ((s >> i) & 1u) << (4 * i + 2);
-    return v;
 }
 
 __device__ __forceinline__ uint32_t iq2_code_of(uint64_t g) {
@@ -287,8 +297,6 @@ __device__ __forceinline__ uint32_t iq2_code_of(uint64_t g) {
 // Copies the replicated images into shared memory; all threads participate.
 __device__ __forceinline__ void fill_iq2_codes(uint32_t* tab, const Tables& t) { copy_table(tab, t.iq2_codes, kIq2CodeBytes); }
 __device__ __forceinline__ void fill_iq3_grid(uint32_t* tab, const Tables& t) { copy_table(tab, t.iq3_grid, kIq3GridBytes); }
-__device__ __forceinline__ void fill_signs(uint32_t* tab, const Tables& t) { copy_table(tab, t.signs, kSignBytes); }
-__device__ __forceinline__ void fill_sign_sel(uint32_t* tab, const Tables& t) { copy_table(tab, t.sign_sel, kSignBytes); }
 
 // Pools for IQ2_S signed-grid expansion through byte permutes: selector
 // nibble c in {0,1,2} picks +8/+25/+43, c+4 picks the negated value.
@@ -503,6 +511,7 @@ __device__ __forceinline__ void load_hb(Iq2HB& o, const MatrixRef& m, uint64_t r
         o.d = ldw_u16(p);
         o.qs = ldw_u128_a2(p + 2 + 16 * h);
         o.sg = ldw_u128_a2(p + 34 + 16 * h);
+        o.sg = make_uint4(sign_transpose(o.sg.x), sign_transpose(o.sg.y), sign_transpose(o.sg.z), sign_transpose(o.sg.w));
         o.qh = qh_transpose(ldw_u32_a2(p + 66 + 4 * h));
         o.sc = ldw_u32_a2(p + 74 + 4 * h);
     }
@@ -527,6 +536,7 @@ __device__ __forceinline__ void load_hb(Iq3HB& o, const MatrixRef& m, uint64_t r
         o.qs1 = ldw_u128_a2(p + 2 + 32 * h + 16);
         o.qh = qh_transpose(ldw_u32_a2(p + 66 + 4 * h));
         o.sg = ldw_u128_a2(p + 74 + 16 * h);
+        o.sg = make_uint4(sign_transpose(o.sg.x), sign_transpose(o.sg.y), sign_transpose(o.sg.z), sign_transpose(o.sg.w));
         o.sc = ldw_u16(p + 106 + 2 * h);
     }
 }
@@ -706,19 +716,17 @@ struct KPart {
 __host__ __device__ constexpr uint32_t sel_idx(int lo, int hi) {
     return (uint32_t)(lo | ((4 + hi) << 4) | ((0xC + hi) << 8) | ((0xC + hi) << 12));
 }
-// [byte `lo` of a, 0, 0, 0] (zeros from b's non-negative byte `z`)
-__host__ __device__ constexpr uint32_t sel_byte(int lo, int z) {
-    return (uint32_t)(lo | ((0xC + z) << 4) | ((0xC + z) << 8) | ((0xC + z) << 12));
-}
 
 // dot_iq2_s (q8_k.rs:339-364) over groups 4h..4h+3 of one block.
-// code_base / sign_base are shared-window addresses of this lane's copy of
-// the replicated tables (entry e at base + 128 e). The qh word is the
+// code_base is the shared-window address of this lane's copy of the
+// replicated code table (entry e at base + 128 e). The qh word is the
 // bit-transposed one (qh_transpose): byte l, bits 2g..2g+1 = high index bits
-// of subgroup l of group g. Per subgroup of 8 lanes: one permute builds the
-// 10-bit index, one multiply-add its table address; the code nibbles plus
-// the sign bits select signed grid bytes from a byte pool.
-__device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, uint32_t code_base, uint32_t sign_base) {
+// of subgroup l of group g; the sign words are transposed too
+// (sign_transpose). Per subgroup of 8 lanes: one permute builds the 10-bit
+// index, one multiply-add its table address; the code nibbles plus the sign
+// bits (shifted to bit 2 of each nibble) select signed grid bytes from a byte
+// pool.
+__device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, uint32_t code_base) {
     int32_t total = 0;
     const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;          // 1 + 2*(scale & 15), four groups
     const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;   // 1 + 2*(scale >> 4)
@@ -727,14 +735,13 @@ __device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, uint32_
         const uint32_t qsw = w32(w.qs, gi);
         const uint32_t sgw = w32(w.sg, gi);
         const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;  // byte l: high index bits of subgroup l
+        const uint32_t sp[4] = {signs_at2<0>(sgw), signs_at2<1>(sgw), signs_at2<2>(sgw), signs_at2<3>(sgw)};
         int32_t part0 = 0, part1 = 0;
 #pragma unroll
         for (int l = 0; l < 4; l++) {
             const uint32_t idx = prmt(qsw, Q, sel_idx(l, l));
             const uint32_t code = lds32(idx * 128u + code_base);
-            const uint32_t sb = prmt(sgw, Q, sel_byte(l, l));
-            const uint32_t sp = lds32(sb * 128u + sign_base);
-            const uint32_t sel = code | sp;
+            const uint32_t sel = code | (sp[l] & 0x44444444u);
             const uint32_t g0 = prmt(kIq2PoolPos, kIq2PoolNeg, sel);
             const uint32_t g1 = prmt(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
             if (l < 2) {
@@ -757,11 +764,11 @@ __device__ __forceinline__ IqPart dot_hb(const Iq2HB& w, const ActHB& a, uint32_
 
 // dot_iq3_s (q8_k.rs:380-428) over groups 4h..4h+3 of one block. The signs
 // are applied to the activations: na holds the negated activation words and
-// a byte permute picks a or -a per lane, its selector read from the
-// sign-select table. qh is bit-transposed as for IQ2_S: bit 0 of byte l
-// holds the high bit of the first index of subgroup l, bit 1 of the second.
-__device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const uint32_t* na, uint32_t grid_base,
-                                         uint32_t sel_base) {
+// a byte permute picks a or -a per lane, its selector (3210 plus bit 2 of
+// each nibble from the transposed sign word) built by a shift and a mask.
+// qh is bit-transposed as for IQ2_S: bit 0 of byte l holds the high bit of
+// the first index of subgroup l, bit 1 of the second.
+__device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const uint32_t* na, uint32_t grid_base) {
     int32_t total = 0;
     // pair scales: bytes [lo0, lo1, hi0, hi1] -> 1 + 2*nibble; group gi uses byte {0,2,1,3}[gi]
     const uint32_t st = (w.sc & 0x0f0fu) | ((w.sc & 0xf0f0u) << 12);
@@ -774,6 +781,7 @@ __device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const u
         const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
         const uint32_t Q1 = Q & 0x01010101u;          // high bit of the first index
         const uint32_t Q2 = (Q >> 1) & 0x01010101u;   // high bit of the second index
+        const uint32_t sp[4] = {signs_at2<0>(sgw), signs_at2<1>(sgw), signs_at2<2>(sgw), signs_at2<3>(sgw)};
         int32_t gsum = 0;
 #pragma unroll
         for (int l = 0; l < 4; l++) {
@@ -782,11 +790,11 @@ __device__ __forceinline__ IqPart dot_hb(const Iq3HB& w, const ActHB& a, const u
             const uint32_t i2 = prmt(q2, Q2, sel_idx(2 * (l & 1) + 1, l));
             const uint32_t g1 = lds32(i1 * 128u + grid_base);
             const uint32_t g2 = lds32(i2 * 128u + grid_base);
-            const uint32_t sb = prmt(sgw, Q1, sel_byte(l, l));
-            const uint32_t ss = lds32(sb * 128u + sel_base);
+            const uint32_t slo = (sp[l] & 0x4444u) | 0x3210u;            // lanes 0-3: sign bits 0-3
+            const uint32_t shi = ((sp[l] >> 16) & 0x4444u) | 0x3210u;    // lanes 4-7: sign bits 4-7
             const int wi = gi * 8 + 2 * l;
-            const uint32_t a1 = prmt(a.w[wi], na[wi], ss);
-            const uint32_t a2 = prmt(a.w[wi + 1], na[wi + 1], ss >> 16);
+            const uint32_t a1 = prmt(a.w[wi], na[wi], slo);
+            const uint32_t a2 = prmt(a.w[wi + 1], na[wi + 1], shi);
             gsum = dp4a(g1, a1, gsum);
             gsum = dp4a(g2, a2, gsum);
         }
@@ -883,7 +891,7 @@ struct ActReg {
 // kStride: bytes between table entries (the lane's copy at base).
 template <int G, int kStride, class Act>
 __device__ __forceinline__ void dot_hb_multi(const Iq2HB& w, const Act& act, uint32_t n, uint32_t code_base,
-                                             uint32_t sign_base, int32_t* tot) {
+                                             int32_t* tot) {
     const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;
     const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;
 #pragma unroll
@@ -893,12 +901,12 @@ __device__ __forceinline__ void dot_hb_multi(const Iq2HB& w, const Act& act, uin
         const uint32_t qsw = w32(w.qs, gi);
         const uint32_t sgw = w32(w.sg, gi);
         const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
+        const uint32_t sp[4] = {signs_at2<0>(sgw), signs_at2<1>(sgw), signs_at2<2>(sgw), signs_at2<3>(sgw)};
         uint32_t wd[8];
 #pragma unroll
         for (int l = 0; l < 4; l++) {
             const uint32_t code = lds32(prmt(qsw, Q, sel_idx(l, l)) * (uint32_t)kStride + code_base);
-            const uint32_t sp = lds32(prmt(sgw, Q, sel_byte(l, l)) * (uint32_t)kStride + sign_base);
-            const uint32_t sel = code | sp;
+            const uint32_t sel = code | (sp[l] & 0x44444444u);
             wd[2 * l] = prmt(kIq2PoolPos, kIq2PoolNeg, sel);
             wd[2 * l + 1] = prmt(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
         }
@@ -927,7 +935,7 @@ __device__ __forceinline__ void dot_hb_multi(const Iq2HB& w, const Act& act, uin
 // selectors, which apply them to the activations: the same products).
 template <int G, int kStride, class Act>
 __device__ __forceinline__ void dot_hb_multi(const Iq3HB& w, const Act& act, uint32_t n, uint32_t grid_base,
-                                             uint32_t sel_base, int32_t* tot) {
+                                             int32_t* tot) {
     const uint32_t st = (w.sc & 0x0f0fu) | ((w.sc & 0xf0f0u) << 12);
     const uint32_t sw = st * 2u + 0x01010101u;
 #pragma unroll
@@ -940,15 +948,17 @@ __device__ __forceinline__ void dot_hb_multi(const Iq3HB& w, const Act& act, uin
         const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
         const uint32_t Q1 = Q & 0x01010101u;
         const uint32_t Q2 = (Q >> 1) & 0x01010101u;
+        const uint32_t sp[4] = {signs_at2<0>(sgw), signs_at2<1>(sgw), signs_at2<2>(sgw), signs_at2<3>(sgw)};
         uint32_t wd[8];
 #pragma unroll
         for (int l = 0; l < 4; l++) {
             const uint32_t q2 = l < 2 ? qa : qb;
             const uint32_t g1 = lds32(prmt(q2, Q1, sel_idx(2 * (l & 1), l)) * (uint32_t)kStride + grid_base);
             const uint32_t g2 = lds32(prmt(q2, Q2, sel_idx(2 * (l & 1) + 1, l)) * (uint32_t)kStride + grid_base);
-            const uint32_t ss = lds32(prmt(sgw, Q1, sel_byte(l, l)) * (uint32_t)kStride + sel_base);
-            wd[2 * l] = prmt(g1, neg4_nonzero(g1), ss);
-            wd[2 * l + 1] = prmt(g2, neg4_nonzero(g2), ss >> 16);
+            const uint32_t slo = (sp[l] & 0x4444u) | 0x3210u;
+            const uint32_t shi = ((sp[l] >> 16) & 0x4444u) | 0x3210u;
+            wd[2 * l] = prmt(g1, neg4_nonzero(g1), slo);
+            wd[2 * l + 1] = prmt(g2, neg4_nonzero(g2), shi);
         }
         const int32_t scale = (int32_t)prmt(sw, 0, 0x4440u | (uint32_t)((gi & 1) * 2 + (gi >> 1)));
 #pragma unroll

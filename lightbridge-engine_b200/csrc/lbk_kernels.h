@@ -119,7 +119,7 @@ struct RepackArgs {
 };
 cudaError_t launch_repack(const RepackArgs& a, cudaStream_t stream);
 cudaError_t launch_build_tables(const uint64_t* iq2s, const uint32_t* iq3s, uint32_t* iq2_img, uint32_t* iq3_img,
-                                uint32_t* sign_img, uint32_t* sel_img, cudaStream_t stream);
+                                cudaStream_t stream);
 // f32 decode of `rows` consecutive GGUF rows of nb blocks (decode.cu)
 struct DecodeArgs {
     int type;                 // Q4_K, Q5_K, IQ2_S or IQ3_S

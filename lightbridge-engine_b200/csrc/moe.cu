@@ -101,15 +101,14 @@ __device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, 
 // Integer dot of one half block, dispatched on the weight type.
 template <int T>
 struct HBDot {
-    // t0 / t1: shared-window addresses of this lane's copy of the type's table
-    // and of the sign table (sign spread for IQ2_S, sign select for IQ3_S).
+    // t0: shared-window address of this lane's copy of the type's table.
     template <class HB>
-    __device__ __forceinline__ static void run(const HB& w, const ActHB& a, const uint32_t* na, uint32_t t0,
-                                               uint32_t t1, int h, IqPart& ip, KPart& kp) {
+    __device__ __forceinline__ static void run(const HB& w, const ActHB& a, const uint32_t* na, uint32_t t0, int h,
+                                               IqPart& ip, KPart& kp) {
         if constexpr (T == LBK_TYPE_IQ2_S) {
-            ip = dot_hb(w, a, t0, t1);
+            ip = dot_hb(w, a, t0);
         } else if constexpr (T == LBK_TYPE_IQ3_S) {
-            ip = dot_hb(w, a, na, t0, t1);
+            ip = dot_hb(w, a, na, t0);
         } else {
             kp = dot_hb(w, a, h);
         }
@@ -184,19 +183,9 @@ constexpr int table_bytes() {
 }
 
 template <int T>
-__device__ __forceinline__ void fill_tables(uint32_t* tab, uint32_t* signs, const Tables& t) {
+__device__ __forceinline__ void fill_tables(uint32_t* tab, const Tables& t) {
     if constexpr (T == LBK_TYPE_IQ2_S) fill_iq2_codes(tab, t);
     if constexpr (T == LBK_TYPE_IQ3_S) fill_iq3_grid(tab, t);
-    (void)signs;
-}
-
-// The sign table a kernel holds: one IQ type per kernel at most.
-template <int TA, int TB>
-__device__ __forceinline__ void fill_sign_table(uint32_t* signs, const Tables& t) {
-    static_assert(!(TA == LBK_TYPE_IQ2_S && TB == LBK_TYPE_IQ3_S) && !(TA == LBK_TYPE_IQ3_S && TB == LBK_TYPE_IQ2_S),
-                  "one IQ type per kernel");
-    if constexpr (TA == LBK_TYPE_IQ3_S || TB == LBK_TYPE_IQ3_S) fill_sign_sel(signs, t);
-    else fill_signs(signs, t);
 }
 
 __device__ __forceinline__ uint32_t lane_addr(const uint32_t* tab) {
@@ -211,15 +200,13 @@ template <int TG, int TS>
 struct GUSmem {
     static constexpr int kTabG = table_bytes<TG>();
     static constexpr int kTabS = (TS == TG) ? 0 : table_bytes<TS>();
-    static constexpr bool kSigns = is_iq<TG>() || is_iq<TS>();
-    static constexpr int kSignB = kSigns ? kSignBytes : 0;
-    static constexpr int kFixed = kTabG + kTabS + kSignB;
+    static constexpr int kFixed = kTabG + kTabS;
 };
 
 template <int T>
 __device__ __forceinline__ void gate_up_rows(const MoeGateUpArgs& a, uint64_t t, uint64_t slot, const uint8_t* gmat,
                                              const uint8_t* umat, uint64_t r0, uint64_t r1, float* prod, float* chains,
-                                             float* res, const uint32_t* tab, const uint32_t* signs) {
+                                             float* res, const uint32_t* tab) {
     using HB = typename HBOf<T>::type;
     constexpr bool kIq = is_iq<T>();
     const int lane = threadIdx.x & 31;
@@ -241,7 +228,6 @@ __device__ __forceinline__ void gate_up_rows(const MoeGateUpArgs& a, uint64_t t,
         }
     }
     const uint32_t t0 = lane_addr(tab);
-    const uint32_t t1 = lane_addr(signs);
     MatrixRef gm{gmat, a.ffn, nb}, um{umat, a.ffn, nb};
 
     // Rows stream through a ring of D prefetched steps held in registers
@@ -280,8 +266,8 @@ __device__ __forceinline__ void gate_up_rows(const MoeGateUpArgs& a, uint64_t t,
             gk.min_sum = uk.min_sum = 0;
             gk.dm = uk.dm = 0;
             if (mine) {
-                HBDot<T>::run(gw, act, nact, t0, t1, h, gi, gk);
-                HBDot<T>::run(uw, act, nact, t0, t1, h, ui, uk);
+                HBDot<T>::run(gw, act, nact, t0, h, gi, gk);
+                HBDot<T>::run(uw, act, nact, t0, h, ui, uk);
             }
             const int ri = (int)(row - rb);
             float* pg = prod + (size_t)(ri * 2 + 0) * nb * kTail;
@@ -350,7 +336,6 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t* tabG = reinterpret_cast<uint32_t*>(smem);
     uint32_t* tabS = S::kTabS ? reinterpret_cast<uint32_t*>(smem + S::kTabG) : tabG;
-    uint32_t* signs = reinterpret_cast<uint32_t*>(smem + S::kTabG + S::kTabS);
     float* prod_all = reinterpret_cast<float*>(smem + S::kFixed);
     const int warp = threadIdx.x >> 5;
     float* prod = prod_all + (size_t)warp * a.prod_floats;
@@ -377,9 +362,8 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
         __syncwarp();
         if (blockIdx.x == 0 && lane < (int)a.k) a.routed_store[lane] = s_routed[lane];
     }
-    fill_tables<TG>(tabG, signs, a.tables);
-    if constexpr (S::kTabS != 0) fill_tables<TS>(tabS, signs, a.tables);
-    if constexpr (S::kSigns) fill_sign_table<TG, TS>(signs, a.tables);
+    fill_tables<TG>(tabG, a.tables);
+    if constexpr (S::kTabS != 0) fill_tables<TS>(tabS, a.tables);
     __syncthreads();
 
     const uint64_t gw = (uint64_t)blockIdx.x * kGUWarps + warp;
@@ -395,13 +379,13 @@ __global__ void __launch_bounds__(kGUThreads, 1) moe_gate_up_kernel(MoeGateUpArg
             e = 0;
         }
         uint64_t r0 = c * a.chunk_r, r1 = r0 + a.chunk_r < a.ffn ? r0 + a.chunk_r : a.ffn;
-        gate_up_rows<TG>(a, t, j, a.gate[e], a.up[e], r0, r1, prod, chains, res, tabG, signs);
+        gate_up_rows<TG>(a, t, j, a.gate[e], a.up[e], r0, r1, prod, chains, res, tabG);
         arrive_and_quantize(a, t, j, r0, r1);
     } else if (gw < routed_items + shared_items) {
         uint64_t q = gw - routed_items;
         uint64_t t = q / a.chunks_s, c = q % a.chunks_s;
         uint64_t r0 = c * a.chunk_s, r1 = r0 + a.chunk_s < a.ffn ? r0 + a.chunk_s : a.ffn;
-        gate_up_rows<TS>(a, t, a.k, a.sgate, a.sup, r0, r1, prod, chains, res, tabS, signs);
+        gate_up_rows<TS>(a, t, a.k, a.sgate, a.sup, r0, r1, prod, chains, res, tabS);
         arrive_and_quantize(a, t, a.k, r0, r1);
     }
 }
@@ -434,8 +418,7 @@ struct GUTRole {
     static constexpr int kChain = kIq ? 0 : kBmax * 2 * 9;
     static constexpr int kRes = 64;
     static constexpr int kTab = table_bytes<T>();
-    static constexpr int kSign = kIq ? kSignBytes : 0;
-    static constexpr int kRingOff = kTab + kSign;
+    static constexpr int kRingOff = kTab;
     static constexpr int kProdOff = kRingOff + kGUTWarps * kStage;
     static constexpr int kChainOff = kProdOff + kGUTWarps * kProd * 4;
     static constexpr int kResOff = kChainOff + kGUTWarps * kChain * 4;
@@ -479,7 +462,6 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
     float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
     const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
-    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
     const StageOff so = stage_off<T>(nb, sub, b, h);
     const int pstride = 2 * nb * kTail;  // prod[(ri*2 + m)*nb + b][kTail]
 
@@ -577,8 +559,8 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
                 kpg.dm = kpu.dm = 0;
             }
             if (mine) {
-                HBDot<T>::run(wg, act, nact, t0, t1, h, ipg, kpg);
-                HBDot<T>::run(wu, act, nact, t0, t1, h, ipu, kpu);
+                HBDot<T>::run(wg, act, nact, t0, h, ipg, kpg);
+                HBDot<T>::run(wu, act, nact, t0, h, ipu, kpu);
             }
             float* pr = prod + (int)(row - rb) * pstride;
             write_products<T>(pr, b, h, mine, ipg, kpg, act.d, a.status, (uint64_t)row * nb + b);
@@ -603,19 +585,18 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     }
 }
 
-// A shared-expert role of an IQ type holds that type's lookup tables too:
-// bulk copies into the start of shared memory, waited for by every thread.
-template <int T, int kTab, int kSign>
+// A shared-expert role of an IQ type holds that type's lookup table too:
+// a bulk copy into the start of shared memory, waited for by every thread.
+template <int T, int kTab>
 __device__ __forceinline__ void load_role_tables(const Tables& t, uint8_t* smem, uint64_t* bar_word, DeviceStatus* st) {
     if constexpr (kTab != 0) {
         const uint32_t bar = (uint32_t)__cvta_generic_to_shared(bar_word);
         if (threadIdx.x == 0) {
             mbar_init(bar, 1);
             mbar_init_fence();
-            mbar_expect_tx(bar, (uint32_t)(kTab + kSign));
+            mbar_expect_tx(bar, (uint32_t)kTab);
             const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
             bulk_g2s(base, T == LBK_TYPE_IQ2_S ? (const void*)t.iq2_codes : (const void*)t.iq3_grid, kTab, bar);
-            bulk_g2s(base + kTab, T == LBK_TYPE_IQ2_S ? (const void*)t.signs : (const void*)t.sign_sel, kSign, bar);
         }
         __syncthreads();
         if (!mbar_wait(bar, 0) && threadIdx.x == 0) report(st, LBK_TIMEOUT, 5, 0);
@@ -661,7 +642,7 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         // the experts' gate / up pointers, staged with the tables (16-byte copies)
         __shared__ __align__(16) const uint8_t* s_ptr[2 * kPtrMax];
         const bool stage_ptr = a.experts <= kPtrMax && a.experts % 2 == 0;
-        const uint32_t tab_tx = (RL::kTab != 0 ? RL::kTab + RL::kSign : 0) + (stage_ptr ? 16u * (uint32_t)a.experts : 0);
+        const uint32_t tab_tx = (uint32_t)RL::kTab + (stage_ptr ? 16u * (uint32_t)a.experts : 0);
         if (threadIdx.x == 0) {
             mbar_init(bar_p, 1);
             mbar_init(bar_t, 1);
@@ -673,8 +654,6 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
                 bulk_g2s(base, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
                          RL::kTab, bar_t);
-                bulk_g2s(base + RL::kTab, TG == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
-                         RL::kSign, bar_t);
             }
             if (stage_ptr) {
                 const uint32_t ps = (uint32_t)__cvta_generic_to_shared(s_ptr);
@@ -737,7 +716,7 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                           stage_ptr ? s_ptr : nullptr);
     } else {
         __shared__ __align__(8) uint64_t s_stab;
-        load_role_tables<TS, GUTRole<TS>::kTab, GUTRole<TS>::kSign>(a.tables, smem, &s_stab, a.status);
+        load_role_tables<TS, GUTRole<TS>::kTab>(a.tables, smem, &s_stab, a.status);
         // shared expert: its first rows are constant data, requested before
         // the wait for the router's output (inside gut_run)
         gut_run<TS, false>(a, smem, bar, nullptr, (blockIdx.x - a.routed_ctas) * kGUTWarps + warp,
@@ -751,15 +730,13 @@ template <int TD, int TSD>
 struct DownSmem {
     static constexpr int kTabD = table_bytes<TD>();
     static constexpr int kTabS = (TSD == TD) ? 0 : table_bytes<TSD>();
-    static constexpr bool kSigns = is_iq<TD>() || is_iq<TSD>();
-    static constexpr int kSignB = kSigns ? kSignBytes : 0;
-    static constexpr int kFixed = kTabD + kTabS + kSignB;
+    static constexpr int kFixed = kTabD + kTabS;
 };
 
 template <int T>
 __device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint64_t slot, const uint8_t* dmat,
                                           int wsub, uint64_t r0, uint64_t r1, float* prod, float* chains, float* res,
-                                          float* dots, const uint32_t* tab, const uint32_t* signs) {
+                                          float* dots, const uint32_t* tab) {
     using HB = typename HBOf<T>::type;
     constexpr bool kIq = is_iq<T>();
     constexpr int kTail = TypeInfo<T>::kTail;
@@ -782,7 +759,6 @@ __device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint
         }
     }
     const uint32_t t0 = lane_addr(tab);
-    const uint32_t t1 = lane_addr(signs);
     MatrixRef dm{dmat, a.hidden, nb};
     // this warp's rows: r0 + wsub*rps + i*wps*rps + sub, through a ring of D
     // prefetched steps in registers
@@ -812,7 +788,7 @@ __device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint
             for (int l = 0; l < 8; l++) kp.lane[l] = 0;
             kp.min_sum = 0;
             kp.dm = 0;
-            if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
+            if (mine) HBDot<T>::run(w, act, nact, t0, h, ip, kp);
             float* pd = prod + (size_t)(nd + sub) * nb * kTail;
             write_products<T>(pd, b, h, mine, ip, kp, act.d, a.status, row * nb + b);
             nd += rps;
@@ -833,7 +809,6 @@ __global__ void __launch_bounds__(kDownMaxThreads, 1) moe_down_kernel(MoeDownArg
     extern __shared__ __align__(16) uint8_t smem[];
     uint32_t* tabD = reinterpret_cast<uint32_t*>(smem);
     uint32_t* tabS = S::kTabS ? reinterpret_cast<uint32_t*>(smem + S::kTabD) : tabD;
-    uint32_t* signs = reinterpret_cast<uint32_t*>(smem + S::kTabD + S::kTabS);
     float* dots = reinterpret_cast<float*>(smem + S::kFixed);
     float* prod_all = dots + (a.k + 1) * a.rows_per_cta;
     const int warp = threadIdx.x >> 5;
@@ -842,9 +817,8 @@ __global__ void __launch_bounds__(kDownMaxThreads, 1) moe_down_kernel(MoeDownArg
     float* chains = prod_all + (size_t)nwarps * a.prod_floats + (size_t)warp * a.chain_floats;
     float* res = chains + a.chain_floats - 64;
 
-    fill_tables<TD>(tabD, signs, a.tables);
-    if constexpr (S::kTabS != 0) fill_tables<TSD>(tabS, signs, a.tables);
-    if constexpr (S::kSigns) fill_sign_table<TD, TSD>(signs, a.tables);
+    fill_tables<TD>(tabD, a.tables);
+    if constexpr (S::kTabS != 0) fill_tables<TSD>(tabS, a.tables);
     __syncthreads();
 
     const uint64_t t = blockIdx.y;
@@ -854,9 +828,9 @@ __global__ void __launch_bounds__(kDownMaxThreads, 1) moe_down_kernel(MoeDownArg
     const int wsub = warp % a.wps;
     if (slot < a.k) {
         uint32_t e = a.routed[t * a.k + slot].expert_id;
-        if (e < a.experts) down_rows<TD>(a, t, slot, a.down[e], wsub, r0, r1, prod, chains, res, dots, tabD, signs);
+        if (e < a.experts) down_rows<TD>(a, t, slot, a.down[e], wsub, r0, r1, prod, chains, res, dots, tabD);
     } else if (slot == a.k) {
-        down_rows<TSD>(a, t, slot, a.sdown, wsub, r0, r1, prod, chains, res, dots, tabS, signs);
+        down_rows<TSD>(a, t, slot, a.sdown, wsub, r0, r1, prod, chains, res, dots, tabS);
     }
     __syncthreads();
     if (status_set(a.status)) return;  // validation failed upstream: leave out unchanged
@@ -898,8 +872,7 @@ struct DNRole {
     static constexpr int kChain = kIq ? 0 : 16 * 9;   // a batch has <= max(kBmax, R) <= 16 rows
     static constexpr int kRes = 32;
     static constexpr int kTab = table_bytes<T>();
-    static constexpr int kSign = kIq ? kSignBytes : 0;
-    static constexpr int kRingOff = kTab + kSign;
+    static constexpr int kRingOff = kTab;
     static constexpr int kProdOff = kRingOff + kDNWarps * kStage;
     static constexpr int kChainOff = kProdOff + kDNWarps * kProd * 4;
     static constexpr int kResOff = kChainOff + kDNWarps * kChain * 4;
@@ -987,7 +960,6 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
     float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
     float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
     const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
-    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
     const StageOff so = stage_off<T>(nb, sub, b, h);
 
     const uint32_t H = (uint32_t)a.hidden;
@@ -1073,7 +1045,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             for (int l = 0; l < 8; l++) kp.lane[l] = 0;
             kp.min_sum = 0;
             kp.dm = 0;
-            if (mine) HBDot<T>::run(w, act, nact, t0, t1, h, ip, kp);
+            if (mine) HBDot<T>::run(w, act, nact, t0, h, ip, kp);
             write_products<T>(prod + (int)(row - rb) * nb * kTail, b, h, mine, ip, kp, act.d, a.status,
                               (uint64_t)row * nb + b);
             const uint32_t rn = ra + R;
@@ -1109,8 +1081,7 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
     // the gate/up kernel: this part overlaps that kernel's tail
     __shared__ __align__(16) const uint8_t* s_ptr[kPtrMax];
     const bool stage_ptr = a.experts <= kPtrMax && a.experts % 2 == 0;
-    const uint32_t tab_tx = (DNRole<TD>::kTab != 0 ? DNRole<TD>::kTab + DNRole<TD>::kSign : 0) +
-                            (stage_ptr ? 8u * (uint32_t)a.experts : 0);
+    const uint32_t tab_tx = (uint32_t)DNRole<TD>::kTab + (stage_ptr ? 8u * (uint32_t)a.experts : 0);
     if (routed_role && threadIdx.x == 0) {
         using RL = DNRole<TD>;
         if (tab_tx != 0) mbar_expect_tx(bar_t, tab_tx);
@@ -1118,8 +1089,6 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
             const uint32_t base = (uint32_t)__cvta_generic_to_shared(smem);
             bulk_g2s(base, TD == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
                      RL::kTab, bar_t);
-            bulk_g2s(base + RL::kTab, TD == LBK_TYPE_IQ2_S ? (const void*)a.tables.signs : (const void*)a.tables.sign_sel,
-                     RL::kSign, bar_t);
         }
         if (stage_ptr) bulk_g2s((uint32_t)__cvta_generic_to_shared(s_ptr), a.down, 8u * (uint32_t)a.experts, bar_t);
     }
@@ -1161,7 +1130,7 @@ __global__ void __launch_bounds__(kDNThreads, 1) moe_down_tma_kernel(MoeDownArgs
                          stage_ptr ? s_ptr : nullptr);
     } else {
         __shared__ __align__(8) uint64_t s_stab;
-        load_role_tables<TSD, DNRole<TSD>::kTab, DNRole<TSD>::kSign>(a.tables, smem, &s_stab, a.status);
+        load_role_tables<TSD, DNRole<TSD>::kTab>(a.tables, smem, &s_stab, a.status);
         // shared expert: its first rows are constant data, requested before
         // the wait for the gate/up kernel's output (inside dn_run)
         dn_run<TSD, false>(a, smem, bar, (blockIdx.x - a.routed_ctas) * kDNWarps + warp,
@@ -1204,8 +1173,7 @@ struct GrpRole {
     static constexpr int kChain = kIq ? 0 : kGrpDots * 9;
     static constexpr int kRes = kGrpDots;
     static constexpr int kTab = table_bytes<T>();
-    static constexpr int kSign = kIq ? kSignBytes : 0;
-    static constexpr int kRingOff = kTab + kSign;
+    static constexpr int kRingOff = kTab;
     static constexpr int kProdOff = kRingOff + W * kStage;
     static constexpr int kChainOff = kProdOff + W * kProd * 4;
     static constexpr int kResOff = kChainOff + W * kChain * 4;
@@ -1222,10 +1190,10 @@ struct GrpRole {
 // two masks per word).
 template <int T, int G>
 __device__ __forceinline__ void grp_dots(const typename HBOf<T>::type& w, const ActHB* act, uint32_t n, uint32_t t0,
-                                         uint32_t t1, int h, IqPart* ip, KPart* kp) {
+                                         int h, IqPart* ip, KPart* kp) {
     if constexpr (is_iq<T>()) {
         int32_t tot[G];
-        dot_hb_multi<G, 128>(w, ActReg{act}, n, t0, t1, tot);
+        dot_hb_multi<G, 128>(w, ActReg{act}, n, t0, tot);
 #pragma unroll
         for (int p = 0; p < G; p++) ip[p] = IqPart{tot[p], w.d};
     } else {
@@ -1234,7 +1202,6 @@ __device__ __forceinline__ void grp_dots(const typename HBOf<T>::type& w, const 
             if ((uint32_t)p < n) kp[p] = dot_hb(w, act[p], h);
     }
     (void)t0;
-    (void)t1;
     (void)h;
 }
 
@@ -1323,7 +1290,6 @@ __device__ __forceinline__ void gup_run(const MoeGateUpArgs& a, uint8_t* smem, u
     float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
     float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
     const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
-    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
     const StageOff so = stage_off<T>(nb, sub, b, h);
 
     const uint32_t ffn = (uint32_t)a.ffn;
@@ -1396,7 +1362,7 @@ __device__ __forceinline__ void gup_run(const MoeGateUpArgs& a, uint8_t* smem, u
                 IqPart ip[G];
                 KPart kp[G];
                 grp_zero<G>(ip, kp);
-                if (mine) grp_dots<T, G>(m == 0 ? wg : wu, act, n, t0, t1, h, ip, kp);
+                if (mine) grp_dots<T, G>(m == 0 ? wg : wu, act, n, t0, h, ip, kp);
 #pragma unroll
                 for (int p = 0; p < G; p++)
                     if ((uint32_t)p < n)
@@ -1450,7 +1416,6 @@ __device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uin
     float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
     float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
     const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
-    const uint32_t t1 = lane_addr(reinterpret_cast<const uint32_t*>(smem + RL::kTab));
     const StageOff so = stage_off<T>(nb, sub, b, h);
 
     const uint32_t H = (uint32_t)a.hidden;
@@ -1512,7 +1477,7 @@ __device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uin
             IqPart ip[G];
             KPart kp[G];
             grp_zero<G>(ip, kp);
-            if (mine) grp_dots<T, G>(w, act, n, t0, t1, h, ip, kp);
+            if (mine) grp_dots<T, G>(w, act, n, t0, h, ip, kp);
 #pragma unroll
             for (int p = 0; p < G; p++)
                 if ((uint32_t)p < n)
@@ -1547,8 +1512,6 @@ template <int T>
 __device__ __forceinline__ void issue_tables(uint32_t base, const Tables& t, uint32_t bar) {
     if constexpr (table_bytes<T>() != 0) {
         bulk_g2s(base, T == LBK_TYPE_IQ2_S ? (const void*)t.iq2_codes : (const void*)t.iq3_grid, table_bytes<T>(), bar);
-        bulk_g2s(base + table_bytes<T>(), T == LBK_TYPE_IQ2_S ? (const void*)t.signs : (const void*)t.sign_sel,
-                 kSignBytes, bar);
     }
     (void)base;
     (void)t;
@@ -1557,7 +1520,7 @@ __device__ __forceinline__ void issue_tables(uint32_t base, const Tables& t, uin
 
 template <int T>
 constexpr uint32_t tables_tx() {
-    return table_bytes<T>() != 0 ? (uint32_t)(table_bytes<T>() + kSignBytes) : 0u;
+    return (uint32_t)table_bytes<T>();
 }
 
 // Grouped gate/up: CTAs [0, routed_ctas) take the routed groups, the others

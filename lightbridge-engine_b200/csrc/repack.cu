@@ -4,7 +4,8 @@
 // permutation of the GGUF bytes: every field of every block lands in its own
 // plane, and Q4_K / Q5_K quant bytes are reordered lane-major inside each
 // 32-byte group. IQ2_S / IQ3_S qh words (one per half block) are stored
-// bit-transposed (qh_transpose, an involution). It exists so that a thread's
+// bit-transposed (qh_transpose, an involution), and so is every 32-bit word
+// of their sign bytes (sign_transpose / sign_untranspose). It exists so that a thread's
 // half block is a handful of aligned loads whose bits feed the decoder
 // directly; both directions are exact.
 //
@@ -21,21 +22,22 @@ struct Field {
     int src_off;   // offset inside the GGUF block
     int bytes;     // field bytes per block
     int lane_major;  // 1: Q4_K/Q5_K qs or Q5_K qh: permute 32-byte groups;
-                     // 2: IQ2_S/IQ3_S qh: transpose each 32-bit word
+                     // 2: IQ2_S/IQ3_S qh: transpose each 32-bit word (qh_transpose);
+                     // 3: IQ2_S/IQ3_S signs: transpose each 32-bit word (sign_transpose)
 };
 
 __host__ __device__ inline int fields_of(int type, Field* f) {
     switch (type) {
         case LBK_TYPE_IQ2_S:  // qs | signs | qh | scales | d
             f[0] = {2, 32, 0};
-            f[1] = {34, 32, 0};
+            f[1] = {34, 32, 3};
             f[2] = {66, 8, 2};
             f[3] = {74, 8, 0};
             f[4] = {0, 2, 0};
             return 5;
         case LBK_TYPE_IQ3_S:  // qs | signs | qh | scales | d
             f[0] = {2, 64, 0};
-            f[1] = {74, 32, 0};
+            f[1] = {74, 32, 3};
             f[2] = {66, 8, 2};
             f[3] = {106, 4, 0};
             f[4] = {0, 2, 0};
@@ -73,14 +75,15 @@ __global__ void repack_kernel(RepackArgs a, int block_bytes) {
         uint64_t plane = row * rs;  // start of field plane k inside the planar row
         for (int k = 0; k < nf; k++) {
             const int fb = f[k].bytes;
-            if (f[k].lane_major == 2) {
+            if (f[k].lane_major >= 2) {
                 for (int j = 0; j < fb; j += 4) {
                     uint64_t g = bi * block_bytes + f[k].src_off + j;
                     uint64_t p = plane + b * fb + j;
                     const uint8_t* s = a.to_planar ? a.src + g : a.src + p;
                     uint8_t* d = a.to_planar ? a.dst + p : a.dst + g;
                     uint32_t w = (uint32_t)s[0] | ((uint32_t)s[1] << 8) | ((uint32_t)s[2] << 16) | ((uint32_t)s[3] << 24);
-                    w = qh_transpose(w);
+                    if (f[k].lane_major == 2) w = qh_transpose(w);
+                    else w = a.to_planar ? sign_transpose(w) : sign_untranspose(w);
                     for (int i = 0; i < 4; i++) d[i] = (uint8_t)(w >> (8 * i));
                 }
                 plane += (uint64_t)a.nb * fb;
@@ -139,21 +142,18 @@ __global__ void report_scale_kernel(int type, int layout, const uint8_t* data, u
 
 // Replicated shared-memory images of the codebooks: word (entry * 32 + c) =
 // entry, for every copy c (see lbk_device.cuh).
-__global__ void build_tables_kernel(const uint64_t* iq2s, const uint32_t* iq3s, uint32_t* iq2_img, uint32_t* iq3_img,
-                                    uint32_t* sign_img, uint32_t* sel_img) {
+__global__ void build_tables_kernel(const uint64_t* iq2s, const uint32_t* iq3s, uint32_t* iq2_img, uint32_t* iq3_img) {
     const int stride = gridDim.x * blockDim.x;
     const int tid = blockIdx.x * blockDim.x + threadIdx.x;
     for (int i = tid; i < kIq2CodeEntries * 32; i += stride) iq2_img[i] = iq2_code_of(iq2s[i >> 5]);
     for (int i = tid; i < kIq3GridEntries * 32; i += stride) iq3_img[i] = iq3s[i >> 5];
-    for (int i = tid; i < kSignEntries * 32; i += stride) sign_img[i] = sign_spread((uint32_t)(i >> 5));
-    for (int i = tid; i < kSignEntries * 32; i += stride) sel_img[i] = sign_select((uint32_t)(i >> 5));
 }
 
 }  // namespace
 
 cudaError_t launch_build_tables(const uint64_t* iq2s, const uint32_t* iq3s, uint32_t* iq2_img, uint32_t* iq3_img,
-                                uint32_t* sign_img, uint32_t* sel_img, cudaStream_t stream) {
-    build_tables_kernel<<<128, 256, 0, stream>>>(iq2s, iq3s, iq2_img, iq3_img, sign_img, sel_img);
+                                cudaStream_t stream) {
+    build_tables_kernel<<<128, 256, 0, stream>>>(iq2s, iq3s, iq2_img, iq3_img);
     return cudaGetLastError();
 }
 

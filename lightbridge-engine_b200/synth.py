@@ -57,9 +57,9 @@ def packed_torch(gen, ty: int, in_w: int, out_w: int, device, d_range=None):
 # ---------------------------------------------------------------- planar
 
 _FIELDS = {  # (GGUF offset, bytes per block, permutation) in plane order
-    # permutation: False none, True lane-major, "qh" bit-transposed words
-    TYPE_IQ2_S: [(2, 32, False), (34, 32, False), (66, 8, "qh"), (74, 8, False), (0, 2, False)],
-    TYPE_IQ3_S: [(2, 64, False), (74, 32, False), (66, 8, "qh"), (106, 4, False), (0, 2, False)],
+    # permutation: False none, True lane-major, "qh" / "sgn" bit-transposed words
+    TYPE_IQ2_S: [(2, 32, False), (34, 32, "sgn"), (66, 8, "qh"), (74, 8, False), (0, 2, False)],
+    TYPE_IQ3_S: [(2, 64, False), (74, 32, "sgn"), (66, 8, "qh"), (106, 4, False), (0, 2, False)],
     TYPE_Q4_K: [(16, 128, True), (4, 12, False), (0, 4, False)],
     TYPE_Q5_K: [(48, 128, True), (16, 32, True), (4, 12, False), (0, 4, False)],
 }
@@ -93,9 +93,33 @@ def _qh_words(field: np.ndarray) -> np.ndarray:
     return qh_transpose(words).astype("<u4").view(np.uint8).reshape(field.shape)
 
 
+def _delta_swap(w: np.ndarray, mask: int, d: int) -> np.ndarray:
+    t = ((w >> np.uint32(d)) ^ w) & np.uint32(mask)
+    return w ^ t ^ (t << np.uint32(d))
+
+
+_SIGN_SWAPS = [(0x22222222, 1), (0x0C0C0C0C, 2), (0x00AA00AA, 7), (0x0000CCCC, 14)]
+
+
+def sign_transpose(w: np.ndarray, inverse: bool = False) -> np.ndarray:
+    """Sign words of the planar IQ layout: bit 8l + i (subgroup l, lane i) ->
+    bit 4i + l, by four delta swaps (the inverse applies them in reverse)."""
+    w = np.asarray(w, dtype=np.uint32)
+    for mask, d in (reversed(_SIGN_SWAPS) if inverse else _SIGN_SWAPS):
+        w = _delta_swap(w, mask, d)
+    return w
+
+
+def _sign_words(field: np.ndarray, inverse: bool) -> np.ndarray:
+    words = np.ascontiguousarray(field).view("<u4")
+    return sign_transpose(words, inverse).astype("<u4").view(np.uint8).reshape(field.shape)
+
+
 def _permute(field: np.ndarray, how, inverse: bool) -> np.ndarray:
     if how == "qh":
         return _qh_words(field)
+    if how == "sgn":
+        return _sign_words(field, inverse)
     if how:
         return _lane_major_inv(field) if inverse else _lane_major(field)
     return field
