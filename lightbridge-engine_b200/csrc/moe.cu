@@ -151,28 +151,26 @@ __device__ __forceinline__ void warp_tails(const float* prod, int ndots, int nb,
     __syncwarp();
 }
 
-// Per-row products of one half block pair, written into prod[dot][b][kTail].
+// Per-row products of one half block pair, written into prod[dot][b][kTail]
+// by the lane holding half 0 when `store`. Every lane computes them (no
+// divergent branch); the store alone is predicated. The binary16 scales were
+// checked when the layer was created (the reference's validate_scales,
+// k_quants.rs:178-208, hoisted out of the call: the weights are immutable).
 template <int T>
-__device__ __forceinline__ void write_products(float* prod_dot, int b, int h, bool mine, IqPart ip, KPart kp, float dx,
-                                               DeviceStatus* st, uint64_t blk_id) {
+__device__ __forceinline__ void write_products(float* prod_dot, int b, int h, bool store, IqPart ip, KPart kp, float dx) {
     if constexpr (is_iq<T>()) {
-        int other = __shfl_xor_sync(0xffffffffu, ip.sum, 1);
-        if (mine && h == 0) {
-            ip.sum += other;
-            prod_dot[b] = iq_block_product(ip, dx);
-            if (!h_finite(ip.d)) report(st, LBK_NON_FINITE_SCALE, blk_id, ip.d);
-        }
+        ip.sum += __shfl_xor_sync(0xffffffffu, ip.sum, 1);
+        const float p = iq_block_product(ip, dx);
+        if (store && h == 0) prod_dot[b] = p;
     } else {
 #pragma unroll
         for (int l = 0; l < 8; l++) kp.lane[l] += __shfl_xor_sync(0xffffffffu, kp.lane[l], 1);
         kp.min_sum += __shfl_xor_sync(0xffffffffu, kp.min_sum, 1);
-        if (mine && h == 0) {
-            float pr[9];
-            k_block_products(kp, dx, pr);
+        float pr[9];
+        k_block_products(kp, dx, pr);
+        if (store && h == 0) {
 #pragma unroll
             for (int i = 0; i < 9; i++) prod_dot[b * 9 + i] = pr[i];
-            if (!h_finite(kp.dm & 0xffffu) || !h_finite(kp.dm >> 16))
-                report(st, LBK_NON_FINITE_SCALE, blk_id, h_finite(kp.dm & 0xffffu) ? kp.dm >> 16 : kp.dm & 0xffffu);
         }
     }
 }
@@ -272,8 +270,8 @@ __device__ __forceinline__ void gate_up_rows(const MoeGateUpArgs& a, uint64_t t,
             const int ri = (int)(row - rb);
             float* pg = prod + (size_t)(ri * 2 + 0) * nb * kTail;
             float* pu = prod + (size_t)(ri * 2 + 1) * nb * kTail;
-            write_products<T>(pg, b, h, mine, gi, gk, act.d, a.status, row * nb + b);
-            write_products<T>(pu, b, h, mine, ui, uk, act.d, a.status, row * nb + b);
+            write_products<T>(pg, b, h, mine, gi, gk, act.d);
+            write_products<T>(pu, b, h, mine, ui, uk, act.d);
             const uint64_t rn = r + rps;
             if (rn - rb >= (uint64_t)bmax || rn >= r1) {
                 const int nrows = (int)((rn < r1 ? rn : r1) - rb);
@@ -433,12 +431,27 @@ __device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const ui
     bulk_g2s(stage, mat + (uint64_t)ra * rs, nr * rs, bar);
 }
 
+// Lane 0: rows [ra, ra+nr) of gate and of up into the two halves of a stage,
+// both completing on one mbarrier (one expected byte count).
+__device__ __forceinline__ void gut_issue2(uint32_t stage, uint32_t bar, const uint8_t* gmat, const uint8_t* umat,
+                                           uint32_t rs, uint32_t mat_bytes, uint32_t ra, uint32_t nr) {
+    mbar_expect_tx(bar, 2 * nr * rs);
+    bulk_g2s(stage, gmat + (uint64_t)ra * rs, nr * rs, bar);
+    bulk_g2s(stage + mat_bytes, umat + (uint64_t)ra * rs, nr * rs, bar);
+}
+
+// Wait for the phase with the given parity: one poll when the data is there
+// (the common case), else the bounded wait. False when it ran out.
+__device__ __forceinline__ bool stage_wait(uint32_t bar, uint32_t parity) {
+    return mbar_try_wait(bar, parity) || mbar_wait(bar, parity);
+}
+
 // One role's items: (token, slot, chunk of rows) spread over the role's warps.
-// Work unit: R rows (one warp step, 32 half blocks) of one matrix. Units
-// alternate gate, up, gate, up ... through the warp's two stages (stage m
-// holds matrix m); each refill is issued as soon as its stage is copied to
-// registers, two units ahead of its use. dep_wait: the grid dependency
-// (router output) is still to be waited for, after the first copies.
+// Work step: R rows (32 half blocks) of gate and the same rows of up, one
+// stage holding both and one mbarrier; the refill for the next step is issued
+// as soon as the stage is copied to registers, so it lands while this step is
+// decoded. dep_wait: the grid dependency (router output) is still to be
+// waited for, after the first copies.
 // s_ptr: the gate / up pointer tables staged in shared memory (gate at 0, up
 // at kPtrMax), or null.
 constexpr int kPtrMax = 256;
@@ -470,7 +483,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     const uint32_t chunks = (uint32_t)(kRouted ? a.chunks_r : a.chunks_s);
     const uint32_t slots = kRouted ? (uint32_t)a.k : 1u;
     const uint32_t items = (uint32_t)a.tokens * slots * chunks;
-    uint32_t phase = 0;  // bit m: parity of stage m's next phase
+    uint32_t phase = 0;  // parity of the stage's next phase
     bool live = true;  // false after a wait ran out: no further copies are issued
     for (uint32_t it = role_warp; it < items; it += role_warps) {
         const uint32_t t = it / (slots * chunks);
@@ -509,9 +522,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
             // item in flight); the per-unit copies into the stages then hit L2.
             prefetch_l2(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs);
             prefetch_l2(umat + (uint64_t)r0 * rs, (r1 - r0) * rs);
-            const uint32_t nr0 = r1 - r0 < (uint32_t)R ? r1 - r0 : R;
-            gut_issue(stage_s, bar0, gmat, rs, r0, nr0);
-            gut_issue(stage_s + RL::kMat, bar0 + 8, umat, rs, r0, nr0);
+            gut_issue2(stage_s, bar0, gmat, umat, rs, RL::kMat, r0, r1 - r0 < (uint32_t)R ? r1 - r0 : R);
         }
         if (dep_wait) {
             grid_dep_wait();
@@ -520,51 +531,40 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         }
         float* hrow = a.h + ((uint64_t)t * (a.k + 1) + slot) * a.ffn;
         uint32_t rb = r0;
-        // one rolled loop over row steps (R rows of gate and of up): the lane
-        // decodes its half block of both matrices, two independent chains on
-        // the same activations; the decode is emitted once (its code is
-        // fetched cold once per launch)
+        // one rolled loop over row steps (R rows of gate and of up, one stage
+        // and one barrier): the lane decodes its half block of both matrices,
+        // two independent chains on the same activations, with no branch on
+        // the lane (rows past the chunk's end decode stale stage bytes and are
+        // not stored); the decode is emitted once (its code is fetched cold
+        // once per launch)
         const uint32_t steps = units >> 1;
 #pragma unroll 1
         for (uint32_t q = 0; q < steps; q++) {
             const uint32_t ra = r0 + q * R;
             const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
-            if (live && (!mbar_wait(bar0, phase & 1u) || !mbar_wait(bar0 + 8, (phase >> 1) & 1u))) {
+            if (live && !stage_wait(bar0, phase)) {
                 live = false;
-                if (lane == 0) report(a.status, LBK_TIMEOUT, it, 0);
+                report(a.status, LBK_TIMEOUT, it, 0);
             }
-            live = __all_sync(0xffffffffu, live);
-            phase ^= 3u;
-            const bool mine = lane_on && (uint32_t)sub < nr;
+            phase ^= 1u;
             HB wg, wu;
-            if (mine) {
-                load_stage(wg, stage, so);
-                load_stage(wu, stage + RL::kMat, so);
-            }
+            load_stage(wg, stage, so);
+            load_stage(wu, stage + RL::kMat, so);
             __syncwarp();
             const uint32_t rn = ra + R;
             if (lane == 0 && live && q + 1 < steps) {
                 fence_proxy_async_smem();
-                const uint32_t nn = r1 - rn < (uint32_t)R ? r1 - rn : R;
-                gut_issue(stage_s, bar0, gmat, rs, rn, nn);
-                gut_issue(stage_s + RL::kMat, bar0 + 8, umat, rs, rn, nn);
+                gut_issue2(stage_s, bar0, gmat, umat, rs, RL::kMat, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
             }
             const uint32_t row = ra + sub;
             IqPart ipg{0, 0}, ipu{0, 0};
             KPart kpg, kpu;
-            if constexpr (!kIq) {
-#pragma unroll
-                for (int l = 0; l < 8; l++) kpg.lane[l] = kpu.lane[l] = 0;
-                kpg.min_sum = kpu.min_sum = 0;
-                kpg.dm = kpu.dm = 0;
-            }
-            if (mine) {
-                HBDot<T>::run(wg, act, nact, t0, h, ipg, kpg);
-                HBDot<T>::run(wu, act, nact, t0, h, ipu, kpu);
-            }
+            HBDot<T>::run(wg, act, nact, t0, h, ipg, kpg);
+            HBDot<T>::run(wu, act, nact, t0, h, ipu, kpu);
+            const bool store = (uint32_t)sub < nr;
             float* pr = prod + (int)(row - rb) * pstride;
-            write_products<T>(pr, b, h, mine, ipg, kpg, act.d, a.status, (uint64_t)row * nb + b);
-            write_products<T>(pr + nb * kTail, b, h, mine, ipu, kpu, act.d, a.status, (uint64_t)row * nb + b);
+            write_products<T>(pr, b, h, store, ipg, kpg, act.d);
+            write_products<T>(pr + nb * kTail, b, h, store, ipu, kpu, act.d);
             if (rn - rb >= (uint32_t)RL::kBmax || rn >= r1) {
                 const int nrows = (int)((rn < r1 ? rn : r1) - rb);
                 __syncwarp();
@@ -790,7 +790,7 @@ __device__ __forceinline__ void down_rows(const MoeDownArgs& a, uint64_t t, uint
             kp.dm = 0;
             if (mine) HBDot<T>::run(w, act, nact, t0, h, ip, kp);
             float* pd = prod + (size_t)(nd + sub) * nb * kTail;
-            write_products<T>(pd, b, h, mine, ip, kp, act.d, a.status, row * nb + b);
+            write_products<T>(pd, b, h, mine, ip, kp, act.d);
             nd += rps;
         }
     }
@@ -953,6 +953,9 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
     const int nb = a.nb_f, tpr = a.tpr_f, R = 32 / tpr;
     const int sub = lane / tpr, hb = lane % tpr, b = hb >> 1, h = hb & 1;
     const bool lane_on = hb < 2 * nb;
+    // lanes past the last whole row of a unit (ffn 1536: 24 of 32 busy) decode
+    // a copy of row 0's first half block and store nothing: no branch per lane
+    const bool lane_ok = lane_on && sub < R;
     const uint32_t rs = planar_row_bytes(RL::kBB, nb);
     const uint8_t* stage = smem + RL::kRingOff + warp * RL::kStage;
     const uint32_t stage_s = (uint32_t)__cvta_generic_to_shared(stage);
@@ -960,7 +963,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
     float* chains = reinterpret_cast<float*>(smem + RL::kChainOff) + warp * RL::kChain;
     float* res = reinterpret_cast<float*>(smem + RL::kResOff) + warp * RL::kRes;
     const uint32_t t0 = lane_addr(reinterpret_cast<const uint32_t*>(smem));
-    const StageOff so = stage_off<T>(nb, sub, b, h);
+    const StageOff so = stage_off<T>(nb, lane_ok ? sub : 0, lane_ok ? b : 0, lane_ok ? h : 0);
 
     const uint32_t H = (uint32_t)a.hidden;
     const uint32_t chunk = (uint32_t)(kRouted ? a.chunk_r : a.chunk_s);
@@ -1023,15 +1026,13 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             const uint32_t s = u & 1;
             const uint32_t ra = r0 + u * R;
             const uint32_t nr = r1 - ra < (uint32_t)R ? r1 - ra : (uint32_t)R;
-            if (live && !mbar_wait(bar0 + 8 * s, (phase >> s) & 1u)) {
+            if (live && !stage_wait(bar0 + 8 * s, (phase >> s) & 1u)) {
                 live = false;
-                if (lane == 0) report(a.status, LBK_TIMEOUT, it, 1);
+                report(a.status, LBK_TIMEOUT, it, 1);
             }
-            live = __all_sync(0xffffffffu, live);
             phase ^= 1u << s;
-            const bool mine = lane_on && (uint32_t)sub < nr;
             HB w;
-            if (mine) load_stage(w, stage + s * RL::kUnit, so);
+            load_stage(w, stage + s * RL::kUnit, so);
             __syncwarp();
             if (lane == 0 && live && u + 2 < units) {
                 fence_proxy_async_smem();
@@ -1041,13 +1042,8 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             const uint32_t row = ra + sub;
             IqPart ip{0, 0};
             KPart kp;
-#pragma unroll
-            for (int l = 0; l < 8; l++) kp.lane[l] = 0;
-            kp.min_sum = 0;
-            kp.dm = 0;
-            if (mine) HBDot<T>::run(w, act, nact, t0, h, ip, kp);
-            write_products<T>(prod + (int)(row - rb) * nb * kTail, b, h, mine, ip, kp, act.d, a.status,
-                              (uint64_t)row * nb + b);
+            HBDot<T>::run(w, act, nact, t0, h, ip, kp);
+            write_products<T>(prod + (int)(row - rb) * nb * kTail, b, h, lane_ok && (uint32_t)sub < nr, ip, kp, act.d);
             const uint32_t rn = ra + R;
             if (rn - rb >= (uint32_t)RL::kBmax || rn >= r1) {
                 const int nrows = (int)((rn < r1 ? rn : r1) - rb);
@@ -1366,8 +1362,7 @@ __device__ __forceinline__ void gup_run(const MoeGateUpArgs& a, uint8_t* smem, u
 #pragma unroll
                 for (int p = 0; p < G; p++)
                     if ((uint32_t)p < n)
-                        write_products<T>(pr + ((size_t)m * n + p) * nb * kTail, b, h, mine, ip[p], kp[p], act[p].d,
-                                          a.status, (uint64_t)row * nb + b);
+                        write_products<T>(pr + ((size_t)m * n + p) * nb * kTail, b, h, mine, ip[p], kp[p], act[p].d);
             }
             if ((rn - rb) / (uint32_t)R >= ub || rn >= r1) {
                 const uint32_t nrows = (rn < r1 ? rn : r1) - rb;
@@ -1481,8 +1476,7 @@ __device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uin
 #pragma unroll
             for (int p = 0; p < G; p++)
                 if ((uint32_t)p < n)
-                    write_products<T>(pr + (size_t)p * nb * kTail, b, h, mine, ip[p], kp[p], act[p].d, a.status,
-                                      (uint64_t)row * nb + b);
+                    write_products<T>(pr + (size_t)p * nb * kTail, b, h, mine, ip[p], kp[p], act[p].d);
             const uint32_t rn = ra + R;
             if ((rn - rb) / (uint32_t)R >= ub || rn >= r1) {
                 const uint32_t nrows = (rn < r1 ? rn : r1) - rb;

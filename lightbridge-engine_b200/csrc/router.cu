@@ -32,20 +32,49 @@ __global__ void topk_kernel(TopkArgs a) {
                   a.status, t, s_tk[warp][0], s_tk[warp][1]);
 }
 
-// Sequential order: bit-identical to dot_f32_row (gemv.rs:286-303).
-__global__ void router_seq_kernel(RouterArgs a) {
-    uint64_t n = a.experts * a.tokens;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
-        uint64_t t = i / a.experts, e = i % a.experts;
-        const float* w = a.w + e * a.hidden;
+// Sequential order: bit-identical to dot_f32_row (gemv.rs:286-303): for each
+// (token, expert), sum = fl(sum + fl(w[j] * x[j])) over j in order. The
+// products do not depend on one another: the CTA's threads form them for
+// kSeqExperts experts at once (coalesced loads, one chunk of the row at a
+// time) into shared memory, and one lane per expert then runs the dependent
+// additions from there, four products per shared load. The chain itself
+// (hidden dependent adds) is the floor of this order.
+constexpr int kSeqExperts = 8;    // experts per CTA (one summing lane each)
+constexpr int kSeqChunk = 1024;   // lanes of a row staged at a time (32 KB of products)
+constexpr int kSeqThreads = 256;
+
+__global__ void __launch_bounds__(kSeqThreads) router_seq_kernel(RouterArgs a) {
+    __shared__ __align__(16) float s_p[kSeqExperts][kSeqChunk];
+    const uint64_t groups = (a.experts + kSeqExperts - 1) / kSeqExperts;
+    for (uint64_t gi = blockIdx.x; gi < groups * a.tokens; gi += gridDim.x) {
+        const uint64_t t = gi / groups, e0 = (gi % groups) * kSeqExperts;
+        const int ne = (int)(a.experts - e0 < (uint64_t)kSeqExperts ? a.experts - e0 : kSeqExperts);
         const float* x = a.x + t * a.hidden;
-        float sum = 0.0f;
-        for (uint64_t j = 0; j < a.hidden; j++) {
-            float wv = w[j];
-            if (!isfinite(wv)) report(a.status, LBK_NON_FINITE_VALUE, e * a.hidden + j, __float_as_uint(wv));
-            sum = __fadd_rn(sum, __fmul_rn(wv, x[j]));
+        float sum = 0.0f;  // lane e of warp 0: expert e0 + e
+        for (uint64_t c0 = 0; c0 < a.hidden; c0 += kSeqChunk) {
+            const int n = (int)(a.hidden - c0 < (uint64_t)kSeqChunk ? a.hidden - c0 : kSeqChunk);
+            __syncthreads();  // the previous chunk's sums are done with s_p
+            for (int i = threadIdx.x; i < ne * n; i += kSeqThreads) {
+                const int e = i / n, j = i - e * n;
+                const float wv = __ldcs(a.w + (e0 + e) * a.hidden + c0 + j);
+                if (!isfinite(wv)) report(a.status, LBK_NON_FINITE_VALUE, (e0 + e) * a.hidden + c0 + j, __float_as_uint(wv));
+                s_p[e][j] = __fmul_rn(wv, __ldg(x + c0 + j));
+            }
+            __syncthreads();
+            if (threadIdx.x < (unsigned)ne) {
+                const float* p = s_p[threadIdx.x];
+                int j = 0;
+                if ((n & 3) == 0) {
+#pragma unroll 8
+                    for (; j < n; j += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(p + j);
+                        sum = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(sum, v.x), v.y), v.z), v.w);
+                    }
+                }
+                for (; j < n; j++) sum = __fadd_rn(sum, p[j]);
+            }
         }
-        a.logits[t * a.experts + e] = sum;
+        if (threadIdx.x < (unsigned)ne) a.logits[t * a.experts + e0 + threadIdx.x] = sum;
     }
 }
 
@@ -232,11 +261,11 @@ cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStre
 
 cudaError_t launch_router(const RouterArgs& a, int mode, int sm_count, cudaStream_t stream) {
     (void)mode;
-    uint64_t n = a.experts * a.tokens;
-    uint64_t grid = (n + 127) / 128;
-    if (grid > (uint64_t)sm_count * 8) grid = (uint64_t)sm_count * 8;
+    const uint64_t n = (a.experts + kSeqExperts - 1) / kSeqExperts * a.tokens;
+    uint64_t grid = n;
+    if (grid > (uint64_t)sm_count * 4) grid = (uint64_t)sm_count * 4;
     if (grid < 1) grid = 1;
-    router_seq_kernel<<<(unsigned)grid, 128, 0, stream>>>(a);
+    router_seq_kernel<<<(unsigned)grid, kSeqThreads, 0, stream>>>(a);
     return cudaGetLastError();
 }
 
