@@ -1041,13 +1041,11 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             const long rc = K == 0 ? 0
                             : !mode.shared ? (long)ctas
                                            : split_roles(ctas, lbk::kMoeGateUpTmaWarps, T * K * hb * gu_hb_cost_us(L->gate_type),
-                                                         defer_topk ? 12.0 : 8.0, T * hb * gu_hb_cost_us(L->sgate_type),
-                                                         defer_topk && x != nullptr ? 2.0 : 8.0);  // self-quantizing shared role starts at once
+                                                         defer_topk ? 12.0 : 8.0, T * hb * gu_hb_cost_us(L->sgate_type), 8.0);
             g.routed_ctas = (uint32_t)rc;
             // single-token decode: the gate/up kernel publishes the routing for early down copies
             if (full && defer_topk && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf))
                 g.route_flag = reinterpret_cast<unsigned int*>(ws + o.rflag);
-            if (defer_topk && x != nullptr) g.xf = x;
             if (full && T <= 4 && lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)) {
                 g.down = L->d_down;
                 g.sdown = static_cast<const uint8_t*>(L->w.shared.down.data);

@@ -51,11 +51,7 @@ struct MoeGateUpArgs {
     const uint4* grp;                // [groups] {expert, first pair, pairs, 0}
     const uint32_t* grp_pairs;       // [tokens*k] routed index t*k + j, grouped by expert
     uint32_t gsize_r, gsize_s;       // pairs per group: routed / shared expert
-    unsigned int* route_flag;        // single token: set (release) once the first routed CTA has stored the routing, or null
-    // single-token decode: the tokens' f32 input; the shared-expert CTAs
-    // quantize it themselves and start before the router grid ends (or null:
-    // they wait for the router's Q8_K image)
-    const float* xf;
+    unsigned int* route_flag;        // single token: set (release) once CTA 0 has stored the routing, or null
     DeviceStatus* status;
     Tables tables;
 };

@@ -98,79 +98,6 @@ __device__ __forceinline__ void load_act_global(ActHB& a, const uint8_t* q8row, 
     for (int i = 0; i < 8; i++) a.bsum[i] = (int32_t)(int16_t)((w32(bs, i >> 1) >> (16 * (i & 1))) & 0xffffu);
 }
 
-// A thread's half block of Q8_K activations quantized from the f32 input
-// (xb: the block's 256 values; this lane holds lanes 128h .. 128h+127, its
-// partner lane the other half). The same arithmetic as quantize_q8k_warp
-// (quantize_row_q8_k_into, q8_k.rs:35-73): the first index of the largest
-// |x| keeps its sign as max, iscale = -127/max, q = min(nearest(iscale x),
-// 127), d = 1/iscale, 16-lane group sums. Returns false when a value is not
-// finite (the router reports it; the activations are then meaningless).
-template <bool kTr>
-__device__ __forceinline__ bool quantize_act_f32(ActHB& a, const float* xb, int h, bool bsums) {
-    const float4* src = reinterpret_cast<const float4*>(xb + 128 * h);
-    unsigned long long key = 0ull;
-    bool bad = false;
-#pragma unroll 8
-    for (int i = 0; i < 32; i++) {
-        const float4 v = __ldg(src + i);
-        const float c[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            const uint32_t idx = (uint32_t)(128 * h + 4 * i + k);
-            const unsigned long long kk =
-                ((unsigned long long)__float_as_uint(fabsf(c[k])) << 32) | (unsigned long long)(0xffffffffu - idx);
-            key = kk > key ? kk : key;
-            bad |= !isfinite(c[k]);
-        }
-    }
-    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, 1);
-    key = other > key ? other : key;
-    if ((uint32_t)(key >> 32) == 0u) {  // an all-zero block: 292 zero bytes
-#pragma unroll
-        for (int i = 0; i < 32; i++) a.w[i] = 0u;
-#pragma unroll
-        for (int g = 0; g < 8; g++) a.bsum[g] = 0;
-        a.d = 0.0f;
-        return !bad;
-    }
-    const uint32_t idx = 0xffffffffu - (uint32_t)(key & 0xffffffffull);
-    const float iscale = __fdiv_rn(-127.0f, __ldg(xb + idx));
-#pragma unroll
-    for (int g = 0; g < 8; g++) a.bsum[g] = 0;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        const float4 v = __ldg(src + i);
-        const float c[4] = {v.x, v.y, v.z, v.w};
-        uint32_t w = 0;
-        int32_t sum = 0;
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            int q = __float2int_rn(__fmul_rn(iscale, c[k]));
-            q = q > 127 ? 127 : q;
-            sum += q;
-            w |= ((uint32_t)q & 0xffu) << (8 * k);
-        }
-        a.w[i] = w;
-        a.bsum[i >> 2] += sum;
-    }
-    if (!bsums) {
-#pragma unroll
-        for (int g = 0; g < 8; g++) a.bsum[g] = 0;
-    }
-    a.d = __fdiv_rn(1.0f, iscale);
-    if (kTr) {
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            uint32_t n[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) n[i] = a.w[8 * j + i];
-            transpose4(n[0], n[2], n[4], n[6], a.w[8 * j + 0], a.w[8 * j + 1], a.w[8 * j + 2], a.w[8 * j + 3]);
-            transpose4(n[1], n[3], n[5], n[7], a.w[8 * j + 4], a.w[8 * j + 5], a.w[8 * j + 6], a.w[8 * j + 7]);
-        }
-    }
-    return !bad;
-}
-
 // Integer dot of one half block, dispatched on the weight type.
 template <int T>
 struct HBDot {
@@ -558,8 +485,6 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     const uint32_t items = (uint32_t)a.tokens * slots * chunks;
     uint32_t phase = 0;  // parity of the stage's next phase
     bool live = true;  // false after a wait ran out: no further copies are issued
-    // the shared expert of a single-token call quantizes the token itself
-    const bool self_quant = !kRouted && a.xf != nullptr;
     for (uint32_t it = role_warp; it < items; it += role_warps) {
         const uint32_t t = it / (slots * chunks);
         const uint32_t rem = it - t * (slots * chunks);
@@ -570,22 +495,17 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         const uint32_t units = 2 * ((r1 - r0 + R - 1) / R);
         ActHB act;
         uint32_t nact[32];
-        bool x_bad = false;  // a non-finite input (reported by the router): report nothing here
         auto load_act = [&]() {
             if (lane_on) {
-                if (self_quant)
-                    x_bad = !quantize_act_f32<!kIq>(act, a.xf + ((uint64_t)t * nb + b) * kQK, h, !kIq);
-                else
-                    load_act_global<!kIq>(act, a.q8x + (uint64_t)t * nb * kQ8IBytes, b, h, !kIq);
+                load_act_global<!kIq>(act, a.q8x + (uint64_t)t * nb * kQ8IBytes, b, h, !kIq);
                 if constexpr (T == LBK_TYPE_IQ3_S) {
 #pragma unroll
                     for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
                 }
             }
-            x_bad = __any_sync(0xffffffffu, x_bad);
         };
         // the activations do not depend on the expert: in flight while it is resolved
-        if (!dep_wait || self_quant) load_act();
+        if (!dep_wait) load_act();
         const uint8_t* gmat = a.sgate;
         const uint8_t* umat = a.sup;
         if constexpr (kRouted) {
@@ -604,7 +524,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
             prefetch_l2(umat + (uint64_t)r0 * rs, (r1 - r0) * rs);
             gut_issue2(stage_s, bar0, gmat, umat, rs, RL::kMat, r0, r1 - r0 < (uint32_t)R ? r1 - r0 : R);
         }
-        if (dep_wait && !self_quant) {
+        if (dep_wait) {
             grid_dep_wait();
             dep_wait = false;
             load_act();
@@ -652,7 +572,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
                 for (int qq = lane; qq < nrows; qq += 32) {
                     float g = res[qq * 2], u = res[qq * 2 + 1];
                     float v = swiglu_ref(g, u);
-                    if (!isfinite(v) && !x_bad)
+                    if (!isfinite(v))
                         report(a.status, LBK_NON_FINITE_VALUE, ((uint64_t)t * (a.k + 1) + slot) * a.ffn + rb + qq,
                                __float_as_uint(v));
                     hrow[rb + qq] = v;
@@ -660,12 +580,6 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
                 __syncwarp();
                 rb = rn;
             }
-        }
-        // the arrival counters are zeroed by the router: a role that started
-        // before its grid ended waits for it here
-        if (dep_wait) {
-            grid_dep_wait();
-            dep_wait = false;
         }
         arrive_and_quantize(a, t, slot, r0, r1);
     }
@@ -703,18 +617,13 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         mbar_init_fence();
     }
     __syncwarp();
-    // CTAs [0, shared_ctas) take the shared expert, the others the routed
-    // slots: the first CTAs to start (on SMs the router grid leaves free) are
-    // the ones with work that does not wait for the routing.
-    const uint32_t shared_ctas = gridDim.x - a.routed_ctas;
-    if (blockIdx.x >= shared_ctas) {
+    if (blockIdx.x < a.routed_ctas) {
         using RL = GUTRole<TG>;
-        const uint32_t rcta = blockIdx.x - shared_ctas;  // routed CTA index
         // Prologue by bulk copies: (single-token decode) the router's chunk
         // partials, then the lookup tables, land in shared memory; the whole
         // CTA finishes the router from the partials (logits in chunk order,
-        // then top-k) while the tables arrive. Routed CTA 0 publishes the
-        // routing for the down kernel.
+        // then top-k) while the tables arrive. CTA 0 publishes the routing
+        // for the down kernel.
         __shared__ __align__(8) uint64_t s_pro[3];  // [0] partials, [1] tables, [2] selection bias
         __shared__ uint32_t s_sel[32];
         __shared__ int s_bad;
@@ -773,11 +682,11 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 if (!mbar_wait(bar_b, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 2, 0);
             }
             topk_cta(s_part, (int)a.chunks, stage_bias ? s_bias : a.bias, (int)a.experts, (int)a.k, a.weight_scale,
-                     s_routed, rcta == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
-            if (rcta == 0 && threadIdx.x < a.k) a.routed_store[threadIdx.x] = s_routed[threadIdx.x];
+                     s_routed, blockIdx.x == 0 ? a.status : nullptr, s_key, s_p, s_sel, &s_bad);
+            if (blockIdx.x == 0 && threadIdx.x < a.k) a.routed_store[threadIdx.x] = s_routed[threadIdx.x];
             // The down kernel may read the routing before its grid wait:
             // publish it (every writer's store, then the flag).
-            if (rcta == 0 && a.route_flag != nullptr) {
+            if (blockIdx.x == 0 && a.route_flag != nullptr) {
                 __threadfence();
                 __syncthreads();
                 if (threadIdx.x == 0) st_release_gpu(a.route_flag, 1u);
@@ -790,7 +699,7 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         // its own rows up to 5 us late.
         if (a.down != nullptr && lane == 0) {
             const uint64_t H = a.hidden, n = a.tokens * a.k;
-            const uint64_t p0 = H * rcta / a.routed_ctas, p1 = H * (rcta + 1) / a.routed_ctas;
+            const uint64_t p0 = H * blockIdx.x / a.routed_ctas, p1 = H * (blockIdx.x + 1) / a.routed_ctas;
             for (uint64_t i = warp; p1 > p0 && i <= n; i += kGUTWarps) {
                 if (i == n) {
                     prefetch_l2(a.sdown + p0 * a.sdown_rs, (uint32_t)((p1 - p0) * a.sdown_rs));
@@ -803,16 +712,15 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
         if (tab_tx != 0) {
             if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 1, 0);
         }
-        gut_run<TG, true>(a, smem, bar, s_routed, rcta * kGUTWarps + warp, a.routed_ctas * kGUTWarps, false,
+        gut_run<TG, true>(a, smem, bar, s_routed, blockIdx.x * kGUTWarps + warp, a.routed_ctas * kGUTWarps, false,
                           stage_ptr ? s_ptr : nullptr);
     } else {
         __shared__ __align__(8) uint64_t s_stab;
         load_role_tables<TS, GUTRole<TS>::kTab>(a.tables, smem, &s_stab, a.status);
         // shared expert: its first rows are constant data, requested before
-        // the wait for the router's output (inside gut_run); a single-token
-        // call quantizes the token here and waits only before its arrivals
-        gut_run<TS, false>(a, smem, bar, nullptr, blockIdx.x * kGUTWarps + warp, shared_ctas * kGUTWarps, true,
-                           nullptr);
+        // the wait for the router's output (inside gut_run)
+        gut_run<TS, false>(a, smem, bar, nullptr, (blockIdx.x - a.routed_ctas) * kGUTWarps + warp,
+                           (gridDim.x - a.routed_ctas) * kGUTWarps, true, nullptr);
     }
 }
 

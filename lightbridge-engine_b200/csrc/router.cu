@@ -230,93 +230,6 @@ __global__ void topk_partials_kernel(RouterFusedArgs f) {
     }
 }
 
-// Single-token decode with the top-k left to the consumer (f.defer): the
-// same chunk partials as router_fused_kernel (each a sequential f32 sum of 16
-// products per lane, then a fixed shuffle tree), laid out so that the router
-// holds few SMs. A warp item is one 512-lane chunk of kR1Rows consecutive
-// expert rows: the chunk of x and the rows' loads are all in flight before
-// any math, so an item is one memory round trip, and 8-warp CTAs leave most
-// SMs to the gate/up kernel, whose CTAs can then start (programmatic
-// dependent launch) while the router still runs.
-constexpr int kR1Rows = 4;
-constexpr int kR1Threads = 512;
-
-__global__ void __launch_bounds__(kR1Threads, 1) router1_kernel(RouterFusedArgs f) {
-    const RouterArgs& a = f.r;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t chunks = (a.hidden + kChunk - 1) / kChunk;
-    const uint64_t groups = a.experts / kR1Rows;  // experts % kR1Rows == 0 (launcher)
-    const uint64_t row_items = groups * chunks;
-    const uint64_t nbq = f.q8x ? a.hidden / kQK : 0;
-    const uint64_t items = row_items + nbq;
-    const uint64_t nw = (uint64_t)gridDim.x * (kR1Threads / 32);
-    grid_dep_launch();
-    if (blockIdx.x == 0)
-        for (uint64_t i = threadIdx.x; i < f.zero_words; i += kR1Threads) f.zero[i] = 0u;
-    for (uint64_t it = (uint64_t)blockIdx.x * (kR1Threads / 32) + warp; it < items; it += nw) {
-        if (it < row_items) {
-            const uint64_t c = it / groups, e0 = (it % groups) * kR1Rows;
-            const uint64_t j0 = c * kChunk;
-            float xr[16], wr[kR1Rows][16];
-#pragma unroll
-            for (int q = 0; q < 16; q++) {
-                const uint64_t j = j0 + (uint64_t)q * 32 + lane;
-                xr[q] = j < a.hidden ? __ldg(a.x + j) : 0.0f;
-            }
-#pragma unroll
-            for (int r = 0; r < kR1Rows; r++)
-#pragma unroll
-                for (int q = 0; q < 16; q++) {
-                    const uint64_t j = j0 + (uint64_t)q * 32 + lane;
-                    wr[r][q] = j < a.hidden ? __ldcs(a.w + (e0 + r) * a.hidden + j) : 0.0f;
-                }
-#pragma unroll
-            for (int r = 0; r < kR1Rows; r++) {
-                float acc = 0.0f;
-#pragma unroll
-                for (int q = 0; q < 16; q++) acc = __fadd_rn(acc, __fmul_rn(wr[r][q], xr[q]));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, o));
-                if (lane == 0) f.partials[(e0 + r) * chunks + c] = acc;
-                int bad_q = -1;
-                uint32_t bad_bits = 0;
-#pragma unroll
-                for (int q = 15; q >= 0; q--)
-                    if (!isfinite(wr[r][q])) {
-                        bad_q = q;
-                        bad_bits = __float_as_uint(wr[r][q]);
-                    }
-                if (bad_q >= 0)
-                    report(a.status, LBK_NON_FINITE_VALUE, (e0 + r) * a.hidden + j0 + (uint64_t)bad_q * 32 + lane,
-                           bad_bits);
-            }
-        } else {
-            const uint64_t b = it - row_items;
-            const float* xb = a.x + b * kQK + lane * 8;
-            float v[8];
-            bool bad = false;
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                v[i] = __ldg(xb + i);
-                bad |= !isfinite(v[i]);
-            }
-            if (__ballot_sync(0xffffffffu, bad)) {
-                if (bad) {
-                    for (int i = 0; i < 8; i++)
-                        if (!isfinite(v[i])) {
-                            report(a.status, LBK_NON_FINITE_VALUE, b * kQK + lane * 8 + i, __float_as_uint(v[i]));
-                            break;
-                        }
-                }
-                continue;
-            }
-            Q8Block qb = quantize_q8k_warp(v, lane);
-            int32_t pair = qb.pair_sum + __shfl_xor_sync(0xffffffffu, qb.pair_sum, 1);
-            store_q8i(f.q8x + b * kQ8IBytes, qb, pair, lane);
-        }
-    }
-}
-
 }  // namespace
 
 size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens) {
@@ -325,13 +238,6 @@ size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens
 
 cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStream_t stream) {
     const uint64_t chunks = (f.r.hidden + kChunk - 1) / kChunk;
-    if (f.defer && f.r.tokens == 1 && f.r.experts % kR1Rows == 0) {
-        const uint64_t items = f.r.experts / kR1Rows * chunks + (f.q8x ? f.r.hidden / kQK : 0);
-        uint64_t ctas = (items + (kR1Threads / 32) - 1) / (kR1Threads / 32);
-        if (ctas > (uint64_t)sm_count) ctas = sm_count;
-        router1_kernel<<<(unsigned)ctas, kR1Threads, 0, stream>>>(f);
-        return cudaGetLastError();
-    }
     uint64_t items = f.r.experts * chunks + (f.q8x ? f.r.tokens * (f.r.hidden / kQK) : 0);
     uint64_t ctas = (items + (kRouterThreads / 32) - 1) / (kRouterThreads / 32);
     if (ctas > (uint64_t)sm_count) ctas = sm_count;
