@@ -428,7 +428,7 @@ struct GUTRole {
 __device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const uint8_t* mat, uint32_t rs, uint32_t ra,
                                           uint32_t nr) {
     mbar_expect_tx(bar, nr * rs);
-    bulk_g2s(stage, mat + (uint64_t)ra * rs, nr * rs, bar);
+    bulk_g2s_stream(stage, mat + (uint64_t)ra * rs, nr * rs, bar, policy_evict_first());
 }
 
 // Lane 0: rows [ra, ra+nr) of gate and of up into the two halves of a stage,
@@ -436,8 +436,9 @@ __device__ __forceinline__ void gut_issue(uint32_t stage, uint32_t bar, const ui
 __device__ __forceinline__ void gut_issue2(uint32_t stage, uint32_t bar, const uint8_t* gmat, const uint8_t* umat,
                                            uint32_t rs, uint32_t mat_bytes, uint32_t ra, uint32_t nr) {
     mbar_expect_tx(bar, 2 * nr * rs);
-    bulk_g2s(stage, gmat + (uint64_t)ra * rs, nr * rs, bar);
-    bulk_g2s(stage + mat_bytes, umat + (uint64_t)ra * rs, nr * rs, bar);
+    const uint64_t pol = policy_evict_first();
+    bulk_g2s_stream(stage, gmat + (uint64_t)ra * rs, nr * rs, bar, pol);
+    bulk_g2s_stream(stage + mat_bytes, umat + (uint64_t)ra * rs, nr * rs, bar, pol);
 }
 
 // Wait for the phase with the given parity: one poll when the data is there
@@ -520,8 +521,8 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         if (lane == 0 && live) {
             // The whole chunk heads for L2 at once (HBM sees every byte of the
             // item in flight); the per-unit copies into the stages then hit L2.
-            prefetch_l2(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs);
-            prefetch_l2(umat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            prefetch_l2_stream(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
+            prefetch_l2_stream(umat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
             gut_issue2(stage_s, bar0, gmat, umat, rs, RL::kMat, r0, r1 - r0 < (uint32_t)R ? r1 - r0 : R);
         }
         if (dep_wait) {
@@ -1007,7 +1008,7 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             mat = s_ptr ? s_ptr[e] : a.down[e];
         }
         if (lane == 0 && live) {
-            prefetch_l2(mat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            prefetch_l2_stream(mat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
             for (uint32_t u = 0; u < 2 && u < units; u++) {
                 const uint32_t ra = r0 + u * R;
                 gut_issue(stage_s + u * RL::kUnit, bar0 + 8 * u, mat, rs, ra, r1 - ra < (uint32_t)R ? r1 - ra : R);
@@ -1313,8 +1314,8 @@ __device__ __forceinline__ void gup_run(const MoeGateUpArgs& a, uint8_t* smem, u
         }
         const uint32_t steps = (r1 - r0 + R - 1) / R;
         if (lane == 0 && live) {
-            prefetch_l2(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs);
-            prefetch_l2(umat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            prefetch_l2_stream(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
+            prefetch_l2_stream(umat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
             const uint32_t nr0 = r1 - r0 < (uint32_t)R ? r1 - r0 : R;
             gut_issue(stage_s, bar0, gmat, rs, r0, nr0);
             gut_issue(stage_s + RL::kUnit, bar0 + 8, umat, rs, r0, nr0);
@@ -1434,7 +1435,7 @@ __device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uin
         }
         const uint32_t units = (r1 - r0 + R - 1) / R;
         if (lane == 0 && live) {
-            prefetch_l2(mat + (uint64_t)r0 * rs, (r1 - r0) * rs);
+            prefetch_l2_stream(mat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
             for (uint32_t u = 0; u < 2 && u < units; u++) {
                 const uint32_t ra = r0 + u * R;
                 gut_issue(stage_s + u * RL::kUnit, bar0 + 8 * u, mat, rs, ra, r1 - ra < (uint32_t)R ? r1 - ra : R);
