@@ -305,13 +305,11 @@ __device__ __forceinline__ void arrive_and_quantize(const MoeGateUpArgs& a, uint
         unsigned n = (unsigned)(hi - lo);
         unsigned int* cnt = a.counters + sidx * a.nb_f + blk;
         unsigned old = 0;
-        if (lane == 0) {
-            __threadfence();
-            old = atomicAdd(cnt, n);
-        }
+        __syncwarp();  // the lanes' h stores before lane 0's release
+        if (lane == 0) old = atom_add_acq_rel_gpu(cnt, n);
         old = __shfl_sync(0xffffffffu, old, 0);
+        __syncwarp();  // lane 0's acquire before the lanes' reads below
         if (old + n != (unsigned)kQK) continue;
-        __threadfence();
         const float* hb = a.h + sidx * a.ffn + blk * kQK + lane * 8;
         float v[8];
         bool bad = false;
@@ -457,10 +455,30 @@ __device__ __forceinline__ bool stage_wait(uint32_t bar, uint32_t parity) {
 // at kPtrMax), or null.
 constexpr int kPtrMax = 256;
 
+// This CTA's slice of every down matrix the call will read heads for L2:
+// HBM streams it while the gate/up rows are being decoded. One matrix per
+// warp (lane 0): a bulk prefetch can hold its thread while the SM's copy
+// queue is full.
+__device__ __forceinline__ void prefetch_down_rows(const MoeGateUpArgs& a, const lbk_routed* s_routed, uint32_t rcta) {
+    const int warp = threadIdx.x >> 5;
+    const uint64_t H = a.hidden, n = a.tokens * a.k;
+    const uint64_t p0 = H * rcta / a.routed_ctas, p1 = H * (rcta + 1) / a.routed_ctas;
+    for (uint64_t i = warp; p1 > p0 && i <= n; i += kGUTWarps) {
+        if (i == n) {
+            prefetch_l2(a.sdown + p0 * a.sdown_rs, (uint32_t)((p1 - p0) * a.sdown_rs));
+        } else {
+            const uint32_t e = a.defer_topk ? s_routed[i].expert_id : a.routed[i].expert_id;
+            if (e < a.experts) prefetch_l2(a.down[e] + p0 * a.down_rs, (uint32_t)((p1 - p0) * a.down_rs));
+        }
+    }
+}
+
 template <int T, bool kRouted>
 __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, uint32_t bar0, const lbk_routed* s_routed,
                                         uint32_t role_warp, uint32_t role_warps, bool dep_wait,
                                         const uint8_t* const* s_ptr) {
+    // the down rows are requested once this warp's first rows are in
+    bool down_pf = kRouted && a.down != nullptr;
     using RL = GUTRole<T>;
     using HB = typename HBOf<T>::type;
     constexpr bool kIq = RL::kIq;
@@ -519,11 +537,14 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
             umat = s_ptr ? s_ptr[kPtrMax + e] : a.up[e];
         }
         if (lane == 0 && live) {
-            // The whole chunk heads for L2 at once (HBM sees every byte of the
-            // item in flight); the per-unit copies into the stages then hit L2.
-            prefetch_l2_stream(gmat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
-            prefetch_l2_stream(umat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
+            // the first step's rows go straight to the stage, ahead of any prefetch
             gut_issue2(stage_s, bar0, gmat, umat, rs, RL::kMat, r0, r1 - r0 < (uint32_t)R ? r1 - r0 : R);
+            // the next two steps' rows head for L2 (later ones as the steps go)
+            const uint32_t rp = r0 + R, rq = r0 + 3 * R < r1 ? r0 + 3 * R : r1;
+            if (rp < rq) {
+                prefetch_l2_stream(gmat + (uint64_t)rp * rs, (rq - rp) * rs, policy_evict_first());
+                prefetch_l2_stream(umat + (uint64_t)rp * rs, (rq - rp) * rs, policy_evict_first());
+            }
         }
         if (dep_wait) {
             grid_dep_wait();
@@ -556,6 +577,18 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
             if (lane == 0 && live && q + 1 < steps) {
                 fence_proxy_async_smem();
                 gut_issue2(stage_s, bar0, gmat, umat, rs, RL::kMat, rn, r1 - rn < (uint32_t)R ? r1 - rn : R);
+                // the rows three steps ahead head for L2: a few requests per
+                // step, so that no copy waits behind a long queue
+                const uint32_t rp = ra + 3 * R;
+                if (rp < r1) {
+                    const uint32_t np = r1 - rp < (uint32_t)R ? r1 - rp : R;
+                    prefetch_l2_stream(gmat + (uint64_t)rp * rs, np * rs, policy_evict_first());
+                    prefetch_l2_stream(umat + (uint64_t)rp * rs, np * rs, policy_evict_first());
+                }
+            }
+            if (q == 1 && down_pf) {
+                if (lane == 0) prefetch_down_rows(a, s_routed, blockIdx.x);
+                down_pf = false;
             }
             const uint32_t row = ra + sub;
             IqPart ipg{0, 0}, ipu{0, 0};
@@ -584,6 +617,7 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
         }
         arrive_and_quantize(a, t, slot, r0, r1);
     }
+    if (down_pf && (threadIdx.x & 31) == 0) prefetch_down_rows(a, s_routed, blockIdx.x);  // a warp without items
 }
 
 // A shared-expert role of an IQ type holds that type's lookup table too:
@@ -691,23 +725,6 @@ __global__ void __launch_bounds__(kGUTThreads, 1) moe_gate_up_tma_kernel(MoeGate
                 __threadfence();
                 __syncthreads();
                 if (threadIdx.x == 0) st_release_gpu(a.route_flag, 1u);
-            }
-        }
-        // This CTA's slice of every down matrix the call will read heads for
-        // L2 now: HBM streams it while the gate/up rows are being decoded.
-        // One matrix per warp: a bulk prefetch can hold its thread while the
-        // SM's copy queue is full, and one thread issuing all of them started
-        // its own rows up to 5 us late.
-        if (a.down != nullptr && lane == 0) {
-            const uint64_t H = a.hidden, n = a.tokens * a.k;
-            const uint64_t p0 = H * blockIdx.x / a.routed_ctas, p1 = H * (blockIdx.x + 1) / a.routed_ctas;
-            for (uint64_t i = warp; p1 > p0 && i <= n; i += kGUTWarps) {
-                if (i == n) {
-                    prefetch_l2(a.sdown + p0 * a.sdown_rs, (uint32_t)((p1 - p0) * a.sdown_rs));
-                } else {
-                    const uint32_t e = a.defer_topk ? s_routed[i].expert_id : a.routed[i].expert_id;
-                    if (e < a.experts) prefetch_l2(a.down[e] + p0 * a.down_rs, (uint32_t)((p1 - p0) * a.down_rs));
-                }
             }
         }
         if (tab_tx != 0) {
@@ -895,13 +912,11 @@ __device__ __forceinline__ void dn_arrive_and_combine(const MoeDownArgs& a, uint
         const uint32_t target = (uint32_t)(a.k + 1) * (bend - blk * kDNBlock);
         unsigned int* cnt = a.counters + (uint64_t)t * nblk + blk;
         unsigned old = 0;
-        if (lane == 0) {
-            __threadfence();
-            old = atomicAdd(cnt, hi - lo);
-        }
+        __syncwarp();  // the lanes' dot stores before lane 0's release
+        if (lane == 0) old = atom_add_acq_rel_gpu(cnt, hi - lo);
         old = __shfl_sync(0xffffffffu, old, 0);
+        __syncwarp();  // lane 0's acquire before the lanes' reads below
         if (old + (hi - lo) != target) continue;
-        __threadfence();
         if (lane == 0) *cnt = 0u;  // ready for the next launch
         if (status_set(a.status)) continue;  // validation failed upstream: leave out unchanged
         const float* dt = a.dots + (uint64_t)t * (a.k + 1) * H;
@@ -1008,7 +1023,8 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             mat = s_ptr ? s_ptr[e] : a.down[e];
         }
         if (lane == 0 && live) {
-            prefetch_l2_stream(mat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
+            // single-token calls: the gate/up kernel has put these rows in L2
+            if (a.route_flag == nullptr) prefetch_l2_stream(mat + (uint64_t)r0 * rs, (r1 - r0) * rs, policy_evict_first());
             for (uint32_t u = 0; u < 2 && u < units; u++) {
                 const uint32_t ra = r0 + u * R;
                 gut_issue(stage_s + u * RL::kUnit, bar0 + 8 * u, mat, rs, ra, r1 - ra < (uint32_t)R ? r1 - ra : R);
