@@ -860,6 +860,7 @@ struct MoeMode {
     const uint8_t* q8x;  // the tokens' Q8_K images (null: the workspace's, from the router kernel)
     float* dots;         // row dots [T][dots_slots][H] (null: the workspace's)
     uint32_t dots_slots;
+    const uint32_t* d_items = nullptr;  // items counted on the device (T is then the capacity)
 };
 
 MoeMode full_mode(const lbk_moe_layer* L) { return MoeMode{L->k, true, true, nullptr, nullptr, (uint32_t)(L->k + 1)}; }
@@ -999,7 +1000,8 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
     if (!full && !(L->fused && lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)nbh) &&
                    lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)))
         return fail(LBK_INVALID_PARAMETER, "expert-parallel calls need planar layers with hidden 2048 or 4096");
-    if (L->fused && !defer_topk && L->group_min != 0 && T >= L->group_min && T >= 2 && L->E_local <= 1024 &&
+    if (L->fused && !defer_topk && mode.d_items == nullptr && L->group_min != 0 && T >= L->group_min && T >= 2 &&
+        L->E_local <= 1024 &&
         T * K <= 8192 &&
         lbk::moe_grouped_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type, (int)nbh, (int)nbf))
         return moe_experts_grouped(L, T, routed, out, ws, o, st, mode);
@@ -1026,6 +1028,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
         g.sup = static_cast<const uint8_t*>(L->w.shared.up.data);
         g.routed = routed;
         g.q8x = mode.q8x ? mode.q8x : ws + o.q8x;
+        g.d_items = mode.d_items;
         g.has_shared = mode.shared ? 1 : 0;
         g.h = reinterpret_cast<float*>(ws + o.h);
         g.hq = ws + o.hq;
@@ -1148,6 +1151,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             d.has_shared = mode.shared ? 1 : 0;
             d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
             d.route_flag = g.route_flag;
+            d.d_items = mode.d_items;
             d.route_readers = g.route_flag ? reinterpret_cast<unsigned int*>(ws + o.rreaders) : nullptr;
             d.route_polls = L->wait_limit;
             e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
@@ -1614,6 +1618,151 @@ LBK_API int32_t lbk_ep_items_forward(lbk_moe_layer* layer, const uint8_t* q8_ite
     // one routed slot per item, the expert ID local to this layer; no shared expert, no combine
     return moe_experts(layer, nullptr, items, items_routed, nullptr, ws, o, st, false,
                        MoeMode{1, false, false, q8_items, dots, 1});
+}
+
+// ---------------------------------------------- peer memory (expert parallelism)
+
+LBK_API int32_t lbk_peer_alloc(lbk_context* ctx, uint64_t bytes, void** ptr, uint8_t handle[64]) {
+    if (ctx == nullptr || ptr == nullptr || handle == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (bytes == 0) return fail(LBK_DIMENSION_MISMATCH, "peer buffer bytes", 0, 1, 0);
+    if (int32_t s = set_device(ctx)) return s;
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc peer buffer");
+    if ((e = cudaMemset(p, 0, bytes)) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "zero peer buffer");
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    if ((e = cudaIpcGetMemHandle(&h, p)) != cudaSuccess) {
+        cudaFree(p);
+        return cuda_fail(e, "cudaIpcGetMemHandle");
+    }
+    std::memcpy(handle, &h, 64);
+    *ptr = p;
+    return ok();
+}
+
+LBK_API int32_t lbk_peer_free(lbk_context* ctx, void* ptr) {
+    if (ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null context");
+    if (ptr == nullptr) return ok();
+    if (int32_t s = set_device(ctx)) return s;
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaFree peer buffer");
+}
+
+LBK_API int32_t lbk_peer_open(lbk_context* ctx, const uint8_t handle[64], void** ptr) {
+    if (ctx == nullptr || handle == nullptr || ptr == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (int32_t s = set_device(ctx)) return s;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, 64);
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    *ptr = p;
+    return ok();
+}
+
+LBK_API int32_t lbk_peer_close(lbk_context* ctx, void* ptr) {
+    if (ctx == nullptr) return fail(LBK_INVALID_PARAMETER, "null context");
+    if (ptr == nullptr) return ok();
+    if (int32_t s = set_device(ctx)) return s;
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+namespace {
+lbk_ep_exchange ep_exchange(const lbk_moe_layer* L, uint64_t cap) {
+    lbk_ep_exchange x{};
+    const uint64_t q8b = L->H / LBK_QK_K * lbk::kQ8IBytes;
+    x.routing = 0;
+    x.tokens = up256(cap * L->k * sizeof(lbk_routed));
+    x.q8 = x.tokens + 256;
+    x.dots = up256(x.q8 + cap * q8b);
+    x.total = up256(x.dots + cap * L->k * L->H * 4);
+    x.q8_bytes = q8b;
+    return x;
+}
+}  // namespace
+
+LBK_API int32_t lbk_ep_exchange_layout(const lbk_moe_layer* layer, uint64_t cap, lbk_ep_exchange* out) {
+    if (layer == nullptr || out == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (cap == 0) return fail(LBK_DIMENSION_MISMATCH, "tokens per rank", 0, 1, 0);
+    *out = ep_exchange(layer, cap);
+    return ok();
+}
+
+LBK_API int32_t lbk_ep_publish(lbk_moe_layer* layer, const float* x, uint64_t tokens, void* xbuf, uint64_t cap,
+                               void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr || xbuf == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (tokens > cap) return fail(LBK_DIMENSION_MISMATCH, "tokens beyond the exchange capacity", 0, cap, tokens);
+    if (!aligned(xbuf, 256)) return fail(LBK_INVALID_PARAMETER, "exchange buffer 256-byte alignment");
+    const lbk_ep_exchange xl = ep_exchange(layer, cap);
+    uint8_t* xb = static_cast<uint8_t*>(xbuf);
+    if (tokens) {
+        if (int32_t s = lbk_ep_route(layer, x, tokens, reinterpret_cast<lbk_routed*>(xb + xl.routing), xb + xl.q8,
+                                     workspace, workspace_bytes, stream))
+            return s;
+    } else if (int32_t s = set_device(layer->ctx)) {
+        return s;
+    }
+    cudaError_t e = lbk::launch_ep_set_tokens(reinterpret_cast<uint32_t*>(xb + xl.tokens), (uint32_t)tokens, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "token count store");
+}
+
+LBK_API int32_t lbk_ep_gather(lbk_moe_layer* layer, const void* const* peers, uint32_t world, uint64_t cap,
+                              uint8_t* q8_items, lbk_routed* items, uint64_t* returns, uint32_t* count,
+                              uint64_t cap_items, void* stream) {
+    if (layer == nullptr || peers == nullptr || q8_items == nullptr || items == nullptr || returns == nullptr ||
+        count == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (world == 0 || cap == 0) return fail(LBK_DIMENSION_MISMATCH, "ranks / tokens per rank", 0, 1, 0);
+    if (cap_items < world * cap * layer->k)
+        return fail(LBK_SCRATCH_TOO_SMALL, "item capacity", 0, world * cap * layer->k, cap_items);
+    if (!aligned(q8_items, 16)) return fail(LBK_INVALID_PARAMETER, "q8 items 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    const lbk_ep_exchange xl = ep_exchange(layer, cap);
+    lbk::EpGatherArgs a{reinterpret_cast<const uint8_t* const*>(peers), world, (uint32_t)cap, (uint32_t)layer->k,
+                        (uint32_t)xl.q8_bytes, xl.tokens, xl.q8, (uint32_t)layer->first, (uint32_t)layer->E_local,
+                        q8_items, items, reinterpret_cast<uint2*>(returns), count, (uint32_t)cap_items};
+    cudaError_t e = lbk::launch_ep_gather(a, ctx->sm_count, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "gather launch");
+}
+
+LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t* q8_items, const lbk_routed* items,
+                                             const uint32_t* count, uint64_t cap_items, float* dots, void* workspace,
+                                             uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (int32_t s = ep_check(layer, cap_items, workspace, workspace_bytes, ep_ws_bytes(layer, cap_items))) return s;
+    if (q8_items == nullptr || items == nullptr || dots == nullptr || count == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(q8_items, 16) || !aligned(dots, 16)) return fail(LBK_INVALID_PARAMETER, "q8 / dots 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    const WsLayout o = moe_ws(layer, cap_items, 1);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
+    if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+    MoeMode m{1, false, false, q8_items, dots, 1};
+    m.d_items = count;
+    return moe_experts(layer, nullptr, cap_items, items, nullptr, ws, o, st, false, m);
+}
+
+LBK_API int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint64_t cap, const float* dots,
+                               const uint64_t* returns, const uint32_t* count, uint64_t cap_items, void* stream) {
+    if (layer == nullptr || peers == nullptr || dots == nullptr || returns == nullptr || count == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(dots, 16) || layer->H % 4) return fail(LBK_INVALID_PARAMETER, "dots 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    const lbk_ep_exchange xl = ep_exchange(layer, cap);
+    lbk::EpScatterArgs a{reinterpret_cast<uint8_t* const*>(peers), xl.dots, dots, reinterpret_cast<const uint2*>(returns),
+                         count, (uint32_t)cap_items, (uint32_t)layer->H};
+    cudaError_t e = lbk::launch_ep_scatter(a, ctx->sm_count, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "scatter launch");
 }
 
 LBK_API int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens, const lbk_routed* routed,

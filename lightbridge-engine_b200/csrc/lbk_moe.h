@@ -52,6 +52,9 @@ struct MoeGateUpArgs {
     const uint32_t* grp_pairs;       // [tokens*k] routed index t*k + j, grouped by expert
     uint32_t gsize_r, gsize_s;       // pairs per group: routed / shared expert
     unsigned int* route_flag;        // single token: set (release) once CTA 0 has stored the routing, or null
+    // expert-parallel items whose count is only known on the device: read
+    // here after the grid dependency (tokens is then the capacity), or null
+    const uint32_t* d_items;
     DeviceStatus* status;
     Tables tables;
 };
@@ -91,6 +94,7 @@ struct MoeDownArgs {
     unsigned int* route_flag;
     unsigned int* route_readers;
     uint32_t route_polls;            // polls of route_flag before LBK_TIMEOUT
+    const uint32_t* d_items;         // see MoeGateUpArgs
     DeviceStatus* status;
     Tables tables;
 };
@@ -145,5 +149,29 @@ cudaError_t launch_moe_gate_up_grp(int gate_type, int shared_gate_type, const Mo
                                    cudaStream_t stream);
 cudaError_t launch_moe_down_grp(int down_type, int shared_down_type, const MoeDownArgs& a, unsigned ctas,
                                 cudaStream_t stream);
+
+// Expert-parallel exchange over peer memory (ep.cu).
+struct EpGatherArgs {
+    const uint8_t* const* peers;  // [world] exchange buffers, as this GPU addresses them
+    uint32_t world, cap, k, q8b;  // cap: tokens per rank at most
+    uint64_t off_ntok, off_q8;    // offsets in an exchange buffer (routing at 0)
+    uint32_t first, count;        // this rank's experts [first, first + count)
+    uint8_t* q8_items;            // [cap_items][q8b]
+    lbk_routed* items;            // [cap_items] local expert ID, coefficient 0
+    uint2* returns;               // [cap_items] {home rank, pair t * k + j}
+    uint32_t* d_count;            // items gathered (zeroed by the launcher)
+    uint32_t cap_items;           // world * cap * k
+};
+struct EpScatterArgs {
+    uint8_t* const* peers;
+    uint64_t off_dots;
+    const float* dots;            // [cap_items][hidden]
+    const uint2* returns;
+    const uint32_t* d_count;
+    uint32_t cap_items, hidden;
+};
+cudaError_t launch_ep_gather(const EpGatherArgs& a, int sm_count, cudaStream_t stream);
+cudaError_t launch_ep_scatter(const EpScatterArgs& a, int sm_count, cudaStream_t stream);
+cudaError_t launch_ep_set_tokens(uint32_t* p, uint32_t v, cudaStream_t stream);
 
 }  // namespace lbk

@@ -175,6 +175,23 @@ __device__ __forceinline__ void write_products(float* prod_dot, int b, int h, bo
     }
 }
 
+// The routed role's work when the item count is read on the device
+// (expert-parallel items; a.tokens is the capacity): the host's chunking
+// (rows spread over the role's warps in whole steps of R rows) on the count.
+struct RoleWork {
+    uint32_t tokens, chunk, chunks;
+};
+__device__ __forceinline__ RoleWork device_work(const uint32_t* d_items, uint64_t cap, uint32_t slots, uint32_t warps,
+                                                uint32_t rows, uint32_t R) {
+    uint32_t n = __ldcg(d_items);
+    n = n < cap ? n : (uint32_t)cap;
+    uint32_t per = n ? warps / (n * slots) : 1u;
+    per = per < 1u ? 1u : per;
+    uint32_t c = (rows + per - 1) / per;
+    c = (c + R - 1) / R * R;
+    return RoleWork{n, c, (rows + c - 1) / c};
+}
+
 template <int T>
 constexpr int table_bytes() {
     return T == LBK_TYPE_IQ2_S ? kIq2CodeBytes : (T == LBK_TYPE_IQ3_S ? kIq3GridBytes : 0);
@@ -498,10 +515,11 @@ __device__ __forceinline__ void gut_run(const MoeGateUpArgs& a, uint8_t* smem, u
     const int pstride = 2 * nb * kTail;  // prod[(ri*2 + m)*nb + b][kTail]
 
     const uint32_t ffn = (uint32_t)a.ffn;
-    const uint32_t chunk = (uint32_t)(kRouted ? a.chunk_r : a.chunk_s);
-    const uint32_t chunks = (uint32_t)(kRouted ? a.chunks_r : a.chunks_s);
     const uint32_t slots = kRouted ? (uint32_t)a.k : 1u;
-    const uint32_t items = (uint32_t)a.tokens * slots * chunks;
+    RoleWork wk{(uint32_t)a.tokens, (uint32_t)(kRouted ? a.chunk_r : a.chunk_s), (uint32_t)(kRouted ? a.chunks_r : a.chunks_s)};
+    if (kRouted && a.d_items != nullptr) wk = device_work(a.d_items, a.tokens, slots, role_warps, ffn, R);
+    const uint32_t chunk = wk.chunk, chunks = wk.chunks;
+    const uint32_t items = wk.tokens * slots * chunks;
     uint32_t phase = 0;  // parity of the stage's next phase
     bool live = true;  // false after a wait ran out: no further copies are issued
     for (uint32_t it = role_warp; it < items; it += role_warps) {
@@ -982,10 +1000,11 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
     const StageOff so = stage_off<T>(nb, lane_ok ? sub : 0, lane_ok ? b : 0, lane_ok ? h : 0);
 
     const uint32_t H = (uint32_t)a.hidden;
-    const uint32_t chunk = (uint32_t)(kRouted ? a.chunk_r : a.chunk_s);
-    const uint32_t chunks = (uint32_t)(kRouted ? a.chunks_r : a.chunks_s);
     const uint32_t slots = kRouted ? (uint32_t)a.k : 1u;
-    const uint32_t items = (uint32_t)a.tokens * slots * chunks;
+    RoleWork wk{(uint32_t)a.tokens, (uint32_t)(kRouted ? a.chunk_r : a.chunk_s), (uint32_t)(kRouted ? a.chunks_r : a.chunks_s)};
+    if (kRouted && a.d_items != nullptr) wk = device_work(a.d_items, a.tokens, slots, role_warps, H, R);
+    const uint32_t chunk = wk.chunk, chunks = wk.chunks;
+    const uint32_t items = wk.tokens * slots * chunks;
     uint32_t phase = 0;  // bit s: parity of stage s's next phase
     bool live = true;
     for (uint32_t it = role_warp; it < items; it += role_warps) {

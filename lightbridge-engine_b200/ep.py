@@ -195,3 +195,77 @@ class ExpertParallelMoe:
             L.combine(q8, tokens, routed, routed_dots, out, self.workspace(tokens, dev))
         if routed_out is not None and tokens:
             routed_out.view(torch.int32).view(-1)[: tokens * k * 2].copy_(routed.view(-1))
+
+
+class PeerExpertParallelMoe:
+    """One rank of an expert-parallel MoE layer whose exchange runs over peer
+    memory (NVLink) instead of collectives: every rank's exchange buffer is
+    mapped into every other rank (lbk.PeerBuffer, plain peer loads and stores),
+    the home rank publishes its routing and Q8_K images there, every rank
+    gathers the pairs of its experts and scatters their row dots back into the
+    home buffers (lbk_ep_publish / gather / items_forward_counted / scatter),
+    and the home rank combines. The item count stays on the device, so a layer
+    step has no size exchange and no device-to-host read; the two barriers are
+    one-element all-reduces on the stream. Results equal lbk_moe_forward on
+    one GPU bit for bit (the combine order is the one-GPU order).
+
+    cap: the most tokens any rank brings to a step. Collective: every rank of
+    the group calls forward once per layer step."""
+
+    def __init__(self, layer, cap: int, group=None):
+        import lbk
+
+        self.layer = layer
+        self.group = group
+        self.world, self.rank = _world(group)
+        E = layer.global_experts
+        if E % self.world:
+            raise ValueError(f"{E} experts do not shard evenly over {self.world} ranks")
+        self.experts_per_rank = E // self.world
+        if layer.local_experts != self.experts_per_rank or layer.first_expert != self.rank * self.experts_per_rank:
+            raise ValueError(f"rank {self.rank} holds the wrong share of the experts")
+        self.cap = cap
+        self.x = layer.exchange_layout(cap)
+        self.buf = lbk.PeerBuffer(layer.ctx, self.x.total)
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.buf.handle, group=group)
+            ptrs = [self.buf.ptr if r == self.rank else self.buf.open(handles[r]) for r in range(self.world)]
+        else:
+            ptrs = [self.buf.ptr]
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        k, H, q8b = layer.top_k, layer.hidden, layer.q8_bytes
+        self.cap_items = self.world * cap * k
+        self.q8_items = torch.empty((self.cap_items, q8b), dtype=torch.uint8, device=dev)
+        self.items = torch.zeros((self.cap_items, 2), dtype=torch.int32, device=dev)
+        self.returns = torch.zeros(self.cap_items, dtype=torch.int64, device=dev)
+        self.count = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.dots = torch.empty((self.cap_items, H), dtype=torch.float32, device=dev)
+        self.ws = torch.zeros(layer.workspace_bytes(max(self.cap_items, cap)), dtype=torch.uint8, device=dev)
+        self._one = torch.ones(1, dtype=torch.float32, device=dev)
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            dist.all_reduce(self._one, op=dist.ReduceOp.MAX, group=self.group)
+
+    def forward(self, x: torch.Tensor, tokens: int, out: torch.Tensor) -> None:
+        """out[tokens * hidden] = the MoE layer on this rank's tokens (tokens <= cap)."""
+        L, b = self.layer, self.buf.ptr
+        L.publish(x, tokens, b, self.cap, self.ws)
+        self.barrier()
+        L.gather(self.peers, self.world, self.cap, self.q8_items, self.items, self.returns, self.count)
+        L.items_forward_counted(self.q8_items, self.items, self.count, self.dots, self.ws)
+        L.scatter(self.peers, self.cap, self.dots, self.returns, self.count)
+        self.barrier()
+        if tokens:
+            L.combine(b + self.x.q8, tokens, b + self.x.routing, b + self.x.dots, out, self.ws)
+
+    def close(self) -> None:
+        """Collective: every rank unmaps its peers' buffers before any buffer is freed."""
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+            self.buf.close_opened()
+            dist.barrier(group=self.group)
+        self.buf.close()

@@ -64,6 +64,11 @@ class Expert(ctypes.Structure):
     _fields_ = [("gate", Matrix), ("up", Matrix), ("down", Matrix)]
 
 
+class EpExchange(ctypes.Structure):
+    _fields_ = [("routing", ctypes.c_uint64), ("tokens", ctypes.c_uint64), ("q8", ctypes.c_uint64),
+                ("dots", ctypes.c_uint64), ("total", ctypes.c_uint64), ("q8_bytes", ctypes.c_uint64)]
+
+
 class Routed(ctypes.Structure):
     _fields_ = [("expert_id", ctypes.c_uint32), ("coefficient", ctypes.c_float)]
 
@@ -192,6 +197,15 @@ def _load() -> ctypes.CDLL:
         "lbk_ep_route": ([P, P, U64, P, P, P, U64, P], I32),
         "lbk_ep_items_forward": ([P, P, P, U64, P, P, U64, P], I32),
         "lbk_ep_combine": ([P, P, U64, P, P, P, P, U64, P], I32),
+        "lbk_peer_alloc": ([P, U64, ctypes.POINTER(P), ctypes.c_char_p], I32),
+        "lbk_peer_free": ([P, P], I32),
+        "lbk_peer_open": ([P, ctypes.c_char_p, ctypes.POINTER(P)], I32),
+        "lbk_peer_close": ([P, P], I32),
+        "lbk_ep_exchange_layout": ([P, U64, ctypes.POINTER(EpExchange)], I32),
+        "lbk_ep_publish": ([P, P, U64, P, U64, P, U64, P], I32),
+        "lbk_ep_gather": ([P, P, U32, U64, P, P, P, P, U64, P], I32),
+        "lbk_ep_items_forward_counted": ([P, P, P, P, U64, P, P, U64, P], I32),
+        "lbk_ep_scatter": ([P, P, U64, P, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
         "lbk_repack": ([P, PM, P, U64, P], I32),
@@ -224,7 +238,8 @@ EXPORTED = (
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
     "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward lbk_moe_block_route lbk_moe_block_finish "
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
-    "lbk_ep_items_forward lbk_ep_combine "
+    "lbk_ep_items_forward lbk_ep_combine lbk_peer_alloc lbk_peer_free lbk_peer_open lbk_peer_close "
+    "lbk_ep_exchange_layout lbk_ep_publish lbk_ep_gather lbk_ep_items_forward_counted lbk_ep_scatter "
     "lbk_repack lbk_unpack lbk_validate_matrix lbk_decode_rows "
     "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
     "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
@@ -245,6 +260,8 @@ def check(status: int) -> None:
 def _ptr(t) -> int | None:
     if t is None:
         return None
+    if isinstance(t, int):  # a raw device address (e.g. inside a PeerBuffer)
+        return t
     return t.data_ptr()
 
 
@@ -466,6 +483,61 @@ class EpLayer(MoeLayer):
     def combine(self, q8, tokens: int, routed, routed_dots, out, workspace, stream=None) -> None:
         check(lib.lbk_ep_combine(self.ptr, _ptr(q8), tokens, _ptr(routed), _ptr(routed_dots), _ptr(out),
                                  _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    # exchange over peer memory (lbk_ep_publish / gather / items_forward_counted / scatter)
+    def exchange_layout(self, cap: int) -> EpExchange:
+        x = EpExchange()
+        check(lib.lbk_ep_exchange_layout(self.ptr, cap, ctypes.byref(x)))
+        return x
+
+    def publish(self, x, tokens: int, xbuf: int, cap: int, workspace, stream=None) -> None:
+        check(lib.lbk_ep_publish(self.ptr, _ptr(x), tokens, xbuf, cap, _ptr(workspace), workspace.numel(),
+                                 _stream(stream)))
+
+    def gather(self, peers, world: int, cap: int, q8_items, items, returns, count, stream=None) -> None:
+        check(lib.lbk_ep_gather(self.ptr, _ptr(peers), world, cap, _ptr(q8_items), _ptr(items), _ptr(returns),
+                                _ptr(count), items.shape[0], _stream(stream)))
+
+    def items_forward_counted(self, q8_items, items, count, dots, workspace, stream=None) -> None:
+        check(lib.lbk_ep_items_forward_counted(self.ptr, _ptr(q8_items), _ptr(items), _ptr(count), items.shape[0],
+                                               _ptr(dots), _ptr(workspace), workspace.numel(), _stream(stream)))
+
+    def scatter(self, peers, cap: int, dots, returns, count, stream=None) -> None:
+        check(lib.lbk_ep_scatter(self.ptr, _ptr(peers), cap, _ptr(dots), _ptr(returns), _ptr(count),
+                                 returns.shape[0], _stream(stream)))
+
+
+class PeerBuffer:
+    """Device memory mapped into the other processes of the node
+    (lbk_peer_alloc / lbk_peer_open): plain peer loads and stores."""
+
+    def __init__(self, ctx: Context, nbytes: int):
+        self.ctx = ctx
+        p = ctypes.c_void_p()
+        h = ctypes.create_string_buffer(64)
+        check(lib.lbk_peer_alloc(ctx.ptr, nbytes, ctypes.byref(p), h))
+        self.ptr = p.value
+        self.handle = h.raw
+        self.nbytes = nbytes
+        self._opened: list[int] = []
+
+    def open(self, handle: bytes) -> int:
+        p = ctypes.c_void_p()
+        check(lib.lbk_peer_open(self.ctx.ptr, handle, ctypes.byref(p)))
+        self._opened.append(p.value)
+        return p.value
+
+    def close_opened(self) -> None:
+        """Unmap the other processes' buffers opened here."""
+        for q in self._opened:
+            lib.lbk_peer_close(self.ctx.ptr, q)
+        self._opened = []
+
+    def close(self) -> None:
+        self.close_opened()
+        if self.ptr:
+            lib.lbk_peer_free(self.ctx.ptr, self.ptr)
+            self.ptr = None
 
 
 class Gguf:

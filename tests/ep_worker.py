@@ -7,7 +7,9 @@ stages run on one rank holding every expert.
 
 --mode gpu: nccl ranks, one GPU each; the compute stages are lbk.EpLayer, and
 each rank's output must equal lbk_moe_forward of the whole layer on its own
-GPU bit for bit (routing identical).
+GPU bit for bit (routing identical), both with the exchange over collectives
+(ep.ExpertParallelMoe) and over IPC-mapped peer memory
+(ep.PeerExpertParallelMoe).
 
 Exits non-zero on any mismatch; rank 0 prints "ok" when every rank passed.
 """
@@ -150,6 +152,17 @@ def gpu_case(rank, world, E, H, F, k, tokens_per_rank, seed):
         ctx.raise_status()
         assert torch.equal(routed[: T * k * 2].cpu(), wr.cpu()), f"rank {rank}: routing differs"
         assert torch.equal(out[: T * H].view(torch.int32).cpu(), want.view(torch.int32).cpu()), f"rank {rank}: output differs"
+    # the same layer step with the exchange over peer memory (IPC-mapped buffers)
+    peer = ep.PeerExpertParallelMoe(epl, max(tokens_per_rank))
+    for step in range(3):  # later steps reuse the buffers
+        out.fill_(float("nan"))
+        peer.forward(x, T, out)
+        torch.cuda.synchronize(dev)
+        ctx.raise_status()
+        if T:
+            assert torch.equal(out[: T * H].view(torch.int32).cpu(), want.view(torch.int32).cpu()), \
+                f"rank {rank}: peer exchange output differs (step {step})"
+    peer.close()
     epl.close()
     full.close()
 

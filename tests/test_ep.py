@@ -275,3 +275,54 @@ def test_grouped_expert_parallel_equals_ungrouped_forward(world, T):
     full.close()
     for r in ranks:
         r.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,H,F,E,k,tokens", [(1, 4096, 1536, 24, 8, (3,)), (2, 4096, 1536, 48, 8, (1, 2)),
+                                                  (4, 2048, 512, 16, 4, (6, 0, 3, 5)),
+                                                  (8, 4096, 256, 64, 8, (2, 1, 0, 2, 2, 1, 2, 2))])
+def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens):
+    """The peer-memory exchange (lbk_ep_publish / gather / items_forward_counted
+    / scatter / combine) with `world` ranks on one GPU: each rank's exchange
+    buffer is device memory of this process, addressed by every rank as its
+    peers would address it, each rank with its own tokens (one with none).
+    Every rank's output equals lbk_moe_forward on its tokens bit for bit."""
+    from gpu_helpers import clean_status, dev
+
+    full, ranks, keep, rng = _gpu_layers(H, F, E, k, 13 * H + F + E + world, world)
+    cap = max(tokens)
+    xl = ranks[0].exchange_layout(cap)
+    bufs = [torch.zeros(xl.total, dtype=torch.uint8, device="cuda") for _ in range(world)]
+    peers = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    cap_items = world * cap * k
+    q8b = ranks[0].q8_bytes
+    ws = [torch.zeros(ranks[0].workspace_bytes(max(cap_items, cap)), dtype=torch.uint8, device="cuda")
+          for _ in range(world)]
+    xs = [dev(rng.standard_normal(max(T, 1) * H).astype(np.float32)) for T in tokens]
+    for r in range(world):
+        ranks[r].publish(xs[r], tokens[r], bufs[r].data_ptr(), cap, ws[r])
+    for r in range(world):
+        q8_items = torch.empty((cap_items, q8b), dtype=torch.uint8, device="cuda")
+        items = torch.zeros((cap_items, 2), dtype=torch.int32, device="cuda")
+        returns = torch.zeros(cap_items, dtype=torch.int64, device="cuda")
+        count = torch.zeros(1, dtype=torch.int32, device="cuda")
+        dots = torch.empty((cap_items, H), dtype=torch.float32, device="cuda")
+        ranks[r].gather(peers, world, cap, q8_items, items, returns, count)
+        ranks[r].items_forward_counted(q8_items, items, count, dots, ws[r])
+        ranks[r].scatter(peers, cap, dots, returns, count)
+    clean_status()
+    for r in range(world):
+        T = tokens[r]
+        if T == 0:
+            continue
+        b = bufs[r].data_ptr()
+        out = torch.full((T * H,), float("nan"), device="cuda")
+        ranks[r].combine(b + xl.q8, T, b + xl.routing, b + xl.dots, out, ws[r])
+        clean_status()
+        want, wr = _full_forward(full, xs[r][:T * H], T)
+        got_routing = bufs[r][xl.routing:xl.routing + T * k * 8].view(torch.int32)
+        assert torch.equal(got_routing.cpu(), wr.cpu()), f"rank {r} routing"
+        assert torch.equal(out.view(torch.int32).cpu(), want.view(torch.int32).cpu()), f"rank {r} output"
+    full.close()
+    for r in ranks:
+        r.close()
