@@ -25,9 +25,16 @@ cpu_baseline: the CPU restatement of the reference's AVX2 path (oracle/),
 With N>1 GPUs every rank runs its own resident copy of the layers on its own
 tokens (replicas; weak scaling).
 
---config 4 measures the batched layer instead: 64 tokens per step per GPU,
-experts sharded over the GPUs (192 / N each), dispatch and return by NCCL
-all-to-all (lightbridge-engine_b200/ep.py); weak scaling.
+ep      : at every N, config 4's layer step with the experts sharded over the
+          N GPUs (192 / N each), 64 tokens per GPU, dispatch and return over
+          peer memory (lightbridge-engine_b200/ep.py, PeerExpertParallelMoe):
+          tokens/s, per-stage times (dispatch, return), gpus_active. `value`
+          stays the config-3 line, so the scaling run's efficiency reflects
+          replicas of config 3; the `ep` record's tokens/s is the expert-
+          parallel curve.
+
+--config 4 measures that batched layer as the line itself (--exchange nccl:
+the NCCL all-to-all exchange instead); weak scaling.
 """
 
 from __future__ import annotations
@@ -448,6 +455,11 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
     e2e_value = e2e_steps * TOKENS_PER_STEP * world / (e2e_ms / 1000.0)
     ctx.raise_status(stream.cuda_stream)
 
+    # expert parallelism at this N: config 4's layer step over the peer exchange
+    ep_rec = None
+    if not args.no_ep:
+        ep_rec = ep_peer_measure(ctx, lbk, torch, dev, rank, world, min(args.steps, 50), 3)
+
     cpu = None
     if rank == 0 and world == 1 and host0 is not None and not args.no_cpu_baseline:
         cpu = cpu_baseline(host0, x_host.numpy()[:16])
@@ -491,6 +503,7 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
             "gpu_launches": args.steps * TOKENS_PER_STEP * 3,
             "clocks": clk,
             "cpu_baseline": cpu,
+            "ep": ep_rec,
         }
         print(json.dumps(line), flush=True)
     del graph
@@ -561,6 +574,127 @@ def build_ep_layer(ctx, lbk, torch, dev, seed: int, first: int, count: int):
     return lbk.EpLayer(ctx, experts, shared, rm, bias, K_TOP, WEIGHT_SCALE, E, first), keep
 
 
+EP_LAYERS = 4  # config 4 through the peer exchange: resident EP layers a step rotates over
+
+
+def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, warmup: int, grouping=None) -> dict:
+    """Config 4 through the peer-memory exchange (ep.PeerExpertParallelMoe):
+    BATCH_TOKENS tokens per rank per layer step, experts sharded E / world per
+    GPU, EP_LAYERS resident layers per rank so that a step's weights exceed
+    L2 at every N (at N = 8, 24 experts are 160 MB per layer). One CUDA graph
+    holds EP_LAYERS layer steps (no host work, no collective inside); timed
+    with CUDA events, max over ranks. Then one pass with events between the
+    stages of every layer step gives each stage's time (a stage's time on a
+    rank includes its wait for the other ranks)."""
+    import torch.distributed as dist
+
+    import ep
+
+    T = BATCH_TOKENS
+    er = E // world
+    layers = [build_ep_layer(ctx, lbk, torch, dev, 4 + 1000 * rank + 17 * i, rank * er, er) for i in range(EP_LAYERS)]
+    if grouping is not None:
+        for L, _ in layers:
+            L.set_grouping(grouping)
+    stream = torch.cuda.Stream(device=dev)
+    moe = ep.PeerExpertParallelMoe(layers[0][0], T, stream=stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 + rank)
+    xs = torch.randn(EP_LAYERS, T * H, device=dev, generator=gen)
+    out = torch.empty(EP_LAYERS, T * H, device=dev)
+
+    def step():
+        for i, (L, _) in enumerate(layers):
+            moe.forward(xs[i], T, out[i], layer=L)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[dev.index])
+
+    with torch.cuda.stream(stream):
+        step()  # sets kernel attributes outside capture
+    barrier()
+    ctx.raise_status()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    barrier()
+    for _ in range(warmup):
+        graph.replay()
+    barrier()
+    ctx.raise_status()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    barrier()
+    ctx.raise_status()
+    ms_layer = e0.elapsed_time(e1) / (steps * EP_LAYERS)
+
+    # stage times: events between the stages, 8 passes over the layers
+    names = ["route", "dispatch", "experts", "return", "combine"]
+    stages = [moe.publish, moe.dispatch, moe.compute, moe.send_back, moe.combine]
+    acc = [0.0] * len(names)
+    passes = 8
+    for _ in range(passes):
+        for i, (L, _) in enumerate(layers):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+            with torch.cuda.stream(stream):
+                ev[0].record(stream)
+                stages[0](xs[i], T, L)
+                ev[1].record(stream)
+                stages[1](L)
+                ev[2].record(stream)
+                stages[2](L)
+                ev[3].record(stream)
+                stages[3](L)
+                ev[4].record(stream)
+                stages[4](T, out[i], L)
+                ev[5].record(stream)
+            stream.synchronize()
+            for j in range(len(names)):
+                acc[j] += ev[j].elapsed_time(ev[j + 1])
+    barrier()
+    ctx.raise_status()
+    stage_ms = [a / (passes * EP_LAYERS) for a in acc]
+    items = int(moe.count.item())
+    t = torch.tensor([ms_layer] + stage_ms + [float(items > 0), float(items)], device=dev)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+    else:
+        tmax = tsum = t
+    ms_layer = float(tmax[0])
+    stage_max = {n: float(tmax[1 + j]) for j, n in enumerate(names)}
+    del graph
+    moe.close()
+    for L, _ in layers:
+        L.close()
+    return {
+        "tokens_per_s": T * world / (ms_layer / 1000.0),
+        "unit": "tokens/s (layer steps of config 4: 64 tokens per GPU)",
+        "ms_per_layer_step": ms_layer,
+        "n_gpus": world,
+        "gpus_active": int(tsum[1 + len(names)]),
+        "experts_per_gpu": er,
+        "pairs_per_gpu_mean": float(tsum[2 + len(names)]) / world,
+        "stage_ms_max_over_ranks": stage_max,
+        "dispatch_ms": stage_max["dispatch"],
+        "return_ms": stage_max["return"],
+        "limiter": max(stage_max, key=stage_max.get),
+        "exchange": "peer memory over NVLink (CUDA IPC; plain peer loads and stores; step flags in the buffers, "
+                    "no collective, no host read; one CUDA graph per step)",
+        "stage_timing": "separate pass with events between stages; a stage's time includes its wait for other ranks",
+        "l2": f"{EP_LAYERS} resident layers per rank rotate within a step",
+        "steps": steps,
+    }
+
+
 def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
     """Config 4: the routed-MoE layer on BATCH_TOKENS tokens per step per rank,
     experts sharded in contiguous ranges over the ranks (E / world each), the
@@ -578,6 +712,35 @@ def batched_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(dev)
     ctx = lbk.Context(local_rank)
     er = E // world
+    if args.exchange == "peer":
+        clocks = Clocks(local_rank)
+        clocks.start()
+        r = ep_peer_measure(ctx, lbk, torch, dev, rank, world, args.steps, args.warmup, args.grouping)
+        clk = clocks.stop()
+        if rank == 0:
+            print(json.dumps({
+                "metric": "routed-MoE batched tokens/s (config 4: 64 tokens per step per GPU, expert-parallel)",
+                "value": r["tokens_per_s"],
+                "unit": "tokens/s",
+                "n_gpus": world,
+                "steps": args.steps,
+                "warmup": args.warmup,
+                "ms_per_step": r["ms_per_layer_step"],
+                "higher_is_better": True,
+                "scaling": "weak",
+                "vs_baseline": None,
+                "dtype": "q8_k x packed (int8 dots, f32 tails)",
+                "data": "synthetic (seeded, config shapes)",
+                "config": {"workload": "config4: routed-MoE FFN layer, 64 tokens per step per GPU", "hidden": H,
+                           "experts": E, "experts_per_gpu": er, "expert_ffn": F, "top_k": K_TOP,
+                           "tokens_per_step_per_gpu": T, "parallelism": f"expert-parallel x{world}",
+                           "l2": r["l2"], "exchange": r["exchange"]},
+                "ep": r,
+                "gpu_launches": None,
+                "clocks": clk,
+            }), flush=True)
+        ctx.close()
+        return
     layer, keep = build_ep_layer(ctx, lbk, torch, dev, 4 + 1000 * rank, rank * er, er)
     if args.grouping is not None:
         layer.set_grouping(args.grouping)
@@ -789,6 +952,116 @@ def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
     ctx.close()
 
 
+def stack_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
+    """Config 5 over N GPUs: the STACK_LAYERS-layer stack with every layer's
+    experts sharded E / N per GPU (24 on 8 GPUs), router and shared expert on
+    every GPU. Every rank decodes its own args.batch tokens through all
+    layers: hidden += MoE(RMSNorm(hidden)), the MoE step through the peer
+    exchange (ep.PeerExpertParallelMoe: route, dispatch, experts, return,
+    combine; one set of exchange buffers for all layers); one CUDA graph per
+    step, no host work or collective inside. Weak scaling: N * batch tokens
+    per step."""
+    import torch
+    import torch.distributed as dist
+
+    import ep
+    import lbk
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    ctx = lbk.Context(local_rank)
+    B = args.batch
+    er = E // world
+    layers = [build_ep_layer(ctx, lbk, torch, dev, 4 + l + 1000 * rank, rank * er, er) for l in range(args.stack_layers)]
+    if args.grouping is not None:
+        for L, _ in layers:
+            L.set_grouping(args.grouping)
+    stream = torch.cuda.Stream(device=dev)
+    moe = ep.PeerExpertParallelMoe(layers[0][0], B, stream=stream.cuda_stream)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3 + rank)
+    hidden = torch.randn(B * H, device=dev, generator=gen)
+    normed = torch.empty(B * H, device=dev)
+    delta = torch.empty(B * H, device=dev)
+    norm_w = torch.ones(H, device=dev)
+
+    def step():
+        for L, _ in layers:
+            ctx.rms_norm(hidden, norm_w, H, B, 1e-6, normed, mode=lbk.ROUTER_TREE, stream=stream.cuda_stream)
+            moe.forward(normed, B, delta, layer=L)
+            ctx.residual_add(hidden, delta, B * H, stream=stream.cuda_stream)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    with torch.cuda.stream(stream):
+        step()
+    barrier()
+    ctx.raise_status()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    barrier()
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier()
+    ctx.raise_status()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        st.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        en.record(stream)
+    barrier()
+    clk = clocks.stop()
+    ctx.raise_status()
+    ms = st.elapsed_time(en) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # weights a GPU streams per step: its experts touched by the step's pairs (at most all of its
+    # E / N), the shared expert and the router, per layer
+    per_expert = 2 * row_bytes(TYPE_IQ2_S, H) * F + row_bytes(TYPE_IQ3_S, F) * H
+    shared_b = 2 * row_bytes(TYPE_Q4_K, H) * F + row_bytes(TYPE_Q4_K, F) * H
+    touched = er * (1.0 - (1.0 - K_TOP / E) ** (B * world))
+    bytes_step = args.stack_layers * (touched * per_expert + shared_b + E * H * 4)
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"routed-MoE stack decode tokens/s (config 5: {args.stack_layers} layers, batch {B} per GPU)",
+            "value": B * world / (ms / 1000.0),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "q8_k x packed (int8 dots, f32 tails)",
+            "data": "synthetic (seeded, config shapes)",
+            "config": {"workload": f"config5: {args.stack_layers}-layer stack, batch {B} per GPU, expert-parallel",
+                       "layers": args.stack_layers, "batch_per_gpu": B, "experts_per_gpu": er,
+                       "resident_gb_per_gpu": round(args.stack_layers * (er * per_expert + shared_b + E * H * 4) / 1e9, 1),
+                       "us_per_layer_step": ms * 1000.0 / args.stack_layers,
+                       "parallelism": f"expert-parallel x{world}",
+                       "exchange": "peer memory over NVLink (ep.PeerExpertParallelMoe), one CUDA graph per step"},
+            "hbm_gbs_per_gpu_expected_touched": bytes_step / (ms / 1000.0) / 1e9,
+            "clocks": clk,
+        }), flush=True)
+    del graph
+    moe.close()
+    for L, _ in layers:
+        L.close()
+    ctx.close()
+
+
 def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
     """Config 5: a stack of STACK_LAYERS config-3 MoE blocks (attention
     omitted), per-layer random weights from seed 4 + layer, all HBM-resident
@@ -878,6 +1151,9 @@ def main() -> None:
                          "1, 2: single quantized matvec; 5: 80-layer stack")
     ap.add_argument("--direct", action="store_true",
                     help="config 4: all experts on every GPU, one lbk_moe_forward call per layer (no expert parallelism)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="config 4: expert-parallel exchange over peer memory (default) or NCCL all-to-all")
+    ap.add_argument("--no-ep", action="store_true", help="config 3: skip the expert-parallel sub-record")
     ap.add_argument("--grouping", type=int, default=None,
                     help="configs 4, 5: token count from which the grouped kernels run (0: never; default: the library's)")
     ap.add_argument("--profile-forwards", type=int, default=0,
@@ -908,6 +1184,8 @@ def main() -> None:
             batched_ep_arm(args, rank, world, local_rank)
         elif args.config in (1, 2):
             gemv_arm(args, args.config, rank, world, local_rank)
+        elif args.config == 5 and world > 1:
+            stack_ep_arm(args, rank, world, local_rank)
         elif args.config == 5:
             stack_arm(args, rank, world, local_rank)
         else:

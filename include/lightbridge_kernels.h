@@ -418,9 +418,10 @@ int32_t lbk_ep_items_forward(lbk_moe_layer* layer, const uint8_t* q8_items, cons
 int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens, const lbk_routed* routed,
                        const float* routed_dots, float* out, void* workspace, uint64_t workspace_bytes, void* stream);
 
-/* Expert-parallel exchange over peer memory: no size exchange and no
- * device-to-host read in a layer step (none of this has a counterpart in the
- * reference, whose MoE step runs every expert on one host).
+/* Expert-parallel exchange over peer memory: no collective, no size exchange
+ * and no device-to-host read in a layer step, so a step can be captured in a
+ * CUDA graph (none of this has a counterpart in the reference, whose MoE step
+ * runs every expert on one host).
  *
  * Peer buffers: lbk_peer_alloc allocates and zero-fills `bytes` of device
  * memory and returns its 64-byte interprocess handle; another process of the
@@ -429,25 +430,35 @@ int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens,
  * with lbk_peer_free.
  *
  * Exchange buffer of a rank (lbk_ep_exchange_layout, `cap` tokens per rank at
- * most): the routing, the token count, the Q8_K images and the routed row
- * dots returned by the other ranks. A layer step on every rank:
- *   lbk_ep_publish   route this rank's tokens into its own buffer;
- *   (barrier: every rank has published)
- *   lbk_ep_gather    collect from every rank's buffer (device array `peers`
- *                    of `world` pointers) the pairs routed to this rank's
- *                    experts: items (local expert ID), their Q8_K images,
- *                    their return addresses {rank, t * k + j} (uint64 each),
- *                    and their count, on the device;
+ * most; zero-filled before the first step): the routing, a 512-byte control
+ * block (token count and step flags), the Q8_K images and the routed row dots
+ * returned by the other ranks. `peers` is a device array of `world` (at most
+ * 64) buffer pointers as this GPU addresses them, indexed by rank. A layer
+ * step, every call on every rank once, in this order, on one stream:
+ *   lbk_ep_publish   route this rank's tokens into its own buffer and
+ *                    publish them (this rank's step number + 1);
+ *   lbk_ep_gather    wait until every rank has published this step, then
+ *                    collect the pairs routed to this rank's experts: items
+ *                    (local expert ID), their Q8_K images, their return
+ *                    addresses {rank, t * k + j} (uint64 each) and their
+ *                    count, on the device;
  *   lbk_ep_items_forward_counted  the items' row dots (as
  *                    lbk_ep_items_forward, the count read on the device;
  *                    cap_items = world * cap * k bounds it);
- *   lbk_ep_scatter   each item's dots into its home rank's buffer;
- *   (barrier: every rank has scattered)
- *   lbk_ep_combine   on the home rank, from its buffer's routing, images and
- *                    dots: bit-identical to lbk_moe_forward on one GPU. */
+ *   lbk_ep_scatter   each item's dots into its home rank's buffer, then flag
+ *                    this rank's step done in every buffer;
+ *   lbk_ep_combine_exchange  on the home rank: wait until every rank's dots
+ *                    of this step are in, then combine from its buffer's
+ *                    routing, images and dots, bit-identical to
+ *                    lbk_moe_forward on one GPU (a rank without tokens still
+ *                    calls it: the wait frees its buffer for the next step).
+ * The waits poll at most the layer's wait limit
+ * (lbk_moe_layer_set_wait_limit) times; one that runs out is reported as
+ * LBK_TIMEOUT through the status word (index 8: gather, 9: combine; bits: the
+ * step) and the kernels still finish. */
 typedef struct lbk_ep_exchange {
-    uint64_t routing, tokens, q8, dots, total; /* byte offsets in a buffer, its size */
-    uint64_t q8_bytes;                         /* one token's Q8_K image */
+    uint64_t routing, control, q8, dots, total; /* byte offsets in a buffer, its size */
+    uint64_t q8_bytes;                          /* one token's Q8_K image */
 } lbk_ep_exchange;
 int32_t lbk_peer_alloc(lbk_context* ctx, uint64_t bytes, void** ptr, uint8_t handle[64]);
 int32_t lbk_peer_free(lbk_context* ctx, void* ptr);
@@ -456,13 +467,17 @@ int32_t lbk_peer_close(lbk_context* ctx, void* ptr);
 int32_t lbk_ep_exchange_layout(const lbk_moe_layer* layer, uint64_t cap, lbk_ep_exchange* out);
 int32_t lbk_ep_publish(lbk_moe_layer* layer, const float* x, uint64_t tokens, void* xbuf, uint64_t cap, void* workspace,
                        uint64_t workspace_bytes, void* stream);
-int32_t lbk_ep_gather(lbk_moe_layer* layer, const void* const* peers, uint32_t world, uint64_t cap, uint8_t* q8_items,
-                      lbk_routed* items, uint64_t* returns, uint32_t* count, uint64_t cap_items, void* stream);
+int32_t lbk_ep_gather(lbk_moe_layer* layer, const void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,
+                      uint8_t* q8_items, lbk_routed* items, uint64_t* returns, uint32_t* count, uint64_t cap_items,
+                      void* stream);
 int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t* q8_items, const lbk_routed* items,
                                      const uint32_t* count, uint64_t cap_items, float* dots, void* workspace,
                                      uint64_t workspace_bytes, void* stream);
-int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint64_t cap, const float* dots,
-                       const uint64_t* returns, const uint32_t* count, uint64_t cap_items, void* stream);
+int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,
+                       const float* dots, const uint64_t* returns, const uint32_t* count, uint64_t cap_items,
+                       void* stream);
+int32_t lbk_ep_combine_exchange(lbk_moe_layer* layer, void* xbuf, uint32_t world, uint64_t cap, uint64_t tokens,
+                                float* out, void* workspace, uint64_t workspace_bytes, void* stream);
 
 /* lbk_moe_forward without a caller workspace and without any allocation: the
  * workspace is a fixed 1 MiB array of this library's device memory, one per

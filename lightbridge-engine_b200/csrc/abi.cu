@@ -1677,12 +1677,20 @@ lbk_ep_exchange ep_exchange(const lbk_moe_layer* L, uint64_t cap) {
     lbk_ep_exchange x{};
     const uint64_t q8b = L->H / LBK_QK_K * lbk::kQ8IBytes;
     x.routing = 0;
-    x.tokens = up256(cap * L->k * sizeof(lbk_routed));
-    x.q8 = x.tokens + 256;
+    x.control = up256(cap * L->k * sizeof(lbk_routed));
+    x.q8 = x.control + 512;
     x.dots = up256(x.q8 + cap * q8b);
     x.total = up256(x.dots + cap * L->k * L->H * 4);
     x.q8_bytes = q8b;
     return x;
+}
+
+int32_t ep_check_ranks(uint32_t world, uint32_t rank, uint64_t cap) {
+    if (world == 0 || world > lbk::kEpMaxRanks)
+        return fail(LBK_DIMENSION_MISMATCH, "ranks", 0, lbk::kEpMaxRanks, world);
+    if (rank >= world) return fail(LBK_DIMENSION_MISMATCH, "rank", 0, world - 1, rank);
+    if (cap == 0) return fail(LBK_DIMENSION_MISMATCH, "tokens per rank", 0, 1, 0);
+    return LBK_OK;
 }
 }  // namespace
 
@@ -1707,26 +1715,28 @@ LBK_API int32_t lbk_ep_publish(lbk_moe_layer* layer, const float* x, uint64_t to
     } else if (int32_t s = set_device(layer->ctx)) {
         return s;
     }
-    cudaError_t e = lbk::launch_ep_set_tokens(reinterpret_cast<uint32_t*>(xb + xl.tokens), (uint32_t)tokens, as_stream(stream));
-    return e == cudaSuccess ? ok() : cuda_fail(e, "token count store");
+    cudaError_t e = lbk::launch_ep_publish(reinterpret_cast<lbk::EpControl*>(xb + xl.control), (uint32_t)tokens,
+                                           as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "publish launch");
 }
 
-LBK_API int32_t lbk_ep_gather(lbk_moe_layer* layer, const void* const* peers, uint32_t world, uint64_t cap,
-                              uint8_t* q8_items, lbk_routed* items, uint64_t* returns, uint32_t* count,
+LBK_API int32_t lbk_ep_gather(lbk_moe_layer* layer, const void* const* peers, uint32_t world, uint32_t rank,
+                              uint64_t cap, uint8_t* q8_items, lbk_routed* items, uint64_t* returns, uint32_t* count,
                               uint64_t cap_items, void* stream) {
     if (layer == nullptr || peers == nullptr || q8_items == nullptr || items == nullptr || returns == nullptr ||
         count == nullptr)
         return fail(LBK_INVALID_PARAMETER, "null pointer");
-    if (world == 0 || cap == 0) return fail(LBK_DIMENSION_MISMATCH, "ranks / tokens per rank", 0, 1, 0);
+    if (int32_t s = ep_check_ranks(world, rank, cap)) return s;
     if (cap_items < world * cap * layer->k)
         return fail(LBK_SCRATCH_TOO_SMALL, "item capacity", 0, world * cap * layer->k, cap_items);
     if (!aligned(q8_items, 16)) return fail(LBK_INVALID_PARAMETER, "q8 items 16-byte alignment");
     lbk_context* ctx = layer->ctx;
     if (int32_t s = set_device(ctx)) return s;
     const lbk_ep_exchange xl = ep_exchange(layer, cap);
-    lbk::EpGatherArgs a{reinterpret_cast<const uint8_t* const*>(peers), world, (uint32_t)cap, (uint32_t)layer->k,
-                        (uint32_t)xl.q8_bytes, xl.tokens, xl.q8, (uint32_t)layer->first, (uint32_t)layer->E_local,
-                        q8_items, items, reinterpret_cast<uint2*>(returns), count, (uint32_t)cap_items};
+    lbk::EpGatherArgs a{reinterpret_cast<const uint8_t* const*>(peers), world, rank, (uint32_t)cap, (uint32_t)layer->k,
+                        (uint32_t)xl.q8_bytes, xl.control, xl.q8, (uint32_t)layer->first, (uint32_t)layer->E_local,
+                        q8_items, items, reinterpret_cast<uint2*>(returns), count, (uint32_t)cap_items,
+                        layer->wait_limit, ctx->status};
     cudaError_t e = lbk::launch_ep_gather(a, ctx->sm_count, as_stream(stream));
     return e == cudaSuccess ? ok() : cuda_fail(e, "gather launch");
 }
@@ -1751,18 +1761,53 @@ LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t
     return moe_experts(layer, nullptr, cap_items, items, nullptr, ws, o, st, false, m);
 }
 
-LBK_API int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint64_t cap, const float* dots,
-                               const uint64_t* returns, const uint32_t* count, uint64_t cap_items, void* stream) {
+LBK_API int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,
+                               const float* dots, const uint64_t* returns, const uint32_t* count, uint64_t cap_items,
+                               void* stream) {
     if (layer == nullptr || peers == nullptr || dots == nullptr || returns == nullptr || count == nullptr)
         return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (int32_t s = ep_check_ranks(world, rank, cap)) return s;
     if (!aligned(dots, 16) || layer->H % 4) return fail(LBK_INVALID_PARAMETER, "dots 16-byte alignment");
     lbk_context* ctx = layer->ctx;
     if (int32_t s = set_device(ctx)) return s;
     const lbk_ep_exchange xl = ep_exchange(layer, cap);
-    lbk::EpScatterArgs a{reinterpret_cast<uint8_t* const*>(peers), xl.dots, dots, reinterpret_cast<const uint2*>(returns),
-                         count, (uint32_t)cap_items, (uint32_t)layer->H};
+    lbk::EpScatterArgs a{reinterpret_cast<uint8_t* const*>(peers), world, rank, xl.control, xl.dots, dots,
+                         reinterpret_cast<const uint2*>(returns), count, (uint32_t)cap_items, (uint32_t)layer->H};
     cudaError_t e = lbk::launch_ep_scatter(a, ctx->sm_count, as_stream(stream));
     return e == cudaSuccess ? ok() : cuda_fail(e, "scatter launch");
+}
+
+LBK_API int32_t lbk_ep_combine_exchange(lbk_moe_layer* layer, void* xbuf, uint32_t world, uint64_t cap,
+                                        uint64_t tokens, float* out, void* workspace, uint64_t workspace_bytes,
+                                        void* stream) {
+    if (layer == nullptr || xbuf == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (int32_t s = ep_check_ranks(world, 0, cap)) return s;
+    if (tokens > cap) return fail(LBK_DIMENSION_MISMATCH, "tokens beyond the exchange capacity", 0, cap, tokens);
+    if (tokens) {  // a rank without tokens only waits
+        if (out == nullptr) return fail(LBK_INVALID_PARAMETER, "null output");
+        if (int32_t s = ep_check(layer, tokens, workspace, workspace_bytes, ep_ws_bytes(layer, tokens))) return s;
+    }
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    const lbk_ep_exchange xl = ep_exchange(layer, cap);
+    uint8_t* xb = static_cast<uint8_t*>(xbuf);
+    const lbk_routed* routed = reinterpret_cast<const lbk_routed*>(xb + xl.routing);
+    const WsLayout o = moe_ws(layer, tokens, 0);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    float* shared_dots = reinterpret_cast<float*>(ws + o.total);
+    if (tokens) {
+        cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
+        if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+        if (int32_t s = moe_experts(layer, nullptr, tokens, routed, nullptr, ws, o, st, false,
+                                    MoeMode{0, true, false, xb + xl.q8, shared_dots, 1}))
+            return s;
+    }
+    cudaError_t e = lbk::launch_ep_combine_wait(reinterpret_cast<const lbk::EpControl*>(xb + xl.control), world,
+                                                layer->wait_limit, routed,
+                                                reinterpret_cast<const float*>(xb + xl.dots), shared_dots, out, tokens,
+                                                layer->k, layer->H, ctx->status, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "combine launch");
 }
 
 LBK_API int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens, const lbk_routed* routed,

@@ -2,17 +2,26 @@
 //
 // Every rank owns one exchange buffer, mapped into every other rank of the
 // node (CUDA IPC, plain peer loads and stores; no multicast):
-//   [routing: cap * k lbk_routed][tokens: u32, padded to 256]
+//   [routing: cap * k lbk_routed][control block: EpControl, 512 bytes]
 //   [Q8_K images: cap * q8b][routed dots: cap * k * H f32]
-// A layer step: the home rank routes its tokens into its own buffer
-// (routing, images, token count); after a barrier, each rank gathers from
-// every buffer the (token, slot) pairs routed to its experts -- their images
-// copied over NVLink into a local item list, the count kept on the device;
-// computes them (the item kernels read the count on the device); scatters
-// each item's row dots straight into the home rank's buffer at
-// routed_dots[t * k + j]; after a second barrier the home rank combines in
-// ascending expert ID, so no size exchange and no device-to-host read is
-// needed, and only the bytes the pairs need cross NVLink.
+// A layer step, with no collective and no host involvement:
+//   publish  the home rank routes its tokens into its own buffer, then raises
+//            its step number and releases `published` = step;
+//   gather   each rank waits until every buffer is published for this step,
+//            then copies the (token, slot) pairs routed to its experts -- their
+//            images over NVLink into a local item list, the count kept on the
+//            device;
+//   (items)  the item kernels read the count on the device;
+//   scatter  each item's row dots go straight into the home rank's buffer at
+//            routed_dots[t * k + j]; the scatter's last CTA then releases
+//            done[rank] = step in every buffer;
+//   combine  the home rank waits until done[r] = step for every rank r and
+//            adds the dots in ascending expert ID (the one-GPU order).
+// Only the bytes the pairs need cross NVLink. A buffer is not overwritten
+// while a peer still reads it: a rank publishes step s + 1 only after its
+// combine of step s saw every rank's scatter of step s, which follows that
+// rank's gather of step s. Every wait is bounded (LBK_TIMEOUT through the
+// status word; the kernels still finish).
 
 #include "lbk_kernels.h"
 #include "lbk_moe.h"
@@ -23,20 +32,51 @@ namespace {
 
 constexpr int kGatherWarps = 8;
 
+__device__ __forceinline__ const EpControl* ctl_of(const uint8_t* buf, uint64_t off) {
+    return reinterpret_cast<const EpControl*>(buf + off);
+}
+
+// Wait until `flag` reaches `step` (wrapping compare), at most `polls` polls;
+// none once an error is recorded (a rank that stopped would otherwise cost
+// every later wait its full limit).
+__device__ __forceinline__ bool wait_step(const uint32_t* flag, uint32_t step, uint32_t polls, const DeviceStatus* st) {
+    for (uint32_t i = 0; i < polls; i++) {
+        if ((int32_t)(ld_acquire_sys(flag) - step) >= 0) return true;
+        if ((i & 255u) == 0u && status_set(st)) return false;
+        __nanosleep(64);
+    }
+    return false;
+}
+
 // One warp per (rank, token): the token's k routing entries; each entry whose
 // expert is local becomes an item (slot from an atomic counter), its image
-// copied from the home buffer in 16-byte words.
+// copied from the home buffer in 16-byte words. Warp 0 of every CTA first
+// waits for every rank's publication of this step.
 __global__ void __launch_bounds__(kGatherWarps * 32) ep_gather_kernel(EpGatherArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ int s_ok;
+    if (warp == 0) {
+        const uint32_t step = __ldcg(&ctl_of(a.peers[a.rank], a.off_ctl)->step);
+        bool ok = true;
+        for (uint32_t r = lane; r < a.world; r += 32)
+            ok &= wait_step(&ctl_of(a.peers[r], a.off_ctl)->published, step, a.polls, a.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (lane == 0) {
+            s_ok = ok;
+            if (!ok) report(a.status, LBK_TIMEOUT, 8, step);
+        }
+    }
+    __syncthreads();  // the flags' acquire before every warp's reads of the buffers
+    if (!s_ok) return;
     const uint64_t pairs_total = (uint64_t)a.world * a.cap;
     for (uint64_t w = (uint64_t)blockIdx.x * kGatherWarps + warp; w < pairs_total;
          w += (uint64_t)gridDim.x * kGatherWarps) {
         const uint32_t s = (uint32_t)(w / a.cap), t = (uint32_t)(w % a.cap);
         const uint8_t* buf = a.peers[s];
-        const uint32_t ntok = __ldcg(reinterpret_cast<const uint32_t*>(buf + a.off_ntok));
+        const uint32_t ntok = __ldcg(&ctl_of(buf, a.off_ctl)->tokens);
         if (t >= ntok) continue;
         const lbk_routed* routing = reinterpret_cast<const lbk_routed*>(buf) + (uint64_t)t * a.k;
-        uint32_t mine = 0;  // bit j: slot j's expert is local
+        uint32_t mine = 0;  // slot `lane`'s expert is local
         uint32_t eid = 0;
         if ((uint32_t)lane < a.k) {
             eid = __ldcg(reinterpret_cast<const uint32_t*>(routing + lane));
@@ -62,8 +102,11 @@ __global__ void __launch_bounds__(kGatherWarps * 32) ep_gather_kernel(EpGatherAr
     }
 }
 
-// One CTA per item (grid-stride): its H row dots into the home buffer.
+// One CTA per item (grid-stride): its H row dots into the home buffer. The
+// last CTA to finish releases done[rank] = step in every rank's buffer.
 __global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterArgs a) {
+    EpControl* me = reinterpret_cast<EpControl*>(a.peers[a.rank] + a.off_ctl);
+    const uint32_t step = __ldcg(&me->step);
     const uint32_t n = __ldcg(a.d_count);
     for (uint32_t i = blockIdx.x; i < n && i < a.cap_items; i += gridDim.x) {
         const uint2 r = a.returns[i];
@@ -71,10 +114,27 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterArgs a) {
         float4* dst = reinterpret_cast<float4*>(a.peers[r.x] + a.off_dots) + (uint64_t)r.y * (a.hidden / 4);
         for (uint32_t q = threadIdx.x; q < a.hidden / 4; q += blockDim.x) dst[q] = __ldcg(src + q);
     }
-    __threadfence_system();  // the peer stores are visible before this grid is seen complete
+    __threadfence_system();  // this thread's peer stores before the CTA's arrival
+    __syncthreads();
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(&me->scatter_ctas, 1u) + 1u == gridDim.x;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence_system();  // the other CTAs' stores (seen through their arrivals) before the flags
+    if (threadIdx.x == 0) me->scatter_ctas = 0u;  // ready for the next step
+    for (uint32_t r = threadIdx.x; r < a.world; r += blockDim.x) {
+        EpControl* c = reinterpret_cast<EpControl*>(a.peers[r] + a.off_ctl);
+        st_release_sys(&c->done[a.rank], step);
+    }
 }
 
-__global__ void ep_set_tokens_kernel(uint32_t* p, uint32_t v) { *p = v; }
+// Raise this rank's step number; store the token count; publish.
+__global__ void ep_publish_kernel(EpControl* ctl, uint32_t tokens) {
+    const uint32_t step = ctl->step + 1u;
+    ctl->step = step;
+    ctl->tokens = tokens;
+    st_release_sys(&ctl->published, step);
+}
 
 }  // namespace
 
@@ -96,8 +156,8 @@ cudaError_t launch_ep_scatter(const EpScatterArgs& a, int sm_count, cudaStream_t
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_set_tokens(uint32_t* p, uint32_t v, cudaStream_t stream) {
-    ep_set_tokens_kernel<<<1, 1, 0, stream>>>(p, v);
+cudaError_t launch_ep_publish(EpControl* ctl, uint32_t tokens, cudaStream_t stream) {
+    ep_publish_kernel<<<1, 1, 0, stream>>>(ctl, tokens);
     return cudaGetLastError();
 }
 

@@ -151,20 +151,39 @@ cudaError_t launch_moe_down_grp(int down_type, int shared_down_type, const MoeDo
                                 cudaStream_t stream);
 
 // Expert-parallel exchange over peer memory (ep.cu).
+//
+// The control block of an exchange buffer: the token count and the flags
+// with which the ranks order a layer step among themselves, without the host.
+// `step` is this rank's step number (raised by the publish); `published` is
+// the step whose routing and images the buffer holds; done[r] is the step
+// whose row dots rank r has finished storing into this buffer.
+constexpr uint32_t kEpMaxRanks = 64;
+struct EpControl {
+    uint32_t tokens;
+    uint32_t published;
+    uint32_t step;
+    uint32_t scatter_ctas;  // CTAs of this rank's scatter that have finished (reset by the last)
+    uint32_t pad[12];
+    uint32_t done[kEpMaxRanks];
+};
+static_assert(sizeof(EpControl) <= 512, "control block");
 struct EpGatherArgs {
     const uint8_t* const* peers;  // [world] exchange buffers, as this GPU addresses them
-    uint32_t world, cap, k, q8b;  // cap: tokens per rank at most
-    uint64_t off_ntok, off_q8;    // offsets in an exchange buffer (routing at 0)
+    uint32_t world, rank, cap, k, q8b;  // cap: tokens per rank at most
+    uint64_t off_ctl, off_q8;     // offsets in an exchange buffer (routing at 0)
     uint32_t first, count;        // this rank's experts [first, first + count)
     uint8_t* q8_items;            // [cap_items][q8b]
     lbk_routed* items;            // [cap_items] local expert ID, coefficient 0
     uint2* returns;               // [cap_items] {home rank, pair t * k + j}
     uint32_t* d_count;            // items gathered (zeroed by the launcher)
     uint32_t cap_items;           // world * cap * k
+    uint32_t polls;               // polls of a peer's flag before LBK_TIMEOUT
+    DeviceStatus* status;
 };
 struct EpScatterArgs {
     uint8_t* const* peers;
-    uint64_t off_dots;
+    uint32_t world, rank;
+    uint64_t off_ctl, off_dots;
     const float* dots;            // [cap_items][hidden]
     const uint2* returns;
     const uint32_t* d_count;
@@ -172,6 +191,11 @@ struct EpScatterArgs {
 };
 cudaError_t launch_ep_gather(const EpGatherArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_ep_scatter(const EpScatterArgs& a, int sm_count, cudaStream_t stream);
-cudaError_t launch_ep_set_tokens(uint32_t* p, uint32_t v, cudaStream_t stream);
+cudaError_t launch_ep_publish(EpControl* ctl, uint32_t tokens, cudaStream_t stream);
+// The home rank's combine once every rank's dots are in (see launch_ep_combine):
+// waits at most `polls` polls for done[0, world) to reach this step.
+cudaError_t launch_ep_combine_wait(const EpControl* ctl, uint32_t world, uint32_t polls, const lbk_routed* routed,
+                                   const float* routed_dots, const float* shared_dots, float* out, uint64_t tokens,
+                                   uint64_t k, uint64_t H, DeviceStatus* status, cudaStream_t stream);
 
 }  // namespace lbk

@@ -1807,15 +1807,40 @@ __global__ void swiglu_kernel(const float* gate, const float* up, float* h, uint
 
 // Expert-parallel combine on the home GPU: out = 0; += c_j * dot_j over the
 // token's routed slots in ascending ID (the routing's order); += 1.0 * shared
-// (moe.rs:331-336), unless validation failed upstream.
+// (moe.rs:331-336), unless validation failed upstream. With a control block,
+// warp 0 of every CTA first waits (bounded) until every rank's dots of this
+// step are in.
 __global__ void ep_combine_kernel(const lbk_routed* routed, const float* routed_dots, const float* shared_dots,
-                                  float* out, uint64_t tokens, uint64_t k, uint64_t H, DeviceStatus* st) {
+                                  float* out, uint64_t tokens, uint64_t k, uint64_t H, DeviceStatus* st,
+                                  const EpControl* ctl, uint32_t world, uint32_t polls) {
+    if (ctl != nullptr) {
+        __shared__ int s_ok;
+        if (threadIdx.x < 32) {
+            const uint32_t step = __ldcg(&ctl->step);
+            bool ok = true;
+            for (uint32_t r = threadIdx.x; r < world; r += 32) {
+                uint32_t i = 0;
+                while ((int32_t)(ld_acquire_sys(&ctl->done[r]) - step) < 0 && ++i < polls) {
+                    if ((i & 255u) == 0u && status_set(st)) i = polls;  // an error is recorded already
+                    __nanosleep(64);
+                }
+                ok &= i < polls;
+            }
+            ok = __all_sync(0xffffffffu, ok);
+            if (threadIdx.x == 0) {
+                s_ok = ok;
+                if (!ok) report(st, LBK_TIMEOUT, 9, step);
+            }
+        }
+        __syncthreads();  // the flags' acquire before every thread's reads of the dots
+        if (!s_ok) return;
+    }
     if (status_set(st)) return;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t t = i / H, r = i % H;
         float acc = 0.0f;
         for (uint64_t j = 0; j < k; j++)
-            acc = __fadd_rn(acc, __fmul_rn(routed[t * k + j].coefficient, routed_dots[(t * k + j) * H + r]));
+            acc = __fadd_rn(acc, __fmul_rn(routed[t * k + j].coefficient, __ldcg(routed_dots + (t * k + j) * H + r)));
         out[i] = __fadd_rn(acc, __fmul_rn(1.0f, shared_dots[i]));
     }
 }
@@ -1826,7 +1851,20 @@ cudaError_t launch_ep_combine(const lbk_routed* routed, const float* routed_dots
                               uint64_t tokens, uint64_t k, uint64_t H, DeviceStatus* status, cudaStream_t stream) {
     uint64_t grid = (tokens * H + 255) / 256;
     if (grid > 4096) grid = 4096;
-    ep_combine_kernel<<<(unsigned)grid, 256, 0, stream>>>(routed, routed_dots, shared_dots, out, tokens, k, H, status);
+    if (grid < 1) grid = 1;
+    ep_combine_kernel<<<(unsigned)grid, 256, 0, stream>>>(routed, routed_dots, shared_dots, out, tokens, k, H, status,
+                                                          nullptr, 0, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine_wait(const EpControl* ctl, uint32_t world, uint32_t polls, const lbk_routed* routed,
+                                   const float* routed_dots, const float* shared_dots, float* out, uint64_t tokens,
+                                   uint64_t k, uint64_t H, DeviceStatus* status, cudaStream_t stream) {
+    uint64_t grid = (tokens * H + 255) / 256;
+    if (grid > 1024) grid = 1024;
+    if (grid < 1) grid = 1;  // a rank without tokens still waits: its buffer is then free for the next step
+    ep_combine_kernel<<<(unsigned)grid, 256, 0, stream>>>(routed, routed_dots, shared_dots, out, tokens, k, H, status,
+                                                          ctl, world, polls);
     return cudaGetLastError();
 }
 

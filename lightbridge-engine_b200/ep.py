@@ -30,6 +30,16 @@ The compute stages are the methods of `layer` (lbk.EpLayer on a GPU: route,
 items_forward, combine, q8_bytes, workspace_bytes). Every rank takes the same
 collective steps in the same order, also with no tokens of its own or no items
 to compute.
+
+Two exchanges implement steps 2 and 4:
+- ExpertParallelMoe: NCCL all-to-all; the per-peer counts are read on the
+  host to size the row exchange (one device-to-host read per layer step).
+  Works wherever torch.distributed does.
+- PeerExpertParallelMoe: the ranks of one node map each other's exchange
+  buffers (CUDA IPC) and move only the pairs' bytes with plain peer loads and
+  stores; the counts stay on the device and the ranks order a step through
+  flags in the buffers, so a step has no collective and no host read and can
+  be captured in a CUDA graph. This is the exchange the benchmark uses.
 """
 
 from __future__ import annotations
@@ -203,20 +213,23 @@ class PeerExpertParallelMoe:
     mapped into every other rank (lbk.PeerBuffer, plain peer loads and stores),
     the home rank publishes its routing and Q8_K images there, every rank
     gathers the pairs of its experts and scatters their row dots back into the
-    home buffers (lbk_ep_publish / gather / items_forward_counted / scatter),
-    and the home rank combines. The item count stays on the device, so a layer
-    step has no size exchange and no device-to-host read; the two barriers are
-    one-element all-reduces on the stream. Results equal lbk_moe_forward on
-    one GPU bit for bit (the combine order is the one-GPU order).
+    home buffers, and the home rank combines (lbk_ep_publish / gather /
+    items_forward_counted / scatter / combine_exchange). The ranks order a
+    step among themselves through flags in the buffers, so a layer step has no
+    collective, no size exchange and no device-to-host read, and can be
+    captured in a CUDA graph. Results equal lbk_moe_forward on one GPU bit for
+    bit (the combine order is the one-GPU order).
 
-    cap: the most tokens any rank brings to a step. Collective: every rank of
-    the group calls forward once per layer step."""
+    cap: the most tokens any rank brings to a step. Every rank of the group
+    calls forward once per layer step (a rank without tokens too). The
+    constructor and close() are collective over the process group."""
 
-    def __init__(self, layer, cap: int, group=None):
+    def __init__(self, layer, cap: int, group=None, stream=None):
         import lbk
 
         self.layer = layer
         self.group = group
+        self.stream = stream
         self.world, self.rank = _world(group)
         E = layer.global_experts
         if E % self.world:
@@ -243,23 +256,43 @@ class PeerExpertParallelMoe:
         self.count = torch.zeros(1, dtype=torch.int32, device=dev)
         self.dots = torch.empty((self.cap_items, H), dtype=torch.float32, device=dev)
         self.ws = torch.zeros(layer.workspace_bytes(max(self.cap_items, cap)), dtype=torch.uint8, device=dev)
-        self._one = torch.ones(1, dtype=torch.float32, device=dev)
-
-    def barrier(self) -> None:
+        torch.cuda.synchronize()
         if self.world > 1:
-            dist.all_reduce(self._one, op=dist.ReduceOp.MAX, group=self.group)
+            dist.barrier(group=group)  # every buffer mapped and zeroed before any rank's first step
 
-    def forward(self, x: torch.Tensor, tokens: int, out: torch.Tensor) -> None:
+    # The stages of one layer step; `layer` (default: the constructor's) may be
+    # any EpLayer of the same shapes and expert share, so that one set of
+    # buffers serves every layer of a stack.
+    def publish(self, x: torch.Tensor, tokens: int, layer=None) -> None:
+        (layer or self.layer).publish(x, tokens, self.buf.ptr, self.cap, self.ws, stream=self.stream)
+
+    def dispatch(self, layer=None) -> None:
+        """Gather this rank's pairs from every buffer (waits for every publication)."""
+        (layer or self.layer).gather(self.peers, self.world, self.rank, self.cap, self.q8_items, self.items,
+                                     self.returns, self.count, stream=self.stream)
+
+    def compute(self, layer=None) -> None:
+        (layer or self.layer).items_forward_counted(self.q8_items, self.items, self.count, self.dots, self.ws,
+                                                    stream=self.stream)
+
+    def send_back(self, layer=None) -> None:
+        (layer or self.layer).scatter(self.peers, self.world, self.rank, self.cap, self.dots, self.returns,
+                                      self.count, stream=self.stream)
+
+    def combine(self, tokens: int, out: torch.Tensor | None, layer=None) -> None:
+        """Waits for every rank's dots, then combines this rank's tokens into out."""
+        (layer or self.layer).combine_exchange(self.buf.ptr, self.world, self.cap, tokens, out, self.ws,
+                                               stream=self.stream)
+
+    def forward(self, x: torch.Tensor, tokens: int, out: torch.Tensor | None, layer=None) -> None:
         """out[tokens * hidden] = the MoE layer on this rank's tokens (tokens <= cap)."""
-        L, b = self.layer, self.buf.ptr
-        L.publish(x, tokens, b, self.cap, self.ws)
-        self.barrier()
-        L.gather(self.peers, self.world, self.cap, self.q8_items, self.items, self.returns, self.count)
-        L.items_forward_counted(self.q8_items, self.items, self.count, self.dots, self.ws)
-        L.scatter(self.peers, self.cap, self.dots, self.returns, self.count)
-        self.barrier()
-        if tokens:
-            L.combine(b + self.x.q8, tokens, b + self.x.routing, b + self.x.dots, out, self.ws)
+        if tokens > self.cap:
+            raise ValueError(f"{tokens} tokens beyond the exchange capacity {self.cap}")
+        self.publish(x, tokens, layer)
+        self.dispatch(layer)
+        self.compute(layer)
+        self.send_back(layer)
+        self.combine(tokens, out, layer)
 
     def close(self) -> None:
         """Collective: every rank unmaps its peers' buffers before any buffer is freed."""

@@ -65,7 +65,7 @@ class Expert(ctypes.Structure):
 
 
 class EpExchange(ctypes.Structure):
-    _fields_ = [("routing", ctypes.c_uint64), ("tokens", ctypes.c_uint64), ("q8", ctypes.c_uint64),
+    _fields_ = [("routing", ctypes.c_uint64), ("control", ctypes.c_uint64), ("q8", ctypes.c_uint64),
                 ("dots", ctypes.c_uint64), ("total", ctypes.c_uint64), ("q8_bytes", ctypes.c_uint64)]
 
 
@@ -203,9 +203,10 @@ def _load() -> ctypes.CDLL:
         "lbk_peer_close": ([P, P], I32),
         "lbk_ep_exchange_layout": ([P, U64, ctypes.POINTER(EpExchange)], I32),
         "lbk_ep_publish": ([P, P, U64, P, U64, P, U64, P], I32),
-        "lbk_ep_gather": ([P, P, U32, U64, P, P, P, P, U64, P], I32),
+        "lbk_ep_gather": ([P, P, U32, U32, U64, P, P, P, P, U64, P], I32),
         "lbk_ep_items_forward_counted": ([P, P, P, P, U64, P, P, U64, P], I32),
-        "lbk_ep_scatter": ([P, P, U64, P, P, P, U64, P], I32),
+        "lbk_ep_scatter": ([P, P, U32, U32, U64, P, P, P, U64, P], I32),
+        "lbk_ep_combine_exchange": ([P, P, U32, U64, U64, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
         "lbk_repack": ([P, PM, P, U64, P], I32),
@@ -240,6 +241,7 @@ EXPORTED = (
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine lbk_peer_alloc lbk_peer_free lbk_peer_open lbk_peer_close "
     "lbk_ep_exchange_layout lbk_ep_publish lbk_ep_gather lbk_ep_items_forward_counted lbk_ep_scatter "
+    "lbk_ep_combine_exchange "
     "lbk_repack lbk_unpack lbk_validate_matrix lbk_decode_rows "
     "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
     "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
@@ -484,7 +486,7 @@ class EpLayer(MoeLayer):
         check(lib.lbk_ep_combine(self.ptr, _ptr(q8), tokens, _ptr(routed), _ptr(routed_dots), _ptr(out),
                                  _ptr(workspace), workspace.numel(), _stream(stream)))
 
-    # exchange over peer memory (lbk_ep_publish / gather / items_forward_counted / scatter)
+    # exchange over peer memory (lbk_ep_publish / gather / items_forward_counted / scatter / combine_exchange)
     def exchange_layout(self, cap: int) -> EpExchange:
         x = EpExchange()
         check(lib.lbk_ep_exchange_layout(self.ptr, cap, ctypes.byref(x)))
@@ -494,17 +496,21 @@ class EpLayer(MoeLayer):
         check(lib.lbk_ep_publish(self.ptr, _ptr(x), tokens, xbuf, cap, _ptr(workspace), workspace.numel(),
                                  _stream(stream)))
 
-    def gather(self, peers, world: int, cap: int, q8_items, items, returns, count, stream=None) -> None:
-        check(lib.lbk_ep_gather(self.ptr, _ptr(peers), world, cap, _ptr(q8_items), _ptr(items), _ptr(returns),
+    def gather(self, peers, world: int, rank: int, cap: int, q8_items, items, returns, count, stream=None) -> None:
+        check(lib.lbk_ep_gather(self.ptr, _ptr(peers), world, rank, cap, _ptr(q8_items), _ptr(items), _ptr(returns),
                                 _ptr(count), items.shape[0], _stream(stream)))
 
     def items_forward_counted(self, q8_items, items, count, dots, workspace, stream=None) -> None:
         check(lib.lbk_ep_items_forward_counted(self.ptr, _ptr(q8_items), _ptr(items), _ptr(count), items.shape[0],
                                                _ptr(dots), _ptr(workspace), workspace.numel(), _stream(stream)))
 
-    def scatter(self, peers, cap: int, dots, returns, count, stream=None) -> None:
-        check(lib.lbk_ep_scatter(self.ptr, _ptr(peers), cap, _ptr(dots), _ptr(returns), _ptr(count),
+    def scatter(self, peers, world: int, rank: int, cap: int, dots, returns, count, stream=None) -> None:
+        check(lib.lbk_ep_scatter(self.ptr, _ptr(peers), world, rank, cap, _ptr(dots), _ptr(returns), _ptr(count),
                                  returns.shape[0], _stream(stream)))
+
+    def combine_exchange(self, xbuf: int, world: int, cap: int, tokens: int, out, workspace, stream=None) -> None:
+        check(lib.lbk_ep_combine_exchange(self.ptr, xbuf, world, cap, tokens, _ptr(out) if out is not None else None,
+                                          _ptr(workspace), workspace.numel(), _stream(stream)))
 
 
 class PeerBuffer:

@@ -277,52 +277,153 @@ def test_grouped_expert_parallel_equals_ungrouped_forward(world, T):
         r.close()
 
 
+def _peer_ranks(ranks, world, cap):
+    """`world` simulated ranks on one GPU: exchange buffers in this process,
+    every rank's scratch as PeerExpertParallelMoe holds it."""
+    xl = ranks[0].exchange_layout(cap)
+    bufs = [torch.zeros(xl.total, dtype=torch.uint8, device="cuda") for _ in range(world)]
+    peers = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+    cap_items = world * cap * ranks[0].top_k
+    q8b, H = ranks[0].q8_bytes, ranks[0].hidden
+    st = []
+    for r in range(world):
+        st.append(dict(
+            q8_items=torch.empty((cap_items, q8b), dtype=torch.uint8, device="cuda"),
+            items=torch.zeros((cap_items, 2), dtype=torch.int32, device="cuda"),
+            returns=torch.zeros(cap_items, dtype=torch.int64, device="cuda"),
+            count=torch.zeros(1, dtype=torch.int32, device="cuda"),
+            dots=torch.empty((cap_items, H), dtype=torch.float32, device="cuda"),
+            ws=torch.zeros(ranks[r].workspace_bytes(max(cap_items, cap)), dtype=torch.uint8, device="cuda")))
+    return xl, bufs, peers, st
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("world,H,F,E,k,tokens", [(1, 4096, 1536, 24, 8, (3,)), (2, 4096, 1536, 48, 8, (1, 2)),
                                                   (4, 2048, 512, 16, 4, (6, 0, 3, 5)),
                                                   (8, 4096, 256, 64, 8, (2, 1, 0, 2, 2, 1, 2, 2))])
 def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens):
     """The peer-memory exchange (lbk_ep_publish / gather / items_forward_counted
-    / scatter / combine) with `world` ranks on one GPU: each rank's exchange
-    buffer is device memory of this process, addressed by every rank as its
-    peers would address it, each rank with its own tokens (one with none).
-    Every rank's output equals lbk_moe_forward on its tokens bit for bit."""
+    / scatter / combine_exchange) with `world` ranks on one GPU: each rank's
+    exchange buffer is device memory of this process, addressed by every rank
+    as its peers would address it, each rank with its own tokens (one with
+    none). Every call of a step is issued after the calls whose flags it waits
+    for, so no kernel waits on another. Two steps on the same buffers: every
+    rank's output equals lbk_moe_forward on its tokens bit for bit."""
     from gpu_helpers import clean_status, dev
 
     full, ranks, keep, rng = _gpu_layers(H, F, E, k, 13 * H + F + E + world, world)
     cap = max(tokens)
-    xl = ranks[0].exchange_layout(cap)
-    bufs = [torch.zeros(xl.total, dtype=torch.uint8, device="cuda") for _ in range(world)]
-    peers = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
-    cap_items = world * cap * k
-    q8b = ranks[0].q8_bytes
-    ws = [torch.zeros(ranks[0].workspace_bytes(max(cap_items, cap)), dtype=torch.uint8, device="cuda")
-          for _ in range(world)]
-    xs = [dev(rng.standard_normal(max(T, 1) * H).astype(np.float32)) for T in tokens]
-    for r in range(world):
-        ranks[r].publish(xs[r], tokens[r], bufs[r].data_ptr(), cap, ws[r])
-    for r in range(world):
-        q8_items = torch.empty((cap_items, q8b), dtype=torch.uint8, device="cuda")
-        items = torch.zeros((cap_items, 2), dtype=torch.int32, device="cuda")
-        returns = torch.zeros(cap_items, dtype=torch.int64, device="cuda")
-        count = torch.zeros(1, dtype=torch.int32, device="cuda")
-        dots = torch.empty((cap_items, H), dtype=torch.float32, device="cuda")
-        ranks[r].gather(peers, world, cap, q8_items, items, returns, count)
-        ranks[r].items_forward_counted(q8_items, items, count, dots, ws[r])
-        ranks[r].scatter(peers, cap, dots, returns, count)
-    clean_status()
-    for r in range(world):
-        T = tokens[r]
-        if T == 0:
-            continue
-        b = bufs[r].data_ptr()
-        out = torch.full((T * H,), float("nan"), device="cuda")
-        ranks[r].combine(b + xl.q8, T, b + xl.routing, b + xl.dots, out, ws[r])
+    xl, bufs, peers, st = _peer_ranks(ranks, world, cap)
+    for step in range(2):
+        xs = [dev(rng.standard_normal(max(T, 1) * H).astype(np.float32)) for T in tokens]
+        for r in range(world):
+            ranks[r].publish(xs[r], tokens[r], bufs[r].data_ptr(), cap, st[r]["ws"])
+        for r in range(world):
+            s = st[r]
+            ranks[r].gather(peers, world, r, cap, s["q8_items"], s["items"], s["returns"], s["count"])
+            ranks[r].items_forward_counted(s["q8_items"], s["items"], s["count"], s["dots"], s["ws"])
+            ranks[r].scatter(peers, world, r, cap, s["dots"], s["returns"], s["count"])
+        outs = [torch.full((max(T, 1) * H,), float("nan"), device="cuda") for T in tokens]
+        for r in range(world):
+            ranks[r].combine_exchange(bufs[r].data_ptr(), world, cap, tokens[r], outs[r] if tokens[r] else None,
+                                      st[r]["ws"])
         clean_status()
-        want, wr = _full_forward(full, xs[r][:T * H], T)
-        got_routing = bufs[r][xl.routing:xl.routing + T * k * 8].view(torch.int32)
-        assert torch.equal(got_routing.cpu(), wr.cpu()), f"rank {r} routing"
-        assert torch.equal(out.view(torch.int32).cpu(), want.view(torch.int32).cpu()), f"rank {r} output"
+        for r in range(world):
+            T = tokens[r]
+            ctl = bufs[r][xl.control:xl.control + 16].view(torch.int32).cpu().tolist()
+            assert ctl[0] == T and ctl[1] == step + 1 and ctl[2] == step + 1, f"rank {r} control {ctl}"
+            assert bufs[r][xl.control + 64:xl.control + 64 + 4 * world].view(torch.int32).cpu().tolist() == \
+                [step + 1] * world, f"rank {r} done flags"
+            if T == 0:
+                continue
+            want, wr = _full_forward(full, xs[r][:T * H], T)
+            got_routing = bufs[r][xl.routing:xl.routing + T * k * 8].view(torch.int32)
+            assert torch.equal(got_routing.cpu(), wr.cpu()), f"rank {r} routing"
+            assert torch.equal(outs[r].view(torch.int32).cpu(), want.view(torch.int32).cpu()), f"rank {r} output"
     full.close()
     for r in ranks:
         r.close()
+
+
+@pytest.mark.gpu
+def test_peer_exchange_wait_that_runs_out_reports_timeout():
+    """Rank 1 of 2 never publishes: rank 0's gather waits its limit out and
+    reports LBK_TIMEOUT (index 8, bits = the step); its combine, with no dots
+    from rank 1, reports LBK_TIMEOUT (index 9). Both return, the context stays
+    usable, and a full step afterwards (rank 1 catching up) is exact."""
+    from gpu_helpers import clean_status, dev, expect_status
+
+    H, F, E, k, world, cap = 2048, 256, 16, 4, 2, 2
+    full, ranks, keep, rng = _gpu_layers(H, F, E, k, 99, world)
+    xl, bufs, peers, st = _peer_ranks(ranks, world, cap)
+    for r in ranks:
+        r.set_wait_limit(2000)
+    x = dev(rng.standard_normal(cap * H).astype(np.float32))
+    s0 = st[0]
+    ranks[0].publish(x, cap, bufs[0].data_ptr(), cap, s0["ws"])
+    ranks[0].gather(peers, world, 0, cap, s0["q8_items"], s0["items"], s0["returns"], s0["count"])
+    d = expect_status(31)
+    assert d.index == 8 and d.bits == 1
+    ranks[0].combine_exchange(bufs[0].data_ptr(), world, cap, cap, torch.zeros(cap * H, device="cuda"), s0["ws"])
+    d = expect_status(31)
+    assert d.index == 9 and d.bits == 1
+    # rank 1 catches up on step 1 (rank 0's own step-1 flags are set; its scatter of step 1 ran short)
+    ranks[1].publish(x, cap, bufs[1].data_ptr(), cap, st[1]["ws"])
+    for r in range(world):
+        s = st[r]
+        ranks[r].gather(peers, world, r, cap, s["q8_items"], s["items"], s["returns"], s["count"])
+        ranks[r].items_forward_counted(s["q8_items"], s["items"], s["count"], s["dots"], s["ws"])
+        ranks[r].scatter(peers, world, r, cap, s["dots"], s["returns"], s["count"])
+    out = torch.full((cap * H,), float("nan"), device="cuda")
+    ranks[1].combine_exchange(bufs[1].data_ptr(), world, cap, cap, out, st[1]["ws"])
+    clean_status()
+    want, _ = _full_forward(full, x, cap)
+    assert torch.equal(out.view(torch.int32).cpu(), want.view(torch.int32).cpu())
+    full.close()
+    for r in ranks:
+        r.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,B", [(4, 1), (2, 4)])
+def test_peer_exchange_stack_chain_equals_block_forward(world, B):
+    """Config 5's expert-parallel chain at reduced depth: three layers of
+    hidden += MoE(RMSNorm(hidden)) with the MoE step through the peer exchange
+    (ranks simulated on one GPU, one set of exchange buffers for all layers,
+    each rank with its own B tokens), against lbk_moe_block_forward of the
+    whole layers fed back into itself: every rank's hidden state equals the
+    one-GPU chain bit for bit after every layer."""
+    import lbk
+    from gpu_helpers import clean_status, ctx, dev
+
+    H, F, E, k, depth = 4096, 512, 32, 8, 3
+    stack = [_gpu_layers(H, F, E, k, 500 + l, world) for l in range(depth)]
+    ranks0 = stack[0][1]
+    xl, bufs, peers, st = _peer_ranks(ranks0, world, B)
+    rng = np.random.default_rng(7)
+    norm_w = dev((1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+    hid = [dev(rng.standard_normal(B * H).astype(np.float32)) for _ in range(world)]
+    ref = [h.clone() for h in hid]
+    normed = [torch.empty(B * H, device="cuda") for _ in range(world)]
+    delta = [torch.empty(B * H, device="cuda") for _ in range(world)]
+    bws = torch.zeros(stack[0][0].block_workspace_bytes(B), dtype=torch.uint8, device="cuda")
+    for l, (full, ranks, keep, _) in enumerate(stack):
+        for r in range(world):
+            ctx().rms_norm(hid[r], norm_w, H, B, 1e-6, normed[r], mode=lbk.ROUTER_TREE)
+            ranks[r].publish(normed[r], B, bufs[r].data_ptr(), B, st[r]["ws"])
+        for r in range(world):
+            s = st[r]
+            ranks[r].gather(peers, world, r, B, s["q8_items"], s["items"], s["returns"], s["count"])
+            ranks[r].items_forward_counted(s["q8_items"], s["items"], s["count"], s["dots"], s["ws"])
+            ranks[r].scatter(peers, world, r, B, s["dots"], s["returns"], s["count"])
+        for r in range(world):
+            ranks[r].combine_exchange(bufs[r].data_ptr(), world, B, B, delta[r], st[r]["ws"])
+            ctx().residual_add(hid[r], delta[r], B * H)
+            full.block_forward(ref[r], norm_w, 1e-6, B, bws)
+        clean_status()
+        for r in range(world):
+            assert torch.equal(hid[r].view(torch.int32).cpu(), ref[r].view(torch.int32).cpu()), f"layer {l} rank {r}"
+    for full, ranks, keep, _ in stack:
+        full.close()
+        for r in ranks:
+            r.close()
