@@ -58,6 +58,7 @@ struct lbk_moe_layer {
     bool tracing;
     void* owned;                         // device memory freed with the layer (lbk_moe_layer_load)
     uint64_t group_min = 8;              // calls of at least this many tokens (items) run the grouped kernels; 0: never
+    bool group_set = false;              // group_min set by lbk_moe_layer_set_grouping
     uint32_t wait_limit = 1u << 20;      // polls of the down kernel's wait for the single-token routing flag
     // Block workspaces between lbk_moe_block_route and lbk_moe_block_finish,
     // with the routed call's token count (the reference keeps this phase in
@@ -749,8 +750,10 @@ LBK_API int32_t lbk_moe_layer_create(lbk_context* ctx, const lbk_moe_weights* w,
 LBK_API int32_t lbk_ep_layer_create(lbk_context* ctx, const lbk_moe_weights* w, uint64_t global_experts,
                                     uint64_t first_expert, void* stream, lbk_moe_layer** out) {
     const int32_t st = layer_create(ctx, w, global_experts, first_expert, stream, out);
-    // The expert-parallel passes (items without the shared expert, the
-    // shared-only combine) measured no faster grouped: off unless asked for.
+    // The expert-parallel passes with host-known sizes (items without the
+    // shared expert, the shared-only combine) measured no faster grouped: off
+    // unless asked for. Device-counted items choose by their capacity per
+    // expert (lbk_ep_items_forward_counted).
     if (st == LBK_OK && out != nullptr && *out != nullptr) (*out)->group_min = 0;
     return st;
 }
@@ -801,6 +804,7 @@ LBK_API int32_t lbk_moe_layer_set_wait_limit(lbk_moe_layer* layer, uint32_t poll
 LBK_API int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens) {
     if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
     layer->group_min = min_tokens;
+    layer->group_set = true;
     return ok();
 }
 
@@ -861,6 +865,7 @@ struct MoeMode {
     float* dots;         // row dots [T][dots_slots][H] (null: the workspace's)
     uint32_t dots_slots;
     const uint32_t* d_items = nullptr;  // items counted on the device (T is then the capacity)
+    bool grouped = false;               // run the grouped kernels whatever the layer's rule
 };
 
 MoeMode full_mode(const lbk_moe_layer* L) { return MoeMode{L->k, true, true, nullptr, nullptr, (uint32_t)(L->k + 1)}; }
@@ -896,7 +901,8 @@ int32_t moe_experts_grouped(lbk_moe_layer* L, uint64_t T, const lbk_routed* rout
     const uint4* grp = reinterpret_cast<const uint4*>(ws + o.grp);
     uint32_t* grp_pairs = reinterpret_cast<uint32_t*>(ws + o.grp_pairs);
     if (K > 0) {
-        lbk::MoeGroupArgs ga{routed, T, K, L->E_local, gr, grp_n, const_cast<uint4*>(grp), grp_pairs, ctx->status};
+        lbk::MoeGroupArgs ga{routed, T, K, L->E_local, gr, grp_n, const_cast<uint4*>(grp), grp_pairs, ctx->status,
+                             mode.d_items};
         if ((e = lbk::launch_moe_group(ga, st)) != cudaSuccess) return cuda_fail(e, "moe grouping launch");
     }
     const double pairs = (double)(T * K);
@@ -1000,7 +1006,7 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
     if (!full && !(L->fused && lbk::moe_gate_up_tma_supported(L->gate_type, L->sgate_type, (int)nbh) &&
                    lbk::moe_down_tma_supported(L->down_type, L->sdown_type, (int)nbf)))
         return fail(LBK_INVALID_PARAMETER, "expert-parallel calls need planar layers with hidden 2048 or 4096");
-    if (L->fused && !defer_topk && mode.d_items == nullptr && L->group_min != 0 && T >= L->group_min && T >= 2 &&
+    if (L->fused && !defer_topk && (mode.grouped || (L->group_min != 0 && T >= L->group_min)) && T >= 2 &&
         L->E_local <= 1024 &&
         T * K <= 8192 &&
         lbk::moe_grouped_supported(L->gate_type, L->sgate_type, L->down_type, L->sdown_type, (int)nbh, (int)nbf))
@@ -1758,6 +1764,12 @@ LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t
     if (e != cudaSuccess) return cuda_fail(e, "zero counters");
     MoeMode m{1, false, false, q8_items, dots, 1};
     m.d_items = count;
+    // Grouped kernels decode a weight half block once per group of pairs: at
+    // 21 items per expert (64 tokens per rank on 8 ranks, 24 experts each)
+    // 23 % faster than one decode per item, equal at 2.7 per expert (one rank
+    // holding all 192). Without a rule set on the layer, the capacity per
+    // expert decides (the count itself is only known on the device).
+    if (!layer->group_set) m.grouped = cap_items >= 4 * layer->E_local;
     return moe_experts(layer, nullptr, cap_items, items, nullptr, ws, o, st, false, m);
 }
 

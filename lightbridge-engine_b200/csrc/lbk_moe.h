@@ -132,6 +132,7 @@ struct MoeGroupArgs {
     uint4* groups;                   // [tokens*k] {expert, first pair, pairs, 0}
     uint32_t* pairs;                 // [tokens*k] routed index t*k + j, grouped by expert, ascending in t
     DeviceStatus* status;
+    const uint32_t* d_items;         // expert-parallel items counted on the device (k = 1), or null
 };
 
 // Pairs per group the grouped kernels of a type pair take (the activations

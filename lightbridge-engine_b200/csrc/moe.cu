@@ -1659,7 +1659,11 @@ __global__ void __launch_bounds__(kGroupThreads) moe_group_kernel(MoeGroupArgs a
     grid_dep_launch();
     const uint32_t tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const uint32_t E = (uint32_t)a.experts;  // <= kGroupThreads (host-checked)
-    const uint64_t n = a.tokens * a.k;
+    uint64_t n = a.tokens * a.k;
+    if (a.d_items != nullptr) {  // the items a gather counted (launched after it, with a memset between)
+        const uint64_t c = __ldcg(a.d_items);
+        n = c < n ? c : n;
+    }
     s_cnt[tid] = 0u;
     __syncthreads();
     for (uint64_t i = tid; i < n; i += kGroupThreads) {
