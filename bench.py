@@ -577,7 +577,8 @@ def build_ep_layer(ctx, lbk, torch, dev, seed: int, first: int, count: int):
 EP_LAYERS = 4  # config 4 through the peer exchange: resident EP layers a step rotates over
 
 
-def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, warmup: int, grouping=None) -> dict:
+def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, warmup: int, grouping=None,
+                    tokens: int = BATCH_TOKENS) -> dict:
     """Config 4 through the peer-memory exchange (ep.PeerExpertParallelMoe):
     BATCH_TOKENS tokens per rank per layer step, experts sharded E / world per
     GPU, EP_LAYERS resident layers per rank so that a step's weights exceed
@@ -590,7 +591,7 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
 
     import ep
 
-    T = BATCH_TOKENS
+    T = tokens
     er = E // world
     layers = [build_ep_layer(ctx, lbk, torch, dev, 4 + 1000 * rank + 17 * i, rank * er, er) for i in range(EP_LAYERS)]
     if grouping is not None:
@@ -634,29 +635,39 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
     ctx.raise_status()
     ms_layer = e0.elapsed_time(e1) / (steps * EP_LAYERS)
 
-    # stage times: events between the stages, 8 passes over the layers
-    names = ["route", "dispatch", "experts", "return", "combine"]
-    stages = [moe.publish, moe.dispatch, moe.compute, moe.send_back, moe.combine]
+    # stage times: a second graph of one step with events recorded between the
+    # stages (graph event nodes), replayed `passes` times
+    names = ["route", "shared", "dispatch", "experts", "return", "combine"]
     acc = [0.0] * len(names)
     passes = 8
-    for _ in range(passes):
+    evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(names) + 1)]
+           for _ in range(EP_LAYERS)]
+    sgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(sgraph, stream=stream):
         for i, (L, _) in enumerate(layers):
-            ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
-            with torch.cuda.stream(stream):
-                ev[0].record(stream)
-                stages[0](xs[i], T, L)
-                ev[1].record(stream)
-                stages[1](L)
-                ev[2].record(stream)
-                stages[2](L)
-                ev[3].record(stream)
-                stages[3](L)
-                ev[4].record(stream)
-                stages[4](T, out[i], L)
-                ev[5].record(stream)
-            stream.synchronize()
+            ev = evs[i]
+            ev[0].record(stream)
+            moe.publish(xs[i], T, L)
+            ev[1].record(stream)
+            moe.shared(T, L)
+            ev[2].record(stream)
+            moe.dispatch(L)
+            ev[3].record(stream)
+            moe.compute(L)
+            ev[4].record(stream)
+            moe.send_back(L)
+            ev[5].record(stream)
+            moe.combine(T, out[i], L, shared_done=True)
+            ev[6].record(stream)
+    barrier()
+    for _ in range(passes):
+        with torch.cuda.stream(stream):
+            sgraph.replay()
+        stream.synchronize()
+        for ev in evs:
             for j in range(len(names)):
                 acc[j] += ev[j].elapsed_time(ev[j + 1])
+    del sgraph
     barrier()
     ctx.raise_status()
     stage_ms = [a / (passes * EP_LAYERS) for a in acc]
@@ -677,7 +688,7 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
         L.close()
     return {
         "tokens_per_s": T * world / (ms_layer / 1000.0),
-        "unit": "tokens/s (layer steps of config 4: 64 tokens per GPU)",
+        "unit": f"tokens/s (layer steps of {T} tokens per GPU)",
         "ms_per_layer_step": ms_layer,
         "n_gpus": world,
         "gpus_active": int(tsum[1 + len(names)]),
@@ -689,7 +700,9 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
         "limiter": max(stage_max, key=stage_max.get),
         "exchange": "peer memory over NVLink (CUDA IPC; plain peer loads and stores; step flags in the buffers, "
                     "no collective, no host read; one CUDA graph per step)",
-        "stage_timing": "separate pass with events between stages; a stage's time includes its wait for other ranks",
+        "stage_timing": "a second graph with event nodes between the stages, run one after another (the timed "
+                        "graph runs the shared expert on a second stream, concurrent with dispatch, experts and "
+                        "return); a stage's time includes its wait for other ranks",
         "l2": f"{EP_LAYERS} resident layers per rank rotate within a step",
         "steps": steps,
     }

@@ -441,7 +441,8 @@ int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens,
  *                    collect the pairs routed to this rank's experts: items
  *                    (local expert ID), their Q8_K images, their return
  *                    addresses {rank, t * k + j} (uint64 each) and their
- *                    count, on the device;
+ *                    count, on the device (`count` is zero-filled before the
+ *                    first step; lbk_ep_scatter resets it for the next);
  *   lbk_ep_items_forward_counted  the items' row dots (as
  *                    lbk_ep_items_forward, the count read on the device;
  *                    cap_items = world * cap * k bounds it);
@@ -452,6 +453,11 @@ int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens,
  *                    routing, images and dots, bit-identical to
  *                    lbk_moe_forward on one GPU (a rank without tokens still
  *                    calls it: the wait frees its buffer for the next step).
+ *                    `shared_dots` null: the shared expert is computed here
+ *                    first; otherwise they are lbk_ep_shared's output, which
+ *                    needs only the publication and so can run on a second
+ *                    stream (with its own workspace) while the pairs are
+ *                    exchanged.
  * The waits poll at most the layer's wait limit
  * (lbk_moe_layer_set_wait_limit) times; one that runs out is reported as
  * LBK_TIMEOUT through the status word (index 8: gather, 9: combine; bits: the
@@ -474,10 +480,12 @@ int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t* q8_ite
                                      const uint32_t* count, uint64_t cap_items, float* dots, void* workspace,
                                      uint64_t workspace_bytes, void* stream);
 int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,
-                       const float* dots, const uint64_t* returns, const uint32_t* count, uint64_t cap_items,
-                       void* stream);
+                       const float* dots, const uint64_t* returns, uint32_t* count, uint64_t cap_items, void* stream);
+int32_t lbk_ep_shared(lbk_moe_layer* layer, void* xbuf, uint64_t cap, uint64_t tokens, float* shared_dots,
+                      void* workspace, uint64_t workspace_bytes, void* stream);
 int32_t lbk_ep_combine_exchange(lbk_moe_layer* layer, void* xbuf, uint32_t world, uint64_t cap, uint64_t tokens,
-                                float* out, void* workspace, uint64_t workspace_bytes, void* stream);
+                                const float* shared_dots, float* out, void* workspace, uint64_t workspace_bytes,
+                                void* stream);
 
 /* lbk_moe_forward without a caller workspace and without any allocation: the
  * workspace is a fixed 1 MiB array of this library's device memory, one per

@@ -1774,7 +1774,7 @@ LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t
 }
 
 LBK_API int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,
-                               const float* dots, const uint64_t* returns, const uint32_t* count, uint64_t cap_items,
+                               const float* dots, const uint64_t* returns, uint32_t* count, uint64_t cap_items,
                                void* stream) {
     if (layer == nullptr || peers == nullptr || dots == nullptr || returns == nullptr || count == nullptr)
         return fail(LBK_INVALID_PARAMETER, "null pointer");
@@ -1789,9 +1789,34 @@ LBK_API int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_
     return e == cudaSuccess ? ok() : cuda_fail(e, "scatter launch");
 }
 
+namespace {
+// The shared expert on a rank's published tokens: dots [tokens][H].
+int32_t ep_shared_pass(lbk_moe_layer* layer, uint8_t* xb, const lbk_ep_exchange& xl, uint64_t tokens, float* dots,
+                       uint8_t* ws, cudaStream_t st) {
+    const WsLayout o = moe_ws(layer, tokens, 0);
+    cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
+    if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+    return moe_experts(layer, nullptr, tokens, reinterpret_cast<const lbk_routed*>(xb + xl.routing), nullptr, ws, o,
+                       st, false, MoeMode{0, true, false, xb + xl.q8, dots, 1});
+}
+}  // namespace
+
+LBK_API int32_t lbk_ep_shared(lbk_moe_layer* layer, void* xbuf, uint64_t cap, uint64_t tokens, float* shared_dots,
+                              void* workspace, uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr || xbuf == nullptr || shared_dots == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (cap == 0) return fail(LBK_DIMENSION_MISMATCH, "tokens per rank", 0, 1, 0);
+    if (tokens > cap) return fail(LBK_DIMENSION_MISMATCH, "tokens beyond the exchange capacity", 0, cap, tokens);
+    if (!aligned(shared_dots, 16)) return fail(LBK_INVALID_PARAMETER, "shared dots 16-byte alignment");
+    if (tokens == 0) return ok();
+    if (int32_t s = ep_check(layer, tokens, workspace, workspace_bytes, ep_ws_bytes(layer, tokens))) return s;
+    if (int32_t s = set_device(layer->ctx)) return s;
+    return ep_shared_pass(layer, static_cast<uint8_t*>(xbuf), ep_exchange(layer, cap), tokens, shared_dots,
+                          static_cast<uint8_t*>(workspace), as_stream(stream));
+}
+
 LBK_API int32_t lbk_ep_combine_exchange(lbk_moe_layer* layer, void* xbuf, uint32_t world, uint64_t cap,
-                                        uint64_t tokens, float* out, void* workspace, uint64_t workspace_bytes,
-                                        void* stream) {
+                                        uint64_t tokens, const float* shared_dots, float* out, void* workspace,
+                                        uint64_t workspace_bytes, void* stream) {
     if (layer == nullptr || xbuf == nullptr) return fail(LBK_INVALID_PARAMETER, "null pointer");
     if (int32_t s = ep_check_ranks(world, 0, cap)) return s;
     if (tokens > cap) return fail(LBK_DIMENSION_MISMATCH, "tokens beyond the exchange capacity", 0, cap, tokens);
@@ -1804,19 +1829,14 @@ LBK_API int32_t lbk_ep_combine_exchange(lbk_moe_layer* layer, void* xbuf, uint32
     cudaStream_t st = as_stream(stream);
     const lbk_ep_exchange xl = ep_exchange(layer, cap);
     uint8_t* xb = static_cast<uint8_t*>(xbuf);
-    const lbk_routed* routed = reinterpret_cast<const lbk_routed*>(xb + xl.routing);
-    const WsLayout o = moe_ws(layer, tokens, 0);
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    float* shared_dots = reinterpret_cast<float*>(ws + o.total);
-    if (tokens) {
-        cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
-        if (e != cudaSuccess) return cuda_fail(e, "zero counters");
-        if (int32_t s = moe_experts(layer, nullptr, tokens, routed, nullptr, ws, o, st, false,
-                                    MoeMode{0, true, false, xb + xl.q8, shared_dots, 1}))
-            return s;
+    if (tokens && shared_dots == nullptr) {  // the shared expert here, in the workspace
+        float* sd = reinterpret_cast<float*>(ws + moe_ws(layer, tokens, 0).total);
+        if (int32_t s = ep_shared_pass(layer, xb, xl, tokens, sd, ws, st)) return s;
+        shared_dots = sd;
     }
     cudaError_t e = lbk::launch_ep_combine_wait(reinterpret_cast<const lbk::EpControl*>(xb + xl.control), world,
-                                                layer->wait_limit, routed,
+                                                layer->wait_limit, reinterpret_cast<const lbk_routed*>(xb + xl.routing),
                                                 reinterpret_cast<const float*>(xb + xl.dots), shared_dots, out, tokens,
                                                 layer->k, layer->H, ctx->status, st);
     return e == cudaSuccess ? ok() : cuda_fail(e, "combine launch");

@@ -10,7 +10,7 @@
 //   gather   each rank waits until every buffer is published for this step,
 //            then copies the (token, slot) pairs routed to its experts -- their
 //            images over NVLink into a local item list, the count kept on the
-//            device;
+//            device (zero at the start of a step: the scatter resets it);
 //   (items)  the item kernels read the count on the device;
 //   scatter  each item's row dots go straight into the home rank's buffer at
 //            routed_dots[t * k + j]; the scatter's last CTA then releases
@@ -48,10 +48,15 @@ __device__ __forceinline__ bool wait_step(const uint32_t* flag, uint32_t step, u
     return false;
 }
 
+// A Q8_K image in 16-byte words per lane: at most kImgWords per lane (hidden
+// 4096: 292 words over 32 lanes), all loads in flight before any store.
+constexpr int kImgWords = 10;
+
 // One warp per (rank, token): the token's k routing entries; each entry whose
-// expert is local becomes an item (slot from an atomic counter), its image
-// copied from the home buffer in 16-byte words. Warp 0 of every CTA first
-// waits for every rank's publication of this step.
+// expert is local becomes an item (slot from an atomic counter). The warp
+// loads the token's image once (all its words in flight) and stores it to
+// every item of the token. Warp 0 of every CTA first waits for every rank's
+// publication of this step.
 __global__ void __launch_bounds__(kGatherWarps * 32) ep_gather_kernel(EpGatherArgs a) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     __shared__ int s_ok;
@@ -68,6 +73,7 @@ __global__ void __launch_bounds__(kGatherWarps * 32) ep_gather_kernel(EpGatherAr
     }
     __syncthreads();  // the flags' acquire before every warp's reads of the buffers
     if (!s_ok) return;
+    const uint32_t words = a.q8b / 16;  // <= 32 * kImgWords (host-checked)
     const uint64_t pairs_total = (uint64_t)a.world * a.cap;
     for (uint64_t w = (uint64_t)blockIdx.x * kGatherWarps + warp; w < pairs_total;
          w += (uint64_t)gridDim.x * kGatherWarps) {
@@ -76,43 +82,63 @@ __global__ void __launch_bounds__(kGatherWarps * 32) ep_gather_kernel(EpGatherAr
         const uint32_t ntok = __ldcg(&ctl_of(buf, a.off_ctl)->tokens);
         if (t >= ntok) continue;
         const lbk_routed* routing = reinterpret_cast<const lbk_routed*>(buf) + (uint64_t)t * a.k;
-        uint32_t mine = 0;  // slot `lane`'s expert is local
         uint32_t eid = 0;
+        bool mine = false;  // slot `lane`'s expert is local
         if ((uint32_t)lane < a.k) {
             eid = __ldcg(reinterpret_cast<const uint32_t*>(routing + lane));
-            mine = eid >= a.first && eid < a.first + a.count ? 1u : 0u;
+            mine = eid >= a.first && eid < a.first + a.count;
         }
-        uint32_t mask = __ballot_sync(0xffffffffu, mine != 0u);
-        while (mask) {
-            const int j = __ffs(mask) - 1;
-            mask &= mask - 1;
-            const uint32_t e = __shfl_sync(0xffffffffu, eid, j);
-            uint32_t slot = 0;
-            if (lane == 0) slot = atomicAdd(a.d_count, 1u);
-            slot = __shfl_sync(0xffffffffu, slot, 0);
-            if (slot >= a.cap_items) continue;  // cannot happen: cap_items = world * cap * k
-            if (lane == 0) {
-                a.items[slot] = lbk_routed{e - a.first, 0.0f};
-                a.returns[slot] = make_uint2(s, t * a.k + (uint32_t)j);
+        const uint32_t mask = __ballot_sync(0xffffffffu, mine);
+        if (mask == 0u) continue;
+        const uint4* src = reinterpret_cast<const uint4*>(buf + a.off_q8 + (uint64_t)t * a.q8b);
+        uint4 v[kImgWords];
+#pragma unroll
+        for (int q = 0; q < kImgWords; q++)
+            if ((uint32_t)(lane + 32 * q) < words) v[q] = __ldcg(src + lane + 32 * q);
+        // the token's items take consecutive slots; slot order within the token follows j
+        uint32_t base = 0;
+        if (lane == 0) base = atomicAdd(a.d_count, (uint32_t)__popc(mask));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (mine) {
+            const uint32_t slot = base + (uint32_t)__popc(mask & ((1u << lane) - 1u));
+            if (slot < a.cap_items) {  // cannot fail: cap_items = world * cap * k
+                a.items[slot] = lbk_routed{eid - a.first, 0.0f};
+                a.returns[slot] = make_uint2(s, t * a.k + (uint32_t)lane);
             }
-            const uint4* src = reinterpret_cast<const uint4*>(buf + a.off_q8 + (uint64_t)t * a.q8b);
+        }
+        for (uint32_t m = mask; m; m &= m - 1) {
+            const uint32_t slot = base + (uint32_t)__popc(mask & ((1u << (__ffs(m) - 1)) - 1u));
+            if (slot >= a.cap_items) continue;
             uint4* dst = reinterpret_cast<uint4*>(a.q8_items + (uint64_t)slot * a.q8b);
-            for (uint32_t i = lane; i < a.q8b / 16; i += 32) dst[i] = __ldcg(src + i);
+#pragma unroll
+            for (int q = 0; q < kImgWords; q++)
+                if ((uint32_t)(lane + 32 * q) < words) dst[lane + 32 * q] = v[q];
         }
     }
 }
 
-// One CTA per item (grid-stride): its H row dots into the home buffer. The
-// last CTA to finish releases done[rank] = step in every rank's buffer.
-__global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterArgs a) {
+// One CTA per item (grid-stride): its H row dots into the home buffer, each
+// thread's words loaded before any is stored. The last CTA to finish resets
+// the item count for the next step and releases done[rank] = step in every
+// rank's buffer.
+constexpr int kScatterThreads = 256;
+constexpr int kScatterWords = 4;  // hidden 4096: 1024 float4 over 256 threads
+__global__ void __launch_bounds__(kScatterThreads) ep_scatter_kernel(EpScatterArgs a) {
     EpControl* me = reinterpret_cast<EpControl*>(a.peers[a.rank] + a.off_ctl);
     const uint32_t step = __ldcg(&me->step);
     const uint32_t n = __ldcg(a.d_count);
+    const uint32_t words = a.hidden / 4;  // <= kScatterThreads * kScatterWords (host-checked)
     for (uint32_t i = blockIdx.x; i < n && i < a.cap_items; i += gridDim.x) {
         const uint2 r = a.returns[i];
-        const float4* src = reinterpret_cast<const float4*>(a.dots + (uint64_t)i * a.hidden);
-        float4* dst = reinterpret_cast<float4*>(a.peers[r.x] + a.off_dots) + (uint64_t)r.y * (a.hidden / 4);
-        for (uint32_t q = threadIdx.x; q < a.hidden / 4; q += blockDim.x) dst[q] = __ldcg(src + q);
+        const float4* __restrict__ src = reinterpret_cast<const float4*>(a.dots + (uint64_t)i * a.hidden);
+        float4* dst = reinterpret_cast<float4*>(a.peers[r.x] + a.off_dots) + (uint64_t)r.y * words;
+        float4 v[kScatterWords];
+#pragma unroll
+        for (int q = 0; q < kScatterWords; q++)
+            if (threadIdx.x + kScatterThreads * q < words) v[q] = __ldcg(src + threadIdx.x + kScatterThreads * q);
+#pragma unroll
+        for (int q = 0; q < kScatterWords; q++)
+            if (threadIdx.x + kScatterThreads * q < words) dst[threadIdx.x + kScatterThreads * q] = v[q];
     }
     __threadfence_system();  // this thread's peer stores before the CTA's arrival
     __syncthreads();
@@ -121,7 +147,10 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(EpScatterArgs a) {
     __syncthreads();
     if (!s_last) return;
     __threadfence_system();  // the other CTAs' stores (seen through their arrivals) before the flags
-    if (threadIdx.x == 0) me->scatter_ctas = 0u;  // ready for the next step
+    if (threadIdx.x == 0) {
+        me->scatter_ctas = 0u;  // ready for the next step
+        *a.d_count = 0u;        // every CTA has read it
+    }
     for (uint32_t r = threadIdx.x; r < a.world; r += blockDim.x) {
         EpControl* c = reinterpret_cast<EpControl*>(a.peers[r] + a.off_ctl);
         st_release_sys(&c->done[a.rank], step);
@@ -139,8 +168,7 @@ __global__ void ep_publish_kernel(EpControl* ctl, uint32_t tokens) {
 }  // namespace
 
 cudaError_t launch_ep_gather(const EpGatherArgs& a, int sm_count, cudaStream_t stream) {
-    cudaError_t e = cudaMemsetAsync(a.d_count, 0, 4, stream);
-    if (e != cudaSuccess) return e;
+    if (a.q8b % 16 != 0 || a.q8b / 16 > 32u * kImgWords) return cudaErrorInvalidValue;
     const uint64_t warps = (uint64_t)a.world * a.cap;
     uint64_t grid = (warps + kGatherWarps - 1) / kGatherWarps;
     if (grid > (uint64_t)sm_count * 4) grid = (uint64_t)sm_count * 4;
@@ -150,9 +178,10 @@ cudaError_t launch_ep_gather(const EpGatherArgs& a, int sm_count, cudaStream_t s
 }
 
 cudaError_t launch_ep_scatter(const EpScatterArgs& a, int sm_count, cudaStream_t stream) {
+    if (a.hidden % 4 != 0 || a.hidden / 4 > (uint32_t)(kScatterThreads * kScatterWords)) return cudaErrorInvalidValue;
     uint64_t grid = a.cap_items < (uint64_t)sm_count * 4 ? a.cap_items : (uint64_t)sm_count * 4;
     if (grid < 1) grid = 1;
-    ep_scatter_kernel<<<(unsigned)grid, 256, 0, stream>>>(a);
+    ep_scatter_kernel<<<(unsigned)grid, kScatterThreads, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -176,7 +176,7 @@ struct EpGatherArgs {
     uint8_t* q8_items;            // [cap_items][q8b]
     lbk_routed* items;            // [cap_items] local expert ID, coefficient 0
     uint2* returns;               // [cap_items] {home rank, pair t * k + j}
-    uint32_t* d_count;            // items gathered (zeroed by the launcher)
+    uint32_t* d_count;            // items gathered (0 at the start: the previous scatter reset it)
     uint32_t cap_items;           // world * cap * k
     uint32_t polls;               // polls of a peer's flag before LBK_TIMEOUT
     DeviceStatus* status;
@@ -187,7 +187,7 @@ struct EpScatterArgs {
     uint64_t off_ctl, off_dots;
     const float* dots;            // [cap_items][hidden]
     const uint2* returns;
-    const uint32_t* d_count;
+    uint32_t* d_count;            // reset to 0 by the last CTA, for the next step's gather
     uint32_t cap_items, hidden;
 };
 cudaError_t launch_ep_gather(const EpGatherArgs& a, int sm_count, cudaStream_t stream);

@@ -224,12 +224,13 @@ class PeerExpertParallelMoe:
     calls forward once per layer step (a rank without tokens too). The
     constructor and close() are collective over the process group."""
 
-    def __init__(self, layer, cap: int, group=None, stream=None):
+    def __init__(self, layer, cap: int, group=None, stream=None, overlap_shared: bool = True):
         import lbk
 
         self.layer = layer
         self.group = group
-        self.stream = stream
+        self.stream = stream  # a raw CUDA stream handle, or None for torch's current stream
+        self.overlap_shared = overlap_shared
         self.world, self.rank = _world(group)
         E = layer.global_experts
         if E % self.world:
@@ -256,43 +257,74 @@ class PeerExpertParallelMoe:
         self.count = torch.zeros(1, dtype=torch.int32, device=dev)
         self.dots = torch.empty((self.cap_items, H), dtype=torch.float32, device=dev)
         self.ws = torch.zeros(layer.workspace_bytes(max(self.cap_items, cap)), dtype=torch.uint8, device=dev)
+        # the shared expert on a second stream, concurrent with the exchange
+        self.shared_dots = torch.empty((cap, H), dtype=torch.float32, device=dev)
+        self.ws_shared = torch.zeros(layer.workspace_bytes(cap), dtype=torch.uint8, device=dev)
+        self.side = torch.cuda.Stream(device=dev)
+        self._ev_pub = torch.cuda.Event()
+        self._ev_shared = torch.cuda.Event()
+        self._ext = torch.cuda.ExternalStream(stream, device=dev) if stream is not None else None
         torch.cuda.synchronize()
         if self.world > 1:
             dist.barrier(group=group)  # every buffer mapped and zeroed before any rank's first step
 
     # The stages of one layer step; `layer` (default: the constructor's) may be
     # any EpLayer of the same shapes and expert share, so that one set of
-    # buffers serves every layer of a stack.
+    # buffers serves every layer of a stack. Each stage runs on the main stream.
+    def _main(self):
+        s = self._ext if self._ext is not None else torch.cuda.current_stream()
+        return s.cuda_stream, s
+
     def publish(self, x: torch.Tensor, tokens: int, layer=None) -> None:
-        (layer or self.layer).publish(x, tokens, self.buf.ptr, self.cap, self.ws, stream=self.stream)
+        (layer or self.layer).publish(x, tokens, self.buf.ptr, self.cap, self.ws, stream=self._main()[0])
 
     def dispatch(self, layer=None) -> None:
         """Gather this rank's pairs from every buffer (waits for every publication)."""
         (layer or self.layer).gather(self.peers, self.world, self.rank, self.cap, self.q8_items, self.items,
-                                     self.returns, self.count, stream=self.stream)
+                                     self.returns, self.count, stream=self._main()[0])
 
     def compute(self, layer=None) -> None:
         (layer or self.layer).items_forward_counted(self.q8_items, self.items, self.count, self.dots, self.ws,
-                                                    stream=self.stream)
+                                                    stream=self._main()[0])
 
     def send_back(self, layer=None) -> None:
         (layer or self.layer).scatter(self.peers, self.world, self.rank, self.cap, self.dots, self.returns,
-                                      self.count, stream=self.stream)
+                                      self.count, stream=self._main()[0])
 
-    def combine(self, tokens: int, out: torch.Tensor | None, layer=None) -> None:
-        """Waits for every rank's dots, then combines this rank's tokens into out."""
+    def shared(self, tokens: int, layer=None) -> None:
+        """The shared expert of the published tokens into shared_dots."""
+        (layer or self.layer).shared(self.buf.ptr, self.cap, tokens, self.shared_dots, self.ws_shared,
+                                     stream=self._main()[0])
+
+    def combine(self, tokens: int, out: torch.Tensor | None, layer=None, shared_done: bool = False) -> None:
+        """Waits for every rank's dots, then combines this rank's tokens into
+        out (the shared expert computed here unless shared_done)."""
         (layer or self.layer).combine_exchange(self.buf.ptr, self.world, self.cap, tokens, out, self.ws,
-                                               stream=self.stream)
+                                               shared_dots=self.shared_dots if shared_done and tokens else None,
+                                               stream=self._main()[0])
 
     def forward(self, x: torch.Tensor, tokens: int, out: torch.Tensor | None, layer=None) -> None:
-        """out[tokens * hidden] = the MoE layer on this rank's tokens (tokens <= cap)."""
+        """out[tokens * hidden] = the MoE layer on this rank's tokens (tokens <= cap).
+        With overlap_shared the shared expert runs on a second stream between
+        the publication and the combine (a fork and a join, also under CUDA
+        graph capture)."""
         if tokens > self.cap:
             raise ValueError(f"{tokens} tokens beyond the exchange capacity {self.cap}")
-        self.publish(x, tokens, layer)
-        self.dispatch(layer)
-        self.compute(layer)
-        self.send_back(layer)
-        self.combine(tokens, out, layer)
+        L = layer or self.layer
+        self.publish(x, tokens, L)
+        side = self.overlap_shared and tokens > 0
+        if side:
+            main = self._main()[1]
+            self._ev_pub.record(main)
+            self.side.wait_event(self._ev_pub)
+            L.shared(self.buf.ptr, self.cap, tokens, self.shared_dots, self.ws_shared, stream=self.side.cuda_stream)
+            self._ev_shared.record(self.side)
+        self.dispatch(L)
+        self.compute(L)
+        self.send_back(L)
+        if side:
+            main.wait_event(self._ev_shared)
+        self.combine(tokens, out, L, shared_done=side)
 
     def close(self) -> None:
         """Collective: every rank unmaps its peers' buffers before any buffer is freed."""

@@ -206,7 +206,8 @@ def _load() -> ctypes.CDLL:
         "lbk_ep_gather": ([P, P, U32, U32, U64, P, P, P, P, U64, P], I32),
         "lbk_ep_items_forward_counted": ([P, P, P, P, U64, P, P, U64, P], I32),
         "lbk_ep_scatter": ([P, P, U32, U32, U64, P, P, P, U64, P], I32),
-        "lbk_ep_combine_exchange": ([P, P, U32, U64, U64, P, P, U64, P], I32),
+        "lbk_ep_shared": ([P, P, U64, U64, P, P, U64, P], I32),
+        "lbk_ep_combine_exchange": ([P, P, U32, U64, U64, P, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
         "lbk_repack": ([P, PM, P, U64, P], I32),
@@ -241,7 +242,7 @@ EXPORTED = (
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine lbk_peer_alloc lbk_peer_free lbk_peer_open lbk_peer_close "
     "lbk_ep_exchange_layout lbk_ep_publish lbk_ep_gather lbk_ep_items_forward_counted lbk_ep_scatter "
-    "lbk_ep_combine_exchange "
+    "lbk_ep_shared lbk_ep_combine_exchange "
     "lbk_repack lbk_unpack lbk_validate_matrix lbk_decode_rows "
     "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
     "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
@@ -508,8 +509,13 @@ class EpLayer(MoeLayer):
         check(lib.lbk_ep_scatter(self.ptr, _ptr(peers), world, rank, cap, _ptr(dots), _ptr(returns), _ptr(count),
                                  returns.shape[0], _stream(stream)))
 
-    def combine_exchange(self, xbuf: int, world: int, cap: int, tokens: int, out, workspace, stream=None) -> None:
-        check(lib.lbk_ep_combine_exchange(self.ptr, xbuf, world, cap, tokens, _ptr(out) if out is not None else None,
+    def shared(self, xbuf: int, cap: int, tokens: int, shared_dots, workspace, stream=None) -> None:
+        check(lib.lbk_ep_shared(self.ptr, xbuf, cap, tokens, _ptr(shared_dots), _ptr(workspace), workspace.numel(),
+                                _stream(stream)))
+
+    def combine_exchange(self, xbuf: int, world: int, cap: int, tokens: int, out, workspace, shared_dots=None,
+                         stream=None) -> None:
+        check(lib.lbk_ep_combine_exchange(self.ptr, xbuf, world, cap, tokens, _ptr(shared_dots), _ptr(out),
                                           _ptr(workspace), workspace.numel(), _stream(stream)))
 
 

@@ -309,8 +309,9 @@ def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, gro
     exchange buffer is device memory of this process, addressed by every rank
     as its peers would address it, each rank with its own tokens (one with
     none). Every call of a step is issued after the calls whose flags it waits
-    for, so no kernel waits on another. Two steps on the same buffers: every
-    rank's output equals lbk_moe_forward on its tokens bit for bit."""
+    for, so no kernel waits on another. Two steps on the same buffers (the
+    second with the shared expert from lbk_ep_shared): every rank's output
+    equals lbk_moe_forward on its tokens bit for bit."""
     from gpu_helpers import clean_status, dev
 
     full, ranks, keep, rng = _gpu_layers(H, F, E, k, 13 * H + F + E + world, world)
@@ -329,8 +330,13 @@ def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, gro
             ranks[r].scatter(peers, world, r, cap, s["dots"], s["returns"], s["count"])
         outs = [torch.full((max(T, 1) * H,), float("nan"), device="cuda") for T in tokens]
         for r in range(world):
+            sd = None
+            if step == 1 and tokens[r]:  # the shared expert by lbk_ep_shared, its own workspace
+                sd = torch.full((cap * H,), float("nan"), device="cuda")
+                ws2 = torch.zeros(ranks[r].workspace_bytes(cap), dtype=torch.uint8, device="cuda")
+                ranks[r].shared(bufs[r].data_ptr(), cap, tokens[r], sd, ws2)
             ranks[r].combine_exchange(bufs[r].data_ptr(), world, cap, tokens[r], outs[r] if tokens[r] else None,
-                                      st[r]["ws"])
+                                      st[r]["ws"], shared_dots=sd)
         clean_status()
         for r in range(world):
             T = tokens[r]
