@@ -56,12 +56,12 @@ WEIGHT_SCALE = 2.826
 TOKENS_PER_STEP = 256
 LAYERS = 8
 BATCH_TOKENS = 64  # config 4, per GPU
-TYPE_IQ2_S, TYPE_IQ3_S, TYPE_Q4_K = 22, 21, 12
+TYPE_IQ2_S, TYPE_IQ3_S, TYPE_Q4_K, TYPE_Q5_K = 22, 21, 12, 13
 METRIC = "routed-MoE decode tokens/s (single-token MoE FFN layer, config 3)"
 
 
 def row_bytes(ty: int, k: int) -> int:
-    return k // 256 * {TYPE_IQ2_S: 82, TYPE_IQ3_S: 110, TYPE_Q4_K: 144}[ty]
+    return k // 256 * {TYPE_IQ2_S: 82, TYPE_IQ3_S: 110, TYPE_Q4_K: 144, TYPE_Q5_K: 176}[ty]
 
 
 # algorithmic bytes per token: router + 8 routed experts + shared (weights read once) + x + out
@@ -898,7 +898,9 @@ def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     ctx = lbk.Context(local_rank)
-    cases = [(TYPE_Q4_K, 4096, 4096)] if cfg == 1 else [(TYPE_IQ2_S, 4096, 6144), (TYPE_IQ3_S, 4096, 6144)]
+    # config 1 adds the checkpoint's output projection (Q5_K, 120832 vocabulary rows)
+    cases = [(TYPE_Q4_K, 4096, 4096), (TYPE_Q5_K, 4096, 120832)] if cfg == 1 else \
+        [(TYPE_IQ2_S, 4096, 6144), (TYPE_IQ3_S, 4096, 6144)]
     results = []
     for ty, k, rows in cases:
         gen = torch.Generator(device=dev)
@@ -936,7 +938,8 @@ def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
         ctx.raise_status()
         us = st.elapsed_time(en) * 1000.0 / (args.steps * copies)
         alg = rows * row_bytes(ty, k) + k * 4 + rows * 4
-        results.append({"type": {TYPE_Q4_K: "Q4_K", TYPE_IQ2_S: "IQ2_S", TYPE_IQ3_S: "IQ3_S"}[ty], "rows": rows,
+        results.append({"type": {TYPE_Q4_K: "Q4_K", TYPE_Q5_K: "Q5_K", TYPE_IQ2_S: "IQ2_S", TYPE_IQ3_S: "IQ3_S"}[ty],
+                        "rows": rows,
                         "input_width": k, "us_per_call": us, "gbs": alg / us / 1e3, "algorithmic_bytes": alg,
                         "copies": copies})
         del graph

@@ -296,8 +296,248 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
     if (in_batch > 0) flush(in_batch * rps, batch_first);
 }
 
+// ---------------------------------------------------------------------------
+// Planar rows by bulk copy. Each warp streams its rows through a ring of
+// `stages` shared-memory stages (one step -- 32 / tpr consecutive rows, one
+// half block per lane -- per stage, one mbarrier each): the copies of the next
+// stages are in flight while a step is decoded, so a warp keeps several KB of
+// its rows in flight instead of one register-held step. The IQ lookup table
+// arrives by one bulk copy of its prebuilt image. Results, validation and
+// reporting are the register kernel's (same products, same tails, same
+// order).
+//
+// Shared memory: [table][stages: kWarps * stages * stage][act qs K][d nb]
+//                [bsums nb*16][tails kWarps*slots*nb*kTail][flag]
+
+template <int T>
+struct BulkLayout {
+    uint32_t stage, ring, act, tail, flag, total;
+};
+
+template <int T>
+__host__ __device__ inline BulkLayout<T> bulk_layout(int nb, int tpr, int slots, int stages) {
+    BulkLayout<T> o{};
+    const uint32_t rs = planar_row_bytes(TypeInfo<T>::kBlockBytes, nb);
+    o.stage = (uint32_t)(32 / tpr) * rs;
+    o.ring = (uint32_t)GemvCfg<T>::kTableBytes;
+    o.act = o.ring + (uint32_t)(kWarps * stages) * o.stage;
+    uint32_t t = o.act + (uint32_t)nb * kQK + (uint32_t)nb * 4 + (uint32_t)nb * 32;
+    o.tail = (t + 15u) & ~15u;
+    o.flag = o.tail + (uint32_t)(kWarps * slots * nb * GemvCfg<T>::kTail) * 4u;
+    o.total = o.flag + 16u;
+    return o;
+}
+
+constexpr int kBulkMaxStages = 8;
+
+template <int T>
+__global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int stages) {
+    using Cfg = GemvCfg<T>;
+    using HB = typename HBOf<T>::type;
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[kWarps * kBulkMaxStages + 1];
+    const int nb = a.w.nb;
+    const BulkLayout<T> lay = bulk_layout<T>(nb, a.tpr, a.tail_slots, stages);
+    uint32_t* tab0 = reinterpret_cast<uint32_t*>(smem);
+    int8_t* qs = reinterpret_cast<int8_t*>(smem + lay.act);
+    float* dsm = reinterpret_cast<float*>(qs + (size_t)nb * kQK);
+    int16_t* bs = reinterpret_cast<int16_t*>(dsm + nb);
+    float* tail_all = reinterpret_cast<float*>(smem + lay.tail);
+    int* flag = reinterpret_cast<int*>(smem + lay.flag);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* tail = tail_all + (size_t)warp * a.tail_slots * nb * Cfg::kTail;
+    const int tpr = a.tpr;  // threads per row, >= 2 * nb (one half block per lane)
+    const int rps = 32 / tpr;
+    const int sub = lane / tpr, hb0 = lane % tpr;
+    const int b0 = hb0 >> 1, h0 = hb0 & 1;
+    const bool lane_on = hb0 < 2 * nb;
+    const uint64_t rows = a.w.rows;
+    const uint64_t steps = (rows + rps - 1) / rps;
+    const uint64_t gwarp = (uint64_t)blockIdx.x * kWarps + warp;
+    const uint64_t nwarp = (uint64_t)gridDim.x * kWarps;
+    const uint32_t rs = planar_row_bytes(TypeInfo<T>::kBlockBytes, nb);
+    const uint8_t* ring = smem + lay.ring + (size_t)warp * stages * lay.stage;
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&s_bar[warp * kBulkMaxStages]);
+    const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_bar[kWarps * kBulkMaxStages]);
+    const uint64_t pol = policy_evict_first();
+
+    // step i of this warp (global step gwarp + i * nwarp) into stage i % stages
+    auto issue = [&](uint64_t i) {
+        const uint64_t st = gwarp + i * nwarp;
+        if (st >= steps) return;
+        const uint64_t r0 = st * rps;
+        const uint32_t nr = (uint32_t)(rows - r0 < (uint64_t)rps ? rows - r0 : (uint64_t)rps);
+        const uint32_t s = (uint32_t)(i % stages);
+        mbar_expect_tx(bar0 + 8 * s, nr * rs);
+        bulk_g2s_stream(ring_s + s * lay.stage, a.w.data + r0 * rs, nr * rs, bar0 + 8 * s, pol);
+    };
+    if (lane == 0) {
+        for (int s = 0; s < stages; s++) mbar_init(bar0 + 8 * s, 1);
+        if (warp == 0 && Cfg::kTableBytes != 0) mbar_init(bar_t, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    // the first stages' rows and the table are in flight during the prologue
+    if (lane == 0)
+        for (int s = 0; s < stages; s++) issue((uint64_t)s);
+    if constexpr (Cfg::kTableBytes != 0) {
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(bar_t, (uint32_t)Cfg::kTableBytes);
+            bulk_g2s((uint32_t)__cvta_generic_to_shared(tab0),
+                     T == LBK_TYPE_IQ2_S ? (const void*)a.tables.iq2_codes : (const void*)a.tables.iq3_grid,
+                     (uint32_t)Cfg::kTableBytes, bar_t);
+        }
+    }
+    const bool ok = stage_activations(a, nb, qs, dsm, bs, flag);
+    if constexpr (Cfg::kTableBytes != 0) {
+        if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 10, 0);
+    }
+    if (!ok) {
+        // nothing is written; the copies in flight complete before the CTA exits
+        for (int s = 0; s < stages; s++)
+            if (gwarp + (uint64_t)s * nwarp < steps) mbar_wait(bar0 + 8 * s, 0);
+        return;
+    }
+
+    ActSmem as{qs, dsm, bs};
+    constexpr bool kTr = !Cfg::kIq;
+    ActHB act;
+    uint32_t nact[32];
+    if (lane_on) {
+        load_act_hb<kTr>(act, as, b0, h0, !Cfg::kIq);
+        if constexpr (T == LBK_TYPE_IQ3_S) {
+#pragma unroll
+            for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
+        }
+    }
+    const uint32_t t0 = (uint32_t)__cvta_generic_to_shared(tab0 + lane);
+    const StageOff so = stage_off<T>(nb, lane_on ? sub : 0, lane_on ? b0 : 0, lane_on ? h0 : 0);
+
+    const int slots = a.tail_slots;  // >= rps, multiple of rps
+    auto flush = [&](int nslots, uint64_t first_step) {
+        __syncwarp();
+        if (lane < nslots) {
+            int s_in = lane / rps, sb = lane % rps;
+            uint64_t row = (first_step + (uint64_t)s_in * nwarp) * rps + sb;
+            if (row < rows) {
+                const float* prod = tail + (size_t)lane * nb * Cfg::kTail;
+                float v = Cfg::kIq ? iq_tail(prod, nb, 1, T == LBK_TYPE_IQ2_S) : k_tail(prod, nb, 9);
+                if (a.mode == kGemvAccumulate)
+                    a.y[row] = __fadd_rn(a.y[row], __fmul_rn(a.scale, v));
+                else
+                    a.y[row] = v;
+            }
+        }
+        __syncwarp();
+    };
+
+    const int steps_per_batch = slots / rps;
+    int in_batch = 0;
+    uint64_t batch_first = gwarp;
+    bool live = true;
+    uint64_t i = 0;
+    for (uint64_t step = gwarp; step < steps; step += nwarp, i++) {
+        const uint32_t s = (uint32_t)(i % stages);
+        if (live && !(mbar_try_wait(bar0 + 8 * s, (uint32_t)((i / stages) & 1)) ||
+                      mbar_wait(bar0 + 8 * s, (uint32_t)((i / stages) & 1)))) {
+            live = false;
+            if (lane == 0) report(a.status, LBK_TIMEOUT, 11, step);
+        }
+        HB w;
+        load_stage(w, ring + s * lay.stage, so);
+        __syncwarp();
+        if (lane == 0 && live) {
+            fence_proxy_async_smem();  // the warp's reads of this stage before its refill
+            issue(i + stages);
+        }
+        const uint64_t row = step * rps + sub;
+        const bool mine = live && lane_on && row < rows;
+        const int slot = in_batch * rps + sub;
+        if constexpr (Cfg::kIq) {
+            IqPart p{0, 0};
+            if constexpr (T == LBK_TYPE_IQ2_S)
+                p = dot_hb(w, act, t0);
+            else
+                p = dot_hb(w, act, nact, t0);
+            int other = __shfl_xor_sync(0xffffffffu, p.sum, 1);
+            if (mine && h0 == 0) {
+                p.sum += other;
+                tail[(size_t)slot * nb + b0] = iq_block_product(p, dsm[b0]);
+                if (!h_finite(p.d)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b0, p.d);
+            }
+        } else {
+            KPart p = dot_hb(w, act, h0);
+#pragma unroll
+            for (int l = 0; l < 8; l++) p.lane[l] += __shfl_xor_sync(0xffffffffu, p.lane[l], 1);
+            p.min_sum += __shfl_xor_sync(0xffffffffu, p.min_sum, 1);
+            if (mine && h0 == 0) {
+                float pr[9];
+                k_block_products(p, dsm[b0], pr);
+                float* dst = tail + ((size_t)slot * nb + b0) * 9;
+#pragma unroll
+                for (int q = 0; q < 9; q++) dst[q] = pr[q];
+                if (!h_finite(p.dm & 0xffffu)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b0, p.dm & 0xffffu);
+                if (!h_finite(p.dm >> 16)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b0, p.dm >> 16);
+            }
+        }
+        if (++in_batch == steps_per_batch) {
+            flush(steps_per_batch * rps, batch_first);
+            in_batch = 0;
+            batch_first = step + nwarp;
+        }
+    }
+    if (in_batch > 0) flush(in_batch * rps, batch_first);
+}
+
+// Stages per warp and tail slots the bulk kernel runs with (stages 0: the
+// register kernel instead): as many stages as shared memory holds next to the
+// tails, at most kBulkMaxStages, at least two; fewer tail slots (rows per
+// tail batch) when that buys stages.
+constexpr uint32_t kBulkStaticSmem = (kWarps * kBulkMaxStages + 1) * 8;
+template <int T>
+int bulk_stages(const GemvArgs& a, int* slots) {
+    if (a.mat_table != nullptr || a.block_sums != nullptr || a.tpr < 2 * a.w.nb) return 0;
+    const int rps = 32 / a.tpr;
+    int best = 0;
+    for (int sl : {a.tail_slots, 16, 8}) {
+        if (sl < rps || sl % rps != 0 || sl > a.tail_slots) continue;
+        for (int s = kBulkMaxStages; s > best && s >= 2; s--)
+            if (bulk_layout<T>(a.w.nb, a.tpr, sl, s).total + kBulkStaticSmem <= kMaxSmem) {
+                best = s;
+                *slots = sl;
+                break;
+            }
+    }
+    return best;
+}
+
+template <int T>
+cudaError_t launch_gemv_bulk(const GemvArgs& a, int stages, int sm_count, cudaStream_t stream) {
+    const size_t smem = bulk_layout<T>(a.w.nb, a.tpr, a.tail_slots, stages).total;
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(gemv_bulk_kernel<T>));
+    if (e != cudaSuccess) return e;
+    const uint64_t rps = 32 / a.tpr;
+    const uint64_t steps = (a.w.rows + rps - 1) / rps;
+    uint64_t ctas = (steps + kWarps - 1) / kWarps;
+    if (ctas > (uint64_t)sm_count) ctas = sm_count;
+    if (ctas < 1) ctas = 1;
+    gemv_bulk_kernel<T><<<(unsigned)ctas, kThreads, smem, stream>>>(a, stages);
+    return cudaGetLastError();
+}
+
 template <int T, int L>
 cudaError_t launch_gemv_t(const GemvArgs& a, int sm_count, cudaStream_t stream) {
+    if constexpr (L == LBK_LAYOUT_PLANAR) {
+        int slots = a.tail_slots;
+        const int stages = bulk_stages<T>(a, &slots);
+        if (stages > 0 && ((uintptr_t)a.w.data & 15u) == 0) {
+            GemvArgs b = a;
+            b.tail_slots = slots;
+            return launch_gemv_bulk<T>(b, stages, sm_count, stream);
+        }
+    }
     size_t smem = gemv_smem_bytes<T>(a.w.nb, a.tail_slots);
     if (smem > kMaxSmem) return cudaErrorInvalidValue;
     cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(gemv_kernel<T, L>));
