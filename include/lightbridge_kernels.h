@@ -675,6 +675,32 @@ int32_t lbk_gguf_metadata_string(const lbk_gguf* gguf, const char* key, char* bu
 int32_t lbk_moe_layer_load(lbk_context* ctx, const lbk_gguf* gguf, uint32_t block, uint64_t first_expert,
                            uint64_t expert_count, void* stream, lbk_moe_layer** out);
 
+/* Grouped row dots of IQ2_S matrices on the tcgen05 tensor cores (int8 MMA,
+ * one int32 accumulator per 16-weight scale group): the row dots of a group
+ * of tokens against one matrix, bit-identical to lbk_gemv per token
+ * (dot_iq2_s, bridge-quant-layout/src/q8_k.rs:339-364, chained as gemv_into,
+ * gemv.rs:88-115). A measured prototype of the grouped-expert path, not used
+ * by lbk_moe_forward. All pointers are device memory:
+ *   mats[nmat]      planar IQ2_S matrices and the column of each one's first
+ *                   row in a pair's dots;
+ *   jobs[njobs][4]  per job {matrix, first row (a multiple of 128), first
+ *                   pair, pairs (1..32)}: one CTA computes 128 rows of the
+ *                   matrix for those pairs;
+ *   q8              token images (the layout lbk_ep_route writes: per 256
+ *                   block 304 bytes -- 256 qs, 16 int16 bsums, f32 d, 12
+ *                   bytes of padding), q8_row_bytes apart;
+ *   pair_tokens     pair -> token;
+ *   dots            [pairs][dots_stride] f32 (only the jobs' rows written).
+ * A malformed job is reported as LBK_INVALID_PARAMETER (index: the job). */
+typedef struct lbk_tc_matrix {
+    const void* data;
+    uint32_t rows, blocks; /* blocks: 256-weight blocks per row */
+    uint64_t out_offset;
+} lbk_tc_matrix;
+int32_t lbk_tc_grouped_dots(lbk_context* ctx, const lbk_tc_matrix* mats, uint32_t nmat, const uint32_t* jobs,
+                            uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes, const uint32_t* pair_tokens,
+                            float* dots, uint64_t dots_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

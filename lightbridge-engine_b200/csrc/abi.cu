@@ -25,6 +25,7 @@
 #include "lbk_kernels.h"
 #include "lbk_host.h"
 #include "lbk_moe.h"
+#include "lbk_tc.h"
 
 struct lbk_context {
     int device;
@@ -1770,6 +1771,10 @@ LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t
     // holding all 192). Without a rule set on the layer, the capacity per
     // expert decides (the count itself is only known on the device).
     if (!layer->group_set) m.grouped = cap_items >= 4 * layer->E_local;
+    if (layer->tracing) {  // no router here: its interval is empty, gate/up starts now
+        trace_record(layer->trace[0], st, cudaEventRecordExternal);
+        trace_record(layer->trace[1], st, cudaEventRecordExternal);
+    }
     return moe_experts(layer, nullptr, cap_items, items, nullptr, ws, o, st, false, m);
 }
 
@@ -2000,4 +2005,22 @@ LBK_API int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void*
                                                 (int)(w->input_width / LBK_QK_K), ctx->scratch_min, ctx->status,
                                                 as_stream(stream));
     return e == cudaSuccess ? ok() : cuda_fail(e, "validate launch");
+}
+
+// ---------------------------------------------- tensor-core grouped dots (prototype)
+
+LBK_API int32_t lbk_tc_grouped_dots(lbk_context* ctx, const lbk_tc_matrix* mats, uint32_t nmat, const uint32_t* jobs,
+                                    uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes,
+                                    const uint32_t* pair_tokens, float* dots, uint64_t dots_stride, void* stream) {
+    if (ctx == nullptr || mats == nullptr || jobs == nullptr || q8 == nullptr || pair_tokens == nullptr ||
+        dots == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (nmat == 0) return fail(LBK_DIMENSION_MISMATCH, "matrices", 0, 1, 0);
+    if (!aligned(q8, 16) || q8_row_bytes % 16 != 0 || !aligned(jobs, 16))
+        return fail(LBK_INVALID_PARAMETER, "q8 / jobs 16-byte alignment");
+    if (int32_t s = set_device(ctx)) return s;
+    lbk::TcDotsArgs a{reinterpret_cast<const lbk::TcMatrix*>(mats), nmat, reinterpret_cast<const uint4*>(jobs), q8,
+                      q8_row_bytes, pair_tokens, dots, dots_stride, ctx->status, ctx->tables()};
+    cudaError_t e = lbk::launch_tc_dots_iq2(a, njobs, as_stream(stream));
+    return e == cudaSuccess ? ok() : cuda_fail(e, "tensor-core dots launch");
 }

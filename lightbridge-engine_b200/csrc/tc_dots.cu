@@ -1,0 +1,331 @@
+// tc_dots.cu -- grouped row dots of IQ2_S matrices on the 5th-generation
+// tensor cores (tcgen05.mma kind::i8), bit-identical to the dp4a kernels.
+//
+// A job is one 128-row tile of one matrix and up to 32 tokens (the pairs
+// routed to one expert). The reference's dot of an IQ2_S block with a Q8_K
+// block (dot_iq2_s, bridge-quant-layout/src/q8_k.rs:339-364) is an integer
+// sum over sixteen 16-weight groups, each multiplied by its own scale
+// 1 + 2s (s a 4-bit field), then one f32 product per block, chained over the
+// blocks. Scaled weights reach 43 * 31 = 1333, beyond int8, so the scales
+// cannot be folded into the operands: instead every 16-weight group gets its
+// own int32 accumulator. One MMA (K = 32 int8) covers two groups; it runs
+// twice, once against the activations with the second 16 bytes of each
+// 32-byte chunk zeroed and once with the first 16 zeroed -- two shared-memory
+// descriptors over one activation copy laid out [lo | zeros | hi], so the
+// masking costs no extra bytes. Per half block (128 weights: 8 groups):
+//   decode  128 threads, one row each, write the half block's int8 weights
+//           into the canonical K-major, no-swizzle layout (4 chunks of
+//           128 rows x 32 bytes);
+//   MMA     one thread issues 8 MMAs (M = 128, N = 16 or 32, K = 32) into 8
+//           TMEM accumulators of this unit's buffer (two buffers: the decode
+//           of the next unit overlaps these MMAs);
+//   epilogue every thread reads its row's 8 x N accumulators (tcgen05.ld),
+//           forms the exact integer sum sum_g (1 + 2 s_g) acc_g per token,
+//           and at the end of a block the reference's f32 block product and
+//           chain (iq_block_product, then 0.125 * the sum over blocks).
+// Waits on MMA completion are bounded (LBK_TIMEOUT).
+
+#include "lbk_kernels.h"
+#include "lbk_tc.h"
+
+namespace lbk {
+
+namespace {
+
+constexpr int kTcThreads = 128;  // one thread per tile row (TMEM lane)
+constexpr int kTcRows = 128;
+constexpr int kTcMaxTok = 32;
+constexpr uint32_t kTmemCols = 512;  // two buffers of 8 accumulators x 32 columns
+constexpr int kTabCopies = 8;        // copies of the 1024-entry code table (bank spread)
+
+// shared memory: [table 1024 * 8 words][W: 2 x 4 chunks x 4 KB][A: 2 x 4 chunks x 3 x 32 x 16 B][dx: 2 x 32]
+constexpr int kTabBytes = 1024 * kTabCopies * 4;
+constexpr int kWChunk = kTcRows * 32;        // 4 KB: 128 rows x 32 bytes
+constexpr int kWUnit = 4 * kWChunk;          // one half block
+constexpr int kAChunkMax = 3 * kTcMaxTok * 16;
+constexpr int kAUnit = 4 * kAChunkMax;
+constexpr int kOffW = kTabBytes;
+constexpr int kOffA = kOffW + 2 * kWUnit;
+constexpr int kOffDx = kOffA + 2 * kAUnit;
+constexpr int kOffChain = kOffDx + 2 * kTcMaxTok * 4;  // [token][thread] f32 chains
+constexpr int kTcSmem = kOffChain + kTcMaxTok * kTcThreads * 4;
+// launched with more than half of an SM's shared memory: one CTA per SM, so
+// no CTA waits in tcgen05.alloc for another's 512 columns
+constexpr int kTcSmemLaunch = 116 * 1024;
+static_assert(kTcSmem <= kTcSmemLaunch, "shared memory");
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    // K-major, no swizzle: start, leading (K-half) and stride (8-row group)
+    // byte offsets in 16-byte units; bits 46-47 = 1 (the sm_100 descriptor)
+    return (uint64_t)((addr & 0x3ffffu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+           (1ull << 46);
+}
+
+// kind::i8: D s32 (bits 4-5 = 2), A and B signed (bits 7-9, 10-12 = 1),
+// both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_i8(int m, int n) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, 0, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Signed grid bytes of one IQ2_S half block (the decode of dot_hb without the
+// dot): words 8g + 2l, 8g + 2l + 1 hold weights 8l .. 8l + 7 of group g.
+__device__ __forceinline__ void decode_iq2_hb(const Iq2HB& w, const uint32_t* tab, uint32_t copy, uint32_t (&out)[32]) {
+#pragma unroll
+    for (int gi = 0; gi < 4; gi++) {
+        const uint32_t qsw = w32(w.qs, gi);
+        const uint32_t sgw = w32(w.sg, gi);
+        const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
+        const uint32_t sp[4] = {signs_at2<0>(sgw), signs_at2<1>(sgw), signs_at2<2>(sgw), signs_at2<3>(sgw)};
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint32_t idx = prmt(qsw, Q, sel_idx(l, l));
+            const uint32_t code = tab[idx * kTabCopies + copy];
+            const uint32_t sel = code | (sp[l] & 0x44444444u);
+            out[gi * 8 + 2 * l] = prmt(kIq2PoolPos, kIq2PoolNeg, sel);
+            out[gi * 8 + 2 * l + 1] = prmt(kIq2PoolPos, kIq2PoolNeg, sel >> 16);
+        }
+    }
+}
+
+// Epilogue of the unit in TMEM buffer BUF (a half block; BUF is its half):
+// the exact integer group sums per token, and after the second half the
+// block's f32 product, chained in block order.
+template <int BUF>
+__device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, uint32_t tmem, int warp, int npad,
+                                            uint32_t n, int b, const float* s_dx, const uint32_t (&ls)[2][8],
+                                            const uint32_t (&dw)[2], uint32_t (&phase)[2], bool& live,
+                                            int32_t (&bsum)[kTcMaxTok], float* chain) {
+    if (live && !(mbar_try_wait(bar0 + 8 * BUF, phase[BUF]) || mbar_wait(bar0 + 8 * BUF, phase[BUF]))) {
+        live = false;
+        report(a.status, LBK_TIMEOUT, 12, (uint32_t)blockIdx.x);
+    }
+    phase[BUF] ^= 1u;
+    tc_fence_after();
+    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(BUF * 256);
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        const int32_t m = (int32_t)ls[BUF][g];
+#pragma unroll
+        for (int c = 0; c < kTcMaxTok; c += 16) {
+            if (c < npad) {
+                uint32_t r[16];
+                tc_ld16(tbase + (uint32_t)(g * npad + c), r);
+                tc_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; i++) bsum[c + i] += m * (int32_t)r[i];
+            }
+        }
+    }
+    tc_fence_before();
+    if constexpr (BUF == 1) {
+#pragma unroll
+        for (int t = 0; t < kTcMaxTok; t++) {
+            if (t < (int)n) {
+                const IqPart p{bsum[t], dw[1]};
+                float* c = chain + t * kTcThreads;
+                *c = __fadd_rn(*c, iq_block_product(p, s_dx[(b & 1) * kTcMaxTok + t]));
+            }
+            bsum[t] = 0;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t s_bar[2];
+    __shared__ uint32_t s_tmem;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const uint4 job = a.jobs[blockIdx.x];  // {matrix, first row, first pair, tokens}
+    if (job.x >= a.nmat || job.w == 0 || job.w > (uint32_t)kTcMaxTok || job.y >= a.mats[job.x].rows ||
+        ((uintptr_t)a.mats[job.x].data & 15u) != 0) {
+        if (tid == 0) report(a.status, LBK_INVALID_PARAMETER, blockIdx.x, job.x);
+        return;  // before any TMEM allocation
+    }
+    const TcMatrix mat = a.mats[job.x];
+    const uint32_t row0 = job.y, p0 = job.z, n = job.w;
+    const int npad = n <= 16 ? 16 : 32;
+    const uint32_t idesc = idesc_i8(kTcRows, npad);
+    const int nb = (int)mat.nb;
+    const uint32_t rs = planar_row_bytes(TypeInfo<LBK_TYPE_IQ2_S>::kBlockBytes, nb);
+    const uint32_t row = row0 + (uint32_t)tid;
+    const bool row_ok = row < mat.rows;
+
+    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+    const uint32_t bar0 = (uint32_t)__cvta_generic_to_shared(&s_bar[0]);
+    float* s_dx = reinterpret_cast<float*>(smem + kOffDx);
+    const int achunk = 3 * npad * 16;  // [lo | zeros | hi] of one 32-byte chunk, npad tokens
+
+    // the code table, compact, kTabCopies interleaved copies (entry e's copy j at e * kTabCopies + j)
+    for (int i = tid; i < 1024 * kTabCopies; i += kTcThreads)
+        tab[i] = reinterpret_cast<const uint32_t*>(a.tables.iq2_codes)[(i / kTabCopies) * 32];
+    // zero rows of the activation buffers (the masks, and padded tokens)
+    for (int i = tid; i < 2 * kAUnit / 16; i += kTcThreads)
+        reinterpret_cast<uint4*>(smem + kOffA)[i] = make_uint4(0, 0, 0, 0);
+    if (tid == 0) {
+        mbar_init(bar0, 1);
+        mbar_init(bar0 + 8, 1);
+        mbar_init_fence();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(&s_tmem)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    float* chain = reinterpret_cast<float*>(smem + kOffChain) + tid;  // this thread's chains, kTcThreads apart
+    int32_t bsum[kTcMaxTok];
+#pragma unroll
+    for (int t = 0; t < kTcMaxTok; t++) {
+        chain[t * kTcThreads] = 0.0f;
+        bsum[t] = 0;
+    }
+    uint32_t ls[2][8];  // the units' group multipliers 1 + 2s (this thread's row)
+    uint32_t dw[2];     // their block scales (binary16 bits)
+    uint32_t phase[2] = {0, 0};
+    bool live = true;
+
+    Iq2HB w{};
+    const uint8_t* rowp = mat.data + (uint64_t)(row_ok ? row : row0) * rs;
+    auto load_w = [&](int bb, int hh) {
+        if (row_ok) {
+            w.qs = __ldg(reinterpret_cast<const uint4*>(rowp + bb * 32 + 16 * hh));
+            w.sg = __ldg(reinterpret_cast<const uint4*>(rowp + nb * 32 + bb * 32 + 16 * hh));
+            w.qh = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 64 + bb * 8 + 4 * hh));
+            w.sc = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 72 + bb * 8 + 4 * hh));
+            w.d = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rowp + nb * 80 + bb * 2));
+        }
+    };
+    load_w(0, 0);
+#pragma unroll 1
+    for (int b = 0; b < nb; b++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const int buf = h;
+            uint8_t* wu = smem + kOffW + buf * kWUnit;
+            uint8_t* au = smem + kOffA + buf * kAUnit;
+            // decode this thread's row, half block (b, h) (loaded one unit ahead)
+            uint32_t q[32];
+            decode_iq2_hb(w, tab, (uint32_t)(tid & (kTabCopies - 1)), q);
+            if (!row_ok) {
+#pragma unroll
+                for (int i = 0; i < 32; i++) q[i] = 0u;
+            }
+            const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;
+            const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;
+#pragma unroll
+            for (int gi = 0; gi < 4; gi++) {
+                ls[buf][2 * gi] = prmt(s1w, 0, 0x4440u | gi);
+                ls[buf][2 * gi + 1] = prmt(s2w, 0, 0x4440u | gi);
+            }
+            dw[buf] = w.d;
+            // the next unit's half block, in flight during this unit's MMAs and epilogue
+            if (h == 0) load_w(b, 1);
+            else if (b + 1 < nb) load_w(b + 1, 0);
+            // chunk gi: [K-half 0: 16 row groups x 128 B][K-half 1: 16 x 128 B]
+#pragma unroll
+            for (int gi = 0; gi < 4; gi++) {
+                uint8_t* ch = wu + gi * kWChunk + (tid >> 3) * 128 + (tid & 7) * 16;
+                *reinterpret_cast<uint4*>(ch) = make_uint4(q[gi * 8 + 0], q[gi * 8 + 1], q[gi * 8 + 2], q[gi * 8 + 3]);
+                *reinterpret_cast<uint4*>(ch + 2048) =
+                    make_uint4(q[gi * 8 + 4], q[gi * 8 + 5], q[gi * 8 + 6], q[gi * 8 + 7]);
+            }
+            // the tokens' activations for this unit: chunk gi, token t -> lo at
+            // (t / 8) * 128 + (t % 8) * 16, hi at 2 * npad * 16 + the same
+            for (int i = tid; i < (int)n * 8; i += kTcThreads) {
+                const int t = i >> 3, gi = (i >> 1) & 3, half = i & 1;
+                const uint8_t* img = a.q8 + (uint64_t)a.pair_tokens[p0 + t] * a.q8_row_bytes + (uint64_t)b * kQ8IBytes;
+                const uint4 v = __ldg(reinterpret_cast<const uint4*>(img + h * 128 + gi * 32 + half * 16));
+                *reinterpret_cast<uint4*>(au + gi * achunk + half * 2 * npad * 16 + (t >> 3) * 128 + (t & 7) * 16) = v;
+            }
+            if (h == 0 && tid < (int)n)
+                s_dx[(b & 1) * kTcMaxTok + tid] =
+                    __uint_as_float(__ldg(reinterpret_cast<const uint32_t*>(
+                        a.q8 + (uint64_t)a.pair_tokens[p0 + tid] * a.q8_row_bytes + (uint64_t)b * kQ8IBytes + 288)));
+            fence_proxy_async_smem();  // the decoded tiles before the tensor core reads them
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0 && live) {
+                const uint32_t wb = sbase + (uint32_t)(kOffW + buf * kWUnit);
+                const uint32_t ab = sbase + (uint32_t)(kOffA + buf * kAUnit);
+#pragma unroll
+                for (int gi = 0; gi < 4; gi++) {
+                    const uint64_t da = smem_desc(wb + gi * kWChunk, 2048, 128);
+                    const uint32_t ac = ab + (uint32_t)(gi * achunk);
+                    const uint64_t dlo = smem_desc(ac, (uint32_t)(npad * 16), 128);  // K-half 1 -> the zeros
+                    const uint64_t dhi = smem_desc(ac + (uint32_t)(npad * 16), (uint32_t)(npad * 16), 128);  // half 0 zeros
+                    const uint32_t d0 = tmem + (uint32_t)(buf * 256 + (2 * gi) * npad);
+                    tc_mma_i8(d0, da, dlo, idesc);
+                    tc_mma_i8(d0 + (uint32_t)npad, da, dhi, idesc);
+                }
+                tc_commit(bar0 + 8 * buf);
+            }
+            // the previous unit's epilogue while these MMAs run
+            if (h == 1)
+                tc_epilogue<0>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
+            else if (b > 0)
+                tc_epilogue<1>(a, bar0, tmem, warp, npad, n, b - 1, s_dx, ls, dw, phase, live, bsum, chain);
+            // the next decode overwrites the other buffer: its MMAs completed
+            // (waited above) and its accumulators are read
+            __syncthreads();
+        }
+    }
+    tc_epilogue<1>(a, bar0, tmem, warp, npad, n, nb - 1, s_dx, ls, dw, phase, live, bsum, chain);
+
+    if (row_ok && live) {
+        float* out = a.dots + (uint64_t)p0 * a.dots_stride + mat.out_offset + row;
+#pragma unroll
+        for (int t = 0; t < kTcMaxTok; t++)
+            if (t < (int)n) out[(uint64_t)t * a.dots_stride] = __fmul_rn(0.125f, chain[t * kTcThreads]);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+}
+
+}  // namespace
+
+int tc_dots_smem_bytes() { return kTcSmemLaunch; }
+
+cudaError_t launch_tc_dots_iq2(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream) {
+    if (jobs == 0) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(tc_dots_iq2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemLaunch);
+    if (e != cudaSuccess) return e;
+    tc_dots_iq2_kernel<<<jobs, kTcThreads, kTcSmemLaunch, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace lbk

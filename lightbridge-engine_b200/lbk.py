@@ -207,6 +207,7 @@ def _load() -> ctypes.CDLL:
         "lbk_ep_items_forward_counted": ([P, P, P, P, U64, P, P, U64, P], I32),
         "lbk_ep_scatter": ([P, P, U32, U32, U64, P, P, P, U64, P], I32),
         "lbk_ep_shared": ([P, P, U64, U64, P, P, U64, P], I32),
+        "lbk_tc_grouped_dots": ([P, P, U32, P, U32, P, U64, P, P, U64, P], I32),
         "lbk_ep_combine_exchange": ([P, P, U32, U64, U64, P, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
@@ -242,7 +243,7 @@ EXPORTED = (
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine lbk_peer_alloc lbk_peer_free lbk_peer_open lbk_peer_close "
     "lbk_ep_exchange_layout lbk_ep_publish lbk_ep_gather lbk_ep_items_forward_counted lbk_ep_scatter "
-    "lbk_ep_shared lbk_ep_combine_exchange "
+    "lbk_ep_shared lbk_ep_combine_exchange lbk_tc_grouped_dots "
     "lbk_repack lbk_unpack lbk_validate_matrix lbk_decode_rows "
     "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
     "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
@@ -258,6 +259,18 @@ def last_error() -> ErrorDetail:
 def check(status: int) -> None:
     if status != 0:
         raise LbkError(status, last_error())
+
+
+def tc_matrices(entries) -> "np.ndarray":
+    """lbk_tc_matrix records (data pointer, rows, blocks, out_offset) packed
+    into a uint8 array (24 bytes each) for a device copy."""
+    import numpy as np
+
+    rec = np.dtype([("data", "<u8"), ("rows", "<u4"), ("blocks", "<u4"), ("out_offset", "<u8")])
+    arr = np.zeros(len(entries), dtype=rec)
+    for i, (data, rows, blocks, off) in enumerate(entries):
+        arr[i] = (data, rows, blocks, off)
+    return arr.view(np.uint8)
 
 
 def _ptr(t) -> int | None:
@@ -324,6 +337,13 @@ class Context:
     def gemv(self, m: Matrix, x, y, q8_scratch=None, stream=None) -> None:
         n = 0 if q8_scratch is None else q8_scratch.numel()
         check(lib.lbk_gemv(self.ptr, ctypes.byref(m), _ptr(x), _ptr(y), _ptr(q8_scratch), n, _stream(stream)))
+
+    def tc_grouped_dots(self, mats, nmat: int, jobs, njobs: int, q8, q8_row_bytes: int, pair_tokens, dots,
+                        dots_stride: int, stream=None) -> None:
+        """lbk_tc_grouped_dots: mats a device tensor of lbk_tc_matrix records
+        (tc_matrices), jobs a device int32 [njobs, 4] tensor."""
+        check(lib.lbk_tc_grouped_dots(self.ptr, _ptr(mats), nmat, _ptr(jobs), njobs, _ptr(q8), q8_row_bytes,
+                                      _ptr(pair_tokens), _ptr(dots), dots_stride, _stream(stream)))
 
     def gemv_accumulate_scaled(self, m: Matrix, x, y, scale: float, q8_scratch=None, stream=None) -> None:
         n = 0 if q8_scratch is None else q8_scratch.numel()
