@@ -126,18 +126,22 @@ __device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, 
     phase[BUF] ^= 1u;
     tc_fence_after();
     const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(BUF * 256);
+    // two groups' accumulators per wait (up to four loads in flight)
 #pragma unroll
-    for (int g = 0; g < 8; g++) {
-        const int32_t m = (int32_t)ls[BUF][g];
+    for (int g = 0; g < 8; g += 2) {
+        uint32_t r[2][kTcMaxTok];
 #pragma unroll
-        for (int c = 0; c < kTcMaxTok; c += 16) {
-            if (c < npad) {
-                uint32_t r[16];
-                tc_ld16(tbase + (uint32_t)(g * npad + c), r);
-                tc_wait_ld();
+        for (int gg = 0; gg < 2; gg++) {
+            tc_ld16(tbase + (uint32_t)((g + gg) * npad), *reinterpret_cast<uint32_t(*)[16]>(&r[gg][0]));
+            if (npad > 16) tc_ld16(tbase + (uint32_t)((g + gg) * npad + 16), *reinterpret_cast<uint32_t(*)[16]>(&r[gg][16]));
+        }
+        tc_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; i++) bsum[c + i] += m * (int32_t)r[i];
-            }
+        for (int gg = 0; gg < 2; gg++) {
+            const int32_t m = (int32_t)ls[BUF][g + gg];
+#pragma unroll
+            for (int i = 0; i < kTcMaxTok; i++)
+                if (i < npad) bsum[i] += m * (int32_t)r[gg][i];
         }
     }
     tc_fence_before();
@@ -217,7 +221,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
 
     Iq2HB w{};
     const uint8_t* rowp = mat.data + (uint64_t)(row_ok ? row : row0) * rs;
+    uint4 av[2];  // this thread's activation words of the next unit (pairs * 8 <= 2 * kTcThreads)
     auto load_w = [&](int bb, int hh) {
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int i = tid + j * kTcThreads;
+            if (i < (int)n * 8) {
+                const int t = i >> 3, gi = (i >> 1) & 3, half = i & 1;
+                const uint8_t* img =
+                    a.q8 + (uint64_t)a.pair_tokens[p0 + t] * a.q8_row_bytes + (uint64_t)bb * kQ8IBytes;
+                av[j] = __ldg(reinterpret_cast<const uint4*>(img + hh * 128 + gi * 32 + half * 16));
+            }
+        }
         if (row_ok) {
             w.qs = __ldg(reinterpret_cast<const uint4*>(rowp + bb * 32 + 16 * hh));
             w.sg = __ldg(reinterpret_cast<const uint4*>(rowp + nb * 32 + bb * 32 + 16 * hh));
@@ -249,9 +264,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
                 ls[buf][2 * gi + 1] = prmt(s2w, 0, 0x4440u | gi);
             }
             dw[buf] = w.d;
-            // the next unit's half block, in flight during this unit's MMAs and epilogue
-            if (h == 0) load_w(b, 1);
-            else if (b + 1 < nb) load_w(b + 1, 0);
             // chunk gi: [K-half 0: 16 row groups x 128 B][K-half 1: 16 x 128 B]
 #pragma unroll
             for (int gi = 0; gi < 4; gi++) {
@@ -260,18 +272,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
                 *reinterpret_cast<uint4*>(ch + 2048) =
                     make_uint4(q[gi * 8 + 4], q[gi * 8 + 5], q[gi * 8 + 6], q[gi * 8 + 7]);
             }
-            // the tokens' activations for this unit: chunk gi, token t -> lo at
-            // (t / 8) * 128 + (t % 8) * 16, hi at 2 * npad * 16 + the same
-            for (int i = tid; i < (int)n * 8; i += kTcThreads) {
-                const int t = i >> 3, gi = (i >> 1) & 3, half = i & 1;
-                const uint8_t* img = a.q8 + (uint64_t)a.pair_tokens[p0 + t] * a.q8_row_bytes + (uint64_t)b * kQ8IBytes;
-                const uint4 v = __ldg(reinterpret_cast<const uint4*>(img + h * 128 + gi * 32 + half * 16));
-                *reinterpret_cast<uint4*>(au + gi * achunk + half * 2 * npad * 16 + (t >> 3) * 128 + (t & 7) * 16) = v;
+            // the tokens' activations for this unit (loaded one unit ahead):
+            // chunk gi, token t -> lo at (t / 8) * 128 + (t % 8) * 16, hi at
+            // 2 * npad * 16 + the same
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int i = tid + j * kTcThreads;
+                if (i < (int)n * 8) {
+                    const int t = i >> 3, gi = (i >> 1) & 3, half = i & 1;
+                    *reinterpret_cast<uint4*>(au + gi * achunk + half * 2 * npad * 16 + (t >> 3) * 128 + (t & 7) * 16) =
+                        av[j];
+                }
             }
             if (h == 0 && tid < (int)n)
                 s_dx[(b & 1) * kTcMaxTok + tid] =
                     __uint_as_float(__ldg(reinterpret_cast<const uint32_t*>(
                         a.q8 + (uint64_t)a.pair_tokens[p0 + tid] * a.q8_row_bytes + (uint64_t)b * kQ8IBytes + 288)));
+            // the next unit's weights and activations, in flight during this
+            // unit's MMAs and epilogue (w and av are consumed above)
+            if (h == 0) load_w(b, 1);
+            else if (b + 1 < nb) load_w(b + 1, 0);
             fence_proxy_async_smem();  // the decoded tiles before the tensor core reads them
             tc_fence_before();
             __syncthreads();
