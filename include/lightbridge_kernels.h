@@ -286,6 +286,16 @@ int32_t lbk_moe_layer_fused(const lbk_moe_layer* layer);
  * (moe_routed_by_id_into, moe.rs:64-147). */
 int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens);
 
+/* Expert-parallel items (lbk_ep_items_forward_counted) on the grouped kernels
+ * run their gate/up projections on the tcgen05 tensor cores (IQ2_S gate/up:
+ * int8 MMA, one accumulator per 16-weight scale group, see
+ * lbk_tc_grouped_dots) when the expected pairs per expert -- cap_items / the
+ * global expert count -- reach `min_pairs_per_expert` (default 10; 0: never).
+ * SwiGLU, Q8_K(h) and the down projection follow as on the grouped path;
+ * results are bit-identical either way. No counterpart in the reference,
+ * which runs each routed expert once per token (moe.rs:64-147). */
+int32_t lbk_moe_layer_set_tensor_cores(lbk_moe_layer* layer, uint64_t min_pairs_per_expert);
+
 /* Bound of a single-token call's wait for its routing: the down kernel polls
  * the flag with which the gate/up kernel publishes the routing (so that it can
  * request its first rows before the gate/up grid ends) at most `polls` times

@@ -23,9 +23,32 @@ struct TcDotsArgs {
     uint64_t dots_stride;
     DeviceStatus* status;
     Tables tables;
+    // Grouped mode (jobs null): the pairs grouped by expert on the device
+    // (moe_group_kernel, groups of at most 32); CTA b is group b / (2 tiles),
+    // matrix (b / tiles) % 2 (gate, up) and row tile b % tiles; a CTA past
+    // the groups written returns. Gate row r goes to column r, up row r to
+    // column rows + r.
+    const uint4* groups;         // {expert, first pair, pairs, 0}
+    const uint32_t* ngroups;
+    const uint8_t* const* gate;  // expert -> planar IQ2_S rows
+    const uint8_t* const* up;
+    uint32_t experts, rows, nb;
+};
+
+// SwiGLU and Q8_K of h per grouped pair, from the tensor-core gate/up dots:
+// h = swiglu(gate, up) (activation.rs:170-178), quantized per 256-row block
+// (quantize_row_q8_k_into) into the image of the pair's item, slot 0 of k + 1.
+struct TcSwigluArgs {
+    const float* dots;           // [pairs][2 ffn] in grouped order
+    const uint32_t* pairs;       // grouped position -> item
+    const uint32_t* count;       // items (device)
+    uint32_t cap, ffn, nb_f, slots;  // slots = k + 1 of the workspace layout
+    uint8_t* hq;
+    DeviceStatus* status;
 };
 
 int tc_dots_smem_bytes();
 cudaError_t launch_tc_dots_iq2(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream);
+cudaError_t launch_tc_swiglu_quant(const TcSwigluArgs& a, int sm_count, cudaStream_t stream);
 
 }  // namespace lbk

@@ -163,13 +163,32 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
     __shared__ __align__(8) uint64_t s_bar[2];
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5;
-    const uint4 job = a.jobs[blockIdx.x];  // {matrix, first row, first pair, tokens}
-    if (job.x >= a.nmat || job.w == 0 || job.w > (uint32_t)kTcMaxTok || job.y >= a.mats[job.x].rows ||
-        ((uintptr_t)a.mats[job.x].data & 15u) != 0) {
-        if (tid == 0) report(a.status, LBK_INVALID_PARAMETER, blockIdx.x, job.x);
-        return;  // before any TMEM allocation
+    uint4 job;  // {matrix, first row, first pair, tokens}
+    TcMatrix mat;
+    if (a.jobs != nullptr) {
+        job = a.jobs[blockIdx.x];
+        if (job.x >= a.nmat || job.w == 0 || job.w > (uint32_t)kTcMaxTok || job.y >= a.mats[job.x].rows ||
+            ((uintptr_t)a.mats[job.x].data & 15u) != 0) {
+            if (tid == 0) report(a.status, LBK_INVALID_PARAMETER, blockIdx.x, job.x);
+            return;  // before any TMEM allocation
+        }
+        mat = a.mats[job.x];
+    } else {
+        const uint32_t tiles = (a.rows + kTcRows - 1) / kTcRows;
+        const uint32_t g = blockIdx.x / (2 * tiles), m = (blockIdx.x / tiles) & 1u, tile = blockIdx.x % tiles;
+        if (g >= __ldcg(a.ngroups)) return;  // fewer groups than the grid's bound
+        const uint4 gr = __ldcg(a.groups + g);
+        if (gr.x >= a.experts || gr.z == 0 || gr.z > (uint32_t)kTcMaxTok) {
+            if (tid == 0) report(a.status, LBK_INVALID_PARAMETER, g, gr.z);
+            return;
+        }
+        mat = TcMatrix{m == 0 ? a.gate[gr.x] : a.up[gr.x], a.rows, a.nb, (uint64_t)m * a.rows};
+        if (((uintptr_t)mat.data & 15u) != 0) {
+            if (tid == 0) report(a.status, LBK_INVALID_PARAMETER, g, gr.x);
+            return;
+        }
+        job = make_uint4(0, tile * kTcRows, gr.y, gr.z);
     }
-    const TcMatrix mat = a.mats[job.x];
     const uint32_t row0 = job.y, p0 = job.z, n = job.w;
     const int npad = n <= 16 ? 16 : 32;
     const uint32_t idesc = idesc_i8(kTcRows, npad);
@@ -336,9 +355,50 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
 }
 
+// One warp per (grouped pair, 256-row block of h): SwiGLU of the block's
+// gate / up dots, then the warp's Q8_K of the block into the pair's image.
+__global__ void __launch_bounds__(256) tc_swiglu_quant_kernel(TcSwigluArgs a) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t n = min(__ldcg(a.count), a.cap);
+    const uint64_t units = (uint64_t)n * a.nb_f;
+    for (uint64_t w = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; w < units;
+         w += ((uint64_t)gridDim.x * blockDim.x) >> 5) {
+        const uint32_t p = (uint32_t)(w / a.nb_f), blk = (uint32_t)(w % a.nb_f);
+        const uint32_t item = __ldcg(a.pairs + p);
+        const float* g = a.dots + (uint64_t)p * 2 * a.ffn + blk * kQK + lane * 8;
+        const float* u = g + a.ffn;
+        float v[8];
+        bool bad = false;
+        int bad_i = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            v[i] = swiglu_ref(__ldcg(g + i), __ldcg(u + i));
+            if (!isfinite(v[i]) && !bad) {
+                bad = true;
+                bad_i = i;
+            }
+        }
+        const uint64_t sidx = (uint64_t)item * a.slots;  // slot 0 of the item
+        if (bad) report(a.status, LBK_NON_FINITE_VALUE, sidx * a.ffn + blk * kQK + lane * 8 + bad_i, __float_as_uint(v[bad_i]));
+        if (__ballot_sync(0xffffffffu, bad)) continue;
+        Q8Block q = quantize_q8k_warp(v, lane);
+        int32_t pair = q.pair_sum + __shfl_xor_sync(0xffffffffu, q.pair_sum, 1);
+        store_q8i(a.hq + (sidx * a.nb_f + blk) * kQ8IBytes, q, pair, lane);
+    }
+}
+
 }  // namespace
 
 int tc_dots_smem_bytes() { return kTcSmemLaunch; }
+
+cudaError_t launch_tc_swiglu_quant(const TcSwigluArgs& a, int sm_count, cudaStream_t stream) {
+    uint64_t warps = (uint64_t)a.cap * a.nb_f;
+    uint64_t grid = (warps + 7) / 8;
+    if (grid > (uint64_t)sm_count * 8) grid = (uint64_t)sm_count * 8;
+    if (grid < 1) grid = 1;
+    tc_swiglu_quant_kernel<<<(unsigned)grid, 256, 0, stream>>>(a);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_tc_dots_iq2(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream) {
     if (jobs == 0) return cudaSuccess;

@@ -181,6 +181,7 @@ def _load() -> ctypes.CDLL:
         "lbk_moe_layer_fused": ([P], I32),
         "lbk_moe_layer_set_grouping": ([P, U64], I32),
         "lbk_moe_layer_set_wait_limit": ([P, U32], I32),
+        "lbk_moe_layer_set_tensor_cores": ([P, U64], I32),
         "lbk_moe_workspace_bytes": ([P, U64, ctypes.POINTER(U64)], I32),
         "lbk_moe_forward": ([P, P, U64, P, P, I32, P, U64, P], I32),
         "lbk_moe_routed": ([P, P, U64, P, P, P, U64, P], I32),
@@ -238,6 +239,7 @@ EXPORTED = (
     "lbk_last_error_detail lbk_required_q8k_bytes lbk_matrix_bytes lbk_planar_bytes lbk_quantize_q8k lbk_vec_dot_q8k lbk_gemv "
     "lbk_gemv_accumulate_scaled lbk_router_logits lbk_route_topk lbk_expert_workspace_bytes "
     "lbk_expert_swiglu_accumulate lbk_moe_layer_create lbk_moe_layer_destroy lbk_moe_layer_fused lbk_moe_layer_set_grouping lbk_moe_layer_set_wait_limit "
+    "lbk_moe_layer_set_tensor_cores "
     "lbk_moe_workspace_bytes lbk_moe_forward lbk_moe_routed lbk_moe_forward_no_alloc lbk_moe_layer_trace "
     "lbk_moe_layer_trace_read lbk_rms_norm lbk_residual_add lbk_moe_block_workspace_bytes lbk_moe_block_forward lbk_moe_block_route lbk_moe_block_finish "
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
@@ -410,6 +412,9 @@ class MoeLayer:
     def set_grouping(self, min_tokens: int) -> None:
         """Calls of at least `min_tokens` tokens run the grouped kernels (0: never)."""
         check(lib.lbk_moe_layer_set_grouping(self.ptr, min_tokens))
+
+    def set_tensor_cores(self, min_pairs_per_expert: int) -> None:
+        check(lib.lbk_moe_layer_set_tensor_cores(self.ptr, min_pairs_per_expert))
 
     def set_wait_limit(self, polls: int) -> None:
         check(lib.lbk_moe_layer_set_wait_limit(self.ptr, polls))

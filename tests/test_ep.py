@@ -298,12 +298,15 @@ def _peer_ranks(ranks, world, cap):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,H,F,E,k,tokens,grouping", [
-    (1, 4096, 1536, 24, 8, (3,), 0), (2, 4096, 1536, 48, 8, (1, 2), 0), (4, 2048, 512, 16, 4, (6, 0, 3, 5), 0),
-    (8, 4096, 256, 64, 8, (2, 1, 0, 2, 2, 1, 2, 2), 0),
+@pytest.mark.parametrize("world,H,F,E,k,tokens,grouping,tc", [
+    (1, 4096, 1536, 24, 8, (3,), 0, 0), (2, 4096, 1536, 48, 8, (1, 2), 0, 0), (4, 2048, 512, 16, 4, (6, 0, 3, 5), 0, 0),
+    (8, 4096, 256, 64, 8, (2, 1, 0, 2, 2, 1, 2, 2), 0, 0),
     # items on the grouped kernels (grouped on the device by local expert, counted there)
-    (2, 4096, 512, 16, 8, (16, 11), 2), (4, 2048, 256, 32, 4, (9, 0, 16, 3), 2)])
-def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, grouping):
+    (2, 4096, 512, 16, 8, (16, 11), 2, 0), (4, 2048, 256, 32, 4, (9, 0, 16, 3), 2, 0),
+    # ... with the gate/up on the tensor cores (groups of up to 32 pairs, partial row tiles)
+    (2, 4096, 512, 16, 8, (16, 11), 2, 1), (4, 2048, 768, 32, 4, (9, 0, 16, 3), 2, 1),
+    (2, 4096, 1536, 8, 8, (40, 33), 2, 1)])
+def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, grouping, tc):
     """The peer-memory exchange (lbk_ep_publish / gather / items_forward_counted
     / scatter / combine_exchange) with `world` ranks on one GPU: each rank's
     exchange buffer is device memory of this process, addressed by every rank
@@ -317,6 +320,7 @@ def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, gro
     full, ranks, keep, rng = _gpu_layers(H, F, E, k, 13 * H + F + E + world, world)
     for r in ranks:
         r.set_grouping(grouping)
+        r.set_tensor_cores(tc)
     cap = max(tokens)
     xl, bufs, peers, st = _peer_ranks(ranks, world, cap)
     for step in range(2):
