@@ -291,8 +291,9 @@ int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens);
  * int8 MMA, one accumulator per 16-weight scale group, see
  * lbk_tc_grouped_dots) when the expected pairs per expert -- cap_items / the
  * global expert count -- reach `min_pairs_per_expert` (default 10; 0: never).
- * SwiGLU, Q8_K(h) and the down projection follow as on the grouped path;
- * results are bit-identical either way. No counterpart in the reference,
+ * SwiGLU and Q8_K(h) follow per pair, and an IQ3_S or IQ2_S down projection
+ * runs on the tensor cores too (else on the grouped kernel); results are
+ * bit-identical either way. No counterpart in the reference,
  * which runs each routed expert once per token (moe.rs:64-147). */
 int32_t lbk_moe_layer_set_tensor_cores(lbk_moe_layer* layer, uint64_t min_pairs_per_expert);
 
@@ -685,14 +686,17 @@ int32_t lbk_gguf_metadata_string(const lbk_gguf* gguf, const char* key, char* bu
 int32_t lbk_moe_layer_load(lbk_context* ctx, const lbk_gguf* gguf, uint32_t block, uint64_t first_expert,
                            uint64_t expert_count, void* stream, lbk_moe_layer** out);
 
-/* Grouped row dots of IQ2_S matrices on the tcgen05 tensor cores (int8 MMA,
- * one int32 accumulator per 16-weight scale group): the row dots of a group
- * of tokens against one matrix, bit-identical to lbk_gemv per token
- * (dot_iq2_s, bridge-quant-layout/src/q8_k.rs:339-364, chained as gemv_into,
- * gemv.rs:88-115). A measured prototype of the grouped-expert path, not used
- * by lbk_moe_forward. All pointers are device memory:
- *   mats[nmat]      planar IQ2_S matrices and the column of each one's first
- *                   row in a pair's dots;
+/* Grouped row dots of IQ2_S or IQ3_S matrices on the tcgen05 tensor cores
+ * (int8 MMA, one int32 accumulator per scale group: 16 weights for IQ2_S,
+ * 32 for IQ3_S): the row dots of a group of tokens against one matrix,
+ * bit-identical to lbk_gemv per token (dot_iq2_s / dot_iq3_s,
+ * bridge-quant-layout/src/q8_k.rs:339-434, chained as gemv_into,
+ * gemv.rs:88-115). The same kernel runs the expert-parallel items' gate/up
+ * and down (lbk_moe_layer_set_tensor_cores); this entry exposes it for any
+ * grouping. All pointers are device memory:
+ *   type            LBK_TYPE_IQ2_S or LBK_TYPE_IQ3_S (else LBK_UNSUPPORTED_TYPE);
+ *   mats[nmat]      planar matrices of that type and the column of each
+ *                   one's first row in a pair's dots;
  *   jobs[njobs][4]  per job {matrix, first row (a multiple of 128), first
  *                   pair, pairs (1..32)}: one CTA computes 128 rows of the
  *                   matrix for those pairs;
@@ -707,9 +711,9 @@ typedef struct lbk_tc_matrix {
     uint32_t rows, blocks; /* blocks: 256-weight blocks per row */
     uint64_t out_offset;
 } lbk_tc_matrix;
-int32_t lbk_tc_grouped_dots(lbk_context* ctx, const lbk_tc_matrix* mats, uint32_t nmat, const uint32_t* jobs,
-                            uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes, const uint32_t* pair_tokens,
-                            float* dots, uint64_t dots_stride, void* stream);
+int32_t lbk_tc_grouped_dots(lbk_context* ctx, int32_t type, const lbk_tc_matrix* mats, uint32_t nmat,
+                            const uint32_t* jobs, uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes,
+                            const uint32_t* pair_tokens, float* dots, uint64_t dots_stride, void* stream);
 
 #ifdef __cplusplus
 }

@@ -904,6 +904,13 @@ double grp_groups_est(double pairs, double experts, double gsize) {
     return 1.15 * (hit > runs ? hit : runs);
 }
 
+// The expert-parallel items' down projection on the tensor cores: IQ
+// weights, one dots row per item, no shared expert, no combine.
+bool tc_down_ok(const lbk_moe_layer* L, const MoeMode& m) {
+    return m.tc && (L->down_type == LBK_TYPE_IQ3_S || L->down_type == LBK_TYPE_IQ2_S) && m.dots != nullptr &&
+           m.dots_slots == 1 && !m.combine && !m.shared && m.k == 1;
+}
+
 // Expert stage of a several-token call on the grouped kernels: the routed
 // pairs are grouped by expert, then gate/up + SwiGLU and down (+ combine) run
 // with each weight half block decoded once per group. Same results, bit for
@@ -921,7 +928,7 @@ int32_t moe_experts_grouped(lbk_moe_layer* L, uint64_t T, const lbk_routed* rout
     uint32_t* grp_n = reinterpret_cast<uint32_t*>(ws + o.grp_n);
     const uint4* grp = reinterpret_cast<const uint4*>(ws + o.grp);
     uint32_t* grp_pairs = reinterpret_cast<uint32_t*>(ws + o.grp_pairs);
-    if (K > 0) {
+    if (K > 0 && !(mode.tc && tc_down_ok(L, mode))) {  // (groups for the dp4a kernels)
         lbk::MoeGroupArgs ga{routed, T, K, L->E_local, gr, grp_n, const_cast<uint4*>(grp), grp_pairs, ctx->status,
                              mode.d_items};
         if ((e = lbk::launch_moe_group(ga, st)) != cudaSuccess) return cuda_fail(e, "moe grouping launch");
@@ -961,13 +968,37 @@ int32_t moe_experts_grouped(lbk_moe_layer* L, uint64_t T, const lbk_routed* rout
         ta.experts = (uint32_t)L->E_local;
         ta.rows = (uint32_t)L->F;
         ta.nb = (uint32_t)nbh;
+        ta.mats_per_group = 2;
         const uint64_t tiles = (L->F + 127) / 128;
         const uint64_t ctas_tc = tc_groups_max(L->E_local, T * K) * 2 * tiles;
-        if ((e = lbk::launch_tc_dots_iq2(ta, (uint32_t)ctas_tc, st)) != cudaSuccess) return cuda_fail(e, "tensor-core gate/up launch");
+        if ((e = lbk::launch_tc_dots(L->gate_type, ta, (uint32_t)ctas_tc, st)) != cudaSuccess)
+            return cuda_fail(e, "tensor-core gate/up launch");
         lbk::TcSwigluArgs sa{tdots, grp_pairs, mode.d_items, (uint32_t)(T * K), (uint32_t)L->F, (uint32_t)nbf,
                              (uint32_t)(K + 1), ws + o.hq, ctx->status};
         if ((e = lbk::launch_tc_swiglu_quant(sa, ctx->sm_count, st)) != cudaSuccess) return cuda_fail(e, "SwiGLU launch");
         if (L->tracing) trace_record(L->trace[2], st, cudaEventRecordExternal);
+        if (tc_down_ok(L, mode)) {
+            // the down projection on the tensor cores too: per (group, 128-row
+            // tile), each pair's h image against the expert's down rows, the
+            // row dots scattered to the pair's item
+            lbk::TcDotsArgs da = ta;
+            da.q8 = ws + o.hq;
+            da.q8_row_bytes = (K + 1) * nbf * lbk::kQ8IBytes;
+            da.dots = mode.dots;
+            da.dots_stride = L->H;
+            da.gate = L->d_down;
+            da.up = nullptr;
+            da.rows = (uint32_t)L->H;
+            da.nb = (uint32_t)nbf;
+            da.mats_per_group = 1;
+            da.out_by_token = true;
+            const uint64_t dtiles = (L->H + 127) / 128;
+            const uint64_t dctas = tc_groups_max(L->E_local, T * K) * dtiles;
+            if ((e = lbk::launch_tc_dots(L->down_type, da, (uint32_t)dctas, st)) != cudaSuccess)
+                return cuda_fail(e, "tensor-core down launch");
+            if (L->tracing) trace_record(L->trace[3], st, cudaEventRecordExternal);
+            return ok();
+        }
     } else {
         lbk::MoeGateUpArgs g{};
         g.hidden = L->H;
@@ -2069,9 +2100,10 @@ LBK_API int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void*
 
 // ---------------------------------------------- tensor-core grouped dots (prototype)
 
-LBK_API int32_t lbk_tc_grouped_dots(lbk_context* ctx, const lbk_tc_matrix* mats, uint32_t nmat, const uint32_t* jobs,
-                                    uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes,
+LBK_API int32_t lbk_tc_grouped_dots(lbk_context* ctx, int32_t type, const lbk_tc_matrix* mats, uint32_t nmat,
+                                    const uint32_t* jobs, uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes,
                                     const uint32_t* pair_tokens, float* dots, uint64_t dots_stride, void* stream) {
+    if (type != LBK_TYPE_IQ2_S && type != LBK_TYPE_IQ3_S) return fail(LBK_UNSUPPORTED_TYPE, "tensor-core dots type");
     if (ctx == nullptr || mats == nullptr || jobs == nullptr || q8 == nullptr || pair_tokens == nullptr ||
         dots == nullptr)
         return fail(LBK_INVALID_PARAMETER, "null pointer");
@@ -2081,6 +2113,6 @@ LBK_API int32_t lbk_tc_grouped_dots(lbk_context* ctx, const lbk_tc_matrix* mats,
     if (int32_t s = set_device(ctx)) return s;
     lbk::TcDotsArgs a{reinterpret_cast<const lbk::TcMatrix*>(mats), nmat, reinterpret_cast<const uint4*>(jobs), q8,
                       q8_row_bytes, pair_tokens, dots, dots_stride, ctx->status, ctx->tables()};
-    cudaError_t e = lbk::launch_tc_dots_iq2(a, njobs, as_stream(stream));
+    cudaError_t e = lbk::launch_tc_dots(type, a, njobs, as_stream(stream));
     return e == cudaSuccess ? ok() : cuda_fail(e, "tensor-core dots launch");
 }

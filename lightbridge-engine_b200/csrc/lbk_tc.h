@@ -6,7 +6,7 @@
 namespace lbk {
 
 struct TcMatrix {  // layout of lbk_tc_matrix
-    const uint8_t* data;  // IQ2_S, planar rows
+    const uint8_t* data;  // IQ2_S or IQ3_S, planar rows
     uint32_t rows, nb;
     uint64_t out_offset;  // column of this matrix's first row in a pair's dots
 };
@@ -30,9 +30,11 @@ struct TcDotsArgs {
     // column rows + r.
     const uint4* groups;         // {expert, first pair, pairs, 0}
     const uint32_t* ngroups;
-    const uint8_t* const* gate;  // expert -> planar IQ2_S rows
+    const uint8_t* const* gate;  // expert -> planar rows (the down matrices when mats_per_group is 1)
     const uint8_t* const* up;
     uint32_t experts, rows, nb;
+    uint32_t mats_per_group;     // 2: gate and up; 1: one matrix per expert
+    bool out_by_token;           // a pair's dots go to row pair_tokens[p] instead of p
 };
 
 // SwiGLU and Q8_K of h per grouped pair, from the tensor-core gate/up dots:
@@ -48,7 +50,9 @@ struct TcSwigluArgs {
 };
 
 int tc_dots_smem_bytes();
-cudaError_t launch_tc_dots_iq2(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream);
+// type: LBK_TYPE_IQ2_S (groups of 16 weights, two masked MMAs per 32) or
+// LBK_TYPE_IQ3_S (groups of 32, one MMA each; no 0.125 factor)
+cudaError_t launch_tc_dots(int type, const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream);
 cudaError_t launch_tc_swiglu_quant(const TcSwigluArgs& a, int sm_count, cudaStream_t stream);
 
 }  // namespace lbk

@@ -114,7 +114,43 @@ __device__ __forceinline__ void decode_iq2_hb(const Iq2HB& w, const uint32_t* ta
 // Epilogue of the unit in TMEM buffer BUF (a half block; BUF is its half):
 // the exact integer group sums per token, and after the second half the
 // block's f32 product, chained in block order.
-template <int BUF>
+// Signed weight bytes of one IQ3_S half block (the decode of dot_hb for
+// IQ3_S, the signs applied to the weights instead of the activations): words
+// 8g + 2l, 8g + 2l + 1 hold weights 8l .. 8l + 7 of group g.
+__device__ __forceinline__ void decode_iq3_hb(const Iq3HB& w, const uint32_t* tab, uint32_t copy, uint32_t (&out)[32]) {
+#pragma unroll
+    for (int gi = 0; gi < 4; gi++) {
+        const uint32_t qa = gi < 2 ? w32(w.qs0, gi * 2) : w32(w.qs1, (gi - 2) * 2);
+        const uint32_t qb = gi < 2 ? w32(w.qs0, gi * 2 + 1) : w32(w.qs1, (gi - 2) * 2 + 1);
+        const uint32_t sgw = w32(w.sg, gi);
+        const uint32_t Q = (w.qh >> (2 * gi)) & 0x03030303u;
+        const uint32_t Q1 = Q & 0x01010101u;
+        const uint32_t Q2 = (Q >> 1) & 0x01010101u;
+        const uint32_t sp[4] = {signs_at2<0>(sgw), signs_at2<1>(sgw), signs_at2<2>(sgw), signs_at2<3>(sgw)};
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const uint32_t q2 = l < 2 ? qa : qb;
+            const uint32_t i1 = prmt(q2, Q1, sel_idx(2 * (l & 1), l));
+            const uint32_t i2 = prmt(q2, Q2, sel_idx(2 * (l & 1) + 1, l));
+            const uint32_t g1 = tab[i1 * kTabCopies + copy];
+            const uint32_t g2 = tab[i2 * kTabCopies + copy];
+            const uint32_t slo = (sp[l] & 0x4444u) | 0x3210u;
+            const uint32_t shi = ((sp[l] >> 16) & 0x4444u) | 0x3210u;
+            out[gi * 8 + 2 * l] = prmt(g1, (uint32_t)__vneg4((int)g1), slo);
+            out[gi * 8 + 2 * l + 1] = prmt(g2, (uint32_t)__vneg4((int)g2), shi);
+        }
+    }
+}
+
+template <int T>
+struct TcType {
+    static constexpr bool kIq2 = T == LBK_TYPE_IQ2_S;
+    static constexpr int kAcc = kIq2 ? 8 : 4;  // accumulators per half block: 16-weight groups / 32-weight groups
+    static constexpr int kEntries = kIq2 ? kIq2CodeEntries : kIq3GridEntries;
+    using HB = typename std::conditional<kIq2, Iq2HB, Iq3HB>::type;
+};
+
+template <int T, int BUF>
 __device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, uint32_t tmem, int warp, int npad,
                                             uint32_t n, int b, const float* s_dx, const uint32_t (&ls)[2][8],
                                             const uint32_t (&dw)[2], uint32_t (&phase)[2], bool& live,
@@ -128,7 +164,7 @@ __device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, 
     const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(BUF * 256);
     // two groups' accumulators per wait (up to four loads in flight)
 #pragma unroll
-    for (int g = 0; g < 8; g += 2) {
+    for (int g = 0; g < TcType<T>::kAcc; g += 2) {
         uint32_t r[2][kTcMaxTok];
 #pragma unroll
         for (int gg = 0; gg < 2; gg++) {
@@ -158,7 +194,9 @@ __device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, 
     }
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a) {
+template <int T>
+__global__ void __launch_bounds__(kTcThreads, 1) tc_dots_kernel(TcDotsArgs a) {
+    using TT = TcType<T>;
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t s_bar[2];
     __shared__ uint32_t s_tmem;
@@ -174,8 +212,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
         }
         mat = a.mats[job.x];
     } else {
-        const uint32_t tiles = (a.rows + kTcRows - 1) / kTcRows;
-        const uint32_t g = blockIdx.x / (2 * tiles), m = (blockIdx.x / tiles) & 1u, tile = blockIdx.x % tiles;
+        const uint32_t tiles = (a.rows + kTcRows - 1) / kTcRows, mpg = a.mats_per_group;
+        const uint32_t g = blockIdx.x / (mpg * tiles), m = (blockIdx.x / tiles) % mpg, tile = blockIdx.x % tiles;
         if (g >= __ldcg(a.ngroups)) return;  // fewer groups than the grid's bound
         const uint4 gr = __ldcg(a.groups + g);
         if (gr.x >= a.experts || gr.z == 0 || gr.z > (uint32_t)kTcMaxTok) {
@@ -193,7 +231,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
     const int npad = n <= 16 ? 16 : 32;
     const uint32_t idesc = idesc_i8(kTcRows, npad);
     const int nb = (int)mat.nb;
-    const uint32_t rs = planar_row_bytes(TypeInfo<LBK_TYPE_IQ2_S>::kBlockBytes, nb);
+    const uint32_t rs = planar_row_bytes(TypeInfo<T>::kBlockBytes, nb);
     const uint32_t row = row0 + (uint32_t)tid;
     const bool row_ok = row < mat.rows;
 
@@ -203,9 +241,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
     float* s_dx = reinterpret_cast<float*>(smem + kOffDx);
     const int achunk = 3 * npad * 16;  // [lo | zeros | hi] of one 32-byte chunk, npad tokens
 
-    // the code table, compact, kTabCopies interleaved copies (entry e's copy j at e * kTabCopies + j)
-    for (int i = tid; i < 1024 * kTabCopies; i += kTcThreads)
-        tab[i] = reinterpret_cast<const uint32_t*>(a.tables.iq2_codes)[(i / kTabCopies) * 32];
+    // the code table / grid, compact, kTabCopies interleaved copies (entry e's copy j at e * kTabCopies + j)
+    const uint32_t* img = reinterpret_cast<const uint32_t*>(TT::kIq2 ? (const void*)a.tables.iq2_codes
+                                                                      : (const void*)a.tables.iq3_grid);
+    for (int i = tid; i < TT::kEntries * kTabCopies; i += kTcThreads) tab[i] = img[(i / kTabCopies) * 32];
     // zero rows of the activation buffers (the masks, and padded tokens)
     for (int i = tid; i < 2 * kAUnit / 16; i += kTcThreads)
         reinterpret_cast<uint4*>(smem + kOffA)[i] = make_uint4(0, 0, 0, 0);
@@ -233,12 +272,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
         chain[t * kTcThreads] = 0.0f;
         bsum[t] = 0;
     }
-    uint32_t ls[2][8];  // the units' group multipliers 1 + 2s (this thread's row)
+    uint32_t ls[2][8];  // the units' group multipliers (this thread's row): IQ2_S 8 x (1 + 2s), IQ3_S 4
     uint32_t dw[2];     // their block scales (binary16 bits)
     uint32_t phase[2] = {0, 0};
     bool live = true;
 
-    Iq2HB w{};
+    typename TT::HB w{};
     const uint8_t* rowp = mat.data + (uint64_t)(row_ok ? row : row0) * rs;
     uint4 av[2];  // this thread's activation words of the next unit (pairs * 8 <= 2 * kTcThreads)
     auto load_w = [&](int bb, int hh) {
@@ -253,11 +292,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
             }
         }
         if (row_ok) {
-            w.qs = __ldg(reinterpret_cast<const uint4*>(rowp + bb * 32 + 16 * hh));
-            w.sg = __ldg(reinterpret_cast<const uint4*>(rowp + nb * 32 + bb * 32 + 16 * hh));
-            w.qh = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 64 + bb * 8 + 4 * hh));
-            w.sc = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 72 + bb * 8 + 4 * hh));
-            w.d = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rowp + nb * 80 + bb * 2));
+            if constexpr (TT::kIq2) {  // planar IQ2_S: qs | signs | qh | scales | d
+                w.qs = __ldg(reinterpret_cast<const uint4*>(rowp + bb * 32 + 16 * hh));
+                w.sg = __ldg(reinterpret_cast<const uint4*>(rowp + nb * 32 + bb * 32 + 16 * hh));
+                w.qh = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 64 + bb * 8 + 4 * hh));
+                w.sc = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 72 + bb * 8 + 4 * hh));
+                w.d = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rowp + nb * 80 + bb * 2));
+            } else {  // planar IQ3_S: qs | signs | qh | scales | d
+                w.qs0 = __ldg(reinterpret_cast<const uint4*>(rowp + bb * 64 + 32 * hh));
+                w.qs1 = __ldg(reinterpret_cast<const uint4*>(rowp + bb * 64 + 32 * hh + 16));
+                w.sg = __ldg(reinterpret_cast<const uint4*>(rowp + nb * 64 + bb * 32 + 16 * hh));
+                w.qh = __ldg(reinterpret_cast<const uint32_t*>(rowp + nb * 96 + bb * 8 + 4 * hh));
+                w.sc = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rowp + nb * 104 + bb * 4 + 2 * hh));
+                w.d = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(rowp + nb * 108 + bb * 2));
+            }
         }
     };
     load_w(0, 0);
@@ -270,17 +318,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
             uint8_t* au = smem + kOffA + buf * kAUnit;
             // decode this thread's row, half block (b, h) (loaded one unit ahead)
             uint32_t q[32];
-            decode_iq2_hb(w, tab, (uint32_t)(tid & (kTabCopies - 1)), q);
+            if constexpr (TT::kIq2)
+                decode_iq2_hb(w, tab, (uint32_t)(tid & (kTabCopies - 1)), q);
+            else
+                decode_iq3_hb(w, tab, (uint32_t)(tid & (kTabCopies - 1)), q);
             if (!row_ok) {
 #pragma unroll
                 for (int i = 0; i < 32; i++) q[i] = 0u;
             }
-            const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;
-            const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;
+            if constexpr (TT::kIq2) {
+                const uint32_t s1w = (w.sc & 0x0f0f0f0fu) * 2u + 0x01010101u;
+                const uint32_t s2w = ((w.sc >> 4) & 0x0f0f0f0fu) * 2u + 0x01010101u;
 #pragma unroll
-            for (int gi = 0; gi < 4; gi++) {
-                ls[buf][2 * gi] = prmt(s1w, 0, 0x4440u | gi);
-                ls[buf][2 * gi + 1] = prmt(s2w, 0, 0x4440u | gi);
+                for (int gi = 0; gi < 4; gi++) {
+                    ls[buf][2 * gi] = prmt(s1w, 0, 0x4440u | gi);
+                    ls[buf][2 * gi + 1] = prmt(s2w, 0, 0x4440u | gi);
+                }
+            } else {  // one multiplier 1 + 2 * nibble per 32-weight group (dot_hb for IQ3_S)
+                const uint32_t st = (w.sc & 0x0f0fu) | ((w.sc & 0xf0f0u) << 12);
+                const uint32_t sw = st * 2u + 0x01010101u;
+#pragma unroll
+                for (int gi = 0; gi < 4; gi++) ls[buf][gi] = prmt(sw, 0, 0x4440u | (uint32_t)((gi & 1) * 2 + (gi >> 1)));
             }
             dw[buf] = w.d;
             // chunk gi: [K-half 0: 16 row groups x 128 B][K-half 1: 16 x 128 B]
@@ -322,31 +380,41 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_iq2_kernel(TcDotsArgs a
                 for (int gi = 0; gi < 4; gi++) {
                     const uint64_t da = smem_desc(wb + gi * kWChunk, 2048, 128);
                     const uint32_t ac = ab + (uint32_t)(gi * achunk);
-                    const uint64_t dlo = smem_desc(ac, (uint32_t)(npad * 16), 128);  // K-half 1 -> the zeros
-                    const uint64_t dhi = smem_desc(ac + (uint32_t)(npad * 16), (uint32_t)(npad * 16), 128);  // half 0 zeros
-                    const uint32_t d0 = tmem + (uint32_t)(buf * 256 + (2 * gi) * npad);
-                    tc_mma_i8(d0, da, dlo, idesc);
-                    tc_mma_i8(d0 + (uint32_t)npad, da, dhi, idesc);
+                    if constexpr (TT::kIq2) {  // two 16-weight groups: one MMA each, the other half zeroed
+                        const uint64_t dlo = smem_desc(ac, (uint32_t)(npad * 16), 128);  // K-half 1 -> the zeros
+                        const uint64_t dhi = smem_desc(ac + (uint32_t)(npad * 16), (uint32_t)(npad * 16), 128);
+                        const uint32_t d0 = tmem + (uint32_t)(buf * 256 + (2 * gi) * npad);
+                        tc_mma_i8(d0, da, dlo, idesc);
+                        tc_mma_i8(d0 + (uint32_t)npad, da, dhi, idesc);
+                    } else {  // one 32-weight group: K-half 1 is the hi part, past the zeros
+                        const uint64_t dfull = smem_desc(ac, (uint32_t)(2 * npad * 16), 128);
+                        tc_mma_i8(tmem + (uint32_t)(buf * 256 + gi * npad), da, dfull, idesc);
+                    }
                 }
                 tc_commit(bar0 + 8 * buf);
             }
             // the previous unit's epilogue while these MMAs run
             if (h == 1)
-                tc_epilogue<0>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
+                tc_epilogue<T, 0>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
             else if (b > 0)
-                tc_epilogue<1>(a, bar0, tmem, warp, npad, n, b - 1, s_dx, ls, dw, phase, live, bsum, chain);
+                tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, b - 1, s_dx, ls, dw, phase, live, bsum, chain);
             // the next decode overwrites the other buffer: its MMAs completed
             // (waited above) and its accumulators are read
             __syncthreads();
         }
     }
-    tc_epilogue<1>(a, bar0, tmem, warp, npad, n, nb - 1, s_dx, ls, dw, phase, live, bsum, chain);
+    tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, nb - 1, s_dx, ls, dw, phase, live, bsum, chain);
 
     if (row_ok && live) {
-        float* out = a.dots + (uint64_t)p0 * a.dots_stride + mat.out_offset + row;
 #pragma unroll
-        for (int t = 0; t < kTcMaxTok; t++)
-            if (t < (int)n) out[(uint64_t)t * a.dots_stride] = __fmul_rn(0.125f, chain[t * kTcThreads]);
+        for (int t = 0; t < kTcMaxTok; t++) {
+            if (t < (int)n) {
+                // the pair's row: its grouped position, or its token (item) when scattering
+                const uint64_t r = a.out_by_token ? (uint64_t)a.pair_tokens[p0 + t] : (uint64_t)(p0 + t);
+                const float c = chain[t * kTcThreads];
+                a.dots[r * a.dots_stride + mat.out_offset + row] = TT::kIq2 ? __fmul_rn(0.125f, c) : c;
+            }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -400,12 +468,19 @@ cudaError_t launch_tc_swiglu_quant(const TcSwigluArgs& a, int sm_count, cudaStre
     return cudaGetLastError();
 }
 
-cudaError_t launch_tc_dots_iq2(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream) {
+template <int T>
+cudaError_t launch_tc_dots_t(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream) {
     if (jobs == 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(tc_dots_iq2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemLaunch);
+    cudaError_t e = cudaFuncSetAttribute(tc_dots_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemLaunch);
     if (e != cudaSuccess) return e;
-    tc_dots_iq2_kernel<<<jobs, kTcThreads, kTcSmemLaunch, stream>>>(a);
+    tc_dots_kernel<T><<<jobs, kTcThreads, kTcSmemLaunch, stream>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t launch_tc_dots(int type, const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream) {
+    if (type == LBK_TYPE_IQ2_S) return launch_tc_dots_t<LBK_TYPE_IQ2_S>(a, jobs, stream);
+    if (type == LBK_TYPE_IQ3_S) return launch_tc_dots_t<LBK_TYPE_IQ3_S>(a, jobs, stream);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace lbk

@@ -208,7 +208,7 @@ def _load() -> ctypes.CDLL:
         "lbk_ep_items_forward_counted": ([P, P, P, P, U64, P, P, U64, P], I32),
         "lbk_ep_scatter": ([P, P, U32, U32, U64, P, P, P, U64, P], I32),
         "lbk_ep_shared": ([P, P, U64, U64, P, P, U64, P], I32),
-        "lbk_tc_grouped_dots": ([P, P, U32, P, U32, P, U64, P, P, U64, P], I32),
+        "lbk_tc_grouped_dots": ([P, I32, P, U32, P, U32, P, U64, P, P, U64, P], I32),
         "lbk_ep_combine_exchange": ([P, P, U32, U64, U64, P, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
         "lbk_moe_layer_trace_read": ([P, ctypes.POINTER(ctypes.c_float)], I32),
@@ -341,10 +341,10 @@ class Context:
         check(lib.lbk_gemv(self.ptr, ctypes.byref(m), _ptr(x), _ptr(y), _ptr(q8_scratch), n, _stream(stream)))
 
     def tc_grouped_dots(self, mats, nmat: int, jobs, njobs: int, q8, q8_row_bytes: int, pair_tokens, dots,
-                        dots_stride: int, stream=None) -> None:
+                        dots_stride: int, stream=None, type: int = TYPE_IQ2_S) -> None:
         """lbk_tc_grouped_dots: mats a device tensor of lbk_tc_matrix records
         (tc_matrices), jobs a device int32 [njobs, 4] tensor."""
-        check(lib.lbk_tc_grouped_dots(self.ptr, _ptr(mats), nmat, _ptr(jobs), njobs, _ptr(q8), q8_row_bytes,
+        check(lib.lbk_tc_grouped_dots(self.ptr, type, _ptr(mats), nmat, _ptr(jobs), njobs, _ptr(q8), q8_row_bytes,
                                       _ptr(pair_tokens), _ptr(dots), dots_stride, _stream(stream)))
 
     def gemv_accumulate_scaled(self, m: Matrix, x, y, scale: float, q8_scratch=None, stream=None) -> None:

@@ -1,7 +1,8 @@
 """GPU parity: GEMV and scaled accumulation against the CPU oracle, bit-exact,
 including BASELINE configs 1 (Q4_K 4096x4096) and 2 (IQ2_S / IQ3_S
-6144x4096) and the checkpoint's output projection (Q5_K, 120832 rows of
-4096) at full size, and the validate-before-write behaviour of
+6144x4096), the checkpoint's output projection (Q5_K, 120832 rows of
+4096) and a block's attention projections at full size, and the
+validate-before-write behaviour of
 bridge-kernels-reference/tests/gemv.rs:110-262.
 """
 
@@ -49,6 +50,12 @@ def test_gemv_matches_oracle(ty, k, rows, layout):
         (orc.TYPE_IQ2_S, 4096, 6144, 1, (0.001, 0.01)),  # config 2
         (orc.TYPE_IQ3_S, 4096, 6144, 1, (0.001, 0.01)),  # config 2, IQ3_S variant
         (orc.TYPE_Q5_K, 4096, 120832, 5, (0.001, 0.02)),  # the checkpoint's output.weight (vocabulary rows)
+        # a Hy3 block's attention projections (schema.rs:120-170; profile.rs:22-29: hidden 4096,
+        # 64 heads, 8 KV heads, key / value length 128)
+        (orc.TYPE_IQ2_S, 4096, 8192, 6, (0.001, 0.01)),  # attn_q
+        (orc.TYPE_IQ2_S, 4096, 1024, 7, (0.001, 0.01)),  # attn_k
+        (orc.TYPE_Q4_K, 4096, 1024, 8, (0.001, 0.02)),   # attn_v
+        (orc.TYPE_IQ3_S, 8192, 4096, 9, (0.001, 0.01)),  # attn_output (input 64 x 128)
     ],
 )
 def test_baseline_matvec_configs_bit_exact(ty, k, rows, seed, d_range, layout):

@@ -1,7 +1,7 @@
-"""GPU parity: grouped row dots of IQ2_S matrices on the tcgen05 tensor cores
-(lbk_tc_grouped_dots, int8 MMA with one accumulator per 16-weight scale
-group) against the CPU oracle's gemv per token, bit for bit: matrices of
-K = 2048 and 4096, row counts that are not multiples of the 128-row tile,
+"""GPU parity: grouped row dots of IQ2_S and IQ3_S matrices on the tcgen05
+tensor cores (lbk_tc_grouped_dots, int8 MMA with one accumulator per scale
+group: 16 weights for IQ2_S, 32 for IQ3_S) against the CPU oracle's gemv per
+token, bit for bit: matrices of K = 1536 to 4096, row counts that are not multiples of the 128-row tile,
 groups of 1 to 32 tokens (both MMA widths, N = 16 and 32), tokens repeated
 across groups, and a malformed job reported without any write.
 """
@@ -42,12 +42,13 @@ def jobs_for(groups, rows_of):
     return np.array(jobs, dtype=np.int32).reshape(-1, 4), np.array(pair_tokens, dtype=np.int32)
 
 
-@pytest.mark.parametrize("k", [2048, 4096])
-def test_tc_grouped_dots_match_oracle_gemv(k):
-    rng = np.random.default_rng(17 + k)
+@pytest.mark.parametrize("ty,k", [(orc.TYPE_IQ2_S, 2048), (orc.TYPE_IQ2_S, 4096), (orc.TYPE_IQ3_S, 1536),
+                                  (orc.TYPE_IQ3_S, 4096)])
+def test_tc_grouped_dots_match_oracle_gemv(ty, k):
+    rng = np.random.default_rng(17 + k + ty)
     shapes = [200, 128, 384, 77]
-    ws = [synth.packed_np(rng, orc.TYPE_IQ2_S, k, rows) for rows in shapes]
-    wd = [planar_dev(orc.TYPE_IQ2_S, w, k) for w in ws]
+    ws = [synth.packed_np(rng, ty, k, rows) for rows in shapes]
+    wd = [planar_dev(ty, w, k) for w in ws]
     T = 40
     xs = rng.standard_normal((T, k)).astype(np.float32)
     q8 = dev(np.concatenate([q8_image(x) for x in xs]))
@@ -57,7 +58,8 @@ def test_tc_grouped_dots_match_oracle_gemv(k):
     stride = max(shapes)
     mats = dev(lbk.tc_matrices([(t.data_ptr(), rows, k // 256, 0) for t, rows in zip(wd, shapes)]))
     dots = torch.full((len(pair_tokens), stride), float("nan"), device="cuda")
-    ctx().tc_grouped_dots(mats, len(shapes), dev(jobs), len(jobs), q8, k // 256 * Q8I, dev(pair_tokens), dots, stride)
+    ctx().tc_grouped_dots(mats, len(shapes), dev(jobs), len(jobs), q8, k // 256 * Q8I, dev(pair_tokens), dots, stride,
+                          type=ty)
     clean_status()
     got = host(dots)
     want = {}
@@ -66,7 +68,7 @@ def test_tc_grouped_dots_match_oracle_gemv(k):
         for t in toks:
             key = (m, int(t))
             if key not in want:
-                want[key] = orc.gemv(orc.TYPE_IQ2_S, k, shapes[m], ws[m], xs[t])[0]
+                want[key] = orc.gemv(ty, k, shapes[m], ws[m], xs[t])[0]
             np.testing.assert_array_equal(bits(got[p, :shapes[m]]), bits(want[key]), err_msg=f"pair {p}: matrix {m} token {t}")
             p += 1
 
