@@ -35,7 +35,8 @@ namespace {
 constexpr int kTcThreads = 128;  // one thread per tile row (TMEM lane)
 constexpr int kTcRows = 128;
 constexpr int kTcMaxTok = 32;
-constexpr uint32_t kTmemCols = 512;  // two buffers of 8 accumulators x 32 columns
+// TMEM per CTA: two buffers of kAcc accumulators x 32 columns (IQ2_S: 512,
+// the whole of an SM's; IQ3_S: 256, so two CTAs share an SM)
 constexpr int kTabCopies = 8;        // copies of the 1024-entry code table (bank spread)
 
 // shared memory: [table 1024 * 8 words][W: 2 x 4 chunks x 4 KB][A: 2 x 4 chunks x 3 x 32 x 16 B][dx: 2 x 32]
@@ -49,10 +50,12 @@ constexpr int kOffA = kOffW + 2 * kWUnit;
 constexpr int kOffDx = kOffA + 2 * kAUnit;
 constexpr int kOffChain = kOffDx + 2 * kTcMaxTok * 4;  // [token][thread] f32 chains
 constexpr int kTcSmem = kOffChain + kTcMaxTok * kTcThreads * 4;
-// launched with more than half of an SM's shared memory: one CTA per SM, so
-// no CTA waits in tcgen05.alloc for another's 512 columns
+// IQ2_S launches take more than half of an SM's shared memory: one CTA per
+// SM, so no CTA waits in tcgen05.alloc for another's 512 columns. IQ3_S
+// launches take less: two CTAs per SM, 256 columns each.
 constexpr int kTcSmemLaunch = 116 * 1024;
 static_assert(kTcSmem <= kTcSmemLaunch, "shared memory");
+static_assert(2 * kTcSmem + 2 * 2048 <= 228 * 1024, "two IQ3_S CTAs per SM");
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
     // K-major, no swizzle: start, leading (K-half) and stride (8-row group)
@@ -147,6 +150,9 @@ struct TcType {
     static constexpr bool kIq2 = T == LBK_TYPE_IQ2_S;
     static constexpr int kAcc = kIq2 ? 8 : 4;  // accumulators per half block: 16-weight groups / 32-weight groups
     static constexpr int kEntries = kIq2 ? kIq2CodeEntries : kIq3GridEntries;
+    static constexpr uint32_t kBufCols = (uint32_t)kAcc * 32;  // one buffer: kAcc accumulators of up to 32 tokens
+    static constexpr uint32_t kTmemCols = 2 * kBufCols;
+    static constexpr int kSmemLaunch = kIq2 ? kTcSmemLaunch : kTcSmem;
     using HB = typename std::conditional<kIq2, Iq2HB, Iq3HB>::type;
 };
 
@@ -161,7 +167,7 @@ __device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, 
     }
     phase[BUF] ^= 1u;
     tc_fence_after();
-    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(BUF * 256);
+    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)BUF * TcType<T>::kBufCols;
     // two groups' accumulators per wait (up to four loads in flight)
 #pragma unroll
     for (int g = 0; g < TcType<T>::kAcc; g += 2) {
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_kernel(TcDotsArgs a) {
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          (uint32_t)__cvta_generic_to_shared(&s_tmem)),
-                     "r"(kTmemCols)
+                     "r"(TT::kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -383,12 +389,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_kernel(TcDotsArgs a) {
                     if constexpr (TT::kIq2) {  // two 16-weight groups: one MMA each, the other half zeroed
                         const uint64_t dlo = smem_desc(ac, (uint32_t)(npad * 16), 128);  // K-half 1 -> the zeros
                         const uint64_t dhi = smem_desc(ac + (uint32_t)(npad * 16), (uint32_t)(npad * 16), 128);
-                        const uint32_t d0 = tmem + (uint32_t)(buf * 256 + (2 * gi) * npad);
+                        const uint32_t d0 = tmem + (uint32_t)buf * TT::kBufCols + (uint32_t)((2 * gi) * npad);
                         tc_mma_i8(d0, da, dlo, idesc);
                         tc_mma_i8(d0 + (uint32_t)npad, da, dhi, idesc);
                     } else {  // one 32-weight group: K-half 1 is the hi part, past the zeros
                         const uint64_t dfull = smem_desc(ac, (uint32_t)(2 * npad * 16), 128);
-                        tc_mma_i8(tmem + (uint32_t)(buf * 256 + gi * npad), da, dfull, idesc);
+                        tc_mma_i8(tmem + (uint32_t)buf * TT::kBufCols + (uint32_t)(gi * npad), da, dfull, idesc);
                     }
                 }
                 tc_commit(bar0 + 8 * buf);
@@ -420,7 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_kernel(TcDotsArgs a) {
     __syncthreads();
     tc_fence_after();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TT::kTmemCols) : "memory");
 }
 
 // One warp per (grouped pair, 256-row block of h): SwiGLU of the block's
@@ -471,9 +477,10 @@ cudaError_t launch_tc_swiglu_quant(const TcSwigluArgs& a, int sm_count, cudaStre
 template <int T>
 cudaError_t launch_tc_dots_t(const TcDotsArgs& a, uint32_t jobs, cudaStream_t stream) {
     if (jobs == 0) return cudaSuccess;
-    cudaError_t e = cudaFuncSetAttribute(tc_dots_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemLaunch);
+    cudaError_t e =
+        cudaFuncSetAttribute(tc_dots_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcType<T>::kSmemLaunch);
     if (e != cudaSuccess) return e;
-    tc_dots_kernel<T><<<jobs, kTcThreads, kTcSmemLaunch, stream>>>(a);
+    tc_dots_kernel<T><<<jobs, kTcThreads, TcType<T>::kSmemLaunch, stream>>>(a);
     return cudaGetLastError();
 }
 
