@@ -642,6 +642,7 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
     passes = 8
     evs = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(names) + 1)]
            for _ in range(EP_LAYERS)]
+    items_seen = torch.zeros(EP_LAYERS, dtype=torch.int32, device=dev)  # the gathered count (the scatter resets it)
     sgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(sgraph, stream=stream):
         for i, (L, _) in enumerate(layers):
@@ -652,6 +653,7 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
             moe.shared(T, L)
             ev[2].record(stream)
             moe.dispatch(L)
+            items_seen[i:i + 1].copy_(moe.count)
             ev[3].record(stream)
             moe.compute(L)
             ev[4].record(stream)
@@ -671,7 +673,7 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
     barrier()
     ctx.raise_status()
     stage_ms = [a / (passes * EP_LAYERS) for a in acc]
-    items = int(moe.count.item())
+    items = int(items_seen[-1].item())
     t = torch.tensor([ms_layer] + stage_ms + [float(items > 0), float(items)], device=dev)
     if world > 1:
         tmax = t.clone()
@@ -899,8 +901,10 @@ def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(dev)
     ctx = lbk.Context(local_rank)
     # config 1 adds the checkpoint's output projection (Q5_K, 120832 vocabulary rows)
+    # config 2 adds a Hy3 block's attention projections (q, k: IQ2_S; v: Q4_K; output: IQ3_S over 8192)
     cases = [(TYPE_Q4_K, 4096, 4096), (TYPE_Q5_K, 4096, 120832)] if cfg == 1 else \
-        [(TYPE_IQ2_S, 4096, 6144), (TYPE_IQ3_S, 4096, 6144)]
+        [(TYPE_IQ2_S, 4096, 6144), (TYPE_IQ3_S, 4096, 6144), (TYPE_IQ2_S, 4096, 8192), (TYPE_IQ2_S, 4096, 1024),
+         (TYPE_Q4_K, 4096, 1024), (TYPE_IQ3_S, 8192, 4096)]
     results = []
     for ty, k, rows in cases:
         gen = torch.Generator(device=dev)
