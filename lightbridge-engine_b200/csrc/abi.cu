@@ -2098,7 +2098,7 @@ LBK_API int32_t lbk_validate_matrix(lbk_context* ctx, const lbk_matrix* w, void*
     return e == cudaSuccess ? ok() : cuda_fail(e, "validate launch");
 }
 
-// ---------------------------------------------- tensor-core grouped dots (prototype)
+// ---------------------------------------------- tensor-core grouped dots
 
 LBK_API int32_t lbk_tc_grouped_dots(lbk_context* ctx, int32_t type, const lbk_tc_matrix* mats, uint32_t nmat,
                                     const uint32_t* jobs, uint32_t njobs, const uint8_t* q8, uint64_t q8_row_bytes,

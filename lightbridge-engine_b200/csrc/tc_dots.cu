@@ -1,5 +1,10 @@
-// tc_dots.cu -- grouped row dots of IQ2_S matrices on the 5th-generation
-// tensor cores (tcgen05.mma kind::i8), bit-identical to the dp4a kernels.
+// tc_dots.cu -- grouped row dots of IQ2_S and IQ3_S matrices on the
+// 5th-generation tensor cores (tcgen05.mma kind::i8), bit-identical to the
+// dp4a kernels. The expert-parallel items path runs its gate/up (IQ2_S) and
+// down (IQ3_S) here when an expert has enough pairs. IQ3_S differs from the
+// IQ2_S scheme below only in its groups: one multiplier per 32 weights, so
+// one MMA and one accumulator per 32-byte chunk, with the signs applied to
+// the weight bytes.
 //
 // A job is one 128-row tile of one matrix and up to 32 tokens (the pairs
 // routed to one expert). The reference's dot of an IQ2_S block with a Q8_K
