@@ -290,7 +290,7 @@ int32_t lbk_moe_layer_set_grouping(lbk_moe_layer* layer, uint64_t min_tokens);
  * run their gate/up projections on the tcgen05 tensor cores (IQ2_S gate/up:
  * int8 MMA, one accumulator per 16-weight scale group, see
  * lbk_tc_grouped_dots) when the expected pairs per expert -- cap_items / the
- * global expert count -- reach `min_pairs_per_expert` (default 10; 0: never).
+ * global expert count -- reach `min_pairs_per_expert` (default 4; 0: never).
  * SwiGLU and Q8_K(h) follow per pair, and an IQ3_S or IQ2_S down projection
  * runs on the tensor cores too (else on the grouped kernel); results are
  * bit-identical either way. No counterpart in the reference,

@@ -60,7 +60,7 @@ struct lbk_moe_layer {
     void* owned;                         // device memory freed with the layer (lbk_moe_layer_load)
     uint64_t group_min = 8;              // calls of at least this many tokens (items) run the grouped kernels; 0: never
     bool group_set = false;              // group_min set by lbk_moe_layer_set_grouping
-    uint64_t tc_min = 10;                // expert-parallel items: tensor-core gate/up from this many pairs per expert; 0: never
+    uint64_t tc_min = 4;                 // expert-parallel items: tensor cores from this many expected pairs per expert; 0: never
     uint32_t wait_limit = 1u << 20;      // polls of the down kernel's wait for the single-token routing flag
     // Block workspaces between lbk_moe_block_route and lbk_moe_block_finish,
     // with the routed call's token count (the reference keeps this phase in
@@ -1857,9 +1857,10 @@ LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t
     // holding all 192). Without a rule set on the layer, the capacity per
     // expert decides (the count itself is only known on the device).
     if (!layer->group_set) m.grouped = cap_items >= 4 * layer->E_local;
-    // Gate/up on the tensor cores (grouped items, IQ2_S): 1.8x the dp4a
-    // grouped kernel at 21 pairs per expert, slower below about 10. With
-    // every rank full, the pairs per local expert are cap_items / E.
+    // Gate/up and down on the tensor cores (grouped items): 3.0x the dp4a
+    // grouped kernels at 21 pairs per expert, 1.2x at 5.3, even at 5.3 with
+    // 24 experts, slower at 2.7. With every rank full, the pairs per local
+    // expert are cap_items / E.
     m.tc = layer->tc_min != 0 && layer->gate_type == LBK_TYPE_IQ2_S && cap_items >= layer->tc_min * layer->E &&
            (m.grouped || (layer->group_min != 0 && cap_items >= layer->group_min));
     if (layer->tracing) {  // no router here: its interval is empty, gate/up starts now

@@ -156,8 +156,13 @@ struct TcType {
     static constexpr int kAcc = kIq2 ? 8 : 4;  // accumulators per half block: 16-weight groups / 32-weight groups
     static constexpr int kEntries = kIq2 ? kIq2CodeEntries : kIq3GridEntries;
     static constexpr uint32_t kBufCols = (uint32_t)kAcc * 32;  // one buffer: kAcc accumulators of up to 32 tokens
-    static constexpr uint32_t kTmemCols = 2 * kBufCols;
-    static constexpr int kSmemLaunch = kIq2 ? kTcSmemLaunch : kTcSmem;
+    // TMEM buffers: IQ3_S double-buffers (its MMAs overlap the previous
+    // unit's epilogue) in 256 columns; IQ2_S (8 accumulators) single-buffers
+    // in 256 columns too, so that two CTAs share an SM and one CTA's MMA
+    // waits overlap the other's decode
+    static constexpr uint32_t kTmemBufs = kIq2 ? 1 : 2;
+    static constexpr uint32_t kTmemCols = kTmemBufs * kBufCols;
+    static constexpr int kSmemLaunch = kTcSmem;
     using HB = typename std::conditional<kIq2, Iq2HB, Iq3HB>::type;
 };
 
@@ -172,7 +177,8 @@ __device__ __forceinline__ void tc_epilogue(const TcDotsArgs& a, uint32_t bar0, 
     }
     phase[BUF] ^= 1u;
     tc_fence_after();
-    const uint32_t tbase = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)BUF * TcType<T>::kBufCols;
+    const uint32_t tbase =
+        tmem + ((uint32_t)(warp * 32) << 16) + (TcType<T>::kTmemBufs == 2 ? (uint32_t)BUF * TcType<T>::kBufCols : 0u);
     // two groups' accumulators per wait (up to four loads in flight)
 #pragma unroll
     for (int g = 0; g < TcType<T>::kAcc; g += 2) {
@@ -394,27 +400,38 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_kernel(TcDotsArgs a) {
                     if constexpr (TT::kIq2) {  // two 16-weight groups: one MMA each, the other half zeroed
                         const uint64_t dlo = smem_desc(ac, (uint32_t)(npad * 16), 128);  // K-half 1 -> the zeros
                         const uint64_t dhi = smem_desc(ac + (uint32_t)(npad * 16), (uint32_t)(npad * 16), 128);
-                        const uint32_t d0 = tmem + (uint32_t)buf * TT::kBufCols + (uint32_t)((2 * gi) * npad);
+                        const uint32_t d0 = tmem + (TT::kTmemBufs == 2 ? (uint32_t)buf * TT::kBufCols : 0u) +
+                                            (uint32_t)((2 * gi) * npad);
                         tc_mma_i8(d0, da, dlo, idesc);
                         tc_mma_i8(d0 + (uint32_t)npad, da, dhi, idesc);
                     } else {  // one 32-weight group: K-half 1 is the hi part, past the zeros
                         const uint64_t dfull = smem_desc(ac, (uint32_t)(2 * npad * 16), 128);
-                        tc_mma_i8(tmem + (uint32_t)buf * TT::kBufCols + (uint32_t)(gi * npad), da, dfull, idesc);
+                        tc_mma_i8(tmem + (TT::kTmemBufs == 2 ? (uint32_t)buf * TT::kBufCols : 0u) + (uint32_t)(gi * npad),
+                                  da, dfull, idesc);
                     }
                 }
                 tc_commit(bar0 + 8 * buf);
             }
-            // the previous unit's epilogue while these MMAs run
-            if (h == 1)
-                tc_epilogue<T, 0>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
-            else if (b > 0)
-                tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, b - 1, s_dx, ls, dw, phase, live, bsum, chain);
+            if constexpr (TT::kTmemBufs == 2) {
+                // the previous unit's epilogue while these MMAs run
+                if (h == 1)
+                    tc_epilogue<T, 0>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
+                else if (b > 0)
+                    tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, b - 1, s_dx, ls, dw, phase, live, bsum, chain);
+            } else {
+                // one TMEM buffer: this unit's epilogue before the next unit's MMAs
+                if (h == 0)
+                    tc_epilogue<T, 0>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
+                else
+                    tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, b, s_dx, ls, dw, phase, live, bsum, chain);
+            }
             // the next decode overwrites the other buffer: its MMAs completed
             // (waited above) and its accumulators are read
             __syncthreads();
         }
     }
-    tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, nb - 1, s_dx, ls, dw, phase, live, bsum, chain);
+    if constexpr (TT::kTmemBufs == 2)
+        tc_epilogue<T, 1>(a, bar0, tmem, warp, npad, n, nb - 1, s_dx, ls, dw, phase, live, bsum, chain);
 
     if (row_ok && live) {
 #pragma unroll
