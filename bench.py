@@ -702,9 +702,11 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
         "limiter": max(stage_max, key=stage_max.get),
         "exchange": "peer memory over NVLink (CUDA IPC; plain peer loads and stores; step flags in the buffers, "
                     "no collective, no host read; one CUDA graph per step)",
-        "stage_timing": "a second graph with event nodes between the stages, run one after another (the timed "
-                        "graph runs the shared expert on a second stream, concurrent with dispatch, experts and "
-                        "return); a stage's time includes its wait for other ranks",
+        "stage_timing": "a second graph with event nodes between the stages, run one after another, with the "
+                        "return as its own call (lbk_ep_scatter); the timed graph runs the shared expert on a "
+                        "second stream, concurrent with dispatch and experts, and stores the experts' down rows "
+                        "straight into the home buffers (lbk_ep_items_return); a stage's time includes its wait "
+                        "for other ranks",
         "l2": f"{EP_LAYERS} resident layers per rank rotate within a step",
         "steps": steps,
     }

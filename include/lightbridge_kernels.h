@@ -458,7 +458,9 @@ int32_t lbk_ep_combine(lbk_moe_layer* layer, const uint8_t* q8, uint64_t tokens,
  *                    lbk_ep_items_forward, the count read on the device;
  *                    cap_items = world * cap * k bounds it);
  *   lbk_ep_scatter   each item's dots into its home rank's buffer, then flag
- *                    this rank's step done in every buffer;
+ *                    this rank's step done in every buffer (or, instead of
+ *                    these two, lbk_ep_items_return: the items' down rows
+ *                    stored in place);
  *   lbk_ep_combine_exchange  on the home rank: wait until every rank's dots
  *                    of this step are in, then combine from its buffer's
  *                    routing, images and dots, bit-identical to
@@ -494,6 +496,15 @@ int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_t world,
                        const float* dots, const uint64_t* returns, uint32_t* count, uint64_t cap_items, void* stream);
 int32_t lbk_ep_shared(lbk_moe_layer* layer, void* xbuf, uint64_t cap, uint64_t tokens, float* shared_dots,
                       void* workspace, uint64_t workspace_bytes, void* stream);
+/* lbk_ep_items_forward_counted and lbk_ep_scatter in one call, with no local
+ * copy of the dots: the down kernels store each item's row dots straight into
+ * its home rank's buffer at its return address (peer stores, then a system
+ * fence), and a one-CTA kernel then resets `count` and flags this rank's step
+ * done in every buffer. Same results bit for bit; one kernel and one round
+ * trip of the dots fewer. */
+int32_t lbk_ep_items_return(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,
+                            const uint8_t* q8_items, const lbk_routed* items, const uint64_t* returns, uint32_t* count,
+                            uint64_t cap_items, void* workspace, uint64_t workspace_bytes, void* stream);
 int32_t lbk_ep_combine_exchange(lbk_moe_layer* layer, void* xbuf, uint32_t world, uint64_t cap, uint64_t tokens,
                                 const float* shared_dots, float* out, void* workspace, uint64_t workspace_bytes,
                                 void* stream);

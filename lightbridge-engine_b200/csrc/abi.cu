@@ -887,6 +887,11 @@ struct MoeMode {
     const uint32_t* d_items = nullptr;  // items counted on the device (T is then the capacity)
     bool grouped = false;               // run the grouped kernels whatever the layer's rule
     bool tc = false;                    // grouped items: gate/up on the tensor cores (IQ2_S)
+    // items returned in place: item t's row dots to its home buffer (see
+    // MoeDownArgs::ret_addr), with no local dots
+    const uint2* ret = nullptr;
+    uint8_t* const* ret_peers = nullptr;
+    uint64_t ret_off = 0;
 };
 
 MoeMode full_mode(const lbk_moe_layer* L) { return MoeMode{L->k, true, true, nullptr, nullptr, (uint32_t)(L->k + 1)}; }
@@ -907,8 +912,8 @@ double grp_groups_est(double pairs, double experts, double gsize) {
 // The expert-parallel items' down projection on the tensor cores: IQ
 // weights, one dots row per item, no shared expert, no combine.
 bool tc_down_ok(const lbk_moe_layer* L, const MoeMode& m) {
-    return m.tc && (L->down_type == LBK_TYPE_IQ3_S || L->down_type == LBK_TYPE_IQ2_S) && m.dots != nullptr &&
-           m.dots_slots == 1 && !m.combine && !m.shared && m.k == 1;
+    return m.tc && (L->down_type == LBK_TYPE_IQ3_S || L->down_type == LBK_TYPE_IQ2_S) &&
+           (m.dots != nullptr || m.ret != nullptr) && m.dots_slots == 1 && !m.combine && !m.shared && m.k == 1;
 }
 
 // Expert stage of a several-token call on the grouped kernels: the routed
@@ -992,6 +997,9 @@ int32_t moe_experts_grouped(lbk_moe_layer* L, uint64_t T, const lbk_routed* rout
             da.nb = (uint32_t)nbf;
             da.mats_per_group = 1;
             da.out_by_token = true;
+            da.ret_addr = mode.ret;
+            da.ret_peers = mode.ret_peers;
+            da.ret_off = mode.ret_off;
             const uint64_t dtiles = (L->H + 127) / 128;
             const uint64_t dctas = tc_groups_max(L->E_local, T * K) * dtiles;
             if ((e = lbk::launch_tc_dots(L->down_type, da, (uint32_t)dctas, st)) != cudaSuccess)
@@ -1062,6 +1070,9 @@ int32_t moe_experts_grouped(lbk_moe_layer* L, uint64_t T, const lbk_routed* rout
     d.grp_pairs = grp_pairs;
     d.gsize_r = gr;
     d.gsize_s = gs;
+    d.ret_addr = mode.ret;
+    d.ret_peers = mode.ret_peers;
+    d.ret_off = mode.ret_off;
     d.status = ctx->status;
     d.tables = ctx->tables();
     {
@@ -1245,6 +1256,9 @@ int32_t moe_experts(lbk_moe_layer* L, const float* x, uint64_t T, const lbk_rout
             d.counters = reinterpret_cast<unsigned int*>(ws + o.dcounters);
             d.route_flag = g.route_flag;
             d.d_items = mode.d_items;
+            d.ret_addr = mode.ret;
+            d.ret_peers = mode.ret_peers;
+            d.ret_off = mode.ret_off;
             d.route_readers = g.route_flag ? reinterpret_cast<unsigned int*>(ws + o.rreaders) : nullptr;
             d.route_polls = L->wait_limit;
             e = lbk::launch_moe_down_tma(L->down_type, L->sdown_type, d, ctas, st);
@@ -1834,6 +1848,24 @@ LBK_API int32_t lbk_ep_gather(lbk_moe_layer* layer, const void* const* peers, ui
     return e == cudaSuccess ? ok() : cuda_fail(e, "gather launch");
 }
 
+namespace {
+// The kernels' choice for device-counted items of a capacity.
+void items_rules(const lbk_moe_layer* layer, uint64_t cap_items, MoeMode& m) {
+    // Grouped kernels decode a weight half block once per group of pairs: at
+    // 21 items per expert (64 tokens per rank on 8 ranks, 24 experts each)
+    // 23 % faster than one decode per item, equal at 2.7 per expert (one rank
+    // holding all 192). Without a rule set on the layer, the capacity per
+    // expert decides (the count itself is only known on the device).
+    if (!layer->group_set) m.grouped = cap_items >= 4 * layer->E_local;
+    // Gate/up and down on the tensor cores (grouped items): 3.0x the dp4a
+    // grouped kernels at 21 pairs per expert, 1.2x at 5.3, even at 5.3 with
+    // 24 experts, slower at 2.7. With every rank full, the pairs per local
+    // expert are cap_items / E.
+    m.tc = layer->tc_min != 0 && layer->gate_type == LBK_TYPE_IQ2_S && cap_items >= layer->tc_min * layer->E &&
+           (m.grouped || (layer->group_min != 0 && cap_items >= layer->group_min));
+}
+}  // namespace
+
 LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t* q8_items, const lbk_routed* items,
                                              const uint32_t* count, uint64_t cap_items, float* dots, void* workspace,
                                              uint64_t workspace_bytes, void* stream) {
@@ -1851,23 +1883,47 @@ LBK_API int32_t lbk_ep_items_forward_counted(lbk_moe_layer* layer, const uint8_t
     if (e != cudaSuccess) return cuda_fail(e, "zero counters");
     MoeMode m{1, false, false, q8_items, dots, 1};
     m.d_items = count;
-    // Grouped kernels decode a weight half block once per group of pairs: at
-    // 21 items per expert (64 tokens per rank on 8 ranks, 24 experts each)
-    // 23 % faster than one decode per item, equal at 2.7 per expert (one rank
-    // holding all 192). Without a rule set on the layer, the capacity per
-    // expert decides (the count itself is only known on the device).
-    if (!layer->group_set) m.grouped = cap_items >= 4 * layer->E_local;
-    // Gate/up and down on the tensor cores (grouped items): 3.0x the dp4a
-    // grouped kernels at 21 pairs per expert, 1.2x at 5.3, even at 5.3 with
-    // 24 experts, slower at 2.7. With every rank full, the pairs per local
-    // expert are cap_items / E.
-    m.tc = layer->tc_min != 0 && layer->gate_type == LBK_TYPE_IQ2_S && cap_items >= layer->tc_min * layer->E &&
-           (m.grouped || (layer->group_min != 0 && cap_items >= layer->group_min));
+    items_rules(layer, cap_items, m);
     if (layer->tracing) {  // no router here: its interval is empty, gate/up starts now
         trace_record(layer->trace[0], st, cudaEventRecordExternal);
         trace_record(layer->trace[1], st, cudaEventRecordExternal);
     }
     return moe_experts(layer, nullptr, cap_items, items, nullptr, ws, o, st, false, m);
+}
+
+LBK_API int32_t lbk_ep_items_return(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank,
+                                    uint64_t cap, const uint8_t* q8_items, const lbk_routed* items,
+                                    const uint64_t* returns, uint32_t* count, uint64_t cap_items, void* workspace,
+                                    uint64_t workspace_bytes, void* stream) {
+    if (layer == nullptr) return fail(LBK_INVALID_PARAMETER, "null layer");
+    if (int32_t s = ep_check_ranks(world, rank, cap)) return s;
+    if (int32_t s = ep_check(layer, cap_items, workspace, workspace_bytes, ep_ws_bytes(layer, cap_items))) return s;
+    if (peers == nullptr || q8_items == nullptr || items == nullptr || returns == nullptr || count == nullptr)
+        return fail(LBK_INVALID_PARAMETER, "null pointer");
+    if (!aligned(q8_items, 16)) return fail(LBK_INVALID_PARAMETER, "q8 items 16-byte alignment");
+    lbk_context* ctx = layer->ctx;
+    if (int32_t s = set_device(ctx)) return s;
+    cudaStream_t st = as_stream(stream);
+    const WsLayout o = moe_ws(layer, cap_items, 1);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + o.counters, 0, o.counter_words * 4, st);
+    if (e != cudaSuccess) return cuda_fail(e, "zero counters");
+    const lbk_ep_exchange xl = ep_exchange(layer, cap);
+    MoeMode m{1, false, false, q8_items, nullptr, 1};
+    m.d_items = count;
+    m.ret = reinterpret_cast<const uint2*>(returns);
+    m.ret_peers = reinterpret_cast<uint8_t* const*>(peers);
+    m.ret_off = xl.dots;
+    items_rules(layer, cap_items, m);
+    if (layer->tracing) {
+        trace_record(layer->trace[0], st, cudaEventRecordExternal);
+        trace_record(layer->trace[1], st, cudaEventRecordExternal);
+    }
+    if (int32_t s = moe_experts(layer, nullptr, cap_items, items, nullptr, ws, o, st, false, m)) return s;
+    lbk::EpScatterArgs a{reinterpret_cast<uint8_t* const*>(peers), world, rank, xl.control, xl.dots, nullptr,
+                         reinterpret_cast<const uint2*>(returns), count, (uint32_t)cap_items, (uint32_t)layer->H};
+    e = lbk::launch_ep_signal(a, st);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "signal launch");
 }
 
 LBK_API int32_t lbk_ep_scatter(lbk_moe_layer* layer, void* const* peers, uint32_t world, uint32_t rank, uint64_t cap,

@@ -157,6 +157,19 @@ __global__ void __launch_bounds__(kScatterThreads) ep_scatter_kernel(EpScatterAr
     }
 }
 
+// Items returned in place by the down kernels (their rows already fenced):
+// reset the item count and release done[rank] = step in every buffer.
+__global__ void ep_signal_kernel(EpScatterArgs a) {
+    EpControl* me = reinterpret_cast<EpControl*>(a.peers[a.rank] + a.off_ctl);
+    const uint32_t step = __ldcg(&me->step);
+    if (threadIdx.x == 0) *a.d_count = 0u;
+    __threadfence_system();
+    for (uint32_t r = threadIdx.x; r < a.world; r += blockDim.x) {
+        EpControl* c = reinterpret_cast<EpControl*>(a.peers[r] + a.off_ctl);
+        st_release_sys(&c->done[a.rank], step);
+    }
+}
+
 // Raise this rank's step number; store the token count; publish.
 __global__ void ep_publish_kernel(EpControl* ctl, uint32_t tokens) {
     const uint32_t step = ctl->step + 1u;
@@ -182,6 +195,11 @@ cudaError_t launch_ep_scatter(const EpScatterArgs& a, int sm_count, cudaStream_t
     uint64_t grid = a.cap_items < (uint64_t)sm_count * 4 ? a.cap_items : (uint64_t)sm_count * 4;
     if (grid < 1) grid = 1;
     ep_scatter_kernel<<<(unsigned)grid, kScatterThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_signal(const EpScatterArgs& a, cudaStream_t stream) {
+    ep_signal_kernel<<<1, 64, 0, stream>>>(a);
     return cudaGetLastError();
 }
 

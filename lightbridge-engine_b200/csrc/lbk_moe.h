@@ -95,6 +95,12 @@ struct MoeDownArgs {
     unsigned int* route_readers;
     uint32_t route_polls;            // polls of route_flag before LBK_TIMEOUT
     const uint32_t* d_items;         // see MoeGateUpArgs
+    // expert-parallel items returned in place: item t's row dots go straight
+    // to (float*)(ret_peers[ret_addr[t].x] + ret_off) + ret_addr[t].y * hidden
+    // (its home rank's buffer, over NVLink), then a system-scope fence; or null
+    const uint2* ret_addr;
+    uint8_t* const* ret_peers;
+    uint64_t ret_off;
     DeviceStatus* status;
     Tables tables;
 };
@@ -193,6 +199,9 @@ struct EpScatterArgs {
 cudaError_t launch_ep_gather(const EpGatherArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_ep_scatter(const EpScatterArgs& a, int sm_count, cudaStream_t stream);
 cudaError_t launch_ep_publish(EpControl* ctl, uint32_t tokens, cudaStream_t stream);
+// After items returned in place: reset the item count, release done[rank] =
+// step in every rank's buffer (what the scatter's last CTA does).
+cudaError_t launch_ep_signal(const EpScatterArgs& a, cudaStream_t stream);
 // The home rank's combine once every rank's dots are in (see launch_ep_combine):
 // waits at most `polls` polls for done[0, world) to reach this step.
 cudaError_t launch_ep_combine_wait(const EpControl* ctl, uint32_t world, uint32_t polls, const lbk_routed* routed,

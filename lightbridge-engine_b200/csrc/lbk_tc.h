@@ -35,6 +35,12 @@ struct TcDotsArgs {
     uint32_t experts, rows, nb;
     uint32_t mats_per_group;     // 2: gate and up; 1: one matrix per expert
     bool out_by_token;           // a pair's dots go to row pair_tokens[p] instead of p
+    // with out_by_token: token r's row goes to (float*)(ret_peers[ret_addr[r].x]
+    // + ret_off) + ret_addr[r].y * dots_stride instead (its home rank's buffer),
+    // then a system-scope fence; or null
+    const uint2* ret_addr;
+    uint8_t* const* ret_peers;
+    uint64_t ret_off;
 };
 
 // SwiGLU and Q8_K of h per grouped pair, from the tensor-core gate/up dots:

@@ -1055,7 +1055,9 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
             load_act();
         }
         negate_act();
-        float* drow = a.dots + ((uint64_t)t * a.dots_slots + slot) * H;
+        float* drow = a.ret_addr != nullptr
+                          ? reinterpret_cast<float*>(a.ret_peers[a.ret_addr[t].x] + a.ret_off) + (uint64_t)a.ret_addr[t].y * H
+                          : a.dots + ((uint64_t)t * a.dots_slots + slot) * H;
         uint32_t rb = r0;
 #pragma unroll 1
         for (uint32_t u = 0; u < units; u++) {
@@ -1092,6 +1094,9 @@ __device__ __forceinline__ void dn_run(const MoeDownArgs& a, uint8_t* smem, uint
         }
         if (a.combine) dn_arrive_and_combine(a, t, r0, r1);
     }
+    // rows returned in place (peer stores): visible system-wide before this
+    // grid is seen complete by the launch that releases the done flags
+    if (a.ret_addr != nullptr) __threadfence_system();
 }
 
 template <int TD, int TSD>
@@ -1521,7 +1526,10 @@ __device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uin
 #pragma unroll
                 for (int p = 0; p < G; p++) {
                     if ((uint32_t)p < n) {
-                        float* drow = a.dots + ((uint64_t)tp[p] * a.dots_slots + sp[p]) * H;
+                        float* drow = a.ret_addr != nullptr
+                                          ? reinterpret_cast<float*>(a.ret_peers[a.ret_addr[tp[p]].x] + a.ret_off) +
+                                                (uint64_t)a.ret_addr[tp[p]].y * H
+                                          : a.dots + ((uint64_t)tp[p] * a.dots_slots + sp[p]) * H;
                         for (uint32_t rr = lane; rr < nrows; rr += 32) drow[rb + rr] = res[rr * n + p];
                     }
                 }
@@ -1535,6 +1543,7 @@ __device__ __forceinline__ void gdn_run(const MoeDownArgs& a, uint8_t* smem, uin
                 if ((uint32_t)p < n) dn_arrive_and_combine(a, tp[p], r0, r1);
         }
     }
+    if (a.ret_addr != nullptr) __threadfence_system();  // rows returned in place (see dn_run)
 }
 
 // Lookup tables of a role's type into the start of shared memory.

@@ -440,10 +440,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_dots_kernel(TcDotsArgs a) {
                 // the pair's row: its grouped position, or its token (item) when scattering
                 const uint64_t r = a.out_by_token ? (uint64_t)a.pair_tokens[p0 + t] : (uint64_t)(p0 + t);
                 const float c = chain[t * kTcThreads];
-                a.dots[r * a.dots_stride + mat.out_offset + row] = TT::kIq2 ? __fmul_rn(0.125f, c) : c;
+                float* dst = a.ret_addr != nullptr
+                                 ? reinterpret_cast<float*>(a.ret_peers[a.ret_addr[r].x] + a.ret_off) +
+                                       (uint64_t)a.ret_addr[r].y * a.dots_stride
+                                 : a.dots + r * a.dots_stride;
+                dst[mat.out_offset + row] = TT::kIq2 ? __fmul_rn(0.125f, c) : c;
             }
         }
     }
+    if (a.ret_addr != nullptr) __threadfence_system();  // rows returned in place: visible before the done flags
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

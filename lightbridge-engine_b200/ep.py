@@ -291,6 +291,11 @@ class PeerExpertParallelMoe:
         (layer or self.layer).scatter(self.peers, self.world, self.rank, self.cap, self.dots, self.returns,
                                       self.count, stream=self._main()[0])
 
+    def compute_return(self, layer=None) -> None:
+        """compute and send_back in one: the down rows stored in the home buffers."""
+        (layer or self.layer).items_return(self.peers, self.world, self.rank, self.cap, self.q8_items, self.items,
+                                           self.returns, self.count, self.ws, stream=self._main()[0])
+
     def shared(self, tokens: int, layer=None) -> None:
         """The shared expert of the published tokens into shared_dots."""
         (layer or self.layer).shared(self.buf.ptr, self.cap, tokens, self.shared_dots, self.ws_shared,
@@ -320,8 +325,7 @@ class PeerExpertParallelMoe:
             L.shared(self.buf.ptr, self.cap, tokens, self.shared_dots, self.ws_shared, stream=self.side.cuda_stream)
             self._ev_shared.record(self.side)
         self.dispatch(L)
-        self.compute(L)
-        self.send_back(L)
+        self.compute_return(L)
         if side:
             main.wait_event(self._ev_shared)
         self.combine(tokens, out, L, shared_done=side)

@@ -208,6 +208,7 @@ def _load() -> ctypes.CDLL:
         "lbk_ep_items_forward_counted": ([P, P, P, P, U64, P, P, U64, P], I32),
         "lbk_ep_scatter": ([P, P, U32, U32, U64, P, P, P, U64, P], I32),
         "lbk_ep_shared": ([P, P, U64, U64, P, P, U64, P], I32),
+        "lbk_ep_items_return": ([P, P, U32, U32, U64, P, P, P, P, U64, P, U64, P], I32),
         "lbk_tc_grouped_dots": ([P, I32, P, U32, P, U32, P, U64, P, P, U64, P], I32),
         "lbk_ep_combine_exchange": ([P, P, U32, U64, U64, P, P, P, U64, P], I32),
         "lbk_moe_layer_trace": ([P, I32], I32),
@@ -245,7 +246,7 @@ EXPORTED = (
     "lbk_ep_layer_create lbk_ep_q8_bytes lbk_ep_workspace_bytes lbk_ep_route "
     "lbk_ep_items_forward lbk_ep_combine lbk_peer_alloc lbk_peer_free lbk_peer_open lbk_peer_close "
     "lbk_ep_exchange_layout lbk_ep_publish lbk_ep_gather lbk_ep_items_forward_counted lbk_ep_scatter "
-    "lbk_ep_shared lbk_ep_combine_exchange lbk_tc_grouped_dots "
+    "lbk_ep_shared lbk_ep_items_return lbk_ep_combine_exchange lbk_tc_grouped_dots "
     "lbk_repack lbk_unpack lbk_validate_matrix lbk_decode_rows "
     "lbk_gguf_default_limits lbk_gguf_open lbk_gguf_close lbk_gguf_info lbk_gguf_tensor_at lbk_gguf_find_tensor "
     "lbk_gguf_metadata lbk_gguf_metadata_string lbk_moe_layer_load"
@@ -533,6 +534,12 @@ class EpLayer(MoeLayer):
     def scatter(self, peers, world: int, rank: int, cap: int, dots, returns, count, stream=None) -> None:
         check(lib.lbk_ep_scatter(self.ptr, _ptr(peers), world, rank, cap, _ptr(dots), _ptr(returns), _ptr(count),
                                  returns.shape[0], _stream(stream)))
+
+    def items_return(self, peers, world: int, rank: int, cap: int, q8_items, items, returns, count, workspace,
+                     stream=None) -> None:
+        check(lib.lbk_ep_items_return(self.ptr, _ptr(peers), world, rank, cap, _ptr(q8_items), _ptr(items),
+                                      _ptr(returns), _ptr(count), items.shape[0], _ptr(workspace), workspace.numel(),
+                                      _stream(stream)))
 
     def shared(self, xbuf: int, cap: int, tokens: int, shared_dots, workspace, stream=None) -> None:
         check(lib.lbk_ep_shared(self.ptr, xbuf, cap, tokens, _ptr(shared_dots), _ptr(workspace), workspace.numel(),

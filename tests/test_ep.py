@@ -313,8 +313,9 @@ def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, gro
     as its peers would address it, each rank with its own tokens (one with
     none). Every call of a step is issued after the calls whose flags it waits
     for, so no kernel waits on another. Two steps on the same buffers (the
-    second with the shared expert from lbk_ep_shared): every rank's output
-    equals lbk_moe_forward on its tokens bit for bit."""
+    second with the shared expert from lbk_ep_shared and the items' rows
+    returned in place by lbk_ep_items_return): every rank's output equals
+    lbk_moe_forward on its tokens bit for bit."""
     from gpu_helpers import clean_status, dev
 
     full, ranks, keep, rng = _gpu_layers(H, F, E, k, 13 * H + F + E + world, world)
@@ -330,8 +331,12 @@ def test_peer_exchange_ranks_simulated_on_one_gpu(world, H, F, E, k, tokens, gro
         for r in range(world):
             s = st[r]
             ranks[r].gather(peers, world, r, cap, s["q8_items"], s["items"], s["returns"], s["count"])
-            ranks[r].items_forward_counted(s["q8_items"], s["items"], s["count"], s["dots"], s["ws"])
-            ranks[r].scatter(peers, world, r, cap, s["dots"], s["returns"], s["count"])
+            if step == 0:  # items, then their dots sent home
+                ranks[r].items_forward_counted(s["q8_items"], s["items"], s["count"], s["dots"], s["ws"])
+                ranks[r].scatter(peers, world, r, cap, s["dots"], s["returns"], s["count"])
+            else:  # the down rows stored in the home buffers directly
+                ranks[r].items_return(peers, world, r, cap, s["q8_items"], s["items"], s["returns"], s["count"],
+                                      s["ws"])
         outs = [torch.full((max(T, 1) * H,), float("nan"), device="cuda") for T in tokens]
         for r in range(world):
             sd = None
@@ -428,8 +433,7 @@ def test_peer_exchange_stack_chain_equals_block_forward(world, B):
         for r in range(world):
             s = st[r]
             ranks[r].gather(peers, world, r, B, s["q8_items"], s["items"], s["returns"], s["count"])
-            ranks[r].items_forward_counted(s["q8_items"], s["items"], s["count"], s["dots"], s["ws"])
-            ranks[r].scatter(peers, world, r, B, s["dots"], s["returns"], s["count"])
+            ranks[r].items_return(peers, world, r, B, s["q8_items"], s["items"], s["returns"], s["count"], s["ws"])
         for r in range(world):
             ranks[r].combine_exchange(bufs[r].data_ptr(), world, B, B, delta[r], st[r]["ws"])
             ctx().residual_add(hid[r], delta[r], B * H)
