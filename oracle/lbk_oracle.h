@@ -98,6 +98,29 @@ int32_t orc_rms_norm(const float* input, uint64_t n, const float* weight, uint64
 // residual_add_in_place (norm.rs:83-100): dest += src, or nothing on error.
 int32_t orc_residual_add(float* dest, uint64_t n, const float* src, uint64_t src_len);
 
+/* Reduced Hy3 model pieces (hy3_reduced.cpp): the deterministic weights of
+ * bridge-test-model/src/hy3.rs and the non-expert steps of its token
+ * (bridge-kernels-reference/src/layer.rs:309-472), for the end-to-end pin
+ * against bridge-test-model/tests/fixtures/hy3-oracle-v1.json. */
+uint16_t orc_f32_to_f16(float v);
+int32_t orc_hy3_fill_matrix(int32_t type, uint64_t input_width, uint64_t output_width, uint64_t seed, uint8_t* out,
+                            uint64_t out_len);
+void orc_hy3_embeddings(float* out, uint64_t n);
+void orc_hy3_norm_weights(uint64_t length, uint64_t seed, float* out);
+int32_t orc_gemv_dequant(const orc_matrix* w, const float* x, float* y);
+int32_t orc_gemv_dequant_accumulate_scaled(const orc_matrix* w, const float* x, float* y, float scale);
+int32_t orc_head_rms_norm(float* values, uint64_t n, const float* weight, uint64_t head_dim, float eps);
+/* Hy3RopeParams, rope.rs:8-18 */
+typedef struct orc_rope {
+    uint64_t head_dim, context_length, original_context;
+    float base, freq_scale, ext_factor, attn_factor, beta_fast, beta_slow;
+} orc_rope;
+int32_t orc_rope_neox_yarn(float* values, uint64_t head_count, uint64_t position, const orc_rope* p);
+int32_t orc_gqa_attention(const float* cache_keys, const float* cache_values, uint64_t stored, uint64_t q_heads,
+                          uint64_t kv_heads, uint64_t dim, const float* q, const float* k, const float* v,
+                          float* out);
+int32_t orc_softmax(const float* logits, uint64_t n, float* out);
+
 float orc_f16_to_f32(uint16_t bits);
 int32_t orc_nearest_int(float v);
 float orc_expf(float v);

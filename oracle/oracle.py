@@ -46,6 +46,22 @@ class Expert(ctypes.Structure):
     _fields_ = [("gate", Matrix), ("up", Matrix), ("down", Matrix)]
 
 
+class Rope(ctypes.Structure):
+    """Hy3RopeParams (bridge-kernels-reference/src/rope.rs:8-18)."""
+
+    _fields_ = [
+        ("head_dim", ctypes.c_uint64),
+        ("context_length", ctypes.c_uint64),
+        ("original_context", ctypes.c_uint64),
+        ("base", ctypes.c_float),
+        ("freq_scale", ctypes.c_float),
+        ("ext_factor", ctypes.c_float),
+        ("attn_factor", ctypes.c_float),
+        ("beta_fast", ctypes.c_float),
+        ("beta_slow", ctypes.c_float),
+    ]
+
+
 def build() -> None:
     """Compile the oracle library in place (make, no reference sources)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
@@ -92,6 +108,19 @@ def _declare(L: ctypes.CDLL) -> None:
     L.orc_expf.restype = F
     L.orc_table_bytes.argtypes = [I32, ctypes.POINTER(U64)]
     L.orc_table_bytes.restype = ctypes.POINTER(ctypes.c_uint8)
+    L.orc_f32_to_f16.argtypes = [F]
+    L.orc_f32_to_f16.restype = ctypes.c_uint16
+    L.orc_hy3_fill_matrix.argtypes = [I32, U64, U64, U64, P, U64]
+    L.orc_hy3_embeddings.argtypes = [P, U64]
+    L.orc_hy3_embeddings.restype = None
+    L.orc_hy3_norm_weights.argtypes = [U64, U64, P]
+    L.orc_hy3_norm_weights.restype = None
+    L.orc_gemv_dequant.argtypes = [ctypes.POINTER(Matrix), P, P]
+    L.orc_gemv_dequant_accumulate_scaled.argtypes = [ctypes.POINTER(Matrix), P, P, F]
+    L.orc_head_rms_norm.argtypes = [P, U64, P, U64, F]
+    L.orc_rope_neox_yarn.argtypes = [P, U64, U64, ctypes.POINTER(Rope)]
+    L.orc_gqa_attention.argtypes = [P, P, U64, U64, U64, U64, P, P, P, P]
+    L.orc_softmax.argtypes = [P, U64, P]
 
 
 def _p(a: np.ndarray) -> int:
@@ -285,3 +314,76 @@ def table_bytes(which: int) -> bytes:
 def hw_threads() -> int:
     return lib().orc_hw_threads()
 
+
+
+# ---------------------------------------------------------------- reduced Hy3
+
+
+def f32_to_f16(v: float) -> int:
+    return int(lib().orc_f32_to_f16(float(v)))
+
+
+def hy3_fill_matrix(ty: int, in_w: int, out_w: int, seed: int) -> np.ndarray:
+    """OwnedMatrix::quantized (bridge-test-model/src/hy3.rs:68-117): GGUF bytes."""
+    out = np.zeros(in_w // 256 * BLOCK_BYTES[ty] * out_w, dtype=np.uint8)
+    _check(lib().orc_hy3_fill_matrix(ty, in_w, out_w, seed, _p(out), out.size))
+    return out
+
+
+def hy3_embeddings(n: int) -> np.ndarray:
+    out = np.zeros(n, dtype=np.float32)
+    lib().orc_hy3_embeddings(_p(out), n)
+    return out
+
+
+def hy3_norm_weights(length: int, seed: int) -> np.ndarray:
+    out = np.zeros(length, dtype=np.float32)
+    lib().orc_hy3_norm_weights(length, seed, _p(out))
+    return out
+
+
+def gemv_dequant(ty: int, in_w: int, out_w: int, w: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """gemv_into in DequantF32 mode (gemv.rs:33-41)."""
+    m = matrix(ty, in_w, out_w, w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(out_w, dtype=np.float32)
+    _check(lib().orc_gemv_dequant(ctypes.byref(m), _p(x), _p(y)))
+    return y
+
+
+def gemv_dequant_accumulate_scaled(ty, in_w, out_w, w, x, y, scale):
+    m = matrix(ty, in_w, out_w, w)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    _check(lib().orc_gemv_dequant_accumulate_scaled(ctypes.byref(m), _p(x), _p(y), float(scale)))
+    return y
+
+
+def head_rms_norm(values: np.ndarray, weight: np.ndarray, head_dim: int, epsilon: float) -> np.ndarray:
+    v = np.array(values, dtype=np.float32, copy=True)
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    _check(lib().orc_head_rms_norm(_p(v), v.size, _p(w), head_dim, float(epsilon)))
+    return v
+
+
+def rope_neox_yarn(values: np.ndarray, head_count: int, position: int, rope: Rope) -> np.ndarray:
+    v = np.array(values, dtype=np.float32, copy=True)
+    _check(lib().orc_rope_neox_yarn(_p(v), head_count, position, ctypes.byref(rope)))
+    return v
+
+
+def gqa_attention(cache_keys, cache_values, stored, q_heads, kv_heads, dim, q, k, v) -> np.ndarray:
+    """One token of causal_gqa_attention_into (attention.rs:28-87) over
+    `stored` cached [token][kv_head][dim] rows plus this token's k / v."""
+    ck = np.ascontiguousarray(cache_keys, dtype=np.float32)
+    cv = np.ascontiguousarray(cache_values, dtype=np.float32)
+    q, k, v = (np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v))
+    out = np.zeros(q_heads * dim, dtype=np.float32)
+    _check(lib().orc_gqa_attention(_p(ck), _p(cv), stored, q_heads, kv_heads, dim, _p(q), _p(k), _p(v), _p(out)))
+    return out
+
+
+def softmax(logits: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    out = np.zeros_like(x)
+    _check(lib().orc_softmax(_p(x), x.size, _p(out)))
+    return out
