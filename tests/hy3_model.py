@@ -237,3 +237,13 @@ def f32_hash(values) -> str:
 
 def hashes(record: dict) -> dict:
     return {k: f32_hash(v) for k, v in record.items() if k.startswith(("block", "final."))}
+
+
+def assert_close(got, want, atol, rtol):
+    """assert_close of llama_logits.rs:34-43: |got - want| <= atol + rtol |want| (f32)."""
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    assert got.shape == want.shape
+    tol = np.float32(atol) + np.float32(rtol) * np.abs(want)
+    bad = np.nonzero(np.abs(got - want) > tol)[0]
+    assert bad.size == 0, f"values {bad[:8]}: got {got[bad[:8]]}, want {want[bad[:8]]}"

@@ -33,6 +33,7 @@ from gpu_helpers import clean_status, ctx, dev, host, planar_dev
 pytestmark = pytest.mark.gpu
 
 FIXTURE = json.loads((REPO / "tests/golden/hy3-oracle-v1.json").read_text())
+LLAMA = json.loads((REPO / "tests/golden/hy3-llama-oracle-v1.json").read_text())
 
 
 class DeviceOps:
@@ -127,6 +128,11 @@ def test_reduced_model_device_path_matches_reference_hashes(layout):
         got = hm.hashes(rec)
         bad = sorted(k for k in step["hashes"] if got[k] != step["hashes"][k])
         assert not bad, f"token {step['token_id']}: {bad}"
+        # and within llama_logits.rs:45-71's tolerances of llama.cpp's run
+        llama = next(x for x in LLAMA["steps"] if x["token_id"] == step["token_id"])
+        assert rec["selected_experts"] == llama["selected_experts"]
+        hm.assert_close(rec["final.logits"], llama["logits"], 3.0e-4, 3.0e-4)
+        hm.assert_close(rec["final.probabilities"], llama["probabilities"], 5.0e-5, 5.0e-5)
     assert ops.calls > 0
     ops.moe_layer.close()
 

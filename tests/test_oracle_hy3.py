@@ -20,6 +20,8 @@ import oracle as orc
 from conftest import REPO
 
 FIXTURE = json.loads((REPO / "tests/golden/hy3-oracle-v1.json").read_text())
+LLAMA = json.loads((REPO / "tests/golden/hy3-llama-oracle-v1.json").read_text())
+
 
 
 def test_fixture_shape():
@@ -42,6 +44,21 @@ def test_two_step_sequence_matches_reference_hashes(mode):
         assert hm.hashes(rec) == step["hashes"]
     assert session.position == 2
     assert [len(k) for k in session.keys] == [2, 2]
+
+
+def test_llama_q8k_mode_matches_llama_cpp_logits():
+    """The same model run by llama.cpp b10153 (llama_logits.rs:45-71): the
+    LlamaQ8K logits within 3e-4 + 3e-4 |want| and probabilities within
+    5e-5 + 5e-5 |want|, same selected experts and greedy tokens."""
+    assert LLAMA["format"] == "lightbridge-llama-hy3-oracle-v1"
+    model = hm.ReducedHy3()
+    session = hm.Session()
+    for step in LLAMA["steps"]:
+        rec = hm.evaluate_token(model, session, hm.OracleOps("llama_q8_k"), step["token_id"])
+        assert rec["selected_experts"] == step["selected_experts"]
+        assert rec["greedy_id"] == step["greedy_id"]
+        hm.assert_close(rec["final.logits"], step["logits"], 3.0e-4, 3.0e-4)
+        hm.assert_close(rec["final.probabilities"], step["probabilities"], 5.0e-5, 5.0e-5)
 
 
 def test_execution_modes_are_numerically_distinct():
