@@ -339,6 +339,7 @@ def our_arm(args, rank: int, world: int, local_rank: int) -> None:
             layer = tables[t % LAYERS][0]
             layer.forward(xs[t], 1, outs[t], wss[t % LAYERS], stream=s.cuda_stream)
 
+    stream.wait_stream(torch.cuda.current_stream())  # weights and inputs come from the default stream
     with torch.cuda.stream(stream):
         step_calls(stream)  # warm: sets kernel attributes outside capture
     torch.cuda.synchronize()
@@ -613,6 +614,7 @@ def ep_peer_measure(ctx, lbk, torch, dev, rank: int, world: int, steps: int, war
         if world > 1:
             dist.barrier(device_ids=[dev.index])
 
+    stream.wait_stream(torch.cuda.current_stream())  # weights and inputs come from the default stream
     with torch.cuda.stream(stream):
         step()  # sets kernel attributes outside capture
     barrier()
@@ -841,6 +843,7 @@ def batched_direct_arm(args, rank: int, world: int, local_rank: int) -> None:
         for l, (layer, _) in enumerate(tables):
             layer.forward(xs[l], T, outs[l], ws, stream=s.cuda_stream)
 
+    stream.wait_stream(torch.cuda.current_stream())  # weights and inputs come from the default stream
     with torch.cuda.stream(stream):
         step(stream)
         stream.synchronize()
@@ -924,6 +927,7 @@ def gemv_arm(args, cfg: int, rank: int, world: int, local_rank: int) -> None:
         y = torch.empty(rows, device=dev)
         q8 = torch.empty(k // 256 * 292, dtype=torch.uint8, device=dev)
         stream = torch.cuda.Stream(device=dev)
+        stream.wait_stream(torch.cuda.current_stream())  # weights and inputs come from the default stream
         with torch.cuda.stream(stream):
             for m in mats:
                 ctx.gemv(m, x, y, q8, stream=stream.cuda_stream)
@@ -1018,6 +1022,7 @@ def stack_ep_arm(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    stream.wait_stream(torch.cuda.current_stream())  # weights and inputs come from the default stream
     with torch.cuda.stream(stream):
         step()
     barrier()
@@ -1117,6 +1122,7 @@ def stack_arm(args, rank: int, world: int, local_rank: int) -> None:
         for layer, _ in layers:
             layer.block_forward(hidden, norm_w, 1e-6, B, ws, stream=s.cuda_stream)
 
+    stream.wait_stream(torch.cuda.current_stream())  # weights and inputs come from the default stream
     with torch.cuda.stream(stream):
         step(stream)
         stream.synchronize()

@@ -306,6 +306,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
 // reporting are the register kernel's (same products, same tails, same
 // order).
 //
+// The kernel is a programmatic dependent launch: it starts while the stream's
+// previous kernel is still running, lets the next one launch at once, and
+// before its grid_dep_wait() only asks L2 for its first rows and copies the
+// context's lookup table (written once at context creation). The prefetch
+// reads the matrix and nothing else, so it is safe whatever the previous
+// kernel wrote: L2 is the point of coherence and the later copies read the
+// current bytes. The shared-memory copies of the rows, x (or its Q8_K image)
+// and every write of y or the status word come after the wait. Back-to-back
+// calls thus overlap one call's launch, prologue and first DRAM round trip
+// with the previous call's tail.
+//
 // Shared memory: [table][stages: kWarps * stages * stage][act qs K][d nb]
 //                [bsums nb*16][tails kWarps*slots*nb*kTail][flag]
 
@@ -363,6 +374,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
     const uint32_t bar_t = (uint32_t)__cvta_generic_to_shared(&s_bar[kWarps * kBulkMaxStages]);
     const uint64_t pol = policy_evict_first();
 
+    grid_dep_launch();
+    if (lane == 0)
+        for (int s = 0; s < stages; s++) {
+            const uint64_t st = gwarp + (uint64_t)s * nwarp;
+            if (st >= steps) break;
+            const uint64_t r0 = st * rps;
+            const uint64_t nr = rows - r0 < (uint64_t)rps ? rows - r0 : (uint64_t)rps;
+            prefetch_l2(a.w.data + r0 * rs, (uint32_t)(nr * rs));
+        }
+
     // step i of this warp (global step gwarp + i * nwarp) into stage i % stages
     auto issue = [&](uint64_t i) {
         const uint64_t st = gwarp + i * nwarp;
@@ -379,9 +400,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
         mbar_init_fence();
     }
     __syncthreads();
-    // the first stages' rows and the table are in flight during the prologue
-    if (lane == 0)
-        for (int s = 0; s < stages; s++) issue((uint64_t)s);
     if constexpr (Cfg::kTableBytes != 0) {
         if (threadIdx.x == 0) {
             mbar_expect_tx(bar_t, (uint32_t)Cfg::kTableBytes);
@@ -390,6 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
                      (uint32_t)Cfg::kTableBytes, bar_t);
         }
     }
+    grid_dep_wait();  // the previous kernel's writes (x, y, the matrix) are visible from here
+    // the first stages' rows are in flight during the activation prologue
+    if (lane == 0)
+        for (int s = 0; s < stages; s++) issue((uint64_t)s);
     const bool ok = stage_activations(a, nb, qs, dsm, bs, flag);
     if constexpr (Cfg::kTableBytes != 0) {
         if (!mbar_wait(bar_t, 0) && threadIdx.x == 0) report(a.status, LBK_TIMEOUT, 10, 0);
@@ -523,8 +545,17 @@ cudaError_t launch_gemv_bulk(const GemvArgs& a, int stages, int sm_count, cudaSt
     uint64_t ctas = (steps + kWarps - 1) / kWarps;
     if (ctas > (uint64_t)sm_count) ctas = sm_count;
     if (ctas < 1) ctas = 1;
-    gemv_bulk_kernel<T><<<(unsigned)ctas, kThreads, smem, stream>>>(a, stages);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)ctas);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see the kernel's grid_dep_wait()
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<T>, a, stages);
 }
 
 template <int T, int L>
