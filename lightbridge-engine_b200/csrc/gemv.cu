@@ -341,7 +341,12 @@ __host__ __device__ inline BulkLayout<T> bulk_layout(int nb, int tpr, int slots,
 
 constexpr int kBulkMaxStages = 8;
 
-template <int T>
+// P = 1: rows of at most 16 blocks, one half block per lane, its activations
+// held in registers for the whole launch. P = 2: rows of 17-32 blocks (a
+// block's 8192-wide attention output projection), one row per step; lane l
+// decodes half blocks l and l + 32 of the row, each pass with its activations
+// loaded from the shared Q8_K image (two sets would not fit in registers).
+template <int T, int P>
 __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int stages) {
     using Cfg = GemvCfg<T>;
     using HB = typename HBOf<T>::type;
@@ -427,15 +432,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
     constexpr bool kTr = !Cfg::kIq;
     ActHB act;
     uint32_t nact[32];
-    if (lane_on) {
-        load_act_hb<kTr>(act, as, b0, h0, !Cfg::kIq);
+    auto load_act = [&](int b) {
+        load_act_hb<kTr>(act, as, b, h0, !Cfg::kIq);
         if constexpr (T == LBK_TYPE_IQ3_S) {
 #pragma unroll
             for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);
         }
+    };
+    if constexpr (P == 1) {
+        if (lane_on) load_act(b0);
     }
     const uint32_t t0 = (uint32_t)__cvta_generic_to_shared(tab0 + lane);
     const StageOff so = stage_off<T>(nb, lane_on ? sub : 0, lane_on ? b0 : 0, lane_on ? h0 : 0);
+    // P = 2: the second pass's half block (lane + 32), block 0's offsets on
+    // lanes past the row's end (decoded, never stored)
+    const bool on1 = P == 2 && lane + 32 < 2 * nb;
+    const int b1 = on1 ? b0 + 16 : 0;
+    const StageOff so1 = stage_off<T>(nb, 0, b1, on1 ? h0 : 0);
 
     const int slots = a.tail_slots;  // >= rps, multiple of rps
     auto flush = [&](int nslots, uint64_t first_step) {
@@ -467,42 +480,53 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
             live = false;
             if (lane == 0) report(a.status, LBK_TIMEOUT, 11, step);
         }
-        HB w;
+        HB w, w1;
         load_stage(w, ring + s * lay.stage, so);
+        if constexpr (P == 2) load_stage(w1, ring + s * lay.stage, so1);
         __syncwarp();
         if (lane == 0 && live) {
             fence_proxy_async_smem();  // the warp's reads of this stage before its refill
             issue(i + stages);
         }
         const uint64_t row = step * rps + sub;
-        const bool mine = live && lane_on && row < rows;
         const int slot = in_batch * rps + sub;
-        if constexpr (Cfg::kIq) {
-            IqPart p{0, 0};
-            if constexpr (T == LBK_TYPE_IQ2_S)
-                p = dot_hb(w, act, t0);
-            else
-                p = dot_hb(w, act, nact, t0);
-            int other = __shfl_xor_sync(0xffffffffu, p.sum, 1);
-            if (mine && h0 == 0) {
-                p.sum += other;
-                tail[(size_t)slot * nb + b0] = iq_block_product(p, dsm[b0]);
-                if (!h_finite(p.d)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b0, p.d);
+        // half block hv of block b: its block product into the row's tail slot
+        auto consume = [&](const HB& hv, int b, bool mine) {
+            if constexpr (Cfg::kIq) {
+                IqPart p{0, 0};
+                if constexpr (T == LBK_TYPE_IQ2_S)
+                    p = dot_hb(hv, act, t0);
+                else
+                    p = dot_hb(hv, act, nact, t0);
+                int other = __shfl_xor_sync(0xffffffffu, p.sum, 1);
+                if (mine && h0 == 0) {
+                    p.sum += other;
+                    tail[(size_t)slot * nb + b] = iq_block_product(p, dsm[b]);
+                    if (!h_finite(p.d)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b, p.d);
+                }
+            } else {
+                KPart p = dot_hb(hv, act, h0);
+#pragma unroll
+                for (int l = 0; l < 8; l++) p.lane[l] += __shfl_xor_sync(0xffffffffu, p.lane[l], 1);
+                p.min_sum += __shfl_xor_sync(0xffffffffu, p.min_sum, 1);
+                if (mine && h0 == 0) {
+                    float pr[9];
+                    k_block_products(p, dsm[b], pr);
+                    float* dst = tail + ((size_t)slot * nb + b) * 9;
+#pragma unroll
+                    for (int q = 0; q < 9; q++) dst[q] = pr[q];
+                    if (!h_finite(p.dm & 0xffffu)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b, p.dm & 0xffffu);
+                    if (!h_finite(p.dm >> 16)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b, p.dm >> 16);
+                }
             }
+        };
+        if constexpr (P == 1) {
+            consume(w, b0, live && lane_on && row < rows);
         } else {
-            KPart p = dot_hb(w, act, h0);
-#pragma unroll
-            for (int l = 0; l < 8; l++) p.lane[l] += __shfl_xor_sync(0xffffffffu, p.lane[l], 1);
-            p.min_sum += __shfl_xor_sync(0xffffffffu, p.min_sum, 1);
-            if (mine && h0 == 0) {
-                float pr[9];
-                k_block_products(p, dsm[b0], pr);
-                float* dst = tail + ((size_t)slot * nb + b0) * 9;
-#pragma unroll
-                for (int q = 0; q < 9; q++) dst[q] = pr[q];
-                if (!h_finite(p.dm & 0xffffu)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b0, p.dm & 0xffffu);
-                if (!h_finite(p.dm >> 16)) report(a.status, LBK_NON_FINITE_SCALE, row * nb + b0, p.dm >> 16);
-            }
+            load_act(b0);
+            consume(w, b0, live && row < rows);
+            load_act(b1);
+            consume(w1, b1, live && on1 && row < rows);
         }
         if (++in_batch == steps_per_batch) {
             flush(steps_per_batch * rps, batch_first);
@@ -520,10 +544,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
 constexpr uint32_t kBulkStaticSmem = (kWarps * kBulkMaxStages + 1) * 8;
 template <int T>
 int bulk_stages(const GemvArgs& a, int* slots) {
-    if (a.mat_table != nullptr || a.block_sums != nullptr || a.tpr < 2 * a.w.nb) return 0;
+    if (a.mat_table != nullptr || a.block_sums != nullptr || a.w.nb > 32) return 0;
+    if (a.tpr < 2 * a.w.nb && a.tpr != 32) return 0;  // 17-32 blocks: one row per step, two passes
     const int rps = 32 / a.tpr;
     int best = 0;
-    for (int sl : {a.tail_slots, 16, 8}) {
+    const bool wide = a.w.nb > 16;  // tail batches down to one row only there (the 16-block plans stay)
+    for (int sl : {a.tail_slots, 16, 8, wide ? 4 : 0, wide ? 2 : 0, wide ? 1 : 0}) {
+        if (sl == 0) continue;
         if (sl < rps || sl % rps != 0 || sl > a.tail_slots) continue;
         for (int s = kBulkMaxStages; s > best && s >= 2; s--)
             if (bulk_layout<T>(a.w.nb, a.tpr, sl, s).total + kBulkStaticSmem <= kMaxSmem) {
@@ -538,7 +565,8 @@ int bulk_stages(const GemvArgs& a, int* slots) {
 template <int T>
 cudaError_t launch_gemv_bulk(const GemvArgs& a, int stages, int sm_count, cudaStream_t stream) {
     const size_t smem = bulk_layout<T>(a.w.nb, a.tpr, a.tail_slots, stages).total;
-    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(gemv_bulk_kernel<T>));
+    void (*kernel)(GemvArgs, int) = a.w.nb > 16 ? gemv_bulk_kernel<T, 2> : gemv_bulk_kernel<T, 1>;
+    cudaError_t e = ensure_max_smem(reinterpret_cast<const void*>(kernel));
     if (e != cudaSuccess) return e;
     const uint64_t rps = 32 / a.tpr;
     const uint64_t steps = (a.w.rows + rps - 1) / rps;
@@ -555,7 +583,7 @@ cudaError_t launch_gemv_bulk(const GemvArgs& a, int stages, int sm_count, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_bulk_kernel<T>, a, stages);
+    return cudaLaunchKernelEx(&cfg, kernel, a, stages);
 }
 
 template <int T, int L>

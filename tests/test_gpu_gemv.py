@@ -31,7 +31,10 @@ def run_gemv(ty, k, rows, w, x, layout):
 
 @pytest.mark.parametrize("layout", [lbk.LAYOUT_GGUF, lbk.LAYOUT_PLANAR])
 @pytest.mark.parametrize("ty", ALL)
-@pytest.mark.parametrize("k,rows", [(256, 1), (512, 17), (768, 8), (1536, 130), (4096, 100), (3072, 5)])
+# rows of 17-32 blocks (4352, 6144, 8192 wide) take the two-pass bulk-copy kernel in the planar layout;
+# 5000 rows of 8192 give every warp two or more rows, so its tail batches flush more than once
+@pytest.mark.parametrize("k,rows", [(256, 1), (512, 17), (768, 8), (1536, 130), (4096, 100), (3072, 5), (4352, 33),
+                                    (6144, 70), (8192, 37), (8192, 5000)])
 def test_gemv_matches_oracle(ty, k, rows, layout):
     rng = np.random.default_rng(1000 + k + rows + ty)
     w = synth.packed_np(rng, ty, k, rows)
