@@ -320,6 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(GemvArgs a) {
 // Shared memory: [table][stages: kWarps * stages * stage][act qs K][d nb]
 //                [bsums nb*16][tails kWarps*slots*nb*kTail][flag]
 
+// Bytes of the activation image's qs: rows of more than 16 blocks keep a full
+// 32-block image (the two-pass kernel rearranges it lane-major in place).
+__host__ __device__ inline uint32_t bulk_qs_bytes(int nb) { return (uint32_t)(nb > 16 ? 32 : nb) * kQK; }
+
 template <int T>
 struct BulkLayout {
     uint32_t stage, ring, act, tail, flag, total;
@@ -332,7 +336,7 @@ __host__ __device__ inline BulkLayout<T> bulk_layout(int nb, int tpr, int slots,
     o.stage = (uint32_t)(32 / tpr) * rs;
     o.ring = (uint32_t)GemvCfg<T>::kTableBytes;
     o.act = o.ring + (uint32_t)(kWarps * stages) * o.stage;
-    uint32_t t = o.act + (uint32_t)nb * kQK + (uint32_t)nb * 4 + (uint32_t)nb * 32;
+    uint32_t t = o.act + bulk_qs_bytes(nb) + (uint32_t)nb * 4 + (uint32_t)nb * 32;
     o.tail = (t + 15u) & ~15u;
     o.flag = o.tail + (uint32_t)(kWarps * slots * nb * GemvCfg<T>::kTail) * 4u;
     o.total = o.flag + 16u;
@@ -356,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
     const BulkLayout<T> lay = bulk_layout<T>(nb, a.tpr, a.tail_slots, stages);
     uint32_t* tab0 = reinterpret_cast<uint32_t*>(smem);
     int8_t* qs = reinterpret_cast<int8_t*>(smem + lay.act);
-    float* dsm = reinterpret_cast<float*>(qs + (size_t)nb * kQK);
+    float* dsm = reinterpret_cast<float*>(qs + bulk_qs_bytes(nb));
     int16_t* bs = reinterpret_cast<int16_t*>(dsm + nb);
     float* tail_all = reinterpret_cast<float*>(smem + lay.tail);
     int* flag = reinterpret_cast<int*>(smem + lay.flag);
@@ -428,12 +432,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs a, int 
         return;
     }
 
+    if constexpr (P == 2) {
+        // The lane-major image: lane l's 16-byte chunk i of pass p (half block
+        // l + 32 p) moves to word (8 p + i) * 32 + l, so that each pass loads
+        // its activations without bank conflicts (in natural order the lanes'
+        // half blocks lie 128 bytes apart, all in the same banks). One chunk
+        // per thread; chunks of half blocks past the row's end are not
+        // moved, and their lanes decode but never store.
+        static_assert(kThreads == 2 * 8 * 32, "one 16-byte chunk per thread");
+        const int t = threadIdx.x, pp = t >> 8, ci = (t >> 5) & 7, l = t & 31;
+        const int hb = pp * 32 + l;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (hb < 2 * nb) v = reinterpret_cast<const uint4*>(qs)[hb * 8 + ci];
+        __syncthreads();
+        if (hb < 2 * nb) reinterpret_cast<uint4*>(qs)[(pp * 8 + ci) * 32 + l] = v;
+        __syncthreads();
+    }
     ActSmem as{qs, dsm, bs};
     constexpr bool kTr = !Cfg::kIq;
     ActHB act;
     uint32_t nact[32];
     auto load_act = [&](int b) {
-        load_act_hb<kTr>(act, as, b, h0, !Cfg::kIq);
+        if constexpr (P == 1) {
+            load_act_hb<kTr>(act, as, b, h0, !Cfg::kIq);
+        } else {
+            const uint4* img = reinterpret_cast<const uint4*>(qs) + (b >= 16 ? 8 * 32 : 0) + lane;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint4 v = img[i * 32];
+                act.w[4 * i + 0] = v.x;
+                act.w[4 * i + 1] = v.y;
+                act.w[4 * i + 2] = v.z;
+                act.w[4 * i + 3] = v.w;
+            }
+            finish_act_hb<kTr>(act, as, b, h0, !Cfg::kIq);
+        }
         if constexpr (T == LBK_TYPE_IQ3_S) {
 #pragma unroll
             for (int i = 0; i < 32; i++) nact[i] = (uint32_t)__vneg4((int)act.w[i]);

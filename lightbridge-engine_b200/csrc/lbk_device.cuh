@@ -448,17 +448,10 @@ struct ActSmem {
     const int16_t* bsums;
 };
 
+// The rest of load_act_hb once a.w holds the half block's 128 activation
+// bytes in natural order: the K-quant transposition, d and the group sums.
 template <bool kTransposed>
-__device__ __forceinline__ void load_act_hb(ActHB& a, const ActSmem& s, int block, int half, bool with_bsums) {
-    const uint4* src = reinterpret_cast<const uint4*>(s.qs + block * kQK + half * 128);
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        uint4 v = src[i];
-        a.w[4 * i + 0] = v.x;
-        a.w[4 * i + 1] = v.y;
-        a.w[4 * i + 2] = v.z;
-        a.w[4 * i + 3] = v.w;
-    }
+__device__ __forceinline__ void finish_act_hb(ActHB& a, const ActSmem& s, int block, int half, bool with_bsums) {
     if (kTransposed) {
         // sub-block j (32 lanes = words 8j..8j+7 in natural order):
         // out word l (l<4)  = byte l of words 8j+0, +2, +4, +6
@@ -480,6 +473,20 @@ __device__ __forceinline__ void load_act_hb(ActHB& a, const ActSmem& s, int bloc
 #pragma unroll
         for (int i = 0; i < 8; i++) a.bsum[i] = 0;
     }
+}
+
+template <bool kTransposed>
+__device__ __forceinline__ void load_act_hb(ActHB& a, const ActSmem& s, int block, int half, bool with_bsums) {
+    const uint4* src = reinterpret_cast<const uint4*>(s.qs + block * kQK + half * 128);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        uint4 v = src[i];
+        a.w[4 * i + 0] = v.x;
+        a.w[4 * i + 1] = v.y;
+        a.w[4 * i + 2] = v.z;
+        a.w[4 * i + 3] = v.w;
+    }
+    finish_act_hb<kTransposed>(a, s, block, half, with_bsums);
 }
 
 // ------------------------------------------------------------ HB weight data
