@@ -1344,6 +1344,9 @@ int32_t launch_routing(lbk_moe_layer* layer, const float* x, uint64_t tokens, lb
     if (router_mode == LBK_ROUTER_TREE) {
         e = lbk::launch_router_fused(f, ctx->sm_count, st);
         if (e != cudaSuccess) return cuda_fail(e, "router launch");
+    } else if (tokens <= 4 && layer->E <= 1024) {
+        // sequential logits, the tokens' Q8_K and top-k in one launch
+        if ((e = lbk::launch_router_seq_fused(f, ctx->sm_count, st)) != cudaSuccess) return cuda_fail(e, "router launch");
     } else {
         if (int32_t s = run_f32_gemv(ctx, &layer->w.router, x, tokens, logits, st)) return s;
         lbk::TopkArgs ta{logits, layer->w.selection_bias, layer->E, tokens, (uint32_t)layer->k, layer->weight_scale, routed,

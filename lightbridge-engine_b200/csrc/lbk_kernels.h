@@ -80,6 +80,9 @@ struct RouterFusedArgs {
 };
 size_t router_partials_floats(uint64_t hidden, uint64_t experts, uint64_t tokens);
 cudaError_t launch_router_fused(const RouterFusedArgs& f, int sm_count, cudaStream_t stream);
+// The sequential (bit-identical) logits, the tokens' Q8_K and top-k in one
+// launch, for at most 4 tokens and 1024 experts (cudaErrorInvalidValue else).
+cudaError_t launch_router_seq_fused(const RouterFusedArgs& f, int sm_count, cudaStream_t stream);
 
 // weighted_rms_norm_into per row (norm.cu): rows x n values.
 struct NormArgs {
