@@ -6,8 +6,9 @@
 // route_experts_into (bridge-model-hy3/src/routing.rs:25-107).
 //
 // Two logit orders:
-//  * sequential -- one thread per (token, expert) runs the reference's single
-//    f32 chain over the hidden lanes, bit-identical, but latency-bound;
+//  * sequential -- one lane per (token, expert) runs the reference's single
+//    f32 chain over the hidden lanes from products the rest of its CTA forms
+//    in shared memory: bit-identical, bound by the chain's latency;
 //  * tree -- rows split into 512-lane chunks over many warps, each chunk a
 //    fixed shuffle tree, chunks summed in chunk order: deterministic and
 //    within 1e-5 of the sequential order. The tree kernel also quantizes the
